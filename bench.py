@@ -1,0 +1,399 @@
+"""Benchmark: MoE FFN layer at Qwen3-30B-A3B shape on B200.
+
+One step = one call of the MoE layer (router -> top-k -> dispatch -> grouped
+Q4_K gate/up + SwiGLU -> grouped Q6_K down -> combine) on a batch of B tokens.
+Weights: 48 layers of configs[1] (d=2048, 128 experts top-8, ff=768, Q4_K
+gate/up + Q6_K down from N(0, 0.02), F32 router N(0, 0.02)) made on the GPU
+with this library's quantizer; step i runs layer i % 48, so the 18.8 GB of
+weights stream from HBM (inputs larger than L2; no step reuses another's
+weights from L2). Activations: f32 N(0, 1), a pool of distinct batches.
+
+  value   tokens/s over all ranks, device-timed (CUDA events, max over ranks)
+  e2e     same metric through the host-pointer C ABI call kc_moe_ffn (pinned
+          host h in, host out back), wall-clock around synchronous calls
+  roofline  dominant kernel's algorithmic HBM bytes / its event-timed
+            duration vs MEASURED_PEAKS.json's copy bandwidth
+  cpu_baseline  the CPU oracle (C++ AVX2 restatement of Kestrel's path) on a
+                bounded sample of the same workload, all host threads
+
+--impl reference times the oracle alone (the reference's CPU arithmetic) on
+the same config. Multi-GPU (torchrun): each rank runs an independent replica
+of the layer stack on its own batch (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(name="qwen3-30b-a3b-moe-layer", d=2048, E=128, k=8, ff=768)
+BYTES_PER_EXPERT = 2 * 768 * (2048 // 256) * 144 + 2048 * (768 // 256) * 210  # 3,059,712
+ROUTER_BYTES = 128 * 2048 * 4
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def algorithmic_bytes(ids: np.ndarray, B: int) -> dict:
+    """Per call: distinct routed experts x bytes/expert + router + x in/out, and
+    the split of expert bytes between the int8 (<4 rows) and f32 paths."""
+    d, ff = CFG["d"], CFG["ff"]
+    cnt = np.bincount(ids.reshape(-1), minlength=CFG["E"])
+    small = int(((cnt >= 1) & (cnt <= 3)).sum())
+    large = int((cnt >= 4).sum())
+    gate_up = 2 * ff * (d // 256) * 144
+    down = d * (ff // 256) * 210
+    return dict(total=(small + large) * BYTES_PER_EXPERT + ROUTER_BYTES + B * d * 4 * 2,
+                gate_up_int8=small * gate_up, down_int8=small * down, gate_up_f32=large * gate_up,
+                down_f32=large * down, router=ROUTER_BYTES, experts=small + large)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------
+def make_layers(ctx, torch, n_layers, seed=0):
+    """configs[1] weights on the GPU: N(0, 0.02) quantised to Q4_K / Q6_K by
+    kc_quantize_dev, uploaded with kc_upload_experts (device source)."""
+    from kestrel_b200 import ggml as G
+    E, d, ff, k = CFG["E"], CFG["d"], CFG["ff"], CFG["k"]
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    bufs = {n: torch.empty((rows, G.bytes_for(t, cols)), dtype=torch.uint8, device="cuda")
+            for n, t, rows, cols in (("gate", G.Q4_K, E * ff, d), ("up", G.Q4_K, E * ff, d),
+                                     ("down", G.Q6_K, E * d, ff))}
+    x = torch.empty((E * ff, d), dtype=torch.float32, device="cuda")
+    for layer in range(n_layers):
+        for n, t in (("gate", G.Q4_K), ("up", G.Q4_K), ("down", G.Q6_K)):
+            xv = x.view(E * d, ff) if n == "down" else x
+            xv.normal_(0.0, 0.02, generator=g)
+            ctx.quantize_dev(t, xv, bufs[n])
+        router = torch.empty((E, d), dtype=torch.float32, device="cuda").normal_(0.0, 0.02, generator=g)
+        ctx.upload_experts(layer, E, d, ff, G.Q4_K, bufs["gate"], G.Q4_K, bufs["up"], G.Q6_K, bufs["down"])
+        ctx.upload_router(layer, router, k)
+        if layer == 0:
+            host0 = {n: b.cpu().numpy() for n, b in bufs.items()}
+            host0["router"] = router.cpu().numpy()
+    del x, bufs
+    torch.cuda.empty_cache()
+    return host0
+
+
+def cpu_oracle_rate(layer_w, B, budget_s, threads, seed=5):
+    """Tokens/s of the oracle's moe_ffn on one configs[1] layer, B tokens per
+    call, repeated until `budget_s` of CPU time has elapsed."""
+    import oracle
+    from kestrel_b200 import ggml as G
+    oracle.set_threads(threads)
+    rng = np.random.default_rng(seed)
+    calls, tokens, t0 = 0, 0, time.perf_counter()
+    while True:
+        h = rng.standard_normal((B, CFG["d"]), dtype=np.float32)
+        oracle.moe_ffn(h, layer_w["router"], CFG["k"], G.Q4_K, layer_w["gate"], G.Q4_K, layer_w["up"], G.Q6_K,
+                       layer_w["down"], CFG["ff"])
+        calls += 1
+        tokens += B
+        el = time.perf_counter() - t0
+        if el >= budget_s and calls >= 2:
+            return tokens / el, calls, el
+
+
+def host_layer_numpy(seed=0):
+    """One configs[1] layer generated on the CPU (numpy quantizer, threads)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from kestrel_b200 import ggml as G
+    E, d, ff = CFG["E"], CFG["d"], CFG["ff"]
+
+    def mat(name, t, rows, cols, s):
+        out = np.empty((rows, G.bytes_for(t, cols)), np.uint8)
+        step = 4096
+
+        def part(r0):
+            rng = np.random.default_rng([s, r0])
+            x = rng.standard_normal((min(step, rows - r0), cols), dtype=np.float32) * np.float32(0.02)
+            out[r0:r0 + x.shape[0]] = G.quantize(t, x)
+
+        with ThreadPoolExecutor(os.cpu_count() or 4) as ex:
+            list(ex.map(part, range(0, rows, step)))
+        return out
+
+    w = {"gate": mat("gate", G.Q4_K, E * ff, d, seed * 10 + 1), "up": mat("up", G.Q4_K, E * ff, d, seed * 10 + 2),
+         "down": mat("down", G.Q6_K, E * d, ff, seed * 10 + 3)}
+    w["router"] = (np.random.default_rng(seed * 10 + 4).standard_normal((E, d), dtype=np.float32) *
+                   np.float32(0.02))
+    return w
+
+
+# ----------------------------------------------------------------------------
+def run_reference(args):
+    """--impl reference: the reference's CPU arithmetic (the oracle restatement;
+    the Rust reference cannot be built in this image) on the same config."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    w = host_layer_numpy()
+    B = args.batch
+    rate, calls, el = None, 0, 0.0
+    for _ in range(args.warmup):
+        cpu_oracle_rate(w, B, 0.0, threads)
+    times = []
+    for i in range(args.steps):
+        r, c, e = cpu_oracle_rate(w, B, 0.0, threads, seed=100 + i)
+        times.append(e / c)
+    ms = 1e3 * sum(times) / len(times)
+    value = B / (ms / 1e3)
+    line = {
+        "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4k/f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": CFG["name"], "batch_tokens": B, "d_model": CFG["d"], "experts": CFG["E"],
+                   "top_k": CFG["k"], "expert_ff": CFG["ff"], "quant": "Q4_K gate/up + Q6_K down"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} calls of one layer at B={B} (oracle restatement of "
+                                   f"Kestrel's AVX2 path; Rust reference not buildable here)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def timed_steps(torch, ctx, hs, outs, n_layers, B, steps, stream):
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(steps):
+        ctx.moe_ffn_dev(i % n_layers, hs[i % len(hs)], outs[i % len(outs)], n_tok=B)
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from kestrel_b200.cuda import Context
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    ctx = Context(local)
+    stream = torch.cuda.current_stream()
+    ctx.set_stream(stream.cuda_stream)
+    n_layers = args.layers
+    host0 = make_layers(ctx, torch, n_layers, seed=rank * 1000)
+    B = args.batch
+    batches = sorted(set([B] + args.sweep))
+    ctx.reserve(max(batches))
+    d = CFG["d"]
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    pool = {b: [torch.randn((b, d), generator=g, device="cuda") for _ in range(16)] for b in batches}
+    outs = {b: [torch.empty((b, d), device="cuda") for _ in range(2)] for b in batches}
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # Warm-up, then the timed region at the headline batch.
+    timed_steps(torch, ctx, pool[B], outs[B], n_layers, B, args.warmup, stream)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms_total = timed_steps(torch, ctx, pool[B], outs[B], n_layers, B, args.steps, stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_total = max_over_ranks(ms_total)
+    ms_step = ms_total / args.steps
+    value = world * B * args.steps / (ms_total / 1e3)
+    clocks = clk.summary()
+
+    # Profiling pass (separate from the timed region): per-stage event times and
+    # the routed experts of every call -> algorithmic bytes per stage.
+    hbm_peak, peak_kind = peaks()
+    prof_steps = max(args.steps, 16)
+    ids_dev = torch.empty((B, CFG["k"]), dtype=torch.int32, device="cuda")
+    ctx.profile_read()
+    ctx.profile_enable(True)
+    byte_acc = {}
+    for i in range(prof_steps):
+        ctx.moe_ffn_dev(i % n_layers, pool[B][i % 16], outs[B][0], ids_dev, None, n_tok=B)
+        ab = algorithmic_bytes(ids_dev.cpu().numpy(), B)
+        for kk, v in ab.items():
+            byte_acc[kk] = byte_acc.get(kk, 0) + v
+    stages = ctx.profile_read()
+    ctx.profile_enable(False)
+    stage_bytes = {"gate_up_int8": byte_acc["gate_up_int8"], "down_int8": byte_acc["down_int8"],
+                   "gate_up_f32": byte_acc["gate_up_f32"], "down_f32": byte_acc["down_f32"],
+                   "router_logits": byte_acc["router"]}
+    dom = max(stages, key=lambda s: stages[s][0])
+    dom_ms, dom_calls = stages[dom]
+    dom_bytes = stage_bytes.get(dom, 0)
+    achieved = (dom_bytes / dom_calls) / (dom_ms / dom_calls / 1e3) / 1e9 if dom_ms > 0 and dom_calls else 0.0
+    layer_bytes = byte_acc["total"] / prof_steps
+    layer_gbs = layer_bytes / (ms_step / 1e3) / 1e9
+    stage_report = {s: {"ms_per_call": (v[0] / v[1]) if v[1] else 0.0,
+                        "share": v[0] / max(1e-9, sum(x[0] for x in stages.values())),
+                        "gbs": (stage_bytes[s] / v[1]) / (v[0] / v[1] / 1e3) / 1e9
+                        if s in stage_bytes and v[0] > 0 else None}
+                    for s, v in stages.items() if v[1]}
+
+    # Sweep of the other batch sizes (device-timed, short).
+    sweep = {}
+    for b in batches:
+        steps_b = max(8, args.steps // 2)
+        timed_steps(torch, ctx, pool[b], outs[b], n_layers, b, 3, stream)
+        barrier()
+        ms_b = max_over_ranks(timed_steps(torch, ctx, pool[b], outs[b], n_layers, b, steps_b, stream))
+        ids_b = torch.empty((b, CFG["k"]), dtype=torch.int32, device="cuda")
+        tot = 0
+        for i in range(4):
+            ctx.moe_ffn_dev(i % n_layers, pool[b][i], outs[b][0], ids_b, None, n_tok=b)
+            tot += algorithmic_bytes(ids_b.cpu().numpy(), b)["total"]
+        per_ms = ms_b / steps_b
+        sweep[str(b)] = {"ms_per_step": per_ms, "tokens_per_s": world * b / (per_ms / 1e3),
+                         "hbm_gbs": (tot / 4) / (per_ms / 1e3) / 1e9,
+                         "hbm_frac": (tot / 4) / (per_ms / 1e3) / 1e9 / hbm_peak}
+
+    # End to end through the host-pointer C ABI call (pinned buffers).
+    hp = [torch.randn((B, d), generator=torch.Generator().manual_seed(i)).pin_memory().numpy()
+          for i in range(4)]
+    e2e_steps = max(4, args.steps // 2)
+    for i in range(3):
+        ctx.moe_ffn(i % n_layers, hp[i % 4])
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        ctx.moe_ffn(i % n_layers, hp[i % 4])
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_value = world * B * e2e_steps / e2e_s
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rate, calls, el = cpu_oracle_rate(host0, B, args.cpu_seconds, threads)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"{calls} calls of layer 0 at B={B} ({el:.1f} s), oracle restatement of Kestrel's "
+                         f"AVX2 path on all host threads"}
+
+    if rank == 0:
+        line = {
+            "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4k/f32", "data": "synthetic",
+            "config": {"workload": CFG["name"], "batch_tokens": B, "d_model": CFG["d"], "experts": CFG["E"],
+                       "top_k": CFG["k"], "expert_ff": CFG["ff"], "quant": "Q4_K gate/up + Q6_K down",
+                       "layers_rotated": n_layers, "l2": "inputs larger than L2 (48 distinct layers, 18.8 GB)",
+                       "parallelism": "replicas" if world > 1 else "single"},
+            "layer_hbm": {"bytes_per_step": layer_bytes, "gbs": layer_gbs, "frac": layer_gbs / hbm_peak,
+                          "peak": hbm_peak, "peak_kind": peak_kind},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": None, "peak_kind": peak_kind},
+            "stages": stage_report,
+            "sweep": sweep,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": B * d * 4,
+                    "d2h_bytes_per_step": B * d * 4 + B * CFG["k"] * 8},
+            "gpu_launches": args.steps * 10,  # kernels per kc_moe_ffn_dev call
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=48)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--sweep", type=lambda s: [int(x) for x in s.split(",") if x], default=[1, 16, 128, 512])
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,193 @@
+/*
+ * kestrel_cuda.h -- C ABI of the B200 (sm_100a) MoE FFN backend for Kestrel.
+ *
+ * The boundary a Kestrel host (Rust `extern "C"` crate, C++ or Python ctypes)
+ * crosses to run the Mixture-of-Experts FFN hot path on an NVIDIA B200. Plain
+ * pointers and sizes only; every entry point returns a kc_status (0 = OK) and
+ * never unwinds across the ABI. The message of the last failure is available
+ * from kc_last_error(). Reference interfaces replaced (paths are relative to
+ * the Kestrel repository, Eduardo7125/kestrel):
+ *
+ *   kc_init / kc_free        NativeSession::load's engine set-up
+ *                            (crates/kestrel-backends/src/lib.rs:125-187)
+ *   kc_upload_experts        ExpertStore::preload_all + ExpertBuf::part
+ *                            (crates/kestrel-memory/src/expert.rs:620-641, 62-76)
+ *   kc_upload_router         the router tensor ffn_gate_inp.weight read through
+ *                            Lease::tensor (crates/kestrel-memory/src/store.rs:233)
+ *   kc_upload_dense          WeightStore::lease + Lease::tensor for a dense weight
+ *                            (crates/kestrel-memory/src/store.rs:233-244, 400-470)
+ *   kc_moe_ffn[_dev]         Transformer::moe_ffn with Transformer::route inside
+ *                            (crates/kestrel-engine/src/transformer.rs:513-589, 472-496)
+ *   kc_matmul[_dev]          quant::matmul (crates/kestrel-engine/src/quant.rs:229-339)
+ *   kc_q8k_quantize_dev      Q8KRow::quantize (crates/kestrel-engine/src/qdot.rs:347-367)
+ *   kc_q8_quantize_dev       Q8Row::quantize (crates/kestrel-engine/src/qdot.rs:29-49)
+ *   kc_route_dev             Transformer::route (transformer.rs:472-496)
+ *   kc_block_sums_dev        the per-superblock integer sums of avx2::dot_q4_k_8k /
+ *                            dot_q6_k_8k (crates/kestrel-engine/src/avx2.rs:351-419)
+ *   kc_last_error            EngineError's message (transformer.rs:15-27)
+ *
+ * Threading: a context is used by one host thread at a time (the reference's
+ * Transformer is `&mut self` per forward, transformer.rs:278). One context per
+ * GPU; for expert parallelism one process per GPU, each with its own context.
+ *
+ * `*_dev` entry points take device pointers and enqueue work on the context's
+ * stream without synchronising; the others take host pointers, copy in, run,
+ * copy out and synchronise.
+ */
+#ifndef KESTREL_CUDA_H
+#define KESTREL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KC_API __attribute__((visibility("default")))
+#else
+#define KC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct kc_ctx kc_ctx;
+
+/* Status codes. Shapes and types are checked before any work is enqueued. */
+enum {
+  KC_OK = 0,
+  KC_ERR_ARG = 1,     /* null pointer, bad layer/tensor id, bad option      */
+  KC_ERR_SHAPE = 2,   /* dimension not supported (block multiple, limits)   */
+  KC_ERR_TYPE = 3,    /* ggml type without a CUDA kernel                    */
+  KC_ERR_CUDA = 4,    /* a CUDA runtime call failed                         */
+  KC_ERR_NCCL = 5,    /* an NCCL call failed                                */
+  KC_ERR_TIMEOUT = 6, /* a kernel's bounded wait expired (device status)    */
+  KC_ERR_STATE = 7,   /* call out of order (e.g. layer not uploaded)        */
+  KC_ERR_OOM = 8      /* device allocation failed                           */
+};
+
+/* ggml type ids (crates/kestrel-gguf/src/types.rs:48-86) with CUDA kernels. */
+enum { KC_F32 = 0, KC_Q8_0 = 8, KC_Q4_K = 12, KC_Q6_K = 14 };
+
+/* ---- context ------------------------------------------------------------ */
+
+/* Create a context on CUDA device `device` with its own stream. */
+KC_API int kc_init(int device, kc_ctx** out);
+/* Free all device memory owned by the context (weights, workspace). */
+KC_API void kc_free(kc_ctx* ctx);
+/* Message of the last failed call on this context ("" if none). ctx may be
+   NULL for errors of kc_init. */
+KC_API const char* kc_last_error(const kc_ctx* ctx);
+/* Enqueue subsequent work on a caller-owned cudaStream_t (NULL: own stream). */
+KC_API int kc_set_stream(kc_ctx* ctx, void* cuda_stream);
+/* Size the workspace for up to `max_tokens` tokens per call (grows on demand
+   otherwise; call before capturing a CUDA graph). */
+KC_API int kc_reserve(kc_ctx* ctx, int max_tokens);
+/* Wait for all work on the context's stream; reports kernel timeouts. */
+KC_API int kc_sync(kc_ctx* ctx);
+/* Bytes of device memory held by the context (weights + workspace). */
+KC_API int64_t kc_device_bytes(const kc_ctx* ctx);
+
+/* ---- weights (HBM-resident expert table) ---------------------------------
+   Expert tensors are GGUF "stacked" tensors: expert e's gate/up rows start at
+   e * ff * bytes_for(t, d) and its down rows at e * d * bytes_for(t, ff)
+   (TensorInfo::slice_offset, crates/kestrel-gguf/src/lib.rs:183-189).
+   `src_on_device` = 1 when the pointers are device memory (e.g. weights made
+   on the GPU), 0 for host memory. The bytes are converted once into the
+   device layout the kernels read; the caller's buffers are not kept. */
+KC_API int kc_upload_experts(kc_ctx* ctx, int layer, int n_expert, int d, int ff, int t_gate, const void* gate,
+                      int t_up, const void* up, int t_down, const void* down, int src_on_device);
+/* Upload a subset of a layer's experts: stacked tensors holding `n_local`
+   experts whose global ids are first_expert .. first_expert+n_local-1
+   (expert-parallel sharding). */
+KC_API int kc_upload_experts_range(kc_ctx* ctx, int layer, int n_expert, int first_expert, int n_local, int d, int ff,
+                            int t_gate, const void* gate, int t_up, const void* up, int t_down, const void* down,
+                            int src_on_device);
+/* Router weights ffn_gate_inp.weight, F32 [n_expert, d], and the MoeInfo
+   routing options (crates/kestrel-model/src/lib.rs:103-117): top-k, whether
+   the selected weights are renormalised, and weights_scale (0 or 1 = none). */
+KC_API int kc_upload_router(kc_ctx* ctx, int layer, const float* router_w, int n_expert, int d, int k, int norm_topk,
+                     float weights_scale, int src_on_device);
+/* A dense weight [rows, cols] of type `t` addressed by `tensor_id`. */
+KC_API int kc_upload_dense(kc_ctx* ctx, int tensor_id, int t, const void* w, int64_t rows, int64_t cols,
+                    int src_on_device);
+
+/* ---- hot path ----------------------------------------------------------- */
+
+/* Transformer::moe_ffn for `layer`: h [n_tok, d] f32 -> out [n_tok, d] f32.
+   router_w may be NULL (use the uploaded router); otherwise it is a host F32
+   [E, d] matrix used for this call with the given k / norm_topk /
+   weights_scale. topk_ids [n_tok, k] / topk_w [n_tok, k] are optional outputs
+   (NULL to skip) in the reference's order (descending probability). Host
+   buffers; synchronous. */
+KC_API int kc_moe_ffn(kc_ctx* ctx, int layer, const float* h, int n_tok, const float* router_w, int n_expert, int k,
+               int norm_topk, float weights_scale, float* out, int32_t* topk_ids, float* topk_w);
+/* Same on device buffers, enqueued on the context stream (uploaded router). */
+KC_API int kc_moe_ffn_dev(kc_ctx* ctx, int layer, const float* h, int n_tok, float* out, int32_t* topk_ids,
+                   float* topk_w);
+
+/* quant::matmul for an uploaded dense tensor: x [n, cols] f32 -> out [n, rows]
+   f32, with the reference's dispatch on n (n < 4: int8 activations for
+   Q4_K/Q6_K/Q8_0; n >= 4: exact f32 arithmetic on dequantised weights). */
+KC_API int kc_matmul(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out);
+KC_API int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out);
+
+/* ---- building blocks on device buffers (tests, custom pipelines) ------- */
+
+/* Q8KRow::quantize of n_rows rows of `cols` floats (cols % 256 == 0):
+   q [n_rows, cols] int8, d [n_rows, cols/256] f32, bsums [n_rows, cols/16]. */
+KC_API int kc_q8k_quantize_dev(kc_ctx* ctx, const float* x, int64_t n_rows, int64_t cols, int8_t* q, float* d,
+                        int32_t* bsums);
+/* Q8Row::quantize (cols % 32 == 0): d [n_rows, cols/32], s16 [n_rows, cols/16]. */
+KC_API int kc_q8_quantize_dev(kc_ctx* ctx, const float* x, int64_t n_rows, int64_t cols, int8_t* q, float* d,
+                       int32_t* s16);
+/* Transformer::route on precomputed logits [n_tok, E]. */
+KC_API int kc_route_dev(kc_ctx* ctx, const float* logits, int n_tok, int n_expert, int k, int norm_topk,
+                 float weights_scale, int32_t* ids, float* w);
+/* Router logits with the reference's exact operation order (quant::matmul of
+   an F32 [E, d] weight): h [n_tok, d] -> logits [n_tok, E]. */
+KC_API int kc_router_logits_dev(kc_ctx* ctx, const float* router_w, int n_expert, int d, const float* h, int n_tok,
+                         float* logits);
+/* Per-superblock integer sums of a GGUF K-quant matrix [rows, cols] (raw GGUF
+   bytes on the device) against Q8_K activation rows: out [n_act, rows,
+   cols/256, 9] int32 = the eight 32-bit lanes of sumi and the min (Q4_K) or
+   offset (Q6_K) term of avx2::dot_q4_k_8k / dot_q6_k_8k. */
+KC_API int kc_block_sums_dev(kc_ctx* ctx, int t, const void* w, int64_t rows, int64_t cols, const int8_t* q,
+                      const int32_t* bsums, int n_act, int32_t* out);
+/* This library's deterministic quantizer (same rules as the Python one):
+   x [rows, cols] f32 -> GGUF bytes [rows, bytes_for(t, cols)]. */
+KC_API int kc_quantize_dev(kc_ctx* ctx, int t, const float* x, int64_t rows, int64_t cols, void* out);
+
+/* ---- profiling ---------------------------------------------------------
+   When enabled, kc_moe_ffn* records a CUDA event pair around each stage of
+   the layer on the context stream; kc_profile_read synchronises, returns the
+   milliseconds and call counts accumulated per stage since the previous read,
+   and resets them. Stage ids: */
+enum {
+  KC_STAGE_ROUTER_LOGITS = 0,
+  KC_STAGE_ROUTE = 1,
+  KC_STAGE_DISPATCH = 2,
+  KC_STAGE_QUANT_X = 3,
+  KC_STAGE_GATE_UP_INT8 = 4,
+  KC_STAGE_GATE_UP_F32 = 5,
+  KC_STAGE_QUANT_ACT = 6,
+  KC_STAGE_DOWN_INT8 = 7,
+  KC_STAGE_DOWN_F32 = 8,
+  KC_STAGE_COMBINE = 9,
+  KC_N_STAGES = 10
+};
+KC_API int kc_profile_enable(kc_ctx* ctx, int on);
+KC_API int kc_profile_read(kc_ctx* ctx, double* stage_ms, int64_t* stage_calls, int n_stages);
+
+/* ---- expert parallelism (one process per GPU, NCCL over NVLink) -------- */
+
+/* 128-byte NCCL unique id, created on one rank and shared by the host. */
+KC_API int kc_ep_unique_id(char out[128]);
+/* Join an expert-parallel group of `world` ranks; experts of every layer are
+   owned by rank e / (E / world) (contiguous blocks). */
+KC_API int kc_ep_init(kc_ctx* ctx, int rank, int world, const char uid[128]);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KESTREL_CUDA_H */

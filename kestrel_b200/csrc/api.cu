@@ -1,0 +1,830 @@
+// C ABI of the B200 MoE FFN backend (include/kestrel_cuda.h): the context, the
+// HBM-resident expert table, the workspace and the layer pipeline
+//   router logits -> route (top-k) -> dispatch (permute metadata)
+//   -> gate/up (+SwiGLU) -> down -> combine (un-permute)
+// behind Transformer::moe_ffn / quant::matmul's call surface.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "ep.h"
+#include "kernels.h"
+
+using namespace kc;
+
+namespace {
+
+struct Layer {
+  // Routed experts: expert e (global id) lives at (e - first_expert) in the
+  // stacked device buffers.
+  bool has_experts = false;
+  int n_expert = 0, first_expert = 0, n_local = 0, d = 0, ff = 0;
+  int t_gate = 0, t_up = 0, t_down = 0;
+  int64_t rs_gate = 0, rs_down = 0;  // device row strides
+  uint8_t* gate = nullptr;
+  uint8_t* up = nullptr;
+  uint8_t* down = nullptr;
+  // Router (ffn_gate_inp.weight) and MoeInfo options.
+  bool has_router = false;
+  float* router = nullptr;
+  int k = 0, norm_topk = 1;
+  float weights_scale = 0.f;
+};
+
+struct Dense {
+  int t = 0;
+  int64_t rows = 0, cols = 0, rs = 0;
+  uint8_t* w = nullptr;
+};
+
+// Workspace sized by (tokens, experts, k, d, ff); carved from one allocation.
+struct Work {
+  int T = 0, E = 0, K = 0, D = 0, F = 0;
+  void* arena = nullptr;
+  size_t bytes = 0;
+  float* logits = nullptr;
+  int* ids = nullptr;
+  float* w = nullptr;
+  int8_t* xq = nullptr;
+  float* xd = nullptr;
+  int32_t* xs = nullptr;
+  DispatchOut meta{};
+  float* act = nullptr;
+  int8_t* aq = nullptr;
+  float* ad = nullptr;
+  int32_t* as = nullptr;
+  float* y = nullptr;
+  float* h_in = nullptr;   // staging for host-pointer calls
+  float* out = nullptr;
+  float* router_tmp = nullptr;
+};
+
+}  // namespace
+
+// Per-stage CUDA event pairs (kc_profile_enable).
+struct Prof {
+  bool on = false;
+  struct Rec {
+    int stage;
+    cudaEvent_t a, b;
+  };
+  std::vector<cudaEvent_t> pool;
+  std::vector<Rec> recs;
+  cudaEvent_t take() {
+    if (pool.empty()) {
+      cudaEvent_t e;
+      cudaEventCreate(&e);
+      return e;
+    }
+    cudaEvent_t e = pool.back();
+    pool.pop_back();
+    return e;
+  }
+};
+
+struct kc_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  int* status = nullptr;  // device word written by kernels on timeout
+  std::string err;
+  std::map<int, Layer> layers;
+  std::map<int, Dense> dense;
+  Work ws;
+  int64_t weight_bytes = 0;
+  EpState ep;
+  Prof prof;
+};
+
+namespace {
+// Brackets one pipeline stage with an event pair when profiling is on.
+struct StageScope {
+  kc_ctx* c;
+  Prof::Rec r{};
+  StageScope(kc_ctx* ctx, int stage) : c(ctx) {
+    if (!c->prof.on) return;
+    r.stage = stage;
+    r.a = c->prof.take();
+    r.b = c->prof.take();
+    cudaEventRecord(r.a, c->stream);
+  }
+  ~StageScope() {
+    if (!c->prof.on) return;
+    cudaEventRecord(r.b, c->stream);
+    c->prof.recs.push_back(r);
+  }
+};
+}  // namespace
+
+namespace {
+
+thread_local std::string g_init_err;
+
+int fail(kc_ctx* c, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  else g_init_err = buf;
+  return code;
+}
+
+#define CK(call)                                                                         \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return fail(ctx, e_ == cudaErrorMemoryAllocation ? KC_ERR_OOM : KC_ERR_CUDA,       \
+                  "%s failed: %s", #call, cudaGetErrorString(e_));                       \
+  } while (0)
+
+#define CKL()                                                                            \
+  do {                                                                                   \
+    cudaError_t e_ = cudaGetLastError();                                                 \
+    if (e_ != cudaSuccess)                                                               \
+      return fail(ctx, KC_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e_)); \
+  } while (0)
+
+#define RC(call)                                \
+  do {                                          \
+    int r_ = (call);                            \
+    if (r_ != KC_OK) {                          \
+      if (ctx->err.empty()) ctx->err = #call;   \
+      return r_;                                \
+    }                                           \
+  } while (0)
+
+bool type_ok(int t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0; }
+bool is_k(int t) { return t == T_Q4_K || t == T_Q6_K; }
+
+size_t al(size_t v) { return (v + 255) & ~size_t(255); }
+
+// (Re)allocate the workspace so it holds at least the given dimensions.
+int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
+  Work& w = ctx->ws;
+  if (T <= w.T && E <= w.E && K <= w.K && D <= w.D && F <= w.F && w.arena) return KC_OK;
+  T = std::max(T, w.T);
+  E = std::max(E, w.E);
+  K = std::max(K, w.K);
+  D = std::max(D, w.D);
+  F = std::max(F, w.F);
+  T = std::max(T, 1);
+  E = std::max(E, 1);
+  K = std::max(K, 1);
+  D = std::max(D, 256);
+  F = std::max(F, 256);
+  const size_t A = (size_t)T * K;
+  std::vector<size_t> sz = {
+      (size_t)T * E * 4,                 // logits
+      A * 4, A * 4,                      // ids, w
+      (size_t)T * D, (size_t)T * (D / 32 + 1) * 4, (size_t)T * (D / 16 + 1) * 4,  // xq xd xs
+      (size_t)E * 4, (size_t)(E + 1) * 4, A * 4, A * 4, A * 4, (size_t)E * 4, (size_t)E * 4, 16,  // meta
+      A * F * 4,                         // act
+      A * F, A * (F / 32 + 1) * 4, A * (F / 16 + 1) * 4,  // aq ad as
+      A * D * 4,                         // y
+      (size_t)T * D * 4, (size_t)T * D * 4,  // h_in, out
+      (size_t)E * D * 4,                 // router_tmp
+  };
+  size_t total = 0;
+  for (size_t s : sz) total += al(s);
+  if (w.arena) {
+    CK(cudaStreamSynchronize(ctx->stream));
+    CK(cudaFree(w.arena));
+    w.arena = nullptr;
+  }
+  CK(cudaMalloc(&w.arena, total));
+  w.bytes = total;
+  w.T = T; w.E = E; w.K = K; w.D = D; w.F = F;
+  char* p = static_cast<char*>(w.arena);
+  size_t i = 0;
+  auto take = [&](void** dst) {
+    *dst = p;
+    p += al(sz[i++]);
+  };
+  take((void**)&w.logits);
+  take((void**)&w.ids);
+  take((void**)&w.w);
+  take((void**)&w.xq);
+  take((void**)&w.xd);
+  take((void**)&w.xs);
+  take((void**)&w.meta.counts);
+  take((void**)&w.meta.offsets);
+  take((void**)&w.meta.slot_tok);
+  take((void**)&w.meta.slot_w);
+  take((void**)&w.meta.tok_slot);
+  take((void**)&w.meta.small_list);
+  take((void**)&w.meta.large_list);
+  take((void**)&w.meta.n_lists);
+  take((void**)&w.act);
+  take((void**)&w.aq);
+  take((void**)&w.ad);
+  take((void**)&w.as);
+  take((void**)&w.y);
+  take((void**)&w.h_in);
+  take((void**)&w.out);
+  take((void**)&w.router_tmp);
+  return KC_OK;
+}
+
+int check_status(kc_ctx* ctx) {
+  int st = 0;
+  CK(cudaMemcpy(&st, ctx->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (st != 0) {
+    CK(cudaMemset(ctx->status, 0, sizeof(int)));
+    return fail(ctx, st, "a kernel reported status %d (bounded wait expired)", st);
+  }
+  return KC_OK;
+}
+
+// Copy `rows` rows of GGUF bytes (host or device) into the device layout.
+int upload_matrix(kc_ctx* ctx, int t, const void* src, int64_t rows, int64_t cols, uint8_t* dst, bool on_dev) {
+  const int64_t srb = gguf_row_bytes(t, cols), drs = dev_row_stride(t, cols);
+  if (on_dev) {
+    RC(launch_repack(t, src, rows, cols, dst, ctx->stream));
+    CKL();
+    return KC_OK;
+  }
+  // Host source: stage through a bounded device buffer (<= 64 MiB per chunk).
+  const int64_t chunk_rows = std::max<int64_t>(1, (64ll << 20) / std::max<int64_t>(srb, 1));
+  void* tmp = nullptr;
+  CK(cudaMalloc(&tmp, std::min(rows, chunk_rows) * srb));
+  for (int64_t r0 = 0; r0 < rows; r0 += chunk_rows) {
+    int64_t nr = std::min(chunk_rows, rows - r0);
+    cudaError_t e = cudaMemcpyAsync(tmp, static_cast<const uint8_t*>(src) + r0 * srb, nr * srb,
+                                    cudaMemcpyHostToDevice, ctx->stream);
+    int rc = e == cudaSuccess ? launch_repack(t, tmp, nr, cols, dst + r0 * drs, ctx->stream) : KC_ERR_CUDA;
+    if (rc == KC_OK) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess || rc != KC_OK) {
+      cudaFree(tmp);
+      return fail(ctx, KC_ERR_CUDA, "upload failed: %s", cudaGetErrorString(e));
+    }
+  }
+  CK(cudaFree(tmp));
+  return KC_OK;
+}
+
+GroupedArgs grouped_base(kc_ctx* ctx) {
+  GroupedArgs a{};
+  a.status = ctx->status;
+  return a;
+}
+
+}  // namespace
+
+namespace kc {
+int num_sms() {
+  static int dev = -1, sms = 0;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (cur != dev) {
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cur);
+    dev = cur;
+  }
+  return sms > 0 ? sms : 1;
+}
+}  // namespace kc
+
+// ---------------------------------------------------------------------------
+// Layer pipeline on device buffers. h/out [n_tok, d]; optional ids/w outputs.
+static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const float* h, int n_tok, float* out,
+                        int32_t* ids_out, float* w_out) {
+  const int E = L.n_expert, k = L.k, d = L.d, ff = L.ff;
+  RC(ensure_work(ctx, n_tok, E, k, d, ff));
+  Work& W = ctx->ws;
+  cudaStream_t st = ctx->stream;
+  if (n_tok == 0) return KC_OK;
+  // 1. router logits and top-k (Transformer::route).
+  {
+    StageScope ss(ctx, KC_STAGE_ROUTER_LOGITS);
+    launch_router_logits(router, d, E, d, h, n_tok, W.logits, st);
+    CKL();
+  }
+  {
+    StageScope ss(ctx, KC_STAGE_ROUTE);
+    launch_route(W.logits, n_tok, E, k, L.norm_topk, L.weights_scale, W.ids, W.w, st);
+    CKL();
+  }
+  if (ctx->ep.world > 1) {
+    return fail(ctx, KC_ERR_STATE, "expert-parallel layer execution is not available in this build");
+  } else {
+    // 2. dispatch metadata (permute).
+    {
+      StageScope ss(ctx, KC_STAGE_DISPATCH);
+      RC(launch_dispatch(W.ids, W.w, n_tok, k, E, W.meta, st));
+      CKL();
+    }
+    // 3. activations for the int8 path.
+    {
+      StageScope ss(ctx, KC_STAGE_QUANT_X);
+      if (is_k(L.t_gate)) launch_q8k_quantize(h, nullptr, n_tok, d, W.xq, W.xd, W.xs, st);
+      else launch_q8_quantize(h, nullptr, n_tok, d, W.xq, W.xd, W.xs, st);
+      CKL();
+    }
+    const int A = n_tok * k;
+    // 4. gate/up + SwiGLU -> act [slot, ff].
+    GroupedArgs g = grouped_base(ctx);
+    g.w0 = L.gate;
+    g.w1 = L.up;
+    g.expert_stride = (int64_t)ff * L.rs_gate;
+    g.expert_base = L.first_expert;
+    g.rows = ff;
+    g.cols = d;
+    g.row_stride = L.rs_gate;
+    g.type = L.t_gate;
+    g.offsets = W.meta.offsets;
+    g.slot_src = W.meta.slot_tok;
+    g.aq = W.xq;
+    g.ad = W.xd;
+    g.asum = W.xs;
+    g.af = h;
+    g.out = W.act;
+    g.out_stride = ff;
+    g.list = W.meta.small_list;
+    g.n_list = W.meta.n_lists;
+    const int max_small = std::min(E, A);
+    {
+      StageScope ss(ctx, KC_STAGE_GATE_UP_INT8);
+      RC(launch_grouped_int8(g, true, max_small * ceil_div(ff, 16), st));
+      CKL();
+    }
+    g.list = W.meta.large_list;
+    g.n_list = W.meta.n_lists + 1;
+    {
+      StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
+      RC(launch_grouped_f32(g, true, std::min(E, A / 4), n_tok, st));
+      CKL();
+    }
+    // 5. quantise act rows for the int8 down path.
+    {
+      StageScope ss(ctx, KC_STAGE_QUANT_ACT);
+      if (is_k(L.t_down)) launch_q8k_quantize(W.act, nullptr, A, ff, W.aq, W.ad, W.as, st);
+      else launch_q8_quantize(W.act, nullptr, A, ff, W.aq, W.ad, W.as, st);
+      CKL();
+    }
+    // 6. down -> y [slot, d].
+    GroupedArgs dn = grouped_base(ctx);
+    dn.w0 = L.down;
+    dn.expert_stride = (int64_t)d * L.rs_down;
+    dn.expert_base = L.first_expert;
+    dn.rows = d;
+    dn.cols = ff;
+    dn.row_stride = L.rs_down;
+    dn.type = L.t_down;
+    dn.offsets = W.meta.offsets;
+    dn.slot_src = nullptr;
+    dn.aq = W.aq;
+    dn.ad = W.ad;
+    dn.asum = W.as;
+    dn.af = W.act;
+    dn.out = W.y;
+    dn.out_stride = d;
+    dn.list = W.meta.small_list;
+    dn.n_list = W.meta.n_lists;
+    {
+      StageScope ss(ctx, KC_STAGE_DOWN_INT8);
+      RC(launch_grouped_int8(dn, false, max_small * ceil_div(d, 16), st));
+      CKL();
+    }
+    dn.list = W.meta.large_list;
+    dn.n_list = W.meta.n_lists + 1;
+    {
+      StageScope ss(ctx, KC_STAGE_DOWN_F32);
+      RC(launch_grouped_f32(dn, false, std::min(E, A / 4), n_tok, st));
+      CKL();
+    }
+    // 7. combine (un-permute, ascending expert id).
+    {
+      StageScope ss(ctx, KC_STAGE_COMBINE);
+      launch_combine(W.y, W.meta.tok_slot, W.ids, W.w, n_tok, k, d, out, st);
+      CKL();
+    }
+  }
+  if (ids_out) CK(cudaMemcpyAsync(ids_out, W.ids, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
+  if (w_out) CK(cudaMemcpyAsync(w_out, W.w, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
+  return KC_OK;
+}
+
+// ===========================================================================
+extern "C" {
+
+int kc_init(int device, kc_ctx** out) {
+  kc_ctx* ctx = nullptr;
+  if (!out) return fail(nullptr, KC_ERR_ARG, "kc_init: out is NULL");
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n)
+    return fail(nullptr, KC_ERR_CUDA, "kc_init: no CUDA device %d (%d visible)", device, n);
+  if (cudaSetDevice(device) != cudaSuccess) return fail(nullptr, KC_ERR_CUDA, "kc_init: cudaSetDevice failed");
+  cudaDeviceProp prop;
+  cudaGetDeviceProperties(&prop, device);
+  if (prop.major < 10) return fail(nullptr, KC_ERR_CUDA, "kc_init: device %d is sm_%d%d, kernels need sm_100a",
+                                   device, prop.major, prop.minor);
+  ctx = new kc_ctx();
+  ctx->device = device;
+  if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&ctx->status, sizeof(int)) != cudaSuccess ||
+      cudaMemset(ctx->status, 0, sizeof(int)) != cudaSuccess) {
+    delete ctx;
+    return fail(nullptr, KC_ERR_CUDA, "kc_init: stream/status allocation failed");
+  }
+  ctx->own_stream = true;
+  *out = ctx;
+  return KC_OK;
+}
+
+void kc_free(kc_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  ep_free(ctx->ep);
+  for (auto& [id, L] : ctx->layers) {
+    cudaFree(L.gate);
+    cudaFree(L.up);
+    cudaFree(L.down);
+    cudaFree(L.router);
+  }
+  for (auto& [id, D] : ctx->dense) cudaFree(D.w);
+  for (auto& r : ctx->prof.recs) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  for (auto e : ctx->prof.pool) cudaEventDestroy(e);
+  cudaFree(ctx->ws.arena);
+  cudaFree(ctx->status);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+const char* kc_last_error(const kc_ctx* ctx) { return ctx ? ctx->err.c_str() : g_init_err.c_str(); }
+
+int kc_set_stream(kc_ctx* ctx, void* s) {
+  if (!ctx) return KC_ERR_ARG;
+  if (ctx->own_stream && s) {
+    cudaStreamDestroy(ctx->stream);
+    ctx->own_stream = false;
+  }
+  if (s) ctx->stream = static_cast<cudaStream_t>(s);
+  else if (!ctx->own_stream) {
+    CK(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
+    ctx->own_stream = true;
+  }
+  return KC_OK;
+}
+
+int kc_reserve(kc_ctx* ctx, int max_tokens) {
+  if (!ctx || max_tokens < 0) return KC_ERR_ARG;
+  cudaSetDevice(ctx->device);
+  int E = 1, K = 1, D = 256, F = 256;
+  for (auto& [id, L] : ctx->layers) {
+    E = std::max(E, L.n_expert);
+    K = std::max(K, L.k);
+    D = std::max(D, L.d);
+    F = std::max(F, L.ff);
+  }
+  for (auto& [id, Dn] : ctx->dense) D = std::max<int>(D, (int)Dn.cols);
+  return ensure_work(ctx, max_tokens, E, K, D, F);
+}
+
+int kc_sync(kc_ctx* ctx) {
+  if (!ctx) return KC_ERR_ARG;
+  CK(cudaStreamSynchronize(ctx->stream));
+  return check_status(ctx);
+}
+
+int64_t kc_device_bytes(const kc_ctx* ctx) {
+  return ctx ? ctx->weight_bytes + (int64_t)ctx->ws.bytes : 0;
+}
+
+int kc_upload_experts_range(kc_ctx* ctx, int layer, int n_expert, int first_expert, int n_local, int d, int ff,
+                            int t_gate, const void* gate, int t_up, const void* up, int t_down, const void* down,
+                            int src_on_device) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!gate || !up || !down || n_expert <= 0 || n_local <= 0 || first_expert < 0 ||
+      first_expert + n_local > n_expert || d <= 0 || ff <= 0)
+    return fail(ctx, KC_ERR_ARG, "kc_upload_experts: bad arguments");
+  if (!type_ok(t_gate) || !type_ok(t_up) || !type_ok(t_down))
+    return fail(ctx, KC_ERR_TYPE, "kc_upload_experts: types %d/%d/%d (kernels: Q4_K, Q6_K, Q8_0)", t_gate, t_up,
+                t_down);
+  if (t_gate != t_up) return fail(ctx, KC_ERR_TYPE, "kc_upload_experts: gate and up types differ");
+  if (d % block_elems(t_gate) || ff % block_elems(t_down))
+    return fail(ctx, KC_ERR_SHAPE, "kc_upload_experts: d=%d / ff=%d not a block multiple", d, ff);
+  if (d % 256 || ff % 32) return fail(ctx, KC_ERR_SHAPE, "kc_upload_experts: d must be a multiple of 256");
+  cudaSetDevice(ctx->device);
+  Layer& L = ctx->layers[layer];
+  cudaFree(L.gate);
+  cudaFree(L.up);
+  cudaFree(L.down);
+  L.gate = L.up = L.down = nullptr;
+  L.has_experts = false;
+  if (L.has_router && L.n_expert != n_expert)
+    return fail(ctx, KC_ERR_SHAPE, "kc_upload_experts: %d experts but the router has %d", n_expert, L.n_expert);
+  L.n_expert = n_expert;
+  L.first_expert = first_expert;
+  L.n_local = n_local;
+  L.d = d;
+  L.ff = ff;
+  L.t_gate = t_gate;
+  L.t_up = t_up;
+  L.t_down = t_down;
+  L.rs_gate = dev_row_stride(t_gate, d);
+  L.rs_down = dev_row_stride(t_down, ff);
+  const int64_t gbytes = (int64_t)n_local * ff * L.rs_gate, dbytes = (int64_t)n_local * d * L.rs_down;
+  CK(cudaMalloc(&L.gate, gbytes));
+  CK(cudaMalloc(&L.up, gbytes));
+  CK(cudaMalloc(&L.down, dbytes));
+  ctx->weight_bytes += 2 * gbytes + dbytes;
+  RC(upload_matrix(ctx, t_gate, gate, (int64_t)n_local * ff, d, L.gate, src_on_device != 0));
+  RC(upload_matrix(ctx, t_up, up, (int64_t)n_local * ff, d, L.up, src_on_device != 0));
+  RC(upload_matrix(ctx, t_down, down, (int64_t)n_local * d, ff, L.down, src_on_device != 0));
+  CK(cudaStreamSynchronize(ctx->stream));
+  L.has_experts = true;
+  return KC_OK;
+}
+
+int kc_upload_experts(kc_ctx* ctx, int layer, int n_expert, int d, int ff, int t_gate, const void* gate, int t_up,
+                      const void* up, int t_down, const void* down, int src_on_device) {
+  return kc_upload_experts_range(ctx, layer, n_expert, 0, n_expert, d, ff, t_gate, gate, t_up, up, t_down, down,
+                                 src_on_device);
+}
+
+int kc_upload_router(kc_ctx* ctx, int layer, const float* router_w, int n_expert, int d, int k, int norm_topk,
+                     float weights_scale, int src_on_device) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!router_w || n_expert <= 0 || d <= 0 || k < 1 || k > 64 || k > n_expert || n_expert > 1024)
+    return fail(ctx, KC_ERR_ARG, "kc_upload_router: bad arguments (E=%d d=%d k=%d; k <= 64, E <= 1024)",
+                n_expert, d, k);
+  cudaSetDevice(ctx->device);
+  Layer& L = ctx->layers[layer];
+  if (L.has_experts && (L.n_expert != n_expert || L.d != d))
+    return fail(ctx, KC_ERR_SHAPE, "kc_upload_router: shape [%d, %d] does not match the experts [%d, %d]",
+                n_expert, d, L.n_expert, L.d);
+  cudaFree(L.router);
+  L.router = nullptr;
+  CK(cudaMalloc(&L.router, (size_t)n_expert * d * 4));
+  CK(cudaMemcpyAsync(L.router, router_w, (size_t)n_expert * d * 4,
+                     src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  ctx->weight_bytes += (int64_t)n_expert * d * 4;
+  L.has_router = true;
+  L.n_expert = n_expert;
+  L.d = d;
+  L.k = k;
+  L.norm_topk = norm_topk ? 1 : 0;
+  L.weights_scale = weights_scale;
+  return KC_OK;
+}
+
+int kc_upload_dense(kc_ctx* ctx, int tensor_id, int t, const void* w, int64_t rows, int64_t cols,
+                    int src_on_device) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!w || rows <= 0 || cols <= 0) return fail(ctx, KC_ERR_ARG, "kc_upload_dense: bad arguments");
+  if (!type_ok(t) && t != T_F32) return fail(ctx, KC_ERR_TYPE, "kc_upload_dense: type %d has no kernel", t);
+  if (cols % block_elems(t)) return fail(ctx, KC_ERR_SHAPE, "kc_upload_dense: cols %lld", (long long)cols);
+  cudaSetDevice(ctx->device);
+  Dense& D = ctx->dense[tensor_id];
+  cudaFree(D.w);
+  D.t = t;
+  D.rows = rows;
+  D.cols = cols;
+  D.rs = dev_row_stride(t, cols);
+  CK(cudaMalloc(&D.w, rows * D.rs));
+  ctx->weight_bytes += rows * D.rs;
+  RC(upload_matrix(ctx, t, w, rows, cols, D.w, src_on_device != 0));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return KC_OK;
+}
+
+int kc_moe_ffn_dev(kc_ctx* ctx, int layer, const float* h, int n_tok, float* out, int32_t* topk_ids,
+                   float* topk_w) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  auto it = ctx->layers.find(layer);
+  if (it == ctx->layers.end() || !it->second.has_experts || !it->second.has_router)
+    return fail(ctx, KC_ERR_STATE, "kc_moe_ffn: layer %d has no uploaded experts and router", layer);
+  if (n_tok < 0 || (n_tok > 0 && (!h || !out))) return fail(ctx, KC_ERR_ARG, "kc_moe_ffn: bad buffers");
+  const Layer& L = it->second;
+  if (ctx->ep.world <= 1 && L.n_local != L.n_expert)
+    return fail(ctx, KC_ERR_STATE, "kc_moe_ffn: layer %d holds a shard of the experts but no expert-parallel "
+                                   "group was joined (kc_ep_init)", layer);
+  cudaSetDevice(ctx->device);
+  return moe_pipeline(ctx, L, L.router, h, n_tok, out, topk_ids, topk_w);
+}
+
+int kc_moe_ffn(kc_ctx* ctx, int layer, const float* h, int n_tok, const float* router_w, int n_expert, int k,
+               int norm_topk, float weights_scale, float* out, int32_t* topk_ids, float* topk_w) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  auto it = ctx->layers.find(layer);
+  if (it == ctx->layers.end() || !it->second.has_experts)
+    return fail(ctx, KC_ERR_STATE, "kc_moe_ffn: layer %d has no uploaded experts", layer);
+  if (n_tok < 0 || (n_tok > 0 && (!h || !out))) return fail(ctx, KC_ERR_ARG, "kc_moe_ffn: bad buffers");
+  cudaSetDevice(ctx->device);
+  Layer L = it->second;
+  if (router_w) {
+    if (n_expert != L.n_expert || k < 1 || k > 64 || k > n_expert)
+      return fail(ctx, KC_ERR_ARG, "kc_moe_ffn: router [%d] / k=%d do not fit the layer's %d experts", n_expert,
+                  k, L.n_expert);
+    L.k = k;
+    L.norm_topk = norm_topk ? 1 : 0;
+    L.weights_scale = weights_scale;
+  } else if (!L.has_router) {
+    return fail(ctx, KC_ERR_STATE, "kc_moe_ffn: no router uploaded for layer %d and none given", layer);
+  }
+  if (ctx->ep.world <= 1 && L.n_local != L.n_expert)
+    return fail(ctx, KC_ERR_STATE, "kc_moe_ffn: layer %d holds a shard of the experts", layer);
+  RC(ensure_work(ctx, n_tok, L.n_expert, L.k, L.d, L.ff));
+  Work& W = ctx->ws;
+  const float* router = L.router;
+  if (router_w) {
+    CK(cudaMemcpyAsync(W.router_tmp, router_w, (size_t)L.n_expert * L.d * 4, cudaMemcpyHostToDevice,
+                       ctx->stream));
+    router = W.router_tmp;
+  }
+  if (n_tok > 0) CK(cudaMemcpyAsync(W.h_in, h, (size_t)n_tok * L.d * 4, cudaMemcpyHostToDevice, ctx->stream));
+  // ids / w land in the workspace; copied out below.
+  RC(moe_pipeline(ctx, L, router, W.h_in, n_tok, W.out, nullptr, nullptr));
+  if (n_tok > 0) CK(cudaMemcpyAsync(out, W.out, (size_t)n_tok * L.d * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (topk_ids && n_tok > 0)
+    CK(cudaMemcpyAsync(topk_ids, W.ids, (size_t)n_tok * L.k * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (topk_w && n_tok > 0)
+    CK(cudaMemcpyAsync(topk_w, W.w, (size_t)n_tok * L.k * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return check_status(ctx);
+}
+
+int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  auto it = ctx->dense.find(tensor_id);
+  if (it == ctx->dense.end()) return fail(ctx, KC_ERR_STATE, "kc_matmul: tensor %d not uploaded", tensor_id);
+  if (n < 0 || (n > 0 && (!x || !out))) return fail(ctx, KC_ERR_ARG, "kc_matmul: bad buffers");
+  const Dense& D = it->second;
+  cudaSetDevice(ctx->device);
+  if (n == 0) return KC_OK;
+  cudaStream_t st = ctx->stream;
+  if (D.t == T_F32) {
+    launch_router_logits(reinterpret_cast<const float*>(D.w), D.rs / 4, (int)D.rows, (int)D.cols, x, n, out, st);
+    CKL();
+    return KC_OK;
+  }
+  RC(ensure_work(ctx, n, 1, 1, (int)std::min<int64_t>(D.cols, 1 << 30), 256));
+  Work& W = ctx->ws;
+  launch_dense_meta(n, W.meta, st);
+  CKL();
+  GroupedArgs a = grouped_base(ctx);
+  a.w0 = D.w;
+  a.expert_stride = 0;
+  a.expert_base = 0;
+  a.rows = (int)D.rows;
+  a.cols = (int)D.cols;
+  a.row_stride = D.rs;
+  a.type = D.t;
+  a.offsets = W.meta.offsets;
+  a.slot_src = nullptr;
+  a.af = x;
+  a.out = out;
+  a.out_stride = D.rows;
+  if (n < 4) {
+    if (is_k(D.t)) launch_q8k_quantize(x, nullptr, n, D.cols, W.xq, W.xd, W.xs, st);
+    else launch_q8_quantize(x, nullptr, n, D.cols, W.xq, W.xd, W.xs, st);
+    CKL();
+    a.aq = W.xq;
+    a.ad = W.xd;
+    a.asum = W.xs;
+    a.list = W.meta.small_list;
+    a.n_list = W.meta.n_lists;
+    RC(launch_grouped_int8(a, false, ceil_div(D.rows, 16), st));
+  } else {
+    a.list = W.meta.large_list;
+    a.n_list = W.meta.n_lists + 1;
+    RC(launch_grouped_f32(a, false, 1, n, st));
+  }
+  CKL();
+  return KC_OK;
+}
+
+int kc_matmul(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  auto it = ctx->dense.find(tensor_id);
+  if (it == ctx->dense.end()) return fail(ctx, KC_ERR_STATE, "kc_matmul: tensor %d not uploaded", tensor_id);
+  if (n <= 0) return n == 0 ? KC_OK : fail(ctx, KC_ERR_ARG, "kc_matmul: n < 0");
+  const Dense D = it->second;
+  cudaSetDevice(ctx->device);
+  // Stage x and out in the workspace's h_in/out buffers.
+  RC(ensure_work(ctx, n, 1, 1, (int)std::max(D.cols, D.rows), 256));
+  Work& W = ctx->ws;
+  CK(cudaMemcpyAsync(W.h_in, x, (size_t)n * D.cols * 4, cudaMemcpyHostToDevice, ctx->stream));
+  RC(kc_matmul_dev(ctx, tensor_id, W.h_in, n, W.out));
+  CK(cudaMemcpyAsync(out, W.out, (size_t)n * D.rows * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return check_status(ctx);
+}
+
+int kc_q8k_quantize_dev(kc_ctx* ctx, const float* x, int64_t n_rows, int64_t cols, int8_t* q, float* d,
+                        int32_t* bsums) {
+  if (!ctx) return KC_ERR_ARG;
+  if (cols % 256) return fail(ctx, KC_ERR_SHAPE, "kc_q8k_quantize: cols %% 256 != 0");
+  cudaSetDevice(ctx->device);
+  launch_q8k_quantize(x, nullptr, n_rows, cols, q, d, bsums, ctx->stream);
+  CKL();
+  return KC_OK;
+}
+
+int kc_q8_quantize_dev(kc_ctx* ctx, const float* x, int64_t n_rows, int64_t cols, int8_t* q, float* d,
+                       int32_t* s16) {
+  if (!ctx) return KC_ERR_ARG;
+  if (cols % 32) return fail(ctx, KC_ERR_SHAPE, "kc_q8_quantize: cols %% 32 != 0");
+  cudaSetDevice(ctx->device);
+  launch_q8_quantize(x, nullptr, n_rows, cols, q, d, s16, ctx->stream);
+  CKL();
+  return KC_OK;
+}
+
+int kc_route_dev(kc_ctx* ctx, const float* logits, int n_tok, int n_expert, int k, int norm_topk,
+                 float weights_scale, int32_t* ids, float* w) {
+  if (!ctx) return KC_ERR_ARG;
+  if (k < 1 || k > 64 || k > n_expert || n_expert > 1024) return fail(ctx, KC_ERR_ARG, "kc_route: bad k/E");
+  cudaSetDevice(ctx->device);
+  launch_route(logits, n_tok, n_expert, k, norm_topk, weights_scale, ids, w, ctx->stream);
+  CKL();
+  return KC_OK;
+}
+
+int kc_router_logits_dev(kc_ctx* ctx, const float* router_w, int n_expert, int d, const float* h, int n_tok,
+                         float* logits) {
+  if (!ctx) return KC_ERR_ARG;
+  cudaSetDevice(ctx->device);
+  launch_router_logits(router_w, d, n_expert, d, h, n_tok, logits, ctx->stream);
+  CKL();
+  return KC_OK;
+}
+
+int kc_block_sums_dev(kc_ctx* ctx, int t, const void* w, int64_t rows, int64_t cols, const int8_t* q,
+                      const int32_t* bsums, int n_act, int32_t* out) {
+  if (!ctx) return KC_ERR_ARG;
+  if (!is_k(t)) return fail(ctx, KC_ERR_TYPE, "kc_block_sums: K-quant types only");
+  if (cols % 256) return fail(ctx, KC_ERR_SHAPE, "kc_block_sums: cols %% 256 != 0");
+  cudaSetDevice(ctx->device);
+  launch_block_sums(t, w, rows, cols, q, bsums, n_act, out, ctx->stream);
+  CKL();
+  return KC_OK;
+}
+
+int kc_quantize_dev(kc_ctx* ctx, int t, const float* x, int64_t rows, int64_t cols, void* out) {
+  if (!ctx) return KC_ERR_ARG;
+  cudaSetDevice(ctx->device);
+  int rc = launch_quantize(t, x, rows, cols, out, ctx->stream);
+  if (rc != KC_OK) return fail(ctx, rc, "kc_quantize: type %d cols %lld", t, (long long)cols);
+  CKL();
+  return KC_OK;
+}
+
+int kc_profile_enable(kc_ctx* ctx, int on) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->prof.on = on != 0;
+  return KC_OK;
+}
+
+int kc_profile_read(kc_ctx* ctx, double* stage_ms, int64_t* stage_calls, int n_stages) {
+  if (!ctx || n_stages < 0) return KC_ERR_ARG;
+  cudaSetDevice(ctx->device);
+  CK(cudaStreamSynchronize(ctx->stream));
+  for (int i = 0; i < n_stages; ++i) {
+    if (stage_ms) stage_ms[i] = 0;
+    if (stage_calls) stage_calls[i] = 0;
+  }
+  for (auto& r : ctx->prof.recs) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, r.a, r.b);
+    if (r.stage < n_stages) {
+      if (stage_ms) stage_ms[r.stage] += ms;
+      if (stage_calls) stage_calls[r.stage] += 1;
+    }
+    ctx->prof.pool.push_back(r.a);
+    ctx->prof.pool.push_back(r.b);
+  }
+  ctx->prof.recs.clear();
+  return KC_OK;
+}
+
+int kc_ep_unique_id(char out[128]) { return ep_unique_id(out); }
+
+int kc_ep_init(kc_ctx* ctx, int rank, int world, const char uid[128]) {
+  if (!ctx) return KC_ERR_ARG;
+  cudaSetDevice(ctx->device);
+  int rc = ep_init(ctx->ep, rank, world, uid);
+  if (rc != KC_OK) return fail(ctx, rc, "kc_ep_init: %s", ep_last_error(ctx->ep));
+  return KC_OK;
+}
+
+}  // extern "C"

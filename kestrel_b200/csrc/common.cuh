@@ -1,0 +1,171 @@
+// Shared device helpers for the sm_100a MoE FFN kernels.
+//
+// The library is compiled with --fmad=false: nvcc may not contract a*b+c into
+// an FMA anywhere, exactly like Rust, which only fuses where Kestrel's kernels
+// call _mm256_fmadd_ps. Where the reference fuses, the kernels call
+// __fmaf_rn explicitly.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/kestrel_cuda.h"
+
+namespace kc {
+
+// ggml type ids with CUDA kernels (crates/kestrel-gguf/src/types.rs:48-86).
+enum : int { T_F32 = 0, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
+
+// ----------------------------------------------------------------------------
+// Device weight layouts. Q4_K rows keep the GGUF layout (144-byte superblocks
+// are 16-byte aligned). Q6_K (210-byte superblocks) and Q8_0 (34-byte blocks)
+// are stored "planar" per row so that every field starts on a 16-byte
+// boundary, with the row padded to a multiple of 16 bytes:
+//   Q6_K row: [ql 128*nb][qh 64*nb][scales 16*nb][d 2*nb][pad]
+//   Q8_0 row: [qs 32*nb][d 2*nb][pad]
+// The bytes are a permutation of GGUF's (plus row padding); the arithmetic on
+// them is unchanged.
+__host__ __device__ inline int64_t round16(int64_t v) { return (v + 15) & ~int64_t(15); }
+
+__host__ __device__ inline int64_t dev_row_stride(int t, int64_t cols) {
+  switch (t) {
+    case T_F32: return round16(cols * 4);
+    case T_Q8_0: return round16(cols / 32 * 34);
+    case T_Q4_K: return cols / 256 * 144;
+    case T_Q6_K: return round16(cols / 256 * 210);
+    default: return -1;
+  }
+}
+__host__ __device__ inline int64_t gguf_row_bytes(int t, int64_t cols) {
+  switch (t) {
+    case T_F32: return cols * 4;
+    case T_Q8_0: return cols / 32 * 34;
+    case T_Q4_K: return cols / 256 * 144;
+    case T_Q6_K: return cols / 256 * 210;
+    default: return -1;
+  }
+}
+inline int block_elems(int t) {
+  switch (t) {
+    case T_F32: return 1;
+    case T_Q8_0: return 32;
+    case T_Q4_K: case T_Q6_K: return 256;
+    default: return 0;
+  }
+}
+
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+  return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFF)));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Kernel-side error reporting: the first failure wins; the host reads the word
+// in kc_sync and maps it to a kc_status.
+__device__ __forceinline__ void report(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+// Limit for every spin-wait in this library: after it expires the waiting
+// thread records KC_ERR_TIMEOUT and stops waiting.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// ---- mbarrier -------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on a phase parity. Returns false (and records a timeout) if the
+// phase did not complete within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      report(status, KC_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+// ---- bulk async copy (TMA, non-tensor): global -> shared ------------------
+// Both addresses 16-byte aligned, size a multiple of 16 (checked by callers).
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---- Kestrel arithmetic helpers -------------------------------------------
+// scale_min_k4 (crates/kestrel-engine/src/quant.rs:54-60) for all eight
+// sub-blocks of a Q4_K superblock, from the 12 packed scale bytes held in
+// three little-endian words.
+__device__ __forceinline__ void q4k_scales(uint32_t w0, uint32_t w1, uint32_t w2, int sc[8], int mn[8]) {
+  // bytes q[0..3] = w0, q[4..7] = w1, q[8..11] = w2
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t qj = (w0 >> (8 * j)) & 0xFF, qj4 = (w1 >> (8 * j)) & 0xFF, qj8 = (w2 >> (8 * j)) & 0xFF;
+    sc[j] = qj & 63;
+    mn[j] = qj4 & 63;
+    sc[j + 4] = (qj8 & 0xF) | ((qj >> 6) << 4);
+    mn[j + 4] = (qj8 >> 4) | ((qj4 >> 6) << 4);
+  }
+}
+
+// hsum (avx2.rs:19-27) over the eight lanes held by eight consecutive threads
+// (lane j = thread j of the group): ((v0+v4)+(v2+v6)) + ((v1+v5)+(v3+v7)).
+// Valid in the group's first thread.
+__device__ __forceinline__ float hsum8_group(float v) {
+  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4, 8));
+  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2, 8));
+  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1, 8));
+  return v;
+}
+
+// Rust `x.round() as i32` then `.clamp(-127, 127)`: round half away from
+// zero, NaN -> 0, saturating.
+__device__ __forceinline__ int q8_round(float v) {
+  float r = roundf(v);
+  if (r != r) return 0;
+  r = fminf(fmaxf(r, -127.f), 127.f);
+  return (int)r;
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+}  // namespace kc

@@ -1,0 +1,71 @@
+// Host-side launchers of the library's kernels (one definition per .cu file).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kc {
+
+// Activation rows of a grouped product: slot i reads activation row
+// slot_src[i] (or i when slot_src is null).
+struct GroupedArgs {
+  const uint8_t* w0;      // weights of the expert(s), device layout
+  const uint8_t* w1;      // second matrix for the gate/up pair (or null)
+  int64_t expert_stride;  // bytes between consecutive experts' matrices
+  int expert_base;        // global id of the first expert held in w0 / w1
+  int rows, cols;         // one expert's matrix
+  int64_t row_stride;     // bytes per row (device layout)
+  int type;               // ggml type of w0 / w1
+  const int* list;        // expert ids to process
+  const int* n_list;      // device scalar: entries in list
+  const int* offsets;     // [E+1]: slots of expert e are offsets[e] .. offsets[e+1]-1
+  const int* slot_src;    // activation row of each slot (null: identity)
+  const int8_t* aq;       // quantised activations [n_act][cols] (int8 path)
+  const float* ad;        // their block scales
+  const int32_t* asum;    // their per-16 sums
+  const float* af;        // f32 activations [n_act][cols] (f32 path)
+  float* out;             // out[slot * out_stride + row]
+  int64_t out_stride;
+  int* status;            // device status word (timeouts)
+};
+
+// quantize.cu
+void launch_q8k_quantize(const float* x, const int* row_map, int64_t n_rows, int64_t cols, int8_t* q, float* d,
+                         int32_t* bsums, cudaStream_t st);
+void launch_q8_quantize(const float* x, const int* row_map, int64_t n_rows, int64_t cols, int8_t* q, float* d,
+                        int32_t* s16, cudaStream_t st);
+int launch_quantize(int t, const float* x, int64_t rows, int64_t cols, void* out, cudaStream_t st);
+int launch_repack(int t, const void* src, int64_t rows, int64_t cols, void* dst, cudaStream_t st);
+void launch_block_sums(int t, const void* w, int64_t rows, int64_t cols, const int8_t* q, const int32_t* bsums,
+                       int n_act, int32_t* out, cudaStream_t st);
+
+// router.cu
+void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int d, const float* h, int n_tok,
+                          float* logits, cudaStream_t st);
+void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
+                  float* w, cudaStream_t st);
+// Dispatch metadata of one routed batch (see router.cu).
+struct DispatchOut {
+  int* counts;     // [E]
+  int* offsets;    // [E+1]
+  int* slot_tok;   // [n_tok*k] token of each slot
+  float* slot_w;   // [n_tok*k] routing weight of each slot
+  int* tok_slot;   // [n_tok*k] slot of token s's j-th selection
+  int* small_list; // experts with 1..3 rows (int8 path)
+  int* large_list; // experts with >= 4 rows (f32 path)
+  int* n_lists;    // [2]: entries in small_list, large_list
+};
+int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st);
+// Metadata of a dense product: one group of n rows, slots = rows 0..n-1.
+void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st);
+void launch_combine(const float* y, const int* tok_slot, const int* ids, const float* w, int n_tok, int k, int d,
+                    float* out, cudaStream_t st);
+
+// grouped.cu
+int launch_grouped_int8(const GroupedArgs& a, bool pair, int max_units, cudaStream_t st);
+int launch_grouped_f32(const GroupedArgs& a, bool pair, int max_experts, int max_rows_per_expert,
+                       cudaStream_t st);
+
+int num_sms();
+
+}  // namespace kc

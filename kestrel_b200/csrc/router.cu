@@ -1,0 +1,332 @@
+// Router logits, softmax/top-k routing, dispatch metadata (the permute) and
+// the weighted combine (the un-permute).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace kc {
+
+// ---------------------------------------------------------------------------
+// Router logits = quant::matmul of the F32 router [E, d] with h [n_tok, d]
+// (crates/kestrel-engine/src/quant.rs:229-339), reproducing the reference's
+// operation order exactly so that the top-k selection is bit-exact:
+//   * n_tok < 4 (or d % 8 != 0): quant::dot (quant.rs:208-224) -- eight lane
+//     accumulators, separate mul and add, lanes folded in order from -0.0, then
+//     the scalar tail;
+//   * n_tok >= 4: avx2::gemm_f32 (avx2.rs:230-286) on 48-row tiles: rows in the
+//     tile's 3-row blocks and tokens in 4-token blocks use one 8-lane FMA chain
+//     per output + hsum; the other outputs use dot_f32 (avx2.rs:289-308), whose
+//     even 8-chunks feed acc0 and odd ones acc1, summed lane-wise before hsum.
+// Thread layout: 8 threads (one per lane) per expert row, 8 rows per block,
+// TS tokens per thread (each weight element loaded once for TS tokens).
+constexpr int RL_ROWS = 8, RL_TS = 4;
+
+__global__ void __launch_bounds__(RL_ROWS * 8) router_logits_kernel(const float* __restrict__ w, int64_t ws,
+                                                                    int E, int d, const float* __restrict__ h,
+                                                                    int n_tok, float* __restrict__ logits) {
+  const int j = threadIdx.x & 7;
+  const int e = blockIdx.x * RL_ROWS + (threadIdx.x >> 3);
+  const int s0 = blockIdx.y * RL_TS;
+  const bool gemm = n_tok >= 4 && (d % 8) == 0;
+  const int n8 = d / 8 * 8;
+  const bool e_ok = e < E;
+  const int ee = e_ok ? e : E - 1;
+  // Method per token: 0 = lane chain, 1 = dot_f32, 2 = scalar dot.
+  int method[RL_TS];
+  int ntok_here = min(RL_TS, n_tok - s0);
+  {
+    int tile = ee / 48, trows = min(48, E - tile * 48), rows3 = trows / 3 * 3;
+    bool row_blocked = (ee - tile * 48) < rows3;
+#pragma unroll
+    for (int t = 0; t < RL_TS; ++t) {
+      int s = s0 + t;
+      method[t] = !gemm ? 2 : (row_blocked && s < n_tok / 4 * 4) ? 0 : 1;
+    }
+  }
+  float a0[RL_TS], a1[RL_TS];
+#pragma unroll
+  for (int t = 0; t < RL_TS; ++t) a0[t] = a1[t] = 0.f;
+  const float* wr = w + (int64_t)ee * ws;
+  for (int c = 0, chunk = 0; c < n8; c += 8, ++chunk) {
+    float wv = wr[c + j];
+#pragma unroll
+    for (int t = 0; t < RL_TS; ++t) {
+      if (t >= ntok_here) break;
+      float xv = h[(int64_t)(s0 + t) * d + c + j];
+      if (method[t] == 0) {
+        a0[t] = __fmaf_rn(wv, xv, a0[t]);
+      } else if (method[t] == 1) {
+        if (chunk & 1) a1[t] = __fmaf_rn(wv, xv, a1[t]);
+        else a0[t] = __fmaf_rn(wv, xv, a0[t]);
+      } else {
+        a0[t] = __fadd_rn(a0[t], __fmul_rn(wv, xv));
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < RL_TS; ++t) {
+    if (t >= ntok_here) break;
+    float v;
+    if (method[t] == 2) {
+      // Sequential fold of the eight lanes from -0.0, then the tail.
+      float s = -0.0f;
+#pragma unroll
+      for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(0xffffffffu, a0[t], l, 8));
+      for (int c = n8; c < d; ++c) s = __fadd_rn(s, __fmul_rn(wr[c], h[(int64_t)(s0 + t) * d + c]));
+      v = s;
+    } else {
+      float lanev = method[t] == 1 ? __fadd_rn(a0[t], a1[t]) : a0[t];
+      v = hsum8_group(lanev);
+    }
+    if (j == 0 && e_ok) logits[(int64_t)(s0 + t) * E + e] = v;
+  }
+}
+
+void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int d, const float* h, int n_tok,
+                          float* logits, cudaStream_t st) {
+  if (n_tok <= 0) return;
+  dim3 grid(ceil_div(E, RL_ROWS), ceil_div(n_tok, RL_TS));
+  router_logits_kernel<<<grid, RL_ROWS * 8, 0, st>>>(w, row_stride_floats, E, d, h, n_tok, logits);
+}
+
+// ---------------------------------------------------------------------------
+// Transformer::route (transformer.rs:472-496): softmax with the sequential
+// sum, stable descending order (ties to the lower index), top-k, optional
+// renormalisation by the selection's sequential sum clamped at 2^-14, and
+// optional weights_scale. One warp per token; p lives in shared memory.
+constexpr int RT_WARPS = 4;
+
+__global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __restrict__ logits, int n_tok, int E,
+                                                               int k, int norm_topk, float weights_scale,
+                                                               int* __restrict__ ids, float* __restrict__ wout) {
+  extern __shared__ float sp[];  // [RT_WARPS][E]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int s = blockIdx.x * RT_WARPS + warp;
+  if (s >= n_tok) return;
+  float* p = sp + warp * E;
+  const float* row = logits + (int64_t)s * E;
+  float m = -INFINITY;
+  for (int e = lane; e < E; e += 32) m = fmaxf(m, row[e]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  for (int e = lane; e < E; e += 32) p[e] = expf(__fsub_rn(row[e], m));
+  __syncwarp();
+  float sum = -0.0f;
+  if (lane == 0)
+    for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, p[e]);
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  for (int e = lane; e < E; e += 32) p[e] = __fdiv_rn(p[e], sum);
+  __syncwarp();
+  // Top-k by repeated arg-max (larger p first, ties to the lower index, which
+  // is the first k of the reference's stable sort). Probabilities are >= 0, so
+  // a taken entry is marked with -1 in shared memory.
+  constexpr int NONE = 0x7fffffff;
+  float selw[64];
+  int seli[64];
+  for (int r = 0; r < k; ++r) {
+    float bp = 0.f;
+    int bi = NONE;
+    for (int e = lane; e < E; e += 32) {
+      float v = p[e];
+      if (v < 0.f) continue;
+      if (bi == NONE || v > bp || (v == bp && e < bi)) {
+        bp = v;
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      float op = __shfl_xor_sync(0xffffffffu, bp, o);
+      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (oi != NONE && (bi == NONE || op > bp || (op == bp && oi < bi))) {
+        bp = op;
+        bi = oi;
+      }
+    }
+    seli[r] = bi;
+    selw[r] = bp;
+    __syncwarp();
+    if (bi != NONE && lane == (bi & 31)) p[bi] = -1.f;
+    __syncwarp();
+  }
+  if (lane == 0) {
+    if (norm_topk) {
+      float ss = -0.0f;
+      for (int r = 0; r < k; ++r) ss = __fadd_rn(ss, selw[r]);
+      ss = fmaxf(ss, 6.1035156e-5f);
+      for (int r = 0; r < k; ++r) selw[r] = __fdiv_rn(selw[r], ss);
+    }
+    if (weights_scale != 0.f && weights_scale != 1.f)
+      for (int r = 0; r < k; ++r) selw[r] = __fmul_rn(selw[r], weights_scale);
+    for (int r = 0; r < k; ++r) {
+      ids[(int64_t)s * k + r] = seli[r];
+      wout[(int64_t)s * k + r] = selw[r];
+    }
+  }
+}
+
+void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
+                  float* w, cudaStream_t st) {
+  if (n_tok <= 0) return;
+  size_t smem = (size_t)RT_WARPS * E * sizeof(float);
+  route_kernel<<<ceil_div(n_tok, RT_WARPS), RT_WARPS * 32, smem, st>>>(logits, n_tok, E, k, norm_topk,
+                                                                       weights_scale, ids, w);
+}
+
+// ---------------------------------------------------------------------------
+// Dispatch (the permute of transformer.rs:525-551 as metadata): slots are
+// grouped by expert in ascending expert id, and within an expert by ascending
+// token -- the order of the reference's BTreeMap<expert, Vec<(token, w)>>.
+// One block of 1024 threads. Tokens are ranked inside each warp with a
+// per-expert bitmask of the warp's tokens (popc of the lower lanes), and
+// across warps and rounds with per-expert running bases.
+constexpr int DP_THREADS = 1024;
+
+__global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restrict__ ids,
+                                                               const float* __restrict__ w, int n_tok, int k, int E,
+                                                               DispatchOut o) {
+  extern __shared__ uint32_t dsm[];
+  uint32_t* mask = dsm;                                // [32][E]
+  int* pref = reinterpret_cast<int*>(dsm + 32 * E);    // [32][E]
+  int* cnt = pref + 32 * E;                            // [E]
+  int* base = cnt + E;                                 // [E]
+  int* offs = base + E;                                // [E+1]
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid & 31;
+  for (int e = tid; e < E; e += DP_THREADS) {
+    cnt[e] = 0;
+    base[e] = 0;
+  }
+  __syncthreads();
+  const int64_t A = (int64_t)n_tok * k;
+  for (int64_t i = tid; i < A; i += DP_THREADS) {
+    const int e = ids[i];
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0, ns = 0, nl = 0;
+    for (int e = 0; e < E; ++e) {
+      offs[e] = run;
+      o.offsets[e] = run;
+      o.counts[e] = cnt[e];
+      run += cnt[e];
+      if (cnt[e] >= 1 && cnt[e] <= 3) o.small_list[ns++] = e;
+      else if (cnt[e] >= 4) o.large_list[nl++] = e;
+    }
+    offs[E] = run;
+    o.offsets[E] = run;
+    o.n_lists[0] = ns;
+    o.n_lists[1] = nl;
+  }
+  __syncthreads();
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int r0 = 0; r0 < n_tok; r0 += DP_THREADS) {
+    for (int i = tid; i < 32 * E; i += DP_THREADS) mask[i] = 0u;
+    __syncthreads();
+    const int s = r0 + tid;
+    if (s < n_tok)
+      for (int j = 0; j < k; ++j) {
+        const int e = ids[(int64_t)s * k + j];
+        if (e >= 0 && e < E) atomicOr(&mask[warp * E + e], 1u << lane);
+      }
+    __syncthreads();
+    for (int e = tid; e < E; e += DP_THREADS) {
+      int run = base[e];
+      for (int wv = 0; wv < 32; ++wv) {
+        pref[wv * E + e] = run;
+        run += __popc(mask[wv * E + e]);
+      }
+      base[e] = run;
+    }
+    __syncthreads();
+    if (s < n_tok)
+      for (int j = 0; j < k; ++j) {
+        int64_t i = (int64_t)s * k + j;
+        int e = ids[i];
+        if (e < 0 || e >= E) {
+          o.tok_slot[i] = 0;
+          continue;
+        }
+        int slot = offs[e] + pref[warp * E + e] + __popc(mask[warp * E + e] & lt);
+        o.slot_tok[slot] = s;
+        o.slot_w[slot] = w[i];
+        o.tok_slot[i] = slot;
+      }
+    __syncthreads();
+  }
+}
+
+int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st) {
+  size_t smem = (size_t)(64 * E + 3 * E + 1) * 4;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr_set = true;
+  }
+  if (smem > 200 * 1024) return KC_ERR_SHAPE;
+  dispatch_kernel<<<1, DP_THREADS, smem, st>>>(ids, w, n_tok, k, E, o);
+  return KC_OK;
+}
+
+// One group (expert 0) holding rows 0..n-1: the metadata of a dense product.
+__global__ void dense_meta_kernel(int n, DispatchOut o) {
+  o.counts[0] = n;
+  o.offsets[0] = 0;
+  o.offsets[1] = n;
+  o.small_list[0] = 0;
+  o.large_list[0] = 0;
+  o.n_lists[0] = (n >= 1 && n <= 3) ? 1 : 0;
+  o.n_lists[1] = n >= 4 ? 1 : 0;
+}
+
+void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st) { dense_meta_kernel<<<1, 1, 0, st>>>(n, o); }
+
+// ---------------------------------------------------------------------------
+// Combine (transformer.rs:566-570): out[s] = sum over the token's experts in
+// ascending expert id of w * y, each step a separate multiply and add, from
+// +0.0. One block per token.
+__global__ void combine_kernel(const float* __restrict__ y, const int* __restrict__ tok_slot,
+                               const int* __restrict__ ids, const float* __restrict__ w, int k, int d,
+                               float* __restrict__ out) {
+  __shared__ int se[64], ss[64];
+  __shared__ float sw[64];
+  const int s = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int n = 0;
+    for (int j = 0; j < k; ++j) {
+      int e = ids[(int64_t)s * k + j];
+      int slot = tok_slot[(int64_t)s * k + j];
+      float wj = w[(int64_t)s * k + j];
+      int p = n++;
+      while (p > 0 && se[p - 1] > e) {
+        se[p] = se[p - 1];
+        ss[p] = ss[p - 1];
+        sw[p] = sw[p - 1];
+        --p;
+      }
+      se[p] = e;
+      ss[p] = slot;
+      sw[p] = wj;
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x * 4; c < d; c += blockDim.x * 4) {
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < k; ++j) {
+      float4 v = *reinterpret_cast<const float4*>(y + (int64_t)ss[j] * d + c);
+      float wj = sw[j];
+      o.x = __fadd_rn(o.x, __fmul_rn(wj, v.x));
+      o.y = __fadd_rn(o.y, __fmul_rn(wj, v.y));
+      o.z = __fadd_rn(o.z, __fmul_rn(wj, v.z));
+      o.w = __fadd_rn(o.w, __fmul_rn(wj, v.w));
+    }
+    *reinterpret_cast<float4*>(out + (int64_t)s * d + c) = o;
+  }
+}
+
+void launch_combine(const float* y, const int* tok_slot, const int* ids, const float* w, int n_tok, int k, int d,
+                    float* out, cudaStream_t st) {
+  if (n_tok <= 0) return;
+  combine_kernel<<<n_tok, 256, 0, st>>>(y, tok_slot, ids, w, k, d, out);
+}
+
+}  // namespace kc

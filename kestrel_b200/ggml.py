@@ -78,9 +78,10 @@ def _f16_round(v: np.ndarray) -> np.ndarray:
 
 
 def _safe_div(num: np.ndarray, den: np.ndarray) -> np.ndarray:
-    with np.errstate(divide="ignore", invalid="ignore"):
-        q = (num / np.where(den > 0, den, np.float32(1))).astype(np.float32)
-    return np.where(den > 0, q, np.float32(0)).astype(np.float32)
+    """num / den (IEEE float32) where den > 0, else 0."""
+    out = np.zeros(np.broadcast_shapes(num.shape, den.shape), np.float32)
+    np.divide(num, den, out=out, where=den > 0)
+    return out
 
 
 def quantize_q8_0(x: np.ndarray) -> np.ndarray:
