@@ -245,7 +245,10 @@ def run_ours(args):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     ctx = Context(local)
-    stream = torch.cuda.current_stream()
+    # A dedicated (non-default) stream shared by torch and the library, so the
+    # CUDA events bracket the library's kernels.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
     n_layers = args.layers
     host0 = make_layers(ctx, torch, n_layers, seed=rank * 1000)

@@ -77,7 +77,8 @@ KC_API void kc_free(kc_ctx* ctx);
 /* Message of the last failed call on this context ("" if none). ctx may be
    NULL for errors of kc_init. */
 KC_API const char* kc_last_error(const kc_ctx* ctx);
-/* Enqueue subsequent work on a caller-owned cudaStream_t (NULL: own stream). */
+/* Enqueue subsequent work on a caller-owned cudaStream_t (NULL = the legacy
+   default stream). The context's own stream is used until this is called. */
 KC_API int kc_set_stream(kc_ctx* ctx, void* cuda_stream);
 /* Size the workspace for up to `max_tokens` tokens per call (grows on demand
    otherwise; call before capturing a CUDA graph). */

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "decode.h"
 #include "ep.h"
 #include "kernels.h"
 
@@ -25,7 +26,7 @@ struct Layer {
   bool has_experts = false;
   int n_expert = 0, first_expert = 0, n_local = 0, d = 0, ff = 0;
   int t_gate = 0, t_up = 0, t_down = 0;
-  int64_t rs_gate = 0, rs_down = 0;  // device row strides
+  int64_t mb_gate = 0, mb_down = 0;  // device bytes of one expert's gate (= up) / down matrix
   uint8_t* gate = nullptr;
   uint8_t* up = nullptr;
   uint8_t* down = nullptr;
@@ -38,7 +39,7 @@ struct Layer {
 
 struct Dense {
   int t = 0;
-  int64_t rows = 0, cols = 0, rs = 0;
+  int64_t rows = 0, cols = 0, rs = 0;  // rs: F32 row stride (bytes)
   uint8_t* w = nullptr;
 };
 
@@ -53,7 +54,11 @@ struct Work {
   int8_t* xq = nullptr;
   float* xd = nullptr;
   int32_t* xs = nullptr;
+  uint8_t* xrec = nullptr;  // activation records of the input rows
   DispatchOut meta{};
+  float* g = nullptr;       // gate / up outputs per slot
+  float* u = nullptr;
+  uint8_t* arec = nullptr;  // activation records of SwiGLU(g, u) per slot
   float* act = nullptr;
   int8_t* aq = nullptr;
   float* ad = nullptr;
@@ -164,6 +169,11 @@ bool type_ok(int t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0; }
 bool is_k(int t) { return t == T_Q4_K || t == T_Q6_K; }
 
 size_t al(size_t v) { return (v + 255) & ~size_t(255); }
+// Bytes of one activation-record row of `cols` values (the larger of the Q8_K
+// and Q8 formats).
+size_t rec_bytes(int64_t cols) {
+  return (size_t)std::max(act_rec_stride(true, cols), act_rec_stride(false, cols)) + 512;
+}
 
 // (Re)allocate the workspace so it holds at least the given dimensions.
 int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
@@ -184,7 +194,10 @@ int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
       (size_t)T * E * 4,                 // logits
       A * 4, A * 4,                      // ids, w
       (size_t)T * D, (size_t)T * (D / 32 + 1) * 4, (size_t)T * (D / 16 + 1) * 4,  // xq xd xs
+      (size_t)T * rec_bytes(D),          // xrec
       (size_t)E * 4, (size_t)(E + 1) * 4, A * 4, A * 4, A * 4, (size_t)E * 4, (size_t)E * 4, 16,  // meta
+      A * F * 4, A * F * 4,              // g, u
+      A * rec_bytes(F),                  // arec
       A * F * 4,                         // act
       A * F, A * (F / 32 + 1) * 4, A * (F / 16 + 1) * 4,  // aq ad as
       A * D * 4,                         // y
@@ -213,6 +226,7 @@ int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
   take((void**)&w.xq);
   take((void**)&w.xd);
   take((void**)&w.xs);
+  take((void**)&w.xrec);
   take((void**)&w.meta.counts);
   take((void**)&w.meta.offsets);
   take((void**)&w.meta.slot_tok);
@@ -221,6 +235,9 @@ int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
   take((void**)&w.meta.small_list);
   take((void**)&w.meta.large_list);
   take((void**)&w.meta.n_lists);
+  take((void**)&w.g);
+  take((void**)&w.u);
+  take((void**)&w.arec);
   take((void**)&w.act);
   take((void**)&w.aq);
   take((void**)&w.ad);
@@ -242,23 +259,25 @@ int check_status(kc_ctx* ctx) {
   return KC_OK;
 }
 
-// Copy `rows` rows of GGUF bytes (host or device) into the device layout.
-int upload_matrix(kc_ctx* ctx, int t, const void* src, int64_t rows, int64_t cols, uint8_t* dst, bool on_dev) {
-  const int64_t srb = gguf_row_bytes(t, cols), drs = dev_row_stride(t, cols);
+// Convert `n_mats` stacked GGUF matrices [rows, cols] (host or device bytes)
+// into the device layout at dst.
+int upload_matrix(kc_ctx* ctx, int t, const void* src, int64_t n_mats, int64_t rows, int64_t cols, uint8_t* dst,
+                  bool on_dev) {
+  const int64_t mat_src = rows * gguf_row_bytes(t, cols), mat_dst = dev_matrix_bytes(t, rows, cols);
   if (on_dev) {
-    RC(launch_repack(t, src, rows, cols, dst, ctx->stream));
+    RC(launch_repack(t, src, n_mats, rows, cols, dst, ctx->stream));
     CKL();
     return KC_OK;
   }
-  // Host source: stage through a bounded device buffer (<= 64 MiB per chunk).
-  const int64_t chunk_rows = std::max<int64_t>(1, (64ll << 20) / std::max<int64_t>(srb, 1));
+  // Host source: stage whole matrices through a bounded device buffer.
+  const int64_t chunk = std::max<int64_t>(1, (256ll << 20) / std::max<int64_t>(mat_src, 1));
   void* tmp = nullptr;
-  CK(cudaMalloc(&tmp, std::min(rows, chunk_rows) * srb));
-  for (int64_t r0 = 0; r0 < rows; r0 += chunk_rows) {
-    int64_t nr = std::min(chunk_rows, rows - r0);
-    cudaError_t e = cudaMemcpyAsync(tmp, static_cast<const uint8_t*>(src) + r0 * srb, nr * srb,
+  CK(cudaMalloc(&tmp, std::min(n_mats, chunk) * mat_src));
+  for (int64_t m0 = 0; m0 < n_mats; m0 += chunk) {
+    const int64_t nm = std::min(chunk, n_mats - m0);
+    cudaError_t e = cudaMemcpyAsync(tmp, static_cast<const uint8_t*>(src) + m0 * mat_src, nm * mat_src,
                                     cudaMemcpyHostToDevice, ctx->stream);
-    int rc = e == cudaSuccess ? launch_repack(t, tmp, nr, cols, dst + r0 * drs, ctx->stream) : KC_ERR_CUDA;
+    int rc = e == cudaSuccess ? launch_repack(t, tmp, nm, rows, cols, dst + m0 * mat_dst, ctx->stream) : KC_ERR_CUDA;
     if (rc == KC_OK) e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess || rc != KC_OK) {
       cudaFree(tmp);
@@ -302,7 +321,7 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
   // 1. router logits and top-k (Transformer::route).
   {
     StageScope ss(ctx, KC_STAGE_ROUTER_LOGITS);
-    launch_router_logits(router, d, E, d, h, n_tok, W.logits, st);
+    launch_router_logits(router, d, E, d, h, n_tok, W.logits, ctx->status, st);
     CKL();
   }
   {
@@ -319,40 +338,54 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
       RC(launch_dispatch(W.ids, W.w, n_tok, k, E, W.meta, st));
       CKL();
     }
-    // 3. activations for the int8 path.
+    // 3. activation records of the input rows (int8 path).
+    const bool kq_in = is_k(L.t_gate), kq_dn = is_k(L.t_down);
     {
       StageScope ss(ctx, KC_STAGE_QUANT_X);
-      if (is_k(L.t_gate)) launch_q8k_quantize(h, nullptr, n_tok, d, W.xq, W.xd, W.xs, st);
-      else launch_q8_quantize(h, nullptr, n_tok, d, W.xq, W.xd, W.xs, st);
+      launch_act_records(kq_in, h, nullptr, n_tok, d, W.xrec, nullptr, nullptr, st);
       CKL();
     }
     const int A = n_tok * k;
-    // 4. gate/up + SwiGLU -> act [slot, ff].
+    const int max_small = std::min(E, A);
+    // 4. gate and up products -> g, u [slot, ff].
+    {
+      StageScope ss(ctx, KC_STAGE_GATE_UP_INT8);
+      DecodeArgs dg{};
+      dg.w[0] = L.gate;
+      dg.w[1] = L.up;
+      dg.n_mat = 2;
+      dg.expert_stride = L.mb_gate;
+      dg.expert_base = L.first_expert;
+      dg.rows = ff;
+      dg.cols = d;
+      dg.type = L.t_gate;
+      dg.list = W.meta.small_list;
+      dg.n_list = W.meta.n_lists;
+      dg.offsets = W.meta.offsets;
+      dg.slot_src = W.meta.slot_tok;
+      dg.act = W.xrec;
+      dg.act_stride = act_rec_stride(kq_in, d);
+      dg.out[0] = W.g;
+      dg.out[1] = W.u;
+      dg.out_stride = ff;
+      dg.status = ctx->status;
+      RC(launch_decode(dg, max_small * 2 * ceil_div(ff, 16), st));
+      CKL();
+    }
     GroupedArgs g = grouped_base(ctx);
     g.w0 = L.gate;
     g.w1 = L.up;
-    g.expert_stride = (int64_t)ff * L.rs_gate;
+    g.expert_stride = L.mb_gate;
     g.expert_base = L.first_expert;
     g.rows = ff;
     g.cols = d;
-    g.row_stride = L.rs_gate;
     g.type = L.t_gate;
     g.offsets = W.meta.offsets;
     g.slot_src = W.meta.slot_tok;
-    g.aq = W.xq;
-    g.ad = W.xd;
-    g.asum = W.xs;
     g.af = h;
-    g.out = W.act;
+    g.out = W.g;
+    g.out2 = W.u;
     g.out_stride = ff;
-    g.list = W.meta.small_list;
-    g.n_list = W.meta.n_lists;
-    const int max_small = std::min(E, A);
-    {
-      StageScope ss(ctx, KC_STAGE_GATE_UP_INT8);
-      RC(launch_grouped_int8(g, true, max_small * ceil_div(ff, 16), st));
-      CKL();
-    }
     g.list = W.meta.large_list;
     g.n_list = W.meta.n_lists + 1;
     {
@@ -360,37 +393,47 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
       RC(launch_grouped_f32(g, true, std::min(E, A / 4), n_tok, st));
       CKL();
     }
-    // 5. quantise act rows for the int8 down path.
+    // 5. SwiGLU of every slot -> act (f32) and its activation records.
     {
       StageScope ss(ctx, KC_STAGE_QUANT_ACT);
-      if (is_k(L.t_down)) launch_q8k_quantize(W.act, nullptr, A, ff, W.aq, W.ad, W.as, st);
-      else launch_q8_quantize(W.act, nullptr, A, ff, W.aq, W.ad, W.as, st);
+      launch_act_records(kq_dn, W.g, W.u, A, ff, W.arec, W.act, nullptr, st);
       CKL();
     }
     // 6. down -> y [slot, d].
+    {
+      StageScope ss(ctx, KC_STAGE_DOWN_INT8);
+      DecodeArgs dd{};
+      dd.w[0] = L.down;
+      dd.n_mat = 1;
+      dd.expert_stride = L.mb_down;
+      dd.expert_base = L.first_expert;
+      dd.rows = d;
+      dd.cols = ff;
+      dd.type = L.t_down;
+      dd.list = W.meta.small_list;
+      dd.n_list = W.meta.n_lists;
+      dd.offsets = W.meta.offsets;
+      dd.slot_src = nullptr;
+      dd.act = W.arec;
+      dd.act_stride = act_rec_stride(kq_dn, ff);
+      dd.out[0] = W.y;
+      dd.out_stride = d;
+      dd.status = ctx->status;
+      RC(launch_decode(dd, max_small * ceil_div(d, 16), st));
+      CKL();
+    }
     GroupedArgs dn = grouped_base(ctx);
     dn.w0 = L.down;
-    dn.expert_stride = (int64_t)d * L.rs_down;
+    dn.expert_stride = L.mb_down;
     dn.expert_base = L.first_expert;
     dn.rows = d;
     dn.cols = ff;
-    dn.row_stride = L.rs_down;
     dn.type = L.t_down;
     dn.offsets = W.meta.offsets;
     dn.slot_src = nullptr;
-    dn.aq = W.aq;
-    dn.ad = W.ad;
-    dn.asum = W.as;
     dn.af = W.act;
     dn.out = W.y;
     dn.out_stride = d;
-    dn.list = W.meta.small_list;
-    dn.n_list = W.meta.n_lists;
-    {
-      StageScope ss(ctx, KC_STAGE_DOWN_INT8);
-      RC(launch_grouped_int8(dn, false, max_small * ceil_div(d, 16), st));
-      CKL();
-    }
     dn.list = W.meta.large_list;
     dn.n_list = W.meta.n_lists + 1;
     {
@@ -465,15 +508,13 @@ const char* kc_last_error(const kc_ctx* ctx) { return ctx ? ctx->err.c_str() : g
 
 int kc_set_stream(kc_ctx* ctx, void* s) {
   if (!ctx) return KC_ERR_ARG;
-  if (ctx->own_stream && s) {
+  // NULL is CUDA's legacy default stream, as everywhere in the runtime API.
+  if (ctx->own_stream) {
+    CK(cudaStreamSynchronize(ctx->stream));
     cudaStreamDestroy(ctx->stream);
     ctx->own_stream = false;
   }
-  if (s) ctx->stream = static_cast<cudaStream_t>(s);
-  else if (!ctx->own_stream) {
-    CK(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
-    ctx->own_stream = true;
-  }
+  ctx->stream = static_cast<cudaStream_t>(s);
   return KC_OK;
 }
 
@@ -533,16 +574,16 @@ int kc_upload_experts_range(kc_ctx* ctx, int layer, int n_expert, int first_expe
   L.t_gate = t_gate;
   L.t_up = t_up;
   L.t_down = t_down;
-  L.rs_gate = dev_row_stride(t_gate, d);
-  L.rs_down = dev_row_stride(t_down, ff);
-  const int64_t gbytes = (int64_t)n_local * ff * L.rs_gate, dbytes = (int64_t)n_local * d * L.rs_down;
+  L.mb_gate = dev_matrix_bytes(t_gate, ff, d);
+  L.mb_down = dev_matrix_bytes(t_down, d, ff);
+  const int64_t gbytes = (int64_t)n_local * L.mb_gate, dbytes = (int64_t)n_local * L.mb_down;
   CK(cudaMalloc(&L.gate, gbytes));
   CK(cudaMalloc(&L.up, gbytes));
   CK(cudaMalloc(&L.down, dbytes));
   ctx->weight_bytes += 2 * gbytes + dbytes;
-  RC(upload_matrix(ctx, t_gate, gate, (int64_t)n_local * ff, d, L.gate, src_on_device != 0));
-  RC(upload_matrix(ctx, t_up, up, (int64_t)n_local * ff, d, L.up, src_on_device != 0));
-  RC(upload_matrix(ctx, t_down, down, (int64_t)n_local * d, ff, L.down, src_on_device != 0));
+  RC(upload_matrix(ctx, t_gate, gate, n_local, ff, d, L.gate, src_on_device != 0));
+  RC(upload_matrix(ctx, t_up, up, n_local, ff, d, L.up, src_on_device != 0));
+  RC(upload_matrix(ctx, t_down, down, n_local, d, ff, L.down, src_on_device != 0));
   CK(cudaStreamSynchronize(ctx->stream));
   L.has_experts = true;
   return KC_OK;
@@ -595,10 +636,11 @@ int kc_upload_dense(kc_ctx* ctx, int tensor_id, int t, const void* w, int64_t ro
   D.t = t;
   D.rows = rows;
   D.cols = cols;
-  D.rs = dev_row_stride(t, cols);
-  CK(cudaMalloc(&D.w, rows * D.rs));
-  ctx->weight_bytes += rows * D.rs;
-  RC(upload_matrix(ctx, t, w, rows, cols, D.w, src_on_device != 0));
+  D.rs = round16(cols * 4);
+  const int64_t bytes = dev_matrix_bytes(t, rows, cols);
+  CK(cudaMalloc(&D.w, bytes));
+  ctx->weight_bytes += bytes;
+  RC(upload_matrix(ctx, t, w, 1, rows, cols, D.w, src_on_device != 0));
   CK(cudaStreamSynchronize(ctx->stream));
   return KC_OK;
 }
@@ -672,7 +714,8 @@ int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out)
   if (n == 0) return KC_OK;
   cudaStream_t st = ctx->stream;
   if (D.t == T_F32) {
-    launch_router_logits(reinterpret_cast<const float*>(D.w), D.rs / 4, (int)D.rows, (int)D.cols, x, n, out, st);
+    launch_router_logits(reinterpret_cast<const float*>(D.w), D.rs / 4, (int)D.rows, (int)D.cols, x, n, out, ctx->status,
+                         st);
     CKL();
     return KC_OK;
   }
@@ -686,7 +729,6 @@ int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out)
   a.expert_base = 0;
   a.rows = (int)D.rows;
   a.cols = (int)D.cols;
-  a.row_stride = D.rs;
   a.type = D.t;
   a.offsets = W.meta.offsets;
   a.slot_src = nullptr;
@@ -694,15 +736,24 @@ int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out)
   a.out = out;
   a.out_stride = D.rows;
   if (n < 4) {
-    if (is_k(D.t)) launch_q8k_quantize(x, nullptr, n, D.cols, W.xq, W.xd, W.xs, st);
-    else launch_q8_quantize(x, nullptr, n, D.cols, W.xq, W.xd, W.xs, st);
+    const bool kq = is_k(D.t);
+    launch_act_records(kq, x, nullptr, n, D.cols, W.xrec, nullptr, nullptr, st);
     CKL();
-    a.aq = W.xq;
-    a.ad = W.xd;
-    a.asum = W.xs;
-    a.list = W.meta.small_list;
-    a.n_list = W.meta.n_lists;
-    RC(launch_grouped_int8(a, false, ceil_div(D.rows, 16), st));
+    DecodeArgs dv{};
+    dv.w[0] = D.w;
+    dv.n_mat = 1;
+    dv.rows = (int)D.rows;
+    dv.cols = (int)D.cols;
+    dv.type = D.t;
+    dv.list = W.meta.small_list;
+    dv.n_list = W.meta.n_lists;
+    dv.offsets = W.meta.offsets;
+    dv.act = W.xrec;
+    dv.act_stride = act_rec_stride(kq, D.cols);
+    dv.out[0] = out;
+    dv.out_stride = D.rows;
+    dv.status = ctx->status;
+    RC(launch_decode(dv, ceil_div(D.rows, 16), st));
   } else {
     a.list = W.meta.large_list;
     a.n_list = W.meta.n_lists + 1;
@@ -764,7 +815,7 @@ int kc_router_logits_dev(kc_ctx* ctx, const float* router_w, int n_expert, int d
                          float* logits) {
   if (!ctx) return KC_ERR_ARG;
   cudaSetDevice(ctx->device);
-  launch_router_logits(router_w, d, n_expert, d, h, n_tok, logits, ctx->stream);
+  launch_router_logits(router_w, d, n_expert, d, h, n_tok, logits, ctx->status, ctx->stream);
   CKL();
   return KC_OK;
 }

@@ -18,24 +18,55 @@ namespace kc {
 enum : int { T_F32 = 0, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
 
 // ----------------------------------------------------------------------------
-// Device weight layouts. Q4_K rows keep the GGUF layout (144-byte superblocks
-// are 16-byte aligned). Q6_K (210-byte superblocks) and Q8_0 (34-byte blocks)
-// are stored "planar" per row so that every field starts on a 16-byte
-// boundary, with the row padded to a multiple of 16 bytes:
-//   Q6_K row: [ql 128*nb][qh 64*nb][scales 16*nb][d 2*nb][pad]
-//   Q8_0 row: [qs 32*nb][d 2*nb][pad]
-// The bytes are a permutation of GGUF's (plus row padding); the arithmetic on
-// them is unchanged.
+// Device weight layouts. Quantized matrices are stored "tiled": rows are
+// grouped in tiles of 16 (the row count is padded to a multiple of 16 with
+// zero rows), and inside a tile the bytes are laid out superblock-major with
+// one plane per field, so that
+//  * the 16 rows x a run of superblocks a decode stage needs are one
+//    contiguous range (one bulk copy of several KB), and
+//  * the reads of four consecutive rows by a quarter warp fall on distinct
+//    shared-memory banks without padding.
+// Per superblock-tile (16 rows):
+//   Q4_K  (2304 B): hdr[16 rows][16 B] (d, dmin, 12 scale bytes)
+//                   | qs[k = 0..3][16 rows][32 B]
+//   Q6_K  (3360 B): ql[c = 0..3][16 rows][32 B]   (c = 2*half + 32-byte run)
+//                   | qh[h = 0..1][16 rows][32 B] | sc[16 rows][16 B]
+//                   | d[16 rows][2 B]
+//   Q8_0  chunk of up to 8 blocks (512*nblk + 256 B):
+//                   qs[block][16 rows][32 B] | d[16 rows][8 x 2 B]
+// The bytes are a permutation of GGUF's (plus zero padding); the arithmetic
+// on them is unchanged. F32 matrices stay row-major (rows padded to 16 B).
+constexpr int kTileRows = 16;
+
 __host__ __device__ inline int64_t round16(int64_t v) { return (v + 15) & ~int64_t(15); }
 
-__host__ __device__ inline int64_t dev_row_stride(int t, int64_t cols) {
-  switch (t) {
-    case T_F32: return round16(cols * 4);
-    case T_Q8_0: return round16(cols / 32 * 34);
-    case T_Q4_K: return cols / 256 * 144;
-    case T_Q6_K: return round16(cols / 256 * 210);
-    default: return -1;
-  }
+// Superblocks (Q8_0: chunks of 8 blocks) per row.
+__host__ __device__ inline int tiled_nsb(int t, int64_t cols) {
+  return t == T_Q8_0 ? (int)((cols / 32 + 7) / 8) : (int)(cols / 256);
+}
+// Bytes of superblock-tile `sb` (Q8_0: chunk sb) of one 16-row tile.
+__host__ __device__ inline int tiled_sbt_bytes(int t, int64_t cols, int sb) {
+  if (t == T_Q4_K) return 2304;
+  if (t == T_Q6_K) return 3360;
+  const int nb32 = (int)(cols / 32);
+  const int nblk = nb32 - 8 * sb < 8 ? nb32 - 8 * sb : 8;
+  return 512 * nblk + 256;
+}
+// Byte offset of superblock-tile sb inside a tile.
+__host__ __device__ inline int64_t tiled_sb_offset(int t, int64_t cols, int sb) {
+  if (t == T_Q4_K) return 2304ll * sb;
+  if (t == T_Q6_K) return 3360ll * sb;
+  return 4352ll * sb;  // all chunks before the last are full
+}
+__host__ __device__ inline int64_t tiled_tile_bytes(int t, int64_t cols) {
+  const int nsb = tiled_nsb(t, cols);
+  return tiled_sb_offset(t, cols, nsb - 1) + tiled_sbt_bytes(t, cols, nsb - 1);
+}
+__host__ __device__ inline int64_t padded_rows(int64_t rows) { return (rows + kTileRows - 1) / kTileRows * kTileRows; }
+// Bytes of a whole [rows, cols] matrix in the device layout.
+__host__ __device__ inline int64_t dev_matrix_bytes(int t, int64_t rows, int64_t cols) {
+  if (t == T_F32) return rows * round16(cols * 4);
+  return padded_rows(rows) / kTileRows * tiled_tile_bytes(t, cols);
 }
 __host__ __device__ inline int64_t gguf_row_bytes(int t, int64_t cols) {
   switch (t) {

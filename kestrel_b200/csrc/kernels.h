@@ -13,8 +13,7 @@ struct GroupedArgs {
   const uint8_t* w1;      // second matrix for the gate/up pair (or null)
   int64_t expert_stride;  // bytes between consecutive experts' matrices
   int expert_base;        // global id of the first expert held in w0 / w1
-  int rows, cols;         // one expert's matrix
-  int64_t row_stride;     // bytes per row (device layout)
+  int rows, cols;         // one expert's matrix (tiled device layout)
   int type;               // ggml type of w0 / w1
   const int* list;        // expert ids to process
   const int* n_list;      // device scalar: entries in list
@@ -25,6 +24,7 @@ struct GroupedArgs {
   const int32_t* asum;    // their per-16 sums
   const float* af;        // f32 activations [n_act][cols] (f32 path)
   float* out;             // out[slot * out_stride + row]
+  float* out2;            // second matrix's output (pair products)
   int64_t out_stride;
   int* status;            // device status word (timeouts)
 };
@@ -35,13 +35,13 @@ void launch_q8k_quantize(const float* x, const int* row_map, int64_t n_rows, int
 void launch_q8_quantize(const float* x, const int* row_map, int64_t n_rows, int64_t cols, int8_t* q, float* d,
                         int32_t* s16, cudaStream_t st);
 int launch_quantize(int t, const float* x, int64_t rows, int64_t cols, void* out, cudaStream_t st);
-int launch_repack(int t, const void* src, int64_t rows, int64_t cols, void* dst, cudaStream_t st);
+int launch_repack(int t, const void* src, int64_t n_mats, int64_t rows, int64_t cols, void* dst, cudaStream_t st);
 void launch_block_sums(int t, const void* w, int64_t rows, int64_t cols, const int8_t* q, const int32_t* bsums,
                        int n_act, int32_t* out, cudaStream_t st);
 
 // router.cu
 void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int d, const float* h, int n_tok,
-                          float* logits, cudaStream_t st);
+                          float* logits, int* status, cudaStream_t st);
 void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
                   float* w, cudaStream_t st);
 // Dispatch metadata of one routed batch (see router.cu).
@@ -62,7 +62,6 @@ void launch_combine(const float* y, const int* tok_slot, const int* ids, const f
                     float* out, cudaStream_t st);
 
 // grouped.cu
-int launch_grouped_int8(const GroupedArgs& a, bool pair, int max_units, cudaStream_t st);
 int launch_grouped_f32(const GroupedArgs& a, bool pair, int max_experts, int max_rows_per_expert,
                        cudaStream_t st);
 

@@ -109,8 +109,8 @@ __global__ void quantize_q4_k_kernel(const float* __restrict__ x, int64_t nblock
       hi = fmaxf(hi, xb[j * 32 + l]);
     }
     lo = fminf(lo, 0.f);
-    scale[j] = __fdiv_rn(__fsub_rn(hi, lo), 15.f);
-    mins[j] = -lo;
+    scale[j] = __fadd_rn(__fdiv_rn(__fsub_rn(hi, lo), 15.f), 0.f);  // +0.0 for constant blocks
+    mins[j] = __fsub_rn(0.f, lo);  // +0.0 (not -0.0) for non-negative blocks
     smax = fmaxf(smax, scale[j]);
     mmax = fmaxf(mmax, mins[j]);
   }
@@ -120,23 +120,34 @@ __global__ void quantize_q4_k_kernel(const float* __restrict__ x, int64_t nblock
     sc[j] = (int)clampf(rintf(safe_div(scale[j], d16)), 0.f, 63.f);
     mm[j] = (int)clampf(rintf(safe_div(mins[j], dm16)), 0.f, 63.f);
   }
-  uint8_t* o = out + b * 144;
-  uint16_t hd = __half_as_ushort(__float2half_rn(d16)), hm = __half_as_ushort(__float2half_rn(dm16));
-  o[0] = hd & 0xFF; o[1] = hd >> 8; o[2] = hm & 0xFF; o[3] = hm >> 8;
+  // Assemble the 144-byte block as 36 words and store it as nine 16-byte
+  // vectors (blocks are 16-byte aligned).
+  uint32_t wv[36];
+  wv[0] = (uint32_t)f16bits(d16) | ((uint32_t)f16bits(dm16) << 16);
+  uint32_t sb[12];
   for (int j = 0; j < 4; ++j) {
-    o[4 + j] = (uint8_t)(sc[j] | ((sc[j + 4] >> 4) << 6));
-    o[8 + j] = (uint8_t)(mm[j] | ((mm[j + 4] >> 4) << 6));
-    o[12 + j] = (uint8_t)((sc[j + 4] & 0xF) | ((mm[j + 4] & 0xF) << 4));
+    sb[j] = (uint32_t)(sc[j] | ((sc[j + 4] >> 4) << 6)) & 0xFF;
+    sb[4 + j] = (uint32_t)(mm[j] | ((mm[j + 4] >> 4) << 6)) & 0xFF;
+    sb[8 + j] = (uint32_t)((sc[j + 4] & 0xF) | ((mm[j + 4] & 0xF) << 4)) & 0xFF;
   }
+  for (int w = 0; w < 3; ++w)
+    wv[1 + w] = sb[4 * w] | (sb[4 * w + 1] << 8) | (sb[4 * w + 2] << 16) | (sb[4 * w + 3] << 24);
   for (int k = 0; k < 4; ++k) {
     float D0 = __fmul_rn(d16, (float)sc[2 * k]), M0 = __fmul_rn(dm16, (float)mm[2 * k]);
     float D1 = __fmul_rn(d16, (float)sc[2 * k + 1]), M1 = __fmul_rn(dm16, (float)mm[2 * k + 1]);
-    for (int l = 0; l < 32; ++l) {
-      int q0 = (int)clampf(rintf(safe_div(__fadd_rn(xb[64 * k + l], M0), D0)), 0.f, 15.f);
-      int q1 = (int)clampf(rintf(safe_div(__fadd_rn(xb[64 * k + 32 + l], M1), D1)), 0.f, 15.f);
-      o[16 + 32 * k + l] = (uint8_t)(q0 | (q1 << 4));
+    for (int w = 0; w < 8; ++w) {
+      uint32_t word = 0;
+      for (int bb = 0; bb < 4; ++bb) {
+        int l = 4 * w + bb;
+        int q0 = (int)clampf(rintf(safe_div(__fadd_rn(xb[64 * k + l], M0), D0)), 0.f, 15.f);
+        int q1 = (int)clampf(rintf(safe_div(__fadd_rn(xb[64 * k + 32 + l], M1), D1)), 0.f, 15.f);
+        word |= (uint32_t)(q0 | (q1 << 4)) << (8 * bb);
+      }
+      wv[4 + 8 * k + w] = word;
     }
   }
+  uint4* o4 = reinterpret_cast<uint4*>(out + b * 144);
+  for (int i = 0; i < 9; ++i) o4[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
 }
 
 __global__ void quantize_q6_k_kernel(const float* __restrict__ x, int64_t nblocks, uint8_t* __restrict__ out) {
@@ -153,7 +164,7 @@ __global__ void quantize_q6_k_kernel(const float* __restrict__ x, int64_t nblock
   float d16 = f16r(__fdiv_rn(smax, 127.f));
   int sc[16];
   for (int j = 0; j < 16; ++j) sc[j] = (int)clampf(rintf(safe_div(s[j], d16)), -128.f, 127.f);
-  uint8_t* o = out + b * 210;
+  uint8_t o[210];
   for (int i = 0; i < 192; ++i) o[i] = 0;
   for (int i = 0; i < 256; ++i) {
     int j = i / 16;
@@ -168,6 +179,8 @@ __global__ void quantize_q6_k_kernel(const float* __restrict__ x, int64_t nblock
   uint16_t hd = f16bits(d16);
   o[208] = hd & 0xFF;
   o[209] = hd >> 8;
+  uint16_t* o16 = reinterpret_cast<uint16_t*>(out + b * 210);
+  for (int i = 0; i < 105; ++i) o16[i] = (uint16_t)(o[2 * i] | (o[2 * i + 1] << 8));
 }
 
 __global__ void quantize_q8_0_kernel(const float* __restrict__ x, int64_t nblocks, uint8_t* __restrict__ out) {
@@ -178,11 +191,13 @@ __global__ void quantize_q8_0_kernel(const float* __restrict__ x, int64_t nblock
   for (int l = 0; l < 32; ++l) amax = fmaxf(amax, fabsf(xb[l]));
   float d16 = f16r(__fdiv_rn(amax, 127.f));
   float inv = safe_div(1.f, d16);
-  uint8_t* o = out + b * 34;
-  uint16_t hd = f16bits(d16);
-  o[0] = hd & 0xFF;
-  o[1] = hd >> 8;
-  for (int l = 0; l < 32; ++l) o[2 + l] = (uint8_t)(int8_t)(int)clampf(rintf(__fmul_rn(xb[l], inv)), -127.f, 127.f);
+  uint16_t* o16 = reinterpret_cast<uint16_t*>(out + b * 34);
+  o16[0] = f16bits(d16);
+  for (int l = 0; l < 32; l += 2) {
+    uint32_t q0 = (uint8_t)(int8_t)(int)clampf(rintf(__fmul_rn(xb[l], inv)), -127.f, 127.f);
+    uint32_t q1 = (uint8_t)(int8_t)(int)clampf(rintf(__fmul_rn(xb[l + 1], inv)), -127.f, 127.f);
+    o16[1 + l / 2] = (uint16_t)(q0 | (q1 << 8));
+  }
 }
 
 int launch_quantize(int t, const float* x, int64_t rows, int64_t cols, void* out, cudaStream_t st) {
@@ -200,35 +215,46 @@ int launch_quantize(int t, const float* x, int64_t rows, int64_t cols, void* out
 }
 
 // ---------------------------------------------------------------------------
-// GGUF rows -> device layout (see common.cuh). One thread per (row, block).
-__global__ void repack_q6_k_kernel(const uint8_t* __restrict__ src, int64_t rows, int64_t nb, int64_t src_stride,
-                                   int64_t dst_stride, uint8_t* __restrict__ dst) {
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= rows * nb) return;
-  int64_t r = i / nb, b = i % nb;
-  const uint8_t* s = src + r * src_stride + b * 210;
-  uint8_t* row = dst + r * dst_stride;
-  for (int j = 0; j < 128; ++j) row[b * 128 + j] = s[j];
-  for (int j = 0; j < 64; ++j) row[nb * 128 + b * 64 + j] = s[128 + j];
-  for (int j = 0; j < 16; ++j) row[nb * 192 + b * 16 + j] = s[192 + j];
-  row[nb * 208 + b * 2] = s[208];
-  row[nb * 208 + b * 2 + 1] = s[209];
-  if (b == 0)
-    for (int64_t p = nb * 210; p < dst_stride; ++p) row[p] = 0;
-}
-
-__global__ void repack_q8_0_kernel(const uint8_t* __restrict__ src, int64_t rows, int64_t nb, int64_t src_stride,
-                                   int64_t dst_stride, uint8_t* __restrict__ dst) {
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= rows * nb) return;
-  int64_t r = i / nb, b = i % nb;
-  const uint8_t* s = src + r * src_stride + b * 34;
-  uint8_t* row = dst + r * dst_stride;
-  for (int j = 0; j < 32; ++j) row[b * 32 + j] = s[2 + j];
-  row[nb * 32 + b * 2] = s[0];
-  row[nb * 32 + b * 2 + 1] = s[1];
-  if (b == 0)
-    for (int64_t p = nb * 34; p < dst_stride; ++p) row[p] = 0;
+// GGUF rows -> tiled device layout (see common.cuh). `n_mats` stacked matrices
+// of `rows` rows each; matrix m starts at m * dev_matrix_bytes in dst. One
+// thread per (row, superblock); destination padding was zeroed by the caller.
+__global__ void repack_tiled_kernel(int t, const uint8_t* __restrict__ src, int64_t n_mats, int64_t rows,
+                                    int64_t cols, uint8_t* __restrict__ dst) {
+  const int nsb = tiled_nsb(t, cols);
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_mats * rows * nsb) return;
+  const int sb = (int)(i % nsb);
+  const int64_t gr = i / nsb;  // global row over all matrices
+  const int64_t m = gr / rows, r = gr % rows;
+  const int64_t tile = r / kTileRows;
+  const int rr = (int)(r % kTileRows);
+  const uint8_t* srow = src + gr * gguf_row_bytes(t, cols);
+  uint8_t* sbt = dst + m * dev_matrix_bytes(t, rows, cols) + tile * tiled_tile_bytes(t, cols) +
+                 tiled_sb_offset(t, cols, sb);
+  if (t == T_Q4_K) {
+    const uint8_t* b = srow + 144 * sb;
+    for (int x = 0; x < 16; ++x) sbt[16 * rr + x] = b[x];
+    for (int k = 0; k < 4; ++k)
+      for (int x = 0; x < 32; ++x) sbt[256 + 512 * k + 32 * rr + x] = b[16 + 32 * k + x];
+  } else if (t == T_Q6_K) {
+    const uint8_t* b = srow + 210 * sb;
+    for (int c = 0; c < 4; ++c)
+      for (int x = 0; x < 32; ++x) sbt[512 * c + 32 * rr + x] = b[32 * c + x];
+    for (int h = 0; h < 2; ++h)
+      for (int x = 0; x < 32; ++x) sbt[2048 + 512 * h + 32 * rr + x] = b[128 + 32 * h + x];
+    for (int x = 0; x < 16; ++x) sbt[3072 + 16 * rr + x] = b[192 + x];
+    sbt[3328 + 2 * rr] = b[208];
+    sbt[3328 + 2 * rr + 1] = b[209];
+  } else {
+    const int nb32 = (int)(cols / 32);
+    const int nblk = min(8, nb32 - 8 * sb);
+    for (int bl = 0; bl < nblk; ++bl) {
+      const uint8_t* b = srow + 34 * (8 * sb + bl);
+      for (int x = 0; x < 32; ++x) sbt[512 * bl + 32 * rr + x] = b[2 + x];
+      sbt[512 * nblk + 16 * rr + 2 * bl] = b[0];
+      sbt[512 * nblk + 16 * rr + 2 * bl + 1] = b[1];
+    }
+  }
 }
 
 __global__ void repack_copy_rows_kernel(const uint8_t* __restrict__ src, int64_t rows, int64_t row_bytes,
@@ -239,25 +265,21 @@ __global__ void repack_copy_rows_kernel(const uint8_t* __restrict__ src, int64_t
   dst[i] = c < row_bytes ? src[r * row_bytes + c] : 0;
 }
 
-int launch_repack(int t, const void* src, int64_t rows, int64_t cols, void* dst, cudaStream_t st) {
-  int64_t srb = gguf_row_bytes(t, cols), drs = dev_row_stride(t, cols);
+// `src` holds n_mats stacked GGUF matrices [rows, cols]; dst receives them in
+// the device layout (dst must hold n_mats * dev_matrix_bytes).
+int launch_repack(int t, const void* src, int64_t n_mats, int64_t rows, int64_t cols, void* dst, cudaStream_t st) {
   const uint8_t* s = static_cast<const uint8_t*>(src);
   uint8_t* d = static_cast<uint8_t*>(dst);
-  if (rows == 0) return KC_OK;
-  if (t == T_Q4_K) {
-    return cudaMemcpyAsync(d, s, rows * srb, cudaMemcpyDeviceToDevice, st) == cudaSuccess ? KC_OK : KC_ERR_CUDA;
+  if (rows == 0 || n_mats == 0) return KC_OK;
+  if (t == T_F32) {
+    const int64_t rb = cols * 4, ds = round16(rb);
+    repack_copy_rows_kernel<<<ceil_div(n_mats * rows * ds, 256), 256, 0, st>>>(s, n_mats * rows, rb, ds, d);
+    return KC_OK;
   }
-  if (t == T_Q6_K) {
-    int64_t nb = cols / 256;
-    repack_q6_k_kernel<<<ceil_div(rows * nb, 256), 256, 0, st>>>(s, rows, nb, srb, drs, d);
-  } else if (t == T_Q8_0) {
-    int64_t nb = cols / 32;
-    repack_q8_0_kernel<<<ceil_div(rows * nb, 256), 256, 0, st>>>(s, rows, nb, srb, drs, d);
-  } else if (t == T_F32) {
-    repack_copy_rows_kernel<<<ceil_div(rows * drs, 256), 256, 0, st>>>(s, rows, srb, drs, d);
-  } else {
-    return KC_ERR_TYPE;
-  }
+  if (t != T_Q4_K && t != T_Q6_K && t != T_Q8_0) return KC_ERR_TYPE;
+  if (cudaMemsetAsync(d, 0, n_mats * dev_matrix_bytes(t, rows, cols), st) != cudaSuccess) return KC_ERR_CUDA;
+  const int64_t n = n_mats * rows * tiled_nsb(t, cols);
+  repack_tiled_kernel<<<ceil_div(n, 128), 128, 0, st>>>(t, s, n_mats, rows, cols, d);
   return KC_OK;
 }
 

@@ -16,76 +16,113 @@ namespace kc {
 //     tile's 3-row blocks and tokens in 4-token blocks use one 8-lane FMA chain
 //     per output + hsum; the other outputs use dot_f32 (avx2.rs:289-308), whose
 //     even 8-chunks feed acc0 and odd ones acc1, summed lane-wise before hsum.
-// Thread layout: 8 threads (one per lane) per expert row, 8 rows per block,
-// TS tokens per thread (each weight element loaded once for TS tokens).
-constexpr int RL_ROWS = 8, RL_TS = 4;
+// Thread layout: 8 threads (one per lane) per (expert row, token) output; a
+// block computes RL_E rows x RL_T tokens. Weight and token rows are streamed
+// through shared memory in K chunks of RL_KC floats with bulk copies
+// (double-buffered), so every thread's chain reads shared memory only; each
+// lane still visits its elements c = lane, lane+8, ... in increasing order.
+constexpr int RL_E = 8, RL_T = 4, RL_KC = 1024;
+constexpr int RL_THREADS = RL_E * RL_T * 8;
 
-__global__ void __launch_bounds__(RL_ROWS * 8) router_logits_kernel(const float* __restrict__ w, int64_t ws,
-                                                                    int E, int d, const float* __restrict__ h,
-                                                                    int n_tok, float* __restrict__ logits) {
-  const int j = threadIdx.x & 7;
-  const int e = blockIdx.x * RL_ROWS + (threadIdx.x >> 3);
-  const int s0 = blockIdx.y * RL_TS;
+__global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* __restrict__ w, int64_t ws, int E,
+                                                                   int d, const float* __restrict__ h, int n_tok,
+                                                                   float* __restrict__ logits, int* status) {
+  extern __shared__ __align__(128) float rsm[];  // [2][(RL_E + RL_T) * RL_KC]
+  __shared__ __align__(8) uint64_t full[2];
+  const int tid = threadIdx.x, j = tid & 7, grp = tid >> 3;
+  const int er = grp % RL_E, tr = grp / RL_E;
+  const int e0 = blockIdx.x * RL_E, s0 = blockIdx.y * RL_T;
+  const int ne = min(RL_E, E - e0), nt = min(RL_T, n_tok - s0);
+  const int e = e0 + min(er, ne - 1), s = s0 + min(tr, nt - 1);
+  const bool valid = er < ne && tr < nt;
   const bool gemm = n_tok >= 4 && (d % 8) == 0;
   const int n8 = d / 8 * 8;
-  const bool e_ok = e < E;
-  const int ee = e_ok ? e : E - 1;
-  // Method per token: 0 = lane chain, 1 = dot_f32, 2 = scalar dot.
-  int method[RL_TS];
-  int ntok_here = min(RL_TS, n_tok - s0);
+  // Method: 0 = gemm_f32 lane chain, 1 = dot_f32 (acc0 even / acc1 odd
+  // 8-chunks), 2 = scalar quant::dot.
+  int method;
   {
-    int tile = ee / 48, trows = min(48, E - tile * 48), rows3 = trows / 3 * 3;
-    bool row_blocked = (ee - tile * 48) < rows3;
-#pragma unroll
-    for (int t = 0; t < RL_TS; ++t) {
-      int s = s0 + t;
-      method[t] = !gemm ? 2 : (row_blocked && s < n_tok / 4 * 4) ? 0 : 1;
-    }
+    const int tile = e / 48, trows = min(48, E - tile * 48), rows3 = trows / 3 * 3;
+    const bool row_blocked = (e - tile * 48) < rows3;
+    method = !gemm ? 2 : (row_blocked && s < n_tok / 4 * 4) ? 0 : 1;
   }
-  float a0[RL_TS], a1[RL_TS];
-#pragma unroll
-  for (int t = 0; t < RL_TS; ++t) a0[t] = a1[t] = 0.f;
-  const float* wr = w + (int64_t)ee * ws;
-  for (int c = 0, chunk = 0; c < n8; c += 8, ++chunk) {
-    float wv = wr[c + j];
-#pragma unroll
-    for (int t = 0; t < RL_TS; ++t) {
-      if (t >= ntok_here) break;
-      float xv = h[(int64_t)(s0 + t) * d + c + j];
-      if (method[t] == 0) {
-        a0[t] = __fmaf_rn(wv, xv, a0[t]);
-      } else if (method[t] == 1) {
-        if (chunk & 1) a1[t] = __fmaf_rn(wv, xv, a1[t]);
-        else a0[t] = __fmaf_rn(wv, xv, a0[t]);
-      } else {
-        a0[t] = __fadd_rn(a0[t], __fmul_rn(wv, xv));
+  const int nchunk = (d + RL_KC - 1) / RL_KC;
+  const bool bulk_ok = (d % 4) == 0 && (ws % 4) == 0 && ((uintptr_t)w & 15) == 0 &&
+                       ((uintptr_t)h & 15) == 0;  // 16-byte aligned rows
+  if (tid == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int c) {
+    float* buf = rsm + (c & 1) * (RL_E + RL_T) * RL_KC;
+    const int k0 = c * RL_KC, kn = min(RL_KC, d - k0);
+    const uint32_t rb = (uint32_t)kn * 4;
+    mbar_expect_tx(&full[c & 1], rb * (ne + nt));
+    for (int r = 0; r < ne; ++r) bulk_g2s(buf + r * RL_KC, w + (int64_t)(e0 + r) * ws + k0, rb, &full[c & 1]);
+    for (int r = 0; r < nt; ++r) bulk_g2s(buf + (RL_E + r) * RL_KC, h + (int64_t)(s0 + r) * d + k0, rb, &full[c & 1]);
+  };
+  float a0 = 0.f, a1 = 0.f;
+  if (bulk_ok) {
+    if (tid == 0) {
+      issue(0);
+      if (nchunk > 1) issue(1);
+    }
+    for (int c = 0; c < nchunk; ++c) {
+      mbar_wait(&full[c & 1], (c >> 1) & 1, status);
+      const float* buf = rsm + (c & 1) * (RL_E + RL_T) * RL_KC;
+      const float* wr = buf + min(er, ne - 1) * RL_KC;
+      const float* xr = buf + (RL_E + min(tr, nt - 1)) * RL_KC;
+      const int k0 = c * RL_KC, kn = min(RL_KC, n8 - k0);
+      for (int cc = 0; cc < kn; cc += 8) {
+        const float wv = wr[cc + j], xv = xr[cc + j];
+        if (method == 0) a0 = __fmaf_rn(wv, xv, a0);
+        else if (method == 1) {
+          if (((k0 + cc) >> 3) & 1) a1 = __fmaf_rn(wv, xv, a1);
+          else a0 = __fmaf_rn(wv, xv, a0);
+        } else a0 = __fadd_rn(a0, __fmul_rn(wv, xv));
       }
+      __syncthreads();  // everyone is done with this buffer
+      if (tid == 0 && c + 2 < nchunk) issue(c + 2);
+    }
+  } else {
+    // Rows not 16-byte aligned: read global memory directly.
+    const float* wr = w + (int64_t)e * ws;
+    const float* xr = h + (int64_t)s * d;
+    for (int c = 0, chunk = 0; c < n8; c += 8, ++chunk) {
+      const float wv = wr[c + j], xv = xr[c + j];
+      if (method == 0) a0 = __fmaf_rn(wv, xv, a0);
+      else if (method == 1) {
+        if (chunk & 1) a1 = __fmaf_rn(wv, xv, a1);
+        else a0 = __fmaf_rn(wv, xv, a0);
+      } else a0 = __fadd_rn(a0, __fmul_rn(wv, xv));
     }
   }
+  float v;
+  if (method == 2) {
+    // Sequential fold of the eight lanes from -0.0, then the tail.
+    float sum = -0.0f;
 #pragma unroll
-  for (int t = 0; t < RL_TS; ++t) {
-    if (t >= ntok_here) break;
-    float v;
-    if (method[t] == 2) {
-      // Sequential fold of the eight lanes from -0.0, then the tail.
-      float s = -0.0f;
-#pragma unroll
-      for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(0xffffffffu, a0[t], l, 8));
-      for (int c = n8; c < d; ++c) s = __fadd_rn(s, __fmul_rn(wr[c], h[(int64_t)(s0 + t) * d + c]));
-      v = s;
-    } else {
-      float lanev = method[t] == 1 ? __fadd_rn(a0[t], a1[t]) : a0[t];
-      v = hsum8_group(lanev);
-    }
-    if (j == 0 && e_ok) logits[(int64_t)(s0 + t) * E + e] = v;
+    for (int l = 0; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, a0, l, 8));
+    for (int c = n8; c < d; ++c) sum = __fadd_rn(sum, __fmul_rn(w[(int64_t)e * ws + c], h[(int64_t)s * d + c]));
+    v = sum;
+  } else {
+    v = hsum8_group(method == 1 ? __fadd_rn(a0, a1) : a0);
   }
+  if (j == 0 && valid) logits[(int64_t)s * E + e] = v;
 }
 
 void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int d, const float* h, int n_tok,
-                          float* logits, cudaStream_t st) {
+                          float* logits, int* status, cudaStream_t st) {
   if (n_tok <= 0) return;
-  dim3 grid(ceil_div(E, RL_ROWS), ceil_div(n_tok, RL_TS));
-  router_logits_kernel<<<grid, RL_ROWS * 8, 0, st>>>(w, row_stride_floats, E, d, h, n_tok, logits);
+  static bool attr = false;
+  const size_t smem = 2 * (RL_E + RL_T) * RL_KC * sizeof(float);
+  if (!attr) {
+    cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
+  }
+  dim3 grid(ceil_div(E, RL_E), ceil_div(n_tok, RL_T));
+  router_logits_kernel<<<grid, RL_THREADS, smem, st>>>(w, row_stride_floats, E, d, h, n_tok, logits, status);
 }
 
 // ---------------------------------------------------------------------------

@@ -112,7 +112,7 @@ def quantize_q4_k(x: np.ndarray) -> np.ndarray:
     """Q4_K: superblocks of 256 = 8 sub-blocks of 32 with 6-bit scale and min.
 
     Per sub-block j: lo_j = min(0, min x), scale_j = (max x - lo_j)/15,
-    min_j = -lo_j. Superblock d = f16(max scale_j / 63), dmin =
+    min_j = 0 - lo_j. Superblock d = f16(max scale_j / 63), dmin =
     f16(max min_j / 63); sc_j = rint(scale_j/d), m_j = rint(min_j/dmin) (0..63);
     q = rint((x + dmin*m_j) / (d*sc_j)) clipped to 0..15, so that the
     dequantised value is d*sc_j*q - dmin*m_j (quant.rs:138-155).
@@ -121,8 +121,8 @@ def quantize_q4_k(x: np.ndarray) -> np.ndarray:
     nb = xb.shape[0]
     lo = np.minimum(xb.min(axis=2), np.float32(0))
     hi = xb.max(axis=2)
-    scale = ((hi - lo) / np.float32(15)).astype(np.float32)
-    mins = (-lo).astype(np.float32)
+    scale = ((hi - lo) / np.float32(15) + np.float32(0)).astype(np.float32)  # +0.0 for constant blocks
+    mins = (np.float32(0) - lo).astype(np.float32)  # +0.0, never -0.0, for non-negative blocks
     d16 = _f16_round(scale.max(axis=1) / np.float32(63))
     dm16 = _f16_round(mins.max(axis=1) / np.float32(63))
     sc = np.clip(np.rint(_safe_div(scale, np.broadcast_to(d16[:, None], scale.shape))), 0, 63).astype(np.int32)

@@ -26,6 +26,9 @@ def ctx():
         pytest.skip("no CUDA device")
     from kestrel_b200.cuda import Context
     c = Context(0)
+    # Share torch's stream so the tests' host->device copies are ordered with
+    # the library's kernels.
+    c.set_stream(torch.cuda.current_stream().cuda_stream)
     yield c
     c.close()
 
