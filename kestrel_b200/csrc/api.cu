@@ -15,6 +15,7 @@
 #include "decode.h"
 #include "ep.h"
 #include "kernels.h"
+#include "mma.h"
 
 using namespace kc;
 
@@ -60,6 +61,8 @@ struct Work {
   float* u = nullptr;
   uint8_t* arec = nullptr;  // activation records of SwiGLU(g, u) per slot
   float* act = nullptr;
+  __half* x16 = nullptr;    // f16 input rows per slot (tensor-core path)
+  __half* act16 = nullptr;  // f16 SwiGLU rows per slot
   int8_t* aq = nullptr;
   float* ad = nullptr;
   int32_t* as = nullptr;
@@ -196,9 +199,11 @@ int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
       (size_t)T * D, (size_t)T * (D / 32 + 1) * 4, (size_t)T * (D / 16 + 1) * 4,  // xq xd xs
       (size_t)T * rec_bytes(D),          // xrec
       (size_t)E * 4, (size_t)(E + 1) * 4, A * 4, A * 4, A * 4, (size_t)E * 4, (size_t)E * 4, 16,  // meta
+      (size_t)(E + 1) * 4,               // large_tt
       A * F * 4, A * F * 4,              // g, u
       A * rec_bytes(F),                  // arec
       A * F * 4,                         // act
+      A * D * 2, A * F * 2,              // x16, act16
       A * F, A * (F / 32 + 1) * 4, A * (F / 16 + 1) * 4,  // aq ad as
       A * D * 4,                         // y
       (size_t)T * D * 4, (size_t)T * D * 4,  // h_in, out
@@ -235,10 +240,13 @@ int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
   take((void**)&w.meta.small_list);
   take((void**)&w.meta.large_list);
   take((void**)&w.meta.n_lists);
+  take((void**)&w.meta.large_tt);
   take((void**)&w.g);
   take((void**)&w.u);
   take((void**)&w.arec);
   take((void**)&w.act);
+  take((void**)&w.x16);
+  take((void**)&w.act16);
   take((void**)&w.aq);
   take((void**)&w.ad);
   take((void**)&w.as);
@@ -372,23 +380,49 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
       RC(launch_decode(dg, max_small * 2 * ceil_div(ff, 16), st));
       CKL();
     }
-    GroupedArgs g = grouped_base(ctx);
-    g.w0 = L.gate;
-    g.w1 = L.up;
-    g.expert_stride = L.mb_gate;
-    g.expert_base = L.first_expert;
-    g.rows = ff;
-    g.cols = d;
-    g.type = L.t_gate;
-    g.offsets = W.meta.offsets;
-    g.slot_src = W.meta.slot_tok;
-    g.af = h;
-    g.out = W.g;
-    g.out2 = W.u;
-    g.out_stride = ff;
-    g.list = W.meta.large_list;
-    g.n_list = W.meta.n_lists + 1;
-    {
+    const int max_tt = ceil_div(A, 128) + std::min(E, A / 4);
+    if (mma_supported(L.t_gate, d, 2)) {
+      StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
+      launch_gather_f16(h, W.meta.slot_tok, A, d, W.x16, st);
+      CKL();
+      alignas(64) unsigned char tmap[128];
+      if (make_tmap_f16(tmap, W.x16, A, d) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
+      MmaArgs ma{};
+      ma.w[0] = L.gate;
+      ma.w[1] = L.up;
+      ma.n_mat = 2;
+      ma.expert_stride = L.mb_gate;
+      ma.expert_base = L.first_expert;
+      ma.rows = ff;
+      ma.cols = d;
+      ma.type = L.t_gate;
+      ma.list = W.meta.large_list;
+      ma.n_list = W.meta.n_lists + 1;
+      ma.offsets = W.meta.offsets;
+      ma.tt_prefix = W.meta.large_tt;
+      ma.out[0] = W.g;
+      ma.out[1] = W.u;
+      ma.out_stride = ff;
+      ma.status = ctx->status;
+      RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(ff, 128), st));
+      CKL();
+    } else {
+      GroupedArgs g = grouped_base(ctx);
+      g.w0 = L.gate;
+      g.w1 = L.up;
+      g.expert_stride = L.mb_gate;
+      g.expert_base = L.first_expert;
+      g.rows = ff;
+      g.cols = d;
+      g.type = L.t_gate;
+      g.offsets = W.meta.offsets;
+      g.slot_src = W.meta.slot_tok;
+      g.af = h;
+      g.out = W.g;
+      g.out2 = W.u;
+      g.out_stride = ff;
+      g.list = W.meta.large_list;
+      g.n_list = W.meta.n_lists + 1;
       StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
       RC(launch_grouped_f32(g, true, std::min(E, A / 4), n_tok, st));
       CKL();
@@ -396,7 +430,7 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
     // 5. SwiGLU of every slot -> act (f32) and its activation records.
     {
       StageScope ss(ctx, KC_STAGE_QUANT_ACT);
-      launch_act_records(kq_dn, W.g, W.u, A, ff, W.arec, W.act, nullptr, st);
+      launch_act_records(kq_dn, W.g, W.u, A, ff, W.arec, W.act, W.act16, st);
       CKL();
     }
     // 6. down -> y [slot, d].
@@ -422,21 +456,42 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
       RC(launch_decode(dd, max_small * ceil_div(d, 16), st));
       CKL();
     }
-    GroupedArgs dn = grouped_base(ctx);
-    dn.w0 = L.down;
-    dn.expert_stride = L.mb_down;
-    dn.expert_base = L.first_expert;
-    dn.rows = d;
-    dn.cols = ff;
-    dn.type = L.t_down;
-    dn.offsets = W.meta.offsets;
-    dn.slot_src = nullptr;
-    dn.af = W.act;
-    dn.out = W.y;
-    dn.out_stride = d;
-    dn.list = W.meta.large_list;
-    dn.n_list = W.meta.n_lists + 1;
-    {
+    if (mma_supported(L.t_down, ff, 1) && ff % 256 == 0) {
+      StageScope ss(ctx, KC_STAGE_DOWN_F32);
+      alignas(64) unsigned char tmap[128];
+      if (make_tmap_f16(tmap, W.act16, A, ff) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (act16) failed");
+      MmaArgs ma{};
+      ma.w[0] = L.down;
+      ma.n_mat = 1;
+      ma.expert_stride = L.mb_down;
+      ma.expert_base = L.first_expert;
+      ma.rows = d;
+      ma.cols = ff;
+      ma.type = L.t_down;
+      ma.list = W.meta.large_list;
+      ma.n_list = W.meta.n_lists + 1;
+      ma.offsets = W.meta.offsets;
+      ma.tt_prefix = W.meta.large_tt;
+      ma.out[0] = W.y;
+      ma.out_stride = d;
+      ma.status = ctx->status;
+      RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(d, 128), st));
+      CKL();
+    } else {
+      GroupedArgs dn = grouped_base(ctx);
+      dn.w0 = L.down;
+      dn.expert_stride = L.mb_down;
+      dn.expert_base = L.first_expert;
+      dn.rows = d;
+      dn.cols = ff;
+      dn.type = L.t_down;
+      dn.offsets = W.meta.offsets;
+      dn.slot_src = nullptr;
+      dn.af = W.act;
+      dn.out = W.y;
+      dn.out_stride = d;
+      dn.list = W.meta.large_list;
+      dn.n_list = W.meta.n_lists + 1;
       StageScope ss(ctx, KC_STAGE_DOWN_F32);
       RC(launch_grouped_f32(dn, false, std::min(E, A / 4), n_tok, st));
       CKL();
@@ -754,6 +809,25 @@ int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out)
     dv.out_stride = D.rows;
     dv.status = ctx->status;
     RC(launch_decode(dv, ceil_div(D.rows, 16), st));
+  } else if (mma_supported(D.t, D.cols, 1)) {
+    launch_gather_f16(x, nullptr, n, D.cols, W.x16, st);
+    CKL();
+    alignas(64) unsigned char tmap[128];
+    if (make_tmap_f16(tmap, W.x16, n, D.cols) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
+    MmaArgs ma{};
+    ma.w[0] = D.w;
+    ma.n_mat = 1;
+    ma.rows = (int)D.rows;
+    ma.cols = (int)D.cols;
+    ma.type = D.t;
+    ma.list = W.meta.large_list;
+    ma.n_list = W.meta.n_lists + 1;
+    ma.offsets = W.meta.offsets;
+    ma.tt_prefix = W.meta.large_tt;
+    ma.out[0] = out;
+    ma.out_stride = D.rows;
+    ma.status = ctx->status;
+    RC(launch_mma_grouped(ma, tmap, ceil_div(n, 128) * ceil_div(D.rows, 128), st));
   } else {
     a.list = W.meta.large_list;
     a.n_list = W.meta.n_lists + 1;

@@ -54,6 +54,7 @@ struct DispatchOut {
   int* small_list; // experts with 1..3 rows (int8 path)
   int* large_list; // experts with >= 4 rows (f32 path)
   int* n_lists;    // [2]: entries in small_list, large_list
+  int* large_tt;   // [E+1]: prefix over large_list of ceil(rows / 128) token tiles
 };
 int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st);
 // Metadata of a dense product: one group of n rows, slots = rows 0..n-1.

@@ -1,0 +1,500 @@
+// Grouped quantized GEMM on the 5th-generation tensor cores (tcgen05), for the
+// experts with >= 4 routed rows and dense products with n >= 4 -- the rows the
+// reference sends through its exact path: dequantise to f32, then an f32 GEMM
+// (crates/kestrel-engine/src/quant.rs:241-260).
+//
+// Per work tile: one expert, 128 weight rows (the MMA's M) x up to 128 slots
+// (N), all of K. Roles:
+//   warp 0 (1 thread)  producer: bulk copies of the raw quantized superblock
+//                      tiles (tiled device layout, >= 2.3 KB each) and TMA
+//                      tensor loads of the f16 activation tile (128B swizzle).
+//   warp 1             TMEM allocation; one thread issues
+//                      tcgen05.mma.cta_group::1.kind::f16 into f32 TMEM
+//                      accumulators (gate and up side by side) and commits to
+//                      mbarriers.
+//   warps 2-5          dequantisation (thread = weight row) with the
+//                      reference's float operations, rounded once to f16 and
+//                      written in the canonical K-major SWIZZLE_128B layout;
+//                      then the epilogue (tcgen05.ld -> global).
+// Operands are f16 (11-bit significand), accumulation f32: results match the
+// reference's f32 path within the 1e-3 tolerance, not bit for bit.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "mma.h"
+
+namespace kc {
+
+constexpr int MM = 128;       // weight rows per tile
+constexpr int MK = 64;        // K elements per operand stage (one 128B swizzle atom)
+constexpr int MN = 128;       // slots per tile
+constexpr int M_THREADS = 192;
+constexpr int M_OPS = 3;      // operand stages
+constexpr int M_RAWS = 2;     // raw superblock stages
+constexpr int A_BYTES = MM * MK * 2;  // 16 KB
+constexpr int B_BYTES = MN * MK * 2;  // 16 KB
+
+__host__ __device__ inline int max_sbt_bytes(int t) { return t == T_Q4_K ? 2304 : t == T_Q6_K ? 3360 : 4352; }
+
+struct MmaSmem {
+  int op_bytes, raw_bytes, total;
+};
+__host__ __device__ inline MmaSmem mma_smem(int t, int n_mat) {
+  MmaSmem s;
+  s.op_bytes = n_mat * A_BYTES + B_BYTES;
+  s.raw_bytes = ((n_mat * 8 * max_sbt_bytes(t) + 1023) / 1024) * 1024;
+  s.total = M_OPS * s.op_bytes + M_RAWS * s.raw_bytes + 1024;  // + alignment slack
+  return s;
+}
+
+// ---- tcgen05 / TMA helpers --------------------------------------------------
+// Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row groups 1024 B
+// apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+// Instruction descriptor, kind::f16: A = B = f16, D = f32, both K-major.
+__device__ __forceinline__ uint32_t f16_idesc(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(MM >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- dequantisation of one row's 64-element K chunk into the A tile ----------
+// Element k of row m goes to byte (m/8)*1024 + (m%8)*128 + ((k/8 ^ m%8)*16) +
+// (k%8)*2: the canonical K-major SWIZZLE_128B layout.
+__device__ __forceinline__ void put8(uint8_t* A, int m, int c, const float v[8]) {
+  __half2 h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(A + (m >> 3) * 1024 + (m & 7) * 128 + ((c ^ (m & 7)) << 4)) =
+      *reinterpret_cast<uint4*>(h);
+}
+
+// Scale and min of Q4_K sub-block jj (scale_min_k4, quant.rs:54-60).
+__device__ __forceinline__ void mma_q4k_sm(int jj, uint32_t w0, uint32_t w1, uint32_t w2, int& s, int& m) {
+  const int sh = 8 * (jj & 3);
+  const uint32_t A = (w0 >> sh) & 0xFF, B = (w1 >> sh) & 0xFF, C = (w2 >> sh) & 0xFF;
+  if (jj < 4) {
+    s = A & 63;
+    m = B & 63;
+  } else {
+    s = (C & 0xF) | ((A >> 6) << 4);
+    m = (C >> 4) | ((B >> 6) << 4);
+  }
+}
+
+// Q4_K (quant.rs:138-155): y = (d*sc)*q - dmin*m, per 32-element sub-block.
+__device__ __forceinline__ void dq_q4k(const uint8_t* sbt, int rr, int kk, uint8_t* A, int m) {
+  const uint4 hdr = *reinterpret_cast<const uint4*>(sbt + 16 * rr);
+  const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
+  int s0, m0, s1, m1;
+  mma_q4k_sm(2 * kk, hdr.y, hdr.z, hdr.w, s0, m0);
+  mma_q4k_sm(2 * kk + 1, hdr.y, hdr.z, hdr.w, s1, m1);
+  const float d1 = __fmul_rn(d, (float)s0), mm1 = __fmul_rn(dmin, (float)m0);
+  const float d2 = __fmul_rn(d, (float)s1), mm2 = __fmul_rn(dmin, (float)m1);
+  const uint4 q0 = *reinterpret_cast<const uint4*>(sbt + 256 + 512 * kk + 32 * rr);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(sbt + 256 + 512 * kk + 32 * rr + 16);
+  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t byte = (qw[2 * c + i / 4] >> (8 * (i & 3))) & 0xFF;
+      lo[i] = __fsub_rn(__fmul_rn(d1, (float)(byte & 0xF)), mm1);
+      hi[i] = __fsub_rn(__fmul_rn(d2, (float)(byte >> 4)), mm2);
+    }
+    put8(A, m, c, lo);
+    put8(A, m, c + 4, hi);
+  }
+}
+
+// Q6_K (quant.rs:180-201): y = (d*sc)*(q-32).
+__device__ __forceinline__ void dq_q6k(const uint8_t* sbt, int rr, int kk, uint8_t* A, int m) {
+  const int h = kk >> 1, nib = kk & 1;
+  const float d = h2f(*reinterpret_cast<const uint16_t*>(sbt + 3328 + 2 * rr));
+  const uint4 scw = *reinterpret_cast<const uint4*>(sbt + 3072 + 16 * rr);
+  const uint32_t sw[4] = {scw.x, scw.y, scw.z, scw.w};
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {  // elements 32*half .. 32*half+31 of the chunk
+    const int r2 = 2 * nib + half;
+    const uint8_t* qlp = sbt + 512 * (2 * h + half) + 32 * rr;
+    const uint8_t* qhp = sbt + 2048 + 512 * h + 32 * rr;
+    const uint4 l0 = *reinterpret_cast<const uint4*>(qlp), l1 = *reinterpret_cast<const uint4*>(qlp + 16);
+    const uint4 h0 = *reinterpret_cast<const uint4*>(qhp), h1 = *reinterpret_cast<const uint4*>(qhp + 16);
+    const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {  // 8 elements l = 8c .. 8c+7
+      const int si = 8 * h + 2 * r2 + (c >> 1);
+      const float dsc = __fmul_rn(d, (float)(int)(int8_t)((sw[si >> 2] >> (8 * (si & 3))) & 0xFF));
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int l = 8 * c + i;
+        const uint32_t qlb = (lw[l >> 2] >> (8 * (l & 3))) & 0xFF;
+        const uint32_t qhb = (hw[l >> 2] >> (8 * (l & 3))) & 0xFF;
+        const int q = (int)(((qlb >> (4 * nib)) & 0xF) | (((qhb >> (2 * r2)) & 3) << 4)) - 32;
+        v[i] = __fmul_rn(dsc, (float)q);
+      }
+      put8(A, m, 4 * half + c, v);
+    }
+  }
+}
+
+// Q8_0 (quant.rs:82-89): y = q*d, chunk of up to 8 blocks.
+__device__ __forceinline__ void dq_q8_0(const uint8_t* cb, int nblk, int rr, int kk, uint8_t* A, int m) {
+#pragma unroll
+  for (int bi = 0; bi < 2; ++bi) {
+    const int b = 2 * kk + bi;
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(cb + 512 * nblk + 16 * rr + 2 * b));
+    const uint4 q0 = *reinterpret_cast<const uint4*>(cb + 512 * b + 32 * rr);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(cb + 512 * b + 32 * rr + 16);
+    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[i] = __fmul_rn((float)(int)(int8_t)((qw[2 * c + i / 4] >> (8 * (i & 3))) & 0xFF), d);
+      put8(A, m, 4 * bi + c, v);
+    }
+  }
+}
+
+// ---- work tiles ---------------------------------------------------------------
+struct Tile {
+  int e, slot0, t0, nt, rt;
+};
+__device__ __forceinline__ Tile tile_of(const MmaArgs& a, int w, int row_tiles, int n_large) {
+  Tile t;
+  const int tt = w / row_tiles;
+  t.rt = w % row_tiles;
+  int lo = 0, hi = n_large - 1;  // last i with tt_prefix[i] <= tt
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (a.tt_prefix[mid] <= tt) lo = mid;
+    else hi = mid - 1;
+  }
+  t.e = a.list[lo];
+  t.slot0 = a.offsets[t.e];
+  const int n = a.offsets[t.e + 1] - t.slot0;
+  t.t0 = (tt - a.tt_prefix[lo]) * MN;
+  t.nt = min(MN, n - t.t0);
+  return t;
+}
+
+template <int T, int NMAT>
+__global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs a,
+                                                                     const __grid_constant__ CUtensorMap tmap_b) {
+  extern __shared__ uint8_t msm_raw[];
+  __shared__ __align__(8) uint64_t raw_full[M_RAWS], raw_empty[M_RAWS], op_full[M_OPS], op_empty[M_OPS];
+  __shared__ __align__(8) uint64_t acc_full, acc_empty;
+  __shared__ uint32_t tmem_base_sh;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_large = *a.n_list;
+  const int row_tiles = (a.rows + MM - 1) / MM;
+  const int total = n_large > 0 ? a.tt_prefix[n_large] * row_tiles : 0;
+  if ((int)blockIdx.x >= total) return;
+  const MmaSmem L = mma_smem(T, NMAT);
+  uint8_t* msm = msm_raw + ((1024 - (smem_u32(msm_raw) & 1023)) & 1023);
+  uint8_t* ops = msm;
+  uint8_t* raws = msm + M_OPS * L.op_bytes;
+  const int nkc = a.cols / MK;
+  const int nsb = tiled_nsb(T, a.cols);
+  const int64_t tile_bytes = tiled_tile_bytes(T, a.cols);
+  const int prows = (int)padded_rows(a.rows);
+  const uint32_t tcols = NMAT * MN;  // 128 or 256 TMEM columns
+
+  if (tid == 0) {
+    for (int i = 0; i < M_RAWS; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], 4);
+    }
+    for (int i = 0; i < M_OPS; ++i) {
+      mbar_init(&op_full[i], 1 + 4);
+      mbar_init(&op_empty[i], 1);
+    }
+    mbar_init(&acc_full, 1);
+    mbar_init(&acc_empty, 4);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                 "r"(tcols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int raw_it = 0, op_it = 0;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        const Tile t = tile_of(a, w, row_tiles, n_large);
+        const int n_rt = min(8, (prows - MM * t.rt) / kTileRows);
+        for (int kc = 0; kc < nkc && ok; ++kc) {
+          const int sb = kc >> 2;
+          if ((kc & 3) == 0) {
+            const int r = raw_it % M_RAWS;
+            if (raw_it >= M_RAWS && !mbar_wait(&raw_empty[r], ((raw_it / M_RAWS) & 1) ^ 1, a.status)) {
+              ok = false;
+              break;
+            }
+            const uint32_t sbytes = (uint32_t)tiled_sbt_bytes(T, a.cols, sb);
+            mbar_expect_tx(&raw_full[r], sbytes * n_rt * NMAT);
+            uint8_t* rbase = raws + r * L.raw_bytes;
+#pragma unroll
+            for (int mt = 0; mt < NMAT; ++mt) {
+              const uint8_t* src = a.w[mt] + (int64_t)(t.e - a.expert_base) * a.expert_stride +
+                                   (int64_t)(8 * t.rt) * tile_bytes + tiled_sb_offset(T, a.cols, sb);
+              for (int x = 0; x < n_rt; ++x)
+                bulk_g2s(rbase + (mt * 8 + x) * max_sbt_bytes(T), src + x * tile_bytes, sbytes, &raw_full[r]);
+            }
+            ++raw_it;
+          }
+          const int o = op_it % M_OPS;
+          if (op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&op_full[o], B_BYTES);
+          tma_load_2d(ops + o * L.op_bytes + NMAT * A_BYTES, &tmap_b, kc * MK, t.slot0 + t.t0, &op_full[o]);
+          ++op_it;
+        }
+      }
+      // Drain: every issued copy lands before the CTA may exit.
+      for (int i = std::max(0, op_it - M_OPS); i < op_it; ++i)
+        mbar_wait(&op_full[i % M_OPS], (i / M_OPS) & 1, a.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int op_it = 0, tile_it = 0;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++tile_it) {
+        const Tile t = tile_of(a, w, row_tiles, n_large);
+        const int n = ((t.nt + 15) / 16) * 16;
+        const uint32_t idesc = f16_idesc(n);
+        if (tile_it > 0 && !mbar_wait(&acc_empty, (tile_it - 1) & 1, a.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kc = 0; kc < nkc; ++kc) {
+          const int o = op_it % M_OPS;
+          if (!mbar_wait(&op_full[o], (op_it / M_OPS) & 1, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(ops + o * L.op_bytes);
+          const uint32_t sbb = sa + NMAT * A_BYTES;
+#pragma unroll
+          for (int k16 = 0; k16 < MK / 16; ++k16) {
+            const uint64_t bd = sw128_desc(sbb + 32 * k16);
+            const uint32_t acc = (kc > 0 || k16 > 0) ? 1u : 0u;
+#pragma unroll
+            for (int mt = 0; mt < NMAT; ++mt)
+              umma_f16(tmem + mt * MN, sw128_desc(sa + mt * A_BYTES + 32 * k16), bd, idesc, acc);
+          }
+          umma_commit(&op_empty[o]);
+          ++op_it;
+        }
+        if (!ok) break;
+        umma_commit(&acc_full);
+      }
+      // Drain: the tensor core has finished with TMEM before it is freed.
+      if (op_it > 0) mbar_wait(&op_empty[(op_it - 1) % M_OPS], ((op_it - 1) / M_OPS) & 1, a.status);
+    }
+  } else {
+    // Dequantisation warps: thread t = weight row t of the tile.
+    const int m = tid - 64, rt_local = m >> 4, rr = m & 15;
+    int raw_it = 0, op_it = 0, tile_it = 0;
+    for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++tile_it) {
+      const Tile t = tile_of(a, w, row_tiles, n_large);
+      int r = 0;
+      for (int kc = 0; kc < nkc; ++kc) {
+        const int sb = kc >> 2, kk = kc & 3;
+        if (kk == 0) {
+          r = raw_it % M_RAWS;
+          if (!mbar_wait(&raw_full[r], (raw_it / M_RAWS) & 1, a.status)) ok = false;
+        }
+        const int o = op_it % M_OPS;
+        if (op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status)) ok = false;
+        if (ok) {
+          uint8_t* A = ops + o * L.op_bytes;
+          const uint8_t* rb = raws + r * L.raw_bytes;
+#pragma unroll
+          for (int mt = 0; mt < NMAT; ++mt) {
+            const uint8_t* sbt = rb + (mt * 8 + rt_local) * max_sbt_bytes(T);
+            if (T == T_Q4_K) dq_q4k(sbt, rr, kk, A + mt * A_BYTES, m);
+            else if (T == T_Q6_K) dq_q6k(sbt, rr, kk, A + mt * A_BYTES, m);
+            else dq_q8_0(sbt, min(8, a.cols / 32 - 8 * sb), rr, kk, A + mt * A_BYTES, m);
+          }
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&op_full[o]);
+        ++op_it;
+        if (kk == 3 || kc == nkc - 1 || (T == T_Q8_0 && kc == nkc - 1)) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&raw_empty[r]);
+          ++raw_it;
+        }
+      }
+      (void)nsb;
+      // Epilogue: rows of this warp's TMEM quadrant.
+      if (!mbar_wait(&acc_full, tile_it & 1, a.status)) ok = false;
+      tc_fence_after();
+      const int quad = warp & 3;
+      const int row = MM * t.rt + quad * 32 + lane;
+      const int n = ((t.nt + 15) / 16) * 16;
+      if (ok) {
+        for (int c0 = 0; c0 < n; c0 += 16) {
+#pragma unroll
+          for (int mt = 0; mt < NMAT; ++mt) {
+            float v[16];
+            tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + mt * MN + c0, v);
+            if (row < a.rows) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (c0 + i < t.nt) a.out[mt][(int64_t)(t.slot0 + t.t0 + c0 + i) * a.out_stride + row] = v[i];
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols));
+}
+
+// ---- host side ------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int make_tmap_f16(void* map_out, const void* ptr, int64_t rows, int64_t cols) {
+  if (!g_encode) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return KC_ERR_CUDA;
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  if (((uintptr_t)ptr & 15) || (cols * 2) % 16) return KC_ERR_SHAPE;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)std::max<int64_t>(rows, 1)};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+  cuuint32_t box[2] = {MK, MN};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(reinterpret_cast<CUtensorMap*>(map_out), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                        const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? KC_OK : KC_ERR_CUDA;
+}
+
+bool mma_supported(int t, int64_t cols, int n_mat) {
+  if (!(t == T_Q4_K || t == T_Q6_K || t == T_Q8_0) || cols % MK != 0) return false;
+  return mma_smem(t, n_mat).total <= 227 * 1024;
+}
+
+template <int T, int NMAT>
+static int launch_t(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st) {
+  const MmaSmem L = mma_smem(T, NMAT);
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(mma_grouped_kernel<T, NMAT>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
+        cudaSuccess)
+      return KC_ERR_CUDA;
+    attr = true;
+  }
+  const int grid = std::max(1, std::min(num_sms(), max_tiles));
+  mma_grouped_kernel<T, NMAT><<<grid, M_THREADS, L.total, st>>>(a, *reinterpret_cast<const CUtensorMap*>(tmap));
+  return KC_OK;
+}
+
+int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st) {
+  if (max_tiles <= 0) return KC_OK;
+  if (!mma_supported(a.type, a.cols, a.n_mat)) return KC_ERR_SHAPE;
+  if (a.n_mat == 2) {
+    if (a.type == T_Q4_K) return launch_t<T_Q4_K, 2>(a, tmap, max_tiles, st);
+    if (a.type == T_Q6_K) return launch_t<T_Q6_K, 2>(a, tmap, max_tiles, st);
+    return launch_t<T_Q8_0, 2>(a, tmap, max_tiles, st);
+  }
+  if (a.type == T_Q4_K) return launch_t<T_Q4_K, 1>(a, tmap, max_tiles, st);
+  if (a.type == T_Q6_K) return launch_t<T_Q6_K, 1>(a, tmap, max_tiles, st);
+  return launch_t<T_Q8_0, 1>(a, tmap, max_tiles, st);
+}
+
+// Gather + convert activation rows to f16: dst[i] = f16(src[map[i]]) (map may
+// be null: identity). One thread per 8 elements.
+__global__ void gather_f16_kernel(const float* __restrict__ src, const int* __restrict__ map, int64_t n_rows,
+                                  int64_t cols, __half* __restrict__ dst) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t per = cols / 8;
+  if (i >= n_rows * per) return;
+  const int64_t r = i / per, c = (i % per) * 8;
+  const int64_t sr = map ? map[r] : r;
+  const float4 a0 = *reinterpret_cast<const float4*>(src + sr * cols + c);
+  const float4 a1 = *reinterpret_cast<const float4*>(src + sr * cols + c + 4);
+  __half2 h[4] = {__floats2half2_rn(a0.x, a0.y), __floats2half2_rn(a0.z, a0.w), __floats2half2_rn(a1.x, a1.y),
+                  __floats2half2_rn(a1.z, a1.w)};
+  *reinterpret_cast<uint4*>(dst + r * cols + c) = *reinterpret_cast<uint4*>(h);
+}
+
+void launch_gather_f16(const float* src, const int* map, int64_t n_rows, int64_t cols, __half* dst,
+                       cudaStream_t st) {
+  const int64_t n = n_rows * (cols / 8);
+  if (n <= 0) return;
+  gather_f16_kernel<<<ceil_div(n, 256), 256, 0, st>>>(src, map, n_rows, cols, dst);
+}
+
+}  // namespace kc

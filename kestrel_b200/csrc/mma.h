@@ -1,0 +1,34 @@
+// tcgen05 grouped GEMM (mma.cu): experts with >= 4 rows and dense n >= 4.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kc {
+
+struct MmaArgs {
+  const uint8_t* w[2];    // gate, up (n_mat = 2) or one matrix
+  int n_mat;
+  int64_t expert_stride;  // device bytes of one expert's matrix
+  int expert_base;
+  int rows, cols, type;
+  const int* list;        // experts to process
+  const int* n_list;      // device scalar
+  const int* offsets;     // [E+1] slot ranges
+  const int* tt_prefix;   // [n_list+1]: prefix of ceil(rows_e / 128) token tiles
+  float* out[2];          // out[m][slot * out_stride + row]
+  int64_t out_stride;
+  int* status;
+};
+
+// 128-byte CUtensorMap for an f16 row-major [rows, cols] activation matrix,
+// box 64 x 128, 128B swizzle.
+int make_tmap_f16(void* map_out, const void* ptr, int64_t rows, int64_t cols);
+bool mma_supported(int t, int64_t cols, int n_mat);
+int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st);
+// dst[i, :] = f16(src[map[i], :]) (map null: identity); cols % 8 == 0.
+void launch_gather_f16(const float* src, const int* map, int64_t n_rows, int64_t cols, __half* dst,
+                       cudaStream_t st);
+
+}  // namespace kc

@@ -240,15 +240,21 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
   }
   __syncthreads();
   if (tid == 0) {
-    int run = 0, ns = 0, nl = 0;
+    int run = 0, ns = 0, nl = 0, tt = 0;
     for (int e = 0; e < E; ++e) {
       offs[e] = run;
       o.offsets[e] = run;
       o.counts[e] = cnt[e];
       run += cnt[e];
-      if (cnt[e] >= 1 && cnt[e] <= 3) o.small_list[ns++] = e;
-      else if (cnt[e] >= 4) o.large_list[nl++] = e;
+      if (cnt[e] >= 1 && cnt[e] <= 3) {
+        o.small_list[ns++] = e;
+      } else if (cnt[e] >= 4) {
+        o.large_tt[nl] = tt;
+        tt += (cnt[e] + 127) / 128;
+        o.large_list[nl++] = e;
+      }
     }
+    o.large_tt[nl] = tt;
     offs[E] = run;
     o.offsets[E] = run;
     o.n_lists[0] = ns;
@@ -313,6 +319,8 @@ __global__ void dense_meta_kernel(int n, DispatchOut o) {
   o.large_list[0] = 0;
   o.n_lists[0] = (n >= 1 && n <= 3) ? 1 : 0;
   o.n_lists[1] = n >= 4 ? 1 : 0;
+  o.large_tt[0] = 0;
+  o.large_tt[1] = n >= 4 ? (n + 127) / 128 : 0;
 }
 
 void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st) { dense_meta_kernel<<<1, 1, 0, st>>>(n, o); }
