@@ -183,6 +183,15 @@ __device__ __forceinline__ uint2 ldg2(const uint8_t* p) { return __ldg(reinterpr
 __device__ __forceinline__ int4 ldg4i(const uint8_t* p) { return __ldg(reinterpret_cast<const int4*>(p)); }
 __device__ __forceinline__ float ldgf(const uint8_t* p) { return __ldg(reinterpret_cast<const float*>(p)); }
 
+// Scale and min of Q4_K sub-block jj for a runtime jj (scale_min_k4,
+// quant.rs:54-60), using shifts only.
+__device__ __forceinline__ void q4k_sm_rt(int jj, uint32_t w0, uint32_t w1, uint32_t w2, int& s, int& m) {
+  const int sh = 8 * (jj & 3);
+  const uint32_t A = (w0 >> sh) & 0xFF, B = (w1 >> sh) & 0xFF, C = (w2 >> sh) & 0xFF;
+  s = jj < 4 ? (int)(A & 63) : (int)((C & 0xF) | ((A >> 6) << 4));
+  m = jj < 4 ? (int)(B & 63) : (int)((C >> 4) | ((B >> 6) << 4));
+}
+
 struct RowAcc {
   float a0[DMAXS], a1[DMAXS], summs[DMAXS];
 };
@@ -205,9 +214,11 @@ __device__ __forceinline__ void q4k_superblock(const uint8_t* __restrict__ sbt, 
     hi[k][1] = (int)((w.y >> 4) & 0x0F0F0F0Fu);
   }
   const float dw = h2f(hdr.x), dmw = h2f(hdr.x >> 16);
-  // Sub-blocks 2q and 2q+1 of the min term, summed over the quad below.
-  const int mq0 = q == 0 ? mn[0] : q == 1 ? mn[2] : q == 2 ? mn[4] : mn[6];
-  const int mq1 = q == 0 ? mn[1] : q == 1 ? mn[3] : q == 2 ? mn[5] : mn[7];
+  // Sub-blocks 2q and 2q+1 of the min term (decoded with shifts: no indexed
+  // register arrays), summed over the quad below.
+  int mq0, mq1, dummy;
+  q4k_sm_rt(2 * q, hdr.y, hdr.z, hdr.w, dummy, mq0);
+  q4k_sm_rt(2 * q + 1, hdr.y, hdr.z, hdr.w, dummy, mq1);
 #pragma unroll
   for (int s = 0; s < NS; ++s) {
     const uint8_t* x = xa[s];
@@ -247,7 +258,7 @@ __device__ __forceinline__ void q6k_superblock(const uint8_t* __restrict__ sbt, 
   for (int h = 0; h < 2; ++h) qh[h] = *reinterpret_cast<const uint2*>(sbt + 2048 + 512 * h + 32 * rr + 8 * q);
   const int jh = q >> 1;
   const uint32_t sw[4] = {scw.x, scw.y, scw.z, scw.w};
-  const uint32_t swq = q == 0 ? scw.x : q == 1 ? scw.y : q == 2 ? scw.z : scw.w;  // offsets m = 4q..4q+3
+  const uint32_t swq = (q & 2) ? ((q & 1) ? scw.w : scw.z) : ((q & 1) ? scw.y : scw.x);  // offsets m = 4q..4q+3
   int qv[8][2], scl[8];
 #pragma unroll
   for (int h = 0; h < 2; ++h)
@@ -394,7 +405,7 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
       const int m = (int)((u / tiles) % a.n_mat);
       const int r0 = (int)(u % tiles) * DR;
       const int e = li - li0 < DMETA ? meta[li - li0].e : a.list[li];
-      const uint8_t* wb = a.w[m] + (int64_t)(e - a.expert_base) * a.expert_stride + (int64_t)(r0 / DR) * g.tile_bytes;
+      const uint8_t* wb = (m == 0 ? a.w[0] : a.w[1]) + (int64_t)(e - a.expert_base) * a.expert_stride + (int64_t)(r0 / DR) * g.tile_bytes;
       for (int seg = 0; seg < g.nseg; ++seg, ++sid) {
         const int st = (int)(sid % n_stages);
         const uint32_t ph = (uint32_t)((sid / n_stages) & 1);
@@ -432,7 +443,7 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
     const UnitMeta um = li - li0 < DMETA ? meta[li - li0] : load_meta(a, li);
     const int r_out = row < nr ? r0 + row : -1;  // padding rows (zeros) are computed, not stored
     const int64_t stage0 = (u - beg) * g.nseg;
-    float* out = a.out[m];
+    float* out = m == 0 ? a.out[0] : a.out[1];
     if (um.ns == 1) run_unit<T, 1>(a, g, smem, full, empty, stage0, n_stages, row, q, r_out, um, out, ok);
     else if (um.ns == 2) run_unit<T, 2>(a, g, smem, full, empty, stage0, n_stages, row, q, r_out, um, out, ok);
     else run_unit<T, 3>(a, g, smem, full, empty, stage0, n_stages, row, q, r_out, um, out, ok);
