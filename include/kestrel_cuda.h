@@ -179,6 +179,28 @@ enum {
 KC_API int kc_profile_enable(kc_ctx* ctx, int on);
 KC_API int kc_profile_read(kc_ctx* ctx, double* stage_ms, int64_t* stage_calls, int n_stages);
 
+/* ---- routing without device allocation ----------------------------------
+   No counterpart in Kestrel: an addition for hosts that cannot let a library
+   allocate device memory -- a session whose memory ledger must account for
+   every byte, a latency-critical decode thread that cannot afford the
+   device-wide synchronisation cudaMalloc/cudaFree may cause, or an embedding
+   that hands out device memory only from its own pool. Computes what kc_router_logits_dev followed by
+   kc_route_dev compute (router logits in the reference's operation order,
+   softmax, top-k, optional renormalisation and weights_scale) on device
+   buffers, enqueued on `stream` (NULL = legacy default stream), with no
+   cudaMalloc/cudaFree: the logits live in a fixed array compiled into the
+   library (65536 floats, 256 KB, held on every GPU that loads the library
+   until the process exits). Needs no context; errors are read with
+   kc_last_error(NULL).
+   Limits: n_tok * n_expert <= 65536 (larger requests return KC_ERR_SHAPE);
+   1 <= k <= min(64, n_expert); n_expert <= 1024.
+   The first call on each device looks up the array's device address; make
+   that first call before capturing a stream. All calls on a device share the
+   one array: calls whose kernels may overlap on the GPU (different streams
+   without ordering) race, so serialise them. */
+KC_API int kc_route_noalloc(const float* router_w, int n_expert, int d, const float* h, int n_tok, int k,
+                            int norm_topk, float weights_scale, int32_t* topk_ids, float* topk_w, void* stream);
+
 /* ---- expert parallelism (one process per GPU, NCCL over NVLink) -------- */
 
 /* 128-byte NCCL unique id, created on one rank and shared by the host. */

@@ -305,6 +305,10 @@ GroupedArgs grouped_base(kc_ctx* ctx) {
 }  // namespace
 
 namespace kc {
+// Message returned by kc_last_error(NULL) on this thread (entry points
+// without a context).
+void set_global_error(const char* msg) { g_init_err = msg ? msg : ""; }
+
 int num_sms() {
   static int dev = -1, sms = 0;
   int cur = 0;

@@ -50,6 +50,7 @@ SIGNATURES = {
     "kc_quantize_dev": (I, [P, I, P, I64, I64, P]),
     "kc_profile_enable": (I, [P, I]),
     "kc_profile_read": (I, [P, P, P, I]),
+    "kc_route_noalloc": (I, [P, I, I, P, I, I, I, F, P, P, P]),
     "kc_ep_unique_id": (I, [ctypes.c_char_p]),
     "kc_ep_init": (I, [P, I, I, ctypes.c_char_p]),
 }
