@@ -172,10 +172,10 @@ bool type_ok(int t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0; }
 bool is_k(int t) { return t == T_Q4_K || t == T_Q6_K; }
 
 size_t al(size_t v) { return (v + 255) & ~size_t(255); }
-// Bytes of one activation-record row of `cols` values (the larger of the Q8_K
-// and Q8 formats).
+// Bytes of the activation records of one slot of `cols` values (the larger of
+// the Q8_K and Q8 formats).
 size_t rec_bytes(int64_t cols) {
-  return (size_t)std::max(act_rec_stride(true, cols), act_rec_stride(false, cols)) + 512;
+  return (size_t)std::max(rec_row_bytes(true, cols), rec_row_bytes(false, cols)) + 512;
 }
 
 // (Re)allocate the workspace so it holds at least the given dimensions.
@@ -197,7 +197,7 @@ int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
       (size_t)T * E * 4,                 // logits
       A * 4, A * 4,                      // ids, w
       (size_t)T * D, (size_t)T * (D / 32 + 1) * 4, (size_t)T * (D / 16 + 1) * 4,  // xq xd xs
-      (size_t)T * rec_bytes(D),          // xrec
+      A * rec_bytes(D),                  // xrec
       (size_t)E * 4, (size_t)(E + 1) * 4, A * 4, A * 4, A * 4, (size_t)E * 4, (size_t)E * 4, 16,  // meta
       (size_t)(E + 1) * 4,               // large_tt
       A * F * 4, A * F * 4,              // g, u
@@ -350,15 +350,17 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
       RC(launch_dispatch(W.ids, W.w, n_tok, k, E, W.meta, st));
       CKL();
     }
-    // 3. activation records of the input rows (int8 path).
+    // 3. activation records of every slot's input row (int8 path) and its f16
+    //    copy (tensor-core path).
     const bool kq_in = is_k(L.t_gate), kq_dn = is_k(L.t_down);
-    {
-      StageScope ss(ctx, KC_STAGE_QUANT_X);
-      launch_act_records(kq_in, h, nullptr, n_tok, d, W.xrec, nullptr, nullptr, st);
-      CKL();
-    }
     const int A = n_tok * k;
     const int max_small = std::min(E, A);
+    const bool mma_gu = mma_supported(L.t_gate, d, 2);
+    {
+      StageScope ss(ctx, KC_STAGE_QUANT_X);
+      launch_act_records(kq_in, h, nullptr, W.meta.slot_tok, A, d, W.xrec, A, nullptr, mma_gu ? W.x16 : nullptr, st);
+      CKL();
+    }
     // 4. gate and up products -> g, u [slot, ff].
     {
       StageScope ss(ctx, KC_STAGE_GATE_UP_INT8);
@@ -374,21 +376,18 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
       dg.list = W.meta.small_list;
       dg.n_list = W.meta.n_lists;
       dg.offsets = W.meta.offsets;
-      dg.slot_src = W.meta.slot_tok;
-      dg.act = W.xrec;
-      dg.act_stride = act_rec_stride(kq_in, d);
+      dg.rec = W.xrec;
+      dg.rec_slots = A;
       dg.out[0] = W.g;
       dg.out[1] = W.u;
       dg.out_stride = ff;
       dg.status = ctx->status;
-      RC(launch_decode(dg, max_small * 2 * ceil_div(ff, 16), st));
+      RC(launch_decode(dg, max_small * 2 * ceil_div(ff, kTileRows), st));
       CKL();
     }
     const int max_tt = ceil_div(A, 128) + std::min(E, A / 4);
-    if (mma_supported(L.t_gate, d, 2)) {
+    if (mma_gu) {
       StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
-      launch_gather_f16(h, W.meta.slot_tok, A, d, W.x16, st);
-      CKL();
       alignas(64) unsigned char tmap[128];
       if (make_tmap_f16(tmap, W.x16, A, d) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
       MmaArgs ma{};
@@ -434,7 +433,7 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
     // 5. SwiGLU of every slot -> act (f32) and its activation records.
     {
       StageScope ss(ctx, KC_STAGE_QUANT_ACT);
-      launch_act_records(kq_dn, W.g, W.u, A, ff, W.arec, W.act, W.act16, st);
+      launch_act_records(kq_dn, W.g, W.u, nullptr, A, ff, W.arec, A, W.act, W.act16, st);
       CKL();
     }
     // 6. down -> y [slot, d].
@@ -451,13 +450,12 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
       dd.list = W.meta.small_list;
       dd.n_list = W.meta.n_lists;
       dd.offsets = W.meta.offsets;
-      dd.slot_src = nullptr;
-      dd.act = W.arec;
-      dd.act_stride = act_rec_stride(kq_dn, ff);
+      dd.rec = W.arec;
+      dd.rec_slots = A;
       dd.out[0] = W.y;
       dd.out_stride = d;
       dd.status = ctx->status;
-      RC(launch_decode(dd, max_small * ceil_div(d, 16), st));
+      RC(launch_decode(dd, max_small * ceil_div(d, kTileRows), st));
       CKL();
     }
     if (mma_supported(L.t_down, ff, 1) && ff % 256 == 0) {
@@ -796,7 +794,7 @@ int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out)
   a.out_stride = D.rows;
   if (n < 4) {
     const bool kq = is_k(D.t);
-    launch_act_records(kq, x, nullptr, n, D.cols, W.xrec, nullptr, nullptr, st);
+    launch_act_records(kq, x, nullptr, nullptr, n, D.cols, W.xrec, n, nullptr, nullptr, st);
     CKL();
     DecodeArgs dv{};
     dv.w[0] = D.w;
@@ -807,14 +805,14 @@ int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out)
     dv.list = W.meta.small_list;
     dv.n_list = W.meta.n_lists;
     dv.offsets = W.meta.offsets;
-    dv.act = W.xrec;
-    dv.act_stride = act_rec_stride(kq, D.cols);
+    dv.rec = W.xrec;
+    dv.rec_slots = n;
     dv.out[0] = out;
     dv.out_stride = D.rows;
     dv.status = ctx->status;
-    RC(launch_decode(dv, ceil_div(D.rows, 16), st));
+    RC(launch_decode(dv, ceil_div(D.rows, kTileRows), st));
   } else if (mma_supported(D.t, D.cols, 1)) {
-    launch_gather_f16(x, nullptr, n, D.cols, W.x16, st);
+    launch_act_records(is_k(D.t), x, nullptr, nullptr, n, D.cols, nullptr, n, nullptr, W.x16, st);
     CKL();
     alignas(64) unsigned char tmap[128];
     if (make_tmap_f16(tmap, W.x16, n, D.cols) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");

@@ -19,24 +19,26 @@ enum : int { T_F32 = 0, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
 
 // ----------------------------------------------------------------------------
 // Device weight layouts. Quantized matrices are stored "tiled": rows are
-// grouped in tiles of 16 (the row count is padded to a multiple of 16 with
-// zero rows), and inside a tile the bytes are laid out superblock-major with
-// one plane per field, so that
-//  * the 16 rows x a run of superblocks a decode stage needs are one
+// grouped in tiles of 32 (the row count is padded to a multiple of 32 with
+// zero rows), and inside a tile the bytes are superblock-major. Within one
+// superblock of a tile every field is stored as planes of 16-byte row chunks,
+// [chunk][32 rows][16 B], so that
+//  * the 32 rows x a run of superblocks a decode stage needs are one
 //    contiguous range (one bulk copy of several KB), and
-//  * the reads of four consecutive rows by a quarter warp fall on distinct
-//    shared-memory banks without padding.
-// Per superblock-tile (16 rows):
-//   Q4_K  (2304 B): hdr[16 rows][16 B] (d, dmin, 12 scale bytes)
-//                   | qs[k = 0..3][16 rows][32 B]
-//   Q6_K  (3360 B): ql[c = 0..3][16 rows][32 B]   (c = 2*half + 32-byte run)
-//                   | qh[h = 0..1][16 rows][32 B] | sc[16 rows][16 B]
-//                   | d[16 rows][2 B]
-//   Q8_0  chunk of up to 8 blocks (512*nblk + 256 B):
-//                   qs[block][16 rows][32 B] | d[16 rows][8 x 2 B]
+//  * a warp whose thread i reads row i's chunk c touches 512 contiguous
+//    bytes of shared memory (no bank conflicts).
+// Per superblock-tile (32 rows), offsets in bytes:
+//   Q4_K  (4608 B): hdr[32][16 B] (d, dmin, 12 scale bytes) at 0
+//                   | qs chunk c = 0..7 (qs bytes 16c..16c+15) at 512 + 512c
+//   Q6_K  (6720 B): ql chunk c = 0..7 at 512c | qh chunk c = 0..3 at 4096 + 512c
+//                   | sc[32][16 B] at 6144 | d[32][2 B] at 6656
+//   Q8_0  chunk of nblk <= 8 blocks (1024*nblk + 512 B):
+//                   qs chunk c = 0..2*nblk-1 (block c/2, bytes 16*(c%2)..) at 512c
+//                   | d[32][8 x 2 B] at 1024*nblk
 // The bytes are a permutation of GGUF's (plus zero padding); the arithmetic
 // on them is unchanged. F32 matrices stay row-major (rows padded to 16 B).
-constexpr int kTileRows = 16;
+constexpr int kTileRows = 32;
+constexpr int kPlane = kTileRows * 16;  // one 16-byte chunk of every row of a tile
 
 __host__ __device__ inline int64_t round16(int64_t v) { return (v + 15) & ~int64_t(15); }
 
@@ -44,19 +46,19 @@ __host__ __device__ inline int64_t round16(int64_t v) { return (v + 15) & ~int64
 __host__ __device__ inline int tiled_nsb(int t, int64_t cols) {
   return t == T_Q8_0 ? (int)((cols / 32 + 7) / 8) : (int)(cols / 256);
 }
-// Bytes of superblock-tile `sb` (Q8_0: chunk sb) of one 16-row tile.
+// Bytes of superblock-tile `sb` (Q8_0: chunk sb) of one tile.
 __host__ __device__ inline int tiled_sbt_bytes(int t, int64_t cols, int sb) {
-  if (t == T_Q4_K) return 2304;
-  if (t == T_Q6_K) return 3360;
+  if (t == T_Q4_K) return 4608;
+  if (t == T_Q6_K) return 6720;
   const int nb32 = (int)(cols / 32);
   const int nblk = nb32 - 8 * sb < 8 ? nb32 - 8 * sb : 8;
-  return 512 * nblk + 256;
+  return 1024 * nblk + 512;
 }
 // Byte offset of superblock-tile sb inside a tile.
 __host__ __device__ inline int64_t tiled_sb_offset(int t, int64_t cols, int sb) {
-  if (t == T_Q4_K) return 2304ll * sb;
-  if (t == T_Q6_K) return 3360ll * sb;
-  return 4352ll * sb;  // all chunks before the last are full
+  if (t == T_Q4_K) return 4608ll * sb;
+  if (t == T_Q6_K) return 6720ll * sb;
+  return 8704ll * sb;  // all chunks before the last are full
 }
 __host__ __device__ inline int64_t tiled_tile_bytes(int t, int64_t cols) {
   const int nsb = tiled_nsb(t, cols);

@@ -3,24 +3,25 @@
 // experts with 1..3 routed rows and dense products with n < 4.
 //
 // Memory-bound design:
-//  * Work unit = 16 rows of one expert matrix. A unit is streamed through one
-//    or more pipeline stages (K segments of up to 8 superblocks). Activation
-//    records (interleaved Q8_K: q[256] | bsums[16] | d per superblock) are
-//    read through the read-only L1 path, where the few rows of an expert
-//    stay hot; per-unit metadata (expert, slots, record rows) is loaded once
-//    into shared memory.
-//  * Weights are in the tiled device layout (common.cuh): a stage (16 rows x
-//    2 superblocks, ~4.6-6.7 KB) is one contiguous range fetched by a single
-//    cp.async.bulk into a ring of up to 48 stages tracked by mbarriers, so
-//    ~170 KB per SM is in flight while consumers hold only the stages they
-//    are computing; four consecutive rows read by a quarter warp fall on
-//    distinct banks by construction.
-//  * Six consumer pairs (2 warps, 64 threads) take units round-robin. Four
-//    threads own a row: thread q holds lanes 2q and 2q+1 of the reference's
-//    eight 32-bit AVX2 lanes. Integer sums are exact in any order; the float
-//    FMA chain over superblocks runs in the reference's order inside each
-//    thread, and the lanes are folded with hsum's tree via shuffles.
+//  * Work unit = one 32-row tile of one expert matrix, streamed through the
+//    row's K segments. A CTA owns a contiguous range of units; its consumer
+//    warps take them DW at a time (a "group"), one unit per warp, and the
+//    producer issues the group's stages segment-major (segment 0 of every
+//    warp's unit, then segment 1, ...), so all warps advance together through
+//    a deep ring of stages.
+//  * A stage is the 32 rows x `ks` superblocks of a segment: one contiguous
+//    range of the tiled device layout (common.cuh), fetched by a single
+//    cp.async.bulk into a ring tracked by mbarriers (~200 KB per SM).
+//  * One thread owns one weight row and all eight of the reference's 32-bit
+//    AVX2 lanes, so scales are decoded once per row-superblock and the float
+//    chains (per-lane FMA over superblocks, then hsum) run in one thread in
+//    the reference's order. Integer sums are exact in any order.
+//  * The slots' activation records (int8 values, block sums, scale) for the
+//    next segment are copied by each warp with cp.async into a double buffer
+//    while the current segment is computed; every thread of the warp then
+//    reads them as shared-memory broadcasts.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "decode.h"
@@ -28,57 +29,55 @@
 
 namespace kc {
 
-constexpr int DR = 16;             // rows per unit
-constexpr int DPAIRS = 6;          // consumer pairs
-constexpr int DTHREADS = 32 + DPAIRS * 64;
-constexpr int DMAX_STAGES = 48;
-constexpr int DMAXS = 3;           // activation rows per unit
+constexpr int DR = kTileRows;  // rows per unit: one per lane
+constexpr int DW = 8;          // consumer warps
+constexpr int DTHREADS = 32 * (DW + 1);
+constexpr int DMAX_STAGES = 64;
+constexpr int DMAXS = 3;       // slots per unit (experts with 1..3 rows)
+constexpr int DSMEM = 220 * 1024;
+constexpr int DMETA = 96;
 
 // ---------------------------------------------------------------------------
-// Activation records. Q8_K (K-quant weights): per superblock 336 bytes =
-// q[256] int8 | bsums[16] int32 | d f32 | pad. Q8 (Q8_0 weights): per chunk of
-// 8 blocks 288 bytes = q[256] int8 | d[8] f32. Record stride = bytes per row.
-__device__ __forceinline__ int64_t q8k_rec_stride(int64_t cols) { return cols / 256 * 336; }
-__device__ __forceinline__ int64_t q8_rec_stride(int64_t cols) { return (cols / 32 + 7) / 8 * 288; }
-
-// Q8KRow::quantize (qdot.rs:347-367) into records; optional SwiGLU first.
-// One warp per (row, superblock): lane l owns elements 8l..8l+7.
-__device__ __forceinline__ int i8_of4(uint32_t w, int b) { return (int)(int8_t)((w >> (8 * b)) & 0xFF); }
-
+// Activation records (layout in decode.h).
+// Q8KRow::quantize (qdot.rs:347-367); optional SwiGLU first. One warp per
+// (slot, superblock): lane l owns elements 8l..8l+7.
 template <bool SWIGLU>
-__global__ void q8k_records_kernel(const float* __restrict__ x, const float* __restrict__ u, int64_t n_rows,
-                                   int64_t cols, uint8_t* __restrict__ rec, float* __restrict__ f32out,
+__global__ void q8k_records_kernel(const float* __restrict__ x, const float* __restrict__ u,
+                                   const int* __restrict__ slot_src, int64_t n_slots, int64_t cols,
+                                   uint8_t* __restrict__ rec, int64_t rec_slots, float* __restrict__ f32out,
                                    __half* __restrict__ f16out) {
   const int64_t nb = cols / 256;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  if (gw >= n_rows * nb) return;
-  const int64_t r = gw / nb, b = gw % nb;
-  const float* xp = x + r * cols + b * 256 + lane * 8;
+  if (gw >= n_slots * nb) return;
+  const int64_t slot = gw / nb, b = gw % nb;
+  const int64_t src = slot_src ? slot_src[slot] : slot;
+  const float* xp = x + src * cols + b * 256 + lane * 8;
   float v[8];
   {
     float4 a0 = reinterpret_cast<const float4*>(xp)[0], a1 = reinterpret_cast<const float4*>(xp)[1];
     v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
   }
   if (SWIGLU) {
-    const float* up = u + r * cols + b * 256 + lane * 8;
+    const float* up = u + src * cols + b * 256 + lane * 8;
     float4 b0 = reinterpret_cast<const float4*>(up)[0], b1 = reinterpret_cast<const float4*>(up)[1];
     float w[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i)  // transformer.rs:558: g / (1 + exp(-g)) * u
       v[i] = __fmul_rn(__fdiv_rn(v[i], __fadd_rn(1.0f, expf(-v[i]))), w[i]);
     if (f32out) {
-      float4* o = reinterpret_cast<float4*>(f32out + r * cols + b * 256 + lane * 8);
+      float4* o = reinterpret_cast<float4*>(f32out + slot * cols + b * 256 + lane * 8);
       o[0] = make_float4(v[0], v[1], v[2], v[3]);
       o[1] = make_float4(v[4], v[5], v[6], v[7]);
     }
-    if (f16out) {
-      __half2 h[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-      *reinterpret_cast<uint4*>(f16out + r * cols + b * 256 + lane * 8) = *reinterpret_cast<uint4*>(h);
-    }
   }
+  if (f16out) {
+    __half2 h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(f16out + slot * cols + b * 256 + lane * 8) = *reinterpret_cast<uint4*>(h);
+  }
+  if (!rec) return;
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -94,65 +93,82 @@ __global__ void q8k_records_kernel(const float* __restrict__ x, const float* __r
     s += qi;
     packed[i / 4] |= (uint32_t)(qi & 0xFF) << (8 * (i % 4));
   }
-  s += __shfl_xor_sync(0xffffffffu, s, 1);
-  uint8_t* rb = rec + r * q8k_rec_stride(cols) + b * 336;
+  const int s16 = s + __shfl_xor_sync(0xffffffffu, s, 1);     // bsums[lane / 2]
+  const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);  // bsums pair lane / 4
+  uint8_t* rb = rec + (b * rec_slots + slot) * kRecK;
   *reinterpret_cast<uint2*>(rb + lane * 8) = make_uint2(packed[0], packed[1]);
-  if ((lane & 1) == 0) reinterpret_cast<int32_t*>(rb + 256)[lane / 2] = s;
-  if (lane == 0) reinterpret_cast<float*>(rb + 320)[0] = scale;
+  if ((lane & 1) == 0) reinterpret_cast<int16_t*>(rb + 256)[lane / 2] = (int16_t)s16;
+  if ((lane & 3) == 0) reinterpret_cast<int16_t*>(rb + 288)[lane / 4] = (int16_t)s32;
+  if (lane == 0) reinterpret_cast<float*>(rb + 304)[0] = scale;
+  if (lane >= 1 && lane < 4) reinterpret_cast<uint32_t*>(rb + 304)[lane] = 0u;
 }
 
-// Q8Row::quantize (qdot.rs:29-49) into records; optional SwiGLU first. One
-// warp per 32-block.
+// Q8Row::quantize (qdot.rs:29-49); optional SwiGLU first. One warp per
+// (slot, 32-block).
 template <bool SWIGLU>
-__global__ void q8_records_kernel(const float* __restrict__ x, const float* __restrict__ u, int64_t n_rows,
-                                  int64_t cols, uint8_t* __restrict__ rec, float* __restrict__ f32out,
+__global__ void q8_records_kernel(const float* __restrict__ x, const float* __restrict__ u,
+                                  const int* __restrict__ slot_src, int64_t n_slots, int64_t cols,
+                                  uint8_t* __restrict__ rec, int64_t rec_slots, float* __restrict__ f32out,
                                   __half* __restrict__ f16out) {
   const int64_t nb = cols / 32;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  if (gw >= n_rows * nb) return;
-  const int64_t r = gw / nb, b = gw % nb;
-  float v = x[r * cols + b * 32 + lane];
+  if (gw >= n_slots * nb) return;
+  const int64_t slot = gw / nb, b = gw % nb;
+  const int64_t src = slot_src ? slot_src[slot] : slot;
+  float v = x[src * cols + b * 32 + lane];
   if (SWIGLU) {
-    v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u[r * cols + b * 32 + lane]);
-    if (f32out) f32out[r * cols + b * 32 + lane] = v;
-    if (f16out) f16out[r * cols + b * 32 + lane] = __float2half_rn(v);
+    v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u[src * cols + b * 32 + lane]);
+    if (f32out) f32out[slot * cols + b * 32 + lane] = v;
   }
+  if (f16out) f16out[slot * cols + b * 32 + lane] = __float2half_rn(v);
+  if (!rec) return;
   float amax = fabsf(v);
 #pragma unroll
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const float scale = __fdiv_rn(amax, 127.0f);
   const float inv = scale > 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
   const int qi = q8_round(__fmul_rn(v, inv));
-  uint8_t* rb = rec + r * q8_rec_stride(cols) + (b / 8) * 288;
+  uint8_t* rb = rec + ((b / 8) * rec_slots + slot) * kRecQ8;
   rb[(b % 8) * 32 + lane] = (uint8_t)(int8_t)qi;
   if (lane == 0) reinterpret_cast<float*>(rb + 256)[b % 8] = scale;
 }
 
-void launch_act_records(bool kquant, const float* x, const float* u, int64_t n_rows, int64_t cols, uint8_t* rec,
-                        float* f32out, __half* f16out, cudaStream_t st) {
-  const int64_t warps = n_rows * (kquant ? cols / 256 : cols / 32);
+void launch_act_records(bool kquant, const float* x, const float* u, const int* slot_src, int64_t n_slots,
+                        int64_t cols, uint8_t* rec, int64_t rec_slots, float* f32out, __half* f16out,
+                        cudaStream_t st) {
+  const int64_t warps = n_slots * (kquant ? cols / 256 : cols / 32);
   if (warps <= 0) return;
   const int grid = ceil_div(warps, 8);
   if (kquant) {
-    if (u) q8k_records_kernel<true><<<grid, 256, 0, st>>>(x, u, n_rows, cols, rec, f32out, f16out);
-    else q8k_records_kernel<false><<<grid, 256, 0, st>>>(x, u, n_rows, cols, rec, f32out, f16out);
+    if (u) q8k_records_kernel<true><<<grid, 256, 0, st>>>(x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
+    else q8k_records_kernel<false><<<grid, 256, 0, st>>>(x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
   } else {
-    if (u) q8_records_kernel<true><<<grid, 256, 0, st>>>(x, u, n_rows, cols, rec, f32out, f16out);
-    else q8_records_kernel<false><<<grid, 256, 0, st>>>(x, u, n_rows, cols, rec, f32out, f16out);
+    if (u) q8_records_kernel<true><<<grid, 256, 0, st>>>(x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
+    else q8_records_kernel<false><<<grid, 256, 0, st>>>(x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
   }
 }
 
 // ---------------------------------------------------------------------------
-// Stage geometry: a stage is one 16-row tile x a segment of `ks` consecutive
-// superblocks (Q8_0: chunks of 8 blocks), one contiguous range of the tiled
-// device layout (common.cuh), fetched with a single bulk copy.
+// Stage geometry: a stage is one 32-row tile x a segment of `ks` consecutive
+// superblocks (Q8_0: chunks of 8 blocks). KESTREL_DECODE_KS overrides ks (a
+// tuning knob; the default is two K-quant superblocks or one Q8_0 chunk of 8
+// blocks per stage, 8.7-13.4 KB).
+static int decode_ks_override() {
+  static const int v = [] {
+    const char* e = std::getenv("KESTREL_DECODE_KS");
+    return e ? std::max(0, std::atoi(e)) : 0;
+  }();
+  return v;
+}
+
 DecodeGeom decode_geom(int t, int64_t cols) {
   DecodeGeom g{};
   g.type = t;
   g.nb32 = t == T_Q8_0 ? (int)(cols / 32) : 0;
   g.nsb = tiled_nsb(t, cols);
-  g.ks = std::min(g.nsb, t == T_Q8_0 ? 1 : 2);
+  const int ov = decode_ks_override();
+  g.ks = std::max(1, std::min(g.nsb, ov > 0 ? ov : (t == T_Q8_0 ? 1 : 2)));
   g.nseg = (g.nsb + g.ks - 1) / g.ks;
   g.tile_bytes = tiled_tile_bytes(t, cols);
   int mx = 0;
@@ -162,215 +178,292 @@ DecodeGeom decode_geom(int t, int64_t cols) {
     mx = std::max(mx, (int)(end - tiled_sb_offset(t, cols, a)));
   }
   g.stage_bytes = ((mx + 127) / 128) * 128;
+  const int rb = rec_bytes_of(t != T_Q8_0);
+  g.act_bytes = ((2 * DMAXS * g.ks * rb + 127) / 128) * 128;
   return g;
 }
 
-// hsum (avx2.rs:19-27) of the eight lanes held two per thread by four
-// consecutive threads (thread q: lanes 2q, 2q+1). Valid in thread q == 0.
-__device__ __forceinline__ float hsum8_quad(float a0, float a1) {
-  a0 = __fadd_rn(a0, __shfl_down_sync(0xffffffffu, a0, 2, 4));  // v_i + v_{i+4}
-  a1 = __fadd_rn(a1, __shfl_down_sync(0xffffffffu, a1, 2, 4));
-  a0 = __fadd_rn(a0, __shfl_down_sync(0xffffffffu, a0, 1, 4));  // (t0 + t2), (t1 + t3)
-  a1 = __fadd_rn(a1, __shfl_down_sync(0xffffffffu, a1, 1, 4));
-  return __fadd_rn(a0, a1);
-}
-__device__ __forceinline__ int quad_sum(int v) {
-  v += __shfl_xor_sync(0xffffffffu, v, 1, 4);
-  v += __shfl_xor_sync(0xffffffffu, v, 2, 4);
+// ---------------------------------------------------------------------------
+// Shared-memory loads by 32-bit shared-window address. Explicit ld.shared
+// (volatile: kept in order with the mbarrier waits that guard the data).
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
   return v;
 }
-__device__ __forceinline__ uint2 ldg2(const uint8_t* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
-__device__ __forceinline__ int4 ldg4i(const uint8_t* p) { return __ldg(reinterpret_cast<const int4*>(p)); }
-__device__ __forceinline__ float ldgf(const uint8_t* p) { return __ldg(reinterpret_cast<const float*>(p)); }
-
-// Scale and min of Q4_K sub-block jj for a runtime jj (scale_min_k4,
-// quant.rs:54-60), using shifts only.
-__device__ __forceinline__ void q4k_sm_rt(int jj, uint32_t w0, uint32_t w1, uint32_t w2, int& s, int& m) {
-  const int sh = 8 * (jj & 3);
-  const uint32_t A = (w0 >> sh) & 0xFF, B = (w1 >> sh) & 0xFF, C = (w2 >> sh) & 0xFF;
-  s = jj < 4 ? (int)(A & 63) : (int)((C & 0xF) | ((A >> 6) << 4));
-  m = jj < 4 ? (int)(B & 63) : (int)((C >> 4) | ((B >> 6) << 4));
+__device__ __forceinline__ float ldsf(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
 }
+__device__ __forceinline__ uint32_t ldsu16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ int sbyte(uint32_t w, int i) { return (int)(int8_t)((w >> (8 * i)) & 0xFF); }
+__device__ __forceinline__ int ubyte(uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xFF); }
+// dp2a: a = two int16, b = four int8; lo uses bytes 0-1 of b, hi bytes 2-3.
+__device__ __forceinline__ int dp2a_lo(uint32_t a, uint32_t b, int c) { return __dp2a_lo((int)a, (int)b, c); }
+__device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) { return __dp2a_hi((int)a, (int)b, c); }
 
-struct RowAcc {
-  float a0[DMAXS], a1[DMAXS], summs[DMAXS];
-};
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// One superblock of a Q4_K row (avx2.rs:351-379), thread q of the row. xa[s]
-// points at token s's activation record of this superblock.
-template <int NS>
-__device__ __forceinline__ void q4k_superblock(const uint8_t* __restrict__ sbt, int rr, const uint8_t* const* xa,
-                                               int q, RowAcc& r) {
-  const uint4 hdr = *reinterpret_cast<const uint4*>(sbt + 16 * rr);
-  int sc[8], mn[8];
-  q4k_scales(hdr.y, hdr.z, hdr.w, sc, mn);
-  int lo[4][2], hi[4][2];
+// One Q4_K superblock of row `row` (avx2.rs:351-379) against NS slots whose
+// records start at xr (stride R).
+template <int NS, int R>
+__device__ __forceinline__ void q4k_sb(uint32_t sbt, int row, uint32_t xr,
+                                       float (&acc)[NS][8], float (&summs)[NS]) {
+  const uint4 hdr = lds128(sbt + 16 * row);
+  const float dw = h2f(hdr.x), dmw = h2f(hdr.x >> 16);
+  // scale_min_k4 (quant.rs:54-60) for all eight sub-blocks, four per word.
+  const uint32_t scA = hdr.y & 0x3F3F3F3Fu;
+  const uint32_t scB = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+  const uint32_t mA = hdr.z & 0x3F3F3F3Fu;
+  const uint32_t mB = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+  int sumi[NS][8];
+#pragma unroll
+  for (int s = 0; s < NS; ++s)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sumi[s][j] = 0;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const uint2 w = *reinterpret_cast<const uint2*>(sbt + 256 + 512 * k + 32 * rr + 8 * q);
-    lo[k][0] = (int)(w.x & 0x0F0F0F0Fu);
-    hi[k][0] = (int)((w.x >> 4) & 0x0F0F0F0Fu);
-    lo[k][1] = (int)(w.y & 0x0F0F0F0Fu);
-    hi[k][1] = (int)((w.y >> 4) & 0x0F0F0F0Fu);
-  }
-  const float dw = h2f(hdr.x), dmw = h2f(hdr.x >> 16);
-  // Sub-blocks 2q and 2q+1 of the min term (decoded with shifts: no indexed
-  // register arrays), summed over the quad below.
-  int mq0, mq1, dummy;
-  q4k_sm_rt(2 * q, hdr.y, hdr.z, hdr.w, dummy, mq0);
-  q4k_sm_rt(2 * q + 1, hdr.y, hdr.z, hdr.w, dummy, mq1);
+    const uint4 qa = lds128(sbt + kPlane + kPlane * (2 * k) + 16 * row);
+    const uint4 qb = lds128(sbt + kPlane + kPlane * (2 * k + 1) + 16 * row);
+    const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    int lo[8], hi[8];
 #pragma unroll
-  for (int s = 0; s < NS; ++s) {
-    const uint8_t* x = xa[s];
-    uint2 xl[4], xh[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      xl[k] = ldg2(x + 64 * k + 8 * q);
-      xh[k] = ldg2(x + 64 * k + 32 + 8 * q);
+    for (int j = 0; j < 8; ++j) {
+      lo[j] = (int)(qw[j] & 0x0F0F0F0Fu);
+      hi[j] = (int)((qw[j] >> 4) & 0x0F0F0F0Fu);
     }
-    const int4 bsq = ldg4i(x + 256 + 16 * q);  // bsums 4q..4q+3
-    const float xd = ldgf(x + 320);
-    int s0 = 0, s1 = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      s0 += sc[2 * k] * dp4a(lo[k][0], (int)xl[k].x, 0) + sc[2 * k + 1] * dp4a(hi[k][0], (int)xh[k].x, 0);
-      s1 += sc[2 * k] * dp4a(lo[k][1], (int)xl[k].y, 0) + sc[2 * k + 1] * dp4a(hi[k][1], (int)xh[k].y, 0);
-    }
-    const int mins = quad_sum(mq0 * (bsq.x + bsq.y) + mq1 * (bsq.z + bsq.w));
-    const float d = __fmul_rn(dw, xd), dmin = __fmul_rn(dmw, xd);
-    r.a0[s] = __fmaf_rn((float)s0, d, r.a0[s]);
-    r.a1[s] = __fmaf_rn((float)s1, d, r.a1[s]);
-    r.summs[s] = __fadd_rn(r.summs[s], __fmul_rn(dmin, (float)mins));
-  }
-}
-
-// One superblock of a planar Q6_K row segment (avx2.rs:384-419), thread q.
-// Lanes 0-3 use the run's first sub-block scale, lanes 4-7 the second.
-template <int NS>
-__device__ __forceinline__ void q6k_superblock(const uint8_t* __restrict__ sbt, int rr, const uint8_t* const* xa,
-                                               int q, RowAcc& r) {
-  const uint4 scw = *reinterpret_cast<const uint4*>(sbt + 3072 + 16 * rr);
-  const float dw = h2f(*reinterpret_cast<const uint16_t*>(sbt + 3328 + 2 * rr));
-  uint2 ql[4], qh[2];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) ql[c] = *reinterpret_cast<const uint2*>(sbt + 512 * c + 32 * rr + 8 * q);
-#pragma unroll
-  for (int h = 0; h < 2; ++h) qh[h] = *reinterpret_cast<const uint2*>(sbt + 2048 + 512 * h + 32 * rr + 8 * q);
-  const int jh = q >> 1;
-  const uint32_t sw[4] = {scw.x, scw.y, scw.z, scw.w};
-  const uint32_t swq = (q & 2) ? ((q & 1) ? scw.w : scw.z) : ((q & 1) ? scw.y : scw.x);  // offsets m = 4q..4q+3
-  int qv[8][2], scl[8];
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-#pragma unroll
-    for (int ri = 0; ri < 4; ++ri) {
-      const uint2 w = ql[2 * h + (ri & 1)];
-      const int sh = 4 * (ri >> 1);
-      qv[4 * h + ri][0] = (int)(((w.x >> sh) & 0x0F0F0F0Fu) | (((qh[h].x >> (2 * ri)) & 0x03030303u) << 4));
-      qv[4 * h + ri][1] = (int)(((w.y >> sh) & 0x0F0F0F0Fu) | (((qh[h].y >> (2 * ri)) & 0x03030303u) << 4));
-      const int m = 8 * h + 2 * ri;
-      const int sc_lo = i8_of4(sw[m >> 2], m & 3), sc_hi = i8_of4(sw[(m + 1) >> 2], (m + 1) & 3);
-      scl[4 * h + ri] = jh ? sc_hi : sc_lo;
-    }
-#pragma unroll
-  for (int s = 0; s < NS; ++s) {
-    const uint8_t* x = xa[s];
-    int s0 = 0, s1 = 0;
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-      for (int ri = 0; ri < 4; ++ri) {
-        const uint2 xv = ldg2(x + 128 * h + 32 * ri + 8 * q);
-        s0 += scl[4 * h + ri] * dp4a(qv[4 * h + ri][0], (int)xv.x, 0);
-        s1 += scl[4 * h + ri] * dp4a(qv[4 * h + ri][1], (int)xv.y, 0);
-      }
-    const int4 bsq = ldg4i(x + 256 + 16 * q);
-    const int offs = quad_sum(i8_of4(swq, 0) * bsq.x + i8_of4(swq, 1) * bsq.y + i8_of4(swq, 2) * bsq.z +
-                              i8_of4(swq, 3) * bsq.w);
-    const float d = __fmul_rn(dw, ldgf(x + 320));
-    r.a0[s] = __fmaf_rn((float)s0, d, r.a0[s]);
-    r.a1[s] = __fmaf_rn((float)s1, d, r.a1[s]);
-    // avx2.rs:416: lane 0 (thread 0's first lane) gets (-32*d)*offs, the
-    // others +0.0.
-    r.a0[s] = __fadd_rn(r.a0[s], q == 0 ? __fmul_rn(__fmul_rn(-32.0f, d), (float)offs) : 0.0f);
-    r.a1[s] = __fadd_rn(r.a1[s], 0.0f);
-  }
-}
-
-// One chunk of up to 8 Q8_0 blocks of a planar row segment (avx2.rs:49-58).
-template <int NS>
-__device__ __forceinline__ void q8_0_chunk(const uint8_t* __restrict__ cb, int nblk, int rr, const uint8_t* const* xa,
-                                           int q, RowAcc& r) {
-#pragma unroll 1
-  for (int bl = 0; bl < nblk; ++bl) {
-    const uint2 w = *reinterpret_cast<const uint2*>(cb + 512 * bl + 32 * rr + 8 * q);
-    const float dw = h2f(*reinterpret_cast<const uint16_t*>(cb + 512 * nblk + 16 * rr + 2 * bl));
+    const int slo = ubyte(k < 2 ? scA : scB, (2 * k) & 3), shi = ubyte(k < 2 ? scA : scB, (2 * k + 1) & 3);
 #pragma unroll
     for (int s = 0; s < NS; ++s) {
-      const uint2 x = ldg2(xa[s] + 32 * bl + 8 * q);
-      const float sc = __fmul_rn(dw, ldgf(xa[s] + 256 + 4 * bl));
-      r.a0[s] = __fmaf_rn((float)dp4a((int)w.x, (int)x.x, 0), sc, r.a0[s]);
-      r.a1[s] = __fmaf_rn((float)dp4a((int)w.y, (int)x.y, 0), sc, r.a1[s]);
-    }
-  }
-}
-
-// Per-unit metadata, read by the producer and the consumers from shared
-// memory (one table entry per expert of the CTA's unit range).
-struct UnitMeta {
-  int e, slot0, ns;
-  int arow[DMAXS];
-};
-constexpr int DMETA = 96;
-
-template <int T, int NS>
-__device__ __forceinline__ void run_unit(const DecodeArgs& a, const DecodeGeom& g, uint8_t* smem, uint64_t* full,
-                                         uint64_t* empty, int64_t stage0, int n_stages, int row, int q, int r_out,
-                                         const UnitMeta& um, float* out, bool& ok) {
-  RowAcc r;
+      const uint32_t x = xr + s * R + 64 * k;
+      const uint4 x0 = lds128(x), x1 = lds128(x + 16), x2 = lds128(x + 32), x3 = lds128(x + 48);
+      const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
 #pragma unroll
-  for (int s = 0; s < DMAXS; ++s) r.a0[s] = r.a1[s] = r.summs[s] = 0.f;
-  const int rec = T == T_Q8_0 ? 288 : 336;
-  for (int seg = 0; seg < g.nseg; ++seg) {
-    const int64_t sid = stage0 + seg;
-    const int st = (int)(sid % n_stages);
-    const uint32_t ph = (uint32_t)((sid / n_stages) & 1);
-    if (ok && !mbar_wait(&full[st], ph, a.status)) ok = false;
-    if (ok) {
-      const uint8_t* sp = smem + (int64_t)st * g.stage_bytes;
-      const int sb0 = seg * g.ks;
-      const int n = min(g.ks, g.nsb - sb0);
-      for (int j = 0; j < n; ++j) {
-        const uint8_t* xa[NS];
-#pragma unroll
-        for (int s = 0; s < NS; ++s) xa[s] = a.act + (int64_t)um.arow[s] * a.act_stride + (int64_t)rec * (sb0 + j);
-        if (T == T_Q4_K) q4k_superblock<NS>(sp + 2304 * j, row, xa, q, r);
-        else if (T == T_Q6_K) q6k_superblock<NS>(sp + 3360 * j, row, xa, q, r);
-        else q8_0_chunk<NS>(sp + 4352 * j, min(8, g.nb32 - 8 * (sb0 + j)), row, xa, q, r);
+      for (int j = 0; j < 8; ++j) {
+        sumi[s][j] += slo * dp4a(lo[j], (int)xl[j], 0);
+        sumi[s][j] += shi * dp4a(hi[j], (int)xh[j], 0);
       }
     }
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[st]);
   }
 #pragma unroll
   for (int s = 0; s < NS; ++s) {
-    float v = hsum8_quad(r.a0[s], r.a1[s]);
-    if (T == T_Q4_K) v = __fsub_rn(v, r.summs[s]);
-    if (q == 0 && r_out >= 0 && ok) out[(int64_t)(um.slot0 + s) * a.out_stride + r_out] = v;
+    const uint32_t x = xr + s * R;
+    const float xd = ldsf(x + 304);
+    const float d = __fmul_rn(dw, xd), dmin = __fmul_rn(dmw, xd);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[s][j] = __fmaf_rn((float)sumi[s][j], d, acc[s][j]);
+    // mins = sum over sub-blocks m[i] * (bsums[2i] + bsums[2i+1])
+    const uint4 bp = lds128(x + 288);
+    const int mins = dp2a_lo(bp.x, mA, dp2a_hi(bp.y, mA, dp2a_lo(bp.z, mB, dp2a_hi(bp.w, mB, 0))));
+    summs[s] = __fadd_rn(summs[s], __fmul_rn(dmin, (float)mins));
   }
 }
+
+// One Q6_K superblock (avx2.rs:384-419). Lanes 0-3 of a 32-run use its first
+// 16-element scale, lanes 4-7 the second.
+template <int NS, int R>
+__device__ __forceinline__ void q6k_sb(uint32_t sbt, int row, uint32_t xr,
+                                       float (&acc)[NS][8]) {
+  const float dw = h2f(ldsu16(sbt + 13 * kPlane + 2 * row));
+  const uint4 scw = lds128(sbt + 12 * kPlane + 16 * row);
+  const uint32_t sw[4] = {scw.x, scw.y, scw.z, scw.w};
+  int sumi[NS][8];
+#pragma unroll
+  for (int s = 0; s < NS; ++s)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sumi[s][j] = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint4 ha = lds128(sbt + 8 * kPlane + kPlane * (2 * h) + 16 * row);
+    const uint4 hb = lds128(sbt + 8 * kPlane + kPlane * (2 * h + 1) + 16 * row);
+    const uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+#pragma unroll
+    for (int run = 0; run < 2; ++run) {
+      const uint4 la = lds128(sbt + kPlane * (4 * h + 2 * run) + 16 * row);
+      const uint4 lb = lds128(sbt + kPlane * (4 * h + 2 * run + 1) + 16 * row);
+      const uint32_t lw[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+#pragma unroll
+      for (int nib = 0; nib < 2; ++nib) {
+        const int ri = 2 * nib + run;
+        int q6[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          q6[j] = (int)(((lw[j] >> (4 * nib)) & 0x0F0F0F0Fu) | (((hw[j] >> (2 * ri)) & 0x03030303u) << 4));
+        const int si = 8 * h + 2 * ri;
+        const int sc0 = sbyte(sw[si >> 2], si & 3), sc1 = sbyte(sw[(si + 1) >> 2], (si + 1) & 3);
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+          const uint32_t x = xr + s * R + 128 * h + 32 * ri;
+          const uint4 x0 = lds128(x), x1 = lds128(x + 16);
+          const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) sumi[s][j] += (j < 4 ? sc0 : sc1) * dp4a(q6[j], (int)xw[j], 0);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    const uint32_t x = xr + s * R;
+    const float d = __fmul_rn(dw, ldsf(x + 304));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[s][j] = __fmaf_rn((float)sumi[s][j], d, acc[s][j]);
+    // offs = sum over the 16 sub-blocks sc[i] * bsums[i]
+    const uint4 b0 = lds128(x + 256), b1 = lds128(x + 272);
+    int offs = dp2a_lo(b0.x, sw[0], 0);
+    offs = dp2a_hi(b0.y, sw[0], offs);
+    offs = dp2a_lo(b0.z, sw[1], offs);
+    offs = dp2a_hi(b0.w, sw[1], offs);
+    offs = dp2a_lo(b1.x, sw[2], offs);
+    offs = dp2a_hi(b1.y, sw[2], offs);
+    offs = dp2a_lo(b1.z, sw[3], offs);
+    offs = dp2a_hi(b1.w, sw[3], offs);
+    // avx2.rs:416: lane 0 gets (-32*d)*offs, the other lanes +0.0.
+    acc[s][0] = __fadd_rn(acc[s][0], __fmul_rn(__fmul_rn(-32.0f, d), (float)offs));
+#pragma unroll
+    for (int j = 1; j < 8; ++j) acc[s][j] = __fadd_rn(acc[s][j], 0.0f);
+  }
+}
+
+// One chunk of up to 8 Q8_0 blocks (avx2.rs:49-58).
+template <int NS, int R>
+__device__ __forceinline__ void q8_0_chunk(uint32_t cb, int nblk, int row, uint32_t xr, float (&acc)[NS][8]) {
+#pragma unroll 1
+  for (int bl = 0; bl < nblk; ++bl) {
+    const uint4 wa = lds128(cb + kPlane * (2 * bl) + 16 * row);
+    const uint4 wb = lds128(cb + kPlane * (2 * bl + 1) + 16 * row);
+    const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    const float dw = h2f(ldsu16(cb + 2 * kPlane * nblk + 16 * row + 2 * bl));
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      const uint32_t x = xr + s * R;
+      const uint4 x0 = lds128(x + 32 * bl), x1 = lds128(x + 32 * bl + 16);
+      const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      const float d = __fmul_rn(dw, ldsf(x + 256 + 4 * bl));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[s][j] = __fmaf_rn((float)dp4a((int)ww[j], (int)xw[j], 0), d, acc[s][j]);
+    }
+  }
+}
+
+// hsum (avx2.rs:19-27): ((v0+v4)+(v2+v6)) + ((v1+v5)+(v3+v7)).
+__device__ __forceinline__ float hsum8(const float (&v)[8]) {
+  const float a = __fadd_rn(__fadd_rn(v[0], v[4]), __fadd_rn(v[2], v[6]));
+  const float b = __fadd_rn(__fadd_rn(v[1], v[5]), __fadd_rn(v[3], v[7]));
+  return __fadd_rn(a, b);
+}
+
+// ---------------------------------------------------------------------------
+struct UnitMeta {
+  int e, slot0, ns;
+};
 
 __device__ __forceinline__ UnitMeta load_meta(const DecodeArgs& a, int li) {
   UnitMeta m;
   m.e = a.list[li];
   m.slot0 = a.offsets[m.e];
-  m.ns = min(DMAXS, a.offsets[m.e + 1] - m.slot0);
-#pragma unroll
-  for (int s = 0; s < DMAXS; ++s) {
-    const int slot = m.slot0 + min(s, m.ns - 1);
-    m.arow[s] = a.slot_src ? a.slot_src[slot] : slot;
-  }
+  m.ns = max(1, min(DMAXS, a.offsets[m.e + 1] - m.slot0));
   return m;
+}
+
+// Position of unit u: list entry, matrix, 32-row tile.
+struct UnitPos {
+  int li, m, tile;
+};
+__device__ __forceinline__ UnitPos unit_pos(int u, int tiles, int n_mat) {
+  UnitPos p;
+  const int q = u / tiles;
+  p.tile = u - q * tiles;
+  p.li = n_mat == 2 ? q >> 1 : q;
+  p.m = n_mat == 2 ? q & 1 : 0;
+  return p;
+}
+
+// Copy the records of unit `um`'s slots for segment `seg` into `dst`
+// ([superblock of the segment][slot][R]) with cp.async, over the warp's lanes.
+template <int R>
+__device__ __forceinline__ void issue_act(const DecodeArgs& a, const DecodeGeom& g, const UnitMeta& um, int seg,
+                                          uint8_t* dst, int lane) {
+  const int sb0 = seg * g.ks;
+  const int n = min(g.ks, g.nsb - sb0);
+  const int per_sb = um.ns * (R / 16);
+  for (int c = lane; c < n * per_sb; c += 32) {
+    const int j = c / per_sb, cc = c - j * per_sb;
+    const uint8_t* src = a.rec + ((int64_t)(sb0 + j) * a.rec_slots + um.slot0) * R + 16 * cc;
+    cp_async16(dst + j * (DMAXS * R) + 16 * cc, src);
+  }
+}
+
+template <int T>
+struct TypeR {
+  static constexpr int R = T == T_Q8_0 ? kRecQ8 : kRecK;
+};
+
+// One unit: NS slots, all segments. `buf` selects the warp's activation
+// buffer holding this step's records (prefetched by the previous step).
+// (st, ph) is the ring slot and phase parity of the unit's first stage; the
+// warp's later stages of the unit are `step` stages apart, and its next unit
+// starts DW stages after this unit's last one. On return (st, ph) point at
+// that next stage.
+template <int T, int NS>
+__device__ __forceinline__ void run_unit(const DecodeArgs& a, const DecodeGeom& g, const uint8_t* ring,
+                                         uint64_t* full, uint64_t* empty, int n_stages, int& st, uint32_t& ph,
+                                         int step, uint8_t* abuf, int& buf, const UnitMeta& um, bool has_next,
+                                         const UnitMeta& next, int lane, float* out, int r_out, bool& ok) {
+  constexpr int R = TypeR<T>::R;
+  const int half = g.act_bytes / 2;
+  float acc[NS][8], summs[NS];
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    summs[s] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[s][j] = 0.f;
+  }
+  for (int seg = 0; seg < g.nseg; ++seg) {
+    // Prefetch the next step's records, then make this step's visible.
+    if (seg + 1 < g.nseg) issue_act<R>(a, g, um, seg + 1, abuf + (buf ^ 1) * half, lane);
+    else if (has_next) issue_act<R>(a, g, next, 0, abuf + (buf ^ 1) * half, lane);
+    cp_async_commit();
+    cp_async_wait1();
+    __syncwarp();
+    if (ok && !mbar_wait(&full[st], ph, a.status)) ok = false;
+    if (ok) {
+      const uint32_t sp = smem_u32(ring) + (uint32_t)(st * g.stage_bytes);
+      const uint32_t xr = smem_u32(abuf) + (uint32_t)(buf * half);
+      const int sb0 = seg * g.ks;
+      const int n = min(g.ks, g.nsb - sb0);
+      for (int j = 0; j < n; ++j) {
+        if (T == T_Q4_K) q4k_sb<NS, R>(sp + 4608 * j, lane, xr + j * (DMAXS * R), acc, summs);
+        else if (T == T_Q6_K) q6k_sb<NS, R>(sp + 6720 * j, lane, xr + j * (DMAXS * R), acc);
+        else q8_0_chunk<NS, R>(sp + 8704 * j, min(8, g.nb32 - 8 * (sb0 + j)), lane, xr + j * (DMAXS * R), acc);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    buf ^= 1;
+    st += seg + 1 < g.nseg ? step : DW;
+    if (st >= n_stages) {
+      st -= n_stages;
+      ph ^= 1u;
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    float v = hsum8(acc[s]);
+    if (T == T_Q4_K) v = __fsub_rn(v, summs[s]);
+    if (r_out >= 0 && ok) out[(int64_t)(um.slot0 + s) * a.out_stride + r_out] = v;
+  }
 }
 
 template <int T>
@@ -378,6 +471,7 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[DMAX_STAGES], empty[DMAX_STAGES];
   __shared__ UnitMeta meta[DMETA];
+  constexpr int R = TypeR<T>::R;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_list = *a.n_list;
   const int tiles = (int)(padded_rows(a.rows) / DR);
@@ -385,79 +479,120 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
   const int64_t total = (int64_t)n_list * per_expert;
   const int64_t beg = total * blockIdx.x / gridDim.x, end = total * (blockIdx.x + 1) / gridDim.x;
   if (beg >= end) return;
+  const int64_t n_units = end - beg;
+  const int n_groups = (int)((n_units + DW - 1) / DW);
   const int li0 = (int)(beg / per_expert);
   const int n_meta = min(DMETA, (int)((end - 1) / per_expert) - li0 + 1);
   for (int i = tid; i < n_meta; i += blockDim.x) meta[i] = load_meta(a, li0 + i);
   if (tid == 0) {
     for (int s = 0; s < n_stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 2);
+      mbar_init(&empty[s], 1);
     }
     fence_mbar_init();
   }
   __syncthreads();
+  uint8_t* ring = smem;
+  auto meta_of = [&](int li) { return li - li0 < DMETA ? meta[li - li0] : load_meta(a, li); };
+
   if (warp == 0) {
-    // Producer: stages in unit order; unit u uses stages (u-beg)*nseg + seg.
-    int64_t sid = 0;
-    bool ok = true;
-    for (int64_t u = beg; u < end && ok; ++u) {
-      const int li = (int)(u / per_expert);
-      const int m = (int)((u / tiles) % a.n_mat);
-      const int r0 = (int)(u % tiles) * DR;
-      const int e = li - li0 < DMETA ? meta[li - li0].e : a.list[li];
-      const uint8_t* wb = (m == 0 ? a.w[0] : a.w[1]) + (int64_t)(e - a.expert_base) * a.expert_stride + (int64_t)(r0 / DR) * g.tile_bytes;
-      for (int seg = 0; seg < g.nseg; ++seg, ++sid) {
-        const int st = (int)(sid % n_stages);
-        const uint32_t ph = (uint32_t)((sid / n_stages) & 1);
-        if (sid >= n_stages && !mbar_wait(&empty[st], ph ^ 1, a.status)) {
-          ok = false;
-          break;
+    // Producer: group by group, segment-major, one stage per (segment, unit).
+    // Per stage only a wait, an expect_tx and one bulk copy: the units' base
+    // addresses are computed once per group and the ring slot and phase are
+    // advanced incrementally.
+    if (lane == 0) {
+      int st = 0, issued = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int gi = 0; gi < n_groups && ok; ++gi) {
+        const int ub = (int)beg + gi * DW;
+        const int wg = (int)min((int64_t)DW, n_units - (int64_t)gi * DW);
+        const uint8_t* up[DW];
+#pragma unroll
+        for (int w = 0; w < DW; ++w) {
+          up[w] = nullptr;
+          if (w < wg) {
+            const UnitPos p = unit_pos(ub + w, tiles, a.n_mat);
+            const int e = meta_of(p.li).e;
+            up[w] = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(e - a.expert_base) * a.expert_stride +
+                    (int64_t)p.tile * g.tile_bytes;
+          }
         }
-        if (lane == 0) {
-          const int sb0 = seg * g.ks, sb1 = min(g.nsb, sb0 + g.ks);
-          const int64_t off0 = tiled_sb_offset(g.type, a.cols, sb0);
+        int64_t off0 = 0;
+        for (int seg = 0; seg < g.nseg && ok; ++seg) {
+          const int sb1 = min(g.nsb, (seg + 1) * g.ks);
           const int64_t off1 = sb1 == g.nsb ? g.tile_bytes : tiled_sb_offset(g.type, a.cols, sb1);
           const uint32_t bytes = (uint32_t)(off1 - off0);
-          mbar_expect_tx(&full[st], bytes);
-          bulk_g2s(smem + (int64_t)st * g.stage_bytes, wb + off0, bytes, &full[st]);
+#pragma unroll
+          for (int w = 0; w < DW; ++w) {
+            if (w < wg && ok) {
+              if (issued >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status)) {
+                ok = false;
+              } else {
+                mbar_expect_tx(&full[st], bytes);
+                bulk_g2s(ring + (int64_t)st * g.stage_bytes, up[w] + off0, bytes, &full[st]);
+                ++issued;
+                if (++st == n_stages) {
+                  st = 0;
+                  ph ^= 1u;
+                }
+              }
+            }
+          }
+          off0 = off1;
         }
-        __syncwarp();
       }
-    }
-    // Keep the CTA alive until every issued copy has landed (bounded).
-    if (lane == 0)
-      for (int64_t k = (sid > n_stages ? sid - n_stages : 0); k < sid; ++k)
+      // Keep the CTA alive until every issued copy has landed (bounded).
+      for (int k = max(0, issued - n_stages); k < issued; ++k)
         mbar_wait(&full[k % n_stages], (uint32_t)((k / n_stages) & 1), a.status);
+    }
     return;
   }
-  // Consumers: pair p = (warp-1)/2 takes units beg+p, beg+p+DPAIRS, ...
-  const int p = (warp - 1) >> 1;
-  const int t = tid - 32 - p * 64;  // 0..63
-  const int row = t >> 2, q = t & 3;
+
+  // Consumers: warp w takes unit gi*DW + w of every group gi.
+  const int w = warp - 1;
+  if (w >= n_units) return;
+  uint8_t* abuf = smem + (int64_t)n_stages * g.stage_bytes + (int64_t)w * g.act_bytes;
+  int buf = 0;
   bool ok = true;
-  for (int64_t u = beg + p; u < end; u += DPAIRS) {
-    const int li = (int)(u / per_expert);
-    const int m = (int)((u / tiles) % a.n_mat);
-    const int r0 = (int)(u % tiles) * DR;
-    const int nr = min(DR, a.rows - r0);
-    const UnitMeta um = li - li0 < DMETA ? meta[li - li0] : load_meta(a, li);
-    const int r_out = row < nr ? r0 + row : -1;  // padding rows (zeros) are computed, not stored
-    const int64_t stage0 = (u - beg) * g.nseg;
-    float* out = m == 0 ? a.out[0] : a.out[1];
-    if (um.ns == 1) run_unit<T, 1>(a, g, smem, full, empty, stage0, n_stages, row, q, r_out, um, out, ok);
-    else if (um.ns == 2) run_unit<T, 2>(a, g, smem, full, empty, stage0, n_stages, row, q, r_out, um, out, ok);
-    else run_unit<T, 3>(a, g, smem, full, empty, stage0, n_stages, row, q, r_out, um, out, ok);
+  const int ubeg = (int)beg;
+  UnitMeta um = meta_of(unit_pos(ubeg + w, tiles, a.n_mat).li);
+  issue_act<R>(a, g, um, 0, abuf, lane);
+  cp_async_commit();
+  int st = w;  // the warp's first stage is stage w (w < DW <= n_stages)
+  uint32_t ph = 0;
+  for (int gi = 0; gi < n_groups; ++gi) {
+    const int wg = (int)min((int64_t)DW, n_units - (int64_t)gi * DW);
+    if (w >= wg) break;
+    const UnitPos p = unit_pos(ubeg + gi * DW + w, tiles, a.n_mat);
+    // The warp's next unit (next group); its first records are prefetched
+    // during this unit's last segment.
+    const int un = (gi + 1) * DW + w;
+    const bool has_next = un < n_units;
+    const UnitMeta next = has_next ? meta_of(unit_pos(ubeg + un, tiles, a.n_mat).li) : um;
+    const int r0 = p.tile * DR;
+    const int r_out = r0 + lane < a.rows ? r0 + lane : -1;  // padding rows are computed, not stored
+    float* out = p.m == 0 ? a.out[0] : a.out[1];
+    if (um.ns == 1)
+      run_unit<T, 1>(a, g, ring, full, empty, n_stages, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
+    else if (um.ns == 2)
+      run_unit<T, 2>(a, g, ring, full, empty, n_stages, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
+    else
+      run_unit<T, 3>(a, g, ring, full, empty, n_stages, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
+    um = next;
   }
+  cp_async_wait0();
 }
 
 template <int T>
 static int launch_decode_t(const DecodeArgs& a, const DecodeGeom& g, int max_units, cudaStream_t st) {
-  int n_stages = std::min(DMAX_STAGES, (int)((200 * 1024) / g.stage_bytes));
+  const int act_total = DW * g.act_bytes;
+  const int n_stages = std::min(DMAX_STAGES, (DSMEM - act_total) / g.stage_bytes);
   if (n_stages < 2) return KC_ERR_SHAPE;
-  const size_t smem = (size_t)n_stages * g.stage_bytes;
+  const size_t smem = (size_t)n_stages * g.stage_bytes + act_total;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(decode_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(decode_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, DSMEM);
     attr = true;
   }
   const int grid = std::min(num_sms(), std::max(1, max_units));
@@ -466,7 +601,7 @@ static int launch_decode_t(const DecodeArgs& a, const DecodeGeom& g, int max_uni
 }
 
 int launch_decode(const DecodeArgs& a, int max_units, cudaStream_t st) {
-  if (a.act_stride % 16 != 0) return KC_ERR_SHAPE;
+  if (a.rec_slots <= 0) return KC_ERR_SHAPE;
   const DecodeGeom g = decode_geom(a.type, a.cols);
   switch (a.type) {
     case T_Q4_K: return launch_decode_t<T_Q4_K>(a, g, max_units, st);

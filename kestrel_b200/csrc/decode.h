@@ -7,6 +7,21 @@
 
 namespace kc {
 
+// Activation records, one per (superblock, slot), stored superblock-major:
+// record (sb, slot) lives at rec + (sb * rec_slots + slot) * record bytes, so
+// the records of an expert's consecutive slots for one superblock are one
+// contiguous range.
+//   Q8_K record (K-quant weights), 320 B: q[256] int8 | bsums int16[16] at 256
+//     | pair sums int16[8] at 288 (bsums[2i] + bsums[2i+1]) | d f32 at 304
+//   Q8 record (Q8_0 weights), per chunk of 8 blocks, 288 B: q[256] | d[8] f32
+constexpr int kRecK = 320;
+constexpr int kRecQ8 = 288;
+inline int rec_bytes_of(bool kquant) { return kquant ? kRecK : kRecQ8; }
+// Records per slot of a row of `cols` values.
+inline int64_t rec_row_bytes(bool kquant, int64_t cols) {
+  return kquant ? cols / 256 * kRecK : (cols / 32 + 7) / 8 * kRecQ8;
+}
+
 struct DecodeArgs {
   const uint8_t* w[2];     // matrices (gate, up) or (down / dense, unused)
   int n_mat;               // 1 or 2
@@ -17,9 +32,8 @@ struct DecodeArgs {
   const int* list;         // expert ids (1..3 rows each)
   const int* n_list;       // device scalar
   const int* offsets;      // [E+1] slot ranges
-  const int* slot_src;     // activation record row of a slot (null: slot)
-  const uint8_t* act;      // activation records
-  int64_t act_stride;      // bytes per record row
+  const uint8_t* rec;      // activation records (superblock-major, see above)
+  int64_t rec_slots;       // slots per superblock plane of rec
   float* out[2];           // out[m][slot * out_stride + row]
   int64_t out_stride;
   int* status;
@@ -30,23 +44,25 @@ struct DecodeGeom {
   int type;
   int nsb;       // superblocks per row (Q8_0: chunks of 8 blocks)
   int nb32;      // Q8_0 blocks per row
-  int ks;        // superblocks per K segment
+  int ks;        // superblocks per K segment (one pipeline stage)
   int nseg;      // segments per row
-  int64_t tile_bytes;  // bytes of one 16-row tile
-  int stage_bytes;
+  int64_t tile_bytes;  // bytes of one 32-row tile
+  int stage_bytes;     // weight bytes of the largest segment, rounded to 128
+  int act_bytes;       // one warp's activation buffer (one segment, all slots)
 };
 
 DecodeGeom decode_geom(int t, int64_t cols);
+// max_units: an upper bound of the work units (expert x matrix x 32-row tile)
+// used to size the grid.
 int launch_decode(const DecodeArgs& a, int max_units, cudaStream_t st);
 
-// Activation records (Q8_K for K-quant weights, Q8 per-32 for Q8_0): x rows
-// [n_rows, cols] f32 -> records; with u != null the rows are first combined
-// as SwiGLU g / (1 + exp(-g)) * u, and the combined rows are also written to
-// f32out / f16out when those are non-null.
-void launch_act_records(bool kquant, const float* x, const float* u, int64_t n_rows, int64_t cols, uint8_t* rec,
-                        float* f32out, __half* f16out, cudaStream_t st);
-inline int64_t act_rec_stride(bool kquant, int64_t cols) {
-  return kquant ? cols / 256 * 336 : (cols / 32 + 7) / 8 * 288;
-}
+// Activation records of `n_slots` rows: slot i reads row slot_src[i] of x (i
+// when slot_src is null). With u != null the rows are first combined as
+// SwiGLU g / (1 + exp(-g)) * u (x = g, both indexed by slot). Any of rec,
+// f32out (SwiGLU only) and f16out may be null; f32out/f16out are written per
+// slot ([n_slots, cols]).
+void launch_act_records(bool kquant, const float* x, const float* u, const int* slot_src, int64_t n_slots,
+                        int64_t cols, uint8_t* rec, int64_t rec_slots, float* f32out, __half* f16out,
+                        cudaStream_t st);
 
 }  // namespace kc

@@ -34,7 +34,7 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* __restrict__ mat, i
   const uint8_t* tile = mat + (int64_t)(r / kTileRows) * tiled_tile_bytes(T, cols);
   if (T == T_Q4_K) {
     const int i = col & 255, k = i >> 6, hi = (i >> 5) & 1, l = i & 31;
-    const uint8_t* sbt = tile + 2304 * (col >> 8);
+    const uint8_t* sbt = tile + 4608 * (col >> 8);
     const uint8_t* hdr = sbt + 16 * rr;
     uint32_t w0 = *reinterpret_cast<const uint32_t*>(hdr + 4), w1 = *reinterpret_cast<const uint32_t*>(hdr + 8),
              w2 = *reinterpret_cast<const uint32_t*>(hdr + 12);
@@ -42,26 +42,28 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* __restrict__ mat, i
     q4k_sm(2 * k + hi, w0, w1, w2, s, m);
     uint32_t dd = *reinterpret_cast<const uint32_t*>(hdr);
     float d1 = __fmul_rn(h2f(dd), (float)s), m1 = __fmul_rn(h2f(dd >> 16), (float)m);
-    const int byte = sbt[256 + 512 * k + 32 * rr + l];
+    const int qb = 32 * k + l;  // byte of qs
+    const int byte = sbt[kPlane + kPlane * (qb >> 4) + 16 * rr + (qb & 15)];
     const int qv = hi ? (byte >> 4) : (byte & 0xF);
     return __fsub_rn(__fmul_rn(d1, (float)qv), m1);
   } else if (T == T_Q6_K) {
     const int i = col & 255, h = i >> 7, r2 = (i >> 5) & 3, l = i & 31;
-    const uint8_t* sbt = tile + 3360 * (col >> 8);
-    const int c = 2 * h + (r2 & 1);
-    const int ql = sbt[512 * c + 32 * rr + l];
+    const uint8_t* sbt = tile + 6720 * (col >> 8);
+    const int lb = 64 * h + 32 * (r2 & 1) + l;  // byte of ql
+    const int ql = sbt[kPlane * (lb >> 4) + 16 * rr + (lb & 15)];
     const int nib = (r2 >> 1) ? (ql >> 4) : (ql & 0xF);
-    const int qh = (sbt[2048 + 512 * h + 32 * rr + l] >> (2 * r2)) & 3;
+    const int hb = 32 * h + l;  // byte of qh
+    const int qh = (sbt[8 * kPlane + kPlane * (hb >> 4) + 16 * rr + (hb & 15)] >> (2 * r2)) & 3;
     const int qv = (nib | (qh << 4)) - 32;
-    const int sc = (int8_t)sbt[3072 + 16 * rr + 8 * h + 2 * r2 + (l >> 4)];
-    const float d = h2f(*reinterpret_cast<const uint16_t*>(sbt + 3328 + 2 * rr));
+    const int sc = (int8_t)sbt[12 * kPlane + 16 * rr + 8 * h + 2 * r2 + (l >> 4)];
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(sbt + 13 * kPlane + 2 * rr));
     return __fmul_rn(__fmul_rn(d, (float)sc), (float)qv);
   } else {
     const int cb = col >> 8, bl = (col & 255) >> 5, l = col & 31;
     const int nb32 = cols >> 5, nblk = min(8, nb32 - 8 * cb);
-    const uint8_t* chunk = tile + 4352ll * cb;
-    const float d = h2f(*reinterpret_cast<const uint16_t*>(chunk + 512 * nblk + 16 * rr + 2 * bl));
-    return __fmul_rn((float)(int8_t)chunk[512 * bl + 32 * rr + l], d);
+    const uint8_t* chunk = tile + 8704ll * cb;
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(chunk + 2 * kPlane * nblk + 16 * rr + 2 * bl));
+    return __fmul_rn((float)(int8_t)chunk[kPlane * (2 * bl + (l >> 4)) + 16 * rr + (l & 15)], d);
   }
 }
 

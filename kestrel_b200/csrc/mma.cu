@@ -6,7 +6,7 @@
 // Per work tile: one expert, 128 weight rows (the MMA's M) x up to 128 slots
 // (N), all of K. Roles:
 //   warp 0 (1 thread)  producer: bulk copies of the raw quantized superblock
-//                      tiles (tiled device layout, >= 2.3 KB each) and TMA
+//                      tiles (tiled device layout, >= 4.6 KB each) and TMA
 //                      tensor loads of the f16 activation tile (128B swizzle).
 //   warp 1             TMEM allocation; one thread issues
 //                      tcgen05.mma.cta_group::1.kind::f16 into f32 TMEM
@@ -38,7 +38,8 @@ constexpr int M_RAWS = 2;     // raw superblock stages
 constexpr int A_BYTES = MM * MK * 2;  // 16 KB
 constexpr int B_BYTES = MN * MK * 2;  // 16 KB
 
-__host__ __device__ inline int max_sbt_bytes(int t) { return t == T_Q4_K ? 2304 : t == T_Q6_K ? 3360 : 4352; }
+__host__ __device__ inline int max_sbt_bytes(int t) { return t == T_Q4_K ? 4608 : t == T_Q6_K ? 6720 : 8704; }
+constexpr int M_RT = MM / kTileRows;  // row tiles per M tile
 
 struct MmaSmem {
   int op_bytes, raw_bytes, total;
@@ -46,7 +47,7 @@ struct MmaSmem {
 __host__ __device__ inline MmaSmem mma_smem(int t, int n_mat) {
   MmaSmem s;
   s.op_bytes = n_mat * A_BYTES + B_BYTES;
-  s.raw_bytes = ((n_mat * 8 * max_sbt_bytes(t) + 1023) / 1024) * 1024;
+  s.raw_bytes = ((n_mat * M_RT * max_sbt_bytes(t) + 1023) / 1024) * 1024;
   s.total = M_OPS * s.op_bytes + M_RAWS * s.raw_bytes + 1024;  // + alignment slack
   return s;
 }
@@ -134,8 +135,8 @@ __device__ __forceinline__ void dq_q4k(const uint8_t* sbt, int rr, int kk, uint8
   mma_q4k_sm(2 * kk + 1, hdr.y, hdr.z, hdr.w, s1, m1);
   const float d1 = __fmul_rn(d, (float)s0), mm1 = __fmul_rn(dmin, (float)m0);
   const float d2 = __fmul_rn(d, (float)s1), mm2 = __fmul_rn(dmin, (float)m1);
-  const uint4 q0 = *reinterpret_cast<const uint4*>(sbt + 256 + 512 * kk + 32 * rr);
-  const uint4 q1 = *reinterpret_cast<const uint4*>(sbt + 256 + 512 * kk + 32 * rr + 16);
+  const uint4 q0 = *reinterpret_cast<const uint4*>(sbt + kPlane + kPlane * (2 * kk) + 16 * rr);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(sbt + kPlane + kPlane * (2 * kk + 1) + 16 * rr);
   const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
@@ -154,16 +155,17 @@ __device__ __forceinline__ void dq_q4k(const uint8_t* sbt, int rr, int kk, uint8
 // Q6_K (quant.rs:180-201): y = (d*sc)*(q-32).
 __device__ __forceinline__ void dq_q6k(const uint8_t* sbt, int rr, int kk, uint8_t* A, int m) {
   const int h = kk >> 1, nib = kk & 1;
-  const float d = h2f(*reinterpret_cast<const uint16_t*>(sbt + 3328 + 2 * rr));
-  const uint4 scw = *reinterpret_cast<const uint4*>(sbt + 3072 + 16 * rr);
+  const float d = h2f(*reinterpret_cast<const uint16_t*>(sbt + 13 * kPlane + 2 * rr));
+  const uint4 scw = *reinterpret_cast<const uint4*>(sbt + 12 * kPlane + 16 * rr);
   const uint32_t sw[4] = {scw.x, scw.y, scw.z, scw.w};
 #pragma unroll
   for (int half = 0; half < 2; ++half) {  // elements 32*half .. 32*half+31 of the chunk
     const int r2 = 2 * nib + half;
-    const uint8_t* qlp = sbt + 512 * (2 * h + half) + 32 * rr;
-    const uint8_t* qhp = sbt + 2048 + 512 * h + 32 * rr;
-    const uint4 l0 = *reinterpret_cast<const uint4*>(qlp), l1 = *reinterpret_cast<const uint4*>(qlp + 16);
-    const uint4 h0 = *reinterpret_cast<const uint4*>(qhp), h1 = *reinterpret_cast<const uint4*>(qhp + 16);
+    // ql bytes 64h + 32half .. +31 = chunks 4h + 2half (+1); qh bytes 32h .. +31 = chunks 2h (+1).
+    const uint8_t* qlp = sbt + kPlane * (4 * h + 2 * half) + 16 * rr;
+    const uint8_t* qhp = sbt + 8 * kPlane + kPlane * (2 * h) + 16 * rr;
+    const uint4 l0 = *reinterpret_cast<const uint4*>(qlp), l1 = *reinterpret_cast<const uint4*>(qlp + kPlane);
+    const uint4 h0 = *reinterpret_cast<const uint4*>(qhp), h1 = *reinterpret_cast<const uint4*>(qhp + kPlane);
     const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
     const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
 #pragma unroll
@@ -189,9 +191,9 @@ __device__ __forceinline__ void dq_q8_0(const uint8_t* cb, int nblk, int rr, int
 #pragma unroll
   for (int bi = 0; bi < 2; ++bi) {
     const int b = 2 * kk + bi;
-    const float d = h2f(*reinterpret_cast<const uint16_t*>(cb + 512 * nblk + 16 * rr + 2 * b));
-    const uint4 q0 = *reinterpret_cast<const uint4*>(cb + 512 * b + 32 * rr);
-    const uint4 q1 = *reinterpret_cast<const uint4*>(cb + 512 * b + 32 * rr + 16);
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(cb + 2 * kPlane * nblk + 16 * rr + 2 * b));
+    const uint4 q0 = *reinterpret_cast<const uint4*>(cb + kPlane * (2 * b) + 16 * rr);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(cb + kPlane * (2 * b + 1) + 16 * rr);
     const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -277,7 +279,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
       int raw_it = 0, op_it = 0;
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
         const Tile t = tile_of(a, w, row_tiles, n_large);
-        const int n_rt = min(8, (prows - MM * t.rt) / kTileRows);
+        const int n_rt = min(M_RT, (prows - MM * t.rt) / kTileRows);
         for (int kc = 0; kc < nkc && ok; ++kc) {
           const int sb = kc >> 2;
           if ((kc & 3) == 0) {
@@ -292,9 +294,9 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
 #pragma unroll
             for (int mt = 0; mt < NMAT; ++mt) {
               const uint8_t* src = a.w[mt] + (int64_t)(t.e - a.expert_base) * a.expert_stride +
-                                   (int64_t)(8 * t.rt) * tile_bytes + tiled_sb_offset(T, a.cols, sb);
+                                   (int64_t)(M_RT * t.rt) * tile_bytes + tiled_sb_offset(T, a.cols, sb);
               for (int x = 0; x < n_rt; ++x)
-                bulk_g2s(rbase + (mt * 8 + x) * max_sbt_bytes(T), src + x * tile_bytes, sbytes, &raw_full[r]);
+                bulk_g2s(rbase + (mt * M_RT + x) * max_sbt_bytes(T), src + x * tile_bytes, sbytes, &raw_full[r]);
             }
             ++raw_it;
           }
@@ -352,7 +354,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
     }
   } else {
     // Dequantisation warps: thread t = weight row t of the tile.
-    const int m = tid - 64, rt_local = m >> 4, rr = m & 15;
+    const int m = tid - 64, rt_local = m / kTileRows, rr = m % kTileRows;
     int raw_it = 0, op_it = 0, tile_it = 0;
     for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++tile_it) {
       const Tile t = tile_of(a, w, row_tiles, n_large);
@@ -370,7 +372,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
           const uint8_t* rb = raws + r * L.raw_bytes;
 #pragma unroll
           for (int mt = 0; mt < NMAT; ++mt) {
-            const uint8_t* sbt = rb + (mt * 8 + rt_local) * max_sbt_bytes(T);
+            const uint8_t* sbt = rb + (mt * M_RT + rt_local) * max_sbt_bytes(T);
             if (T == T_Q4_K) dq_q4k(sbt, rr, kk, A + mt * A_BYTES, m);
             else if (T == T_Q6_K) dq_q6k(sbt, rr, kk, A + mt * A_BYTES, m);
             else dq_q8_0(sbt, min(8, a.cols / 32 - 8 * sb), rr, kk, A + mt * A_BYTES, m);
@@ -472,29 +474,6 @@ int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaSt
   if (a.type == T_Q4_K) return launch_t<T_Q4_K, 1>(a, tmap, max_tiles, st);
   if (a.type == T_Q6_K) return launch_t<T_Q6_K, 1>(a, tmap, max_tiles, st);
   return launch_t<T_Q8_0, 1>(a, tmap, max_tiles, st);
-}
-
-// Gather + convert activation rows to f16: dst[i] = f16(src[map[i]]) (map may
-// be null: identity). One thread per 8 elements.
-__global__ void gather_f16_kernel(const float* __restrict__ src, const int* __restrict__ map, int64_t n_rows,
-                                  int64_t cols, __half* __restrict__ dst) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t per = cols / 8;
-  if (i >= n_rows * per) return;
-  const int64_t r = i / per, c = (i % per) * 8;
-  const int64_t sr = map ? map[r] : r;
-  const float4 a0 = *reinterpret_cast<const float4*>(src + sr * cols + c);
-  const float4 a1 = *reinterpret_cast<const float4*>(src + sr * cols + c + 4);
-  __half2 h[4] = {__floats2half2_rn(a0.x, a0.y), __floats2half2_rn(a0.z, a0.w), __floats2half2_rn(a1.x, a1.y),
-                  __floats2half2_rn(a1.z, a1.w)};
-  *reinterpret_cast<uint4*>(dst + r * cols + c) = *reinterpret_cast<uint4*>(h);
-}
-
-void launch_gather_f16(const float* src, const int* map, int64_t n_rows, int64_t cols, __half* dst,
-                       cudaStream_t st) {
-  const int64_t n = n_rows * (cols / 8);
-  if (n <= 0) return;
-  gather_f16_kernel<<<ceil_div(n, 256), 256, 0, st>>>(src, map, n_rows, cols, dst);
 }
 
 }  // namespace kc

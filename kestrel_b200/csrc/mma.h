@@ -27,8 +27,5 @@ struct MmaArgs {
 int make_tmap_f16(void* map_out, const void* ptr, int64_t rows, int64_t cols);
 bool mma_supported(int t, int64_t cols, int n_mat);
 int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st);
-// dst[i, :] = f16(src[map[i], :]) (map null: identity); cols % 8 == 0.
-void launch_gather_f16(const float* src, const int* map, int64_t n_rows, int64_t cols, __half* dst,
-                       cudaStream_t st);
 
 }  // namespace kc

@@ -234,25 +234,25 @@ __global__ void repack_tiled_kernel(int t, const uint8_t* __restrict__ src, int6
   if (t == T_Q4_K) {
     const uint8_t* b = srow + 144 * sb;
     for (int x = 0; x < 16; ++x) sbt[16 * rr + x] = b[x];
-    for (int k = 0; k < 4; ++k)
-      for (int x = 0; x < 32; ++x) sbt[256 + 512 * k + 32 * rr + x] = b[16 + 32 * k + x];
+    for (int c = 0; c < 8; ++c)
+      for (int x = 0; x < 16; ++x) sbt[kPlane + kPlane * c + 16 * rr + x] = b[16 + 16 * c + x];
   } else if (t == T_Q6_K) {
     const uint8_t* b = srow + 210 * sb;
+    for (int c = 0; c < 8; ++c)
+      for (int x = 0; x < 16; ++x) sbt[kPlane * c + 16 * rr + x] = b[16 * c + x];
     for (int c = 0; c < 4; ++c)
-      for (int x = 0; x < 32; ++x) sbt[512 * c + 32 * rr + x] = b[32 * c + x];
-    for (int h = 0; h < 2; ++h)
-      for (int x = 0; x < 32; ++x) sbt[2048 + 512 * h + 32 * rr + x] = b[128 + 32 * h + x];
-    for (int x = 0; x < 16; ++x) sbt[3072 + 16 * rr + x] = b[192 + x];
-    sbt[3328 + 2 * rr] = b[208];
-    sbt[3328 + 2 * rr + 1] = b[209];
+      for (int x = 0; x < 16; ++x) sbt[8 * kPlane + kPlane * c + 16 * rr + x] = b[128 + 16 * c + x];
+    for (int x = 0; x < 16; ++x) sbt[12 * kPlane + 16 * rr + x] = b[192 + x];
+    sbt[13 * kPlane + 2 * rr] = b[208];
+    sbt[13 * kPlane + 2 * rr + 1] = b[209];
   } else {
     const int nb32 = (int)(cols / 32);
     const int nblk = min(8, nb32 - 8 * sb);
     for (int bl = 0; bl < nblk; ++bl) {
       const uint8_t* b = srow + 34 * (8 * sb + bl);
-      for (int x = 0; x < 32; ++x) sbt[512 * bl + 32 * rr + x] = b[2 + x];
-      sbt[512 * nblk + 16 * rr + 2 * bl] = b[0];
-      sbt[512 * nblk + 16 * rr + 2 * bl + 1] = b[1];
+      for (int x = 0; x < 32; ++x) sbt[kPlane * (2 * bl + (x >> 4)) + 16 * rr + (x & 15)] = b[2 + x];
+      sbt[2 * kPlane * nblk + 16 * rr + 2 * bl] = b[0];
+      sbt[2 * kPlane * nblk + 16 * rr + 2 * bl + 1] = b[1];
     }
   }
 }
