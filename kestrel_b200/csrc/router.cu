@@ -22,28 +22,43 @@ namespace kc {
 // (double-buffered), so every thread's chain reads shared memory only; each
 // lane still visits its elements c = lane, lane+8, ... in increasing order.
 constexpr int RL_E = 8, RL_T = 4, RL_KC = 1024;
+constexpr int RL_ROW = RL_KC + 8;  // padded shared row: the 4 expert rows a warp reads hit distinct banks
 constexpr int RL_THREADS = RL_E * RL_T * 8;
 
+// One 8-chunk step of output lane j's chain. GEMM: gemm_f32 lane chain (all
+// chunks into a0) or, for m1, dot_f32 (even chunks a0, odd chunks a1); else
+// quant::dot (separate multiply and add).
+template <bool GEMM>
+__device__ __forceinline__ void rl_step(float wv, float xv, bool odd, bool m1, float& a0, float& a1) {
+  if (GEMM) {
+    if (odd && m1) a1 = __fmaf_rn(wv, xv, a1);
+    else a0 = __fmaf_rn(wv, xv, a0);
+  } else {
+    a0 = __fadd_rn(a0, __fmul_rn(wv, xv));
+  }
+}
+
+template <bool GEMM>
 __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* __restrict__ w, int64_t ws, int E,
                                                                    int d, const float* __restrict__ h, int n_tok,
                                                                    float* __restrict__ logits, int* status) {
-  extern __shared__ __align__(128) float rsm[];  // [2][(RL_E + RL_T) * RL_KC]
+  extern __shared__ __align__(128) float rsm[];  // [2][RL_E + RL_T][RL_ROW]
   __shared__ __align__(8) uint64_t full[2];
   const int tid = threadIdx.x, j = tid & 7, grp = tid >> 3;
   const int er = grp % RL_E, tr = grp / RL_E;
   const int e0 = blockIdx.x * RL_E, s0 = blockIdx.y * RL_T;
   const int ne = min(RL_E, E - e0), nt = min(RL_T, n_tok - s0);
-  const int e = e0 + min(er, ne - 1), s = s0 + min(tr, nt - 1);
+  const int erc = min(er, ne - 1), trc = min(tr, nt - 1);
+  const int e = e0 + erc, s = s0 + trc;
   const bool valid = er < ne && tr < nt;
-  const bool gemm = n_tok >= 4 && (d % 8) == 0;
   const int n8 = d / 8 * 8;
-  // Method: 0 = gemm_f32 lane chain, 1 = dot_f32 (acc0 even / acc1 odd
-  // 8-chunks), 2 = scalar quant::dot.
-  int method;
-  {
+  // gemm_f32 blocks rows in 3s inside 48-row tiles and tokens in 4s; the
+  // outputs outside those blocks go through dot_f32 (m1).
+  bool m1 = false;
+  if (GEMM) {
     const int tile = e / 48, trows = min(48, E - tile * 48), rows3 = trows / 3 * 3;
     const bool row_blocked = (e - tile * 48) < rows3;
-    method = !gemm ? 2 : (row_blocked && s < n_tok / 4 * 4) ? 0 : 1;
+    m1 = !(row_blocked && s < n_tok / 4 * 4);
   }
   const int nchunk = (d + RL_KC - 1) / RL_KC;
   const bool bulk_ok = (d % 4) == 0 && (ws % 4) == 0 && ((uintptr_t)w & 15) == 0 &&
@@ -55,12 +70,12 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* 
   }
   __syncthreads();
   auto issue = [&](int c) {
-    float* buf = rsm + (c & 1) * (RL_E + RL_T) * RL_KC;
+    float* buf = rsm + (c & 1) * (RL_E + RL_T) * RL_ROW;
     const int k0 = c * RL_KC, kn = min(RL_KC, d - k0);
     const uint32_t rb = (uint32_t)kn * 4;
     mbar_expect_tx(&full[c & 1], rb * (ne + nt));
-    for (int r = 0; r < ne; ++r) bulk_g2s(buf + r * RL_KC, w + (int64_t)(e0 + r) * ws + k0, rb, &full[c & 1]);
-    for (int r = 0; r < nt; ++r) bulk_g2s(buf + (RL_E + r) * RL_KC, h + (int64_t)(s0 + r) * d + k0, rb, &full[c & 1]);
+    for (int r = 0; r < ne; ++r) bulk_g2s(buf + r * RL_ROW, w + (int64_t)(e0 + r) * ws + k0, rb, &full[c & 1]);
+    for (int r = 0; r < nt; ++r) bulk_g2s(buf + (RL_E + r) * RL_ROW, h + (int64_t)(s0 + r) * d + k0, rb, &full[c & 1]);
   };
   float a0 = 0.f, a1 = 0.f;
   if (bulk_ok) {
@@ -70,18 +85,22 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* 
     }
     for (int c = 0; c < nchunk; ++c) {
       mbar_wait(&full[c & 1], (c >> 1) & 1, status);
-      const float* buf = rsm + (c & 1) * (RL_E + RL_T) * RL_KC;
-      const float* wr = buf + min(er, ne - 1) * RL_KC;
-      const float* xr = buf + (RL_E + min(tr, nt - 1)) * RL_KC;
-      const int k0 = c * RL_KC, kn = min(RL_KC, n8 - k0);
-      for (int cc = 0; cc < kn; cc += 8) {
-        const float wv = wr[cc + j], xv = xr[cc + j];
-        if (method == 0) a0 = __fmaf_rn(wv, xv, a0);
-        else if (method == 1) {
-          if (((k0 + cc) >> 3) & 1) a1 = __fmaf_rn(wv, xv, a1);
-          else a0 = __fmaf_rn(wv, xv, a0);
-        } else a0 = __fadd_rn(a0, __fmul_rn(wv, xv));
+      const float* buf = rsm + (c & 1) * (RL_E + RL_T) * RL_ROW;
+      const float* wr = buf + erc * RL_ROW + j;
+      const float* xr = buf + (RL_E + trc) * RL_ROW + j;
+      const int k0 = c * RL_KC, kn = min(RL_KC, n8 - k0);  // k0 is an even number of 8-chunks
+      int cc = 0;
+      for (; cc + 64 <= kn; cc += 64) {
+        float wv[8], xv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          wv[u] = wr[cc + 8 * u];
+          xv[u] = xr[cc + 8 * u];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) rl_step<GEMM>(wv[u], xv[u], u & 1, m1, a0, a1);
       }
+      for (; cc < kn; cc += 8) rl_step<GEMM>(wr[cc], xr[cc], (cc >> 3) & 1, m1, a0, a1);
       __syncthreads();  // everyone is done with this buffer
       if (tid == 0 && c + 2 < nchunk) issue(c + 2);
     }
@@ -89,17 +108,10 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* 
     // Rows not 16-byte aligned: read global memory directly.
     const float* wr = w + (int64_t)e * ws;
     const float* xr = h + (int64_t)s * d;
-    for (int c = 0, chunk = 0; c < n8; c += 8, ++chunk) {
-      const float wv = wr[c + j], xv = xr[c + j];
-      if (method == 0) a0 = __fmaf_rn(wv, xv, a0);
-      else if (method == 1) {
-        if (chunk & 1) a1 = __fmaf_rn(wv, xv, a1);
-        else a0 = __fmaf_rn(wv, xv, a0);
-      } else a0 = __fadd_rn(a0, __fmul_rn(wv, xv));
-    }
+    for (int c = 0; c < n8; c += 8) rl_step<GEMM>(wr[c + j], xr[c + j], (c >> 3) & 1, m1, a0, a1);
   }
   float v;
-  if (method == 2) {
+  if (!GEMM) {
     // Sequential fold of the eight lanes from -0.0, then the tail.
     float sum = -0.0f;
 #pragma unroll
@@ -107,7 +119,7 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* 
     for (int c = n8; c < d; ++c) sum = __fadd_rn(sum, __fmul_rn(w[(int64_t)e * ws + c], h[(int64_t)s * d + c]));
     v = sum;
   } else {
-    v = hsum8_group(method == 1 ? __fadd_rn(a0, a1) : a0);
+    v = hsum8_group(m1 ? __fadd_rn(a0, a1) : a0);
   }
   if (j == 0 && valid) logits[(int64_t)s * E + e] = v;
 }
@@ -116,13 +128,19 @@ void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int 
                           float* logits, int* status, cudaStream_t st) {
   if (n_tok <= 0) return;
   static bool attr = false;
-  const size_t smem = 2 * (RL_E + RL_T) * RL_KC * sizeof(float);
+  const size_t smem = 2 * (RL_E + RL_T) * RL_ROW * sizeof(float);
   if (!attr) {
-    cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(router_logits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(router_logits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr = true;
   }
   dim3 grid(ceil_div(E, RL_E), ceil_div(n_tok, RL_T));
-  router_logits_kernel<<<grid, RL_THREADS, smem, st>>>(w, row_stride_floats, E, d, h, n_tok, logits, status);
+  // quant::matmul's dispatch (quant.rs:241): the GEMM path needs >= 4 rows and
+  // d % 8 == 0; otherwise quant::dot per output.
+  if (n_tok >= 4 && d % 8 == 0)
+    router_logits_kernel<true><<<grid, RL_THREADS, smem, st>>>(w, row_stride_floats, E, d, h, n_tok, logits, status);
+  else
+    router_logits_kernel<false><<<grid, RL_THREADS, smem, st>>>(w, row_stride_floats, E, d, h, n_tok, logits, status);
 }
 
 // ---------------------------------------------------------------------------
@@ -131,15 +149,18 @@ void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int 
 // renormalisation by the selection's sequential sum clamped at 2^-14, and
 // optional weights_scale. One warp per token; p lives in shared memory.
 constexpr int RT_WARPS = 4;
+constexpr int RT_MAXK = 64;
 
 __global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __restrict__ logits, int n_tok, int E,
                                                                int k, int norm_topk, float weights_scale,
                                                                int* __restrict__ ids, float* __restrict__ wout) {
-  extern __shared__ float sp[];  // [RT_WARPS][E]
+  extern __shared__ float sp[];  // [RT_WARPS][E] probabilities, then [RT_WARPS][RT_MAXK] selections
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int s = blockIdx.x * RT_WARPS + warp;
   if (s >= n_tok) return;
   float* p = sp + warp * E;
+  float* selw = sp + RT_WARPS * E + warp * RT_MAXK;
+  int* seli = reinterpret_cast<int*>(sp + RT_WARPS * (E + RT_MAXK)) + warp * RT_MAXK;
   const float* row = logits + (int64_t)s * E;
   float m = -INFINITY;
   for (int e = lane; e < E; e += 32) m = fmaxf(m, row[e]);
@@ -147,9 +168,19 @@ __global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __res
   for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   for (int e = lane; e < E; e += 32) p[e] = expf(__fsub_rn(row[e], m));
   __syncwarp();
+  // Sequential sum (transformer.rs:481), loads batched ahead of the adds.
   float sum = -0.0f;
-  if (lane == 0)
-    for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, p[e]);
+  if (lane == 0) {
+    int e = 0;
+    for (; e + 8 <= E; e += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = p[e + u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) sum = __fadd_rn(sum, v[u]);
+    }
+    for (; e < E; ++e) sum = __fadd_rn(sum, p[e]);
+  }
   sum = __shfl_sync(0xffffffffu, sum, 0);
   for (int e = lane; e < E; e += 32) p[e] = __fdiv_rn(p[e], sum);
   __syncwarp();
@@ -157,31 +188,30 @@ __global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __res
   // is the first k of the reference's stable sort). Probabilities are >= 0, so
   // a taken entry is marked with -1 in shared memory.
   constexpr int NONE = 0x7fffffff;
-  float selw[64];
-  int seli[64];
   for (int r = 0; r < k; ++r) {
     float bp = 0.f;
     int bi = NONE;
     for (int e = lane; e < E; e += 32) {
-      float v = p[e];
+      const float v = p[e];
       if (v < 0.f) continue;
-      if (bi == NONE || v > bp || (v == bp && e < bi)) {
+      if (bi == NONE || v > bp) {  // e increases within a lane: ties keep the lower index
         bp = v;
         bi = e;
       }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
-      float op = __shfl_xor_sync(0xffffffffu, bp, o);
-      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (oi != NONE && (bi == NONE || op > bp || (op == bp && oi < bi))) {
         bp = op;
         bi = oi;
       }
     }
-    seli[r] = bi;
-    selw[r] = bp;
-    __syncwarp();
+    if (lane == 0) {
+      seli[r] = bi;
+      selw[r] = bp;
+    }
     if (bi != NONE && lane == (bi & 31)) p[bi] = -1.f;
     __syncwarp();
   }
@@ -194,17 +224,18 @@ __global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __res
     }
     if (weights_scale != 0.f && weights_scale != 1.f)
       for (int r = 0; r < k; ++r) selw[r] = __fmul_rn(selw[r], weights_scale);
-    for (int r = 0; r < k; ++r) {
-      ids[(int64_t)s * k + r] = seli[r];
-      wout[(int64_t)s * k + r] = selw[r];
-    }
+  }
+  __syncwarp();
+  for (int r = lane; r < k; r += 32) {
+    ids[(int64_t)s * k + r] = seli[r];
+    wout[(int64_t)s * k + r] = selw[r];
   }
 }
 
 void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
                   float* w, cudaStream_t st) {
   if (n_tok <= 0) return;
-  size_t smem = (size_t)RT_WARPS * E * sizeof(float);
+  size_t smem = (size_t)RT_WARPS * (E + 2 * RT_MAXK) * sizeof(float);
   route_kernel<<<ceil_div(n_tok, RT_WARPS), RT_WARPS * 32, smem, st>>>(logits, n_tok, E, k, norm_topk,
                                                                        weights_scale, ids, w);
 }
@@ -227,6 +258,7 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
   int* cnt = pref + 32 * E;                            // [E]
   int* base = cnt + E;                                 // [E]
   int* offs = base + E;                                // [E+1]
+  __shared__ int4 wsum[32];
   const int tid = threadIdx.x, warp = tid / 32, lane = tid & 31;
   for (int e = tid; e < E; e += DP_THREADS) {
     cnt[e] = 0;
@@ -239,26 +271,62 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
     if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (tid == 0) {
-    int run = 0, ns = 0, nl = 0, tt = 0;
-    for (int e = 0; e < E; ++e) {
-      offs[e] = run;
-      o.offsets[e] = run;
-      o.counts[e] = cnt[e];
-      run += cnt[e];
-      if (cnt[e] >= 1 && cnt[e] <= 3) {
-        o.small_list[ns++] = e;
-      } else if (cnt[e] >= 4) {
-        o.large_tt[nl] = tt;
-        tt += (cnt[e] + 127) / 128;
-        o.large_list[nl++] = e;
+  // Block-wide exclusive scan over experts (thread e): slot offsets, positions
+  // in the small (1..3 rows) and large (>= 4 rows) lists, and the large
+  // experts' 128-slot tile prefix.
+  {
+    const int e = tid;
+    const int c = e < E ? cnt[e] : 0;
+    const int fs = (c >= 1 && c <= 3) ? 1 : 0, fl = c >= 4 ? 1 : 0, ft = fl ? (c + 127) / 128 : 0;
+    int4 v = make_int4(c, fs, fl, ft);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, v.x, o), y = __shfl_up_sync(0xffffffffu, v.y, o);
+      const int z = __shfl_up_sync(0xffffffffu, v.z, o), t = __shfl_up_sync(0xffffffffu, v.w, o);
+      if (lane >= o) {
+        v.x += x;
+        v.y += y;
+        v.z += z;
+        v.w += t;
       }
     }
-    o.large_tt[nl] = tt;
-    offs[E] = run;
-    o.offsets[E] = run;
-    o.n_lists[0] = ns;
-    o.n_lists[1] = nl;
+    if (lane == 31) wsum[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int4 u = wsum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, u.x, o), y = __shfl_up_sync(0xffffffffu, u.y, o);
+        const int z = __shfl_up_sync(0xffffffffu, u.z, o), t = __shfl_up_sync(0xffffffffu, u.w, o);
+        if (lane >= o) {
+          u.x += x;
+          u.y += y;
+          u.z += z;
+          u.w += t;
+        }
+      }
+      wsum[lane] = u;  // inclusive over warps
+    }
+    __syncthreads();
+    const int4 wb = warp > 0 ? wsum[warp - 1] : make_int4(0, 0, 0, 0);
+    const int4 ex = make_int4(wb.x + v.x - c, wb.y + v.y - fs, wb.z + v.z - fl, wb.w + v.w - ft);
+    if (e < E) {
+      offs[e] = ex.x;
+      o.offsets[e] = ex.x;
+      o.counts[e] = c;
+      if (fs) o.small_list[ex.y] = e;
+      if (fl) {
+        o.large_list[ex.z] = e;
+        o.large_tt[ex.z] = ex.w;
+      }
+    }
+    if (e == E - 1) {
+      offs[E] = ex.x + c;
+      o.offsets[E] = ex.x + c;
+      o.n_lists[0] = ex.y + fs;
+      o.n_lists[1] = ex.z + fl;
+      o.large_tt[ex.z + fl] = ex.w + ft;
+    }
   }
   __syncthreads();
   const uint32_t lt = (1u << lane) - 1u;
@@ -305,7 +373,7 @@ int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, con
     cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr_set = true;
   }
-  if (smem > 200 * 1024) return KC_ERR_SHAPE;
+  if (smem > 200 * 1024 || E > DP_THREADS) return KC_ERR_SHAPE;
   dispatch_kernel<<<1, DP_THREADS, smem, st>>>(ids, w, n_tok, k, E, o);
   return KC_OK;
 }
@@ -332,26 +400,26 @@ void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st) { dense_met
 __global__ void combine_kernel(const float* __restrict__ y, const int* __restrict__ tok_slot,
                                const int* __restrict__ ids, const float* __restrict__ w, int k, int d,
                                float* __restrict__ out) {
-  __shared__ int se[64], ss[64];
+  __shared__ int ea[64], ss[64];
   __shared__ float sw[64];
   const int s = blockIdx.x;
-  if (threadIdx.x == 0) {
-    int n = 0;
-    for (int j = 0; j < k; ++j) {
-      int e = ids[(int64_t)s * k + j];
-      int slot = tok_slot[(int64_t)s * k + j];
-      float wj = w[(int64_t)s * k + j];
-      int p = n++;
-      while (p > 0 && se[p - 1] > e) {
-        se[p] = se[p - 1];
-        ss[p] = ss[p - 1];
-        sw[p] = sw[p - 1];
-        --p;
-      }
-      se[p] = e;
-      ss[p] = slot;
-      sw[p] = wj;
-    }
+  // Order the token's k selections by expert id: entry j goes to position
+  // rank(j) = number of its selections with a smaller id (ids are distinct).
+  const int t = threadIdx.x;
+  int e = 0, slot = 0;
+  float wj = 0.f;
+  if (t < k) {
+    e = ids[(int64_t)s * k + t];
+    slot = tok_slot[(int64_t)s * k + t];
+    wj = w[(int64_t)s * k + t];
+    ea[t] = e;
+  }
+  __syncthreads();
+  if (t < k) {
+    int rank = 0;
+    for (int i = 0; i < k; ++i) rank += (ea[i] < e || (ea[i] == e && i < t)) ? 1 : 0;
+    ss[rank] = slot;
+    sw[rank] = wj;
   }
   __syncthreads();
   for (int c = threadIdx.x * 4; c < d; c += blockDim.x * 4) {
