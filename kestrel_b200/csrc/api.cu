@@ -70,6 +70,8 @@ struct Work {
   float* h_in = nullptr;   // staging for host-pointer calls
   float* out = nullptr;
   float* router_tmp = nullptr;
+  float* mma_part = nullptr;  // split-K partial tiles of the tcgen05 kernel
+  int* mma_cnt = nullptr;     // its per-tile counters (zeroed at allocation)
 };
 
 }  // namespace
@@ -208,6 +210,7 @@ int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
       A * D * 4,                         // y
       (size_t)T * D * 4, (size_t)T * D * 4,  // h_in, out
       (size_t)E * D * 4,                 // router_tmp
+      mma_part_bytes(), mma_cnt_bytes(),  // mma_part, mma_cnt
   };
   size_t total = 0;
   for (size_t s : sz) total += al(s);
@@ -254,6 +257,9 @@ int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
   take((void**)&w.h_in);
   take((void**)&w.out);
   take((void**)&w.router_tmp);
+  take((void**)&w.mma_part);
+  take((void**)&w.mma_cnt);
+  CK(cudaMemsetAsync(w.mma_cnt, 0, mma_cnt_bytes(), ctx->stream));
   return KC_OK;
 }
 
@@ -391,6 +397,8 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
       alignas(64) unsigned char tmap[128];
       if (make_tmap_f16(tmap, W.x16, A, d) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
       MmaArgs ma{};
+      ma.part = W.mma_part;
+      ma.tile_cnt = W.mma_cnt;
       ma.w[0] = L.gate;
       ma.w[1] = L.up;
       ma.n_mat = 2;
@@ -463,6 +471,8 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
       alignas(64) unsigned char tmap[128];
       if (make_tmap_f16(tmap, W.act16, A, ff) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (act16) failed");
       MmaArgs ma{};
+      ma.part = W.mma_part;
+      ma.tile_cnt = W.mma_cnt;
       ma.w[0] = L.down;
       ma.n_mat = 1;
       ma.expert_stride = L.mb_down;
@@ -817,6 +827,8 @@ int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out)
     alignas(64) unsigned char tmap[128];
     if (make_tmap_f16(tmap, W.x16, n, D.cols) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
     MmaArgs ma{};
+    ma.part = W.mma_part;
+    ma.tile_cnt = W.mma_cnt;
     ma.w[0] = D.w;
     ma.n_mat = 1;
     ma.rows = (int)D.rows;

@@ -32,7 +32,8 @@ namespace kc {
 constexpr int MM = 128;       // weight rows per tile
 constexpr int MK = 64;        // K elements per operand stage (one 128B swizzle atom)
 constexpr int MN = 128;       // slots per tile
-constexpr int M_THREADS = 192;
+constexpr int M_DQW = 8;      // dequantisation + epilogue warps (two per row: one per 32-element half)
+constexpr int M_THREADS = 64 + 32 * M_DQW;
 constexpr int M_OPS = 3;      // operand stages
 constexpr int M_RAWS = 2;     // raw superblock stages
 constexpr int A_BYTES = MM * MK * 2;  // 16 KB
@@ -126,83 +127,83 @@ __device__ __forceinline__ void mma_q4k_sm(int jj, uint32_t w0, uint32_t w1, uin
   }
 }
 
-// Q4_K (quant.rs:138-155): y = (d*sc)*q - dmin*m, per 32-element sub-block.
-__device__ __forceinline__ void dq_q4k(const uint8_t* sbt, int rr, int kk, uint8_t* A, int m) {
+// Exact float of byte i of w (0..255): the byte is placed under the exponent
+// of 2^23 and 2^23 + `bias` is subtracted, with full-rate instructions.
+__device__ __forceinline__ float byte_f(uint32_t w, int i, float bias) {
+  return __fsub_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)i)), bias);
+}
+
+// Half `hf` (32 elements) of the 64-element K chunk kk of a row, per type.
+// Q4_K (quant.rs:138-155): y = (d*sc)*q - dmin*m; half 0 = sub-block 2kk (low
+// nibbles), half 1 = sub-block 2kk+1 (high nibbles).
+__device__ __forceinline__ void dq_q4k(const uint8_t* sbt, int rr, int kk, int hf, uint8_t* A, int m) {
   const uint4 hdr = *reinterpret_cast<const uint4*>(sbt + 16 * rr);
   const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
-  int s0, m0, s1, m1;
-  mma_q4k_sm(2 * kk, hdr.y, hdr.z, hdr.w, s0, m0);
-  mma_q4k_sm(2 * kk + 1, hdr.y, hdr.z, hdr.w, s1, m1);
-  const float d1 = __fmul_rn(d, (float)s0), mm1 = __fmul_rn(dmin, (float)m0);
-  const float d2 = __fmul_rn(d, (float)s1), mm2 = __fmul_rn(dmin, (float)m1);
+  int sc, mn;
+  mma_q4k_sm(2 * kk + hf, hdr.y, hdr.z, hdr.w, sc, mn);
+  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
   const uint4 q0 = *reinterpret_cast<const uint4*>(sbt + kPlane + kPlane * (2 * kk) + 16 * rr);
   const uint4 q1 = *reinterpret_cast<const uint4*>(sbt + kPlane + kPlane * (2 * kk + 1) + 16 * rr);
   const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    float lo[8], hi[8];
+    float v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t byte = (qw[2 * c + i / 4] >> (8 * (i & 3))) & 0xFF;
-      lo[i] = __fsub_rn(__fmul_rn(d1, (float)(byte & 0xF)), mm1);
-      hi[i] = __fsub_rn(__fmul_rn(d2, (float)(byte >> 4)), mm2);
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const uint32_t nw = (hf ? (qw[2 * c + h2] >> 4) : qw[2 * c + h2]) & 0x0F0F0F0Fu;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[4 * h2 + i] = __fsub_rn(__fmul_rn(d1, byte_f(nw, i, 8388608.0f)), m1);
     }
-    put8(A, m, c, lo);
-    put8(A, m, c + 4, hi);
+    put8(A, m, 4 * hf + c, v);
   }
 }
 
 // Q6_K (quant.rs:180-201): y = (d*sc)*(q-32).
-__device__ __forceinline__ void dq_q6k(const uint8_t* sbt, int rr, int kk, uint8_t* A, int m) {
-  const int h = kk >> 1, nib = kk & 1;
+__device__ __forceinline__ void dq_q6k(const uint8_t* sbt, int rr, int kk, int hf, uint8_t* A, int m) {
+  const int h = kk >> 1, nib = kk & 1, r2 = 2 * nib + hf;
   const float d = h2f(*reinterpret_cast<const uint16_t*>(sbt + 13 * kPlane + 2 * rr));
   const uint4 scw = *reinterpret_cast<const uint4*>(sbt + 12 * kPlane + 16 * rr);
-  const uint32_t sw[4] = {scw.x, scw.y, scw.z, scw.w};
+  // ql bytes 64h + 32hf .. +31 = chunks 4h + 2hf (+1); qh bytes 32h .. +31 = chunks 2h (+1).
+  const uint8_t* qlp = sbt + kPlane * (4 * h + 2 * hf) + 16 * rr;
+  const uint8_t* qhp = sbt + 8 * kPlane + kPlane * (2 * h) + 16 * rr;
+  const uint4 l0 = *reinterpret_cast<const uint4*>(qlp), l1 = *reinterpret_cast<const uint4*>(qlp + kPlane);
+  const uint4 h0 = *reinterpret_cast<const uint4*>(qhp), h1 = *reinterpret_cast<const uint4*>(qhp + kPlane);
+  const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+  const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {  // elements 32*half .. 32*half+31 of the chunk
-    const int r2 = 2 * nib + half;
-    // ql bytes 64h + 32half .. +31 = chunks 4h + 2half (+1); qh bytes 32h .. +31 = chunks 2h (+1).
-    const uint8_t* qlp = sbt + kPlane * (4 * h + 2 * half) + 16 * rr;
-    const uint8_t* qhp = sbt + 8 * kPlane + kPlane * (2 * h) + 16 * rr;
-    const uint4 l0 = *reinterpret_cast<const uint4*>(qlp), l1 = *reinterpret_cast<const uint4*>(qlp + kPlane);
-    const uint4 h0 = *reinterpret_cast<const uint4*>(qhp), h1 = *reinterpret_cast<const uint4*>(qhp + kPlane);
-    const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  for (int c = 0; c < 4; ++c) {  // 8 elements l = 8c .. 8c+7
+    const int si = 8 * h + 2 * r2 + (c >> 1);
+    const uint32_t swd = (si >> 3) ? ((si >> 2) & 1 ? scw.w : scw.z) : ((si >> 2) & 1 ? scw.y : scw.x);
+    const float dsc = __fmul_rn(d, (float)(int)(int8_t)((swd >> (8 * (si & 3))) & 0xFF));
+    float v[8];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {  // 8 elements l = 8c .. 8c+7
-      const int si = 8 * h + 2 * r2 + (c >> 1);
-      const float dsc = __fmul_rn(d, (float)(int)(int8_t)((sw[si >> 2] >> (8 * (si & 3))) & 0xFF));
-      float v[8];
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int wi = 2 * c + h2;
+      const uint32_t qv = ((lw[wi] >> (4 * nib)) & 0x0F0F0F0Fu) | (((hw[wi] >> (2 * r2)) & 0x03030303u) << 4);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int l = 8 * c + i;
-        const uint32_t qlb = (lw[l >> 2] >> (8 * (l & 3))) & 0xFF;
-        const uint32_t qhb = (hw[l >> 2] >> (8 * (l & 3))) & 0xFF;
-        const int q = (int)(((qlb >> (4 * nib)) & 0xF) | (((qhb >> (2 * r2)) & 3) << 4)) - 32;
-        v[i] = __fmul_rn(dsc, (float)q);
-      }
-      put8(A, m, 4 * half + c, v);
+      for (int i = 0; i < 4; ++i) v[4 * h2 + i] = __fmul_rn(dsc, byte_f(qv, i, 8388640.0f));  // q - 32
     }
+    put8(A, m, 4 * hf + c, v);
   }
 }
 
-// Q8_0 (quant.rs:82-89): y = q*d, chunk of up to 8 blocks.
-__device__ __forceinline__ void dq_q8_0(const uint8_t* cb, int nblk, int rr, int kk, uint8_t* A, int m) {
+// Q8_0 (quant.rs:82-89): y = q*d; half hf = block 2kk + hf of the chunk.
+__device__ __forceinline__ void dq_q8_0(const uint8_t* cb, int nblk, int rr, int kk, int hf, uint8_t* A, int m) {
+  const int b = 2 * kk + hf;
+  const float d = h2f(*reinterpret_cast<const uint16_t*>(cb + 2 * kPlane * nblk + 16 * rr + 2 * b));
+  const uint4 q0 = *reinterpret_cast<const uint4*>(cb + kPlane * (2 * b) + 16 * rr);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(cb + kPlane * (2 * b + 1) + 16 * rr);
+  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-  for (int bi = 0; bi < 2; ++bi) {
-    const int b = 2 * kk + bi;
-    const float d = h2f(*reinterpret_cast<const uint16_t*>(cb + 2 * kPlane * nblk + 16 * rr + 2 * b));
-    const uint4 q0 = *reinterpret_cast<const uint4*>(cb + kPlane * (2 * b) + 16 * rr);
-    const uint4 q1 = *reinterpret_cast<const uint4*>(cb + kPlane * (2 * b + 1) + 16 * rr);
-    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  for (int c = 0; c < 4; ++c) {
+    float v[8];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float v[8];
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const uint32_t uw = qw[2 * c + h2] ^ 0x80808080u;  // q + 128 per byte
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        v[i] = __fmul_rn((float)(int)(int8_t)((qw[2 * c + i / 4] >> (8 * (i & 3))) & 0xFF), d);
-      put8(A, m, 4 * bi + c, v);
+      for (int i = 0; i < 4; ++i) v[4 * h2 + i] = __fmul_rn(byte_f(uw, i, 8388736.0f), d);
     }
+    put8(A, m, 4 * hf + c, v);
   }
 }
 
@@ -228,6 +229,19 @@ __device__ __forceinline__ Tile tile_of(const MmaArgs& a, int w, int row_tiles, 
   return t;
 }
 
+// Named barrier among the dequantisation/epilogue warps only.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(32 * M_DQW) : "memory"); }
+
+// Work items: (tile, split). With few tiles (decode-sized batches) the K range
+// of each tile is split over S work items so that more SMs stream weights; each
+// writes an f32 partial tile and the last one to finish (a per-tile counter)
+// adds the S partials in split order and stores the result.
+__device__ __forceinline__ int split_count(const MmaArgs& a, int total, int nsb) {
+  if (!a.part || total <= 0) return 1;
+  const int s = min(nsb, (int)gridDim.x / total);
+  return s >= 2 ? s : 1;
+}
+
 template <int T, int NMAT>
 __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs a,
                                                                      const __grid_constant__ CUtensorMap tmap_b) {
@@ -235,32 +249,40 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
   __shared__ __align__(8) uint64_t raw_full[M_RAWS], raw_empty[M_RAWS], op_full[M_OPS], op_empty[M_OPS];
   __shared__ __align__(8) uint64_t acc_full, acc_empty;
   __shared__ uint32_t tmem_base_sh;
+  __shared__ int last_sh;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_large = *a.n_list;
   const int row_tiles = (a.rows + MM - 1) / MM;
   const int total = n_large > 0 ? a.tt_prefix[n_large] * row_tiles : 0;
-  if ((int)blockIdx.x >= total) return;
+  const int nkc = a.cols / MK;
+  const int nsb = tiled_nsb(T, a.cols);
+  const int S = split_count(a, total, nsb);
+  const int items = total * S;
+  if ((int)blockIdx.x >= items) return;
   const MmaSmem L = mma_smem(T, NMAT);
   uint8_t* msm = msm_raw + ((1024 - (smem_u32(msm_raw) & 1023)) & 1023);
   uint8_t* ops = msm;
   uint8_t* raws = msm + M_OPS * L.op_bytes;
-  const int nkc = a.cols / MK;
-  const int nsb = tiled_nsb(T, a.cols);
   const int64_t tile_bytes = tiled_tile_bytes(T, a.cols);
   const int prows = (int)padded_rows(a.rows);
   const uint32_t tcols = NMAT * MN;  // 128 or 256 TMEM columns
+  // K chunks [kc0, kc1) of split s: whole superblocks (4 chunks of 64).
+  auto k_range = [&](int s, int& kc0, int& kc1) {
+    kc0 = 4 * (s * nsb / S);
+    kc1 = min(nkc, 4 * ((s + 1) * nsb / S));
+  };
 
   if (tid == 0) {
     for (int i = 0; i < M_RAWS; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 4);
+      mbar_init(&raw_empty[i], M_DQW);
     }
     for (int i = 0; i < M_OPS; ++i) {
-      mbar_init(&op_full[i], 1 + 4);
+      mbar_init(&op_full[i], 1 + M_DQW);
       mbar_init(&op_empty[i], 1);
     }
     mbar_init(&acc_full, 1);
-    mbar_init(&acc_empty, 4);
+    mbar_init(&acc_empty, M_DQW);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -277,10 +299,12 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
   if (warp == 0) {
     if (lane == 0) {
       int raw_it = 0, op_it = 0;
-      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
-        const Tile t = tile_of(a, w, row_tiles, n_large);
+      for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
+        const Tile t = tile_of(a, w / S, row_tiles, n_large);
+        int kc0, kc1;
+        k_range(w % S, kc0, kc1);
         const int n_rt = min(M_RT, (prows - MM * t.rt) / kTileRows);
-        for (int kc = 0; kc < nkc && ok; ++kc) {
+        for (int kc = kc0; kc < kc1 && ok; ++kc) {
           const int sb = kc >> 2;
           if ((kc & 3) == 0) {
             const int r = raw_it % M_RAWS;
@@ -317,8 +341,10 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
   } else if (warp == 1) {
     if (lane == 0) {
       int op_it = 0, tile_it = 0;
-      for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++tile_it) {
-        const Tile t = tile_of(a, w, row_tiles, n_large);
+      for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++tile_it) {
+        const Tile t = tile_of(a, w / S, row_tiles, n_large);
+        int kc0, kc1;
+        k_range(w % S, kc0, kc1);
         const int n = ((t.nt + 15) / 16) * 16;
         const uint32_t idesc = f16_idesc(n);
         if (tile_it > 0 && !mbar_wait(&acc_empty, (tile_it - 1) & 1, a.status)) {
@@ -326,7 +352,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
           break;
         }
         tc_fence_after();
-        for (int kc = 0; kc < nkc; ++kc) {
+        for (int kc = kc0; kc < kc1; ++kc) {
           const int o = op_it % M_OPS;
           if (!mbar_wait(&op_full[o], (op_it / M_OPS) & 1, a.status)) {
             ok = false;
@@ -338,7 +364,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
 #pragma unroll
           for (int k16 = 0; k16 < MK / 16; ++k16) {
             const uint64_t bd = sw128_desc(sbb + 32 * k16);
-            const uint32_t acc = (kc > 0 || k16 > 0) ? 1u : 0u;
+            const uint32_t acc = (kc > kc0 || k16 > 0) ? 1u : 0u;
 #pragma unroll
             for (int mt = 0; mt < NMAT; ++mt)
               umma_f16(tmem + mt * MN, sw128_desc(sa + mt * A_BYTES + 32 * k16), bd, idesc, acc);
@@ -353,58 +379,73 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
       if (op_it > 0) mbar_wait(&op_empty[(op_it - 1) % M_OPS], ((op_it - 1) / M_OPS) & 1, a.status);
     }
   } else {
-    // Dequantisation warps: thread t = weight row t of the tile.
-    const int m = tid - 64, rt_local = m / kTileRows, rr = m % kTileRows;
+    // Dequantisation warps: thread t holds weight row m = t % 128 of the tile
+    // and half hf = t / 128 of each 64-element K chunk.
+    const int t_dq = tid - 64, m = t_dq & (MM - 1), hf = t_dq >> 7;
+    const int rt_local = m / kTileRows, rr = m % kTileRows;
     int raw_it = 0, op_it = 0, tile_it = 0;
-    for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++tile_it) {
-      const Tile t = tile_of(a, w, row_tiles, n_large);
+    // Every dequantisation warp runs every item (failed waits only skip the
+    // work), so all of them reach the named barriers below equally often.
+    for (int w = blockIdx.x; w < items; w += gridDim.x, ++tile_it) {
+      const int tile = w / S, split = w % S;
+      const Tile t = tile_of(a, tile, row_tiles, n_large);
+      int kc0, kc1;
+      k_range(split, kc0, kc1);
       int r = 0;
-      for (int kc = 0; kc < nkc; ++kc) {
+      for (int kc = kc0; kc < kc1; ++kc) {
         const int sb = kc >> 2, kk = kc & 3;
         if (kk == 0) {
           r = raw_it % M_RAWS;
-          if (!mbar_wait(&raw_full[r], (raw_it / M_RAWS) & 1, a.status)) ok = false;
+          if (ok && !mbar_wait(&raw_full[r], (raw_it / M_RAWS) & 1, a.status)) ok = false;
         }
         const int o = op_it % M_OPS;
-        if (op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status)) ok = false;
+        if (ok && op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status)) ok = false;
         if (ok) {
           uint8_t* A = ops + o * L.op_bytes;
           const uint8_t* rb = raws + r * L.raw_bytes;
 #pragma unroll
           for (int mt = 0; mt < NMAT; ++mt) {
             const uint8_t* sbt = rb + (mt * M_RT + rt_local) * max_sbt_bytes(T);
-            if (T == T_Q4_K) dq_q4k(sbt, rr, kk, A + mt * A_BYTES, m);
-            else if (T == T_Q6_K) dq_q6k(sbt, rr, kk, A + mt * A_BYTES, m);
-            else dq_q8_0(sbt, min(8, a.cols / 32 - 8 * sb), rr, kk, A + mt * A_BYTES, m);
+            if (T == T_Q4_K) dq_q4k(sbt, rr, kk, hf, A + mt * A_BYTES, m);
+            else if (T == T_Q6_K) dq_q6k(sbt, rr, kk, hf, A + mt * A_BYTES, m);
+            else dq_q8_0(sbt, min(8, a.cols / 32 - 8 * sb), rr, kk, hf, A + mt * A_BYTES, m);
           }
         }
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&op_full[o]);
         ++op_it;
-        if (kk == 3 || kc == nkc - 1 || (T == T_Q8_0 && kc == nkc - 1)) {
+        if (kk == 3 || kc == kc1 - 1) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&raw_empty[r]);
           ++raw_it;
         }
       }
-      (void)nsb;
-      // Epilogue: rows of this warp's TMEM quadrant.
-      if (!mbar_wait(&acc_full, tile_it & 1, a.status)) ok = false;
+      // Epilogue: rows of this warp's TMEM quadrant (warp % 4); the two warps
+      // of a quadrant take alternate 16-column blocks.
+      if (ok && !mbar_wait(&acc_full, tile_it & 1, a.status)) ok = false;
       tc_fence_after();
-      const int quad = warp & 3;
-      const int row = MM * t.rt + quad * 32 + lane;
+      const int quad = warp & 3, colh = (warp - 2) >> 2;
+      const int rl = quad * 32 + lane;
+      const int row = MM * t.rt + rl;
       const int n = ((t.nt + 15) / 16) * 16;
       if (ok) {
-        for (int c0 = 0; c0 < n; c0 += 16) {
+        for (int c0 = 16 * colh; c0 < n; c0 += 32) {
 #pragma unroll
           for (int mt = 0; mt < NMAT; ++mt) {
             float v[16];
             tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + mt * MN + c0, v);
-            if (row < a.rows) {
+            if (S == 1) {
+              if (row < a.rows) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                  if (c0 + i < t.nt) a.out[mt][(int64_t)(t.slot0 + t.t0 + c0 + i) * a.out_stride + row] = v[i];
+              }
+            } else {
+              float* pp = a.part + ((int64_t)w * NMAT + mt) * (MM * MN);
 #pragma unroll
               for (int i = 0; i < 16; ++i)
-                if (c0 + i < t.nt) a.out[mt][(int64_t)(t.slot0 + t.t0 + c0 + i) * a.out_stride + row] = v[i];
+                if (c0 + i < t.nt) pp[(c0 + i) * MM + rl] = v[i];
             }
           }
         }
@@ -412,6 +453,28 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty);
+      if (S > 1) {
+        // Last split of this tile adds the partials in split order.
+        __threadfence();
+        epi_sync();
+        if (tid == 64) last_sh = atomicAdd(&a.tile_cnt[tile], 1) == S - 1 ? 1 : 0;
+        epi_sync();
+        if (last_sh) {
+          __threadfence();
+          if (ok && row < a.rows) {
+            for (int c = colh; c < t.nt; c += 2) {
+#pragma unroll
+              for (int mt = 0; mt < NMAT; ++mt) {
+                float acc = 0.f;
+                for (int s2 = 0; s2 < S; ++s2)
+                  acc = __fadd_rn(acc, __ldcg(a.part + ((int64_t)(tile * S + s2) * NMAT + mt) * (MM * MN) + c * MM + rl));
+                a.out[mt][(int64_t)(t.slot0 + t.t0 + c) * a.out_stride + row] = acc;
+              }
+            }
+          }
+          if (tid == 64) a.tile_cnt[tile] = 0;  // ready for the next launch
+        }
+      }
     }
   }
   tc_fence_before();
@@ -458,10 +521,15 @@ static int launch_t(const MmaArgs& a, const void* tmap, int max_tiles, cudaStrea
       return KC_ERR_CUDA;
     attr = true;
   }
-  const int grid = std::max(1, std::min(num_sms(), max_tiles));
+  // With a split-K workspace every SM gets a CTA (the kernel splits K when the
+  // batch has few tiles); otherwise one CTA per tile at most.
+  const int grid = a.part ? num_sms() : std::max(1, std::min(num_sms(), max_tiles));
   mma_grouped_kernel<T, NMAT><<<grid, M_THREADS, L.total, st>>>(a, *reinterpret_cast<const CUtensorMap*>(tmap));
   return KC_OK;
 }
+
+size_t mma_part_bytes() { return (size_t)num_sms() * 2 * MM * MN * sizeof(float); }
+size_t mma_cnt_bytes() { return (size_t)num_sms() * sizeof(int); }
 
 int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st) {
   if (max_tiles <= 0) return KC_OK;

@@ -20,7 +20,16 @@ struct MmaArgs {
   float* out[2];          // out[m][slot * out_stride + row]
   int64_t out_stride;
   int* status;
+  // Split-K workspace (null: no split): f32 partial tiles for up to gridDim
+  // work items ([item][n_mat][128 x 128]) and per-tile arrival counters
+  // (zero before the first launch; each launch leaves them zero).
+  float* part;
+  int* tile_cnt;
 };
+// Bytes of the split-K workspace a launch may use: partial tiles for one work
+// item per SM, and one counter per SM.
+size_t mma_part_bytes();
+size_t mma_cnt_bytes();
 
 // 128-byte CUtensorMap for an f16 row-major [rows, cols] activation matrix,
 // box 64 x 128, 128B swizzle.
