@@ -74,6 +74,29 @@ struct Work {
   int* mma_cnt = nullptr;     // its per-tile counters (zeroed at allocation)
 };
 
+// Expert-parallel exchange buffers. Home side (this rank's tokens): routing,
+// plans, the rows sent and the result rows received. Owner side (rows received
+// from every rank): the rows, their selections and the result rows sent back.
+struct EpBufs {
+  int T = 0, k = 0, d = 0;  // home capacity: tokens, selections, d
+  int* ids_home = nullptr;
+  float* w_home = nullptr;
+  int* send_tok = nullptr;  // [world][T]
+  int* ret_pos = nullptr;   // [T * k]
+  int* xch = nullptr;       // [2][world][2]: counts sent, counts received
+  float* sendbuf = nullptr; // [world * T][d]
+  int32_t* sendmeta = nullptr;
+  float* retrecv = nullptr; // [T * k][d]
+  int R = 0, RS = 0;        // owner capacity: received rows, result rows sent
+  float* recvbuf = nullptr;
+  int32_t* recvmeta = nullptr;
+  int* ids_loc = nullptr;
+  float* w_loc = nullptr;
+  int* ret_send_pos = nullptr;
+  float* retsend = nullptr;
+  int* xch_host = nullptr;  // pinned copy of xch
+};
+
 }  // namespace
 
 // Per-stage CUDA event pairs (kc_profile_enable).
@@ -106,8 +129,10 @@ struct kc_ctx {
   std::map<int, Layer> layers;
   std::map<int, Dense> dense;
   Work ws;
+  Work ws_ep;  // the owner-side expert products of expert parallelism
   int64_t weight_bytes = 0;
   EpState ep;
+  EpBufs epb;
   Prof prof;
 };
 
@@ -180,9 +205,8 @@ size_t rec_bytes(int64_t cols) {
   return (size_t)std::max(rec_row_bytes(true, cols), rec_row_bytes(false, cols)) + 512;
 }
 
-// (Re)allocate the workspace so it holds at least the given dimensions.
-int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
-  Work& w = ctx->ws;
+// (Re)allocate workspace w so it holds at least the given dimensions.
+int ensure_work(kc_ctx* ctx, Work& w, int T, int E, int K, int D, int F) {
   if (T <= w.T && E <= w.E && K <= w.K && D <= w.D && F <= w.F && w.arena) return KC_OK;
   T = std::max(T, w.T);
   E = std::max(E, w.E);
@@ -262,6 +286,7 @@ int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) {
   CK(cudaMemsetAsync(w.mma_cnt, 0, mma_cnt_bytes(), ctx->stream));
   return KC_OK;
 }
+int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) { return ensure_work(ctx, ctx->ws, T, E, K, D, F); }
 
 int check_status(kc_ctx* ctx) {
   int st = 0;
@@ -329,8 +354,350 @@ int num_sms() {
 
 // ---------------------------------------------------------------------------
 // Layer pipeline on device buffers. h/out [n_tok, d]; optional ids/w outputs.
+// Expert products of n_rows activation rows h for their k selections ids
+// (expert ids in [0, E) of the layer's device table, offset by ebase; -1 or
+// out-of-range ids are skipped): dispatch (permute), activation records,
+// gate/up (+SwiGLU), down. Leaves y [slot, d] and the dispatch metadata
+// (slot of every selection in W.meta.tok_slot) in workspace W, which must be
+// sized for (n_rows, E, k, d, ff).
+static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebase, const float* h, int n_rows,
+                           const int* ids, const float* wts, int k) {
+  const int d = L.d, ff = L.ff;
+  cudaStream_t st = ctx->stream;
+  if (n_rows == 0) return KC_OK;
+  // 2. dispatch metadata (permute).
+  {
+    StageScope ss(ctx, KC_STAGE_DISPATCH);
+    RC(launch_dispatch(ids, wts, n_rows, k, E, W.meta, st));
+    CKL();
+  }
+  // 3. activation records of every slot's input row (int8 path) and its f16
+  //    copy (tensor-core path).
+  const bool kq_in = is_k(L.t_gate), kq_dn = is_k(L.t_down);
+  const int A = n_rows * k;
+  const int max_small = std::min(E, A);
+  const bool mma_gu = mma_supported(L.t_gate, d, 2);
+  {
+    StageScope ss(ctx, KC_STAGE_QUANT_X);
+    launch_act_records(kq_in, h, nullptr, W.meta.slot_tok, A, d, W.xrec, A, nullptr, mma_gu ? W.x16 : nullptr, st);
+    CKL();
+  }
+  // 4. gate and up products -> g, u [slot, ff].
+  {
+    StageScope ss(ctx, KC_STAGE_GATE_UP_INT8);
+    DecodeArgs dg{};
+    dg.w[0] = L.gate;
+    dg.w[1] = L.up;
+    dg.n_mat = 2;
+    dg.expert_stride = L.mb_gate;
+    dg.expert_base = ebase;
+    dg.rows = ff;
+    dg.cols = d;
+    dg.type = L.t_gate;
+    dg.list = W.meta.small_list;
+    dg.n_list = W.meta.n_lists;
+    dg.offsets = W.meta.offsets;
+    dg.rec = W.xrec;
+    dg.rec_slots = A;
+    dg.out[0] = W.g;
+    dg.out[1] = W.u;
+    dg.out_stride = ff;
+    dg.status = ctx->status;
+    RC(launch_decode(dg, max_small * 2 * ceil_div(ff, kTileRows), st));
+    CKL();
+  }
+  const int max_tt = ceil_div(A, 128) + std::min(E, A / 4);
+  if (mma_gu) {
+    StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
+    alignas(64) unsigned char tmap[128];
+    if (make_tmap_f16(tmap, W.x16, A, d) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
+    MmaArgs ma{};
+    ma.part = W.mma_part;
+    ma.tile_cnt = W.mma_cnt;
+    ma.w[0] = L.gate;
+    ma.w[1] = L.up;
+    ma.n_mat = 2;
+    ma.expert_stride = L.mb_gate;
+    ma.expert_base = ebase;
+    ma.rows = ff;
+    ma.cols = d;
+    ma.type = L.t_gate;
+    ma.list = W.meta.large_list;
+    ma.n_list = W.meta.n_lists + 1;
+    ma.offsets = W.meta.offsets;
+    ma.tt_prefix = W.meta.large_tt;
+    ma.out[0] = W.g;
+    ma.out[1] = W.u;
+    ma.out_stride = ff;
+    ma.status = ctx->status;
+    RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(ff, 128), st));
+    CKL();
+  } else {
+    GroupedArgs g = grouped_base(ctx);
+    g.w0 = L.gate;
+    g.w1 = L.up;
+    g.expert_stride = L.mb_gate;
+    g.expert_base = ebase;
+    g.rows = ff;
+    g.cols = d;
+    g.type = L.t_gate;
+    g.offsets = W.meta.offsets;
+    g.slot_src = W.meta.slot_tok;
+    g.af = h;
+    g.out = W.g;
+    g.out2 = W.u;
+    g.out_stride = ff;
+    g.list = W.meta.large_list;
+    g.n_list = W.meta.n_lists + 1;
+    StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
+    RC(launch_grouped_f32(g, true, std::min(E, A / 4), n_rows, st));
+    CKL();
+  }
+  // 5. SwiGLU of every slot -> act (f32) and its activation records.
+  {
+    StageScope ss(ctx, KC_STAGE_QUANT_ACT);
+    launch_act_records(kq_dn, W.g, W.u, nullptr, A, ff, W.arec, A, W.act, W.act16, st);
+    CKL();
+  }
+  // 6. down -> y [slot, d].
+  {
+    StageScope ss(ctx, KC_STAGE_DOWN_INT8);
+    DecodeArgs dd{};
+    dd.w[0] = L.down;
+    dd.n_mat = 1;
+    dd.expert_stride = L.mb_down;
+    dd.expert_base = ebase;
+    dd.rows = d;
+    dd.cols = ff;
+    dd.type = L.t_down;
+    dd.list = W.meta.small_list;
+    dd.n_list = W.meta.n_lists;
+    dd.offsets = W.meta.offsets;
+    dd.rec = W.arec;
+    dd.rec_slots = A;
+    dd.out[0] = W.y;
+    dd.out_stride = d;
+    dd.status = ctx->status;
+    RC(launch_decode(dd, max_small * ceil_div(d, kTileRows), st));
+    CKL();
+  }
+  if (mma_supported(L.t_down, ff, 1) && ff % 256 == 0) {
+    StageScope ss(ctx, KC_STAGE_DOWN_F32);
+    alignas(64) unsigned char tmap[128];
+    if (make_tmap_f16(tmap, W.act16, A, ff) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (act16) failed");
+    MmaArgs ma{};
+    ma.part = W.mma_part;
+    ma.tile_cnt = W.mma_cnt;
+    ma.w[0] = L.down;
+    ma.n_mat = 1;
+    ma.expert_stride = L.mb_down;
+    ma.expert_base = ebase;
+    ma.rows = d;
+    ma.cols = ff;
+    ma.type = L.t_down;
+    ma.list = W.meta.large_list;
+    ma.n_list = W.meta.n_lists + 1;
+    ma.offsets = W.meta.offsets;
+    ma.tt_prefix = W.meta.large_tt;
+    ma.out[0] = W.y;
+    ma.out_stride = d;
+    ma.status = ctx->status;
+    RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(d, 128), st));
+    CKL();
+  } else {
+    GroupedArgs dn = grouped_base(ctx);
+    dn.w0 = L.down;
+    dn.expert_stride = L.mb_down;
+    dn.expert_base = ebase;
+    dn.rows = d;
+    dn.cols = ff;
+    dn.type = L.t_down;
+    dn.offsets = W.meta.offsets;
+    dn.slot_src = nullptr;
+    dn.af = W.act;
+    dn.out = W.y;
+    dn.out_stride = d;
+    dn.list = W.meta.large_list;
+    dn.n_list = W.meta.n_lists + 1;
+    StageScope ss(ctx, KC_STAGE_DOWN_F32);
+    RC(launch_grouped_f32(dn, false, std::min(E, A / 4), n_rows, st));
+    CKL();
+  }
+  return KC_OK;
+}
+
+// ---- expert parallelism --------------------------------------------------
+template <typename P>
+static int regrow(P*& p, size_t bytes) {
+  if (p) cudaFree(p);
+  p = nullptr;
+  return cudaMalloc(reinterpret_cast<void**>(&p), std::max<size_t>(bytes, 256)) == cudaSuccess ? KC_OK : KC_ERR_OOM;
+}
+
+static int ep_grow_home(kc_ctx* ctx, int T, int k, int d) {
+  EpBufs& B = ctx->epb;
+  const int G = ctx->ep.world;
+  if (T <= B.T && k <= B.k && d <= B.d && B.ids_home) return KC_OK;
+  CK(cudaStreamSynchronize(ctx->stream));
+  T = std::max(T, B.T);
+  k = std::max(k, B.k);
+  d = std::max(d, B.d);
+  const size_t tk = (size_t)T * k;
+  int rc = KC_OK;
+  if (rc == KC_OK) rc = regrow(B.ids_home, tk * 4);
+  if (rc == KC_OK) rc = regrow(B.w_home, tk * 4);
+  if (rc == KC_OK) rc = regrow(B.send_tok, (size_t)G * T * 4);
+  if (rc == KC_OK) rc = regrow(B.ret_pos, tk * 4);
+  if (rc == KC_OK) rc = regrow(B.xch, (size_t)4 * kEpMaxWorld * 4);
+  if (rc == KC_OK) rc = regrow(B.sendbuf, (size_t)G * T * d * 4);
+  if (rc == KC_OK) rc = regrow(B.sendmeta, (size_t)G * T * 2 * k * 4);
+  if (rc == KC_OK) rc = regrow(B.retrecv, tk * d * 4);
+  if (rc == KC_OK && !B.xch_host && cudaMallocHost(reinterpret_cast<void**>(&B.xch_host), 4 * kEpMaxWorld * 4) != cudaSuccess)
+    rc = KC_ERR_OOM;
+  if (rc != KC_OK) return fail(ctx, rc, "expert-parallel buffers: device allocation failed");
+  B.T = T;
+  B.k = k;
+  B.d = d;
+  return KC_OK;
+}
+
+static int ep_grow_owner(kc_ctx* ctx, int R, int RS, int k, int d) {
+  EpBufs& B = ctx->epb;
+  if (R <= B.R && RS <= B.RS && k <= B.k && d <= B.d && B.recvbuf) return KC_OK;
+  CK(cudaStreamSynchronize(ctx->stream));
+  R = std::max(std::max(R, B.R), 1);
+  RS = std::max(std::max(RS, B.RS), 1);
+  const size_t rk = (size_t)R * k;
+  int rc = KC_OK;
+  if (rc == KC_OK) rc = regrow(B.recvbuf, (size_t)R * d * 4);
+  if (rc == KC_OK) rc = regrow(B.recvmeta, rk * 2 * 4);
+  if (rc == KC_OK) rc = regrow(B.ids_loc, rk * 4);
+  if (rc == KC_OK) rc = regrow(B.w_loc, rk * 4);
+  if (rc == KC_OK) rc = regrow(B.ret_send_pos, rk * 4);
+  if (rc == KC_OK) rc = regrow(B.retsend, (size_t)RS * d * 4);
+  if (rc != KC_OK) return fail(ctx, rc, "expert-parallel buffers: device allocation failed");
+  B.R = R;
+  B.RS = RS;
+  return KC_OK;
+}
+
+static void ep_free_bufs(EpBufs& B) {
+  void* ps[] = {B.ids_home, B.w_home, B.send_tok, B.ret_pos, B.xch, B.sendbuf, B.sendmeta, B.retrecv,
+                B.recvbuf, B.recvmeta, B.ids_loc, B.w_loc, B.ret_send_pos, B.retsend};
+  for (void* p : ps)
+    if (p) cudaFree(p);
+  if (B.xch_host) cudaFreeHost(B.xch_host);
+  B = EpBufs{};
+}
+
+static int ep_rc(kc_ctx* ctx, int rc) {
+  return rc == KC_OK ? KC_OK : fail(ctx, rc, "expert parallel: %s", ep_last_error(ctx->ep));
+}
+
+// Transformer::moe_ffn with the experts sharded over the group: route this
+// rank's tokens, send each token once to every rank owning one of its
+// experts, run the local experts on the rows received from all ranks, send
+// each (token, expert) result row back, and combine in ascending expert id.
+// Every rank must make the same sequence of calls (collectives).
+static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const float* h, int n_tok, float* out,
+                       int32_t* ids_out, float* w_out) {
+  EpState& S = ctx->ep;
+  const int G = S.world, me = S.rank;
+  const int E = L.n_expert, k = L.k, d = L.d, ff = L.ff;
+  if (E % G != 0 || L.n_local != E / G || L.first_expert != me * (E / G))
+    return fail(ctx, KC_ERR_STATE, "expert parallel: layer must hold experts [%d, %d) of %d on rank %d",
+                me * (E / std::max(G, 1)), (me + 1) * (E / std::max(G, 1)), E, me);
+  if (d % 4) return fail(ctx, KC_ERR_SHAPE, "expert parallel: d %% 4 != 0");
+  const int epr = E / G;
+  const int T = std::max(n_tok, 1);
+  RC(ensure_work(ctx, T, E, k, d, ff));
+  RC(ep_grow_home(ctx, T, k, d));
+  EpBufs& B = ctx->epb;
+  cudaStream_t st = ctx->stream;
+  // 1. route this rank's tokens.
+  if (n_tok > 0) {
+    {
+      StageScope ss(ctx, KC_STAGE_ROUTER_LOGITS);
+      launch_router_logits(router, d, E, d, h, n_tok, ctx->ws.logits, ctx->status, st);
+      CKL();
+    }
+    StageScope ss(ctx, KC_STAGE_ROUTE);
+    launch_route(ctx->ws.logits, n_tok, E, k, L.norm_topk, L.weights_scale, B.ids_home, B.w_home, st);
+    CKL();
+  }
+  // 2. plan and pack the rows for every owner; exchange the counts.
+  int* xch_out = B.xch;
+  int* xch_in = B.xch + 2 * kEpMaxWorld;
+  {
+    StageScope ss(ctx, KC_STAGE_DISPATCH);
+    launch_ep_plan(B.ids_home, n_tok, k, G, epr, T, B.send_tok, B.ret_pos, xch_out, st);
+    launch_ep_pack(h, B.ids_home, B.w_home, B.send_tok, xch_out, G, T, k, d, B.sendbuf, B.sendmeta, st);
+    CKL();
+    RC(ep_rc(ctx, ep_exchange_counts(S, xch_out, xch_in, st)));
+    CK(cudaMemcpyAsync(B.xch_host, B.xch, 4 * kEpMaxWorld * sizeof(int), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+  }
+  const int* ho = B.xch_host;                   // [r]: rows sent to r, result rows expected from r
+  const int* hi = B.xch_host + 2 * kEpMaxWorld;  // [r]: rows received from r, result rows owed to r
+  int64_t so[kEpMaxWorld], sb[kEpMaxWorld], ro[kEpMaxWorld], rb[kEpMaxWorld];
+  int64_t mso[kEpMaxWorld], msb[kEpMaxWorld], mro[kEpMaxWorld], mrb[kEpMaxWorld];
+  int64_t yso[kEpMaxWorld], ysb[kEpMaxWorld], yro[kEpMaxWorld], yrb[kEpMaxWorld];
+  int64_t n_recv = 0, n_send = 0, n_ret_send = 0, n_ret_recv = 0;
+  for (int q = 0; q < G; ++q) {
+    so[q] = n_send * d * 4;
+    sb[q] = (int64_t)ho[2 * q] * d * 4;
+    mso[q] = n_send * 2 * k * 4;
+    msb[q] = (int64_t)ho[2 * q] * 2 * k * 4;
+    ro[q] = n_recv * d * 4;
+    rb[q] = (int64_t)hi[2 * q] * d * 4;
+    mro[q] = n_recv * 2 * k * 4;
+    mrb[q] = (int64_t)hi[2 * q] * 2 * k * 4;
+    yso[q] = n_ret_send * d * 4;
+    ysb[q] = (int64_t)hi[2 * q + 1] * d * 4;
+    yro[q] = n_ret_recv * d * 4;
+    yrb[q] = (int64_t)ho[2 * q + 1] * d * 4;
+    n_send += ho[2 * q];
+    n_recv += hi[2 * q];
+    n_ret_send += hi[2 * q + 1];
+    n_ret_recv += ho[2 * q + 1];
+  }
+  if (n_ret_recv != (int64_t)n_tok * k || n_recv > (int64_t)1 << 30)
+    return fail(ctx, KC_ERR_STATE, "expert parallel: inconsistent exchange counts");
+  RC(ep_grow_owner(ctx, (int)n_recv, (int)n_ret_send, k, d));
+  // 3. rows and their selections to the owners.
+  RC(ep_rc(ctx, ep_alltoallv(S, B.sendbuf, so, sb, B.recvbuf, ro, rb, st)));
+  RC(ep_rc(ctx, ep_alltoallv(S, B.sendmeta, mso, msb, B.recvmeta, mro, mrb, st)));
+  // 4. the local experts on every received row.
+  if (n_recv > 0) {
+    const int nr = (int)n_recv;
+    launch_ep_local_ids(B.recvmeta, nr, k, L.first_expert, epr, B.ids_loc, B.w_loc, st);
+    CKL();
+    Work& WO = ctx->ws_ep;
+    RC(ensure_work(ctx, WO, nr, epr, k, d, ff));
+    Layer LL = L;
+    LL.n_expert = epr;
+    RC(experts_forward(ctx, WO, LL, epr, 0, B.recvbuf, nr, B.ids_loc, B.w_loc, k));
+    launch_ep_ret_plan(B.ids_loc, nr, k, B.ret_send_pos, st);
+    launch_ep_ret_pack(WO.y, WO.meta.tok_slot, B.ret_send_pos, nr, k, d, (int)n_ret_send, B.retsend, st);
+    CKL();
+  }
+  // 5. result rows back to their tokens' ranks; combine in ascending expert id.
+  RC(ep_rc(ctx, ep_alltoallv(S, B.retsend, yso, ysb, B.retrecv, yro, yrb, st)));
+  if (n_tok > 0) {
+    StageScope ss(ctx, KC_STAGE_COMBINE);
+    launch_combine(B.retrecv, B.ret_pos, B.ids_home, B.w_home, n_tok, k, d, out, st);
+    CKL();
+  }
+  if (ids_out && n_tok > 0)
+    CK(cudaMemcpyAsync(ids_out, B.ids_home, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
+  if (w_out && n_tok > 0)
+    CK(cudaMemcpyAsync(w_out, B.w_home, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
+  return KC_OK;
+}
+
 static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const float* h, int n_tok, float* out,
                         int32_t* ids_out, float* w_out) {
+  if (ctx->ep.world > 1) return ep_pipeline(ctx, L, router, h, n_tok, out, ids_out, w_out);
   const int E = L.n_expert, k = L.k, d = L.d, ff = L.ff;
   RC(ensure_work(ctx, n_tok, E, k, d, ff));
   Work& W = ctx->ws;
@@ -347,173 +714,13 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
     launch_route(W.logits, n_tok, E, k, L.norm_topk, L.weights_scale, W.ids, W.w, st);
     CKL();
   }
-  if (ctx->ep.world > 1) {
-    return fail(ctx, KC_ERR_STATE, "expert-parallel layer execution is not available in this build");
-  } else {
-    // 2. dispatch metadata (permute).
-    {
-      StageScope ss(ctx, KC_STAGE_DISPATCH);
-      RC(launch_dispatch(W.ids, W.w, n_tok, k, E, W.meta, st));
-      CKL();
-    }
-    // 3. activation records of every slot's input row (int8 path) and its f16
-    //    copy (tensor-core path).
-    const bool kq_in = is_k(L.t_gate), kq_dn = is_k(L.t_down);
-    const int A = n_tok * k;
-    const int max_small = std::min(E, A);
-    const bool mma_gu = mma_supported(L.t_gate, d, 2);
-    {
-      StageScope ss(ctx, KC_STAGE_QUANT_X);
-      launch_act_records(kq_in, h, nullptr, W.meta.slot_tok, A, d, W.xrec, A, nullptr, mma_gu ? W.x16 : nullptr, st);
-      CKL();
-    }
-    // 4. gate and up products -> g, u [slot, ff].
-    {
-      StageScope ss(ctx, KC_STAGE_GATE_UP_INT8);
-      DecodeArgs dg{};
-      dg.w[0] = L.gate;
-      dg.w[1] = L.up;
-      dg.n_mat = 2;
-      dg.expert_stride = L.mb_gate;
-      dg.expert_base = L.first_expert;
-      dg.rows = ff;
-      dg.cols = d;
-      dg.type = L.t_gate;
-      dg.list = W.meta.small_list;
-      dg.n_list = W.meta.n_lists;
-      dg.offsets = W.meta.offsets;
-      dg.rec = W.xrec;
-      dg.rec_slots = A;
-      dg.out[0] = W.g;
-      dg.out[1] = W.u;
-      dg.out_stride = ff;
-      dg.status = ctx->status;
-      RC(launch_decode(dg, max_small * 2 * ceil_div(ff, kTileRows), st));
-      CKL();
-    }
-    const int max_tt = ceil_div(A, 128) + std::min(E, A / 4);
-    if (mma_gu) {
-      StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
-      alignas(64) unsigned char tmap[128];
-      if (make_tmap_f16(tmap, W.x16, A, d) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
-      MmaArgs ma{};
-      ma.part = W.mma_part;
-      ma.tile_cnt = W.mma_cnt;
-      ma.w[0] = L.gate;
-      ma.w[1] = L.up;
-      ma.n_mat = 2;
-      ma.expert_stride = L.mb_gate;
-      ma.expert_base = L.first_expert;
-      ma.rows = ff;
-      ma.cols = d;
-      ma.type = L.t_gate;
-      ma.list = W.meta.large_list;
-      ma.n_list = W.meta.n_lists + 1;
-      ma.offsets = W.meta.offsets;
-      ma.tt_prefix = W.meta.large_tt;
-      ma.out[0] = W.g;
-      ma.out[1] = W.u;
-      ma.out_stride = ff;
-      ma.status = ctx->status;
-      RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(ff, 128), st));
-      CKL();
-    } else {
-      GroupedArgs g = grouped_base(ctx);
-      g.w0 = L.gate;
-      g.w1 = L.up;
-      g.expert_stride = L.mb_gate;
-      g.expert_base = L.first_expert;
-      g.rows = ff;
-      g.cols = d;
-      g.type = L.t_gate;
-      g.offsets = W.meta.offsets;
-      g.slot_src = W.meta.slot_tok;
-      g.af = h;
-      g.out = W.g;
-      g.out2 = W.u;
-      g.out_stride = ff;
-      g.list = W.meta.large_list;
-      g.n_list = W.meta.n_lists + 1;
-      StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
-      RC(launch_grouped_f32(g, true, std::min(E, A / 4), n_tok, st));
-      CKL();
-    }
-    // 5. SwiGLU of every slot -> act (f32) and its activation records.
-    {
-      StageScope ss(ctx, KC_STAGE_QUANT_ACT);
-      launch_act_records(kq_dn, W.g, W.u, nullptr, A, ff, W.arec, A, W.act, W.act16, st);
-      CKL();
-    }
-    // 6. down -> y [slot, d].
-    {
-      StageScope ss(ctx, KC_STAGE_DOWN_INT8);
-      DecodeArgs dd{};
-      dd.w[0] = L.down;
-      dd.n_mat = 1;
-      dd.expert_stride = L.mb_down;
-      dd.expert_base = L.first_expert;
-      dd.rows = d;
-      dd.cols = ff;
-      dd.type = L.t_down;
-      dd.list = W.meta.small_list;
-      dd.n_list = W.meta.n_lists;
-      dd.offsets = W.meta.offsets;
-      dd.rec = W.arec;
-      dd.rec_slots = A;
-      dd.out[0] = W.y;
-      dd.out_stride = d;
-      dd.status = ctx->status;
-      RC(launch_decode(dd, max_small * ceil_div(d, kTileRows), st));
-      CKL();
-    }
-    if (mma_supported(L.t_down, ff, 1) && ff % 256 == 0) {
-      StageScope ss(ctx, KC_STAGE_DOWN_F32);
-      alignas(64) unsigned char tmap[128];
-      if (make_tmap_f16(tmap, W.act16, A, ff) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (act16) failed");
-      MmaArgs ma{};
-      ma.part = W.mma_part;
-      ma.tile_cnt = W.mma_cnt;
-      ma.w[0] = L.down;
-      ma.n_mat = 1;
-      ma.expert_stride = L.mb_down;
-      ma.expert_base = L.first_expert;
-      ma.rows = d;
-      ma.cols = ff;
-      ma.type = L.t_down;
-      ma.list = W.meta.large_list;
-      ma.n_list = W.meta.n_lists + 1;
-      ma.offsets = W.meta.offsets;
-      ma.tt_prefix = W.meta.large_tt;
-      ma.out[0] = W.y;
-      ma.out_stride = d;
-      ma.status = ctx->status;
-      RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(d, 128), st));
-      CKL();
-    } else {
-      GroupedArgs dn = grouped_base(ctx);
-      dn.w0 = L.down;
-      dn.expert_stride = L.mb_down;
-      dn.expert_base = L.first_expert;
-      dn.rows = d;
-      dn.cols = ff;
-      dn.type = L.t_down;
-      dn.offsets = W.meta.offsets;
-      dn.slot_src = nullptr;
-      dn.af = W.act;
-      dn.out = W.y;
-      dn.out_stride = d;
-      dn.list = W.meta.large_list;
-      dn.n_list = W.meta.n_lists + 1;
-      StageScope ss(ctx, KC_STAGE_DOWN_F32);
-      RC(launch_grouped_f32(dn, false, std::min(E, A / 4), n_tok, st));
-      CKL();
-    }
-    // 7. combine (un-permute, ascending expert id).
-    {
-      StageScope ss(ctx, KC_STAGE_COMBINE);
-      launch_combine(W.y, W.meta.tok_slot, W.ids, W.w, n_tok, k, d, out, st);
-      CKL();
-    }
+  // 2-6. dispatch, records, gate/up, SwiGLU, down.
+  RC(experts_forward(ctx, W, L, E, L.first_expert, h, n_tok, W.ids, W.w, k));
+  // 7. combine (un-permute, ascending expert id).
+  {
+    StageScope ss(ctx, KC_STAGE_COMBINE);
+    launch_combine(W.y, W.meta.tok_slot, W.ids, W.w, n_tok, k, d, out, st);
+    CKL();
   }
   if (ids_out) CK(cudaMemcpyAsync(ids_out, W.ids, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
   if (w_out) CK(cudaMemcpyAsync(w_out, W.w, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
@@ -553,6 +760,7 @@ void kc_free(kc_ctx* ctx) {
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   ep_free(ctx->ep);
+  ep_free_bufs(ctx->epb);
   for (auto& [id, L] : ctx->layers) {
     cudaFree(L.gate);
     cudaFree(L.up);
@@ -566,6 +774,7 @@ void kc_free(kc_ctx* ctx) {
   }
   for (auto e : ctx->prof.pool) cudaEventDestroy(e);
   cudaFree(ctx->ws.arena);
+  cudaFree(ctx->ws_ep.arena);
   cudaFree(ctx->status);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -606,7 +815,7 @@ int kc_sync(kc_ctx* ctx) {
 }
 
 int64_t kc_device_bytes(const kc_ctx* ctx) {
-  return ctx ? ctx->weight_bytes + (int64_t)ctx->ws.bytes : 0;
+  return ctx ? ctx->weight_bytes + (int64_t)ctx->ws.bytes + (int64_t)ctx->ws_ep.bytes : 0;
 }
 
 int kc_upload_experts_range(kc_ctx* ctx, int layer, int n_expert, int first_expert, int n_local, int d, int ff,
@@ -762,10 +971,13 @@ int kc_moe_ffn(kc_ctx* ctx, int layer, const float* h, int n_tok, const float* r
   // ids / w land in the workspace; copied out below.
   RC(moe_pipeline(ctx, L, router, W.h_in, n_tok, W.out, nullptr, nullptr));
   if (n_tok > 0) CK(cudaMemcpyAsync(out, W.out, (size_t)n_tok * L.d * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  const bool ep = ctx->ep.world > 1;
   if (topk_ids && n_tok > 0)
-    CK(cudaMemcpyAsync(topk_ids, W.ids, (size_t)n_tok * L.k * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaMemcpyAsync(topk_ids, ep ? ctx->epb.ids_home : W.ids, (size_t)n_tok * L.k * 4, cudaMemcpyDeviceToHost,
+                       ctx->stream));
   if (topk_w && n_tok > 0)
-    CK(cudaMemcpyAsync(topk_w, W.w, (size_t)n_tok * L.k * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaMemcpyAsync(topk_w, ep ? ctx->epb.w_home : W.w, (size_t)n_tok * L.k * 4, cudaMemcpyDeviceToHost,
+                       ctx->stream));
   CK(cudaStreamSynchronize(ctx->stream));
   return check_status(ctx);
 }

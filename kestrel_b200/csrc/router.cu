@@ -280,10 +280,10 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
     const int fs = (c >= 1 && c <= 3) ? 1 : 0, fl = c >= 4 ? 1 : 0, ft = fl ? (c + 127) / 128 : 0;
     int4 v = make_int4(c, fs, fl, ft);
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int x = __shfl_up_sync(0xffffffffu, v.x, o), y = __shfl_up_sync(0xffffffffu, v.y, o);
-      const int z = __shfl_up_sync(0xffffffffu, v.z, o), t = __shfl_up_sync(0xffffffffu, v.w, o);
-      if (lane >= o) {
+    for (int sh = 1; sh < 32; sh <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, v.x, sh), y = __shfl_up_sync(0xffffffffu, v.y, sh);
+      const int z = __shfl_up_sync(0xffffffffu, v.z, sh), t = __shfl_up_sync(0xffffffffu, v.w, sh);
+      if (lane >= sh) {
         v.x += x;
         v.y += y;
         v.z += z;
@@ -295,10 +295,10 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
     if (warp == 0) {
       int4 u = wsum[lane];
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int x = __shfl_up_sync(0xffffffffu, u.x, o), y = __shfl_up_sync(0xffffffffu, u.y, o);
-        const int z = __shfl_up_sync(0xffffffffu, u.z, o), t = __shfl_up_sync(0xffffffffu, u.w, o);
-        if (lane >= o) {
+      for (int sh = 1; sh < 32; sh <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, u.x, sh), y = __shfl_up_sync(0xffffffffu, u.y, sh);
+        const int z = __shfl_up_sync(0xffffffffu, u.z, sh), t = __shfl_up_sync(0xffffffffu, u.w, sh);
+        if (lane >= sh) {
           u.x += x;
           u.y += y;
           u.z += z;

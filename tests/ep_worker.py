@@ -1,0 +1,83 @@
+"""One rank of the expert-parallel check (launched by tests/test_gpu_ep.py
+through torch.distributed.run, one process per GPU).
+
+Every rank builds the same seeded layer, uploads its contiguous block of
+experts and the full router, joins the NCCL group, and runs kc_moe_ffn on its
+own tokens. A second, single-GPU context on the same device holding all the
+experts runs the union of every rank's tokens (rank-major, the order the
+expert-parallel combine reproduces). Top-k ids and weights must be identical;
+layer outputs must be bit-identical when every expert gets at most 3 rows (the
+int8 path, exact on any grouping) and within the reference's tolerance
+otherwise (the tensor-core path splits K depending on the batch).
+"""
+import json
+import os
+import sys
+from datetime import timedelta
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(HERE))
+sys.path.insert(0, HERE)
+
+from gpu_util import bits, make_layer, tol_ok  # noqa: E402
+from kestrel_b200 import ep  # noqa: E402
+from kestrel_b200.cuda import Context  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dist.init_process_group("gloo", timeout=timedelta(seconds=120))
+    torch.cuda.set_device(rank)
+    E, k, d, ff = 16, 4, 512, 768
+    L = make_layer(E, k, d, ff, seed=11)
+    blk = ep.expert_block(E, world, rank)
+    ctx = Context(rank)
+    ep.join(ctx, rank, world)
+    sl = lambda t, a, rows, cols: ep.slice_experts(t, a, rows, cols, blk)
+    ctx.upload_experts(0, E, d, ff, L["t_gate"], sl(L["t_gate"], L["gate"], ff, d), L["t_gate"],
+                       sl(L["t_gate"], L["up"], ff, d), L["t_down"], sl(L["t_down"], L["down"], d, ff),
+                       first_expert=blk.first, n_local=blk.count)
+    ctx.upload_router(0, L["router"], k)
+    ref = Context(rank)
+    ref.upload_experts(0, E, d, ff, L["t_gate"], L["gate"], L["t_gate"], L["up"], L["t_down"], L["down"])
+    ref.upload_router(0, L["router"], k)
+
+    results = []
+    cases = [[1] * world, [3] + [0] * (world - 1), [16] * world, [64 - 8 * r for r in range(world)], [1] * world]
+    for ci, ns in enumerate(cases):
+        rng = np.random.default_rng(100 + ci)
+        h_all = rng.standard_normal((sum(ns), d)).astype(np.float32)
+        lo = sum(ns[:rank])
+        mine = h_all[lo:lo + ns[rank]]
+        out, ids, w = ctx.moe_ffn(0, mine)
+        r_out, all_ids, r_w = ref.moe_ffn(0, h_all)
+        r_out, r_ids, r_w = r_out[lo:lo + ns[rank]], all_ids[lo:lo + ns[rank]], r_w[lo:lo + ns[rank]]
+        max_rows = int(np.bincount(all_ids.reshape(-1), minlength=E).max()) if all_ids.size else 0
+        res = dict(case=ci, ns=ns, rank=rank, ids=bool(np.array_equal(ids, r_ids)),
+                   w=bool(np.array_equal(bits(w), bits(r_w))), max_rows=max_rows)
+        if max_rows <= 3:
+            res["out_bit_exact"] = bool(np.array_equal(bits(out), bits(r_out)))
+            res["ok"] = res["ids"] and res["w"] and res["out_bit_exact"]
+        else:
+            ok, err, scale = tol_ok(out, r_out)
+            res.update(out_tol=ok, err=err, scale=scale)
+            res["ok"] = res["ids"] and res["w"] and ok
+        results.append(res)
+    gathered = [None] * world
+    dist.all_gather_object(gathered, results)
+    ctx.close()
+    ref.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0:
+        flat = [r for rs in gathered for r in rs]
+        print(json.dumps(flat))
+        sys.exit(0 if all(r["ok"] for r in flat) else 1)
+
+
+if __name__ == "__main__":
+    main()
