@@ -17,8 +17,10 @@ weights from L2). Activations: f32 N(0, 1), a pool of distinct batches.
                 bounded sample of the same workload, all host threads
 
 --impl reference times the oracle alone (the reference's CPU arithmetic) on
-the same config. Multi-GPU (torchrun): each rank runs an independent replica
-of the layer stack on its own batch (weak scaling).
+the same config. Multi-GPU (torchrun, N ranks): expert parallelism -- rank r
+holds experts [r*E/N, (r+1)*E/N) of every layer and a copy of the router, routes
+its own B tokens, and exchanges token rows and result rows with NCCL inside
+each layer call (weak scaling: N*B tokens per step).
 """
 from __future__ import annotations
 
@@ -51,11 +53,15 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def algorithmic_bytes(ids: np.ndarray, B: int) -> dict:
+def algorithmic_bytes(ids: np.ndarray, B: int, block=None) -> dict:
     """Per call: distinct routed experts x bytes/expert + router + x in/out, and
-    the split of expert bytes between the int8 (<4 rows) and f32 paths."""
+    the split of expert bytes between the int8 (<4 rows) and f32 paths. ids are
+    the selections of every token the experts see; with an expert block only
+    that block's experts count (the weights this rank streams)."""
     d, ff = CFG["d"], CFG["ff"]
     cnt = np.bincount(ids.reshape(-1), minlength=CFG["E"])
+    if block is not None:
+        cnt = cnt[block.first:block.first + block.count]
     small = int(((cnt >= 1) & (cnt <= 3)).sum())
     large = int((cnt >= 4).sum())
     gate_up = 2 * ff * (d // 256) * 144
@@ -114,23 +120,28 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------
-def make_layers(ctx, torch, n_layers, seed=0):
+def make_layers(ctx, torch, n_layers, seed=0, block=None):
     """configs[1] weights on the GPU: N(0, 0.02) quantised to Q4_K / Q6_K by
-    kc_quantize_dev, uploaded with kc_upload_experts (device source)."""
+    kc_quantize_dev, uploaded with kc_upload_experts (device source). With an
+    expert block (expert parallelism) only that block is generated; the router
+    is the same on every rank."""
     from kestrel_b200 import ggml as G
     E, d, ff, k = CFG["E"], CFG["d"], CFG["ff"], CFG["k"]
-    g = torch.Generator(device="cuda").manual_seed(seed)
+    first, n_loc = (0, E) if block is None else (block.first, block.count)
+    g = torch.Generator(device="cuda").manual_seed(seed + first)
+    gr = torch.Generator(device="cuda").manual_seed(seed + 777)
     bufs = {n: torch.empty((rows, G.bytes_for(t, cols)), dtype=torch.uint8, device="cuda")
-            for n, t, rows, cols in (("gate", G.Q4_K, E * ff, d), ("up", G.Q4_K, E * ff, d),
-                                     ("down", G.Q6_K, E * d, ff))}
-    x = torch.empty((E * ff, d), dtype=torch.float32, device="cuda")
+            for n, t, rows, cols in (("gate", G.Q4_K, n_loc * ff, d), ("up", G.Q4_K, n_loc * ff, d),
+                                     ("down", G.Q6_K, n_loc * d, ff))}
+    x = torch.empty((n_loc * ff, d), dtype=torch.float32, device="cuda")
     for layer in range(n_layers):
         for n, t in (("gate", G.Q4_K), ("up", G.Q4_K), ("down", G.Q6_K)):
-            xv = x.view(E * d, ff) if n == "down" else x
+            xv = x.view(n_loc * d, ff) if n == "down" else x
             xv.normal_(0.0, 0.02, generator=g)
             ctx.quantize_dev(t, xv, bufs[n])
-        router = torch.empty((E, d), dtype=torch.float32, device="cuda").normal_(0.0, 0.02, generator=g)
-        ctx.upload_experts(layer, E, d, ff, G.Q4_K, bufs["gate"], G.Q4_K, bufs["up"], G.Q6_K, bufs["down"])
+        router = torch.empty((E, d), dtype=torch.float32, device="cuda").normal_(0.0, 0.02, generator=gr)
+        ctx.upload_experts(layer, E, d, ff, G.Q4_K, bufs["gate"], G.Q4_K, bufs["up"], G.Q6_K, bufs["down"],
+                           first_expert=first, n_local=n_loc)
         ctx.upload_router(layer, router, k)
         if layer == 0:
             host0 = {n: b.cpu().numpy() for n, b in bufs.items()}
@@ -245,13 +256,18 @@ def run_ours(args):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     ctx = Context(local)
+    block = None
+    if world > 1:
+        from kestrel_b200 import ep
+        block = ep.expert_block(CFG["E"], world, rank)
+        ep.join(ctx, rank, world)
     # A dedicated (non-default) stream shared by torch and the library, so the
     # CUDA events bracket the library's kernels.
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
     n_layers = args.layers
-    host0 = make_layers(ctx, torch, n_layers, seed=rank * 1000)
+    host0 = make_layers(ctx, torch, n_layers, seed=0, block=block)
     B = args.batch
     batches = sorted(set([B] + args.sweep))
     ctx.reserve(max(batches))
@@ -270,6 +286,14 @@ def run_ours(args):
         t = torch.tensor([v], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    def all_ids(ids_dev):
+        """Selections of every rank's tokens (what this rank's experts see)."""
+        if world == 1:
+            return ids_dev.cpu().numpy()
+        parts = [torch.empty_like(ids_dev) for _ in range(world)]
+        dist.all_gather(parts, ids_dev)
+        return torch.cat(parts).cpu().numpy()
 
     # Warm-up, then the timed region at the headline batch.
     timed_steps(torch, ctx, pool[B], outs[B], n_layers, B, args.warmup, stream)
@@ -294,7 +318,7 @@ def run_ours(args):
     byte_acc = {}
     for i in range(prof_steps):
         ctx.moe_ffn_dev(i % n_layers, pool[B][i % 16], outs[B][0], ids_dev, None, n_tok=B)
-        ab = algorithmic_bytes(ids_dev.cpu().numpy(), B)
+        ab = algorithmic_bytes(all_ids(ids_dev), B, block)
         for kk, v in ab.items():
             byte_acc[kk] = byte_acc.get(kk, 0) + v
     stages = ctx.profile_read()
@@ -302,7 +326,9 @@ def run_ours(args):
     stage_bytes = {"gate_up_int8": byte_acc["gate_up_int8"], "down_int8": byte_acc["down_int8"],
                    "gate_up_f32": byte_acc["gate_up_f32"], "down_f32": byte_acc["down_f32"],
                    "router_logits": byte_acc["router"]}
-    dom = max(stages, key=lambda s: stages[s][0])
+    # Dominant kernel stage among those that stream weights (the exchange and
+    # small metadata stages move no weight bytes).
+    dom = max((s for s in stages if s in stage_bytes and stages[s][1]), key=lambda s: stages[s][0])
     dom_ms, dom_calls = stages[dom]
     dom_bytes = stage_bytes.get(dom, 0)
     achieved = (dom_bytes / dom_calls) / (dom_ms / dom_calls / 1e3) / 1e9 if dom_ms > 0 and dom_calls else 0.0
@@ -325,7 +351,7 @@ def run_ours(args):
         tot = 0
         for i in range(4):
             ctx.moe_ffn_dev(i % n_layers, pool[b][i], outs[b][0], ids_b, None, n_tok=b)
-            tot += algorithmic_bytes(ids_b.cpu().numpy(), b)["total"]
+            tot += algorithmic_bytes(all_ids(ids_b), b, block)["total"]
         per_ms = ms_b / steps_b
         sweep[str(b)] = {"ms_per_step": per_ms, "tokens_per_s": world * b / (per_ms / 1e3),
                          "hbm_gbs": (tot / 4) / (per_ms / 1e3) / 1e9,
@@ -360,7 +386,8 @@ def run_ours(args):
             "config": {"workload": CFG["name"], "batch_tokens": B, "d_model": CFG["d"], "experts": CFG["E"],
                        "top_k": CFG["k"], "expert_ff": CFG["ff"], "quant": "Q4_K gate/up + Q6_K down",
                        "layers_rotated": n_layers, "l2": "inputs larger than L2 (48 distinct layers, 18.8 GB)",
-                       "parallelism": "replicas" if world > 1 else "single"},
+                       "parallelism": f"ep{world}" if world > 1 else "single",
+                       "experts_per_gpu": CFG["E"] // world},
             "layer_hbm": {"bytes_per_step": layer_bytes, "gbs": layer_gbs, "frac": layer_gbs / hbm_peak,
                           "peak": hbm_peak, "peak_kind": peak_kind},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -369,7 +396,10 @@ def run_ours(args):
             "sweep": sweep,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": B * d * 4,
                     "d2h_bytes_per_step": B * d * 4 + B * CFG["k"] * 8},
-            "gpu_launches": args.steps * 10,  # kernels per kc_moe_ffn_dev call
+            # this library's kernels per kc_moe_ffn_dev call: router logits, route, dispatch, 2 record
+            # kernels, int8 and tcgen05 gate/up, int8 and tcgen05 down, combine (+ the expert-parallel
+            # plan, pack, local ids, return plan and return pack with N > 1; NCCL's own not counted)
+            "gpu_launches": args.steps * (10 if world == 1 else 15),
             "clocks": clocks,
             "cpu_baseline": cpu,
         }

@@ -665,8 +665,10 @@ static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const f
     return fail(ctx, KC_ERR_STATE, "expert parallel: inconsistent exchange counts");
   RC(ep_grow_owner(ctx, (int)n_recv, (int)n_ret_send, k, d));
   // 3. rows and their selections to the owners.
-  RC(ep_rc(ctx, ep_alltoallv(S, B.sendbuf, so, sb, B.recvbuf, ro, rb, st)));
-  RC(ep_rc(ctx, ep_alltoallv(S, B.sendmeta, mso, msb, B.recvmeta, mro, mrb, st)));
+  {
+    const EpA2A parts[2] = {{B.sendbuf, so, sb, B.recvbuf, ro, rb}, {B.sendmeta, mso, msb, B.recvmeta, mro, mrb}};
+    RC(ep_rc(ctx, ep_alltoallv(S, parts, 2, st)));
+  }
   // 4. the local experts on every received row.
   if (n_recv > 0) {
     const int nr = (int)n_recv;
@@ -682,7 +684,10 @@ static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const f
     CKL();
   }
   // 5. result rows back to their tokens' ranks; combine in ascending expert id.
-  RC(ep_rc(ctx, ep_alltoallv(S, B.retsend, yso, ysb, B.retrecv, yro, yrb, st)));
+  {
+    const EpA2A parts[1] = {{B.retsend, yso, ysb, B.retrecv, yro, yrb}};
+    RC(ep_rc(ctx, ep_alltoallv(S, parts, 1, st)));
+  }
   if (n_tok > 0) {
     StageScope ss(ctx, KC_STAGE_COMBINE);
     launch_combine(B.retrecv, B.ret_pos, B.ids_home, B.w_home, n_tok, k, d, out, st);

@@ -322,33 +322,39 @@ int ep_exchange_counts(EpState& s, const int* send_dev, int* recv_dev, cudaStrea
   return KC_OK;
 }
 
-int ep_alltoallv(EpState& s, const void* send, const int64_t* send_off, const int64_t* send_bytes, void* recv,
-                 const int64_t* recv_off, const int64_t* recv_bytes, cudaStream_t st) {
+int ep_alltoallv(EpState& s, const EpA2A* parts, int n_parts, cudaStream_t st) {
   ncclComm_t comm = static_cast<ncclComm_t>(s.comm);
-  const char* sp = static_cast<const char*>(send);
-  char* rp = static_cast<char*>(recv);
+  const int me = s.rank;
+  for (int p = 0; p < n_parts; ++p)
+    if (parts[p].send_bytes[me] != parts[p].recv_bytes[me]) {
+      s.err = "all-to-all: own section sizes differ";
+      return KC_ERR_STATE;
+    }
   ncclResult_t r = ncclGroupStart();
-  for (int q = 0; q < s.world && r == ncclSuccess; ++q) {
-    if (q == s.rank) continue;
-    if (send_bytes[q] > 0) r = ncclSend(sp + send_off[q], (size_t)send_bytes[q], ncclInt8, q, comm, st);
-    if (r == ncclSuccess && recv_bytes[q] > 0)
-      r = ncclRecv(rp + recv_off[q], (size_t)recv_bytes[q], ncclInt8, q, comm, st);
+  for (int p = 0; p < n_parts && r == ncclSuccess; ++p) {
+    const EpA2A& a = parts[p];
+    const char* sp = static_cast<const char*>(a.send);
+    char* rp = static_cast<char*>(a.recv);
+    for (int q = 0; q < s.world && r == ncclSuccess; ++q) {
+      if (q == me) continue;
+      if (a.send_bytes[q] > 0) r = ncclSend(sp + a.send_off[q], (size_t)a.send_bytes[q], ncclInt8, q, comm, st);
+      if (r == ncclSuccess && a.recv_bytes[q] > 0)
+        r = ncclRecv(rp + a.recv_off[q], (size_t)a.recv_bytes[q], ncclInt8, q, comm, st);
+    }
   }
   const ncclResult_t r2 = ncclGroupEnd();
   if (r != ncclSuccess || r2 != ncclSuccess) {
     s.err = std::string("all-to-all: ") + ncclGetErrorString(r != ncclSuccess ? r : r2);
     return KC_ERR_NCCL;
   }
-  const int me = s.rank;
-  if (send_bytes[me] != recv_bytes[me]) {
-    s.err = "all-to-all: own section sizes differ";
-    return KC_ERR_STATE;
-  }
-  if (send_bytes[me] > 0 &&
-      cudaMemcpyAsync(rp + recv_off[me], sp + send_off[me], (size_t)send_bytes[me], cudaMemcpyDeviceToDevice, st) !=
-          cudaSuccess) {
-    s.err = "all-to-all: self copy failed";
-    return KC_ERR_CUDA;
+  for (int p = 0; p < n_parts; ++p) {
+    const EpA2A& a = parts[p];
+    if (a.send_bytes[me] > 0 &&
+        cudaMemcpyAsync(static_cast<char*>(a.recv) + a.recv_off[me], static_cast<const char*>(a.send) + a.send_off[me],
+                        (size_t)a.send_bytes[me], cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
+      s.err = "all-to-all: self copy failed";
+      return KC_ERR_CUDA;
+    }
   }
   return KC_OK;
 }

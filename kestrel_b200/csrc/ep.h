@@ -57,9 +57,18 @@ void launch_ep_ret_pack(const float* y, const int* tok_slot, const int* ret_send
 
 // Exchange two ints with every rank: recv[2r..2r+1] <- rank r's send[2*me..].
 int ep_exchange_counts(EpState& s, const int* send_dev, int* recv_dev, cudaStream_t st);
-// All-to-all with per-peer byte counts and offsets (host arrays of `world`
-// entries); the rank's own section is copied on the device.
-int ep_alltoallv(EpState& s, const void* send, const int64_t* send_off, const int64_t* send_bytes, void* recv,
-                 const int64_t* recv_off, const int64_t* recv_bytes, cudaStream_t st);
+// One buffer pair of an all-to-all: per-peer byte offsets and counts (host
+// arrays of `world` entries).
+struct EpA2A {
+  const void* send;
+  const int64_t* send_off;
+  const int64_t* send_bytes;
+  void* recv;
+  const int64_t* recv_off;
+  const int64_t* recv_bytes;
+};
+// All-to-all of n_parts buffer pairs in one NCCL group; the rank's own
+// sections are copied on the device.
+int ep_alltoallv(EpState& s, const EpA2A* parts, int n_parts, cudaStream_t st);
 
 }  // namespace kc
