@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -339,6 +340,14 @@ namespace kc {
 // Message returned by kc_last_error(NULL) on this thread (entry points
 // without a context).
 void set_global_error(const char* msg) { g_init_err = msg ? msg : ""; }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("KESTREL_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 int num_sms() {
   static int dev = -1, sms = 0;

@@ -46,6 +46,7 @@ __global__ void q8k_records_kernel(const float* __restrict__ x, const float* __r
                                    const int* __restrict__ slot_src, int64_t n_slots, int64_t cols,
                                    uint8_t* __restrict__ rec, int64_t rec_slots, float* __restrict__ f32out,
                                    __half* __restrict__ f16out) {
+  pdl_enter();
   const int64_t nb = cols / 256;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -110,6 +111,7 @@ __global__ void q8_records_kernel(const float* __restrict__ x, const float* __re
                                   const int* __restrict__ slot_src, int64_t n_slots, int64_t cols,
                                   uint8_t* __restrict__ rec, int64_t rec_slots, float* __restrict__ f32out,
                                   __half* __restrict__ f16out) {
+  pdl_enter();
   const int64_t nb = cols / 32;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -141,11 +143,11 @@ void launch_act_records(bool kquant, const float* x, const float* u, const int* 
   if (warps <= 0) return;
   const int grid = ceil_div(warps, 8);
   if (kquant) {
-    if (u) q8k_records_kernel<true><<<grid, 256, 0, st>>>(x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
-    else q8k_records_kernel<false><<<grid, 256, 0, st>>>(x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
+    if (u) launch_k(q8k_records_kernel<true>, grid, 256, 0, st, x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
+    else launch_k(q8k_records_kernel<false>, grid, 256, 0, st, x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
   } else {
-    if (u) q8_records_kernel<true><<<grid, 256, 0, st>>>(x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
-    else q8_records_kernel<false><<<grid, 256, 0, st>>>(x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
+    if (u) launch_k(q8_records_kernel<true>, grid, 256, 0, st, x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
+    else launch_k(q8_records_kernel<false>, grid, 256, 0, st, x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
   }
 }
 
@@ -468,6 +470,7 @@ __device__ __forceinline__ void run_unit(const DecodeArgs& a, const DecodeGeom& 
 
 template <int T>
 __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, DecodeGeom g, int n_stages) {
+  pdl_enter();
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[DMAX_STAGES], empty[DMAX_STAGES];
   __shared__ UnitMeta meta[DMETA];
@@ -596,7 +599,7 @@ static int launch_decode_t(const DecodeArgs& a, const DecodeGeom& g, int max_uni
     attr = true;
   }
   const int grid = std::min(num_sms(), std::max(1, max_units));
-  decode_kernel<T><<<grid, DTHREADS, smem, st>>>(a, g, n_stages);
+  launch_k(decode_kernel<T>, grid, DTHREADS, smem, st, a, g, n_stages);
   return KC_OK;
 }
 

@@ -103,6 +103,7 @@ __device__ __forceinline__ void block_scan(const int (&v)[N], int (&ex)[N], int 
 __global__ void __launch_bounds__(EP_THREADS) ep_plan_kernel(const int* __restrict__ ids, int n_tok, int k, int G,
                                                               int epr, int T, int* __restrict__ send_tok,
                                                               int* __restrict__ ret_pos, int* __restrict__ xch_out) {
+  pdl_enter();
   __shared__ int sh[32 * 2 * kEpMaxWorld];
   __shared__ int base_f[kEpMaxWorld], base_c[kEpMaxWorld], off_c[kEpMaxWorld];
   const int tid = threadIdx.x;
@@ -191,7 +192,7 @@ __global__ void __launch_bounds__(EP_THREADS) ep_plan_kernel(const int* __restri
 
 void launch_ep_plan(const int* ids, int n_tok, int k, int world, int epr, int T, int* send_tok, int* ret_pos,
                     int* xch_out, cudaStream_t st) {
-  ep_plan_kernel<<<1, EP_THREADS, 0, st>>>(ids, n_tok, k, world, epr, T, send_tok, ret_pos, xch_out);
+  launch_k(ep_plan_kernel, 1, EP_THREADS, 0, st, ids, n_tok, k, world, epr, T, send_tok, ret_pos, xch_out);
 }
 
 // One warp per (destination, row): rows r's section starts at the prefix of
@@ -199,6 +200,7 @@ void launch_ep_plan(const int* ids, int n_tok, int k, int world, int epr, int T,
 __global__ void ep_pack_kernel(const float* __restrict__ h, const int* __restrict__ ids, const float* __restrict__ w,
                                const int* __restrict__ send_tok, const int* __restrict__ xch_out, int G, int T,
                                int k, int d, float* __restrict__ sendbuf, int32_t* __restrict__ sendmeta) {
+  pdl_enter();
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
   const int r = (int)(gw / T), i = (int)(gw % T);
@@ -220,12 +222,13 @@ void launch_ep_pack(const float* h, const int* ids, const float* w, const int* s
                     int world, int T, int k, int d, float* sendbuf, int32_t* sendmeta, cudaStream_t st) {
   const int64_t warps = (int64_t)world * T;
   if (warps <= 0) return;
-  ep_pack_kernel<<<ceil_div(warps * 32, 256), 256, 0, st>>>(h, ids, w, send_tok, xch_out, world, T, k, d, sendbuf,
-                                                            sendmeta);
+  launch_k(ep_pack_kernel, ceil_div(warps * 32, 256), 256, 0, st, h, ids, w, send_tok, xch_out, world, T, k, d,
+           sendbuf, sendmeta);
 }
 
 __global__ void ep_local_ids_kernel(const int32_t* __restrict__ meta, int n_recv, int k, int first, int n_local,
                                     int* __restrict__ ids_loc, float* __restrict__ w_loc) {
+  pdl_enter();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)n_recv * k) return;
   const int64_t row = i / k, j = i % k;
@@ -238,11 +241,12 @@ void launch_ep_local_ids(const int32_t* recvmeta, int n_recv, int k, int first, 
                          float* w_loc, cudaStream_t st) {
   const int64_t n = (int64_t)n_recv * k;
   if (n <= 0) return;
-  ep_local_ids_kernel<<<ceil_div(n, 256), 256, 0, st>>>(recvmeta, n_recv, k, first, n_local, ids_loc, w_loc);
+  launch_k(ep_local_ids_kernel, ceil_div(n, 256), 256, 0, st, recvmeta, n_recv, k, first, n_local, ids_loc, w_loc);
 }
 
 __global__ void __launch_bounds__(EP_THREADS) ep_ret_plan_kernel(const int* __restrict__ ids_loc, int n_recv, int k,
                                                                   int* __restrict__ pos) {
+  pdl_enter();
   __shared__ int sh[32];
   __shared__ int base;
   if (threadIdx.x == 0) base = 0;
@@ -275,13 +279,14 @@ __global__ void __launch_bounds__(EP_THREADS) ep_ret_plan_kernel(const int* __re
 
 void launch_ep_ret_plan(const int* ids_loc, int n_recv, int k, int* ret_send_pos, cudaStream_t st) {
   if (n_recv <= 0) return;
-  ep_ret_plan_kernel<<<1, EP_THREADS, 0, st>>>(ids_loc, n_recv, k, ret_send_pos);
+  launch_k(ep_ret_plan_kernel, 1, EP_THREADS, 0, st, ids_loc, n_recv, k, ret_send_pos);
 }
 
 // One warp per (row, selection).
 __global__ void ep_ret_pack_kernel(const float* __restrict__ y, const int* __restrict__ tok_slot,
                                    const int* __restrict__ pos, int n_recv, int k, int d, int cap,
                                    float* __restrict__ out) {
+  pdl_enter();
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
   if (gw >= (int64_t)n_recv * k) return;
@@ -296,8 +301,8 @@ void launch_ep_ret_pack(const float* y, const int* tok_slot, const int* ret_send
                         int cap, float* retsend, cudaStream_t st) {
   const int64_t warps = (int64_t)n_recv * k;
   if (warps <= 0) return;
-  ep_ret_pack_kernel<<<ceil_div(warps * 32, 256), 256, 0, st>>>(y, tok_slot, ret_send_pos, n_recv, k, d, cap,
-                                                                retsend);
+  launch_k(ep_ret_pack_kernel, ceil_div(warps * 32, 256), 256, 0, st, y, tok_slot, ret_send_pos, n_recv, k, d,
+           cap, retsend);
 }
 
 // ---- NCCL steps ---------------------------------------------------------------

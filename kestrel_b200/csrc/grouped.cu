@@ -69,6 +69,7 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* __restrict__ mat, i
 
 template <int T, bool PAIR>
 __global__ void __launch_bounds__(F_THREADS) grouped_f32_kernel(GroupedArgs a) {
+  pdl_enter();
   __shared__ float Wg[F_ROWS][F_K + 1];
   __shared__ float Wu[PAIR ? F_ROWS : 1][F_K + 1];
   __shared__ float X[F_TOK][F_K + 1];
@@ -142,7 +143,7 @@ __global__ void __launch_bounds__(F_THREADS) grouped_f32_kernel(GroupedArgs a) {
 template <int T, bool PAIR>
 static int launch_f32_t(const GroupedArgs& a, int max_experts, int max_rows, cudaStream_t st) {
   dim3 grid(ceil_div(a.rows, F_ROWS), max_experts, ceil_div(max_rows, F_TOK));
-  grouped_f32_kernel<T, PAIR><<<grid, F_THREADS, 0, st>>>(a);
+  launch_k(grouped_f32_kernel<T, PAIR>, grid, F_THREADS, 0, st, a);
   return KC_OK;
 }
 

@@ -245,6 +245,7 @@ __device__ __forceinline__ int split_count(const MmaArgs& a, int total, int nsb)
 template <int T, int NMAT>
 __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs a,
                                                                      const __grid_constant__ CUtensorMap tmap_b) {
+  pdl_enter();
   extern __shared__ uint8_t msm_raw[];
   __shared__ __align__(8) uint64_t raw_full[M_RAWS], raw_empty[M_RAWS], op_full[M_OPS], op_empty[M_OPS];
   __shared__ __align__(8) uint64_t acc_full, acc_empty;
@@ -524,7 +525,8 @@ static int launch_t(const MmaArgs& a, const void* tmap, int max_tiles, cudaStrea
   // With a split-K workspace every SM gets a CTA (the kernel splits K when the
   // batch has few tiles); otherwise one CTA per tile at most.
   const int grid = a.part ? num_sms() : std::max(1, std::min(num_sms(), max_tiles));
-  mma_grouped_kernel<T, NMAT><<<grid, M_THREADS, L.total, st>>>(a, *reinterpret_cast<const CUtensorMap*>(tmap));
+  launch_k(mma_grouped_kernel<T, NMAT>, grid, M_THREADS, (size_t)L.total, st, a,
+           *reinterpret_cast<const CUtensorMap*>(tmap));
   return KC_OK;
 }
 

@@ -42,6 +42,7 @@ template <bool GEMM>
 __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* __restrict__ w, int64_t ws, int E,
                                                                    int d, const float* __restrict__ h, int n_tok,
                                                                    float* __restrict__ logits, int* status) {
+  pdl_enter();
   extern __shared__ __align__(128) float rsm[];  // [2][RL_E + RL_T][RL_ROW]
   __shared__ __align__(8) uint64_t full[2];
   const int tid = threadIdx.x, j = tid & 7, grp = tid >> 3;
@@ -138,9 +139,9 @@ void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int 
   // quant::matmul's dispatch (quant.rs:241): the GEMM path needs >= 4 rows and
   // d % 8 == 0; otherwise quant::dot per output.
   if (n_tok >= 4 && d % 8 == 0)
-    router_logits_kernel<true><<<grid, RL_THREADS, smem, st>>>(w, row_stride_floats, E, d, h, n_tok, logits, status);
+    launch_k(router_logits_kernel<true>, grid, RL_THREADS, smem, st, w, row_stride_floats, E, d, h, n_tok, logits, status);
   else
-    router_logits_kernel<false><<<grid, RL_THREADS, smem, st>>>(w, row_stride_floats, E, d, h, n_tok, logits, status);
+    launch_k(router_logits_kernel<false>, grid, RL_THREADS, smem, st, w, row_stride_floats, E, d, h, n_tok, logits, status);
 }
 
 // ---------------------------------------------------------------------------
@@ -154,6 +155,7 @@ constexpr int RT_MAXK = 64;
 __global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __restrict__ logits, int n_tok, int E,
                                                                int k, int norm_topk, float weights_scale,
                                                                int* __restrict__ ids, float* __restrict__ wout) {
+  pdl_enter();
   extern __shared__ float sp[];  // [RT_WARPS][E] probabilities, then [RT_WARPS][RT_MAXK] selections
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int s = blockIdx.x * RT_WARPS + warp;
@@ -236,8 +238,8 @@ void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, f
                   float* w, cudaStream_t st) {
   if (n_tok <= 0) return;
   size_t smem = (size_t)RT_WARPS * (E + 2 * RT_MAXK) * sizeof(float);
-  route_kernel<<<ceil_div(n_tok, RT_WARPS), RT_WARPS * 32, smem, st>>>(logits, n_tok, E, k, norm_topk,
-                                                                       weights_scale, ids, w);
+  launch_k(route_kernel, ceil_div(n_tok, RT_WARPS), RT_WARPS * 32, smem, st, logits, n_tok, E, k, norm_topk,
+           weights_scale, ids, w);
 }
 
 // ---------------------------------------------------------------------------
@@ -252,6 +254,7 @@ constexpr int DP_THREADS = 1024;
 __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restrict__ ids,
                                                                const float* __restrict__ w, int n_tok, int k, int E,
                                                                DispatchOut o) {
+  pdl_enter();
   extern __shared__ uint32_t dsm[];
   uint32_t* mask = dsm;                                // [32][E]
   int* pref = reinterpret_cast<int*>(dsm + 32 * E);    // [32][E]
@@ -374,12 +377,13 @@ int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, con
     attr_set = true;
   }
   if (smem > 200 * 1024 || E > DP_THREADS) return KC_ERR_SHAPE;
-  dispatch_kernel<<<1, DP_THREADS, smem, st>>>(ids, w, n_tok, k, E, o);
+  launch_k(dispatch_kernel, 1, DP_THREADS, smem, st, ids, w, n_tok, k, E, o);
   return KC_OK;
 }
 
 // One group (expert 0) holding rows 0..n-1: the metadata of a dense product.
 __global__ void dense_meta_kernel(int n, DispatchOut o) {
+  pdl_enter();
   o.counts[0] = n;
   o.offsets[0] = 0;
   o.offsets[1] = n;
@@ -391,7 +395,7 @@ __global__ void dense_meta_kernel(int n, DispatchOut o) {
   o.large_tt[1] = n >= 4 ? (n + 127) / 128 : 0;
 }
 
-void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st) { dense_meta_kernel<<<1, 1, 0, st>>>(n, o); }
+void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st) { launch_k(dense_meta_kernel, 1, 1, 0, st, n, o); }
 
 // ---------------------------------------------------------------------------
 // Combine (transformer.rs:566-570): out[s] = sum over the token's experts in
@@ -400,6 +404,7 @@ void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st) { dense_met
 __global__ void combine_kernel(const float* __restrict__ y, const int* __restrict__ tok_slot,
                                const int* __restrict__ ids, const float* __restrict__ w, int k, int d,
                                float* __restrict__ out) {
+  pdl_enter();
   __shared__ int ea[64], ss[64];
   __shared__ float sw[64];
   const int s = blockIdx.x;
@@ -439,7 +444,7 @@ __global__ void combine_kernel(const float* __restrict__ y, const int* __restric
 void launch_combine(const float* y, const int* tok_slot, const int* ids, const float* w, int n_tok, int k, int d,
                     float* out, cudaStream_t st) {
   if (n_tok <= 0) return;
-  combine_kernel<<<n_tok, 256, 0, st>>>(y, tok_slot, ids, w, k, d, out);
+  launch_k(combine_kernel, n_tok, 256, 0, st, y, tok_slot, ids, w, k, d, out);
 }
 
 }  // namespace kc
