@@ -332,6 +332,15 @@ def run_ours(args):
     dom_ms, dom_calls = stages[dom]
     dom_bytes = stage_bytes.get(dom, 0)
     achieved = (dom_bytes / dom_calls) / (dom_ms / dom_calls / 1e3) / 1e9 if dom_ms > 0 and dom_calls else 0.0
+    # DRAM traffic of the dominant kernel per launch: ncu's dram read+write of the
+    # same kernel on the profile_layer B=16 case, as a ratio to that launch's
+    # algorithmic bytes (profiles/decode_kernel_c1_b16.md), scaled to this
+    # launch's algorithmic bytes. Traffic grows with the experts served.
+    traffic_ratio = {"gate_up_int8": 1.053, "down_int8": 1.035}
+    traffic = (dom_bytes / dom_calls) * traffic_ratio[dom] if dom in traffic_ratio and dom_calls else None
+    traffic_src = ("ncu dram read+write / algorithmic bytes of this kernel on the B=16 profile case "
+                   "(profiles/decode_kernel_c1_b16.md), times this launch's algorithmic bytes"
+                   if traffic is not None else None)
     layer_bytes = byte_acc["total"] / prof_steps
     layer_gbs = layer_bytes / (ms_step / 1e3) / 1e9
     stage_report = {s: {"ms_per_call": (v[0] / v[1]) if v[1] else 0.0,
@@ -391,7 +400,8 @@ def run_ours(args):
             "layer_hbm": {"bytes_per_step": layer_bytes, "gbs": layer_gbs, "frac": layer_gbs / hbm_peak,
                           "peak": hbm_peak, "peak_kind": peak_kind},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "traffic": None, "peak_kind": peak_kind},
+                         "frac": achieved / hbm_peak, "traffic": traffic, "traffic_source": traffic_src,
+                         "peak_kind": peak_kind},
             "stages": stage_report,
             "sweep": sweep,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": B * d * 4,
