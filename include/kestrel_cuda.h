@@ -112,6 +112,17 @@ KC_API int kc_upload_router(kc_ctx* ctx, int layer, const float* router_w, int n
 KC_API int kc_upload_dense(kc_ctx* ctx, int tensor_id, int t, const void* w, int64_t rows, int64_t cols,
                     int src_on_device);
 
+/* Shared expert of layer `layer` (qwen2moe: ffn_{gate,up,down}_shexp.weight,
+   read at crates/kestrel-engine/src/transformer.rs:188-191): gate / up
+   [ff_shared, d], down [d, ff_shared], and the optional F32 gate vector
+   ffn_gate_inp_shexp.weight [d] (NULL: gate 1). kc_moe_ffn then adds, after
+   the routed experts, out[s] += sigmoid(gate_inp . h[s]) *
+   down(SwiGLU(gate h[s], up h[s])) as Transformer::moe_ffn does
+   (transformer.rs:571-587). d % 256 == 0, ff_shared % 32 == 0. */
+KC_API int kc_upload_shared_expert(kc_ctx* ctx, int layer, int ff_shared, int d, int t_gate, const void* gate,
+                                   int t_up, const void* up, int t_down, const void* down, const float* gate_inp,
+                                   int src_on_device);
+
 /* ---- hot path ----------------------------------------------------------- */
 
 /* Transformer::moe_ffn for `layer`: h [n_tok, d] f32 -> out [n_tok, d] f32.

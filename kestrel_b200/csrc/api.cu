@@ -37,6 +37,16 @@ struct Layer {
   float* router = nullptr;
   int k = 0, norm_topk = 1;
   float weights_scale = 0.f;
+  // Shared expert (qwen2moe): dense gate/up [sh_ff, d], down [d, sh_ff],
+  // optional F32 gate vector [d].
+  bool has_shared = false;
+  int sh_ff = 0;
+  struct Mat {
+    int t = 0;
+    int64_t rows = 0, cols = 0;
+    uint8_t* w = nullptr;
+  } sh_gate, sh_up, sh_down;
+  float* sh_inp = nullptr;
 };
 
 struct Dense {
@@ -535,6 +545,124 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   return KC_OK;
 }
 
+// quant::matmul of an uploaded dense matrix D on device rows x [n, cols] ->
+// out [n, rows] (quant.rs:229-339 dispatch: F32 -> router kernel order, n < 4
+// -> int8 decode, n >= 4 -> tcgen05, else CUDA-core f32). Uses the workspace's
+// records, f16 copy and dispatch metadata, which must already hold n rows of
+// D.cols values (it is grown here only if it does not).
+static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, float* out) {
+  if (n == 0) return KC_OK;
+  cudaStream_t st = ctx->stream;
+  if (D.t == T_F32) {
+    launch_router_logits(reinterpret_cast<const float*>(D.w), D.rs / 4, (int)D.rows, (int)D.cols, x, n, out, ctx->status,
+                         st);
+    CKL();
+    return KC_OK;
+  }
+  RC(ensure_work(ctx, n, 1, 1, (int)std::min<int64_t>(D.cols, 1 << 30), 256));
+  Work& W = ctx->ws;
+  launch_dense_meta(n, W.meta, st);
+  CKL();
+  GroupedArgs a = grouped_base(ctx);
+  a.w0 = D.w;
+  a.expert_stride = 0;
+  a.expert_base = 0;
+  a.rows = (int)D.rows;
+  a.cols = (int)D.cols;
+  a.type = D.t;
+  a.offsets = W.meta.offsets;
+  a.slot_src = nullptr;
+  a.af = x;
+  a.out = out;
+  a.out_stride = D.rows;
+  if (n < 4) {
+    const bool kq = is_k(D.t);
+    launch_act_records(kq, x, nullptr, nullptr, n, D.cols, W.xrec, n, nullptr, nullptr, st);
+    CKL();
+    DecodeArgs dv{};
+    dv.w[0] = D.w;
+    dv.n_mat = 1;
+    dv.rows = (int)D.rows;
+    dv.cols = (int)D.cols;
+    dv.type = D.t;
+    dv.list = W.meta.small_list;
+    dv.n_list = W.meta.n_lists;
+    dv.offsets = W.meta.offsets;
+    dv.rec = W.xrec;
+    dv.rec_slots = n;
+    dv.out[0] = out;
+    dv.out_stride = D.rows;
+    dv.status = ctx->status;
+    RC(launch_decode(dv, ceil_div(D.rows, kTileRows), st));
+  } else if (mma_supported(D.t, D.cols, 1)) {
+    launch_act_records(is_k(D.t), x, nullptr, nullptr, n, D.cols, nullptr, n, nullptr, W.x16, st);
+    CKL();
+    alignas(64) unsigned char tmap[128];
+    if (make_tmap_f16(tmap, W.x16, n, D.cols) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
+    MmaArgs ma{};
+    ma.part = W.mma_part;
+    ma.tile_cnt = W.mma_cnt;
+    ma.w[0] = D.w;
+    ma.n_mat = 1;
+    ma.rows = (int)D.rows;
+    ma.cols = (int)D.cols;
+    ma.type = D.t;
+    ma.list = W.meta.large_list;
+    ma.n_list = W.meta.n_lists + 1;
+    ma.offsets = W.meta.offsets;
+    ma.tt_prefix = W.meta.large_tt;
+    ma.out[0] = out;
+    ma.out_stride = D.rows;
+    ma.status = ctx->status;
+    RC(launch_mma_grouped(ma, tmap, ceil_div(n, 128) * ceil_div(D.rows, 128), st));
+  } else {
+    a.list = W.meta.large_list;
+    a.n_list = W.meta.n_lists + 1;
+    RC(launch_grouped_f32(a, false, 1, n, st));
+  }
+  CKL();
+  return KC_OK;
+}
+
+static Dense as_dense(const Layer::Mat& m) {
+  Dense D;
+  D.t = m.t;
+  D.rows = m.rows;
+  D.cols = m.cols;
+  D.rs = round16(m.cols * 4);
+  D.w = m.w;
+  return D;
+}
+
+// Workspace columns the layer's products need (routed experts and shared
+// expert): D >= d and the shared ff, F >= ff and the shared ff.
+static int layer_work_d(const Layer& L) { return std::max(L.d, L.has_shared ? L.sh_ff : 0); }
+static int layer_work_f(const Layer& L) { return std::max(L.ff, L.has_shared ? L.sh_ff : 0); }
+
+// The shared expert's contribution (transformer.rs:571-587): g = gate h,
+// u = up h, g = g / (1 + exp(-g)) * u, y = down g, then
+// out[s] += sigmoid(gate_inp . h[s]) * y[s] (gate 1 without gate_inp). The
+// matmuls follow quant::matmul's dispatch on the token count, like
+// Transformer::mm. Runs after the routed experts' combine.
+static int shared_forward(kc_ctx* ctx, const Layer& L, const float* h, int n_tok, float* out) {
+  if (!L.has_shared || n_tok == 0) return KC_OK;
+  Work& W = ctx->ws;
+  cudaStream_t st = ctx->stream;
+  const int d = L.d, sf = L.sh_ff;
+  RC(dense_forward(ctx, as_dense(L.sh_gate), h, n_tok, W.g));
+  RC(dense_forward(ctx, as_dense(L.sh_up), h, n_tok, W.u));
+  launch_act_records(false, W.g, W.u, nullptr, n_tok, sf, nullptr, n_tok, W.act, nullptr, st);
+  CKL();
+  RC(dense_forward(ctx, as_dense(L.sh_down), W.act, n_tok, W.y));
+  if (L.sh_inp) {
+    launch_router_logits(L.sh_inp, d, 1, d, h, n_tok, W.logits, ctx->status, st, /*force_dot=*/true);
+    CKL();
+  }
+  launch_shared_add(W.y, L.sh_inp ? W.logits : nullptr, n_tok, d, out, st);
+  CKL();
+  return KC_OK;
+}
+
 // ---- expert parallelism --------------------------------------------------
 template <typename P>
 static int regrow(P*& p, size_t bytes) {
@@ -619,7 +747,7 @@ static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const f
   if (d % 4) return fail(ctx, KC_ERR_SHAPE, "expert parallel: d %% 4 != 0");
   const int epr = E / G;
   const int T = std::max(n_tok, 1);
-  RC(ensure_work(ctx, T, E, k, d, ff));
+  RC(ensure_work(ctx, T, E, k, layer_work_d(L), layer_work_f(L)));
   RC(ep_grow_home(ctx, T, k, d));
   EpBufs& B = ctx->epb;
   cudaStream_t st = ctx->stream;
@@ -706,14 +834,16 @@ static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const f
     CK(cudaMemcpyAsync(ids_out, B.ids_home, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
   if (w_out && n_tok > 0)
     CK(cudaMemcpyAsync(w_out, B.w_home, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
+  // The shared expert is dense and replicated: every rank adds it for its own tokens.
+  RC(shared_forward(ctx, L, h, n_tok, out));
   return KC_OK;
 }
 
 static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const float* h, int n_tok, float* out,
                         int32_t* ids_out, float* w_out) {
   if (ctx->ep.world > 1) return ep_pipeline(ctx, L, router, h, n_tok, out, ids_out, w_out);
-  const int E = L.n_expert, k = L.k, d = L.d, ff = L.ff;
-  RC(ensure_work(ctx, n_tok, E, k, d, ff));
+  const int E = L.n_expert, k = L.k, d = L.d;
+  RC(ensure_work(ctx, n_tok, E, k, layer_work_d(L), layer_work_f(L)));
   Work& W = ctx->ws;
   cudaStream_t st = ctx->stream;
   if (n_tok == 0) return KC_OK;
@@ -738,6 +868,8 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
   }
   if (ids_out) CK(cudaMemcpyAsync(ids_out, W.ids, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
   if (w_out) CK(cudaMemcpyAsync(w_out, W.w, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
+  // 8. shared expert (qwen2moe), after the routed experts.
+  RC(shared_forward(ctx, L, h, n_tok, out));
   return KC_OK;
 }
 
@@ -780,6 +912,10 @@ void kc_free(kc_ctx* ctx) {
     cudaFree(L.up);
     cudaFree(L.down);
     cudaFree(L.router);
+    cudaFree(L.sh_gate.w);
+    cudaFree(L.sh_up.w);
+    cudaFree(L.sh_down.w);
+    cudaFree(L.sh_inp);
   }
   for (auto& [id, D] : ctx->dense) cudaFree(D.w);
   for (auto& r : ctx->prof.recs) {
@@ -935,6 +1071,54 @@ int kc_upload_dense(kc_ctx* ctx, int tensor_id, int t, const void* w, int64_t ro
   return KC_OK;
 }
 
+int kc_upload_shared_expert(kc_ctx* ctx, int layer, int ff_shared, int d, int t_gate, const void* gate, int t_up,
+                            const void* up, int t_down, const void* down, const float* gate_inp,
+                            int src_on_device) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!gate || !up || !down || ff_shared <= 0 || d <= 0)
+    return fail(ctx, KC_ERR_ARG, "kc_upload_shared_expert: bad arguments");
+  for (int t : {t_gate, t_up, t_down})
+    if (!type_ok(t)) return fail(ctx, KC_ERR_TYPE, "kc_upload_shared_expert: type %d has no kernel", t);
+  if (d % block_elems(t_gate) || d % block_elems(t_up) || ff_shared % block_elems(t_down) || d % 256 ||
+      ff_shared % 32)
+    return fail(ctx, KC_ERR_SHAPE, "kc_upload_shared_expert: d=%d / ff=%d do not fit the block sizes", d,
+                ff_shared);
+  cudaSetDevice(ctx->device);
+  Layer& L = ctx->layers[layer];
+  if (L.has_experts && L.d != d) return fail(ctx, KC_ERR_SHAPE, "kc_upload_shared_expert: d differs from the layer's");
+  const struct {
+    Layer::Mat* m;
+    int t;
+    const void* src;
+    int64_t rows, cols;
+  } mats[3] = {{&L.sh_gate, t_gate, gate, ff_shared, d}, {&L.sh_up, t_up, up, ff_shared, d},
+               {&L.sh_down, t_down, down, d, ff_shared}};
+  for (const auto& x : mats) {
+    cudaFree(x.m->w);
+    x.m->w = nullptr;
+    x.m->t = x.t;
+    x.m->rows = x.rows;
+    x.m->cols = x.cols;
+    const int64_t bytes = dev_matrix_bytes(x.t, x.rows, x.cols);
+    CK(cudaMalloc(&x.m->w, bytes));
+    ctx->weight_bytes += bytes;
+    RC(upload_matrix(ctx, x.t, x.src, 1, x.rows, x.cols, x.m->w, src_on_device != 0));
+  }
+  cudaFree(L.sh_inp);
+  L.sh_inp = nullptr;
+  if (gate_inp) {
+    CK(cudaMalloc(&L.sh_inp, (size_t)d * 4));
+    CK(cudaMemcpyAsync(L.sh_inp, gate_inp, (size_t)d * 4, src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                       ctx->stream));
+  }
+  L.sh_ff = ff_shared;
+  L.d = d;
+  L.has_shared = true;
+  CK(cudaStreamSynchronize(ctx->stream));
+  return KC_OK;
+}
+
 int kc_moe_ffn_dev(kc_ctx* ctx, int layer, const float* h, int n_tok, float* out, int32_t* topk_ids,
                    float* topk_w) {
   if (!ctx) return KC_ERR_ARG;
@@ -973,7 +1157,7 @@ int kc_moe_ffn(kc_ctx* ctx, int layer, const float* h, int n_tok, const float* r
   }
   if (ctx->ep.world <= 1 && L.n_local != L.n_expert)
     return fail(ctx, KC_ERR_STATE, "kc_moe_ffn: layer %d holds a shard of the experts", layer);
-  RC(ensure_work(ctx, n_tok, L.n_expert, L.k, L.d, L.ff));
+  RC(ensure_work(ctx, n_tok, L.n_expert, L.k, layer_work_d(L), layer_work_f(L)));
   Work& W = ctx->ws;
   const float* router = L.router;
   if (router_w) {
@@ -1005,76 +1189,7 @@ int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out)
   const Dense& D = it->second;
   cudaSetDevice(ctx->device);
   if (n == 0) return KC_OK;
-  cudaStream_t st = ctx->stream;
-  if (D.t == T_F32) {
-    launch_router_logits(reinterpret_cast<const float*>(D.w), D.rs / 4, (int)D.rows, (int)D.cols, x, n, out, ctx->status,
-                         st);
-    CKL();
-    return KC_OK;
-  }
-  RC(ensure_work(ctx, n, 1, 1, (int)std::min<int64_t>(D.cols, 1 << 30), 256));
-  Work& W = ctx->ws;
-  launch_dense_meta(n, W.meta, st);
-  CKL();
-  GroupedArgs a = grouped_base(ctx);
-  a.w0 = D.w;
-  a.expert_stride = 0;
-  a.expert_base = 0;
-  a.rows = (int)D.rows;
-  a.cols = (int)D.cols;
-  a.type = D.t;
-  a.offsets = W.meta.offsets;
-  a.slot_src = nullptr;
-  a.af = x;
-  a.out = out;
-  a.out_stride = D.rows;
-  if (n < 4) {
-    const bool kq = is_k(D.t);
-    launch_act_records(kq, x, nullptr, nullptr, n, D.cols, W.xrec, n, nullptr, nullptr, st);
-    CKL();
-    DecodeArgs dv{};
-    dv.w[0] = D.w;
-    dv.n_mat = 1;
-    dv.rows = (int)D.rows;
-    dv.cols = (int)D.cols;
-    dv.type = D.t;
-    dv.list = W.meta.small_list;
-    dv.n_list = W.meta.n_lists;
-    dv.offsets = W.meta.offsets;
-    dv.rec = W.xrec;
-    dv.rec_slots = n;
-    dv.out[0] = out;
-    dv.out_stride = D.rows;
-    dv.status = ctx->status;
-    RC(launch_decode(dv, ceil_div(D.rows, kTileRows), st));
-  } else if (mma_supported(D.t, D.cols, 1)) {
-    launch_act_records(is_k(D.t), x, nullptr, nullptr, n, D.cols, nullptr, n, nullptr, W.x16, st);
-    CKL();
-    alignas(64) unsigned char tmap[128];
-    if (make_tmap_f16(tmap, W.x16, n, D.cols) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
-    MmaArgs ma{};
-    ma.part = W.mma_part;
-    ma.tile_cnt = W.mma_cnt;
-    ma.w[0] = D.w;
-    ma.n_mat = 1;
-    ma.rows = (int)D.rows;
-    ma.cols = (int)D.cols;
-    ma.type = D.t;
-    ma.list = W.meta.large_list;
-    ma.n_list = W.meta.n_lists + 1;
-    ma.offsets = W.meta.offsets;
-    ma.tt_prefix = W.meta.large_tt;
-    ma.out[0] = out;
-    ma.out_stride = D.rows;
-    ma.status = ctx->status;
-    RC(launch_mma_grouped(ma, tmap, ceil_div(n, 128) * ceil_div(D.rows, 128), st));
-  } else {
-    a.list = W.meta.large_list;
-    a.n_list = W.meta.n_lists + 1;
-    RC(launch_grouped_f32(a, false, 1, n, st));
-  }
-  CKL();
-  return KC_OK;
+  return dense_forward(ctx, D, x, n, out);
 }
 
 int kc_matmul(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out) {

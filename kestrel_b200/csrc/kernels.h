@@ -40,8 +40,13 @@ void launch_block_sums(int t, const void* w, int64_t rows, int64_t cols, const i
                        int n_act, int32_t* out, cudaStream_t st);
 
 // router.cu
+// force_dot: always quant::dot's order (the reference's vector dots, e.g. the
+// shared-expert gate), whatever n_tok.
 void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int d, const float* h, int n_tok,
-                          float* logits, int* status, cudaStream_t st);
+                          float* logits, int* status, cudaStream_t st, bool force_dot = false);
+// out[s, :] += g[s] * y[s, :] with g[s] = 1 / (1 + exp(-logit[s])) (logit
+// null: g = 1): the shared expert's contribution (transformer.rs:577-585).
+void launch_shared_add(const float* y, const float* logit, int n_tok, int d, float* out, cudaStream_t st);
 void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
                   float* w, cudaStream_t st);
 // Dispatch metadata of one routed batch (see router.cu).

@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* 
 }
 
 void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int d, const float* h, int n_tok,
-                          float* logits, int* status, cudaStream_t st) {
+                          float* logits, int* status, cudaStream_t st, bool force_dot) {
   if (n_tok <= 0) return;
   static bool attr = false;
   const size_t smem = 2 * (RL_E + RL_T) * RL_ROW * sizeof(float);
@@ -138,7 +138,7 @@ void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int 
   dim3 grid(ceil_div(E, RL_E), ceil_div(n_tok, RL_T));
   // quant::matmul's dispatch (quant.rs:241): the GEMM path needs >= 4 rows and
   // d % 8 == 0; otherwise quant::dot per output.
-  if (n_tok >= 4 && d % 8 == 0)
+  if (!force_dot && n_tok >= 4 && d % 8 == 0)
     launch_k(router_logits_kernel<true>, grid, RL_THREADS, smem, st, w, row_stride_floats, E, d, h, n_tok, logits, status);
   else
     launch_k(router_logits_kernel<false>, grid, RL_THREADS, smem, st, w, row_stride_floats, E, d, h, n_tok, logits, status);
@@ -445,6 +445,33 @@ void launch_combine(const float* y, const int* tok_slot, const int* ids, const f
                     float* out, cudaStream_t st) {
   if (n_tok <= 0) return;
   launch_k(combine_kernel, n_tok, 256, 0, st, y, tok_slot, ids, w, k, d, out);
+}
+
+// ---------------------------------------------------------------------------
+// Shared expert (qwen2moe, transformer.rs:577-585): gate = 1 / (1 + exp(-dot)),
+// then out += gate * y elementwise (multiply, then add). One thread per 4
+// floats.
+__global__ void shared_add_kernel(const float* __restrict__ y, const float* __restrict__ logit, int n_tok, int d,
+                                  float* __restrict__ out) {
+  pdl_enter();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t per = d / 4;
+  if (i >= (int64_t)n_tok * per) return;
+  const int64_t s = i / per;
+  const float g = logit ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-logit[s]))) : 1.0f;
+  const float4 v = reinterpret_cast<const float4*>(y)[i];
+  float4 o = reinterpret_cast<float4*>(out)[i];
+  o.x = __fadd_rn(o.x, __fmul_rn(g, v.x));
+  o.y = __fadd_rn(o.y, __fmul_rn(g, v.y));
+  o.z = __fadd_rn(o.z, __fmul_rn(g, v.z));
+  o.w = __fadd_rn(o.w, __fmul_rn(g, v.w));
+  reinterpret_cast<float4*>(out)[i] = o;
+}
+
+void launch_shared_add(const float* y, const float* logit, int n_tok, int d, float* out, cudaStream_t st) {
+  const int64_t n = (int64_t)n_tok * (d / 4);
+  if (n <= 0) return;
+  launch_k(shared_add_kernel, ceil_div(n, 256), 256, 0, st, y, logit, n_tok, d, out);
 }
 
 }  // namespace kc

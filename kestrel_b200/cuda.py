@@ -51,6 +51,7 @@ SIGNATURES = {
     "kc_profile_enable": (I, [P, I]),
     "kc_profile_read": (I, [P, P, P, I]),
     "kc_route_noalloc": (I, [P, I, I, P, I, I, I, F, P, P, P]),
+    "kc_upload_shared_expert": (I, [P, I, I, I, I, P, I, P, I, P, P, I]),
     "kc_ep_unique_id": (I, [ctypes.c_char_p]),
     "kc_ep_init": (I, [P, I, I, ctypes.c_char_p]),
 }
@@ -162,6 +163,17 @@ class Context:
         self._check(lib().kc_upload_router(self.h, layer, _ptr(rw), E, d, k, int(norm_topk), weights_scale,
                                            int(_is_dev(rw))))
         self._k[layer] = k
+
+    def upload_shared_expert(self, layer: int, ff: int, d: int, t_gate: int, gate, t_up: int, up, t_down: int,
+                             down, gate_inp=None):
+        """qwen2moe shared expert of `layer` (host numpy GGUF bytes or torch CUDA
+        uint8); gate_inp: optional F32 [d] gate vector."""
+        gate, up, down = _host_u8(gate), _host_u8(up), _host_u8(down)
+        dev = _is_dev(gate)
+        gi = None if gate_inp is None else (gate_inp if _is_dev(gate_inp) else
+                                            np.ascontiguousarray(gate_inp, dtype=np.float32))
+        self._check(lib().kc_upload_shared_expert(self.h, layer, ff, d, t_gate, _ptr(gate), t_up, _ptr(up), t_down,
+                                                  _ptr(down), _ptr(gi), int(dev)))
 
     def upload_dense(self, tensor_id: int, t: int, w, rows: int, cols: int):
         w = _host_u8(w) if t != G.F32 or not isinstance(w, np.ndarray) else \

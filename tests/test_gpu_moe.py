@@ -154,3 +154,31 @@ def test_repeat_calls_identical(ctx):
     ctx.moe_ffn(60, h2)
     b = ctx.moe_ffn(60, h1)[0]
     assert np.array_equal(bits(a), bits(b))
+
+
+@pytest.mark.parametrize("with_gate", [True, False])
+def test_shared_expert_layer(ctx, with_gate):
+    """qwen2moe layer: routed experts (no top-k renormalisation) plus the
+    always-on shared expert scaled by sigmoid(gate_inp . h)
+    (transformer.rs:571-587), against the oracle at token counts on both sides
+    of quant::matmul's n < 4 / n >= 4 dispatch."""
+    lid = 950 + int(with_gate)
+    L = make_layer(8, 4, 512, 512, seed=21)
+    upload(ctx, lid, L, norm_topk=False)
+    rng = np.random.default_rng(22)
+    sf = 1024
+    sh = dict(t_gate=G.Q4_K, t_up=G.Q4_K, t_down=G.Q6_K, ff=sf,
+              gate=G.quantize(G.Q4_K, rng.standard_normal((sf, 512), dtype=np.float32) * np.float32(0.02)),
+              up=G.quantize(G.Q4_K, rng.standard_normal((sf, 512), dtype=np.float32) * np.float32(0.02)),
+              down=G.quantize(G.Q6_K, rng.standard_normal((512, sf), dtype=np.float32) * np.float32(0.02)),
+              inp=(rng.standard_normal(512, dtype=np.float32) * np.float32(0.05)) if with_gate else None)
+    ctx.upload_shared_expert(lid, sf, 512, sh["t_gate"], sh["gate"], sh["t_up"], sh["up"], sh["t_down"], sh["down"],
+                             sh["inp"])
+    for n in (1, 3, 4, 16):
+        h = rng.standard_normal((n, 512)).astype(np.float32)
+        out, ids, w = ctx.moe_ffn(lid, h)
+        r_out, r_ids, r_w = oracle.moe_ffn(h, L["router"], L["k"], L["t_gate"], L["gate"], L["t_gate"], L["up"],
+                                           L["t_down"], L["down"], L["ff"], norm_topk=False, shared=sh)
+        assert np.array_equal(ids, r_ids)
+        ok, err, scale = tol_ok(out, r_out)
+        assert ok, f"n={n}: max err {err} vs scale {scale}"
