@@ -16,6 +16,9 @@ weights from L2). Activations: f32 N(0, 1), a pool of distinct batches.
   cpu_baseline  the CPU oracle (C++ AVX2 restatement of Kestrel's path) on a
                 bounded sample of the same workload, all host threads
 
+--config c2 / c4 measure the other single-layer configs the same way
+(Mixtral-8x7B shape; Qwen3-235B-A22B shape with Zipf-skewed routing).
+
 --impl reference times the oracle alone (the reference's CPU arithmetic) on
 the same config. Multi-GPU (torchrun, N ranks): expert parallelism -- rank r
 holds experts [r*E/N, (r+1)*E/N) of every layer and a copy of the router, routes
@@ -39,9 +42,34 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CFG = dict(name="qwen3-30b-a3b-moe-layer", d=2048, E=128, k=8, ff=768)
-BYTES_PER_EXPERT = 2 * 768 * (2048 // 256) * 144 + 2048 * (768 // 256) * 210  # 3,059,712
-ROUTER_BYTES = 128 * 2048 * 4
+# The single-layer configs of the benchmark list: c1 (the headline), c2 and c4.
+# `layers`: distinct layers rotated so that no step finds its weights in L2.
+CONFIGS = {
+    "c1": dict(name="qwen3-30b-a3b-moe-layer", d=2048, E=128, k=8, ff=768, layers=48, batch=16,
+               sweep=[1, 16, 128, 512], zipf=False),
+    "c2": dict(name="mixtral-8x7b-moe-layer", d=4096, E=8, k=2, ff=14336, layers=8, batch=1,
+               sweep=[1, 512, 2048, 4096], zipf=False),
+    "c4": dict(name="qwen3-235b-a22b-moe-layer-zipf", d=4096, E=128, k=8, ff=1536, layers=8, batch=64,
+               sweep=[1, 64, 2048], zipf=True),
+}
+CFG = dict(CONFIGS["c1"])
+
+
+def bytes_per_expert() -> int:
+    """Q4_K gate + up and Q6_K down of one expert (c1: 3,059,712 B)."""
+    return 2 * CFG["ff"] * (CFG["d"] // 256) * 144 + CFG["d"] * (CFG["ff"] // 256) * 210
+
+
+def router_bytes() -> int:
+    return CFG["E"] * CFG["d"] * 4
+
+
+def zipf_router_column(rng, E, d):
+    """configs[4]'s skew: router column 0 holds beta_e = -1.2 ln(1 + rank(e))
+    sigma_logit for a seeded rank permutation; with input feature 0 set to 1
+    this adds beta_e to expert e's logit (popularity ~ Zipf s=1.2)."""
+    rank = rng.permutation(E)
+    return (-1.2 * np.log1p(rank) * 0.02 * np.sqrt(d)).astype(np.float32)
 
 
 def peaks():
@@ -51,6 +79,15 @@ def peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def bf16_peak_tflops() -> float:
+    """Measured dense bf16 GEMM throughput (burst), else the pool's fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
 
 
 def algorithmic_bytes(ids: np.ndarray, B: int, block=None) -> dict:
@@ -66,9 +103,9 @@ def algorithmic_bytes(ids: np.ndarray, B: int, block=None) -> dict:
     large = int((cnt >= 4).sum())
     gate_up = 2 * ff * (d // 256) * 144
     down = d * (ff // 256) * 210
-    return dict(total=(small + large) * BYTES_PER_EXPERT + ROUTER_BYTES + B * d * 4 * 2,
+    return dict(total=(small + large) * bytes_per_expert() + router_bytes() + B * d * 4 * 2,
                 gate_up_int8=small * gate_up, down_int8=small * down, gate_up_f32=large * gate_up,
-                down_f32=large * down, router=ROUTER_BYTES, experts=small + large)
+                down_f32=large * down, router=router_bytes(), experts=small + large)
 
 
 class ClockSampler:
@@ -140,6 +177,8 @@ def make_layers(ctx, torch, n_layers, seed=0, block=None):
             xv.normal_(0.0, 0.02, generator=g)
             ctx.quantize_dev(t, xv, bufs[n])
         router = torch.empty((E, d), dtype=torch.float32, device="cuda").normal_(0.0, 0.02, generator=gr)
+        if CFG["zipf"]:
+            router[:, 0] = torch.from_numpy(zipf_router_column(np.random.default_rng(layer), E, d)).cuda()
         ctx.upload_experts(layer, E, d, ff, G.Q4_K, bufs["gate"], G.Q4_K, bufs["up"], G.Q6_K, bufs["down"],
                            first_expert=first, n_local=n_loc)
         ctx.upload_router(layer, router, k)
@@ -161,6 +200,8 @@ def cpu_oracle_rate(layer_w, B, budget_s, threads, seed=5):
     calls, tokens, t0 = 0, 0, time.perf_counter()
     while True:
         h = rng.standard_normal((B, CFG["d"]), dtype=np.float32)
+        if CFG["zipf"]:
+            h[:, 0] = 1.0
         oracle.moe_ffn(h, layer_w["router"], CFG["k"], G.Q4_K, layer_w["gate"], G.Q4_K, layer_w["up"], G.Q6_K,
                        layer_w["down"], CFG["ff"])
         calls += 1
@@ -194,6 +235,8 @@ def host_layer_numpy(seed=0):
          "down": mat("down", G.Q6_K, E * d, ff, seed * 10 + 3)}
     w["router"] = (np.random.default_rng(seed * 10 + 4).standard_normal((E, d), dtype=np.float32) *
                    np.float32(0.02))
+    if CFG["zipf"]:
+        w["router"][:, 0] = zipf_router_column(np.random.default_rng(0), E, d)
     return w
 
 
@@ -274,6 +317,10 @@ def run_ours(args):
     d = CFG["d"]
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     pool = {b: [torch.randn((b, d), generator=g, device="cuda") for _ in range(16)] for b in batches}
+    if CFG["zipf"]:
+        for b in batches:
+            for t in pool[b]:
+                t[:, 0] = 1.0
     outs = {b: [torch.empty((b, d), device="cuda") for _ in range(2)] for b in batches}
 
     def barrier():
@@ -311,6 +358,7 @@ def run_ours(args):
     # Profiling pass (separate from the timed region): per-stage event times and
     # the routed experts of every call -> algorithmic bytes per stage.
     hbm_peak, peak_kind = peaks()
+    bf16_peak = bf16_peak_tflops()
     prof_steps = max(args.steps, 16)
     ids_dev = torch.empty((B, CFG["k"]), dtype=torch.int32, device="cuda")
     ctx.profile_read()
@@ -362,13 +410,19 @@ def run_ours(args):
             ctx.moe_ffn_dev(i % n_layers, pool[b][i], outs[b][0], ids_b, None, n_tok=b)
             tot += algorithmic_bytes(all_ids(ids_b), b, block)["total"]
         per_ms = ms_b / steps_b
+        flops = 2.0 * b * CFG["k"] * 3 * CFG["d"] * CFG["ff"]  # routed experts' products of one rank's batch
         sweep[str(b)] = {"ms_per_step": per_ms, "tokens_per_s": world * b / (per_ms / 1e3),
                          "hbm_gbs": (tot / 4) / (per_ms / 1e3) / 1e9,
-                         "hbm_frac": (tot / 4) / (per_ms / 1e3) / 1e9 / hbm_peak}
+                         "hbm_frac": (tot / 4) / (per_ms / 1e3) / 1e9 / hbm_peak,
+                         "tflops": flops / (per_ms / 1e3) / 1e12,
+                         "tensor_frac": flops / (per_ms / 1e3) / 1e12 / bf16_peak}
 
     # End to end through the host-pointer C ABI call (pinned buffers).
     hp = [torch.randn((B, d), generator=torch.Generator().manual_seed(i)).pin_memory().numpy()
           for i in range(4)]
+    if CFG["zipf"]:
+        for a in hp:
+            a[:, 0] = 1.0
     e2e_steps = max(4, args.steps // 2)
     for i in range(3):
         ctx.moe_ffn(i % n_layers, hp[i % 4])
@@ -394,7 +448,9 @@ def run_ours(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4k/f32", "data": "synthetic",
             "config": {"workload": CFG["name"], "batch_tokens": B, "d_model": CFG["d"], "experts": CFG["E"],
                        "top_k": CFG["k"], "expert_ff": CFG["ff"], "quant": "Q4_K gate/up + Q6_K down",
-                       "layers_rotated": n_layers, "l2": "inputs larger than L2 (48 distinct layers, 18.8 GB)",
+                       "layers_rotated": n_layers,
+                       "l2": f"inputs larger than L2 ({n_layers} distinct layers, "
+                             f"{n_layers * CFG['E'] * bytes_per_expert() / 1e9:.1f} GB of expert weights)",
                        "parallelism": f"ep{world}" if world > 1 else "single",
                        "experts_per_gpu": CFG["E"] // world},
             "layer_hbm": {"bytes_per_step": layer_bytes, "gbs": layer_gbs, "frac": layer_gbs / hbm_peak,
@@ -425,13 +481,20 @@ def main():
     ap.add_argument("--steps", type=int, default=48)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=16)
-    ap.add_argument("--sweep", type=lambda s: [int(x) for x in s.split(",") if x], default=[1, 16, 128, 512])
-    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c1",
+                    help="c1: Qwen3-30B-A3B layer (headline); c2: Mixtral-8x7B layer; c4: Qwen3-235B-A22B "
+                         "layer with Zipf-skewed routing")
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--sweep", type=lambda s: [int(x) for x in s.split(",") if x], default=None)
+    ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    CFG.update(CONFIGS[args.config])
+    args.batch = CFG["batch"] if args.batch is None else args.batch
+    args.sweep = CFG["sweep"] if args.sweep is None else args.sweep
+    args.layers = CFG["layers"] if args.layers is None else args.layers
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -304,7 +304,15 @@ int check_status(kc_ctx* ctx) {
   CK(cudaMemcpy(&st, ctx->status, sizeof(int), cudaMemcpyDeviceToHost));
   if (st != 0) {
     CK(cudaMemset(ctx->status, 0, sizeof(int)));
-    return fail(ctx, st, "a kernel reported status %d (bounded wait expired)", st);
+    static const char* sites[] = {"unknown", "decode producer (empty stage)", "decode consumer (full stage)",
+                                  "decode drain", "tcgen05 producer (raw stage)", "tcgen05 producer (operand stage)",
+                                  "tcgen05 producer drain", "tcgen05 MMA issuer (operand stage)",
+                                  "tcgen05 MMA issuer (accumulator)", "tcgen05 dequantiser (raw stage)",
+                                  "tcgen05 dequantiser (operand stage)", "tcgen05 epilogue (accumulator)",
+                                  "router logits (bulk copy)", "tcgen05 MMA issuer drain"};
+    const int site = st >> 8;
+    return fail(ctx, st & 0xFF, "a kernel's bounded wait expired (status %d) at: %s", st & 0xFF,
+                site >= 0 && site < (int)(sizeof(sites) / sizeof(sites[0])) ? sites[site] : "unknown");
   }
   return KC_OK;
 }

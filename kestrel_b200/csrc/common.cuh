@@ -108,8 +108,9 @@ __device__ __forceinline__ void report(int* status, int code) {
 }
 
 // Limit for every spin-wait in this library: after it expires the waiting
-// thread records KC_ERR_TIMEOUT and stops waiting.
-constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+// thread records KC_ERR_TIMEOUT and stops waiting. Generous against time
+// slicing or preemption of the GPU; every wait still ends.
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -140,19 +141,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait on a phase parity. Returns false (and records a timeout) if the
-// phase did not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+// Bounded wait on a phase parity. Returns false if the phase did not complete
+// within kWaitLimitNs, and records KC_ERR_TIMEOUT with the wait's site tag in
+// bits 8.. of the status word (kc_last_error names the site).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int site = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
     if (globaltimer() - t0 > kWaitLimitNs) {
-      report(status, KC_ERR_TIMEOUT);
+      report(status, KC_ERR_TIMEOUT | (site << 8));
       return false;
     }
   }
   return true;
 }
+// Site tags of the bounded waits.
+enum : int {
+  W_DEC_EMPTY = 1, W_DEC_FULL = 2, W_DEC_DRAIN = 3, W_MMA_RAW_EMPTY = 4, W_MMA_OP_EMPTY_P = 5, W_MMA_DRAIN = 6,
+  W_MMA_OP_FULL = 7, W_MMA_ACC_EMPTY = 8, W_MMA_RAW_FULL = 9, W_MMA_OP_EMPTY_D = 10, W_MMA_ACC_FULL = 11,
+  W_ROUTER = 12, W_MMA_TC_DRAIN = 13
+};
 
 // ---- bulk async copy (TMA, non-tensor): global -> shared ------------------
 // Both addresses 16-byte aligned, size a multiple of 16 (checked by callers).

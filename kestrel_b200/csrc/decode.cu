@@ -439,7 +439,7 @@ __device__ __forceinline__ void run_unit(const DecodeArgs& a, const DecodeGeom& 
     cp_async_commit();
     cp_async_wait1();
     __syncwarp();
-    if (ok && !mbar_wait(&full[st], ph, a.status)) ok = false;
+    if (ok && !mbar_wait(&full[st], ph, a.status, W_DEC_FULL)) ok = false;
     if (ok) {
       const uint32_t sp = smem_u32(ring) + (uint32_t)(st * g.stage_bytes);
       const uint32_t xr = smem_u32(abuf) + (uint32_t)(buf * half);
@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
 #pragma unroll
           for (int w = 0; w < DW; ++w) {
             if (w < wg && ok) {
-              if (issued >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status)) {
+              if (issued >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status, W_DEC_EMPTY)) {
                 ok = false;
               } else {
                 mbar_expect_tx(&full[st], bytes);
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
       }
       // Keep the CTA alive until every issued copy has landed (bounded).
       for (int k = max(0, issued - n_stages); k < issued; ++k)
-        mbar_wait(&full[k % n_stages], (uint32_t)((k / n_stages) & 1), a.status);
+        mbar_wait(&full[k % n_stages], (uint32_t)((k / n_stages) & 1), a.status, W_DEC_DRAIN);
     }
     return;
   }

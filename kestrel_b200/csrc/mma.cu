@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
           const int sb = kc >> 2;
           if ((kc & 3) == 0) {
             const int r = raw_it % M_RAWS;
-            if (raw_it >= M_RAWS && !mbar_wait(&raw_empty[r], ((raw_it / M_RAWS) & 1) ^ 1, a.status)) {
+            if (raw_it >= M_RAWS && !mbar_wait(&raw_empty[r], ((raw_it / M_RAWS) & 1) ^ 1, a.status, W_MMA_RAW_EMPTY)) {
               ok = false;
               break;
             }
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
             ++raw_it;
           }
           const int o = op_it % M_OPS;
-          if (op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status)) {
+          if (op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status, W_MMA_OP_EMPTY_P)) {
             ok = false;
             break;
           }
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
       }
       // Drain: every issued copy lands before the CTA may exit.
       for (int i = std::max(0, op_it - M_OPS); i < op_it; ++i)
-        mbar_wait(&op_full[i % M_OPS], (i / M_OPS) & 1, a.status);
+        mbar_wait(&op_full[i % M_OPS], (i / M_OPS) & 1, a.status, W_MMA_DRAIN);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -348,14 +348,14 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
         k_range(w % S, kc0, kc1);
         const int n = ((t.nt + 15) / 16) * 16;
         const uint32_t idesc = f16_idesc(n);
-        if (tile_it > 0 && !mbar_wait(&acc_empty, (tile_it - 1) & 1, a.status)) {
+        if (tile_it > 0 && !mbar_wait(&acc_empty, (tile_it - 1) & 1, a.status, W_MMA_ACC_EMPTY)) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int kc = kc0; kc < kc1; ++kc) {
           const int o = op_it % M_OPS;
-          if (!mbar_wait(&op_full[o], (op_it / M_OPS) & 1, a.status)) {
+          if (!mbar_wait(&op_full[o], (op_it / M_OPS) & 1, a.status, W_MMA_OP_FULL)) {
             ok = false;
             break;
           }
@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
         umma_commit(&acc_full);
       }
       // Drain: the tensor core has finished with TMEM before it is freed.
-      if (op_it > 0) mbar_wait(&op_empty[(op_it - 1) % M_OPS], ((op_it - 1) / M_OPS) & 1, a.status);
+      if (op_it > 0) mbar_wait(&op_empty[(op_it - 1) % M_OPS], ((op_it - 1) / M_OPS) & 1, a.status, W_MMA_TC_DRAIN);
     }
   } else {
     // Dequantisation warps: thread t holds weight row m = t % 128 of the tile
@@ -397,10 +397,10 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
         const int sb = kc >> 2, kk = kc & 3;
         if (kk == 0) {
           r = raw_it % M_RAWS;
-          if (ok && !mbar_wait(&raw_full[r], (raw_it / M_RAWS) & 1, a.status)) ok = false;
+          if (ok && !mbar_wait(&raw_full[r], (raw_it / M_RAWS) & 1, a.status, W_MMA_RAW_FULL)) ok = false;
         }
         const int o = op_it % M_OPS;
-        if (ok && op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status)) ok = false;
+        if (ok && op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status, W_MMA_OP_EMPTY_D)) ok = false;
         if (ok) {
           uint8_t* A = ops + o * L.op_bytes;
           const uint8_t* rb = raws + r * L.raw_bytes;
@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
       }
       // Epilogue: rows of this warp's TMEM quadrant (warp % 4); the two warps
       // of a quadrant take alternate 16-column blocks.
-      if (ok && !mbar_wait(&acc_full, tile_it & 1, a.status)) ok = false;
+      if (ok && !mbar_wait(&acc_full, tile_it & 1, a.status, W_MMA_ACC_FULL)) ok = false;
       tc_fence_after();
       const int quad = warp & 3, colh = (warp - 2) >> 2;
       const int rl = quad * 32 + lane;

@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* 
       if (nchunk > 1) issue(1);
     }
     for (int c = 0; c < nchunk; ++c) {
-      mbar_wait(&full[c & 1], (c >> 1) & 1, status);
+      mbar_wait(&full[c & 1], (c >> 1) & 1, status, W_ROUTER);
       const float* buf = rsm + (c & 1) * (RL_E + RL_T) * RL_ROW;
       const float* wr = buf + erc * RL_ROW + j;
       const float* xr = buf + (RL_E + trc) * RL_ROW + j;
