@@ -309,7 +309,8 @@ int check_status(kc_ctx* ctx) {
                                   "tcgen05 producer drain", "tcgen05 MMA issuer (operand stage)",
                                   "tcgen05 MMA issuer (accumulator)", "tcgen05 dequantiser (raw stage)",
                                   "tcgen05 dequantiser (operand stage)", "tcgen05 epilogue (accumulator)",
-                                  "router logits (bulk copy)", "tcgen05 MMA issuer drain"};
+                                  "router logits (bulk copy)", "tcgen05 MMA issuer drain",
+                                  "decode consumer (previous lap of a stage)"};
     const int site = st >> 8;
     return fail(ctx, st & 0xFF, "a kernel's bounded wait expired (status %d) at: %s", st & 0xFF,
                 site >= 0 && site < (int)(sizeof(sites) / sizeof(sites[0])) ? sites[site] : "unknown");
@@ -433,7 +434,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     RC(launch_decode(dg, max_small * 2 * ceil_div(ff, kTileRows), st));
     CKL();
   }
-  const int max_tt = ceil_div(A, 128) + std::min(E, A / 4);
+  const int max_tt = ceil_div(A, kMmaTileN) + std::min(E, A / 4);
   if (mma_gu) {
     StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
     alignas(64) unsigned char tmap[128];
@@ -622,7 +623,7 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     ma.out[0] = out;
     ma.out_stride = D.rows;
     ma.status = ctx->status;
-    RC(launch_mma_grouped(ma, tmap, ceil_div(n, 128) * ceil_div(D.rows, 128), st));
+    RC(launch_mma_grouped(ma, tmap, ceil_div(n, kMmaTileN) * ceil_div(D.rows, 128), st));
   } else {
     a.list = W.meta.large_list;
     a.n_list = W.meta.n_lists + 1;

@@ -414,13 +414,13 @@ struct TypeR {
 
 // One unit: NS slots, all segments. `buf` selects the warp's activation
 // buffer holding this step's records (prefetched by the previous step).
-// (st, ph) is the ring slot and phase parity of the unit's first stage; the
-// warp's later stages of the unit are `step` stages apart, and its next unit
-// starts DW stages after this unit's last one. On return (st, ph) point at
-// that next stage.
+// (sid, st, ph) are the stage number, ring slot and phase parity of the
+// unit's first stage; the warp's later stages of the unit are `step` stages
+// apart, and its next unit starts DW stages after this unit's last one. On
+// return they point at that next stage.
 template <int T, int NS>
 __device__ __forceinline__ void run_unit(const DecodeArgs& a, const DecodeGeom& g, const uint8_t* ring,
-                                         uint64_t* full, uint64_t* empty, int n_stages, int& st, uint32_t& ph,
+                                         uint64_t* full, uint64_t* empty, int n_stages, int& sid, int& st, uint32_t& ph,
                                          int step, uint8_t* abuf, int& buf, const UnitMeta& um, bool has_next,
                                          const UnitMeta& next, int lane, float* out, int r_out, bool& ok) {
   constexpr int R = TypeR<T>::R;
@@ -439,6 +439,11 @@ __device__ __forceinline__ void run_unit(const DecodeArgs& a, const DecodeGeom& 
     cp_async_commit();
     cp_async_wait1();
     __syncwarp();
+    // A slot is used lap after lap by different warps, and bulk copies may land
+    // out of order: before waiting on this lap's copy, wait until the slot's
+    // previous lap has been released. Only then is the copy barrier known to be
+    // in this lap's phase, so its parity test cannot alias an older phase.
+    if (ok && sid >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status, W_DEC_PREV)) ok = false;
     if (ok && !mbar_wait(&full[st], ph, a.status, W_DEC_FULL)) ok = false;
     if (ok) {
       const uint32_t sp = smem_u32(ring) + (uint32_t)(st * g.stage_bytes);
@@ -454,7 +459,9 @@ __device__ __forceinline__ void run_unit(const DecodeArgs& a, const DecodeGeom& 
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     buf ^= 1;
-    st += seg + 1 < g.nseg ? step : DW;
+    const int inc = seg + 1 < g.nseg ? step : DW;
+    sid += inc;
+    st += inc;
     if (st >= n_stages) {
       st -= n_stages;
       ph ^= 1u;
@@ -562,7 +569,7 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
   UnitMeta um = meta_of(unit_pos(ubeg + w, tiles, a.n_mat).li);
   issue_act<R>(a, g, um, 0, abuf, lane);
   cp_async_commit();
-  int st = w;  // the warp's first stage is stage w (w < DW <= n_stages)
+  int sid = w, st = w;  // the warp's first stage is stage w (w < DW <= n_stages)
   uint32_t ph = 0;
   for (int gi = 0; gi < n_groups; ++gi) {
     const int wg = (int)min((int64_t)DW, n_units - (int64_t)gi * DW);
@@ -577,11 +584,11 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
     const int r_out = r0 + lane < a.rows ? r0 + lane : -1;  // padding rows are computed, not stored
     float* out = p.m == 0 ? a.out[0] : a.out[1];
     if (um.ns == 1)
-      run_unit<T, 1>(a, g, ring, full, empty, n_stages, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
+      run_unit<T, 1>(a, g, ring, full, empty, n_stages, sid, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
     else if (um.ns == 2)
-      run_unit<T, 2>(a, g, ring, full, empty, n_stages, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
+      run_unit<T, 2>(a, g, ring, full, empty, n_stages, sid, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
     else
-      run_unit<T, 3>(a, g, ring, full, empty, n_stages, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
+      run_unit<T, 3>(a, g, ring, full, empty, n_stages, sid, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
     um = next;
   }
   cp_async_wait0();

@@ -6,6 +6,9 @@
 
 namespace kc {
 
+// Slots per work tile of the tensor-core grouped products (the MMA's N).
+constexpr int kMmaTileN = 256;
+
 // Activation rows of a grouped product: slot i reads activation row
 // slot_src[i] (or i when slot_src is null).
 struct GroupedArgs {
@@ -59,7 +62,7 @@ struct DispatchOut {
   int* small_list; // experts with 1..3 rows (int8 path)
   int* large_list; // experts with >= 4 rows (f32 path)
   int* n_lists;    // [2]: entries in small_list, large_list
-  int* large_tt;   // [E+1]: prefix over large_list of ceil(rows / 128) token tiles
+  int* large_tt;   // [E+1]: prefix over large_list of ceil(rows / kMmaTileN) token tiles
 };
 int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st);
 // Metadata of a dense product: one group of n rows, slots = rows 0..n-1.

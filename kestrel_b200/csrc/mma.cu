@@ -31,25 +31,33 @@ namespace kc {
 
 constexpr int MM = 128;       // weight rows per tile
 constexpr int MK = 64;        // K elements per operand stage (one 128B swizzle atom)
-constexpr int MN = 128;       // slots per tile
+constexpr int MN = kMmaTileN; // slots per tile (N of the MMA: up to 256)
 constexpr int M_DQW = 8;      // dequantisation + epilogue warps (two per row: one per 32-element half)
 constexpr int M_THREADS = 64 + 32 * M_DQW;
-constexpr int M_OPS = 3;      // operand stages
+constexpr int M_OPS_MAX = 3;  // operand stages (fewer where shared memory is short)
 constexpr int M_RAWS = 2;     // raw superblock stages
 constexpr int A_BYTES = MM * MK * 2;  // 16 KB
-constexpr int B_BYTES = MN * MK * 2;  // 16 KB
+constexpr int B_BYTES = MN * MK * 2;  // 32 KB
 
-__host__ __device__ inline int max_sbt_bytes(int t) { return t == T_Q4_K ? 4608 : t == T_Q6_K ? 6720 : 8704; }
+__host__ __device__ constexpr int max_sbt_bytes(int t) { return t == T_Q4_K ? 4608 : t == T_Q6_K ? 6720 : 8704; }
 constexpr int M_RT = MM / kTileRows;  // row tiles per M tile
 
+__host__ __device__ constexpr int mma_raw_bytes(int t, int n_mat) {
+  return ((n_mat * M_RT * max_sbt_bytes(t) + 1023) / 1024) * 1024;
+}
+__host__ __device__ constexpr int mma_op_bytes(int n_mat) { return n_mat * A_BYTES + B_BYTES; }
+// Operand stages: three where they fit in 227 KB of shared memory, else two.
+__host__ __device__ constexpr int mma_ops(int t, int n_mat) {
+  return 3 * mma_op_bytes(n_mat) + M_RAWS * mma_raw_bytes(t, n_mat) + 1024 <= 227 * 1024 ? 3 : 2;
+}
 struct MmaSmem {
   int op_bytes, raw_bytes, total;
 };
 __host__ __device__ inline MmaSmem mma_smem(int t, int n_mat) {
   MmaSmem s;
-  s.op_bytes = n_mat * A_BYTES + B_BYTES;
-  s.raw_bytes = ((n_mat * M_RT * max_sbt_bytes(t) + 1023) / 1024) * 1024;
-  s.total = M_OPS * s.op_bytes + M_RAWS * s.raw_bytes + 1024;  // + alignment slack
+  s.op_bytes = mma_op_bytes(n_mat);
+  s.raw_bytes = mma_raw_bytes(t, n_mat);
+  s.total = mma_ops(t, n_mat) * s.op_bytes + M_RAWS * s.raw_bytes + 1024;  // + alignment slack
   return s;
 }
 
@@ -247,7 +255,8 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
                                                                      const __grid_constant__ CUtensorMap tmap_b) {
   pdl_enter();
   extern __shared__ uint8_t msm_raw[];
-  __shared__ __align__(8) uint64_t raw_full[M_RAWS], raw_empty[M_RAWS], op_full[M_OPS], op_empty[M_OPS];
+  constexpr int M_OPS = mma_ops(T, NMAT);
+  __shared__ __align__(8) uint64_t raw_full[M_RAWS], raw_empty[M_RAWS], op_full[M_OPS_MAX], op_empty[M_OPS_MAX];
   __shared__ __align__(8) uint64_t acc_full, acc_empty;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int last_sh;
@@ -266,7 +275,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
   uint8_t* raws = msm + M_OPS * L.op_bytes;
   const int64_t tile_bytes = tiled_tile_bytes(T, a.cols);
   const int prows = (int)padded_rows(a.rows);
-  const uint32_t tcols = NMAT * MN;  // 128 or 256 TMEM columns
+  const uint32_t tcols = NMAT * MN;  // 256 or 512 TMEM columns
   // K chunks [kc0, kc1) of split s: whole superblocks (4 chunks of 64).
   auto k_range = [&](int s, int& kc0, int& kc1) {
     kc0 = 4 * (s * nsb / S);

@@ -16,12 +16,12 @@ struct MmaArgs {
   const int* list;        // experts to process
   const int* n_list;      // device scalar
   const int* offsets;     // [E+1] slot ranges
-  const int* tt_prefix;   // [n_list+1]: prefix of ceil(rows_e / 128) token tiles
+  const int* tt_prefix;   // [n_list+1]: prefix of ceil(rows_e / kMmaTileN) token tiles
   float* out[2];          // out[m][slot * out_stride + row]
   int64_t out_stride;
   int* status;
   // Split-K workspace (null: no split): f32 partial tiles for up to gridDim
-  // work items ([item][n_mat][128 x 128]) and per-tile arrival counters
+  // work items ([item][n_mat][128 x kMmaTileN]) and per-tile arrival counters
   // (zero before the first launch; each launch leaves them zero).
   float* part;
   int* tile_cnt;
@@ -32,7 +32,7 @@ size_t mma_part_bytes();
 size_t mma_cnt_bytes();
 
 // 128-byte CUtensorMap for an f16 row-major [rows, cols] activation matrix,
-// box 64 x 128, 128B swizzle.
+// box 64 x kMmaTileN, 128B swizzle.
 int make_tmap_f16(void* map_out, const void* ptr, int64_t rows, int64_t cols);
 bool mma_supported(int t, int64_t cols, int n_mat);
 int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st);

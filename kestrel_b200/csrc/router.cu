@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
   {
     const int e = tid;
     const int c = e < E ? cnt[e] : 0;
-    const int fs = (c >= 1 && c <= 3) ? 1 : 0, fl = c >= 4 ? 1 : 0, ft = fl ? (c + 127) / 128 : 0;
+    const int fs = (c >= 1 && c <= 3) ? 1 : 0, fl = c >= 4 ? 1 : 0, ft = fl ? (c + kMmaTileN - 1) / kMmaTileN : 0;
     int4 v = make_int4(c, fs, fl, ft);
 #pragma unroll
     for (int sh = 1; sh < 32; sh <<= 1) {
@@ -392,7 +392,7 @@ __global__ void dense_meta_kernel(int n, DispatchOut o) {
   o.n_lists[0] = (n >= 1 && n <= 3) ? 1 : 0;
   o.n_lists[1] = n >= 4 ? 1 : 0;
   o.large_tt[0] = 0;
-  o.large_tt[1] = n >= 4 ? (n + 127) / 128 : 0;
+  o.large_tt[1] = n >= 4 ? (n + kMmaTileN - 1) / kMmaTileN : 0;
 }
 
 void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st) { launch_k(dense_meta_kernel, 1, 1, 0, st, n, o); }
