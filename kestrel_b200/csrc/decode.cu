@@ -507,55 +507,56 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
 
   if (warp == 0) {
     // Producer: group by group, segment-major, one stage per (segment, unit).
-    // Per stage only a wait, an expect_tx and one bulk copy: the units' base
-    // addresses are computed once per group and the ring slot and phase are
-    // advanced incrementally.
-    if (lane == 0) {
-      int st = 0, issued = 0;
-      uint32_t ph = 0;
+    // Lane w issues consumer warp w's stage of every segment, so the stages of
+    // a segment go out in parallel; per stage a lane does only a wait, an
+    // expect_tx and one bulk copy.
+    int last = -1;  // highest stage number this lane issued
+    if (lane < DW) {
+      const int w = lane;
       bool ok = true;
-      for (int gi = 0; gi < n_groups && ok; ++gi) {
-        const int ub = (int)beg + gi * DW;
+      for (int gi = 0; gi < n_groups; ++gi) {
         const int wg = (int)min((int64_t)DW, n_units - (int64_t)gi * DW);
-        const uint8_t* up[DW];
-#pragma unroll
-        for (int w = 0; w < DW; ++w) {
-          up[w] = nullptr;
-          if (w < wg) {
-            const UnitPos p = unit_pos(ub + w, tiles, a.n_mat);
-            const int e = meta_of(p.li).e;
-            up[w] = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(e - a.expert_base) * a.expert_stride +
-                    (int64_t)p.tile * g.tile_bytes;
-          }
+        const bool active = w < wg;
+        const uint8_t* up = nullptr;
+        if (active) {
+          const UnitPos p = unit_pos((int)beg + gi * DW + w, tiles, a.n_mat);
+          const int e = meta_of(p.li).e;
+          up = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(e - a.expert_base) * a.expert_stride +
+               (int64_t)p.tile * g.tile_bytes;
         }
         int64_t off0 = 0;
-        for (int seg = 0; seg < g.nseg && ok; ++seg) {
+        for (int seg = 0; seg < g.nseg; ++seg) {
           const int sb1 = min(g.nsb, (seg + 1) * g.ks);
           const int64_t off1 = sb1 == g.nsb ? g.tile_bytes : tiled_sb_offset(g.type, a.cols, sb1);
-          const uint32_t bytes = (uint32_t)(off1 - off0);
-#pragma unroll
-          for (int w = 0; w < DW; ++w) {
-            if (w < wg && ok) {
-              if (issued >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status, W_DEC_EMPTY)) {
-                ok = false;
-              } else {
-                mbar_expect_tx(&full[st], bytes);
-                bulk_g2s(ring + (int64_t)st * g.stage_bytes, up[w] + off0, bytes, &full[st]);
-                ++issued;
-                if (++st == n_stages) {
-                  st = 0;
-                  ph ^= 1u;
-                }
-              }
+          if (active && ok) {
+            const int sid = (gi * g.nseg + seg) * DW - seg * (DW - wg) + w;  // = gi*nseg*DW + seg*wg + w
+            const int st = sid % n_stages;
+            const uint32_t ph = (uint32_t)((sid / n_stages) & 1);
+            if (sid >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status, W_DEC_EMPTY)) {
+              ok = false;
+            } else {
+              const uint32_t bytes = (uint32_t)(off1 - off0);
+              mbar_expect_tx(&full[st], bytes);
+              bulk_g2s(ring + (int64_t)st * g.stage_bytes, up + off0, bytes, &full[st]);
+              last = sid;
             }
           }
           off0 = off1;
+          // Lanes stay within one segment of each other (independent thread
+          // scheduling could let one run ahead while another waits), so a
+          // slot's previous lap (n_stages > DW stages back) is always issued
+          // before a lane waits for its release.
+          __syncwarp((1u << DW) - 1u);
         }
       }
-      // Keep the CTA alive until every issued copy has landed (bounded).
-      for (int k = max(0, issued - n_stages); k < issued; ++k)
-        mbar_wait(&full[k % n_stages], (uint32_t)((k / n_stages) & 1), a.status, W_DEC_DRAIN);
     }
+    // Keep the CTA alive until every issued copy has landed (bounded): lane 0
+    // waits for the last n_stages stages up to the highest one issued.
+#pragma unroll
+    for (int o = 16; o; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+    if (lane == 0)
+      for (int k = max(0, last + 1 - n_stages); k <= last; ++k)
+        mbar_wait(&full[k % n_stages], (uint32_t)((k / n_stages) & 1), a.status, W_DEC_DRAIN);
     return;
   }
 
