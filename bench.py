@@ -53,6 +53,7 @@ CONFIGS = {
                sweep=[1, 64, 2048], zipf=True),
 }
 CFG = dict(CONFIGS["c1"])
+EP_P2P_TOKENS = 64  # tokens per rank and call exchanged over peer memory (multi-GPU)
 
 
 def bytes_per_expert() -> int:
@@ -311,6 +312,10 @@ def run_ours(args):
     ctx.set_stream(stream.cuda_stream)
     n_layers = args.layers
     host0 = make_layers(ctx, torch, n_layers, seed=0, block=block)
+    if world > 1:
+        # Decode-sized calls exchange rows through NVLink peer memory; larger
+        # ones (the sweep's prefill sizes) go through NCCL.
+        ctx.ep_reserve(EP_P2P_TOKENS)
     B = args.batch
     batches = sorted(set([B] + args.sweep))
     ctx.reserve(max(batches))

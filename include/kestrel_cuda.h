@@ -219,6 +219,13 @@ KC_API int kc_ep_unique_id(char out[128]);
 /* Join an expert-parallel group of `world` ranks; experts of every layer are
    owned by rank e / (E / world) (contiguous blocks). */
 KC_API int kc_ep_init(kc_ctx* ctx, int rank, int world, const char uid[128]);
+/* Map every rank's exchange arena over NVLink (CUDA IPC) for up to
+   `max_tokens` tokens per rank and kc_moe_ffn call (collective; call after
+   uploading the layers and routers, on every rank). Calls within that
+   capacity then exchange token rows and result rows with this library's own
+   kernels through peer memory, with no host synchronisation; larger calls use
+   NCCL. */
+KC_API int kc_ep_reserve(kc_ctx* ctx, int max_tokens);
 
 #ifdef __cplusplus
 }

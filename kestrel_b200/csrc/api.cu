@@ -310,7 +310,8 @@ int check_status(kc_ctx* ctx) {
                                   "tcgen05 MMA issuer (accumulator)", "tcgen05 dequantiser (raw stage)",
                                   "tcgen05 dequantiser (operand stage)", "tcgen05 epilogue (accumulator)",
                                   "router logits (bulk copy)", "tcgen05 MMA issuer drain",
-                                  "decode consumer (previous lap of a stage)"};
+                                  "decode consumer (previous lap of a stage)",
+                                  "expert-parallel peer exchange (another rank did not publish)"};
     const int site = st >> 8;
     return fail(ctx, st & 0xFF, "a kernel's bounded wait expired (status %d) at: %s", st & 0xFF,
                 site >= 0 && site < (int)(sizeof(sites) / sizeof(sites[0])) ? sites[site] : "unknown");
@@ -407,7 +408,8 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   const bool mma_gu = mma_supported(L.t_gate, d, 2);
   {
     StageScope ss(ctx, KC_STAGE_QUANT_X);
-    launch_act_records(kq_in, h, nullptr, W.meta.slot_tok, A, d, W.xrec, A, nullptr, mma_gu ? W.x16 : nullptr, st);
+    launch_act_records(kq_in, h, nullptr, W.meta.slot_tok, A, d, W.xrec, A, nullptr, mma_gu ? W.x16 : nullptr, st,
+                       W.meta.offsets + E);
     CKL();
   }
   // 4. gate and up products -> g, u [slot, ff].
@@ -484,7 +486,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   // 5. SwiGLU of every slot -> act (f32) and its activation records.
   {
     StageScope ss(ctx, KC_STAGE_QUANT_ACT);
-    launch_act_records(kq_dn, W.g, W.u, nullptr, A, ff, W.arec, A, W.act, W.act16, st);
+    launch_act_records(kq_dn, W.g, W.u, nullptr, A, ff, W.arec, A, W.act, W.act16, st, W.meta.offsets + E);
     CKL();
   }
   // 6. down -> y [slot, d].
@@ -740,6 +742,67 @@ static int ep_rc(kc_ctx* ctx, int rc) {
   return rc == KC_OK ? KC_OK : fail(ctx, rc, "expert parallel: %s", ep_last_error(ctx->ep));
 }
 
+// The expert-parallel layer on decode-sized batches (n_tok within the
+// capacity mapped by kc_ep_reserve): the same steps as ep_pipeline, with every
+// exchange done by this library's kernels over NVLink peer memory -- rows and
+// their selections are stored straight into the owners' arenas, results
+// straight into the home ranks' arenas, each followed by a published sequence
+// number that the receiver waits for on the device. No host synchronisation,
+// no NCCL call. The owner runs its experts on the arena's fixed-capacity
+// layout ([source][capacity] rows; rows beyond a source's count carry no
+// selection).
+static int ep_pipeline_p2p(kc_ctx* ctx, const Layer& L, const float* router, const float* h, int n_tok,
+                           float* out, int32_t* ids_out, float* w_out) {
+  EpState& S = ctx->ep;
+  const int G = S.world, E = L.n_expert, k = L.k, d = L.d, ff = L.ff;
+  const int epr = E / G, T = std::max(n_tok, 1);
+  EpBufs& B = ctx->epb;
+  cudaStream_t st = ctx->stream;
+  if (n_tok > 0) {
+    {
+      StageScope ss(ctx, KC_STAGE_ROUTER_LOGITS);
+      launch_router_logits(router, d, E, d, h, n_tok, ctx->ws.logits, ctx->status, st);
+      CKL();
+    }
+    StageScope ss(ctx, KC_STAGE_ROUTE);
+    launch_route(ctx->ws.logits, n_tok, E, k, L.norm_topk, L.weights_scale, B.ids_home, B.w_home, st);
+    CKL();
+  }
+  const int R = G * S.p2p.T;  // owner-side rows: every source's capacity
+  RC(ep_grow_owner(ctx, R, 1, k, d));
+  ++S.p2p.seq;
+  const EpP2PArgs pa = ep_p2p_args(S, ctx->status);
+  {
+    StageScope ss(ctx, KC_STAGE_DISPATCH);
+    launch_ep_plan(B.ids_home, n_tok, k, G, epr, T, B.send_tok, B.ret_pos, B.xch, st, S.p2p.ret_cap);
+    launch_ep_p2p_send(pa, h, B.ids_home, B.w_home, B.send_tok, B.xch, T, st);
+    launch_ep_p2p_wait(pa, 0, st);
+    launch_ep_p2p_local_ids(pa, L.first_expert, epr, B.ids_loc, B.w_loc, st);
+    CKL();
+  }
+  Work& WO = ctx->ws_ep;
+  RC(ensure_work(ctx, WO, R, epr, k, d, ff));
+  Layer LL = L;
+  LL.n_expert = epr;
+  RC(experts_forward(ctx, WO, LL, epr, 0, reinterpret_cast<const float*>(S.p2p.arena), R, B.ids_loc, B.w_loc, k));
+  launch_ep_p2p_ret_plan(B.ids_loc, G, S.p2p.T, k, B.ret_send_pos, st);
+  launch_ep_p2p_ret_send(pa, WO.y, WO.meta.tok_slot, B.ret_send_pos, st);
+  launch_ep_p2p_wait(pa, 1, st);
+  CKL();
+  if (n_tok > 0) {
+    StageScope ss(ctx, KC_STAGE_COMBINE);
+    launch_combine(reinterpret_cast<const float*>(S.p2p.arena + S.p2p.off_ret), B.ret_pos, B.ids_home, B.w_home,
+                   n_tok, k, d, out, st);
+    CKL();
+  }
+  if (ids_out && n_tok > 0)
+    CK(cudaMemcpyAsync(ids_out, B.ids_home, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
+  if (w_out && n_tok > 0)
+    CK(cudaMemcpyAsync(w_out, B.w_home, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
+  RC(shared_forward(ctx, L, h, n_tok, out));
+  return KC_OK;
+}
+
 // Transformer::moe_ffn with the experts sharded over the group: route this
 // rank's tokens, send each token once to every rank owning one of its
 // experts, run the local experts on the rows received from all ranks, send
@@ -760,6 +823,8 @@ static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const f
   RC(ep_grow_home(ctx, T, k, d));
   EpBufs& B = ctx->epb;
   cudaStream_t st = ctx->stream;
+  if (S.p2p.ready && n_tok <= S.p2p.T && d == S.p2p.d && k == S.p2p.k)
+    return ep_pipeline_p2p(ctx, L, router, h, n_tok, out, ids_out, w_out);
   // 1. route this rank's tokens.
   if (n_tok > 0) {
     {
@@ -1313,6 +1378,24 @@ int kc_ep_init(kc_ctx* ctx, int rank, int world, const char uid[128]) {
   cudaSetDevice(ctx->device);
   int rc = ep_init(ctx->ep, rank, world, uid);
   if (rc != KC_OK) return fail(ctx, rc, "kc_ep_init: %s", ep_last_error(ctx->ep));
+  return KC_OK;
+}
+
+int kc_ep_reserve(kc_ctx* ctx, int max_tokens) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (ctx->ep.world < 2) return fail(ctx, KC_ERR_STATE, "kc_ep_reserve: join an expert-parallel group first");
+  int d = 0, k = 0;
+  for (const auto& [id, L] : ctx->layers)
+    if (L.has_experts) {
+      d = std::max(d, L.d);
+      k = std::max(k, L.k);
+    }
+  if (d == 0 || k == 0) return fail(ctx, KC_ERR_STATE, "kc_ep_reserve: upload the layers and routers first");
+  cudaSetDevice(ctx->device);
+  CK(cudaStreamSynchronize(ctx->stream));
+  const int rc = ep_p2p_setup(ctx->ep, max_tokens, d, k, ctx->stream);
+  if (rc != KC_OK) return fail(ctx, rc, "kc_ep_reserve: %s", ep_last_error(ctx->ep));
   return KC_OK;
 }
 

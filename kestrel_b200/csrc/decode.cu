@@ -43,7 +43,7 @@ constexpr int DMETA = 96;
 // (slot, superblock): lane l owns elements 8l..8l+7.
 template <bool SWIGLU>
 __global__ void q8k_records_kernel(const float* __restrict__ x, const float* __restrict__ u,
-                                   const int* __restrict__ slot_src, int64_t n_slots, int64_t cols,
+                                   const int* __restrict__ slot_src, int64_t n_slots, const int* __restrict__ n_slots_dev, int64_t cols,
                                    uint8_t* __restrict__ rec, int64_t rec_slots, float* __restrict__ f32out,
                                    __half* __restrict__ f16out) {
   pdl_enter();
@@ -51,6 +51,7 @@ __global__ void q8k_records_kernel(const float* __restrict__ x, const float* __r
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (gw >= n_slots * nb) return;
+  if (n_slots_dev && gw / nb >= *n_slots_dev) return;
   const int64_t slot = gw / nb, b = gw % nb;
   const int64_t src = slot_src ? slot_src[slot] : slot;
   const float* xp = x + src * cols + b * 256 + lane * 8;
@@ -108,7 +109,7 @@ __global__ void q8k_records_kernel(const float* __restrict__ x, const float* __r
 // (slot, 32-block).
 template <bool SWIGLU>
 __global__ void q8_records_kernel(const float* __restrict__ x, const float* __restrict__ u,
-                                  const int* __restrict__ slot_src, int64_t n_slots, int64_t cols,
+                                  const int* __restrict__ slot_src, int64_t n_slots, const int* __restrict__ n_slots_dev, int64_t cols,
                                   uint8_t* __restrict__ rec, int64_t rec_slots, float* __restrict__ f32out,
                                   __half* __restrict__ f16out) {
   pdl_enter();
@@ -116,6 +117,7 @@ __global__ void q8_records_kernel(const float* __restrict__ x, const float* __re
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (gw >= n_slots * nb) return;
+  if (n_slots_dev && gw / nb >= *n_slots_dev) return;
   const int64_t slot = gw / nb, b = gw % nb;
   const int64_t src = slot_src ? slot_src[slot] : slot;
   float v = x[src * cols + b * 32 + lane];
@@ -138,16 +140,16 @@ __global__ void q8_records_kernel(const float* __restrict__ x, const float* __re
 
 void launch_act_records(bool kquant, const float* x, const float* u, const int* slot_src, int64_t n_slots,
                         int64_t cols, uint8_t* rec, int64_t rec_slots, float* f32out, __half* f16out,
-                        cudaStream_t st) {
+                        cudaStream_t st, const int* n_slots_dev) {
   const int64_t warps = n_slots * (kquant ? cols / 256 : cols / 32);
   if (warps <= 0) return;
   const int grid = ceil_div(warps, 8);
   if (kquant) {
-    if (u) launch_k(q8k_records_kernel<true>, grid, 256, 0, st, x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
-    else launch_k(q8k_records_kernel<false>, grid, 256, 0, st, x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
+    if (u) launch_k(q8k_records_kernel<true>, grid, 256, 0, st, x, u, slot_src, n_slots, n_slots_dev, cols, rec, rec_slots, f32out, f16out);
+    else launch_k(q8k_records_kernel<false>, grid, 256, 0, st, x, u, slot_src, n_slots, n_slots_dev, cols, rec, rec_slots, f32out, f16out);
   } else {
-    if (u) launch_k(q8_records_kernel<true>, grid, 256, 0, st, x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
-    else launch_k(q8_records_kernel<false>, grid, 256, 0, st, x, u, slot_src, n_slots, cols, rec, rec_slots, f32out, f16out);
+    if (u) launch_k(q8_records_kernel<true>, grid, 256, 0, st, x, u, slot_src, n_slots, n_slots_dev, cols, rec, rec_slots, f32out, f16out);
+    else launch_k(q8_records_kernel<false>, grid, 256, 0, st, x, u, slot_src, n_slots, n_slots_dev, cols, rec, rec_slots, f32out, f16out);
   }
 }
 

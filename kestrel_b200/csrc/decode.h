@@ -61,8 +61,10 @@ int launch_decode(const DecodeArgs& a, int max_units, cudaStream_t st);
 // SwiGLU g / (1 + exp(-g)) * u (x = g, both indexed by slot). Any of rec,
 // f32out (SwiGLU only) and f16out may be null; f32out/f16out are written per
 // slot ([n_slots, cols]).
+// n_slots_dev (optional): device count of the valid slots; slots at or beyond
+// it are skipped (their slot_src entries may be stale).
 void launch_act_records(bool kquant, const float* x, const float* u, const int* slot_src, int64_t n_slots,
                         int64_t cols, uint8_t* rec, int64_t rec_slots, float* f32out, __half* f16out,
-                        cudaStream_t st);
+                        cudaStream_t st, const int* n_slots_dev = nullptr);
 
 }  // namespace kc

@@ -2,6 +2,7 @@
 #include <nccl.h>
 
 #include <cstring>
+#include <vector>
 
 #include "common.cuh"
 #include "ep.h"
@@ -43,6 +44,7 @@ int ep_init(EpState& s, int rank, int world, const char uid[128]) {
 }
 
 void ep_free(EpState& s) {
+  ep_p2p_free(s);
   if (s.comm) ncclCommDestroy(static_cast<ncclComm_t>(s.comm));
   s.comm = nullptr;
   s.world = 1;
@@ -102,7 +104,8 @@ __device__ __forceinline__ void block_scan(const int (&v)[N], int (&ex)[N], int 
 
 __global__ void __launch_bounds__(EP_THREADS) ep_plan_kernel(const int* __restrict__ ids, int n_tok, int k, int G,
                                                               int epr, int T, int* __restrict__ send_tok,
-                                                              int* __restrict__ ret_pos, int* __restrict__ xch_out) {
+                                                              int* __restrict__ ret_pos, int* __restrict__ xch_out,
+                                                              int64_t ret_stride) {
   pdl_enter();
   __shared__ int sh[32 * 2 * kEpMaxWorld];
   __shared__ int base_f[kEpMaxWorld], base_c[kEpMaxWorld], off_c[kEpMaxWorld];
@@ -176,7 +179,7 @@ __global__ void __launch_bounds__(EP_THREADS) ep_plan_kernel(const int* __restri
 #pragma unroll
         for (int q = 0; q < kEpMaxWorld; ++q)
           if (q == r) exc = base_c[q] + ex[kEpMaxWorld + q];
-        ret_pos[(int64_t)s * k + j] = off_c[r] + exc + rank;
+        ret_pos[(int64_t)s * k + j] = (int)((ret_stride > 0 ? r * ret_stride : off_c[r]) + exc + rank);
       }
     }
     __syncthreads();
@@ -191,8 +194,9 @@ __global__ void __launch_bounds__(EP_THREADS) ep_plan_kernel(const int* __restri
 }
 
 void launch_ep_plan(const int* ids, int n_tok, int k, int world, int epr, int T, int* send_tok, int* ret_pos,
-                    int* xch_out, cudaStream_t st) {
-  launch_k(ep_plan_kernel, 1, EP_THREADS, 0, st, ids, n_tok, k, world, epr, T, send_tok, ret_pos, xch_out);
+                    int* xch_out, cudaStream_t st, int64_t ret_stride) {
+  launch_k(ep_plan_kernel, 1, EP_THREADS, 0, st, ids, n_tok, k, world, epr, T, send_tok, ret_pos, xch_out,
+           ret_stride);
 }
 
 // One warp per (destination, row): rows r's section starts at the prefix of
@@ -362,6 +366,277 @@ int ep_alltoallv(EpState& s, const EpA2A* parts, int n_parts, cudaStream_t st) {
     }
   }
   return KC_OK;
+}
+
+
+// ===========================================================================
+// Device-initiated exchange over NVLink peer memory (see ep.h).
+
+static int64_t al256(int64_t v) { return (v + 255) & ~int64_t(255); }
+
+void ep_p2p_free(EpState& s) {
+  EpP2P& p = s.p2p;
+  for (int r = 0; r < kEpMaxWorld; ++r)
+    if (p.peer[r] && p.peer[r] != p.arena) cudaIpcCloseMemHandle(p.peer[r]);
+  if (p.arena) cudaFree(p.arena);
+  if (p.counter) cudaFree(p.counter);
+  p = EpP2P{};
+}
+
+int ep_p2p_setup(EpState& s, int T, int d, int k, cudaStream_t st) {
+  if (s.world < 2 || !s.comm) {
+    s.err = "peer exchange needs an expert-parallel group";
+    return KC_ERR_STATE;
+  }
+  if (T < 1 || d < 4 || d % 4 || k < 1 || k > 64) {
+    s.err = "peer exchange: bad capacity";
+    return KC_ERR_ARG;
+  }
+  ep_p2p_free(s);
+  EpP2P& p = s.p2p;
+  const int G = s.world;
+  p.T = T;
+  p.d = d;
+  p.k = k;
+  p.ret_cap = (int64_t)T * k;
+  p.off_meta = al256((int64_t)G * T * d * 4);
+  p.off_ret = p.off_meta + al256((int64_t)G * T * 2 * k * 4);
+  p.off_lines = p.off_ret + al256((int64_t)G * p.ret_cap * d * 4);
+  p.bytes = p.off_lines + al256((int64_t)G * 2 * 32 * 4);
+  auto fail_cuda = [&](const char* what) {
+    s.err = std::string("peer exchange: ") + what;
+    ep_p2p_free(s);
+    return KC_ERR_CUDA;
+  };
+  if (cudaMalloc(&p.arena, p.bytes) != cudaSuccess) return fail_cuda("arena allocation failed");
+  if (cudaMemsetAsync(p.arena, 0, p.bytes, st) != cudaSuccess) return fail_cuda("arena clear failed");
+  if (cudaMalloc(&p.counter, 2 * sizeof(int)) != cudaSuccess) return fail_cuda("counter allocation failed");
+  if (cudaMemsetAsync(p.counter, 0, 2 * sizeof(int), st) != cudaSuccess) return fail_cuda("counter clear failed");
+  cudaIpcMemHandle_t mine;
+  if (cudaIpcGetMemHandle(&mine, p.arena) != cudaSuccess) return fail_cuda("cudaIpcGetMemHandle failed");
+  // Share the handles (64 bytes each) with an NCCL all-gather.
+  char* dbuf = nullptr;
+  if (cudaMalloc(&dbuf, (size_t)(G + 1) * sizeof(mine)) != cudaSuccess) return fail_cuda("handle buffer");
+  cudaMemcpyAsync(dbuf + G * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice, st);
+  ncclResult_t r = ncclAllGather(dbuf + G * sizeof(mine), dbuf, sizeof(mine), ncclInt8,
+                                 static_cast<ncclComm_t>(s.comm), st);
+  std::vector<cudaIpcMemHandle_t> all(G);
+  if (r == ncclSuccess)
+    cudaMemcpyAsync(all.data(), dbuf, (size_t)G * sizeof(mine), cudaMemcpyDeviceToHost, st);
+  const cudaError_t e = cudaStreamSynchronize(st);
+  cudaFree(dbuf);
+  if (r != ncclSuccess) {
+    s.err = std::string("peer exchange: handle all-gather: ") + ncclGetErrorString(r);
+    ep_p2p_free(s);
+    return KC_ERR_NCCL;
+  }
+  if (e != cudaSuccess) return fail_cuda("handle exchange failed");
+  for (int q = 0; q < G; ++q) {
+    if (q == s.rank) {
+      p.peer[q] = p.arena;
+      continue;
+    }
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+      return fail_cuda("cudaIpcOpenMemHandle failed (GPUs without peer access?)");
+    p.peer[q] = static_cast<uint8_t*>(ptr);
+  }
+  p.seq = 0;
+  p.ready = true;
+  return KC_OK;
+}
+
+EpP2PArgs ep_p2p_args(const EpState& s, int* status) {
+  EpP2PArgs a{};
+  const EpP2P& p = s.p2p;
+  for (int r = 0; r < kEpMaxWorld; ++r) a.peer[r] = p.peer[r];
+  a.world = s.world;
+  a.me = s.rank;
+  a.T = p.T;
+  a.d = p.d;
+  a.k = p.k;
+  a.ret_cap = p.ret_cap;
+  a.off_meta = p.off_meta;
+  a.off_ret = p.off_ret;
+  a.off_lines = p.off_lines;
+  a.seq = p.seq;
+  a.counter = p.counter;
+  a.status = status;
+  return a;
+}
+
+__device__ __forceinline__ uint32_t* ep_line(uint8_t* arena, int64_t off_lines, int src, int which) {
+  return reinterpret_cast<uint32_t*>(arena + off_lines) + (src * 2 + which) * 32;
+}
+
+// The last CTA of a sending grid publishes (count, seq) on every rank's line.
+// Every CTA fences its peer stores at system scope before counting itself.
+__device__ __forceinline__ bool ep_last_cta(int* counter) {
+  __shared__ int last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(counter, 1);
+    last = prev == (int)(gridDim.x * gridDim.y) - 1;
+    if (last) *counter = 0;  // ready for the next launch (nobody else touches it now)
+  }
+  __syncthreads();
+  if (last) __threadfence_system();
+  return last;
+}
+
+__device__ __forceinline__ void ep_publish(uint32_t* line, uint32_t count, uint32_t seq) {
+  volatile uint32_t* v = line;
+  v[1] = count;
+  __threadfence_system();
+  v[0] = seq;
+}
+
+// One warp per (owner r, row i): rows of the home's tokens to r's arena at
+// [me][i], then the last CTA publishes the counts.
+__global__ void ep_p2p_send_kernel(const EpP2PArgs a, const float* __restrict__ h, const int* __restrict__ ids,
+                                   const float* __restrict__ w, const int* __restrict__ send_tok,
+                                   const int* __restrict__ xch_out, int T_home) {
+  pdl_enter();
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  const int r = (int)(gw / T_home), i = (int)(gw % T_home);
+  if (r < a.world && i < xch_out[2 * r]) {
+    const int s = send_tok[(int64_t)r * T_home + i];
+    uint8_t* base = a.peer[r];
+    const int64_t row = (int64_t)a.me * a.T + i;
+    const float4* src = reinterpret_cast<const float4*>(h + (int64_t)s * a.d);
+    float4* dst = reinterpret_cast<float4*>(base) + row * (a.d / 4);
+    for (int c = lane; c < a.d / 4; c += 32) dst[c] = src[c];
+    int32_t* meta = reinterpret_cast<int32_t*>(base + a.off_meta) + row * 2 * a.k;
+    for (int c = lane; c < a.k; c += 32) {
+      meta[c] = ids[(int64_t)s * a.k + c];
+      meta[a.k + c] = __float_as_int(w[(int64_t)s * a.k + c]);
+    }
+  }
+  if (ep_last_cta(a.counter)) {
+    for (int q = threadIdx.x; q < a.world; q += blockDim.x)
+      ep_publish(ep_line(a.peer[q], a.off_lines, a.me, 0), (uint32_t)xch_out[2 * q], a.seq);
+  }
+}
+
+void launch_ep_p2p_send(const EpP2PArgs& a, const float* h, const int* ids, const float* w, const int* send_tok,
+                        const int* xch_out, int T_home, cudaStream_t st) {
+  const int64_t warps = (int64_t)a.world * T_home;
+  launch_k(ep_p2p_send_kernel, ceil_div(std::max<int64_t>(warps, 1) * 32, 256), 256, 0, st, a, h, ids, w, send_tok,
+           xch_out, T_home);
+}
+
+// One thread per source: bounded spin until its line carries this call's
+// sequence number.
+__global__ void ep_p2p_wait_kernel(const EpP2PArgs a, int which) {
+  pdl_enter();
+  const int src = threadIdx.x;
+  if (src >= a.world) return;
+  volatile uint32_t* f = ep_line(a.peer[a.me], a.off_lines, src, which);
+  if ((int)(*f - a.seq) < 0) {
+    const uint64_t t0 = globaltimer();
+    while ((int)(*f - a.seq) < 0) {
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        report(a.status, KC_ERR_TIMEOUT | (W_EP_PEER << 8));
+        break;
+      }
+    }
+  }
+  __threadfence_system();
+}
+
+void launch_ep_p2p_wait(const EpP2PArgs& a, int which, cudaStream_t st) {
+  launch_k(ep_p2p_wait_kernel, 1, 32, 0, st, a, which);
+}
+
+__global__ void ep_p2p_local_ids_kernel(const EpP2PArgs a, int first, int n_local, int* __restrict__ ids_loc,
+                                        float* __restrict__ w_loc) {
+  pdl_enter();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)a.world * a.T * a.k) return;
+  const int64_t row = i / a.k, j = i % a.k;
+  const int src = (int)(row / a.T), r = (int)(row % a.T);
+  const uint32_t cnt = ep_line(a.peer[a.me], a.off_lines, src, 0)[1];
+  const int32_t* meta = reinterpret_cast<const int32_t*>(a.peer[a.me] + a.off_meta) + row * 2 * a.k;
+  const bool valid = (uint32_t)r < cnt;
+  const int e = valid ? meta[j] : -1;
+  ids_loc[i] = (e >= first && e < first + n_local) ? e - first : -1;
+  w_loc[i] = valid ? __int_as_float(meta[a.k + j]) : 0.f;
+}
+
+void launch_ep_p2p_local_ids(const EpP2PArgs& a, int first, int n_local, int* ids_loc, float* w_loc,
+                             cudaStream_t st) {
+  const int64_t n = (int64_t)a.world * a.T * a.k;
+  launch_k(ep_p2p_local_ids_kernel, ceil_div(n, 256), 256, 0, st, a, first, n_local, ids_loc, w_loc);
+}
+
+__global__ void __launch_bounds__(EP_THREADS) ep_p2p_ret_plan_kernel(const int* __restrict__ ids_loc, int world,
+                                                                      int T, int k, int* __restrict__ pos) {
+  pdl_enter();
+  __shared__ int sh[32];
+  __shared__ int base, sec_base[kEpMaxWorld];
+  if (threadIdx.x == 0) base = 0;
+  __syncthreads();
+  const int n = world * T;
+  for (int r0 = 0; r0 < n; r0 += EP_THREADS) {
+    const int q = r0 + threadIdx.x;
+    int c[1] = {0}, ex[1], tot[1];
+    if (q < n)
+      for (int j = 0; j < k; ++j) c[0] += ids_loc[(int64_t)q * k + j] >= 0 ? 1 : 0;
+    block_scan<1>(c, ex, tot, sh);
+    if (q < n && q % T == 0) sec_base[q / T] = base + ex[0];
+    __syncthreads();
+    if (q < n)
+      for (int j = 0; j < k; ++j) {
+        const int e = ids_loc[(int64_t)q * k + j];
+        if (e < 0) {
+          pos[(int64_t)q * k + j] = -1;
+          continue;
+        }
+        int rank = 0;
+        for (int j2 = 0; j2 < k; ++j2) {
+          const int e2 = ids_loc[(int64_t)q * k + j2];
+          rank += (e2 >= 0 && e2 < e) ? 1 : 0;
+        }
+        pos[(int64_t)q * k + j] = base + ex[0] - sec_base[q / T] + rank;
+      }
+    __syncthreads();
+    if (threadIdx.x == 0) base += tot[0];
+    __syncthreads();
+  }
+}
+
+void launch_ep_p2p_ret_plan(const int* ids_loc, int world, int T, int k, int* pos, cudaStream_t st) {
+  launch_k(ep_p2p_ret_plan_kernel, 1, EP_THREADS, 0, st, ids_loc, world, T, k, pos);
+}
+
+// One warp per (row, selection): the result row to its source's arena at
+// [me][pos]; then the last CTA publishes on every source's line [me][1].
+__global__ void ep_p2p_ret_send_kernel(const EpP2PArgs a, const float* __restrict__ y,
+                                       const int* __restrict__ tok_slot, const int* __restrict__ pos) {
+  pdl_enter();
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (gw < (int64_t)a.world * a.T * a.k) {
+    const int p = pos[gw];
+    if (p >= 0 && p < a.ret_cap) {
+      const int src = (int)(gw / a.k / a.T);
+      const float4* s4 = reinterpret_cast<const float4*>(y + (int64_t)tok_slot[gw] * a.d);
+      float4* d4 = reinterpret_cast<float4*>(a.peer[src] + a.off_ret) + ((int64_t)a.me * a.ret_cap + p) * (a.d / 4);
+      for (int c = lane; c < a.d / 4; c += 32) d4[c] = s4[c];
+    }
+  }
+  if (ep_last_cta(a.counter + 1)) {
+    for (int q = threadIdx.x; q < a.world; q += blockDim.x)
+      ep_publish(ep_line(a.peer[q], a.off_lines, a.me, 1), 0u, a.seq);
+  }
+}
+
+void launch_ep_p2p_ret_send(const EpP2PArgs& a, const float* y, const int* tok_slot, const int* pos,
+                            cudaStream_t st) {
+  const int64_t warps = (int64_t)a.world * a.T * a.k;
+  launch_k(ep_p2p_ret_send_kernel, ceil_div(warps * 32, 256), 256, 0, st, a, y, tok_slot, pos);
 }
 
 }  // namespace kc

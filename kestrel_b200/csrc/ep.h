@@ -17,12 +17,64 @@ namespace kc {
 
 constexpr int kEpMaxWorld = 8;
 
+// Device-initiated exchange over NVLink peer memory. Every rank holds an
+// arena (CUDA IPC, mapped by every peer) with fixed capacity: T tokens per
+// source rank. Layout (byte offsets, the same on every rank):
+//   rows [src][T][d] f32 | meta [src][T][2k] i32 (ids, weight bits)
+//   | ret [owner][T * k][d] f32 | lines [src][2][32] u32 (flag, count)
+// Senders store rows / results straight into the peer's arena, then publish
+// (count, sequence number) on the line [sender][0 rows | 1 results].
+struct EpP2P {
+  bool ready = false;
+  int T = 0, d = 0, k = 0;
+  int64_t ret_cap = 0;  // result rows per owner section: T * k
+  int64_t off_meta = 0, off_ret = 0, off_lines = 0, bytes = 0;
+  uint8_t* arena = nullptr;
+  uint8_t* peer[kEpMaxWorld] = {};  // every rank's arena, own included
+  int* counter = nullptr;           // last-CTA counters of the two send kernels
+  uint32_t seq = 0;                 // per-call sequence number, the same on every rank
+};
+
 struct EpState {
   int world = 1;
   int rank = 0;
   void* comm = nullptr;  // ncclComm_t
   std::string err;
+  EpP2P p2p;
 };
+
+// Map the peer arenas for up to T tokens per rank of rows of d values with k
+// selections (collective over the group; replaces an earlier mapping).
+int ep_p2p_setup(EpState& s, int T, int d, int k, cudaStream_t st);
+void ep_p2p_free(EpState& s);
+
+struct EpP2PArgs {
+  uint8_t* peer[kEpMaxWorld];
+  int world, me, T, d, k;
+  int64_t ret_cap, off_meta, off_ret, off_lines;
+  uint32_t seq;
+  int* counter;
+  int* status;
+};
+EpP2PArgs ep_p2p_args(const EpState& s, int* status);
+// Home: store the rows (and meta) for every owner into its arena at
+// [me][i], then publish (count, seq) on each owner's line [me][0].
+void launch_ep_p2p_send(const EpP2PArgs& a, const float* h, const int* ids, const float* w, const int* send_tok,
+                        const int* xch_out, int T_home, cudaStream_t st);
+// Wait (bounded) until every rank has published sequence a.seq on this rank's
+// lines [src][which] (0: rows arrived, 1: results arrived).
+void launch_ep_p2p_wait(const EpP2PArgs& a, int which, cudaStream_t st);
+// Owner: local ids / weights of the arena's rows [src][T] (-1 beyond each
+// source's count and for other owners' experts).
+void launch_ep_p2p_local_ids(const EpP2PArgs& a, int first, int n_local, int* ids_loc, float* w_loc,
+                             cudaStream_t st);
+// Owner: position of (row, selection) in its source's result section: rows of
+// a source in order, each row's local experts ascending (-1: not local).
+void launch_ep_p2p_ret_plan(const int* ids_loc, int world, int T, int k, int* pos, cudaStream_t st);
+// Owner: store every local (row, selection) result row into its source's
+// arena at [me][pos], then publish seq on each source's line [me][1].
+void launch_ep_p2p_ret_send(const EpP2PArgs& a, const float* y, const int* tok_slot, const int* pos,
+                            cudaStream_t st);
 
 int ep_unique_id(char out[128]);
 int ep_init(EpState& s, int rank, int world, const char uid[128]);
@@ -35,8 +87,10 @@ const char* ep_last_error(const EpState& s);
 // from r; ret_pos[s * k + j] = row of (token s, selection j) in the
 // concatenated return buffer (sections in rank order, within a section tokens
 // ascending, within a token its experts owned by r ascending).
+// ret_stride > 0: owner r's section starts at r * ret_stride instead of the
+// prefix of the sections before it (the fixed-capacity arena layout).
 void launch_ep_plan(const int* ids, int n_tok, int k, int world, int epr, int T, int* send_tok, int* ret_pos,
-                    int* xch_out, cudaStream_t st);
+                    int* xch_out, cudaStream_t st, int64_t ret_stride = 0);
 // Pack the rows (and each row's k ids and weights as 2k 32-bit words) sent to
 // every destination into contiguous sections in rank order.
 void launch_ep_pack(const float* h, const int* ids, const float* w, const int* send_tok, const int* xch_out,

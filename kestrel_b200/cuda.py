@@ -54,6 +54,7 @@ SIGNATURES = {
     "kc_upload_shared_expert": (I, [P, I, I, I, I, P, I, P, I, P, P, I]),
     "kc_ep_unique_id": (I, [ctypes.c_char_p]),
     "kc_ep_init": (I, [P, I, I, ctypes.c_char_p]),
+    "kc_ep_reserve": (I, [P, I]),
 }
 
 
@@ -258,6 +259,11 @@ class Context:
 
     def ep_init(self, rank: int, world: int, uid: bytes):
         self._check(lib().kc_ep_init(self.h, rank, world, uid))
+
+    def ep_reserve(self, max_tokens: int):
+        """Collective: map the peer exchange arenas for up to max_tokens tokens
+        per rank and call (after uploading the layers)."""
+        self._check(lib().kc_ep_reserve(self.h, max_tokens))
 
 
 def ep_unique_id() -> bytes:

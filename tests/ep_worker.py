@@ -5,7 +5,10 @@ Every rank builds the same seeded layer, uploads its contiguous block of
 experts and the full router, joins the NCCL group, and runs kc_moe_ffn on its
 own tokens. A second, single-GPU context on the same device holding all the
 experts runs the union of every rank's tokens (rank-major, the order the
-expert-parallel combine reproduces). Top-k ids and weights must be identical;
+expert-parallel combine reproduces). Each rank routes its own tokens, and the
+reference's router product orders its sums by batch size (quant::matmul:
+dot for n < 4, gemm_f32 otherwise), so every case keeps each rank's count on
+the same side of 4 as the union's. Top-k ids and weights must be identical;
 layer outputs must be bit-identical when every expert gets at most 3 rows (the
 int8 path, exact on any grouping) and within the reference's tolerance
 otherwise (the tensor-core path splits K depending on the batch).
@@ -42,12 +45,16 @@ def main():
                        sl(L["t_gate"], L["up"], ff, d), L["t_down"], sl(L["t_down"], L["down"], d, ff),
                        first_expert=blk.first, n_local=blk.count)
     ctx.upload_router(0, L["router"], k)
+    # Calls of up to 32 tokens per rank exchange through peer memory; the
+    # larger case below goes through NCCL.
+    ctx.ep_reserve(32)
     ref = Context(rank)
     ref.upload_experts(0, E, d, ff, L["t_gate"], L["gate"], L["t_gate"], L["up"], L["t_down"], L["down"])
     ref.upload_router(0, L["router"], k)
 
     results = []
-    cases = [[1] * world, [3] + [0] * (world - 1), [16] * world, [64 - 8 * r for r in range(world)], [1] * world]
+    cases = [[1] * world, [3] + [0] * (world - 1), [16] * world, [64 - 8 * r for r in range(world)], [1] * world,
+             [32] * world, [4, 28] + [5] * (world - 2)]
     for ci, ns in enumerate(cases):
         rng = np.random.default_rng(100 + ci)
         h_all = rng.standard_normal((sum(ns), d)).astype(np.float32)
