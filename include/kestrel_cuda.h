@@ -25,6 +25,13 @@
  *   kc_block_sums_dev        the per-superblock integer sums of avx2::dot_q4_k_8k /
  *                            dot_q6_k_8k (crates/kestrel-engine/src/avx2.rs:351-419)
  *   kc_last_error            EngineError's message (transformer.rs:15-27)
+ *   kc_model_init / _tensor  Transformer::new's weight lookup and KV cache
+ *                            (crates/kestrel-engine/src/transformer.rs:147-272)
+ *   kc_model_forward         Transformer::forward (transformer.rs:280-302, 375-467)
+ *   kc_model_generate        the greedy loop of Engine::generate with
+ *                            SamplerConfig::greedy (crates/kestrel-engine/src/
+ *                            lib.rs:116-145, sampler.rs:25-27, 104-112)
+ *   kc_model_truncate        Transformer::truncate (transformer.rs:276-278)
  *
  * Threading: a context is used by one host thread at a time (the reference's
  * Transformer is `&mut self` per forward, transformer.rs:278). One context per
@@ -211,6 +218,65 @@ KC_API int kc_profile_read(kc_ctx* ctx, double* stage_ms, int64_t* stage_calls, 
    without ordering) race, so serialise them. */
 KC_API int kc_route_noalloc(const float* router_w, int n_expert, int d, const float* h, int n_tok, int k,
                             int norm_topk, float weights_scale, int32_t* topk_ids, float* topk_w, void* stream);
+
+/* ---- options ------------------------------------------------------------ */
+enum {
+  /* value 1: products with n >= 4 rows (prefill) run on CUDA cores in f32 on
+     exactly dequantised weights, as quant::matmul's gemm_f32 path does,
+     instead of tcgen05 with f16 operands (0, the default). */
+  KC_OPT_F32_PREFILL = 1
+};
+KC_API int kc_set_option(kc_ctx* ctx, int option, int value);
+
+/* ---- whole model: the dense decode path around the MoE layers ----------
+   Transformer::forward for llama / qwen2 / qwen3 and their MoE variants:
+   embedding rows (quant::get_row), per layer RMSNorm, q/k/v projections
+   (+ biases for qwen2, q/k RMSNorm for qwen3), RoPE (interleaved for llama,
+   NeoX otherwise; angles from the C library's powf/sinf/cosf), an f16 KV
+   cache of n_ctx positions, causal GQA attention, the output projection, the
+   FFN and the residuals; then the final norm, the output head (the embedding
+   when no output tensor is given) and argmax. Routed layers use the experts,
+   router and shared expert uploaded with kc_upload_experts /
+   kc_upload_router / kc_upload_shared_expert under the same layer index;
+   other layers need KC_T_FFN_GATE/UP/DOWN. Prompts are processed in chunks of
+   256 tokens (Transformer::n_batch). */
+enum { KC_ARCH_LLAMA = 0, KC_ARCH_QWEN2 = 1, KC_ARCH_QWEN3 = 2 };
+/* Tensor kinds of a layer (GGUF blk.N.*). Norms and biases are F32 vectors;
+   the matrices are quantized [rows, cols] with GGUF's row-major bytes. */
+enum {
+  KC_T_ATTN_NORM = 0,   /* attn_norm.weight [d]                          */
+  KC_T_ATTN_Q = 1,      /* attn_q.weight [n_head * head_dim, d]          */
+  KC_T_ATTN_K = 2,      /* attn_k.weight [n_head_kv * head_dim, d]       */
+  KC_T_ATTN_V = 3,      /* attn_v.weight [n_head_kv * head_dim, d]       */
+  KC_T_ATTN_OUT = 4,    /* attn_output.weight [d, n_head * head_dim]     */
+  KC_T_ATTN_Q_BIAS = 5, /* attn_q.bias (qwen2)                           */
+  KC_T_ATTN_K_BIAS = 6,
+  KC_T_ATTN_V_BIAS = 7,
+  KC_T_ATTN_Q_NORM = 8, /* attn_q_norm.weight [head_dim] (qwen3)         */
+  KC_T_ATTN_K_NORM = 9,
+  KC_T_FFN_NORM = 10,   /* ffn_norm.weight [d]                           */
+  KC_T_FFN_GATE = 11,   /* dense FFN: ffn_gate / ffn_up [n_ff, d]        */
+  KC_T_FFN_UP = 12,
+  KC_T_FFN_DOWN = 13    /* ffn_down [d, n_ff]                            */
+};
+/* Model tensors (layer = -1). */
+enum { KC_T_TOKEN_EMBD = 0, KC_T_OUTPUT_NORM = 1, KC_T_OUTPUT = 2 };
+
+/* Declare the model (replaces a previous one and its KV cache). */
+KC_API int kc_model_init(kc_ctx* ctx, int n_layer, int d, int n_head, int n_head_kv, int head_dim, int n_vocab,
+                         int n_ctx, int rope_dim, float rope_base, float rms_eps, int arch);
+KC_API int kc_model_tensor(kc_ctx* ctx, int layer, int kind, int t, const void* w, int64_t rows, int64_t cols,
+                           int src_on_device);
+/* Feed n tokens after the cached ones; logits [n_vocab] of the last token
+   and/or its argmax (either may be NULL). Host buffers; synchronous. */
+KC_API int kc_model_forward(kc_ctx* ctx, const uint32_t* tokens, int n, float* logits, uint32_t* next_token);
+/* Greedy decode: forward the prompt, then n_gen tokens, each step's argmax
+   fed to the next step from device memory (no host round trip per token).
+   out_tokens [n_gen]. */
+KC_API int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, int n_gen, uint32_t* out_tokens);
+/* Forget cached positions from `keep` on; kc_model_cached = positions held. */
+KC_API int kc_model_truncate(kc_ctx* ctx, int keep);
+KC_API int kc_model_cached(const kc_ctx* ctx);
 
 /* ---- expert parallelism (one process per GPU, NCCL over NVLink) -------- */
 

@@ -17,6 +17,7 @@
 #include "ep.h"
 #include "kernels.h"
 #include "mma.h"
+#include "model.h"
 
 using namespace kc;
 
@@ -131,8 +132,18 @@ struct Prof {
   }
 };
 
+struct Model;  // the dense decode path of a whole model (kc_model_*)
+
 struct kc_ctx {
   int device = 0;
+  // n >= 4 products on CUDA cores in f32 instead of tcgen05 with f16
+  // operands (KC_OPT_F32_PREFILL).
+  bool f32_prefill = false;
+  Model* model = nullptr;
+  // Auxiliary stream for the n >= 4 products that run beside the int8 ones,
+  // and the fork / join events (created on first use).
+  cudaStream_t aux = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   cudaStream_t stream = nullptr;
   bool own_stream = false;
   int* status = nullptr;  // device word written by kernels on timeout
@@ -348,6 +359,14 @@ int upload_matrix(kc_ctx* ctx, int t, const void* src, int64_t n_mats, int64_t r
   return KC_OK;
 }
 
+int ensure_aux(kc_ctx* ctx) {
+  if (ctx->aux) return KC_OK;
+  CK(cudaStreamCreateWithFlags(&ctx->aux, cudaStreamNonBlocking));
+  CK(cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming));
+  CK(cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming));
+  return KC_OK;
+}
+
 GroupedArgs grouped_base(kc_ctx* ctx) {
   GroupedArgs a{};
   a.status = ctx->status;
@@ -400,44 +419,52 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     RC(launch_dispatch(ids, wts, n_rows, k, E, W.meta, st));
     CKL();
   }
-  // 3. activation records of every slot's input row (int8 path) and its f16
-  //    copy (tensor-core path).
   const bool kq_in = is_k(L.t_gate), kq_dn = is_k(L.t_down);
   const int A = n_rows * k;
   const int max_small = std::min(E, A);
-  const bool mma_gu = mma_supported(L.t_gate, d, 2);
+  // An expert holds at most one row per token, so with fewer than 4 rows no
+  // expert reaches the n >= 4 path and its launches are skipped.
+  const bool any_large = n_rows >= 4;
+  const bool mma_gu = !ctx->f32_prefill && mma_supported(L.t_gate, d, 2);
+  const bool mma_dn = !ctx->f32_prefill && mma_supported(L.t_down, ff, 1) && ff % 256 == 0;
+  const int max_tt = ceil_div(A, kMmaTileN) + std::min(E, A / 4);
+  // The int8 (1-3 rows) and n >= 4 launches of a stage are independent: the
+  // n >= 4 one runs on the auxiliary stream, concurrently, and the int8 kernel
+  // leaves it `split` SMs (the rest of its grid queues for the SMs the int8
+  // kernel frees). The split follows the expected weight bytes of each path,
+  // with routing modelled as uniform (rows per expert ~ Poisson(A / E)).
+  int split = 0;
+  const bool fork = any_large && !ctx->prof.on;
+  if (fork) {
+    RC(ensure_aux(ctx));
+    const double lam = (double)A / E, p0 = std::exp(-lam);
+    const double f_small = p0 * (lam + lam * lam / 2 + lam * lam * lam / 6), f_large = std::max(0.0, 1 - p0 - f_small);
+    const int nsm = num_sms();
+    split = std::min(nsm - 8, std::max(8, (int)std::lround(nsm * f_large / std::max(1e-9, f_small + f_large))));
+  }
+  const int dec_ctas = num_sms() - split;
+  auto fork_aux = [&]() -> int {
+    CK(cudaEventRecord(ctx->ev_fork, st));
+    CK(cudaStreamWaitEvent(ctx->aux, ctx->ev_fork, 0));
+    return KC_OK;
+  };
+  auto join_aux = [&]() -> int {
+    CK(cudaEventRecord(ctx->ev_join, ctx->aux));
+    CK(cudaStreamWaitEvent(st, ctx->ev_join, 0));
+    return KC_OK;
+  };
+  cudaStream_t lst = fork ? ctx->aux : st;  // stream of the n >= 4 launches
+  // 3. activation records of every slot's input row (int8 path) and its f16
+  //    copy (tensor-core path).
   {
     StageScope ss(ctx, KC_STAGE_QUANT_X);
-    launch_act_records(kq_in, h, nullptr, W.meta.slot_tok, A, d, W.xrec, A, nullptr, mma_gu ? W.x16 : nullptr, st,
-                       W.meta.offsets + E);
+    launch_act_records(kq_in, h, nullptr, W.meta.slot_tok, A, d, W.xrec, A, nullptr,
+                       mma_gu && any_large ? W.x16 : nullptr, st, W.meta.offsets + E);
     CKL();
   }
   // 4. gate and up products -> g, u [slot, ff].
-  {
-    StageScope ss(ctx, KC_STAGE_GATE_UP_INT8);
-    DecodeArgs dg{};
-    dg.w[0] = L.gate;
-    dg.w[1] = L.up;
-    dg.n_mat = 2;
-    dg.expert_stride = L.mb_gate;
-    dg.expert_base = ebase;
-    dg.rows = ff;
-    dg.cols = d;
-    dg.type = L.t_gate;
-    dg.list = W.meta.small_list;
-    dg.n_list = W.meta.n_lists;
-    dg.offsets = W.meta.offsets;
-    dg.rec = W.xrec;
-    dg.rec_slots = A;
-    dg.out[0] = W.g;
-    dg.out[1] = W.u;
-    dg.out_stride = ff;
-    dg.status = ctx->status;
-    RC(launch_decode(dg, max_small * 2 * ceil_div(ff, kTileRows), st));
-    CKL();
-  }
-  const int max_tt = ceil_div(A, kMmaTileN) + std::min(E, A / 4);
-  if (mma_gu) {
+  if (fork) RC(fork_aux());
+  if (any_large && mma_gu) {
     StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
     alignas(64) unsigned char tmap[128];
     if (make_tmap_f16(tmap, W.x16, A, d) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
@@ -460,9 +487,9 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.out[1] = W.u;
     ma.out_stride = ff;
     ma.status = ctx->status;
-    RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(ff, 128), st));
+    RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(ff, 128), lst));
     CKL();
-  } else {
+  } else if (any_large) {
     GroupedArgs g = grouped_base(ctx);
     g.w0 = L.gate;
     g.w1 = L.up;
@@ -480,38 +507,44 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     g.list = W.meta.large_list;
     g.n_list = W.meta.n_lists + 1;
     StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
-    RC(launch_grouped_f32(g, true, std::min(E, A / 4), n_rows, st));
+    RC(launch_grouped_f32(g, true, std::min(E, A / 4), n_rows, lst));
     CKL();
   }
+  {
+    StageScope ss(ctx, KC_STAGE_GATE_UP_INT8);
+    DecodeArgs dg{};
+    dg.w[0] = L.gate;
+    dg.w[1] = L.up;
+    dg.n_mat = 2;
+    dg.expert_stride = L.mb_gate;
+    dg.expert_base = ebase;
+    dg.rows = ff;
+    dg.cols = d;
+    dg.type = L.t_gate;
+    dg.list = W.meta.small_list;
+    dg.n_list = W.meta.n_lists;
+    dg.offsets = W.meta.offsets;
+    dg.n_experts = E;
+    dg.rec = W.xrec;
+    dg.rec_slots = A;
+    dg.out[0] = W.g;
+    dg.out[1] = W.u;
+    dg.out_stride = ff;
+    dg.status = ctx->status;
+    RC(launch_decode(dg, max_small * 2 * ceil_div(ff, kTileRows), st, dec_ctas));
+    CKL();
+  }
+  if (fork) RC(join_aux());
   // 5. SwiGLU of every slot -> act (f32) and its activation records.
   {
     StageScope ss(ctx, KC_STAGE_QUANT_ACT);
-    launch_act_records(kq_dn, W.g, W.u, nullptr, A, ff, W.arec, A, W.act, W.act16, st, W.meta.offsets + E);
+    launch_act_records(kq_dn, W.g, W.u, nullptr, A, ff, W.arec, A, any_large ? W.act : nullptr,
+                       any_large && mma_dn ? W.act16 : nullptr, st, W.meta.offsets + E);
     CKL();
   }
   // 6. down -> y [slot, d].
-  {
-    StageScope ss(ctx, KC_STAGE_DOWN_INT8);
-    DecodeArgs dd{};
-    dd.w[0] = L.down;
-    dd.n_mat = 1;
-    dd.expert_stride = L.mb_down;
-    dd.expert_base = ebase;
-    dd.rows = d;
-    dd.cols = ff;
-    dd.type = L.t_down;
-    dd.list = W.meta.small_list;
-    dd.n_list = W.meta.n_lists;
-    dd.offsets = W.meta.offsets;
-    dd.rec = W.arec;
-    dd.rec_slots = A;
-    dd.out[0] = W.y;
-    dd.out_stride = d;
-    dd.status = ctx->status;
-    RC(launch_decode(dd, max_small * ceil_div(d, kTileRows), st));
-    CKL();
-  }
-  if (mma_supported(L.t_down, ff, 1) && ff % 256 == 0) {
+  if (fork) RC(fork_aux());
+  if (any_large && mma_dn) {
     StageScope ss(ctx, KC_STAGE_DOWN_F32);
     alignas(64) unsigned char tmap[128];
     if (make_tmap_f16(tmap, W.act16, A, ff) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (act16) failed");
@@ -532,9 +565,9 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.out[0] = W.y;
     ma.out_stride = d;
     ma.status = ctx->status;
-    RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(d, 128), st));
+    RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(d, 128), lst));
     CKL();
-  } else {
+  } else if (any_large) {
     GroupedArgs dn = grouped_base(ctx);
     dn.w0 = L.down;
     dn.expert_stride = L.mb_down;
@@ -550,9 +583,32 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     dn.list = W.meta.large_list;
     dn.n_list = W.meta.n_lists + 1;
     StageScope ss(ctx, KC_STAGE_DOWN_F32);
-    RC(launch_grouped_f32(dn, false, std::min(E, A / 4), n_rows, st));
+    RC(launch_grouped_f32(dn, false, std::min(E, A / 4), n_rows, lst));
     CKL();
   }
+  {
+    StageScope ss(ctx, KC_STAGE_DOWN_INT8);
+    DecodeArgs dd{};
+    dd.w[0] = L.down;
+    dd.n_mat = 1;
+    dd.expert_stride = L.mb_down;
+    dd.expert_base = ebase;
+    dd.rows = d;
+    dd.cols = ff;
+    dd.type = L.t_down;
+    dd.list = W.meta.small_list;
+    dd.n_list = W.meta.n_lists;
+    dd.offsets = W.meta.offsets;
+    dd.n_experts = E;
+    dd.rec = W.arec;
+    dd.rec_slots = A;
+    dd.out[0] = W.y;
+    dd.out_stride = d;
+    dd.status = ctx->status;
+    RC(launch_decode(dd, max_small * ceil_div(d, kTileRows), st, dec_ctas));
+    CKL();
+  }
+  if (fork) RC(join_aux());
   return KC_OK;
 }
 
@@ -599,13 +655,14 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     dv.list = W.meta.small_list;
     dv.n_list = W.meta.n_lists;
     dv.offsets = W.meta.offsets;
+    dv.n_experts = 1;
     dv.rec = W.xrec;
     dv.rec_slots = n;
     dv.out[0] = out;
     dv.out_stride = D.rows;
     dv.status = ctx->status;
     RC(launch_decode(dv, ceil_div(D.rows, kTileRows), st));
-  } else if (mma_supported(D.t, D.cols, 1)) {
+  } else if (!ctx->f32_prefill && mma_supported(D.t, D.cols, 1)) {
     launch_act_records(is_k(D.t), x, nullptr, nullptr, n, D.cols, nullptr, n, nullptr, W.x16, st);
     CKL();
     alignas(64) unsigned char tmap[128];
@@ -948,6 +1005,249 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
 }
 
 // ===========================================================================
+// The dense decode path of a whole model (Transformer::forward,
+// transformer.rs:287-302, 375-467): embedding rows, per layer RMSNorm ->
+// q/k/v -> bias / q-k norm / RoPE -> f16 KV cache -> causal GQA attention ->
+// output projection -> residual -> RMSNorm -> FFN (routed experts through
+// moe_pipeline, or dense SwiGLU) -> residual; then the final norm, the output
+// head and argmax. The matvecs go through dense_forward (quant::matmul's
+// dispatch), so decode steps run the int8 path bit for bit.
+constexpr int kModelBatch = 256;  // Transformer::n_batch (transformer.rs:269)
+
+struct Model {
+  int n_layer = 0, d = 0, nh = 0, nkv = 0, hd = 0, n_vocab = 0, n_ctx = 0, rd = 0, arch = 0;
+  float eps = 0.f, rope_base = 0.f;
+  struct Lay {
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *qn = nullptr, *kn = nullptr;
+    float *bq = nullptr, *bk = nullptr, *bv = nullptr;
+    Dense q, k, v, o, qkv, gate, up, down;
+  };
+  std::vector<Lay> L;
+  uint8_t* embd = nullptr;  // raw GGUF rows (get_row)
+  int embd_t = -1;
+  int64_t embd_rb = 0;
+  float* out_norm = nullptr;
+  Dense output;
+  bool ready = false;
+  __half* kc = nullptr;  // [n_layer][n_ctx][nkv * hd]
+  __half* vc = nullptr;
+  float2* rope = nullptr;  // [n_ctx][rd / 2] (sin, cos)
+  int cached = 0;
+  // Activations for up to T tokens per forward chunk.
+  int T = 0, F = 0;
+  float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *tmp = nullptr, *ffn = nullptr;
+  float *g = nullptr, *u = nullptr, *logits = nullptr;
+  uint32_t* tok = nullptr;  // [T]
+  uint32_t* next = nullptr; // argmax result
+  int64_t bytes = 0;
+};
+
+void free_dense(kc_ctx* ctx, Dense& D) {
+  if (D.w) cudaFree(D.w);
+  D = Dense{};
+  (void)ctx;
+}
+
+void model_free(kc_ctx* ctx) {
+  Model* m = ctx->model;
+  if (!m) return;
+  for (auto& l : m->L) {
+    for (float* v : {l.attn_norm, l.ffn_norm, l.qn, l.kn, l.bq, l.bk, l.bv}) cudaFree(v);
+    for (Dense* D : {&l.q, &l.k, &l.v, &l.o, &l.qkv, &l.gate, &l.up, &l.down}) free_dense(ctx, *D);
+  }
+  cudaFree(m->embd);
+  cudaFree(m->out_norm);
+  free_dense(ctx, m->output);
+  cudaFree(m->kc);
+  cudaFree(m->vc);
+  cudaFree(m->rope);
+  for (void* p : {(void*)m->x, (void*)m->h, (void*)m->qkv, (void*)m->q, (void*)m->att, (void*)m->tmp,
+                  (void*)m->ffn, (void*)m->g, (void*)m->u, (void*)m->logits, (void*)m->tok, (void*)m->next})
+    cudaFree(p);
+  delete m;
+  ctx->model = nullptr;
+}
+
+int model_dense(kc_ctx* ctx, Dense& D, int t, const void* w, int64_t rows, int64_t cols, bool on_dev) {
+  free_dense(ctx, D);
+  D.t = t;
+  D.rows = rows;
+  D.cols = cols;
+  D.rs = round16(cols * 4);
+  CK(cudaMalloc(&D.w, dev_matrix_bytes(t, rows, cols)));
+  RC(upload_matrix(ctx, t, w, 1, rows, cols, D.w, on_dev));
+  return KC_OK;
+}
+
+int model_vec(kc_ctx* ctx, float*& dst, const void* w, int64_t n, bool on_dev) {
+  cudaFree(dst);
+  dst = nullptr;
+  CK(cudaMalloc(&dst, n * 4));
+  CK(cudaMemcpyAsync(dst, w, n * 4, on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->stream));
+  return KC_OK;
+}
+
+// Activation buffers for T tokens.
+int model_buffers(kc_ctx* ctx, Model& m, int T) {
+  int F = 256;
+  for (auto& l : m.L)
+    if (l.gate.w) F = std::max<int>(F, (int)l.gate.rows);
+  if (T <= m.T && F <= m.F) return KC_OK;
+  T = std::max(T, m.T);
+  CK(cudaStreamSynchronize(ctx->stream));
+  for (void* p : {(void*)m.x, (void*)m.h, (void*)m.qkv, (void*)m.q, (void*)m.att, (void*)m.tmp, (void*)m.ffn,
+                  (void*)m.g, (void*)m.u, (void*)m.tok})
+    cudaFree(p);
+  const int width = (m.nh + 2 * m.nkv) * m.hd;
+  CK(cudaMalloc(&m.x, (size_t)T * m.d * 4));
+  CK(cudaMalloc(&m.h, (size_t)T * m.d * 4));
+  CK(cudaMalloc(&m.qkv, (size_t)T * width * 4));
+  CK(cudaMalloc(&m.q, (size_t)T * m.nh * m.hd * 4));
+  CK(cudaMalloc(&m.att, (size_t)T * m.nh * m.hd * 4));
+  CK(cudaMalloc(&m.tmp, (size_t)T * m.d * 4));
+  CK(cudaMalloc(&m.ffn, (size_t)T * m.d * 4));
+  CK(cudaMalloc(&m.g, (size_t)T * F * 4));
+  CK(cudaMalloc(&m.u, (size_t)T * F * 4));
+  CK(cudaMalloc(&m.tok, (size_t)T * 4));
+  m.T = T;
+  m.F = F;
+  return KC_OK;
+}
+
+// First forward: check the tensors, fuse q/k/v into one matrix where their
+// types and row lengths agree (each row's arithmetic is unchanged), tie the
+// output head to the embedding if there is no output tensor.
+int model_finalize(kc_ctx* ctx, Model& m) {
+  if (m.ready) return KC_OK;
+  if (!m.embd || !m.out_norm) return fail(ctx, KC_ERR_STATE, "kc_model_forward: embedding or output norm missing");
+  if (!m.output.w) {
+    RC(model_dense(ctx, m.output, m.embd_t, m.embd, m.n_vocab, m.d, true));
+  }
+  for (int l = 0; l < m.n_layer; ++l) {
+    Model::Lay& y = m.L[l];
+    if (!y.attn_norm || !y.ffn_norm || !y.q.w || !y.k.w || !y.v.w || !y.o.w)
+      return fail(ctx, KC_ERR_STATE, "kc_model_forward: layer %d lacks an attention tensor or a norm", l);
+    // A layer with dense FFN tensors is dense; otherwise it needs routed experts.
+    const bool dense = y.gate.w || y.up.w || y.down.w;
+    const bool moe = !dense && ctx->layers.count(l) && ctx->layers[l].has_experts && ctx->layers[l].has_router;
+    if (dense && !(y.gate.w && y.up.w && y.down.w))
+      return fail(ctx, KC_ERR_STATE, "kc_model_forward: layer %d lacks a dense FFN tensor", l);
+    if (!dense && !moe)
+      return fail(ctx, KC_ERR_STATE, "kc_model_forward: layer %d has neither routed experts nor a dense FFN", l);
+    if (moe && ctx->layers[l].d != m.d) return fail(ctx, KC_ERR_SHAPE, "kc_model_forward: layer %d expert d", l);
+    if (moe && ctx->ep.world <= 1 && ctx->layers[l].n_local != ctx->layers[l].n_expert)
+      return fail(ctx, KC_ERR_STATE, "kc_model_forward: layer %d holds an expert shard outside an expert-parallel "
+                                     "group", l);
+    if (dense && (y.gate.cols != m.d || y.up.rows != y.gate.rows || y.down.rows != m.d || y.down.cols != y.gate.rows))
+      return fail(ctx, KC_ERR_SHAPE, "kc_model_forward: layer %d dense FFN shapes", l);
+    if (y.q.rows != (int64_t)m.nh * m.hd || y.k.rows != (int64_t)m.nkv * m.hd || y.v.rows != (int64_t)m.nkv * m.hd ||
+        y.q.cols != m.d || y.o.rows != m.d || y.o.cols != (int64_t)m.nh * m.hd)
+      return fail(ctx, KC_ERR_SHAPE, "kc_model_forward: layer %d attention shapes", l);
+    const bool fuse = y.q.t == y.k.t && y.q.t == y.v.t && y.k.cols == y.q.cols && y.v.cols == y.q.cols &&
+                      (y.q.t == T_F32 || (y.q.rows % kTileRows == 0 && y.k.rows % kTileRows == 0));
+    if (!fuse) return fail(ctx, KC_ERR_SHAPE, "kc_model_forward: layer %d q/k/v differ in type or shape", l);
+    free_dense(ctx, y.qkv);
+    y.qkv.t = y.q.t;
+    y.qkv.rows = y.q.rows + y.k.rows + y.v.rows;
+    y.qkv.cols = y.q.cols;
+    y.qkv.rs = y.q.rs;
+    const int64_t bq = dev_matrix_bytes(y.q.t, y.q.rows, y.q.cols), bk = dev_matrix_bytes(y.k.t, y.k.rows, y.k.cols);
+    CK(cudaMalloc(&y.qkv.w, dev_matrix_bytes(y.qkv.t, y.qkv.rows, y.qkv.cols)));
+    CK(cudaMemcpyAsync(y.qkv.w, y.q.w, bq, cudaMemcpyDeviceToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(y.qkv.w + bq, y.k.w, bk, cudaMemcpyDeviceToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(y.qkv.w + bq + bk, y.v.w, bk, cudaMemcpyDeviceToDevice, ctx->stream));
+  }
+  CK(cudaStreamSynchronize(ctx->stream));
+  m.ready = true;
+  return KC_OK;
+}
+
+// One forward chunk of n tokens already in m.tok; logits of the last token
+// in m.logits and its argmax in m.next.
+int model_chunk(kc_ctx* ctx, Model& m, int n) {
+  cudaStream_t st = ctx->stream;
+  const int d = m.d, pos0 = m.cached;
+  const float scale = 1.0f / std::sqrt((float)m.hd);  // transformer.rs:598
+  launch_embed(m.embd, m.embd_t, m.embd_rb, m.tok, n, d, m.n_vocab, m.x, ctx->status, st);
+  CKL();
+  const float* resid = nullptr;  // the previous FFN output, added before the next norm
+  for (int l = 0; l < m.n_layer; ++l) {
+    Model::Lay& y = m.L[l];
+    launch_add_rmsnorm(m.x, resid, y.attn_norm, n, d, m.eps, m.h, st);
+    CKL();
+    RC(dense_forward(ctx, y.qkv, m.h, n, m.qkv));
+    QkPostArgs qa{};
+    qa.qkv = m.qkv;
+    qa.n = n;
+    qa.nh = m.nh;
+    qa.nkv = m.nkv;
+    qa.hd = m.hd;
+    qa.rd = m.rd;
+    qa.pos0 = pos0;
+    qa.neox = m.arch != KC_ARCH_LLAMA;
+    qa.eps = m.eps;
+    qa.bq = y.bq;
+    qa.bk = y.bk;
+    qa.bv = y.bv;
+    qa.qn = y.qn;
+    qa.kn = y.kn;
+    qa.rope = m.rope;
+    qa.q_out = m.q;
+    const size_t cache_off = (size_t)l * m.n_ctx * m.nkv * m.hd;
+    qa.kc = m.kc + cache_off;
+    qa.vc = m.vc + cache_off;
+    launch_qk_post(qa, st);
+    CKL();
+    launch_attention(m.q, qa.kc, qa.vc, n, m.nh, m.nkv, m.hd, pos0, scale, m.att, st);
+    CKL();
+    RC(dense_forward(ctx, y.o, m.att, n, m.tmp));
+    launch_add_rmsnorm(m.x, m.tmp, y.ffn_norm, n, d, m.eps, m.h, st);
+    CKL();
+    if (!y.gate.w) {  // routed experts (checked in model_finalize)
+      const Layer& R = ctx->layers[l];
+      RC(moe_pipeline(ctx, R, R.router, m.h, n, m.ffn, nullptr, nullptr));
+    } else {
+      RC(dense_forward(ctx, y.gate, m.h, n, m.g));
+      RC(dense_forward(ctx, y.up, m.h, n, m.u));
+      launch_swiglu(m.g, m.u, (int64_t)n * y.gate.rows, st);
+      CKL();
+      RC(dense_forward(ctx, y.down, m.g, n, m.ffn));
+    }
+    resid = m.ffn;
+  }
+  // Final norm of the last row only (transformer.rs:459-466).
+  const int64_t last = (int64_t)(n - 1) * d;
+  launch_add_rmsnorm(m.x + last, resid + last, m.out_norm, 1, d, m.eps, m.h, st);
+  CKL();
+  RC(dense_forward(ctx, m.output, m.h, 1, m.logits));
+  launch_argmax(m.logits, m.n_vocab, m.next, st);
+  CKL();
+  m.cached += n;
+  return KC_OK;
+}
+
+int model_forward(kc_ctx* ctx, const uint32_t* tokens, bool tokens_on_dev, int n) {
+  Model& m = *ctx->model;
+  RC(model_finalize(ctx, m));
+  if (n < 1) return fail(ctx, KC_ERR_ARG, "kc_model_forward: forward() needs at least one token");
+  if (m.cached + n > m.n_ctx)
+    return fail(ctx, KC_ERR_ARG, "kc_model_forward: context full: %d positions needed, n_ctx = %d", m.cached + n,
+                m.n_ctx);
+  if (!tokens_on_dev)
+    for (int i = 0; i < n; ++i)
+      if (tokens[i] >= (uint32_t)m.n_vocab)
+        return fail(ctx, KC_ERR_ARG, "kc_model_forward: token id %u out of range", tokens[i]);
+  for (int c = 0; c < n; c += kModelBatch) {  // n_batch chunks (transformer.rs:293)
+    const int nc = std::min(kModelBatch, n - c);
+    RC(model_buffers(ctx, m, nc));
+    CK(cudaMemcpyAsync(m.tok, tokens + c, (size_t)nc * 4,
+                       tokens_on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->stream));
+    RC(model_chunk(ctx, m, nc));
+  }
+  return KC_OK;
+}
+
+// ===========================================================================
 extern "C" {
 
 int kc_init(int device, kc_ctx** out) {
@@ -979,6 +1279,7 @@ void kc_free(kc_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  model_free(ctx);
   ep_free(ctx->ep);
   ep_free_bufs(ctx->epb);
   for (auto& [id, L] : ctx->layers) {
@@ -1000,6 +1301,12 @@ void kc_free(kc_ctx* ctx) {
   cudaFree(ctx->ws.arena);
   cudaFree(ctx->ws_ep.arena);
   cudaFree(ctx->status);
+  if (ctx->aux) {
+    cudaStreamSynchronize(ctx->aux);
+    cudaStreamDestroy(ctx->aux);
+    cudaEventDestroy(ctx->ev_fork);
+    cudaEventDestroy(ctx->ev_join);
+  }
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
 }
@@ -1398,5 +1705,177 @@ int kc_ep_reserve(kc_ctx* ctx, int max_tokens) {
   if (rc != KC_OK) return fail(ctx, rc, "kc_ep_reserve: %s", ep_last_error(ctx->ep));
   return KC_OK;
 }
+
+// ---- whole model (dense decode path) ---------------------------------------
+int kc_set_option(kc_ctx* ctx, int option, int value) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (option == KC_OPT_F32_PREFILL) {
+    ctx->f32_prefill = value != 0;
+    return KC_OK;
+  }
+  return fail(ctx, KC_ERR_ARG, "kc_set_option: unknown option %d", option);
+}
+
+int kc_model_init(kc_ctx* ctx, int n_layer, int d, int n_head, int n_head_kv, int head_dim, int n_vocab, int n_ctx,
+                  int rope_dim, float rope_base, float rms_eps, int arch) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (n_layer < 1 || d < 1 || n_head < 1 || n_head_kv < 1 || n_head % n_head_kv || head_dim < 1 ||
+      head_dim > 256 || n_vocab < 1 || n_ctx < 1 || rope_dim < 0 || rope_dim > head_dim || rope_dim % 2 ||
+      arch < KC_ARCH_LLAMA || arch > KC_ARCH_QWEN3)
+    return fail(ctx, KC_ERR_ARG, "kc_model_init: bad hyper-parameters");
+  cudaSetDevice(ctx->device);
+  model_free(ctx);
+  Model* m = new Model();
+  ctx->model = m;
+  m->n_layer = n_layer; m->d = d; m->nh = n_head; m->nkv = n_head_kv; m->hd = head_dim; m->n_vocab = n_vocab;
+  m->n_ctx = n_ctx; m->rd = rope_dim; m->rope_base = rope_base; m->eps = rms_eps; m->arch = arch;
+  m->L.resize(n_layer);
+  const size_t cache = (size_t)n_layer * n_ctx * n_head_kv * head_dim;
+  CK(cudaMalloc(&m->kc, cache * 2));
+  CK(cudaMalloc(&m->vc, cache * 2));
+  CK(cudaMemsetAsync(m->kc, 0, cache * 2, ctx->stream));
+  CK(cudaMemsetAsync(m->vc, 0, cache * 2, ctx->stream));
+  // RoPE angles on the host with the C library's powf / sinf / cosf, as Rust's
+  // f32::powf / sin_cos call them (transformer.rs:248, 350).
+  const int half = std::max(1, rope_dim / 2);
+  std::vector<float> inv(half);
+  for (int i = 0; i < rope_dim / 2; ++i) inv[i] = std::pow(rope_base, -(2.0f * (float)i) / (float)rope_dim);
+  std::vector<float2> tab((size_t)n_ctx * half);
+  for (int p = 0; p < n_ctx; ++p)
+    for (int i = 0; i < rope_dim / 2; ++i) {
+      const float a = (float)p * inv[i];
+      tab[(size_t)p * half + i] = make_float2(std::sin(a), std::cos(a));
+    }
+  CK(cudaMalloc(&m->rope, tab.size() * sizeof(float2)));
+  CK(cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&m->logits, (size_t)n_vocab * 4));
+  CK(cudaMalloc(&m->next, 4));
+  m->bytes = (int64_t)cache * 4 + (int64_t)tab.size() * 8;
+  return KC_OK;
+}
+
+int kc_model_tensor(kc_ctx* ctx, int layer, int kind, int t, const void* w, int64_t rows, int64_t cols,
+                    int src_on_device) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  Model* m = ctx->model;
+  if (!m) return fail(ctx, KC_ERR_STATE, "kc_model_tensor: call kc_model_init first");
+  if (!w || rows < 1 || cols < 1) return fail(ctx, KC_ERR_ARG, "kc_model_tensor: bad arguments");
+  if (!type_ok(t) && t != T_F32) return fail(ctx, KC_ERR_TYPE, "kc_model_tensor: type %d has no kernel", t);
+  if (cols % block_elems(t)) return fail(ctx, KC_ERR_SHAPE, "kc_model_tensor: cols %lld", (long long)cols);
+  cudaSetDevice(ctx->device);
+  const bool on_dev = src_on_device != 0;
+  m->ready = false;
+  if (layer < 0) {
+    switch (kind) {
+      case KC_T_TOKEN_EMBD:
+        if (cols != m->d || rows != m->n_vocab) return fail(ctx, KC_ERR_SHAPE, "kc_model_tensor: embedding shape");
+        cudaFree(m->embd);
+        m->embd_t = t;
+        m->embd_rb = gguf_row_bytes(t, cols);
+        CK(cudaMalloc(&m->embd, rows * m->embd_rb));
+        CK(cudaMemcpy(m->embd, w, rows * m->embd_rb, on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+        return KC_OK;
+      case KC_T_OUTPUT_NORM:
+        if (t != T_F32 || rows * cols != m->d) return fail(ctx, KC_ERR_SHAPE, "kc_model_tensor: output norm");
+        RC(model_vec(ctx, m->out_norm, w, m->d, on_dev));
+        break;
+      case KC_T_OUTPUT:
+        if (cols != m->d || rows != m->n_vocab) return fail(ctx, KC_ERR_SHAPE, "kc_model_tensor: output shape");
+        RC(model_dense(ctx, m->output, t, w, rows, cols, on_dev));
+        break;
+      default:
+        return fail(ctx, KC_ERR_ARG, "kc_model_tensor: unknown model tensor kind %d", kind);
+    }
+    CK(cudaStreamSynchronize(ctx->stream));
+    return KC_OK;
+  }
+  if (layer >= m->n_layer) return fail(ctx, KC_ERR_ARG, "kc_model_tensor: layer %d of %d", layer, m->n_layer);
+  Model::Lay& y = m->L[layer];
+  const int64_t n = rows * cols;
+  auto vec = [&](float*& dst, int64_t expect) -> int {
+    if (t != T_F32 || n != expect) return fail(ctx, KC_ERR_SHAPE, "kc_model_tensor: vector kind %d", kind);
+    return model_vec(ctx, dst, w, n, on_dev);
+  };
+  switch (kind) {
+    case KC_T_ATTN_NORM: RC(vec(y.attn_norm, m->d)); break;
+    case KC_T_FFN_NORM: RC(vec(y.ffn_norm, m->d)); break;
+    case KC_T_ATTN_Q_NORM: RC(vec(y.qn, m->hd)); break;
+    case KC_T_ATTN_K_NORM: RC(vec(y.kn, m->hd)); break;
+    case KC_T_ATTN_Q_BIAS: RC(vec(y.bq, (int64_t)m->nh * m->hd)); break;
+    case KC_T_ATTN_K_BIAS: RC(vec(y.bk, (int64_t)m->nkv * m->hd)); break;
+    case KC_T_ATTN_V_BIAS: RC(vec(y.bv, (int64_t)m->nkv * m->hd)); break;
+    case KC_T_ATTN_Q: RC(model_dense(ctx, y.q, t, w, rows, cols, on_dev)); break;
+    case KC_T_ATTN_K: RC(model_dense(ctx, y.k, t, w, rows, cols, on_dev)); break;
+    case KC_T_ATTN_V: RC(model_dense(ctx, y.v, t, w, rows, cols, on_dev)); break;
+    case KC_T_ATTN_OUT: RC(model_dense(ctx, y.o, t, w, rows, cols, on_dev)); break;
+    case KC_T_FFN_GATE: RC(model_dense(ctx, y.gate, t, w, rows, cols, on_dev)); break;
+    case KC_T_FFN_UP: RC(model_dense(ctx, y.up, t, w, rows, cols, on_dev)); break;
+    case KC_T_FFN_DOWN: RC(model_dense(ctx, y.down, t, w, rows, cols, on_dev)); break;
+    default: return fail(ctx, KC_ERR_ARG, "kc_model_tensor: unknown layer tensor kind %d", kind);
+  }
+  CK(cudaStreamSynchronize(ctx->stream));
+  return KC_OK;
+}
+
+int kc_model_forward(kc_ctx* ctx, const uint32_t* tokens, int n, float* logits, uint32_t* next_token) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!ctx->model) return fail(ctx, KC_ERR_STATE, "kc_model_forward: call kc_model_init first");
+  if (!tokens) return fail(ctx, KC_ERR_ARG, "kc_model_forward: tokens is NULL");
+  cudaSetDevice(ctx->device);
+  Model& m = *ctx->model;
+  RC(model_forward(ctx, tokens, false, n));
+  if (logits) CK(cudaMemcpyAsync(logits, m.logits, (size_t)m.n_vocab * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (next_token) CK(cudaMemcpyAsync(next_token, m.next, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return check_status(ctx);
+}
+
+int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, int n_gen, uint32_t* out_tokens) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!ctx->model) return fail(ctx, KC_ERR_STATE, "kc_model_generate: call kc_model_init first");
+  if (!prompt || n_prompt < 1 || n_gen < 0 || (n_gen > 0 && !out_tokens))
+    return fail(ctx, KC_ERR_ARG, "kc_model_generate: bad arguments");
+  cudaSetDevice(ctx->device);
+  Model& m = *ctx->model;
+  if (m.cached + n_prompt + std::max(0, n_gen - 1) > m.n_ctx)
+    return fail(ctx, KC_ERR_ARG, "kc_model_generate: context full (n_ctx = %d)", m.n_ctx);
+  RC(model_forward(ctx, prompt, false, n_prompt));
+  if (n_gen == 0) {
+    CK(cudaStreamSynchronize(ctx->stream));
+    return check_status(ctx);
+  }
+  // Each step feeds the previous argmax straight from device memory.
+  uint32_t* hist = nullptr;
+  CK(cudaMalloc(&hist, (size_t)n_gen * 4));
+  int rc = KC_OK;
+  for (int i = 0; i < n_gen && rc == KC_OK; ++i) {
+    if (cudaMemcpyAsync(hist + i, m.next, 4, cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess) {
+      rc = fail(ctx, KC_ERR_CUDA, "kc_model_generate: copy failed");
+      break;
+    }
+    if (i + 1 < n_gen) rc = model_forward(ctx, hist + i, true, 1);
+  }
+  if (rc == KC_OK && cudaMemcpyAsync(out_tokens, hist, (size_t)n_gen * 4, cudaMemcpyDeviceToHost, ctx->stream) !=
+                         cudaSuccess)
+    rc = fail(ctx, KC_ERR_CUDA, "kc_model_generate: copy failed");
+  cudaStreamSynchronize(ctx->stream);
+  cudaFree(hist);
+  if (rc != KC_OK) return rc;
+  return check_status(ctx);
+}
+
+int kc_model_truncate(kc_ctx* ctx, int keep) {
+  if (!ctx) return KC_ERR_ARG;
+  if (!ctx->model) return fail(ctx, KC_ERR_STATE, "kc_model_truncate: no model");
+  ctx->model->cached = std::min(ctx->model->cached, std::max(0, keep));
+  return KC_OK;
+}
+
+int kc_model_cached(const kc_ctx* ctx) { return ctx && ctx->model ? ctx->model->cached : 0; }
 
 }  // extern "C"

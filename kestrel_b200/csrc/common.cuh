@@ -95,6 +95,12 @@ __device__ __forceinline__ float h2f(uint32_t bits16) {
   return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFF)));
 }
 
+// exp of a float evaluated in double and rounded once to float. Rust's
+// f32::exp calls the C library's expf, which is correctly rounded except for
+// rare arguments; this agrees with it on all but ~0.06% of arguments (there by
+// one ulp), where CUDA's single-precision expf differs far more often.
+__device__ __forceinline__ float exp_rn(float x) { return (float)exp((double)x); }
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -129,6 +135,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Arrive `count` times at once.
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;

@@ -4,22 +4,24 @@
 //
 // Memory-bound design:
 //  * Work unit = one 32-row tile of one expert matrix, streamed through the
-//    row's K segments. A CTA owns a contiguous range of units; its consumer
-//    warps take them DW at a time (a "group"), one unit per warp, and the
-//    producer issues the group's stages segment-major (segment 0 of every
-//    warp's unit, then segment 1, ...), so all warps advance together through
-//    a deep ring of stages.
-//  * A stage is the 32 rows x `ks` superblocks of a segment: one contiguous
-//    range of the tiled device layout (common.cuh), fetched by a single
-//    cp.async.bulk into a ring tracked by mbarriers (~200 KB per SM).
-//  * One thread owns one weight row and all eight of the reference's 32-bit
-//    AVX2 lanes, so scales are decoded once per row-superblock and the float
-//    chains (per-lane FMA over superblocks, then hsum) run in one thread in
-//    the reference's order. Integer sums are exact in any order.
-//  * The slots' activation records (int8 values, block sums, scale) for the
-//    next segment are copied by each warp with cp.async into a double buffer
-//    while the current segment is computed; every thread of the warp then
-//    reads them as shared-memory broadcasts.
+//    row's K segments. Units are dealt to the CTAs round-robin, so each CTA
+//    gets a mix of experts with 1, 2 and 3 rows; a CTA takes its units DW at
+//    a time (a "group"); the producer warp issues the group's stages
+//    segment-major (segment 0 of every unit, then segment 1, ...), so all
+//    units of a group advance together through a deep ring of stages.
+//  * A stage is the 32 rows x `ks` superblocks of a segment -- one contiguous
+//    range of the tiled device layout (common.cuh), one cp.async.bulk --
+//    followed by the unit's activation records (int8 values, block sums,
+//    scale) of those superblocks, one bulk copy per superblock. The ring
+//    (~220 KB per SM) is tracked by mbarriers.
+//  * Consumers: 2 * DW warps. In a full group every unit has two warps, each
+//    holding 16 rows with two threads per row, four of the reference's eight
+//    32-bit AVX2 lanes per thread. The last, partial group of a CTA spreads
+//    its units over all warps (four or eight threads per row), so the tail
+//    does not run on a few warps. Scales are decoded per row-superblock in
+//    each thread; the per-lane float chains run in superblock order as in the
+//    reference, and the row's first thread gathers the eight lanes (warp
+//    shuffles) for the hsum. Integer sums are exact in any order.
 #include <algorithm>
 #include <cstdlib>
 
@@ -29,13 +31,15 @@
 
 namespace kc {
 
-constexpr int DR = kTileRows;  // rows per unit: one per lane
-constexpr int DW = 8;          // consumer warps
-constexpr int DTHREADS = 32 * (DW + 1);
+constexpr int DR = kTileRows;  // rows per unit
+constexpr int DW = 8;          // units per group (one producer lane each)
+constexpr int DC = 2 * DW;     // consumer warps
+constexpr int DARR = 8;        // consumer arrivals that release a stage
+constexpr int DTHREADS = 32 * (DC + 1);
 constexpr int DMAX_STAGES = 64;
 constexpr int DMAXS = 3;       // slots per unit (experts with 1..3 rows)
-constexpr int DSMEM = 220 * 1024;
-constexpr int DMETA = 96;
+constexpr int DSMEM = 216 * 1024;
+constexpr int DMAX_E = 1024;   // experts whose list / offsets are copied to shared memory
 
 // ---------------------------------------------------------------------------
 // Activation records (layout in decode.h).
@@ -66,7 +70,7 @@ __global__ void q8k_records_kernel(const float* __restrict__ x, const float* __r
     float w[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i)  // transformer.rs:558: g / (1 + exp(-g)) * u
-      v[i] = __fmul_rn(__fdiv_rn(v[i], __fadd_rn(1.0f, expf(-v[i]))), w[i]);
+      v[i] = __fmul_rn(__fdiv_rn(v[i], __fadd_rn(1.0f, exp_rn(-v[i]))), w[i]);
     if (f32out) {
       float4* o = reinterpret_cast<float4*>(f32out + slot * cols + b * 256 + lane * 8);
       o[0] = make_float4(v[0], v[1], v[2], v[3]);
@@ -122,7 +126,7 @@ __global__ void q8_records_kernel(const float* __restrict__ x, const float* __re
   const int64_t src = slot_src ? slot_src[slot] : slot;
   float v = x[src * cols + b * 32 + lane];
   if (SWIGLU) {
-    v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u[src * cols + b * 32 + lane]);
+    v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, exp_rn(-v))), u[src * cols + b * 32 + lane]);
     if (f32out) f32out[slot * cols + b * 32 + lane] = v;
   }
   if (f16out) f16out[slot * cols + b * 32 + lane] = __float2half_rn(v);
@@ -155,9 +159,10 @@ void launch_act_records(bool kquant, const float* x, const float* u, const int* 
 
 // ---------------------------------------------------------------------------
 // Stage geometry: a stage is one 32-row tile x a segment of `ks` consecutive
-// superblocks (Q8_0: chunks of 8 blocks). KESTREL_DECODE_KS overrides ks (a
-// tuning knob; the default is two K-quant superblocks or one Q8_0 chunk of 8
-// blocks per stage, 8.7-13.4 KB).
+// superblocks (Q8_0: chunks of 8 blocks), followed by the unit's activation
+// records for those superblocks. KESTREL_DECODE_KS overrides ks (a tuning
+// knob; the default is two K-quant superblocks or one Q8_0 chunk of 8 blocks
+// per stage, 10.6-15.4 KB with the records).
 static int decode_ks_override() {
   static const int v = [] {
     const char* e = std::getenv("KESTREL_DECODE_KS");
@@ -181,9 +186,9 @@ DecodeGeom decode_geom(int t, int64_t cols) {
     const int64_t end = b == g.nsb ? g.tile_bytes : tiled_sb_offset(t, cols, b);
     mx = std::max(mx, (int)(end - tiled_sb_offset(t, cols, a)));
   }
-  g.stage_bytes = ((mx + 127) / 128) * 128;
+  g.rec_off = ((mx + 127) / 128) * 128;
   const int rb = rec_bytes_of(t != T_Q8_0);
-  g.act_bytes = ((2 * DMAXS * g.ks * rb + 127) / 128) * 128;
+  g.stage_bytes = ((g.rec_off + g.ks * DMAXS * rb + 127) / 128) * 128;
   return g;
 }
 
@@ -194,6 +199,17 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
   return v;
+}
+// N consecutive 32-bit words (N = 4, 2, 1; address aligned to 4N bytes).
+template <int N>
+__device__ __forceinline__ void ldsw(uint32_t a, uint32_t (&w)[N]) {
+  if constexpr (N == 4) {
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "r"(a));
+  } else if constexpr (N == 2) {
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "r"(a));
+  } else {
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w[0]) : "r"(a));
+  }
 }
 __device__ __forceinline__ float ldsf(uint32_t a) {
   float v;
@@ -211,18 +227,17 @@ __device__ __forceinline__ int ubyte(uint32_t w, int i) { return (int)((w >> (8 
 __device__ __forceinline__ int dp2a_lo(uint32_t a, uint32_t b, int c) { return __dp2a_lo((int)a, (int)b, c); }
 __device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) { return __dp2a_hi((int)a, (int)b, c); }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// The per-superblock kernels below compute, for one weight row, LPT of the
+// reference's eight 32-bit AVX2 lanes: lanes l0 .. l0+LPT-1 (LPT = 4, 2 or 1;
+// l0 a multiple of LPT). Lane j of a 32-byte vector is its word j, so the
+// thread's lanes are words (l0 & 3) .. of the vector's 16-byte chunk l0 >> 2.
+// acc[s][i] is lane l0 + i of slot s.
 
 // One Q4_K superblock of row `row` (avx2.rs:351-379) against NS slots whose
 // records start at xr (stride R).
-template <int NS, int R>
-__device__ __forceinline__ void q4k_sb(uint32_t sbt, int row, uint32_t xr,
-                                       float (&acc)[NS][8], float (&summs)[NS]) {
+template <int NS, int R, int LPT>
+__device__ __forceinline__ void q4k_sb(uint32_t sbt, int row, int l0, uint32_t xr,
+                                       float (&acc)[NS][LPT], float (&summs)[NS]) {
   const uint4 hdr = lds128(sbt + 16 * row);
   const float dw = h2f(hdr.x), dmw = h2f(hdr.x >> 16);
   // scale_min_k4 (quant.rs:54-60) for all eight sub-blocks, four per word.
@@ -230,31 +245,32 @@ __device__ __forceinline__ void q4k_sb(uint32_t sbt, int row, uint32_t xr,
   const uint32_t scB = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
   const uint32_t mA = hdr.z & 0x3F3F3F3Fu;
   const uint32_t mB = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
-  int sumi[NS][8];
+  int sumi[NS][LPT];
 #pragma unroll
   for (int s = 0; s < NS; ++s)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) sumi[s][j] = 0;
+    for (int j = 0; j < LPT; ++j) sumi[s][j] = 0;
+  // qs bytes 32k..32k+31 (sub-blocks 2k and 2k+1 in the low / high nibbles).
+  const uint32_t qa = sbt + kPlane + kPlane * (l0 >> 2) + 16 * row + 4 * (l0 & 3);
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const uint4 qa = lds128(sbt + kPlane + kPlane * (2 * k) + 16 * row);
-    const uint4 qb = lds128(sbt + kPlane + kPlane * (2 * k + 1) + 16 * row);
-    const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    int lo[8], hi[8];
+    uint32_t qw[LPT];
+    ldsw<LPT>(qa + 2 * kPlane * k, qw);
+    int lo[LPT], hi[LPT];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < LPT; ++j) {
       lo[j] = (int)(qw[j] & 0x0F0F0F0Fu);
       hi[j] = (int)((qw[j] >> 4) & 0x0F0F0F0Fu);
     }
     const int slo = ubyte(k < 2 ? scA : scB, (2 * k) & 3), shi = ubyte(k < 2 ? scA : scB, (2 * k + 1) & 3);
 #pragma unroll
     for (int s = 0; s < NS; ++s) {
-      const uint32_t x = xr + s * R + 64 * k;
-      const uint4 x0 = lds128(x), x1 = lds128(x + 16), x2 = lds128(x + 32), x3 = lds128(x + 48);
-      const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-      const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+      const uint32_t x = xr + s * R + 64 * k + 4 * l0;
+      uint32_t xl[LPT], xh[LPT];
+      ldsw<LPT>(x, xl);
+      ldsw<LPT>(x + 32, xh);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < LPT; ++j) {
         sumi[s][j] += slo * dp4a(lo[j], (int)xl[j], 0);
         sumi[s][j] += shi * dp4a(hi[j], (int)xh[j], 0);
       }
@@ -266,8 +282,9 @@ __device__ __forceinline__ void q4k_sb(uint32_t sbt, int row, uint32_t xr,
     const float xd = ldsf(x + 304);
     const float d = __fmul_rn(dw, xd), dmin = __fmul_rn(dmw, xd);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[s][j] = __fmaf_rn((float)sumi[s][j], d, acc[s][j]);
-    // mins = sum over sub-blocks m[i] * (bsums[2i] + bsums[2i+1])
+    for (int j = 0; j < LPT; ++j) acc[s][j] = __fmaf_rn((float)sumi[s][j], d, acc[s][j]);
+    // mins = sum over sub-blocks m[i] * (bsums[2i] + bsums[2i+1]) (one per row;
+    // every thread of the row computes it, the lane-0 thread uses it)
     const uint4 bp = lds128(x + 288);
     const int mins = dp2a_lo(bp.x, mA, dp2a_hi(bp.y, mA, dp2a_lo(bp.z, mB, dp2a_hi(bp.w, mB, 0))));
     summs[s] = __fadd_rn(summs[s], __fmul_rn(dmin, (float)mins));
@@ -276,43 +293,42 @@ __device__ __forceinline__ void q4k_sb(uint32_t sbt, int row, uint32_t xr,
 
 // One Q6_K superblock (avx2.rs:384-419). Lanes 0-3 of a 32-run use its first
 // 16-element scale, lanes 4-7 the second.
-template <int NS, int R>
-__device__ __forceinline__ void q6k_sb(uint32_t sbt, int row, uint32_t xr,
-                                       float (&acc)[NS][8]) {
+template <int NS, int R, int LPT>
+__device__ __forceinline__ void q6k_sb(uint32_t sbt, int row, int l0, uint32_t xr, float (&acc)[NS][LPT]) {
   const float dw = h2f(ldsu16(sbt + 13 * kPlane + 2 * row));
   const uint4 scw = lds128(sbt + 12 * kPlane + 16 * row);
   const uint32_t sw[4] = {scw.x, scw.y, scw.z, scw.w};
-  int sumi[NS][8];
+  const int hf = l0 >> 2;  // which 16-byte chunk (and scale) of a 32-run
+  const uint32_t wo = 16 * row + 4 * (l0 & 3);
+  int sumi[NS][LPT];
 #pragma unroll
   for (int s = 0; s < NS; ++s)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) sumi[s][j] = 0;
+    for (int j = 0; j < LPT; ++j) sumi[s][j] = 0;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const uint4 ha = lds128(sbt + 8 * kPlane + kPlane * (2 * h) + 16 * row);
-    const uint4 hb = lds128(sbt + 8 * kPlane + kPlane * (2 * h + 1) + 16 * row);
-    const uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+    uint32_t hw[LPT];
+    ldsw<LPT>(sbt + 8 * kPlane + kPlane * (2 * h + hf) + wo, hw);
 #pragma unroll
     for (int run = 0; run < 2; ++run) {
-      const uint4 la = lds128(sbt + kPlane * (4 * h + 2 * run) + 16 * row);
-      const uint4 lb = lds128(sbt + kPlane * (4 * h + 2 * run + 1) + 16 * row);
-      const uint32_t lw[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+      uint32_t lw[LPT];
+      ldsw<LPT>(sbt + kPlane * (4 * h + 2 * run + hf) + wo, lw);
 #pragma unroll
       for (int nib = 0; nib < 2; ++nib) {
         const int ri = 2 * nib + run;
-        int q6[8];
+        int q6[LPT];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < LPT; ++j)
           q6[j] = (int)(((lw[j] >> (4 * nib)) & 0x0F0F0F0Fu) | (((hw[j] >> (2 * ri)) & 0x03030303u) << 4));
         const int si = 8 * h + 2 * ri;
-        const int sc0 = sbyte(sw[si >> 2], si & 3), sc1 = sbyte(sw[(si + 1) >> 2], (si + 1) & 3);
+        const uint32_t sa = sw[si >> 2], sb = sw[(si + 1) >> 2];
+        const int sc = hf ? sbyte(sb, (si + 1) & 3) : sbyte(sa, si & 3);
 #pragma unroll
         for (int s = 0; s < NS; ++s) {
-          const uint32_t x = xr + s * R + 128 * h + 32 * ri;
-          const uint4 x0 = lds128(x), x1 = lds128(x + 16);
-          const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          uint32_t xw[LPT];
+          ldsw<LPT>(xr + s * R + 128 * h + 32 * ri + 4 * l0, xw);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) sumi[s][j] += (j < 4 ? sc0 : sc1) * dp4a(q6[j], (int)xw[j], 0);
+          for (int j = 0; j < LPT; ++j) sumi[s][j] += sc * dp4a(q6[j], (int)xw[j], 0);
         }
       }
     }
@@ -322,7 +338,7 @@ __device__ __forceinline__ void q6k_sb(uint32_t sbt, int row, uint32_t xr,
     const uint32_t x = xr + s * R;
     const float d = __fmul_rn(dw, ldsf(x + 304));
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[s][j] = __fmaf_rn((float)sumi[s][j], d, acc[s][j]);
+    for (int j = 0; j < LPT; ++j) acc[s][j] = __fmaf_rn((float)sumi[s][j], d, acc[s][j]);
     // offs = sum over the 16 sub-blocks sc[i] * bsums[i]
     const uint4 b0 = lds128(x + 256), b1 = lds128(x + 272);
     int offs = dp2a_lo(b0.x, sw[0], 0);
@@ -334,29 +350,31 @@ __device__ __forceinline__ void q6k_sb(uint32_t sbt, int row, uint32_t xr,
     offs = dp2a_lo(b1.z, sw[3], offs);
     offs = dp2a_hi(b1.w, sw[3], offs);
     // avx2.rs:416: lane 0 gets (-32*d)*offs, the other lanes +0.0.
-    acc[s][0] = __fadd_rn(acc[s][0], __fmul_rn(__fmul_rn(-32.0f, d), (float)offs));
+    const float o = __fmul_rn(__fmul_rn(-32.0f, d), (float)offs);
+    acc[s][0] = __fadd_rn(acc[s][0], l0 == 0 ? o : 0.0f);
 #pragma unroll
-    for (int j = 1; j < 8; ++j) acc[s][j] = __fadd_rn(acc[s][j], 0.0f);
+    for (int j = 1; j < LPT; ++j) acc[s][j] = __fadd_rn(acc[s][j], 0.0f);
   }
 }
 
 // One chunk of up to 8 Q8_0 blocks (avx2.rs:49-58).
-template <int NS, int R>
-__device__ __forceinline__ void q8_0_chunk(uint32_t cb, int nblk, int row, uint32_t xr, float (&acc)[NS][8]) {
+template <int NS, int R, int LPT>
+__device__ __forceinline__ void q8_0_chunk(uint32_t cb, int nblk, int row, int l0, uint32_t xr,
+                                           float (&acc)[NS][LPT]) {
+  const uint32_t wo = kPlane * (l0 >> 2) + 16 * row + 4 * (l0 & 3);
 #pragma unroll 1
   for (int bl = 0; bl < nblk; ++bl) {
-    const uint4 wa = lds128(cb + kPlane * (2 * bl) + 16 * row);
-    const uint4 wb = lds128(cb + kPlane * (2 * bl + 1) + 16 * row);
-    const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    uint32_t ww[LPT];
+    ldsw<LPT>(cb + 2 * kPlane * bl + wo, ww);
     const float dw = h2f(ldsu16(cb + 2 * kPlane * nblk + 16 * row + 2 * bl));
 #pragma unroll
     for (int s = 0; s < NS; ++s) {
       const uint32_t x = xr + s * R;
-      const uint4 x0 = lds128(x + 32 * bl), x1 = lds128(x + 32 * bl + 16);
-      const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      uint32_t xw[LPT];
+      ldsw<LPT>(x + 32 * bl + 4 * l0, xw);
       const float d = __fmul_rn(dw, ldsf(x + 256 + 4 * bl));
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[s][j] = __fmaf_rn((float)dp4a((int)ww[j], (int)xw[j], 0), d, acc[s][j]);
+      for (int j = 0; j < LPT; ++j) acc[s][j] = __fmaf_rn((float)dp4a((int)ww[j], (int)xw[j], 0), d, acc[s][j]);
     }
   }
 }
@@ -373,11 +391,12 @@ struct UnitMeta {
   int e, slot0, ns;
 };
 
-__device__ __forceinline__ UnitMeta load_meta(const DecodeArgs& a, int li) {
+// Meta of list entry li from the shared copies of the list and offsets.
+__device__ __forceinline__ UnitMeta meta_at(const int* list_s, const int* off_s, int li) {
   UnitMeta m;
-  m.e = a.list[li];
-  m.slot0 = a.offsets[m.e];
-  m.ns = max(1, min(DMAXS, a.offsets[m.e + 1] - m.slot0));
+  m.e = list_s[li];
+  m.slot0 = off_s[m.e];
+  m.ns = max(1, min(DMAXS, off_s[m.e + 1] - m.slot0));
   return m;
 }
 
@@ -394,53 +413,41 @@ __device__ __forceinline__ UnitPos unit_pos(int u, int tiles, int n_mat) {
   return p;
 }
 
-// Copy the records of unit `um`'s slots for segment `seg` into `dst`
-// ([superblock of the segment][slot][R]) with cp.async, over the warp's lanes.
-template <int R>
-__device__ __forceinline__ void issue_act(const DecodeArgs& a, const DecodeGeom& g, const UnitMeta& um, int seg,
-                                          uint8_t* dst, int lane) {
-  const int sb0 = seg * g.ks;
-  const int n = min(g.ks, g.nsb - sb0);
-  const int per_sb = um.ns * (R / 16);
-  for (int c = lane; c < n * per_sb; c += 32) {
-    const int j = c / per_sb, cc = c - j * per_sb;
-    const uint8_t* src = a.rec + ((int64_t)(sb0 + j) * a.rec_slots + um.slot0) * R + 16 * cc;
-    cp_async16(dst + j * (DMAXS * R) + 16 * cc, src);
-  }
-}
-
 template <int T>
 struct TypeR {
   static constexpr int R = T == T_Q8_0 ? kRecQ8 : kRecK;
 };
 
-// One unit: NS slots, all segments. `buf` selects the warp's activation
-// buffer holding this step's records (prefetched by the previous step).
-// (sid, st, ph) are the stage number, ring slot and phase parity of the
-// unit's first stage; the warp's later stages of the unit are `step` stages
-// apart, and its next unit starts DW stages after this unit's last one. On
-// return they point at that next stage.
-template <int T, int NS>
+// Threads per weight row for a group of wg units (1..DW): full and
+// nearly full groups take two threads per row (DC = 2 * DW warps, two per
+// unit); smaller groups spread each unit over more warps, so the tail of a
+// CTA's range runs on all its warps.
+__host__ __device__ constexpr int tpr_of(int wg) { return wg > DW / 2 ? 2 : (wg > DW / 4 ? 4 : 8); }
+static_assert(DC == 2 * DW && DW % 4 == 0, "warp layout");
+
+// One unit, all segments, on TPR threads per row. This warp holds rows
+// `row` (one per lane / TPR) and lanes l0 = (lane % TPR) * LPT .. of each.
+// The unit's stages are sid0, sid0 + wg, sid0 + 2 wg, ... (segment-major
+// order of its group).
+template <int T, int TPR, int NS>
 __device__ __forceinline__ void run_unit(const DecodeArgs& a, const DecodeGeom& g, const uint8_t* ring,
-                                         uint64_t* full, uint64_t* empty, int n_stages, int& sid, int& st, uint32_t& ph,
-                                         int step, uint8_t* abuf, int& buf, const UnitMeta& um, bool has_next,
-                                         const UnitMeta& next, int lane, float* out, int r_out, bool& ok) {
+                                         uint64_t* full, uint64_t* empty, int n_stages, int sid0, int wg, int lane,
+                                         int row, float* out, int r_out, bool& ok) {
   constexpr int R = TypeR<T>::R;
-  const int half = g.act_bytes / 2;
-  float acc[NS][8], summs[NS];
+  constexpr int LPT = 8 / TPR;
+  const int l0 = (lane % TPR) * LPT;
+  float acc[NS][LPT], summs[NS];
 #pragma unroll
   for (int s = 0; s < NS; ++s) {
     summs[s] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[s][j] = 0.f;
+    for (int j = 0; j < LPT; ++j) acc[s][j] = 0.f;
   }
+  // Stage number, ring slot and phase of the unit's segment 0; each later
+  // segment is wg stages on (wg <= DW < n_stages).
+  int sid = sid0, st = sid0 % n_stages;
+  uint32_t ph = (uint32_t)((sid0 / n_stages) & 1);
   for (int seg = 0; seg < g.nseg; ++seg) {
-    // Prefetch the next step's records, then make this step's visible.
-    if (seg + 1 < g.nseg) issue_act<R>(a, g, um, seg + 1, abuf + (buf ^ 1) * half, lane);
-    else if (has_next) issue_act<R>(a, g, next, 0, abuf + (buf ^ 1) * half, lane);
-    cp_async_commit();
-    cp_async_wait1();
-    __syncwarp();
     // A slot is used lap after lap by different warps, and bulk copies may land
     // out of order: before waiting on this lap's copy, wait until the slot's
     // previous lap has been released. Only then is the copy barrier known to be
@@ -449,32 +456,47 @@ __device__ __forceinline__ void run_unit(const DecodeArgs& a, const DecodeGeom& 
     if (ok && !mbar_wait(&full[st], ph, a.status, W_DEC_FULL)) ok = false;
     if (ok) {
       const uint32_t sp = smem_u32(ring) + (uint32_t)(st * g.stage_bytes);
-      const uint32_t xr = smem_u32(abuf) + (uint32_t)(buf * half);
+      const uint32_t xr = sp + (uint32_t)g.rec_off;
       const int sb0 = seg * g.ks;
       const int n = min(g.ks, g.nsb - sb0);
       for (int j = 0; j < n; ++j) {
-        if (T == T_Q4_K) q4k_sb<NS, R>(sp + 4608 * j, lane, xr + j * (DMAXS * R), acc, summs);
-        else if (T == T_Q6_K) q6k_sb<NS, R>(sp + 6720 * j, lane, xr + j * (DMAXS * R), acc);
-        else q8_0_chunk<NS, R>(sp + 8704 * j, min(8, g.nb32 - 8 * (sb0 + j)), lane, xr + j * (DMAXS * R), acc);
+        if (T == T_Q4_K) q4k_sb<NS, R, LPT>(sp + 4608 * j, row, l0, xr + j * (DMAXS * R), acc, summs);
+        else if (T == T_Q6_K) q6k_sb<NS, R, LPT>(sp + 6720 * j, row, l0, xr + j * (DMAXS * R), acc);
+        else q8_0_chunk<NS, R, LPT>(sp + 8704 * j, min(8, g.nb32 - 8 * (sb0 + j)), row, l0, xr + j * (DMAXS * R), acc);
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-    buf ^= 1;
-    const int inc = seg + 1 < g.nseg ? step : DW;
-    sid += inc;
-    st += inc;
+    // TPR warps hold the unit; each releases DARR / TPR of the slot's DARR arrivals.
+    if (lane == 0) mbar_arrive_cnt(&empty[st], DARR / TPR);
+    sid += wg;
+    st += wg;
     if (st >= n_stages) {
       st -= n_stages;
       ph ^= 1u;
     }
   }
+  // Gather the row's eight lanes in its first thread, then hsum in the
+  // reference's order.
 #pragma unroll
   for (int s = 0; s < NS; ++s) {
-    float v = hsum8(acc[s]);
-    if (T == T_Q4_K) v = __fsub_rn(v, summs[s]);
-    if (r_out >= 0 && ok) out[(int64_t)(um.slot0 + s) * a.out_stride + r_out] = v;
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < TPR; ++q)
+#pragma unroll
+      for (int i = 0; i < LPT; ++i) v[q * LPT + i] = __shfl_sync(0xffffffffu, acc[s][i], (lane & ~(TPR - 1)) + q);
+    float r = hsum8(v);
+    if (T == T_Q4_K) r = __fsub_rn(r, summs[s]);
+    if (l0 == 0 && r_out >= 0 && ok) out[(int64_t)s * a.out_stride + r_out] = r;
   }
+}
+
+template <int T, int TPR>
+__device__ __forceinline__ void run_unit_ns(int ns, const DecodeArgs& a, const DecodeGeom& g, const uint8_t* ring,
+                                            uint64_t* full, uint64_t* empty, int n_stages, int sid0, int wg,
+                                            int lane, int row, float* out, int r_out, bool& ok) {
+  if (ns == 1) run_unit<T, TPR, 1>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+  else if (ns == 2) run_unit<T, TPR, 2>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+  else run_unit<T, TPR, 3>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
 }
 
 template <int T>
@@ -482,64 +504,76 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
   pdl_enter();
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[DMAX_STAGES], empty[DMAX_STAGES];
-  __shared__ UnitMeta meta[DMETA];
+  __shared__ int list_s[DMAX_E], off_s[DMAX_E + 1];
   constexpr int R = TypeR<T>::R;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_list = *a.n_list;
+  const int n_list = min(*a.n_list, DMAX_E);
   const int tiles = (int)(padded_rows(a.rows) / DR);
   const int per_expert = a.n_mat * tiles;
-  const int64_t total = (int64_t)n_list * per_expert;
-  const int64_t beg = total * blockIdx.x / gridDim.x, end = total * (blockIdx.x + 1) / gridDim.x;
-  if (beg >= end) return;
-  const int64_t n_units = end - beg;
-  const int n_groups = (int)((n_units + DW - 1) / DW);
-  const int li0 = (int)(beg / per_expert);
-  const int n_meta = min(DMETA, (int)((end - 1) / per_expert) - li0 + 1);
-  for (int i = tid; i < n_meta; i += blockDim.x) meta[i] = load_meta(a, li0 + i);
+  const int total = n_list * per_expert;
+  // Units are dealt to the CTAs round-robin (unit b, b + G, b + 2G, ...), so
+  // every CTA gets a mix of experts with 1, 2 and 3 rows, whose compute
+  // differs, instead of a contiguous run of one or two experts.
+  const int G = gridDim.x, b = blockIdx.x;
+  if (b >= total) return;
+  const int n_units = (total - b + G - 1) / G;
+  const int n_groups = (n_units + DW - 1) / DW;
+  for (int i = tid; i < n_list; i += blockDim.x) list_s[i] = a.list[i];
+  for (int i = tid; i <= a.n_experts && i <= DMAX_E; i += blockDim.x) off_s[i] = a.offsets[i];
   if (tid == 0) {
     for (int s = 0; s < n_stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], DARR);
     }
     fence_mbar_init();
   }
   __syncthreads();
   uint8_t* ring = smem;
-  auto meta_of = [&](int li) { return li - li0 < DMETA ? meta[li - li0] : load_meta(a, li); };
+  auto unit_at = [&](int i) { return unit_pos(b + i * G, tiles, a.n_mat); };
 
   if (warp == 0) {
-    // Producer: group by group, segment-major, one stage per (segment, unit).
-    // Lane w issues consumer warp w's stage of every segment, so the stages of
-    // a segment go out in parallel; per stage a lane does only a wait, an
-    // expect_tx and one bulk copy.
+    // Producer: group by group, segment-major, one stage per (segment, unit):
+    // the segment's weight bytes of the unit's 32-row tile (one bulk copy),
+    // then the unit's activation records of each superblock of the segment
+    // (one bulk copy per superblock: ns records are contiguous). Lane w
+    // issues unit w's stage of every segment, so the stages of a segment go
+    // out in parallel.
     int last = -1;  // highest stage number this lane issued
     if (lane < DW) {
       const int w = lane;
       bool ok = true;
       for (int gi = 0; gi < n_groups; ++gi) {
-        const int wg = (int)min((int64_t)DW, n_units - (int64_t)gi * DW);
+        const int wg = min(DW, n_units - gi * DW);
         const bool active = w < wg;
         const uint8_t* up = nullptr;
+        const uint8_t* rp = nullptr;
+        int rbytes = 0;
         if (active) {
-          const UnitPos p = unit_pos((int)beg + gi * DW + w, tiles, a.n_mat);
-          const int e = meta_of(p.li).e;
-          up = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(e - a.expert_base) * a.expert_stride +
+          const UnitPos p = unit_at(gi * DW + w);
+          const UnitMeta um = meta_at(list_s, off_s, p.li);
+          up = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(um.e - a.expert_base) * a.expert_stride +
                (int64_t)p.tile * g.tile_bytes;
+          rp = a.rec + (int64_t)um.slot0 * R;
+          rbytes = um.ns * R;
         }
         int64_t off0 = 0;
         for (int seg = 0; seg < g.nseg; ++seg) {
-          const int sb1 = min(g.nsb, (seg + 1) * g.ks);
+          const int sb0 = seg * g.ks, sb1 = min(g.nsb, sb0 + g.ks);
           const int64_t off1 = sb1 == g.nsb ? g.tile_bytes : tiled_sb_offset(g.type, a.cols, sb1);
           if (active && ok) {
-            const int sid = (gi * g.nseg + seg) * DW - seg * (DW - wg) + w;  // = gi*nseg*DW + seg*wg + w
+            const int sid = gi * g.nseg * DW + seg * wg + w;
             const int st = sid % n_stages;
             const uint32_t ph = (uint32_t)((sid / n_stages) & 1);
             if (sid >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status, W_DEC_EMPTY)) {
               ok = false;
             } else {
-              const uint32_t bytes = (uint32_t)(off1 - off0);
-              mbar_expect_tx(&full[st], bytes);
-              bulk_g2s(ring + (int64_t)st * g.stage_bytes, up + off0, bytes, &full[st]);
+              const uint32_t wbytes = (uint32_t)(off1 - off0);
+              uint8_t* dst = ring + (int64_t)st * g.stage_bytes;
+              mbar_expect_tx(&full[st], wbytes + (uint32_t)((sb1 - sb0) * rbytes));
+              bulk_g2s(dst, up + off0, wbytes, &full[st]);
+              for (int sb = sb0; sb < sb1; ++sb)
+                bulk_g2s(dst + g.rec_off + (sb - sb0) * (DMAXS * R), rp + (int64_t)sb * a.rec_slots * R,
+                         (uint32_t)rbytes, &full[st]);
               last = sid;
             }
           }
@@ -562,64 +596,52 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
     return;
   }
 
-  // Consumers: warp w takes unit gi*DW + w of every group gi.
-  const int w = warp - 1;
-  if (w >= n_units) return;
-  uint8_t* abuf = smem + (int64_t)n_stages * g.stage_bytes + (int64_t)w * g.act_bytes;
-  int buf = 0;
+  // Consumers: in group gi (wg units), warp c serves unit c / TPR with
+  // TPR = tpr_of(wg) threads per row; the TPR warps of a unit split its 32
+  // rows, 32 / TPR each.
+  const int c = warp - 1;
   bool ok = true;
-  const int ubeg = (int)beg;
-  UnitMeta um = meta_of(unit_pos(ubeg + w, tiles, a.n_mat).li);
-  issue_act<R>(a, g, um, 0, abuf, lane);
-  cp_async_commit();
-  int sid = w, st = w;  // the warp's first stage is stage w (w < DW <= n_stages)
-  uint32_t ph = 0;
   for (int gi = 0; gi < n_groups; ++gi) {
-    const int wg = (int)min((int64_t)DW, n_units - (int64_t)gi * DW);
-    if (w >= wg) break;
-    const UnitPos p = unit_pos(ubeg + gi * DW + w, tiles, a.n_mat);
-    // The warp's next unit (next group); its first records are prefetched
-    // during this unit's last segment.
-    const int un = (gi + 1) * DW + w;
-    const bool has_next = un < n_units;
-    const UnitMeta next = has_next ? meta_of(unit_pos(ubeg + un, tiles, a.n_mat).li) : um;
-    const int r0 = p.tile * DR;
-    const int r_out = r0 + lane < a.rows ? r0 + lane : -1;  // padding rows are computed, not stored
-    float* out = p.m == 0 ? a.out[0] : a.out[1];
-    if (um.ns == 1)
-      run_unit<T, 1>(a, g, ring, full, empty, n_stages, sid, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
-    else if (um.ns == 2)
-      run_unit<T, 2>(a, g, ring, full, empty, n_stages, sid, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
-    else
-      run_unit<T, 3>(a, g, ring, full, empty, n_stages, sid, st, ph, wg, abuf, buf, um, has_next, next, lane, out, r_out, ok);
-    um = next;
+    const int wg = min(DW, n_units - gi * DW);
+    const int tpr = tpr_of(wg);
+    const int u = c / tpr;
+    if (u >= wg) continue;
+    const UnitPos p = unit_at(gi * DW + u);
+    const UnitMeta um = meta_at(list_s, off_s, p.li);
+    const int row = (c % tpr) * (DR / tpr) + lane / tpr;
+    const int r = p.tile * DR + row;
+    const int r_out = r < a.rows ? r : -1;  // padding rows are computed, not stored
+    float* out = (p.m == 0 ? a.out[0] : a.out[1]) + (int64_t)um.slot0 * a.out_stride;
+    const int sid0 = gi * g.nseg * DW + u;
+    if (tpr == 2) run_unit_ns<T, 2>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+    else if (tpr == 4) run_unit_ns<T, 4>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+    else run_unit_ns<T, 8>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
   }
-  cp_async_wait0();
 }
 
 template <int T>
-static int launch_decode_t(const DecodeArgs& a, const DecodeGeom& g, int max_units, cudaStream_t st) {
-  const int act_total = DW * g.act_bytes;
-  const int n_stages = std::min(DMAX_STAGES, (DSMEM - act_total) / g.stage_bytes);
-  if (n_stages < 2) return KC_ERR_SHAPE;
-  const size_t smem = (size_t)n_stages * g.stage_bytes + act_total;
+static int launch_decode_t(const DecodeArgs& a, const DecodeGeom& g, int max_units, cudaStream_t st, int max_ctas) {
+  const int n_stages = std::min(DMAX_STAGES, DSMEM / g.stage_bytes);
+  if (n_stages <= DW) return KC_ERR_SHAPE;
+  const size_t smem = (size_t)n_stages * g.stage_bytes;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(decode_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, DSMEM);
     attr = true;
   }
-  const int grid = std::min(num_sms(), std::max(1, max_units));
+  const int cap = max_ctas > 0 ? std::min(max_ctas, num_sms()) : num_sms();
+  const int grid = std::min(cap, std::max(1, max_units));
   launch_k(decode_kernel<T>, grid, DTHREADS, smem, st, a, g, n_stages);
   return KC_OK;
 }
 
-int launch_decode(const DecodeArgs& a, int max_units, cudaStream_t st) {
-  if (a.rec_slots <= 0) return KC_ERR_SHAPE;
+int launch_decode(const DecodeArgs& a, int max_units, cudaStream_t st, int max_ctas) {
+  if (a.rec_slots <= 0 || a.n_experts < 1 || a.n_experts > DMAX_E) return KC_ERR_SHAPE;
   const DecodeGeom g = decode_geom(a.type, a.cols);
   switch (a.type) {
-    case T_Q4_K: return launch_decode_t<T_Q4_K>(a, g, max_units, st);
-    case T_Q6_K: return launch_decode_t<T_Q6_K>(a, g, max_units, st);
-    case T_Q8_0: return launch_decode_t<T_Q8_0>(a, g, max_units, st);
+    case T_Q4_K: return launch_decode_t<T_Q4_K>(a, g, max_units, st, max_ctas);
+    case T_Q6_K: return launch_decode_t<T_Q6_K>(a, g, max_units, st, max_ctas);
+    case T_Q8_0: return launch_decode_t<T_Q8_0>(a, g, max_units, st, max_ctas);
     default: return KC_ERR_TYPE;
   }
 }

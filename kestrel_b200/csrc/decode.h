@@ -31,7 +31,8 @@ struct DecodeArgs {
   int type;                // KC_Q4_K / KC_Q6_K / KC_Q8_0
   const int* list;         // expert ids (1..3 rows each)
   const int* n_list;       // device scalar
-  const int* offsets;      // [E+1] slot ranges
+  const int* offsets;      // [n_experts + 1] slot ranges
+  int n_experts;           // entries of offsets minus one (<= 1024)
   const uint8_t* rec;      // activation records (superblock-major, see above)
   int64_t rec_slots;       // slots per superblock plane of rec
   float* out[2];           // out[m][slot * out_stride + row]
@@ -47,14 +48,15 @@ struct DecodeGeom {
   int ks;        // superblocks per K segment (one pipeline stage)
   int nseg;      // segments per row
   int64_t tile_bytes;  // bytes of one 32-row tile
-  int stage_bytes;     // weight bytes of the largest segment, rounded to 128
-  int act_bytes;       // one warp's activation buffer (one segment, all slots)
+  int rec_off;         // weight bytes of the largest segment, rounded to 128:
+                       // the stage's activation records start there
+  int stage_bytes;     // rec_off + ks superblocks x 3 slots of records, rounded to 128
 };
 
 DecodeGeom decode_geom(int t, int64_t cols);
 // max_units: an upper bound of the work units (expert x matrix x 32-row tile)
-// used to size the grid.
-int launch_decode(const DecodeArgs& a, int max_units, cudaStream_t st);
+// used to size the grid; max_ctas (> 0) caps it below the SM count.
+int launch_decode(const DecodeArgs& a, int max_units, cudaStream_t st, int max_ctas = 0);
 
 // Activation records of `n_slots` rows: slot i reads row slot_src[i] of x (i
 // when slot_src is null). With u != null the rows are first combined as

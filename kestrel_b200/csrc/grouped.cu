@@ -1,6 +1,7 @@
 // f32 path of the grouped products (experts with >= 4 rows): the reference
 // dequantises exactly and runs an f32 GEMM (quant.rs:241-260); this kernel
-// does the same arithmetic on CUDA cores (tolerance-checked, not bit-exact).
+// does the same arithmetic on CUDA cores in the same order, bit for bit. It
+// serves shapes the tensor-core kernel does not take and KC_OPT_F32_PREFILL.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -21,9 +22,10 @@ __device__ __forceinline__ void q4k_sm(int jj, uint32_t w0, uint32_t w1, uint32_
 }
 
 // ---------------------------------------------------------------------------
-// f32 path: exact dequantisation (quant.rs:63-205 arithmetic) and f32 FMA
-// products on CUDA cores. CTA tile: 64 weight rows x 32 slots, K chunks of 32.
-constexpr int F_ROWS = 64, F_TOK = 32, F_K = 32, F_THREADS = 256;
+// f32 path: exact dequantisation (quant.rs:63-205 arithmetic), then the
+// reference's f32 GEMM operation order. CTA tile: F_RE weight rows x F_TE
+// slots x 8 lanes; K chunks of F_KC elements.
+constexpr int F_RE = 8, F_TE = 4, F_KC = 512, F_THREADS = F_RE * F_TE * 8;
 
 // Element (r, col) of one expert matrix in the tiled device layout
 // (common.cuh), dequantised with the reference's float operations
@@ -67,82 +69,83 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* __restrict__ mat, i
   }
 }
 
+// One output (weight row r, slot s of an expert with n rows) is computed by 8
+// threads, one per AVX2 lane, exactly as the reference's n >= 4 path does it
+// (quant.rs:241-260 on 48-row tiles, avx2::gemm_f32 / dot_f32 avx2.rs:230-308):
+//  * rows in a tile's 3-row blocks and slots in 4-slot blocks (s < n / 4 * 4):
+//    one fused multiply-add chain per lane over the 8-element chunks, then
+//    hsum;
+//  * the other outputs (dot_f32): even chunks into a0, odd chunks into a1,
+//    a0 + a1 lane-wise, then hsum.
+// The weights are dequantised exactly into shared memory, K chunk by chunk;
+// each lane visits its elements in increasing order, so the results are the
+// reference's bit for bit. CTA: 8 rows x 4 slots x 8 lanes.
 template <int T, bool PAIR>
 __global__ void __launch_bounds__(F_THREADS) grouped_f32_kernel(GroupedArgs a) {
   pdl_enter();
-  __shared__ float Wg[F_ROWS][F_K + 1];
-  __shared__ float Wu[PAIR ? F_ROWS : 1][F_K + 1];
-  __shared__ float X[F_TOK][F_K + 1];
+  __shared__ float Wg[F_RE][F_KC + 4];
+  __shared__ float Wu[PAIR ? F_RE : 1][F_KC + 4];
+  __shared__ float X[F_TE][F_KC + 4];
   const int i = blockIdx.y;
   if (i >= *a.n_list) return;
   const int e = a.list[i];
   const int sbeg = a.offsets[e], n = a.offsets[e + 1] - sbeg;
-  const int t0 = blockIdx.z * F_TOK;
+  const int t0 = blockIdx.z * F_TE;
   if (t0 >= n) return;
-  const int r0 = blockIdx.x * F_ROWS;
-  const int tid = threadIdx.x;
-  const int tr = (tid & 15) * 4, tt = (tid >> 4) * 2;  // 4 rows x 2 slots per thread
-  float ag[4][2], au[4][2];
-#pragma unroll
-  for (int x = 0; x < 4; ++x)
-#pragma unroll
-    for (int y = 0; y < 2; ++y) ag[x][y] = au[x][y] = 0.f;
+  const int r0 = blockIdx.x * F_RE;
+  const int tid = threadIdx.x, j = tid & 7, grp = tid >> 3;
+  const int er = grp % F_RE, tr = grp / F_RE;
+  const int r = r0 + er, t = t0 + tr;
+  // quant.rs:243 tiles rows by 48; gemm_f32 blocks each tile's rows in 3s and
+  // the slots in 4s.
+  const int tile = r / 48, trows = min(48, a.rows - tile * 48);
+  const bool m1 = !((r - tile * 48) < trows / 3 * 3 && t < n / 4 * 4);
   const uint8_t* base0 = a.w0 + (int64_t)(e - a.expert_base) * a.expert_stride;
   const uint8_t* base1 = PAIR ? a.w1 + (int64_t)(e - a.expert_base) * a.expert_stride : nullptr;
-  for (int k0 = 0; k0 < a.cols; k0 += F_K) {
-    for (int idx = tid; idx < F_ROWS * F_K; idx += F_THREADS) {
-      int rr = idx / F_K, kk = idx % F_K, r = r0 + rr;
-      float vg = 0.f, vu = 0.f;
-      if (r < a.rows) {
-        vg = dequant_elem<T>(base0, a.cols, r, k0 + kk);
-        if (PAIR) vu = dequant_elem<T>(base1, a.cols, r, k0 + kk);
-      }
-      Wg[rr][kk] = vg;
-      if (PAIR) Wu[rr][kk] = vu;
+  float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
+  for (int k0 = 0; k0 < a.cols; k0 += F_KC) {
+    const int kn = min(F_KC, a.cols - k0);
+    for (int idx = tid; idx < F_RE * kn; idx += F_THREADS) {
+      const int rr = idx / kn, kk = idx - rr * kn, row = r0 + rr;
+      const bool ok = row < a.rows;
+      Wg[rr][kk] = ok ? dequant_elem<T>(base0, a.cols, row, k0 + kk) : 0.f;
+      if (PAIR) Wu[rr][kk] = ok ? dequant_elem<T>(base1, a.cols, row, k0 + kk) : 0.f;
     }
-    for (int idx = tid; idx < F_TOK * F_K; idx += F_THREADS) {
-      int ss = idx / F_K, kk = idx % F_K, t = t0 + ss;
+    for (int idx = tid; idx < F_TE * kn; idx += F_THREADS) {
+      const int ss = idx / kn, kk = idx - ss * kn, tt = t0 + ss;
       float v = 0.f;
-      if (t < n) {
-        int slot = sbeg + t;
-        int64_t ar = a.slot_src ? a.slot_src[slot] : slot;
+      if (tt < n) {
+        const int slot = sbeg + tt;
+        const int64_t ar = a.slot_src ? a.slot_src[slot] : slot;
         v = a.af[ar * a.cols + k0 + kk];
       }
       X[ss][kk] = v;
     }
     __syncthreads();
-#pragma unroll 8
-    for (int kk = 0; kk < F_K; ++kk) {
-      float xv0 = X[tt][kk], xv1 = X[tt + 1][kk];
-#pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        float wg = Wg[tr + x][kk];
-        ag[x][0] = __fmaf_rn(wg, xv0, ag[x][0]);
-        ag[x][1] = __fmaf_rn(wg, xv1, ag[x][1]);
-        if (PAIR) {
-          float wu = Wu[tr + x][kk];
-          au[x][0] = __fmaf_rn(wu, xv0, au[x][0]);
-          au[x][1] = __fmaf_rn(wu, xv1, au[x][1]);
-        }
+    for (int c = j; c < kn; c += 8) {
+      const bool odd = (((k0 + c) >> 3) & 1) != 0;
+      const float xv = X[tr][c];
+      if (odd && m1) {
+        g1 = __fmaf_rn(Wg[er][c], xv, g1);
+        if (PAIR) u1 = __fmaf_rn(Wu[er][c], xv, u1);
+      } else {
+        g0 = __fmaf_rn(Wg[er][c], xv, g0);
+        if (PAIR) u0 = __fmaf_rn(Wu[er][c], xv, u0);
       }
     }
     __syncthreads();
   }
-#pragma unroll
-  for (int x = 0; x < 4; ++x)
-#pragma unroll
-    for (int y = 0; y < 2; ++y) {
-      int r = r0 + tr + x, t = t0 + tt + y;
-      if (r < a.rows && t < n) {
-        a.out[(int64_t)(sbeg + t) * a.out_stride + r] = ag[x][y];
-        if (PAIR) a.out2[(int64_t)(sbeg + t) * a.out_stride + r] = au[x][y];
-      }
-    }
+  const float vg = hsum8_group(m1 ? __fadd_rn(g0, g1) : g0);
+  const float vu = PAIR ? hsum8_group(m1 ? __fadd_rn(u0, u1) : u0) : 0.f;
+  if (j == 0 && r < a.rows && t < n) {
+    a.out[(int64_t)(sbeg + t) * a.out_stride + r] = vg;
+    if (PAIR) a.out2[(int64_t)(sbeg + t) * a.out_stride + r] = vu;
+  }
 }
 
 template <int T, bool PAIR>
 static int launch_f32_t(const GroupedArgs& a, int max_experts, int max_rows, cudaStream_t st) {
-  dim3 grid(ceil_div(a.rows, F_ROWS), max_experts, ceil_div(max_rows, F_TOK));
+  dim3 grid(ceil_div(a.rows, F_RE), max_experts, ceil_div(max_rows, F_TE));
   launch_k(grouped_f32_kernel<T, PAIR>, grid, F_THREADS, 0, st, a);
   return KC_OK;
 }
@@ -150,7 +153,7 @@ static int launch_f32_t(const GroupedArgs& a, int max_experts, int max_rows, cud
 int launch_grouped_f32(const GroupedArgs& a, bool pair, int max_experts, int max_rows_per_expert,
                        cudaStream_t st) {
   if (max_experts <= 0 || max_rows_per_expert <= 0) return KC_OK;
-  if (a.cols % F_K) return KC_ERR_SHAPE;
+  if (a.cols % 32) return KC_ERR_SHAPE;
   switch (a.type) {
     case T_Q4_K: return pair ? launch_f32_t<T_Q4_K, true>(a, max_experts, max_rows_per_expert, st)
                              : launch_f32_t<T_Q4_K, false>(a, max_experts, max_rows_per_expert, st);

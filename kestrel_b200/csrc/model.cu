@@ -1,0 +1,308 @@
+// Dense decode path kernels (model.h): embedding rows, residual add +
+// RMSNorm, q/k post-processing with the f16 KV cache, causal GQA attention,
+// argmax and the dense SwiGLU. Each follows the reference's operation order
+// (transformer.rs:330-358, 375-467, 594-631) with separate multiplies and
+// adds (the library is built with --fmad=false).
+//
+// Sums the reference folds sequentially (RMSNorm's sum of squares, the
+// attention softmax denominator) are folded by one thread in the same order;
+// only their independent terms are computed in parallel. exp is exp_rn
+// (common.cuh).
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "model.h"
+
+namespace kc {
+
+__device__ __forceinline__ float h2f_at(const uint8_t* p) {
+  return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+}
+
+// scale_min_k4 (quant.rs:54-60).
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& d, int& m) {
+  if (j < 4) {
+    d = q[j] & 63;
+    m = q[j + 4] & 63;
+  } else {
+    d = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+    m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+// Element j of a GGUF row (dequant_row, quant.rs:63-205).
+__device__ float dequant_elem(int t, const uint8_t* row, int j) {
+  if (t == T_F32) return reinterpret_cast<const float*>(row)[j];
+  if (t == T_Q8_0) {
+    const uint8_t* blk = row + (j / 32) * 34;
+    return __fmul_rn((float)(int8_t)blk[2 + j % 32], h2f_at(blk));
+  }
+  if (t == T_Q4_K) {
+    const uint8_t* blk = row + (j / 256) * 144;
+    const int r = j % 256, k = r / 64, l = r % 64, hi = l >= 32, ll = l % 32;
+    int s, m;
+    scale_min_k4(2 * k + hi, blk + 4, s, m);
+    const float dl = __fmul_rn(h2f_at(blk), (float)s), ml = __fmul_rn(h2f_at(blk + 2), (float)m);
+    const uint8_t q = blk[16 + 32 * k + ll];
+    return __fsub_rn(__fmul_rn(dl, (float)(hi ? q >> 4 : q & 0xF)), ml);
+  }
+  if (t == T_Q6_K) {
+    const uint8_t* blk = row + (j / 256) * 210;
+    const int r = j % 256, h = r / 128, qr = (r % 128) / 32, l = r % 32, is = l / 16;
+    const uint8_t* ql = blk + h * 64;
+    const uint8_t* qh = blk + 128 + h * 32;
+    const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + h * 8);
+    const uint8_t lo = qr & 1 ? ql[l + 32] : ql[l];
+    const int nib = qr >= 2 ? lo >> 4 : lo & 0xF;
+    const int q = (nib | (((qh[l] >> (2 * qr)) & 3) << 4)) - 32;
+    return __fmul_rn(__fmul_rn(h2f_at(blk + 208), (float)sc[is + 2 * qr]), (float)q);
+  }
+  return 0.f;
+}
+
+__global__ void embed_kernel(const uint8_t* __restrict__ E, int t, int64_t row_bytes, const uint32_t* __restrict__ tok,
+                             int d, int n_vocab, float* __restrict__ x, int* status) {
+  pdl_enter();
+  const int s = blockIdx.x;
+  const uint32_t id = tok[s];
+  const bool ok = id < (uint32_t)n_vocab;
+  if (!ok && threadIdx.x == 0) report(status, KC_ERR_ARG);
+  const uint8_t* row = E + (int64_t)(ok ? id : 0) * row_bytes;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) x[(int64_t)s * d + j] = ok ? dequant_elem(t, row, j) : 0.f;
+}
+
+void launch_embed(const uint8_t* E, int t, int64_t row_bytes, const uint32_t* tok, int n, int d, int n_vocab,
+                  float* x, int* status, cudaStream_t st) {
+  if (n <= 0) return;
+  launch_k(embed_kernel, n, 256, 0, st, E, t, row_bytes, tok, d, n_vocab, x, status);
+}
+
+// One CTA per row. The squares are formed in parallel; thread 0 folds them in
+// order from -0.0 (Rust's f32 Sum), as transformer.rs:333 does.
+constexpr int NORM_THREADS = 256;
+__global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ y,
+                                                                   const float* __restrict__ w, int dim, float eps,
+                                                                   float* __restrict__ out) {
+  pdl_enter();
+  extern __shared__ float sq[];
+  __shared__ float r_s;
+  float* xr = x + (int64_t)blockIdx.x * dim;
+  float* orow = out + (int64_t)blockIdx.x * dim;
+  for (int j = threadIdx.x; j < dim; j += blockDim.x) {
+    float v = xr[j];
+    if (y) {
+      v = __fadd_rn(v, y[(int64_t)blockIdx.x * dim + j]);
+      xr[j] = v;
+    }
+    sq[j] = __fmul_rn(v, v);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float ss = -0.0f;
+#pragma unroll 8
+    for (int j = 0; j < dim; ++j) ss = __fadd_rn(ss, sq[j]);
+    ss = __fdiv_rn(ss, (float)dim);
+    r_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, eps)));
+  }
+  __syncthreads();
+  const float r = r_s;
+  for (int j = threadIdx.x; j < dim; j += blockDim.x) orow[j] = __fmul_rn(__fmul_rn(xr[j], r), w[j]);
+}
+
+void launch_add_rmsnorm(float* x, const float* y, const float* w, int rows, int dim, float eps, float* out,
+                        cudaStream_t st) {
+  if (rows <= 0) return;
+  launch_k(add_rmsnorm_kernel, rows, NORM_THREADS, (size_t)dim * 4, st, x, y, w, dim, eps, out);
+}
+
+// One warp per (token, head); the head's hd values live in shared memory.
+constexpr int QK_MAX_HD = 256;
+__global__ void __launch_bounds__(32) qk_post_kernel(QkPostArgs a) {
+  pdl_enter();
+  __shared__ float v[QK_MAX_HD];
+  __shared__ float r_s;
+  const int s = blockIdx.x, head = blockIdx.y, lane = threadIdx.x;
+  const int hd = a.hd;
+  const int kind = head < a.nh ? 0 : (head < a.nh + a.nkv ? 1 : 2);  // q, k, v
+  const int hi = kind == 0 ? head : (kind == 1 ? head - a.nh : head - a.nh - a.nkv);
+  const int width = (a.nh + 2 * a.nkv) * hd;
+  const float* src = a.qkv + (int64_t)s * width + (int64_t)head * hd;
+  const float* bias = kind == 0 ? a.bq : (kind == 1 ? a.bk : a.bv);
+  for (int j = lane; j < hd; j += 32) v[j] = bias ? __fadd_rn(src[j], bias[hi * hd + j]) : src[j];
+  __syncwarp();
+  const float* nw = kind == 0 ? a.qn : (kind == 1 ? a.kn : nullptr);
+  if (nw) {
+    if (lane == 0) {
+      float ss = -0.0f;
+      for (int j = 0; j < hd; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+      ss = __fdiv_rn(ss, (float)hd);
+      r_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, a.eps)));
+    }
+    __syncwarp();
+    const float r = r_s;
+    for (int j = lane; j < hd; j += 32) v[j] = __fmul_rn(__fmul_rn(v[j], r), nw[j]);
+    __syncwarp();
+  }
+  const int pos = a.pos0 + s;
+  if (kind < 2) {
+    const int half = a.rd / 2;
+    const float2* tab = a.rope + (int64_t)pos * half;
+    for (int i = lane; i < half; i += 32) {
+      const int ia = a.neox ? i : 2 * i, ib = a.neox ? i + half : 2 * i + 1;
+      const float x0 = v[ia], x1 = v[ib];
+      const float sn = tab[i].x, cs = tab[i].y;
+      v[ia] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+      v[ib] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+    }
+    __syncwarp();
+  }
+  if (kind == 0) {
+    float* q = a.q_out + ((int64_t)s * a.nh + hi) * hd;
+    for (int j = lane; j < hd; j += 32) q[j] = v[j];
+  } else {
+    __half* c = (kind == 1 ? a.kc : a.vc) + (int64_t)pos * a.nkv * hd + (int64_t)hi * hd;
+    for (int j = lane; j < hd; j += 32) c[j] = __float2half_rn(v[j]);
+  }
+}
+
+void launch_qk_post(const QkPostArgs& a, cudaStream_t st) {
+  if (a.n <= 0) return;
+  launch_k(qk_post_kernel, dim3(a.n, a.nh + 2 * a.nkv), 32, 0, st, a);
+}
+
+// One CTA per (query, head). Scores: quant::dot's eight accumulators per
+// position (quant.rs:208-224), in parallel over positions; the max is exact
+// in any order; the exp'd scores are summed by one thread in position order
+// from +0.0; each output element then accumulates (score * inv) * v over the
+// positions in order.
+constexpr int ATT_THREADS = 128;
+__global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __restrict__ q,
+                                                                const __half* __restrict__ kc,
+                                                                const __half* __restrict__ vc, int nh, int nkv,
+                                                                int hd, int pos0, float scale,
+                                                                float* __restrict__ out) {
+  pdl_enter();
+  extern __shared__ float sm[];
+  float* qs = sm;        // [hd]
+  float* sc = sm + hd;   // [n_pos]
+  __shared__ float red[ATT_THREADS / 32];
+  __shared__ float inv_s;
+  const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int kvh = h / (nh / nkv), kvw = nkv * hd;
+  const int n_pos = pos0 + s + 1;
+  for (int j = tid; j < hd; j += blockDim.x) qs[j] = q[((int64_t)s * nh + h) * hd + j];
+  __syncthreads();
+  const int n8 = hd / 8 * 8;
+  float mx = -INFINITY;
+  for (int p = tid; p < n_pos; p += blockDim.x) {
+    const __half* kr = kc + (int64_t)p * kvw + (int64_t)kvh * hd;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < n8; c += 8)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(qs[c + i], __half2float(kr[c + i])));
+    float d = -0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d = __fadd_rn(d, acc[i]);
+    for (int c = n8; c < hd; ++c) d = __fadd_rn(d, __fmul_rn(qs[c], __half2float(kr[c])));
+    const float v = __fmul_rn(d, scale);
+    sc[p] = v;
+    mx = fmaxf(mx, v);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int i = 1; i < ATT_THREADS / 32; ++i) mx = fmaxf(mx, red[i]);
+  for (int p = tid; p < n_pos; p += blockDim.x) sc[p] = exp_rn(__fsub_rn(sc[p], mx));
+  __syncthreads();
+  if (tid == 0) {
+    float sum = 0.0f;
+    for (int p = 0; p < n_pos; ++p) sum = __fadd_rn(sum, sc[p]);
+    inv_s = __fdiv_rn(1.0f, sum);
+  }
+  __syncthreads();
+  const float inv = inv_s;
+  for (int j = tid; j < hd; j += blockDim.x) {
+    float o = 0.0f;
+    const __half* vr = vc + (int64_t)kvh * hd + j;
+    for (int p = 0; p < n_pos; ++p) o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[p], inv), __half2float(vr[(int64_t)p * kvw])));
+    out[((int64_t)s * nh + h) * hd + j] = o;
+  }
+}
+
+void launch_attention(const float* q, const __half* kc, const __half* vc, int n, int nh, int nkv, int hd, int pos0,
+                      float scale, float* out, cudaStream_t st) {
+  if (n <= 0) return;
+  const size_t smem = (size_t)(hd + pos0 + n) * 4;
+  static int attr = 0;
+  if ((int)smem > 48 * 1024 && attr < (int)smem) {
+    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr = 227 * 1024;
+  }
+  launch_k(attention_kernel, dim3(n, nh), ATT_THREADS, smem, st, q, kc, vc, nh, nkv, hd, pos0, scale, out);
+}
+
+// One CTA: strided scans keep the first maximum of each thread, then a
+// reduction that prefers the larger value and, on equal values, the lower
+// index. A NaN never compares greater, so it is never chosen, except at
+// index 0, where the reference's scan starts.
+constexpr int AM_THREADS = 1024;
+__global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restrict__ l, int n, uint32_t* out) {
+  pdl_enter();
+  __shared__ float bv[AM_THREADS / 32];
+  __shared__ int bi[AM_THREADS / 32];
+  const int tid = threadIdx.x;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const float v = l[i];
+    if (idx == 0x7fffffff ? !(v != v) : v > best) {
+      best = v;
+      idx = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (oi != 0x7fffffff && (idx == 0x7fffffff || ov > best || (ov == best && oi < idx))) {
+      best = ov;
+      idx = oi;
+    }
+  }
+  if ((tid & 31) == 0) {
+    bv[tid >> 5] = best;
+    bi[tid >> 5] = idx;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < AM_THREADS / 32; ++w)
+      if (bi[w] != 0x7fffffff && (idx == 0x7fffffff || bv[w] > best || (bv[w] == best && bi[w] < idx))) {
+        best = bv[w];
+        idx = bi[w];
+      }
+    const float l0 = l[0];
+    *out = (l0 != l0 || idx == 0x7fffffff) ? 0u : (uint32_t)idx;
+  }
+}
+
+void launch_argmax(const float* l, int n, uint32_t* out, cudaStream_t st) {
+  launch_k(argmax_kernel, 1, AM_THREADS, 0, st, l, n, out);
+}
+
+__global__ void swiglu_kernel(float* __restrict__ g, const float* __restrict__ u, int64_t n) {
+  pdl_enter();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float gv = g[i];
+    g[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, exp_rn(-gv))), u[i]);
+  }
+}
+
+void launch_swiglu(float* g, const float* u, int64_t n, cudaStream_t st) {
+  if (n <= 0) return;
+  launch_k(swiglu_kernel, (int)std::min<int64_t>(ceil_div(n, 256), 4 * 148), 256, 0, st, g, u, n);
+}
+
+}  // namespace kc

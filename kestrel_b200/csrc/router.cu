@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __res
   for (int e = lane; e < E; e += 32) m = fmaxf(m, row[e]);
 #pragma unroll
   for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  for (int e = lane; e < E; e += 32) p[e] = expf(__fsub_rn(row[e], m));
+  for (int e = lane; e < E; e += 32) p[e] = exp_rn(__fsub_rn(row[e], m));
   __syncwarp();
   // Sequential sum (transformer.rs:481), loads batched ahead of the adds.
   float sum = -0.0f;
@@ -458,7 +458,7 @@ __global__ void shared_add_kernel(const float* __restrict__ y, const float* __re
   const int64_t per = d / 4;
   if (i >= (int64_t)n_tok * per) return;
   const int64_t s = i / per;
-  const float g = logit ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-logit[s]))) : 1.0f;
+  const float g = logit ? __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_rn(-logit[s]))) : 1.0f;
   const float4 v = reinterpret_cast<const float4*>(y)[i];
   float4 o = reinterpret_cast<float4*>(out)[i];
   o.x = __fadd_rn(o.x, __fmul_rn(g, v.x));

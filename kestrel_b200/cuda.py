@@ -55,7 +55,21 @@ SIGNATURES = {
     "kc_ep_unique_id": (I, [ctypes.c_char_p]),
     "kc_ep_init": (I, [P, I, I, ctypes.c_char_p]),
     "kc_ep_reserve": (I, [P, I]),
+    "kc_set_option": (I, [P, I, I]),
+    "kc_model_init": (I, [P, I, I, I, I, I, I, I, I, F, F, I]),
+    "kc_model_tensor": (I, [P, I, I, I, P, I64, I64, I]),
+    "kc_model_forward": (I, [P, P, I, P, P]),
+    "kc_model_generate": (I, [P, P, I, I, P]),
+    "kc_model_truncate": (I, [P, I]),
+    "kc_model_cached": (I, [P]),
 }
+
+# Options (kc_set_option) and whole-model tensor kinds (kc_model_tensor).
+OPT_F32_PREFILL = 1
+ARCH_LLAMA, ARCH_QWEN2, ARCH_QWEN3 = 0, 1, 2
+(T_ATTN_NORM, T_ATTN_Q, T_ATTN_K, T_ATTN_V, T_ATTN_OUT, T_ATTN_Q_BIAS, T_ATTN_K_BIAS, T_ATTN_V_BIAS,
+ T_ATTN_Q_NORM, T_ATTN_K_NORM, T_FFN_NORM, T_FFN_GATE, T_FFN_UP, T_FFN_DOWN) = range(14)
+T_TOKEN_EMBD, T_OUTPUT_NORM, T_OUTPUT = 0, 1, 2
 
 
 class KestrelCudaError(RuntimeError):
@@ -184,16 +198,21 @@ class Context:
 
     # ---- hot path (host buffers) -------------------------------------------
     def moe_ffn(self, layer: int, h, router_w=None, k: int = 0, norm_topk: bool = True,
-                weights_scale: float = 0.0):
-        """Transformer::moe_ffn on host f32 h [n, d] -> (out, topk ids, topk w)."""
+                weights_scale: float = 0.0, out=None, topk: bool = True):
+        """Transformer::moe_ffn on host f32 h [n, d] -> (out, topk ids, topk w).
+        `out`: optional caller buffer (e.g. pinned) for the result; with
+        topk=False the ids and weights are not copied back (returned as None)."""
         h = np.ascontiguousarray(h, dtype=np.float32)
         n, d = h.shape
         rw = None if router_w is None else np.ascontiguousarray(router_w, dtype=np.float32)
         E = 0 if rw is None else rw.shape[0]
         kk = k if rw is not None else self._layer_k(layer)
-        out = np.empty((n, d), np.float32)
-        ids = np.empty((n, kk), np.int32)
-        w = np.empty((n, kk), np.float32)
+        if out is None:
+            out = np.empty((n, d), np.float32)
+        elif out.dtype != np.float32 or out.shape != (n, d) or not out.flags.c_contiguous:
+            raise ValueError("out must be a C-contiguous float32 [n, d] array")
+        ids = np.empty((n, kk), np.int32) if topk else None
+        w = np.empty((n, kk), np.float32) if topk else None
         self._check(lib().kc_moe_ffn(self.h, layer, _ptr(h), n, _ptr(rw), E, k, int(norm_topk), weights_scale,
                                      _ptr(out), _ptr(ids), _ptr(w)))
         return out, ids, w
@@ -259,6 +278,45 @@ class Context:
 
     def ep_init(self, rank: int, world: int, uid: bytes):
         self._check(lib().kc_ep_init(self.h, rank, world, uid))
+
+    # ---- whole model (dense decode path) ---------------------------------------
+    def set_option(self, option: int, value: int):
+        self._check(lib().kc_set_option(self.h, option, int(value)))
+
+    def model_init(self, n_layer: int, d: int, n_head: int, n_head_kv: int, head_dim: int, n_vocab: int,
+                   n_ctx: int, rope_dim: int, rope_base: float, rms_eps: float, arch: int):
+        self._n_vocab = n_vocab
+        self._check(lib().kc_model_init(self.h, n_layer, d, n_head, n_head_kv, head_dim, n_vocab, n_ctx, rope_dim,
+                                        rope_base, rms_eps, arch))
+
+    def model_tensor(self, layer: int, kind: int, t: int, w, rows: int, cols: int):
+        """A model tensor (layer -1) or a layer tensor; host numpy bytes / f32
+        or a torch CUDA tensor."""
+        if _is_dev(w):
+            self._check(lib().kc_model_tensor(self.h, layer, kind, t, _ptr(w), rows, cols, 1))
+            return
+        a = np.ascontiguousarray(w, dtype=np.float32) if t == G.F32 else _host_u8(w)
+        self._check(lib().kc_model_tensor(self.h, layer, kind, t, _ptr(a), rows, cols, 0))
+
+    def model_forward(self, tokens):
+        """Transformer::forward: logits of the last token (and its argmax)."""
+        tk = np.ascontiguousarray(tokens, dtype=np.uint32)
+        logits = np.empty(self._n_vocab, np.float32)
+        nxt = np.zeros(1, np.uint32)
+        self._check(lib().kc_model_forward(self.h, _ptr(tk), tk.size, _ptr(logits), _ptr(nxt)))
+        return logits, int(nxt[0])
+
+    def model_generate(self, prompt, n_gen: int):
+        tk = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(max(1, n_gen), np.uint32)
+        self._check(lib().kc_model_generate(self.h, _ptr(tk), tk.size, n_gen, _ptr(out)))
+        return [int(t) for t in out[:n_gen]]
+
+    def model_truncate(self, keep: int):
+        self._check(lib().kc_model_truncate(self.h, keep))
+
+    def model_cached(self) -> int:
+        return int(lib().kc_model_cached(self.h))
 
     def ep_reserve(self, max_tokens: int):
         """Collective: map the peer exchange arenas for up to max_tokens tokens

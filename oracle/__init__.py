@@ -53,6 +53,11 @@ def lib() -> ctypes.CDLL:
             "ko_moe_ffn": (I, [P, I64, I64, P, I, I, I, F, I, P, I, P, I, P, I64, P, P, P,
                                I, P, I, P, I, P, I64, P]),
             "ko_argmax": (I, [P, I64]),
+            "ko_model_new": (P, [I, I, I, I, I, I, I, I, F, F, I, I, I, I, F]),
+            "ko_model_free": (None, [P]),
+            "ko_model_set": (I, [P, I, I, I, P, I64, I64]),
+            "ko_model_forward": (I, [P, P, I, P]),
+            "ko_model_truncate": (None, [P, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -226,3 +231,60 @@ def moe_ffn(h, router_w, k: int, t_gate: int, gate, t_up: int, up, t_down: int, 
 def argmax(logits) -> int:
     lg = _f32(logits)
     return int(lib().ko_argmax(_p(lg), lg.size))
+
+
+class Model:
+    """Transformer::forward (transformer.rs:287-467) over host weights.
+
+    hp: n_layer, d, n_head, n_kv, head_dim, n_vocab, n_ctx, rope_dim,
+    rope_base, eps, arch (0 llama, 1 qwen2, 2 qwen3), n_expert, k, norm_topk,
+    weights_scale. Tensors are (layer, kind, ggml type, bytes or f32 array,
+    rows, cols); layer -1 for the model tensors (embedding, output norm,
+    output)."""
+
+    def __init__(self, hp: dict):
+        self.hp = dict(hp)
+        L = lib()
+        self._h = L.ko_model_new(hp["n_layer"], hp["d"], hp["n_head"], hp["n_kv"], hp["head_dim"], hp["n_vocab"],
+                                 hp["n_ctx"], hp["rope_dim"], hp["rope_base"], hp["eps"], hp["arch"],
+                                 hp.get("n_expert", 0), hp.get("k", 0), 1 if hp.get("norm_topk", True) else 0,
+                                 hp.get("weights_scale", 0.0))
+        self._keep = []
+
+    def set(self, layer: int, kind: int, t: int, w, rows: int, cols: int) -> None:
+        a = np.ascontiguousarray(w)
+        self._keep.append(a)
+        if lib().ko_model_set(self._h, layer, kind, t, a.ctypes.data, rows, cols):
+            raise ValueError(f"oracle model rejected tensor kind {kind} of layer {layer}")
+
+    def forward(self, tokens) -> np.ndarray:
+        tk = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty(self.hp["n_vocab"], np.float32)
+        rc = lib().ko_model_forward(self._h, tk.ctypes.data, tk.size, out.ctypes.data)
+        if rc:
+            raise ValueError(f"oracle forward failed ({rc})")
+        return out
+
+    def truncate(self, keep: int) -> None:
+        lib().ko_model_truncate(self._h, keep)
+
+    def generate(self, prompt, n_gen: int):
+        """Greedy decode (crates/kestrel-engine/src/lib.rs:116-145 with
+        SamplerConfig::greedy): returns n_gen tokens and the logits each was
+        taken from."""
+        logits = self.forward(prompt)
+        toks, all_logits = [], []
+        for i in range(n_gen):
+            t = int(lib().ko_argmax(logits.ctypes.data, logits.size))
+            toks.append(t)
+            all_logits.append(logits)
+            if i + 1 == n_gen:
+                break
+            logits = self.forward([t])
+        return toks, all_logits
+
+    def __del__(self):
+        try:
+            lib().ko_model_free(self._h)
+        except Exception:
+            pass

@@ -920,6 +920,206 @@ inline float silu_mul(float g, float u) { return g / (1.0f + std::exp(-g)) * u; 
 
 }  // namespace
 
+extern "C" int ko_moe_ffn(const float* h, int64_t n_tok, int64_t d, const float* router_w, int E, int k, int norm_topk,
+               float weights_scale, int t_gate, const uint8_t* gate, int t_up, const uint8_t* up, int t_down,
+               const uint8_t* down, int64_t ff, float* out, int32_t* ids_out, float* w_out, int t_sh_gate,
+               const uint8_t* sh_gate, int t_sh_up, const uint8_t* sh_up, int t_sh_down, const uint8_t* sh_down,
+               int64_t sh_ff, const float* sh_inp);
+
+namespace {
+// ---------------------------------------------------------------------------
+// Transformer::forward (transformer.rs:287-302, 360-467) for llama / qwen2 /
+// qwen3 and their MoE variants, every weight resident in host memory (the
+// pointers given to ko_model_set are kept, not copied). Tensor kinds of a
+// layer (KO_*) and of the model (KO_G_*) share their numbering with the CUDA
+// library's kc_model_tensor.
+enum {
+  KO_ATTN_NORM = 0, KO_WQ, KO_WK, KO_WV, KO_WO, KO_BQ, KO_BK, KO_BV, KO_QNORM, KO_KNORM, KO_FFN_NORM,
+  KO_GATE, KO_UP, KO_DOWN, KO_ROUTER, KO_GATE_EXPS, KO_UP_EXPS, KO_DOWN_EXPS, KO_SH_GATE, KO_SH_UP,
+  KO_SH_DOWN, KO_SH_INP, KO_N_LAYER_T
+};
+enum { KO_G_EMBD = 0, KO_G_OUT_NORM = 1, KO_G_OUTPUT = 2, KO_N_G = 3 };
+
+struct OTensor {
+  int t = -1;
+  const uint8_t* w = nullptr;
+  int64_t rows = 0, cols = 0;
+};
+
+struct OModel {
+  int n_layer = 0, d = 0, n_head = 0, n_kv = 0, hd = 0, n_vocab = 0, n_ctx = 0, rope_dim = 0;
+  float eps = 0.f;
+  bool neox = true;
+  int n_expert = 0, k = 0;
+  bool norm_topk = true;
+  float weights_scale = 0.f;
+  std::vector<float> inv_freq;
+  std::vector<std::vector<OTensor>> layers;
+  OTensor g[KO_N_G];
+  std::vector<std::vector<uint16_t>> kc, vc;  // f16 bits [n_ctx][n_kv * hd] per layer
+  int cached = 0;
+};
+
+// Transformer::vec_of: a small tensor dequantised to f32.
+std::vector<float> vec_of(const OTensor& t) {
+  std::vector<float> v(t.rows * t.cols);
+  const int64_t rb = bytes_for(t.t, t.cols);
+  for (int64_t r = 0; r < t.rows; ++r) dequant_row(t.t, t.w + r * rb, t.cols, v.data() + r * t.cols);
+  return v;
+}
+
+std::vector<float> mm(const OTensor& t, const std::vector<float>& x) {
+  const int64_t s = (int64_t)x.size() / t.cols;
+  std::vector<float> out(s * t.rows);
+  matmul(t.t, t.w, t.rows, t.cols, x.data(), s, out.data(), g_exact);
+  return out;
+}
+
+// Transformer::rmsnorm (transformer.rs:330-340): sum of squares folded in
+// order from -0.0, divided by dim, r = 1 / sqrt(ss + eps), then x * r * w.
+std::vector<float> rmsnorm(const float* x, int64_t n, const std::vector<float>& w, int64_t dim, float eps) {
+  std::vector<float> out(n);
+  for (int64_t r0 = 0; r0 < n; r0 += dim) {
+    float ss = -0.0f;
+    for (int64_t j = 0; j < dim; ++j) ss = ss + x[r0 + j] * x[r0 + j];
+    ss = ss / (float)dim;
+    const float r = 1.0f / std::sqrt(ss + eps);
+    for (int64_t j = 0; j < dim; ++j) out[r0 + j] = x[r0 + j] * r * w[j];
+  }
+  return out;
+}
+
+// Transformer::rope (transformer.rs:342-358).
+void rope(const OModel& m, float* x, int64_t n, int n_heads, int pos0) {
+  const int hd = m.hd, rd = m.rope_dim;
+  const int64_t s_rows = n / ((int64_t)n_heads * hd);
+  for (int64_t s = 0; s < s_rows; ++s) {
+    const float p = (float)(pos0 + s);
+    for (int h = 0; h < n_heads; ++h) {
+      float* v = x + (s * n_heads + h) * hd;
+      for (int i = 0; i < rd / 2; ++i) {
+        const float a_ = p * m.inv_freq[i];
+        const float sn = std::sin(a_), cs = std::cos(a_);
+        const int a = m.neox ? i : 2 * i, b = m.neox ? i + rd / 2 : 2 * i + 1;
+        const float x0 = v[a], x1 = v[b];
+        v[a] = x0 * cs - x1 * sn;
+        v[b] = x0 * sn + x1 * cs;
+      }
+    }
+  }
+}
+
+uint16_t f2h(float f) { return _cvtss_sh(f, _MM_FROUND_TO_NEAREST_INT); }
+float h2f16(uint16_t h) { return _cvtsh_ss(h); }
+
+// Transformer::attention (transformer.rs:594-631): causal GQA over the f16
+// cache; per (query, head) scores = dot * scale, max, exp, sum from +0.0,
+// inv = 1 / sum, then o += (sc * inv) * v position by position.
+std::vector<float> attention(const OModel& m, int l, const std::vector<float>& q, int pos0, int s_rows) {
+  const int hd = m.hd, nh = m.n_head, nkv = m.n_kv, group = nh / nkv;
+  const float scale = 1.0f / std::sqrt((float)hd);
+  const int kvw = nkv * hd, n_tot = pos0 + s_rows;
+  std::vector<float> kf((int64_t)n_tot * kvw), vf((int64_t)n_tot * kvw);
+  for (int64_t i = 0; i < (int64_t)n_tot * kvw; ++i) {
+    kf[i] = h2f16(m.kc[l][i]);
+    vf[i] = h2f16(m.vc[l][i]);
+  }
+  std::vector<float> out((int64_t)s_rows * nh * hd, 0.f);
+  parallel_for((int64_t)s_rows * nh, [&](int64_t i) {
+    const int s = (int)(i / nh), h = (int)(i % nh), kvh = h / group;
+    const float* qv = q.data() + ((int64_t)s * nh + h) * hd;
+    const int n = pos0 + s + 1;
+    std::vector<float> sc(n);
+    for (int p = 0; p < n; ++p) sc[p] = dot_scalar(qv, kf.data() + (int64_t)p * kvw + kvh * hd, hd) * scale;
+    float mx = -INFINITY;
+    for (int p = 0; p < n; ++p) mx = std::fmax(mx, sc[p]);
+    float sum = 0.0f;
+    for (int p = 0; p < n; ++p) {
+      sc[p] = std::exp(sc[p] - mx);
+      sum = sum + sc[p];
+    }
+    const float inv = 1.0f / sum;
+    float* o = out.data() + i * hd;
+    for (int p = 0; p < n; ++p) {
+      const float w = sc[p] * inv;
+      const float* vr = vf.data() + (int64_t)p * kvw + kvh * hd;
+      for (int j = 0; j < hd; ++j) o[j] = o[j] + w * vr[j];
+    }
+  });
+  return out;
+}
+
+void add_into(std::vector<float>& x, const std::vector<float>& y) {
+  for (size_t i = 0; i < x.size(); ++i) x[i] = x[i] + y[i];
+}
+
+// Transformer::forward_chunk_inner (transformer.rs:375-467) for one chunk.
+int forward_chunk(OModel& m, const uint32_t* tokens, int s_rows, float* logits) {
+  const int d = m.d, pos0 = m.cached;
+  std::vector<float> x((int64_t)s_rows * d);
+  const OTensor& E = m.g[KO_G_EMBD];
+  const int64_t erb = bytes_for(E.t, d);
+  for (int s = 0; s < s_rows; ++s) {
+    if ((int)tokens[s] >= m.n_vocab) return -1;
+    dequant_row(E.t, E.w + (int64_t)tokens[s] * erb, d, x.data() + (int64_t)s * d);  // quant::get_row
+  }
+  for (int l = 0; l < m.n_layer; ++l) {
+    const auto& L = m.layers[l];
+    {
+      std::vector<float> h = rmsnorm(x.data(), (int64_t)x.size(), vec_of(L[KO_ATTN_NORM]), d, m.eps);
+      std::vector<float> q = mm(L[KO_WQ], h), k = mm(L[KO_WK], h), v = mm(L[KO_WV], h);
+      const int bias_kind[3] = {KO_BQ, KO_BK, KO_BV};
+      std::vector<float>* ys[3] = {&q, &k, &v};
+      for (int i = 0; i < 3; ++i)
+        if (L[bias_kind[i]].w) {
+          std::vector<float> b = vec_of(L[bias_kind[i]]);
+          for (size_t r = 0; r < ys[i]->size(); ++r) (*ys[i])[r] = (*ys[i])[r] + b[r % b.size()];
+        }
+      if (L[KO_QNORM].w) q = rmsnorm(q.data(), (int64_t)q.size(), vec_of(L[KO_QNORM]), m.hd, m.eps);
+      if (L[KO_KNORM].w) k = rmsnorm(k.data(), (int64_t)k.size(), vec_of(L[KO_KNORM]), m.hd, m.eps);
+      rope(m, q.data(), (int64_t)q.size(), m.n_head, pos0);
+      rope(m, k.data(), (int64_t)k.size(), m.n_kv, pos0);
+      const int kvw = m.n_kv * m.hd;
+      for (int s = 0; s < s_rows; ++s)
+        for (int j = 0; j < kvw; ++j) {
+          m.kc[l][(int64_t)(pos0 + s) * kvw + j] = f2h(k[(int64_t)s * kvw + j]);
+          m.vc[l][(int64_t)(pos0 + s) * kvw + j] = f2h(v[(int64_t)s * kvw + j]);
+        }
+      std::vector<float> ctx = attention(m, l, q, pos0, s_rows);
+      add_into(x, mm(L[KO_WO], ctx));
+    }
+    {
+      std::vector<float> h = rmsnorm(x.data(), (int64_t)x.size(), vec_of(L[KO_FFN_NORM]), d, m.eps);
+      std::vector<float> y((int64_t)s_rows * d);
+      if (L[KO_ROUTER].w) {
+        const OTensor &G = L[KO_GATE_EXPS], &U = L[KO_UP_EXPS], &D = L[KO_DOWN_EXPS];
+        const int64_t ff = G.rows / m.n_expert;
+        const OTensor &SG = L[KO_SH_GATE], &SU = L[KO_SH_UP], &SD = L[KO_SH_DOWN];
+        std::vector<float> sh_inp;
+        if (L[KO_SH_INP].w) sh_inp = vec_of(L[KO_SH_INP]);
+        int rc = ko_moe_ffn(h.data(), s_rows, d, (const float*)L[KO_ROUTER].w, m.n_expert, m.k, m.norm_topk,
+                            m.weights_scale, G.t, G.w, U.t, U.w, D.t, D.w, ff, y.data(), nullptr, nullptr, SG.t,
+                            SG.w, SU.t, SU.w, SD.t, SD.w, SG.rows, sh_inp.empty() ? nullptr : sh_inp.data());
+        if (rc) return rc;
+      } else {
+        std::vector<float> g = mm(L[KO_GATE], h), u = mm(L[KO_UP], h);
+        for (size_t i = 0; i < g.size(); ++i) g[i] = silu_mul(g[i], u[i]);
+        y = mm(L[KO_DOWN], g);
+      }
+      add_into(x, y);
+    }
+  }
+  m.cached += s_rows;
+  const float* last = x.data() + (int64_t)(s_rows - 1) * d;
+  std::vector<float> normed = rmsnorm(last, d, vec_of(m.g[KO_G_OUT_NORM]), d, m.eps);
+  const OTensor& O = m.g[KO_G_OUTPUT].w ? m.g[KO_G_OUTPUT] : m.g[KO_G_EMBD];  // tied embeddings
+  std::vector<float> lg = mm(O, normed);
+  std::memcpy(logits, lg.data(), lg.size() * 4);
+  return 0;
+}
+
+}  // namespace
+
 // ===========================================================================
 // C ABI (ctypes). All pointers are host pointers; sizes in elements.
 extern "C" {
@@ -1060,6 +1260,52 @@ int ko_moe_ffn(const float* h, int64_t n_tok, int64_t d, const float* router_w, 
     }
   }
   return 0;
+}
+
+// ---- model (Transformer) ----------------------------------------------------
+// arch: 0 llama (interleaved RoPE), 1 qwen2, 2 qwen3 (NeoX RoPE; transformer.rs:241).
+void* ko_model_new(int n_layer, int d, int n_head, int n_kv, int head_dim, int n_vocab, int n_ctx, int rope_dim,
+                   float rope_base, float eps, int arch, int n_expert, int k, int norm_topk, float weights_scale) {
+  OModel* m = new OModel();
+  m->n_layer = n_layer; m->d = d; m->n_head = n_head; m->n_kv = n_kv; m->hd = head_dim; m->n_vocab = n_vocab;
+  m->n_ctx = n_ctx; m->rope_dim = rope_dim; m->eps = eps; m->neox = arch != 0;
+  m->n_expert = n_expert; m->k = k; m->norm_topk = norm_topk != 0; m->weights_scale = weights_scale;
+  for (int i = 0; i < rope_dim / 2; ++i)  // transformer.rs:248
+    m->inv_freq.push_back(std::pow(rope_base, -(2.0f * (float)i) / (float)rope_dim));
+  m->layers.assign(n_layer, std::vector<OTensor>(KO_N_LAYER_T));
+  m->kc.assign(n_layer, std::vector<uint16_t>((int64_t)n_ctx * n_kv * head_dim, 0));
+  m->vc.assign(n_layer, std::vector<uint16_t>((int64_t)n_ctx * n_kv * head_dim, 0));
+  return m;
+}
+void ko_model_free(void* p) { delete (OModel*)p; }
+// layer < 0: a model tensor (KO_G_*).
+int ko_model_set(void* p, int layer, int kind, int t, const void* w, int64_t rows, int64_t cols) {
+  OModel* m = (OModel*)p;
+  OTensor T;
+  T.t = t; T.w = (const uint8_t*)w; T.rows = rows; T.cols = cols;
+  if (layer < 0) {
+    if (kind < 0 || kind >= KO_N_G) return -1;
+    m->g[kind] = T;
+  } else {
+    if (layer >= m->n_layer || kind < 0 || kind >= KO_N_LAYER_T) return -1;
+    m->layers[layer][kind] = T;
+  }
+  return 0;
+}
+// Transformer::forward: feed tokens after the cached ones (chunks of
+// n_batch = 256, transformer.rs:287-302); logits [n_vocab] of the last token.
+int ko_model_forward(void* p, const uint32_t* tokens, int n, float* logits) {
+  OModel* m = (OModel*)p;
+  if (n < 1 || m->cached + n > m->n_ctx) return -2;
+  for (int c = 0; c < n; c += 256) {
+    int rc = forward_chunk(*m, tokens + c, std::min(256, n - c), logits);
+    if (rc) return rc;
+  }
+  return 0;
+}
+void ko_model_truncate(void* p, int keep) {
+  OModel* m = (OModel*)p;
+  m->cached = std::min(m->cached, std::max(0, keep));
 }
 
 // sampler::argmax (sampler.rs:104-112): first maximum wins.

@@ -36,3 +36,25 @@ def upload(ctx, layer_id, L, norm_topk=True, weights_scale=0.0):
 def oracle_layer(oracle, L, h, norm_topk=True, weights_scale=0.0):
     return oracle.moe_ffn(h, L["router"], L["k"], L["t_gate"], L["gate"], L["t_gate"], L["up"], L["t_down"],
                           L["down"], L["ff"], norm_topk=norm_topk, weights_scale=weights_scale)
+
+
+# Oracle tensor kinds (oracle/kestrel_oracle.cpp KO_*) by GGUF name.
+ORACLE_KINDS = {"attn_norm": 0, "attn_q": 1, "attn_k": 2, "attn_v": 3, "attn_output": 4, "attn_q_bias": 5,
+                "attn_k_bias": 6, "attn_v_bias": 7, "attn_q_norm": 8, "attn_k_norm": 9, "ffn_norm": 10,
+                "ffn_gate": 11, "ffn_up": 12, "ffn_down": 13, "ffn_gate_inp": 14, "ffn_gate_exps": 15,
+                "ffn_up_exps": 16, "ffn_down_exps": 17}
+ORACLE_MODEL_KINDS = {"token_embd": 0, "output_norm": 1, "output": 2}
+
+
+def oracle_model(oracle, model, n_ctx):
+    """The oracle's Transformer over a kestrel_b200.synth model."""
+    c = model["cfg"]
+    m = oracle.Model(dict(n_layer=c["n_layer"], d=c["d"], n_head=c["n_head"], n_kv=c["n_kv"],
+                          head_dim=c["head_dim"], n_vocab=c["n_vocab"], n_ctx=n_ctx, rope_dim=c["rope_dim"],
+                          rope_base=c["rope_base"], eps=c["eps"], arch=c["arch"], n_expert=c.get("n_expert", 0),
+                          k=c.get("k", 0), norm_topk=c.get("norm_topk", True),
+                          weights_scale=c.get("weights_scale", 0.0)))
+    for layer, name, t, data, rows, cols in model["tensors"]:
+        kind = ORACLE_MODEL_KINDS[name] if layer < 0 else ORACLE_KINDS[name]
+        m.set(layer, kind, t, data, rows, cols)
+    return m
