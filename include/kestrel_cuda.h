@@ -278,6 +278,30 @@ KC_API int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, 
 KC_API int kc_model_truncate(kc_ctx* ctx, int keep);
 KC_API int kc_model_cached(const kc_ctx* ctx);
 
+/* ---- model files -----------------------------------------------------------
+   GGUF v2/v3 and Kestrel-prepared KGUF containers (GgufFile::open,
+   crates/kestrel-gguf/src/lib.rs:196-311; strided expert slices read at
+   TensorInfo::slice_offset, lib.rs:183-189). Hyper-parameters as kestrel-model
+   reads them (crates/kestrel-model/src/lib.rs:170-215, 338-373). */
+
+/* Declare the file's model on the context (kc_model_init) and upload every
+   tensor Transformer::new reads (transformer.rs:147-213): the dense ones
+   through kc_model_tensor, routed experts, router and shared expert through
+   kc_upload_experts / kc_upload_router / kc_upload_shared_expert -- the
+   HBM-resident expert table in place of ExpertStore::preload_all
+   (NativeSession::load, crates/kestrel-backends/src/lib.rs:133-157). Before
+   uploading anything, the device bytes of the weights, the f16 KV cache for
+   n_ctx positions and a workspace allowance are checked against the GPU's
+   free memory: a model that does not fit returns KC_ERR_OOM (the VRAM tier
+   of the planner's placement decision, crates/kestrel-planner/src/
+   lib.rs:429-439). info_json (optional, cap bytes) receives a JSON summary.
+   Types with kernels: F32, Q8_0, Q4_K, Q6_K; others return KC_ERR_TYPE. */
+KC_API int kc_load_gguf(kc_ctx* ctx, const char* path, int n_ctx, char* info_json, int64_t cap);
+/* Parse a GGUF / KGUF file without a GPU or a context: a JSON description
+   (version, alignment, derived hyper-parameters, tensors with file offsets,
+   sizes and strides) into out (cap bytes). Errors: kc_last_error(NULL). */
+KC_API int kc_gguf_inspect(const char* path, char* out, int64_t cap);
+
 /* ---- expert parallelism (one process per GPU, NCCL over NVLink) -------- */
 
 /* 128-byte NCCL unique id, created on one rank and shared by the host. */

@@ -17,6 +17,7 @@
 #include "ep.h"
 #include "kernels.h"
 #include "mma.h"
+#include "loader.h"
 #include "model.h"
 
 using namespace kc;
@@ -84,6 +85,10 @@ struct Work {
   float* router_tmp = nullptr;
   float* mma_part = nullptr;  // split-K partial tiles of the tcgen05 kernel
   int* mma_cnt = nullptr;     // its per-tile counters (zeroed at allocation)
+  // Metadata of a dense product of dmeta_n rows (one group), kept apart from
+  // the MoE dispatch so that repeated products with the same n reuse it.
+  DispatchOut dmeta{};
+  int dmeta_n = -1;
 };
 
 // Expert-parallel exchange buffers. Home side (this rank's tokens): routing,
@@ -257,6 +262,7 @@ int ensure_work(kc_ctx* ctx, Work& w, int T, int E, int K, int D, int F) {
       (size_t)T * D * 4, (size_t)T * D * 4,  // h_in, out
       (size_t)E * D * 4,                 // router_tmp
       mma_part_bytes(), mma_cnt_bytes(),  // mma_part, mma_cnt
+      64, 64, 64, 64, 64, 64,             // dmeta: counts, offsets, small, large, n_lists, large_tt
   };
   size_t total = 0;
   for (size_t s : sz) total += al(s);
@@ -305,6 +311,13 @@ int ensure_work(kc_ctx* ctx, Work& w, int T, int E, int K, int D, int F) {
   take((void**)&w.router_tmp);
   take((void**)&w.mma_part);
   take((void**)&w.mma_cnt);
+  take((void**)&w.dmeta.counts);
+  take((void**)&w.dmeta.offsets);
+  take((void**)&w.dmeta.small_list);
+  take((void**)&w.dmeta.large_list);
+  take((void**)&w.dmeta.n_lists);
+  take((void**)&w.dmeta.large_tt);
+  w.dmeta_n = -1;
   CK(cudaMemsetAsync(w.mma_cnt, 0, mma_cnt_bytes(), ctx->stream));
   return KC_OK;
 }
@@ -428,19 +441,22 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   const bool mma_gu = !ctx->f32_prefill && mma_supported(L.t_gate, d, 2);
   const bool mma_dn = !ctx->f32_prefill && mma_supported(L.t_down, ff, 1) && ff % 256 == 0;
   const int max_tt = ceil_div(A, kMmaTileN) + std::min(E, A / 4);
-  // The int8 (1-3 rows) and n >= 4 launches of a stage are independent: the
-  // n >= 4 one runs on the auxiliary stream, concurrently, and the int8 kernel
-  // leaves it `split` SMs (the rest of its grid queues for the SMs the int8
-  // kernel frees). The split follows the expected weight bytes of each path,
-  // with routing modelled as uniform (rows per expert ~ Poisson(A / E)).
+  // The int8 (1-3 rows) and n >= 4 launches of a stage are independent. When
+  // few experts are expected to reach 4 rows (rows per expert ~ Poisson(A / E)
+  // for uniform routing, A / E <= 2), the n >= 4 launch, which is then
+  // latency-bound, runs on the auxiliary stream beside the int8 one: the int8
+  // kernel leaves it `split` SMs (in proportion to the expected weight bytes
+  // of each path, at least 8) and the rest of its grid takes the SMs the int8
+  // kernel frees. With more rows per expert both run one after the other on
+  // all SMs.
   int split = 0;
-  const bool fork = any_large && !ctx->prof.on;
+  const bool fork = any_large && !ctx->prof.on && (double)A <= 2.0 * E;
   if (fork) {
     RC(ensure_aux(ctx));
     const double lam = (double)A / E, p0 = std::exp(-lam);
     const double f_small = p0 * (lam + lam * lam / 2 + lam * lam * lam / 6), f_large = std::max(0.0, 1 - p0 - f_small);
     const int nsm = num_sms();
-    split = std::min(nsm - 8, std::max(8, (int)std::lround(nsm * f_large / std::max(1e-9, f_small + f_large))));
+    split = std::min(nsm / 2, std::max(8, (int)std::lround(nsm * f_large / std::max(1e-9, f_small + f_large))));
   }
   const int dec_ctas = num_sms() - split;
   auto fork_aux = [&]() -> int {
@@ -628,8 +644,12 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
   }
   RC(ensure_work(ctx, n, 1, 1, (int)std::min<int64_t>(D.cols, 1 << 30), 256));
   Work& W = ctx->ws;
-  launch_dense_meta(n, W.meta, st);
-  CKL();
+  if (W.dmeta_n != n) {
+    launch_dense_meta(n, W.dmeta, st);
+    CKL();
+    W.dmeta_n = n;
+  }
+  const DispatchOut& M = W.dmeta;
   GroupedArgs a = grouped_base(ctx);
   a.w0 = D.w;
   a.expert_stride = 0;
@@ -637,7 +657,7 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
   a.rows = (int)D.rows;
   a.cols = (int)D.cols;
   a.type = D.t;
-  a.offsets = W.meta.offsets;
+  a.offsets = M.offsets;
   a.slot_src = nullptr;
   a.af = x;
   a.out = out;
@@ -652,9 +672,9 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     dv.rows = (int)D.rows;
     dv.cols = (int)D.cols;
     dv.type = D.t;
-    dv.list = W.meta.small_list;
-    dv.n_list = W.meta.n_lists;
-    dv.offsets = W.meta.offsets;
+    dv.list = M.small_list;
+    dv.n_list = M.n_lists;
+    dv.offsets = M.offsets;
     dv.n_experts = 1;
     dv.rec = W.xrec;
     dv.rec_slots = n;
@@ -675,17 +695,17 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     ma.rows = (int)D.rows;
     ma.cols = (int)D.cols;
     ma.type = D.t;
-    ma.list = W.meta.large_list;
-    ma.n_list = W.meta.n_lists + 1;
-    ma.offsets = W.meta.offsets;
-    ma.tt_prefix = W.meta.large_tt;
+    ma.list = M.large_list;
+    ma.n_list = M.n_lists + 1;
+    ma.offsets = M.offsets;
+    ma.tt_prefix = M.large_tt;
     ma.out[0] = out;
     ma.out_stride = D.rows;
     ma.status = ctx->status;
     RC(launch_mma_grouped(ma, tmap, ceil_div(n, kMmaTileN) * ceil_div(D.rows, 128), st));
   } else {
-    a.list = W.meta.large_list;
-    a.n_list = W.meta.n_lists + 1;
+    a.list = M.large_list;
+    a.n_list = M.n_lists + 1;
     RC(launch_grouped_f32(a, false, 1, n, st));
   }
   CKL();
@@ -1322,6 +1342,7 @@ int kc_set_stream(kc_ctx* ctx, void* s) {
     ctx->own_stream = false;
   }
   ctx->stream = static_cast<cudaStream_t>(s);
+  ctx->ws.dmeta_n = -1;  // rewritten on the new stream before its next use
   return KC_OK;
 }
 
@@ -1722,7 +1743,8 @@ int kc_model_init(kc_ctx* ctx, int n_layer, int d, int n_head, int n_head_kv, in
   if (!ctx) return KC_ERR_ARG;
   ctx->err.clear();
   if (n_layer < 1 || d < 1 || n_head < 1 || n_head_kv < 1 || n_head % n_head_kv || head_dim < 1 ||
-      head_dim > 256 || n_vocab < 1 || n_ctx < 1 || rope_dim < 0 || rope_dim > head_dim || rope_dim % 2 ||
+      head_dim > 256 || head_dim % 8 || n_vocab < 1 || n_ctx < 1 || n_ctx > attention_max_positions(head_dim) ||
+      rope_dim < 0 || rope_dim > head_dim || rope_dim % 2 ||
       arch < KC_ARCH_LLAMA || arch > KC_ARCH_QWEN3)
     return fail(ctx, KC_ERR_ARG, "kc_model_init: bad hyper-parameters");
   cudaSetDevice(ctx->device);
@@ -1877,5 +1899,59 @@ int kc_model_truncate(kc_ctx* ctx, int keep) {
 }
 
 int kc_model_cached(const kc_ctx* ctx) { return ctx && ctx->model ? ctx->model->cached : 0; }
+
+// ---- model files -----------------------------------------------------------
+int kc_gguf_inspect(const char* path, char* out, int64_t cap) {
+  if (!path || (!out && cap > 0)) {
+    set_global_error("kc_gguf_inspect: bad arguments");
+    return KC_ERR_ARG;
+  }
+  std::string json, err;
+  const int rc = gguf_inspect(path, json, err);
+  if (rc != KC_OK) {
+    set_global_error(("kc_gguf_inspect: " + err).c_str());
+    return rc;
+  }
+  if ((int64_t)json.size() + 1 > cap) {
+    set_global_error("kc_gguf_inspect: output buffer too small");
+    return KC_ERR_SHAPE;
+  }
+  memcpy(out, json.c_str(), json.size() + 1);
+  return KC_OK;
+}
+
+int kc_load_gguf(kc_ctx* ctx, const char* path, int n_ctx, char* info_json, int64_t cap) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!path || n_ctx < 1) return fail(ctx, KC_ERR_ARG, "kc_load_gguf: bad arguments");
+  cudaSetDevice(ctx->device);
+  LoadSink s{};
+  s.ctx = ctx;
+  s.model_init = [](void* c, int nl, int d, int nh, int nkv, int hd, int nv, int nc, int rd, float rb, float eps,
+                    int arch) { return kc_model_init((kc_ctx*)c, nl, d, nh, nkv, hd, nv, nc, rd, rb, eps, arch); };
+  s.model_tensor = [](void* c, int l, int kind, int t, const void* w, int64_t r, int64_t cl) {
+    return kc_model_tensor((kc_ctx*)c, l, kind, t, w, r, cl, 0);
+  };
+  s.experts = [](void* c, int l, int E, int d, int ff, int tg, const void* g, int tu, const void* u, int td,
+                 const void* dn) { return kc_upload_experts((kc_ctx*)c, l, E, d, ff, tg, g, tu, u, td, dn, 0); };
+  s.router = [](void* c, int l, const float* w, int E, int d, int k, int nt, float ws) {
+    return kc_upload_router((kc_ctx*)c, l, w, E, d, k, nt, ws, 0);
+  };
+  s.shared = [](void* c, int l, int ff, int d, int tg, const void* g, int tu, const void* u, int td, const void* dn,
+                const float* gi) { return kc_upload_shared_expert((kc_ctx*)c, l, ff, d, tg, g, tu, u, td, dn, gi, 0); };
+  s.device_bytes_of = [](int t, int64_t rows, int64_t cols) -> int64_t { return dev_matrix_bytes(t, rows, cols); };
+  std::string err, info;
+  const int rc = gguf_load(path, n_ctx, s, err, info);
+  if (info_json && cap > 0) {
+    const size_t n = std::min<size_t>(info.size(), (size_t)cap - 1);
+    memcpy(info_json, info.data(), n);
+    info_json[n] = 0;
+  }
+  if (rc != KC_OK) {
+    if (!err.empty() && ctx->err.empty()) ctx->err = "kc_load_gguf: " + err;
+    return rc;
+  }
+  return KC_OK;
+}
 
 }  // extern "C"

@@ -511,13 +511,7 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
   const int tiles = (int)(padded_rows(a.rows) / DR);
   const int per_expert = a.n_mat * tiles;
   const int total = n_list * per_expert;
-  // Units are dealt to the CTAs round-robin (unit b, b + G, b + 2G, ...), so
-  // every CTA gets a mix of experts with 1, 2 and 3 rows, whose compute
-  // differs, instead of a contiguous run of one or two experts.
-  const int G = gridDim.x, b = blockIdx.x;
-  if (b >= total) return;
-  const int n_units = (total - b + G - 1) / G;
-  const int n_groups = (n_units + DW - 1) / DW;
+  if (total == 0) return;
   for (int i = tid; i < n_list; i += blockDim.x) list_s[i] = a.list[i];
   for (int i = tid; i <= a.n_experts && i <= DMAX_E; i += blockDim.x) off_s[i] = a.offsets[i];
   if (tid == 0) {
@@ -528,6 +522,13 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
     fence_mbar_init();
   }
   __syncthreads();
+  // Units are dealt to the CTAs round-robin (unit b, b + G, b + 2G, ...): a
+  // CTA's groups then mix experts with 1, 2 and 3 rows, whose compute
+  // differs, and every CTA gets the same mix on average.
+  const int G = gridDim.x, b = blockIdx.x;
+  const int n_units = b < total ? (total - b + G - 1) / G : 0;
+  if (n_units <= 0) return;
+  const int n_groups = (n_units + DW - 1) / DW;
   uint8_t* ring = smem;
   auto unit_at = [&](int i) { return unit_pos(b + i * G, tiles, a.n_mat); };
 

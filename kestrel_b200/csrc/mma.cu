@@ -522,7 +522,7 @@ bool mma_supported(int t, int64_t cols, int n_mat) {
 }
 
 template <int T, int NMAT>
-static int launch_t(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st) {
+static int launch_t(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st, int max_ctas) {
   const MmaSmem L = mma_smem(T, NMAT);
   static bool attr = false;
   if (!attr) {
@@ -533,7 +533,8 @@ static int launch_t(const MmaArgs& a, const void* tmap, int max_tiles, cudaStrea
   }
   // With a split-K workspace every SM gets a CTA (the kernel splits K when the
   // batch has few tiles); otherwise one CTA per tile at most.
-  const int grid = a.part ? num_sms() : std::max(1, std::min(num_sms(), max_tiles));
+  const int cap = max_ctas > 0 ? std::min(max_ctas, num_sms()) : num_sms();
+  const int grid = a.part ? cap : std::max(1, std::min(cap, max_tiles));
   launch_k(mma_grouped_kernel<T, NMAT>, grid, M_THREADS, (size_t)L.total, st, a,
            *reinterpret_cast<const CUtensorMap*>(tmap));
   return KC_OK;
@@ -542,17 +543,17 @@ static int launch_t(const MmaArgs& a, const void* tmap, int max_tiles, cudaStrea
 size_t mma_part_bytes() { return (size_t)num_sms() * 2 * MM * MN * sizeof(float); }
 size_t mma_cnt_bytes() { return (size_t)num_sms() * sizeof(int); }
 
-int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st) {
+int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st, int max_ctas) {
   if (max_tiles <= 0) return KC_OK;
   if (!mma_supported(a.type, a.cols, a.n_mat)) return KC_ERR_SHAPE;
   if (a.n_mat == 2) {
-    if (a.type == T_Q4_K) return launch_t<T_Q4_K, 2>(a, tmap, max_tiles, st);
-    if (a.type == T_Q6_K) return launch_t<T_Q6_K, 2>(a, tmap, max_tiles, st);
-    return launch_t<T_Q8_0, 2>(a, tmap, max_tiles, st);
+    if (a.type == T_Q4_K) return launch_t<T_Q4_K, 2>(a, tmap, max_tiles, st, max_ctas);
+    if (a.type == T_Q6_K) return launch_t<T_Q6_K, 2>(a, tmap, max_tiles, st, max_ctas);
+    return launch_t<T_Q8_0, 2>(a, tmap, max_tiles, st, max_ctas);
   }
-  if (a.type == T_Q4_K) return launch_t<T_Q4_K, 1>(a, tmap, max_tiles, st);
-  if (a.type == T_Q6_K) return launch_t<T_Q6_K, 1>(a, tmap, max_tiles, st);
-  return launch_t<T_Q8_0, 1>(a, tmap, max_tiles, st);
+  if (a.type == T_Q4_K) return launch_t<T_Q4_K, 1>(a, tmap, max_tiles, st, max_ctas);
+  if (a.type == T_Q6_K) return launch_t<T_Q6_K, 1>(a, tmap, max_tiles, st, max_ctas);
+  return launch_t<T_Q8_0, 1>(a, tmap, max_tiles, st, max_ctas);
 }
 
 }  // namespace kc

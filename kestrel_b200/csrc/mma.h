@@ -35,6 +35,7 @@ size_t mma_cnt_bytes();
 // box 64 x kMmaTileN, 128B swizzle.
 int make_tmap_f16(void* map_out, const void* ptr, int64_t rows, int64_t cols);
 bool mma_supported(int t, int64_t cols, int n_mat);
-int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st);
+// max_ctas > 0: at most that many CTAs (the kernel splits K over what it gets).
+int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st, int max_ctas = 0);
 
 }  // namespace kc

@@ -171,51 +171,82 @@ void launch_qk_post(const QkPostArgs& a, cudaStream_t st) {
   launch_k(qk_post_kernel, dim3(a.n, a.nh + 2 * a.nkv), 32, 0, st, a);
 }
 
-// One CTA per (query, head). Scores: quant::dot's eight accumulators per
-// position (quant.rs:208-224), in parallel over positions; the max is exact
-// in any order; the exp'd scores are summed by one thread in position order
-// from +0.0; each output element then accumulates (score * inv) * v over the
-// positions in order.
-constexpr int ATT_THREADS = 128;
+// One CTA per (query, head). K and V of the head's KV group are staged
+// through shared memory in chunks of ATT_PC positions with 16-byte coalesced
+// loads. Scores: quant::dot's eight accumulators per position (quant.rs:
+// 208-224) -- thread (position, i) forms accumulator i over the 8-element
+// chunks in order, and the position's first thread folds the eight from -0.0
+// -- then * scale. The max is exact in any order; the exp'd scores are summed
+// by one thread in position order from +0.0; each output element then
+// accumulates (score * inv) * v over the positions in order.
+constexpr int ATT_THREADS = 256;
+constexpr int ATT_PC = 64;  // positions per staged chunk
+
+__device__ __forceinline__ void stage_rows(__half* dst, const __half* src, int n_rows, int hd, int64_t row_stride,
+                                           int tid) {
+  // n_rows rows of hd halves (hd % 8 == 0: 16-byte pieces).
+  const int per_row = hd / 8;
+  for (int i = tid; i < n_rows * per_row; i += ATT_THREADS) {
+    const int r = i / per_row, c = i - r * per_row;
+    reinterpret_cast<uint4*>(dst + (int64_t)r * hd)[c] = reinterpret_cast<const uint4*>(src + r * row_stride)[c];
+  }
+}
+
 __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __restrict__ q,
                                                                 const __half* __restrict__ kc,
                                                                 const __half* __restrict__ vc, int nh, int nkv,
                                                                 int hd, int pos0, float scale,
                                                                 float* __restrict__ out) {
   pdl_enter();
-  extern __shared__ float sm[];
-  float* qs = sm;        // [hd]
-  float* sc = sm + hd;   // [n_pos]
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                                        // [hd]
+  __half* ks = reinterpret_cast<__half*>(sm + hd);      // [ATT_PC][hd] (K, then V)
+  float* sc = sm + hd + ATT_PC * hd / 2;                 // [n_pos]
   __shared__ float red[ATT_THREADS / 32];
   __shared__ float inv_s;
-  const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
   const int kvh = h / (nh / nkv), kvw = nkv * hd;
   const int n_pos = pos0 + s + 1;
-  for (int j = tid; j < hd; j += blockDim.x) qs[j] = q[((int64_t)s * nh + h) * hd + j];
-  __syncthreads();
-  const int n8 = hd / 8 * 8;
+  for (int j = tid; j < hd; j += ATT_THREADS) qs[j] = q[((int64_t)s * nh + h) * hd + j];
+  const __half* kbase = kc + (int64_t)kvh * hd;
+  const __half* vbase = vc + (int64_t)kvh * hd;
+  const int n8 = hd / 8;
   float mx = -INFINITY;
-  for (int p = tid; p < n_pos; p += blockDim.x) {
-    const __half* kr = kc + (int64_t)p * kvw + (int64_t)kvh * hd;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < n8; c += 8)
+  for (int p0 = 0; p0 < n_pos; p0 += ATT_PC) {
+    const int np = min(ATT_PC, n_pos - p0);
+    __syncthreads();
+    stage_rows(ks, kbase + (int64_t)p0 * kvw, np, hd, kvw, tid);
+    __syncthreads();
+    // Whole warps take part in every iteration (the shuffles below): the
+    // bound is rounded up to 32 and positions past np compute nothing.
+    const int tot = (np * 8 + 31) & ~31;
+    for (int t = tid; t < tot; t += ATT_THREADS) {
+      const int pp = t >> 3, i = t & 7;
+      const bool valid = pp < np;
+      const __half* kr = ks + (valid ? pp : 0) * hd;
+      float acc = 0.f;
+      if (valid)
+        for (int m = 0; m < n8; ++m) acc = __fadd_rn(acc, __fmul_rn(qs[8 * m + i], __half2float(kr[8 * m + i])));
+      // Fold the position's eight accumulators in order (8-lane groups are
+      // aligned within the warp: t and tid share their low 3 bits).
+      float d = -0.0f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(qs[c + i], __half2float(kr[c + i])));
-    float d = -0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) d = __fadd_rn(d, acc[i]);
-    for (int c = n8; c < hd; ++c) d = __fadd_rn(d, __fmul_rn(qs[c], __half2float(kr[c])));
-    const float v = __fmul_rn(d, scale);
-    sc[p] = v;
-    mx = fmaxf(mx, v);
+      for (int ii = 0; ii < 8; ++ii) d = __fadd_rn(d, __shfl_sync(0xffffffffu, acc, (lane & ~7) + ii));
+      if (valid && i == 0) {
+        for (int c = n8 * 8; c < hd; ++c) d = __fadd_rn(d, __fmul_rn(qs[c], __half2float(kr[c])));
+        const float v = __fmul_rn(d, scale);
+        sc[p0 + pp] = v;
+        mx = fmaxf(mx, v);
+      }
+    }
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  if (lane == 0) red[tid >> 5] = mx;
   __syncthreads();
   mx = red[0];
   for (int i = 1; i < ATT_THREADS / 32; ++i) mx = fmaxf(mx, red[i]);
-  for (int p = tid; p < n_pos; p += blockDim.x) sc[p] = exp_rn(__fsub_rn(sc[p], mx));
+  for (int p = tid; p < n_pos; p += ATT_THREADS) sc[p] = exp_rn(__fsub_rn(sc[p], mx));
   __syncthreads();
   if (tid == 0) {
     float sum = 0.0f;
@@ -224,22 +255,29 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __r
   }
   __syncthreads();
   const float inv = inv_s;
-  for (int j = tid; j < hd; j += blockDim.x) {
-    float o = 0.0f;
-    const __half* vr = vc + (int64_t)kvh * hd + j;
-    for (int p = 0; p < n_pos; ++p) o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[p], inv), __half2float(vr[(int64_t)p * kvw])));
-    out[((int64_t)s * nh + h) * hd + j] = o;
+  float o = 0.0f;
+  for (int p0 = 0; p0 < n_pos; p0 += ATT_PC) {
+    const int np = min(ATT_PC, n_pos - p0);
+    __syncthreads();
+    stage_rows(ks, vbase + (int64_t)p0 * kvw, np, hd, kvw, tid);
+    __syncthreads();
+    if (tid < hd)
+      for (int pp = 0; pp < np; ++pp)
+        o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[p0 + pp], inv), __half2float(ks[pp * hd + tid])));
   }
+  if (tid < hd) out[((int64_t)s * nh + h) * hd + tid] = o;
 }
+
+int attention_max_positions(int hd) { return 200 * 1024 / 4 - hd - ATT_PC * hd / 2; }
 
 void launch_attention(const float* q, const __half* kc, const __half* vc, int n, int nh, int nkv, int hd, int pos0,
                       float scale, float* out, cudaStream_t st) {
   if (n <= 0) return;
-  const size_t smem = (size_t)(hd + pos0 + n) * 4;
-  static int attr = 0;
-  if ((int)smem > 48 * 1024 && attr < (int)smem) {
-    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr = 227 * 1024;
+  const size_t smem = (size_t)(hd + ATT_PC * hd / 2 + pos0 + n) * 4;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
   }
   launch_k(attention_kernel, dim3(n, nh), ATT_THREADS, smem, st, q, kc, vc, nh, nkv, hd, pos0, scale, out);
 }

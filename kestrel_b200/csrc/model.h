@@ -38,7 +38,9 @@ struct QkPostArgs {
 void launch_qk_post(const QkPostArgs& a, cudaStream_t st);
 
 // Causal GQA attention of n queries at positions pos0.. over the f16 caches
-// (transformer.rs:594-631): out [n, nh * hd].
+// (transformer.rs:594-631): out [n, nh * hd]. hd % 8 == 0 and at most
+// attention_max_positions(hd) positions.
+int attention_max_positions(int hd);
 void launch_attention(const float* q, const __half* kc, const __half* vc, int n, int nh, int nkv, int hd, int pos0,
                       float scale, float* out, cudaStream_t st);
 

@@ -21,9 +21,19 @@ namespace kc {
 // through shared memory in K chunks of RL_KC floats with bulk copies
 // (double-buffered), so every thread's chain reads shared memory only; each
 // lane still visits its elements c = lane, lane+8, ... in increasing order.
+constexpr int RT_WARPS = 4;      // route_kernel: tokens (warps) per CTA
+constexpr int RT_MAXK = 64;      // largest top-k
+constexpr int DP_THREADS = 1024; // dispatch: one block
+
+__device__ void route_row(const float* __restrict__ row, int E, int k, int norm_topk, float weights_scale, float* p,
+                          float* selw, int* seli, int lane, int* __restrict__ ids_out, float* __restrict__ w_out);
+__device__ void dispatch_block(const int* __restrict__ ids, const float* __restrict__ w, int n_tok, int k, int E,
+                               const DispatchOut& o, uint32_t* dsm);
+
 constexpr int RL_E = 8, RL_T = 4, RL_KC = 1024;
 constexpr int RL_ROW = RL_KC + 8;  // padded shared row: the 4 expert rows a warp reads hit distinct banks
 constexpr int RL_THREADS = RL_E * RL_T * 8;
+constexpr size_t rl_smem(int rt) { return 2 * (size_t)(RL_E + rt) * RL_ROW * sizeof(float); }
 
 // One 8-chunk step of output lane j's chain. GEMM: gemm_f32 lane chain (all
 // chunks into a0) or, for m1, dot_f32 (even chunks a0, odd chunks a1); else
@@ -38,17 +48,17 @@ __device__ __forceinline__ void rl_step(float wv, float xv, bool odd, bool m1, f
   }
 }
 
-template <bool GEMM>
-__global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* __restrict__ w, int64_t ws, int E,
-                                                                   int d, const float* __restrict__ h, int n_tok,
-                                                                   float* __restrict__ logits, int* status) {
+template <bool GEMM, int RT>
+__global__ void __launch_bounds__(RL_E * RT * 8) router_logits_kernel(const float* __restrict__ w, int64_t ws, int E,
+                                                                      int d, const float* __restrict__ h, int n_tok,
+                                                                      float* __restrict__ logits, int* status) {
   pdl_enter();
-  extern __shared__ __align__(128) float rsm[];  // [2][RL_E + RL_T][RL_ROW]
+  extern __shared__ __align__(128) float rsm[];  // [2][RL_E + RT][RL_ROW]
   __shared__ __align__(8) uint64_t full[2];
   const int tid = threadIdx.x, j = tid & 7, grp = tid >> 3;
   const int er = grp % RL_E, tr = grp / RL_E;
-  const int e0 = blockIdx.x * RL_E, s0 = blockIdx.y * RL_T;
-  const int ne = min(RL_E, E - e0), nt = min(RL_T, n_tok - s0);
+  const int e0 = blockIdx.x * RL_E, s0 = blockIdx.y * RT;
+  const int ne = min(RL_E, E - e0), nt = min(RT, n_tok - s0);
   const int erc = min(er, ne - 1), trc = min(tr, nt - 1);
   const int e = e0 + erc, s = s0 + trc;
   const bool valid = er < ne && tr < nt;
@@ -71,7 +81,7 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* 
   }
   __syncthreads();
   auto issue = [&](int c) {
-    float* buf = rsm + (c & 1) * (RL_E + RL_T) * RL_ROW;
+    float* buf = rsm + (c & 1) * (RL_E + RT) * RL_ROW;
     const int k0 = c * RL_KC, kn = min(RL_KC, d - k0);
     const uint32_t rb = (uint32_t)kn * 4;
     mbar_expect_tx(&full[c & 1], rb * (ne + nt));
@@ -86,7 +96,7 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* 
     }
     for (int c = 0; c < nchunk; ++c) {
       mbar_wait(&full[c & 1], (c >> 1) & 1, status, W_ROUTER);
-      const float* buf = rsm + (c & 1) * (RL_E + RL_T) * RL_ROW;
+      const float* buf = rsm + (c & 1) * (RL_E + RT) * RL_ROW;
       const float* wr = buf + erc * RL_ROW + j;
       const float* xr = buf + (RL_E + trc) * RL_ROW + j;
       const int k0 = c * RL_KC, kn = min(RL_KC, n8 - k0);  // k0 is an even number of 8-chunks
@@ -129,19 +139,21 @@ void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int 
                           float* logits, int* status, cudaStream_t st, bool force_dot) {
   if (n_tok <= 0) return;
   static bool attr = false;
-  const size_t smem = 2 * (RL_E + RL_T) * RL_ROW * sizeof(float);
+  const size_t smem = rl_smem(RL_T);
   if (!attr) {
-    cudaFuncSetAttribute(router_logits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(router_logits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(router_logits_kernel<true, RL_T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(router_logits_kernel<false, RL_T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr = true;
   }
   dim3 grid(ceil_div(E, RL_E), ceil_div(n_tok, RL_T));
   // quant::matmul's dispatch (quant.rs:241): the GEMM path needs >= 4 rows and
   // d % 8 == 0; otherwise quant::dot per output.
   if (!force_dot && n_tok >= 4 && d % 8 == 0)
-    launch_k(router_logits_kernel<true>, grid, RL_THREADS, smem, st, w, row_stride_floats, E, d, h, n_tok, logits, status);
+    launch_k(router_logits_kernel<true, RL_T>, grid, RL_THREADS, smem, st, w, row_stride_floats, E, d, h, n_tok,
+             logits, status);
   else
-    launch_k(router_logits_kernel<false>, grid, RL_THREADS, smem, st, w, row_stride_floats, E, d, h, n_tok, logits, status);
+    launch_k(router_logits_kernel<false, RL_T>, grid, RL_THREADS, smem, st, w, row_stride_floats, E, d, h,
+             n_tok, logits, status);
 }
 
 // ---------------------------------------------------------------------------
@@ -149,21 +161,11 @@ void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int 
 // sum, stable descending order (ties to the lower index), top-k, optional
 // renormalisation by the selection's sequential sum clamped at 2^-14, and
 // optional weights_scale. One warp per token; p lives in shared memory.
-constexpr int RT_WARPS = 4;
-constexpr int RT_MAXK = 64;
 
-__global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __restrict__ logits, int n_tok, int E,
-                                                               int k, int norm_topk, float weights_scale,
-                                                               int* __restrict__ ids, float* __restrict__ wout) {
-  pdl_enter();
-  extern __shared__ float sp[];  // [RT_WARPS][E] probabilities, then [RT_WARPS][RT_MAXK] selections
-  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int s = blockIdx.x * RT_WARPS + warp;
-  if (s >= n_tok) return;
-  float* p = sp + warp * E;
-  float* selw = sp + RT_WARPS * E + warp * RT_MAXK;
-  int* seli = reinterpret_cast<int*>(sp + RT_WARPS * (E + RT_MAXK)) + warp * RT_MAXK;
-  const float* row = logits + (int64_t)s * E;
+// One token's routing by one warp: p [E] and the selection scratch (selw,
+// seli: RT_MAXK each) in shared memory.
+__device__ void route_row(const float* __restrict__ row, int E, int k, int norm_topk, float weights_scale, float* p,
+                          float* selw, int* seli, int lane, int* __restrict__ ids_out, float* __restrict__ w_out) {
   float m = -INFINITY;
   for (int e = lane; e < E; e += 32) m = fmaxf(m, row[e]);
 #pragma unroll
@@ -229,9 +231,25 @@ __global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __res
   }
   __syncwarp();
   for (int r = lane; r < k; r += 32) {
-    ids[(int64_t)s * k + r] = seli[r];
-    wout[(int64_t)s * k + r] = selw[r];
+    ids_out[r] = seli[r];
+    w_out[r] = selw[r];
   }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __restrict__ logits, int n_tok, int E,
+                                                               int k, int norm_topk, float weights_scale,
+                                                               int* __restrict__ ids, float* __restrict__ wout) {
+  pdl_enter();
+  extern __shared__ float sp[];  // [RT_WARPS][E] probabilities, then [RT_WARPS][RT_MAXK] selections
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int s = blockIdx.x * RT_WARPS + warp;
+  if (s >= n_tok) return;
+  float* p = sp + warp * E;
+  float* selw = sp + RT_WARPS * E + warp * RT_MAXK;
+  int* seli = reinterpret_cast<int*>(sp + RT_WARPS * (E + RT_MAXK)) + warp * RT_MAXK;
+  route_row(logits + (int64_t)s * E, E, k, norm_topk, weights_scale, p, selw, seli, lane, ids + (int64_t)s * k,
+            wout + (int64_t)s * k);
 }
 
 void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
@@ -249,13 +267,11 @@ void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, f
 // One block of 1024 threads. Tokens are ranked inside each warp with a
 // per-expert bitmask of the warp's tokens (popc of the lower lanes), and
 // across warps and rounds with per-expert running bases.
-constexpr int DP_THREADS = 1024;
 
-__global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restrict__ ids,
-                                                               const float* __restrict__ w, int n_tok, int k, int E,
-                                                               DispatchOut o) {
-  pdl_enter();
-  extern __shared__ uint32_t dsm[];
+// The dispatch metadata by one 1024-thread block; dsm: (64 E + 3 E + 1) words
+// of shared memory.
+__device__ void dispatch_block(const int* __restrict__ ids, const float* __restrict__ w, int n_tok, int k, int E,
+                               const DispatchOut& o, uint32_t* dsm) {
   uint32_t* mask = dsm;                                // [32][E]
   int* pref = reinterpret_cast<int*>(dsm + 32 * E);    // [32][E]
   int* cnt = pref + 32 * E;                            // [E]
@@ -367,6 +383,14 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
       }
     __syncthreads();
   }
+}
+
+__global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restrict__ ids,
+                                                               const float* __restrict__ w, int n_tok, int k, int E,
+                                                               DispatchOut o) {
+  pdl_enter();
+  extern __shared__ uint32_t dsm[];
+  dispatch_block(ids, w, n_tok, k, E, o, dsm);
 }
 
 int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st) {

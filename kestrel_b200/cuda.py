@@ -62,6 +62,8 @@ SIGNATURES = {
     "kc_model_generate": (I, [P, P, I, I, P]),
     "kc_model_truncate": (I, [P, I]),
     "kc_model_cached": (I, [P]),
+    "kc_load_gguf": (I, [P, ctypes.c_char_p, I, ctypes.c_char_p, I64]),
+    "kc_gguf_inspect": (I, [ctypes.c_char_p, ctypes.c_char_p, I64]),
 }
 
 # Options (kc_set_option) and whole-model tensor kinds (kc_model_tensor).
@@ -318,10 +320,32 @@ class Context:
     def model_cached(self) -> int:
         return int(lib().kc_model_cached(self.h))
 
+    def load_gguf(self, path: str, n_ctx: int) -> dict:
+        """kc_load_gguf: declare and upload a GGUF / KGUF model; returns the
+        loader's summary (weight, KV-cache and free bytes)."""
+        import json
+        buf = ctypes.create_string_buffer(4096)
+        rc = lib().kc_load_gguf(self.h, os.fsencode(path), n_ctx, buf, len(buf))
+        info = json.loads(buf.value.decode()) if buf.value else {}
+        self._check(rc)
+        self._n_vocab = int(info.get("n_vocab", getattr(self, "_n_vocab", 0)))
+        return info
+
     def ep_reserve(self, max_tokens: int):
         """Collective: map the peer exchange arenas for up to max_tokens tokens
         per rank and call (after uploading the layers)."""
         self._check(lib().kc_ep_reserve(self.h, max_tokens))
+
+
+def gguf_inspect(path: str) -> dict:
+    """kc_gguf_inspect: parse a GGUF / KGUF file (no GPU needed)."""
+    import json
+    cap = 1 << 22
+    buf = ctypes.create_string_buffer(cap)
+    rc = lib().kc_gguf_inspect(os.fsencode(path), buf, cap)
+    if rc != 0:
+        raise KestrelCudaError(rc, (lib().kc_last_error(None) or b"").decode())
+    return json.loads(buf.value.decode())
 
 
 def ep_unique_id() -> bytes:

@@ -134,3 +134,35 @@ def test_model_errors(ctx, c0):
         ctx.model_forward([c0["cfg"]["n_vocab"]])  # token id out of range
     assert e.value.code == 1
     assert ctx.model_cached() == 0
+
+
+@pytest.mark.parametrize("prepared", [False, True], ids=["gguf", "kguf-strided"])
+def test_load_gguf_generates_same_tokens(ctx, c0, tmp_path, prepared):
+    """kc_load_gguf of the configs[0] model written as GGUF / strided KGUF
+    decodes the same tokens as the oracle."""
+    from kestrel_b200 import gguf
+    from kestrel_b200.cuda import OPT_F32_PREFILL
+    p = str(tmp_path / "c0.gguf")
+    gguf.write_model(p, c0, prepared=prepared)
+    prompt = prompt_of(c0["cfg"], 16, seed=3)
+    ref_toks, _ = oracle_model(oracle, c0, n_ctx=64).generate(prompt, 16)
+    ctx.set_option(OPT_F32_PREFILL, 1)
+    try:
+        info = ctx.load_gguf(p, 64)
+        assert info["arch"] == "qwen3moe" and info["n_expert"] == 8
+        toks = ctx.model_generate(prompt, 16)
+    finally:
+        ctx.set_option(OPT_F32_PREFILL, 0)
+    assert toks == ref_toks
+
+
+def test_load_gguf_refuses_what_does_not_fit(ctx, c0, tmp_path):
+    from kestrel_b200 import gguf
+    from kestrel_b200.cuda import KestrelCudaError
+    p = str(tmp_path / "c0.gguf")
+    gguf.write_model(p, c0)
+    before = ctx.device_bytes()
+    with pytest.raises(KestrelCudaError) as e:
+        ctx.load_gguf(p, 200_000_000)  # a KV cache of ~200 GB
+    assert e.value.code == 8 and "HBM" in str(e.value)
+    assert ctx.device_bytes() == before
