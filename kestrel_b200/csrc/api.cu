@@ -393,6 +393,15 @@ namespace kc {
 // without a context).
 void set_global_error(const char* msg) { g_init_err = msg ? msg : ""; }
 
+// KESTREL_GRAPHS=0 runs every decode step eagerly.
+bool model_graphs_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("KESTREL_GRAPHS");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 bool pdl_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("KESTREL_PDL");
@@ -1059,6 +1068,7 @@ struct Model {
   float *g = nullptr, *u = nullptr, *logits = nullptr;
   uint32_t* tok = nullptr;  // [T]
   uint32_t* next = nullptr; // argmax result
+  int* counters = nullptr;  // [0] generated-token index, [1] position (graph-replayed decode steps)
   int64_t bytes = 0;
 };
 
@@ -1082,7 +1092,8 @@ void model_free(kc_ctx* ctx) {
   cudaFree(m->vc);
   cudaFree(m->rope);
   for (void* p : {(void*)m->x, (void*)m->h, (void*)m->qkv, (void*)m->q, (void*)m->att, (void*)m->tmp,
-                  (void*)m->ffn, (void*)m->g, (void*)m->u, (void*)m->logits, (void*)m->tok, (void*)m->next})
+                  (void*)m->ffn, (void*)m->g, (void*)m->u, (void*)m->logits, (void*)m->tok, (void*)m->next,
+                  (void*)m->counters})
     cudaFree(p);
   delete m;
   ctx->model = nullptr;
@@ -1182,13 +1193,16 @@ int model_finalize(kc_ctx* ctx, Model& m) {
   return KC_OK;
 }
 
-// One forward chunk of n tokens already in m.tok; logits of the last token
-// in m.logits and its argmax in m.next.
-int model_chunk(kc_ctx* ctx, Model& m, int n) {
+// One forward chunk of n tokens read from `tok` (device); logits of the last
+// token in m.logits and its argmax in m.next. With dev_pos the chunk's
+// position is m.counters[1] on the device (a graph-replayed decode step), and
+// the caller advances m.cached.
+int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos) {
   cudaStream_t st = ctx->stream;
   const int d = m.d, pos0 = m.cached;
+  const int* pos_dev = dev_pos ? m.counters + 1 : nullptr;
   const float scale = 1.0f / std::sqrt((float)m.hd);  // transformer.rs:598
-  launch_embed(m.embd, m.embd_t, m.embd_rb, m.tok, n, d, m.n_vocab, m.x, ctx->status, st);
+  launch_embed(m.embd, m.embd_t, m.embd_rb, tok, n, d, m.n_vocab, m.x, ctx->status, st);
   CKL();
   const float* resid = nullptr;  // the previous FFN output, added before the next norm
   for (int l = 0; l < m.n_layer; ++l) {
@@ -1216,9 +1230,10 @@ int model_chunk(kc_ctx* ctx, Model& m, int n) {
     const size_t cache_off = (size_t)l * m.n_ctx * m.nkv * m.hd;
     qa.kc = m.kc + cache_off;
     qa.vc = m.vc + cache_off;
+    qa.pos_dev = pos_dev;
     launch_qk_post(qa, st);
     CKL();
-    launch_attention(m.q, qa.kc, qa.vc, n, m.nh, m.nkv, m.hd, pos0, scale, m.att, st);
+    launch_attention(m.q, qa.kc, qa.vc, n, m.nh, m.nkv, m.hd, pos0, pos_dev, m.n_ctx, scale, m.att, st);
     CKL();
     RC(dense_forward(ctx, y.o, m.att, n, m.tmp));
     launch_add_rmsnorm(m.x, m.tmp, y.ffn_norm, n, d, m.eps, m.h, st);
@@ -1242,7 +1257,7 @@ int model_chunk(kc_ctx* ctx, Model& m, int n) {
   RC(dense_forward(ctx, m.output, m.h, 1, m.logits));
   launch_argmax(m.logits, m.n_vocab, m.next, st);
   CKL();
-  m.cached += n;
+  if (!dev_pos) m.cached += n;
   return KC_OK;
 }
 
@@ -1262,7 +1277,7 @@ int model_forward(kc_ctx* ctx, const uint32_t* tokens, bool tokens_on_dev, int n
     RC(model_buffers(ctx, m, nc));
     CK(cudaMemcpyAsync(m.tok, tokens + c, (size_t)nc * 4,
                        tokens_on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->stream));
-    RC(model_chunk(ctx, m, nc));
+    RC(model_chunk(ctx, m, nc, m.tok, false));
   }
   return KC_OK;
 }
@@ -1774,6 +1789,7 @@ int kc_model_init(kc_ctx* ctx, int n_layer, int d, int n_head, int n_head_kv, in
   CK(cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
   CK(cudaMalloc(&m->logits, (size_t)n_vocab * 4));
   CK(cudaMalloc(&m->next, 4));
+  CK(cudaMalloc(&m->counters, 2 * sizeof(int)));
   m->bytes = (int64_t)cache * 4 + (int64_t)tab.size() * 8;
   return KC_OK;
 }
@@ -1871,21 +1887,56 @@ int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, int n_g
     CK(cudaStreamSynchronize(ctx->stream));
     return check_status(ctx);
   }
-  // Each step feeds the previous argmax straight from device memory.
+  // Decode steps read their token (the previous argmax) and position from
+  // device memory and append their argmax to `hist`: no host round trip per
+  // token. The first step runs eagerly (it also sizes every buffer for one
+  // row); it is then captured once as a CUDA graph and replayed for the rest.
   uint32_t* hist = nullptr;
   CK(cudaMalloc(&hist, (size_t)n_gen * 4));
   int rc = KC_OK;
-  for (int i = 0; i < n_gen && rc == KC_OK; ++i) {
-    if (cudaMemcpyAsync(hist + i, m.next, 4, cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess) {
-      rc = fail(ctx, KC_ERR_CUDA, "kc_model_generate: copy failed");
-      break;
+  const int init[2] = {1, m.cached};
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  auto step = [&]() -> int {
+    RC(model_chunk(ctx, m, 1, m.next, true));
+    launch_advance(m.next, hist, m.counters, m.counters + 1, ctx->stream);
+    CKL();
+    return KC_OK;
+  };
+  if (cudaMemcpyAsync(hist, m.next, 4, cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess ||
+      cudaMemcpyAsync(m.counters, init, sizeof init, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
+    rc = fail(ctx, KC_ERR_CUDA, "kc_model_generate: copy failed");
+  const bool graphs = ctx->ep.world <= 1 && !ctx->prof.on && model_graphs_enabled();
+  for (int i = 1; i < n_gen && rc == KC_OK; ++i) {
+    if (exec) {
+      if (cudaGraphLaunch(exec, ctx->stream) != cudaSuccess) rc = fail(ctx, KC_ERR_CUDA, "cudaGraphLaunch failed");
+    } else if (i >= 2 && graphs) {
+      if (cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        rc = fail(ctx, KC_ERR_CUDA, "kc_model_generate: stream capture failed");
+        break;
+      }
+      const int src = step();
+      const cudaError_t ec = cudaStreamEndCapture(ctx->stream, &graph);
+      if (src != KC_OK) {
+        rc = src;
+        break;
+      }
+      if (ec != cudaSuccess || cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) {
+        rc = fail(ctx, KC_ERR_CUDA, "kc_model_generate: graph capture of a decode step failed");
+        break;
+      }
+      if (cudaGraphLaunch(exec, ctx->stream) != cudaSuccess) rc = fail(ctx, KC_ERR_CUDA, "cudaGraphLaunch failed");
+    } else {
+      rc = step();
     }
-    if (i + 1 < n_gen) rc = model_forward(ctx, hist + i, true, 1);
+    if (rc == KC_OK) ++m.cached;
   }
   if (rc == KC_OK && cudaMemcpyAsync(out_tokens, hist, (size_t)n_gen * 4, cudaMemcpyDeviceToHost, ctx->stream) !=
                          cudaSuccess)
     rc = fail(ctx, KC_ERR_CUDA, "kc_model_generate: copy failed");
   cudaStreamSynchronize(ctx->stream);
+  if (exec) cudaGraphExecDestroy(exec);
+  if (graph) cudaGraphDestroy(graph);
   cudaFree(hist);
   if (rc != KC_OK) return rc;
   return check_status(ctx);

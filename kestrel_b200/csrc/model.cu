@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(32) qk_post_kernel(QkPostArgs a) {
     for (int j = lane; j < hd; j += 32) v[j] = __fmul_rn(__fmul_rn(v[j], r), nw[j]);
     __syncwarp();
   }
-  const int pos = a.pos0 + s;
+  const int pos = (a.pos_dev ? *a.pos_dev : a.pos0) + s;
   if (kind < 2) {
     const int half = a.rd / 2;
     const float2* tab = a.rope + (int64_t)pos * half;
@@ -195,8 +195,8 @@ __device__ __forceinline__ void stage_rows(__half* dst, const __half* src, int n
 __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __restrict__ q,
                                                                 const __half* __restrict__ kc,
                                                                 const __half* __restrict__ vc, int nh, int nkv,
-                                                                int hd, int pos0, float scale,
-                                                                float* __restrict__ out) {
+                                                                int hd, int pos0, const int* __restrict__ pos_dev,
+                                                                float scale, float* __restrict__ out) {
   pdl_enter();
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                                        // [hd]
@@ -206,6 +206,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __r
   __shared__ float inv_s;
   const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
   const int kvh = h / (nh / nkv), kvw = nkv * hd;
+  if (pos_dev) pos0 = *pos_dev;
   const int n_pos = pos0 + s + 1;
   for (int j = tid; j < hd; j += ATT_THREADS) qs[j] = q[((int64_t)s * nh + h) * hd + j];
   const __half* kbase = kc + (int64_t)kvh * hd;
@@ -271,15 +272,17 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __r
 int attention_max_positions(int hd) { return 200 * 1024 / 4 - hd - ATT_PC * hd / 2; }
 
 void launch_attention(const float* q, const __half* kc, const __half* vc, int n, int nh, int nkv, int hd, int pos0,
-                      float scale, float* out, cudaStream_t st) {
+                      const int* pos_dev, int max_pos, float scale, float* out, cudaStream_t st) {
   if (n <= 0) return;
-  const size_t smem = (size_t)(hd + ATT_PC * hd / 2 + pos0 + n) * 4;
+  // With the position on the device (graph replays), shared memory is sized
+  // for max_pos positions.
+  const size_t smem = (size_t)(hd + ATT_PC * hd / 2 + (pos_dev ? max_pos : pos0 + n)) * 4;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr = true;
   }
-  launch_k(attention_kernel, dim3(n, nh), ATT_THREADS, smem, st, q, kc, vc, nh, nkv, hd, pos0, scale, out);
+  launch_k(attention_kernel, dim3(n, nh), ATT_THREADS, smem, st, q, kc, vc, nh, nkv, hd, pos0, pos_dev, scale, out);
 }
 
 // One CTA: strided scans keep the first maximum of each thread, then a
@@ -343,4 +346,19 @@ void launch_swiglu(float* g, const float* u, int64_t n, cudaStream_t st) {
   launch_k(swiglu_kernel, (int)std::min<int64_t>(ceil_div(n, 256), 4 * 148), 256, 0, st, g, u, n);
 }
 
+}  // namespace kc
+
+namespace kc {
+// End of a graph-replayed decode step: append the step's argmax to the
+// history and advance the step and position counters.
+__global__ void advance_kernel(const uint32_t* next, uint32_t* hist, int* step, int* pos) {
+  pdl_enter();
+  hist[*step] = *next;
+  *step += 1;
+  *pos += 1;
+}
+
+void launch_advance(const uint32_t* next, uint32_t* hist, int* step, int* pos, cudaStream_t st) {
+  launch_k(advance_kernel, 1, 1, 0, st, next, hist, step, pos);
+}
 }  // namespace kc

@@ -34,6 +34,7 @@ struct QkPostArgs {
   const float2* rope;
   float* q_out;
   __half *kc, *vc;
+  const int* pos_dev;  // non-null: the position of token 0 is *pos_dev (pos0 ignored)
 };
 void launch_qk_post(const QkPostArgs& a, cudaStream_t st);
 
@@ -41,8 +42,12 @@ void launch_qk_post(const QkPostArgs& a, cudaStream_t st);
 // (transformer.rs:594-631): out [n, nh * hd]. hd % 8 == 0 and at most
 // attention_max_positions(hd) positions.
 int attention_max_positions(int hd);
+// pos_dev non-null: positions start at *pos_dev (at most max_pos of them).
 void launch_attention(const float* q, const __half* kc, const __half* vc, int n, int nh, int nkv, int hd, int pos0,
-                      float scale, float* out, cudaStream_t st);
+                      const int* pos_dev, int max_pos, float scale, float* out, cudaStream_t st);
+
+// hist[*step] = *next; ++*step; ++*pos (one thread).
+void launch_advance(const uint32_t* next, uint32_t* hist, int* step, int* pos, cudaStream_t st);
 
 // sampler::argmax (sampler.rs:104-112) of l [n]: the first maximum.
 void launch_argmax(const float* l, int n, uint32_t* out, cudaStream_t st);

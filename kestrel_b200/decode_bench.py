@@ -91,6 +91,7 @@ def main():
     ap.add_argument("--gen", type=int, default=None)
     ap.add_argument("--n-ctx", type=int, default=None)
     ap.add_argument("--f32-prefill", action="store_true")
+    ap.add_argument("--no-warmup", action="store_true", help="skip the warm-up generation (profiling runs)")
     args = ap.parse_args()
     import torch
     from .cuda import OPT_F32_PREFILL, Context
@@ -108,11 +109,14 @@ def main():
     ctx.set_option(OPT_F32_PREFILL, 1 if args.f32_prefill else 0)
     prompt = [int(t) for t in np.random.default_rng(1).integers(0, cfg["n_vocab"], n_prompt)]
     # Warm-up (workspace sizing, first launches), then timed runs.
-    ctx.model_generate(prompt[:8], 4)
-    ctx.model_truncate(0)
+    if not args.no_warmup:
+        ctx.model_generate(prompt[:8], 4)
+        ctx.model_truncate(0)
     t0 = time.perf_counter()
-    ctx.model_forward(prompt)
+    logits, _ = ctx.model_forward(prompt)
     t_prefill = time.perf_counter() - t0
+    finite = bool(np.isfinite(logits).all())
+    absmax = float(np.abs(logits[np.isfinite(logits)]).max()) if finite or np.isfinite(logits).any() else None
     ctx.model_truncate(0)
     t0 = time.perf_counter()
     toks = ctx.model_generate(prompt, n_gen)
@@ -128,6 +132,7 @@ def main():
         "step_weight_bytes": step_bytes(cfg, k), "step_gbs": step_bytes(cfg, k) / (t_decode / steps) / 1e9,
         "timing": "wall clock around synchronous kc_model_forward / kc_model_generate calls",
         "f32_prefill": bool(args.f32_prefill), "tokens_head": toks[:8],
+        "prompt_logits_finite": finite, "prompt_logits_absmax": absmax,
     }
     print(json.dumps(line))
     ctx.close()

@@ -166,3 +166,34 @@ def test_load_gguf_refuses_what_does_not_fit(ctx, c0, tmp_path):
         ctx.load_gguf(p, 200_000_000)  # a KV cache of ~200 GB
     assert e.value.code == 8 and "HBM" in str(e.value)
     assert ctx.device_bytes() == before
+
+
+@pytest.mark.parametrize("f32_prefill", [1, 0], ids=["f32-prefill", "tcgen05-prefill"])
+def test_qwen3_30b_shape_family(ctx, f32_prefill):
+    """configs[3]'s layer family at reduced size: head_dim 128 with 4:1 GQA,
+    Q4_K attention and embedding, Q6_K head, RoPE theta 1e6, routed Q4_K/Q6_K
+    experts."""
+    from kestrel_b200.cuda import OPT_F32_PREFILL
+    cfg = dict(synth.CONFIG0, n_layer=2, d=1024, n_head=8, n_kv=2, head_dim=128, rope_dim=128, rope_base=1e6,
+               n_vocab=2048, n_expert=16, k=4, ff=512, t_attn=G.Q4_K, t_embd=G.Q4_K, t_out=G.Q6_K, t_gate=G.Q4_K,
+               t_down=G.Q6_K)
+    model = synth.make_model(cfg, seed=13)
+    prompt = prompt_of(cfg, 40, seed=14)
+    om = oracle_model(oracle, model, n_ctx=64)
+    ref_logits = om.forward(prompt)
+    om.truncate(0)
+    ref_toks, _ = om.generate(prompt, 8)
+    ctx.set_option(OPT_F32_PREFILL, f32_prefill)
+    try:
+        synth.load_cuda(ctx, model, n_ctx=64)
+        logits, _ = ctx.model_forward(prompt)
+        assert np.isfinite(logits).all()
+        scale = max(float(np.abs(ref_logits).max()), 1.0)
+        err = float(np.abs(logits - ref_logits).max())
+        assert err <= (1e-5 if f32_prefill else 1e-2) * scale, err
+        ctx.model_truncate(0)
+        toks = ctx.model_generate(prompt, 8)
+    finally:
+        ctx.set_option(OPT_F32_PREFILL, 0)
+    if f32_prefill:
+        assert toks == ref_toks
