@@ -262,7 +262,9 @@ enum {
 /* Model tensors (layer = -1). */
 enum { KC_T_TOKEN_EMBD = 0, KC_T_OUTPUT_NORM = 1, KC_T_OUTPUT = 2 };
 
-/* Declare the model (replaces a previous one and its KV cache). */
+/* Declare the model. Replaces a previous model, its KV cache and the routed
+   layers uploaded under indices 0 .. n_layer-1: upload the new model's
+   experts and routers after this call. */
 KC_API int kc_model_init(kc_ctx* ctx, int n_layer, int d, int n_head, int n_head_kv, int head_dim, int n_vocab,
                          int n_ctx, int rope_dim, float rope_base, float rms_eps, int arch);
 KC_API int kc_model_tensor(kc_ctx* ctx, int layer, int kind, int t, const void* w, int64_t rows, int64_t cols,

@@ -149,6 +149,9 @@ struct kc_ctx {
   // and the fork / join events (created on first use).
   cudaStream_t aux = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  // Stream on which decode steps are captured as a graph (the context stream
+  // may be the legacy default stream, which cannot be captured).
+  cudaStream_t cap = nullptr;
   cudaStream_t stream = nullptr;
   bool own_stream = false;
   int* status = nullptr;  // device word written by kernels on timeout
@@ -372,6 +375,14 @@ int upload_matrix(kc_ctx* ctx, int t, const void* src, int64_t n_mats, int64_t r
   return KC_OK;
 }
 
+// Device-memory sources of an upload may still be written by work on another
+// stream (e.g. a framework's default stream): wait for the whole device before
+// reading them on the context stream.
+int wait_device_source(kc_ctx* ctx, bool on_dev) {
+  if (on_dev) CK(cudaDeviceSynchronize());
+  return KC_OK;
+}
+
 int ensure_aux(kc_ctx* ctx) {
   if (ctx->aux) return KC_OK;
   CK(cudaStreamCreateWithFlags(&ctx->aux, cudaStreamNonBlocking));
@@ -430,13 +441,15 @@ int num_sms() {
 // gate/up (+SwiGLU), down. Leaves y [slot, d] and the dispatch metadata
 // (slot of every selection in W.meta.tok_slot) in workspace W, which must be
 // sized for (n_rows, E, k, d, ff).
+// front_done: the dispatch metadata and the input rows' records are already
+// in W (route_dispatch_kernel).
 static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebase, const float* h, int n_rows,
-                           const int* ids, const float* wts, int k) {
+                           const int* ids, const float* wts, int k, bool front_done = false) {
   const int d = L.d, ff = L.ff;
   cudaStream_t st = ctx->stream;
   if (n_rows == 0) return KC_OK;
   // 2. dispatch metadata (permute).
-  {
+  if (!front_done) {
     StageScope ss(ctx, KC_STAGE_DISPATCH);
     RC(launch_dispatch(ids, wts, n_rows, k, E, W.meta, st));
     CKL();
@@ -481,7 +494,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   cudaStream_t lst = fork ? ctx->aux : st;  // stream of the n >= 4 launches
   // 3. activation records of every slot's input row (int8 path) and its f16
   //    copy (tensor-core path).
-  {
+  if (!front_done) {
     StageScope ss(ctx, KC_STAGE_QUANT_X);
     launch_act_records(kq_in, h, nullptr, W.meta.slot_tok, A, d, W.xrec, A, nullptr,
                        mma_gu && any_large ? W.x16 : nullptr, st, W.meta.offsets + E);
@@ -642,7 +655,11 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
 // -> int8 decode, n >= 4 -> tcgen05, else CUDA-core f32). Uses the workspace's
 // records, f16 copy and dispatch metadata, which must already hold n rows of
 // D.cols values (it is grown here only if it does not).
-static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, float* out) {
+// rec_ready (optional, K-quant D, n < 4): x's Q8_K records already made
+// ([cols / 256][n] records), e.g. by the RMSNorm that produced x.
+static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, float* out,
+                         const uint8_t* rec_ready = nullptr, int64_t out_stride = 0) {
+  if (out_stride <= 0) out_stride = D.rows;
   if (n == 0) return KC_OK;
   cudaStream_t st = ctx->stream;
   if (D.t == T_F32) {
@@ -670,11 +687,14 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
   a.slot_src = nullptr;
   a.af = x;
   a.out = out;
-  a.out_stride = D.rows;
+  a.out_stride = out_stride;
   if (n < 4) {
     const bool kq = is_k(D.t);
-    launch_act_records(kq, x, nullptr, nullptr, n, D.cols, W.xrec, n, nullptr, nullptr, st);
-    CKL();
+    const bool ready = rec_ready && kq;
+    if (!ready) {
+      launch_act_records(kq, x, nullptr, nullptr, n, D.cols, W.xrec, n, nullptr, nullptr, st);
+      CKL();
+    }
     DecodeArgs dv{};
     dv.w[0] = D.w;
     dv.n_mat = 1;
@@ -685,10 +705,10 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     dv.n_list = M.n_lists;
     dv.offsets = M.offsets;
     dv.n_experts = 1;
-    dv.rec = W.xrec;
+    dv.rec = ready ? rec_ready : W.xrec;
     dv.rec_slots = n;
     dv.out[0] = out;
-    dv.out_stride = D.rows;
+    dv.out_stride = out_stride;
     dv.status = ctx->status;
     RC(launch_decode(dv, ceil_div(D.rows, kTileRows), st));
   } else if (!ctx->f32_prefill && mma_supported(D.t, D.cols, 1)) {
@@ -709,7 +729,7 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     ma.offsets = M.offsets;
     ma.tt_prefix = M.large_tt;
     ma.out[0] = out;
-    ma.out_stride = D.rows;
+    ma.out_stride = out_stride;
     ma.status = ctx->status;
     RC(launch_mma_grouped(ma, tmap, ceil_div(n, kMmaTileN) * ceil_div(D.rows, 128), st));
   } else {
@@ -999,8 +1019,11 @@ static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const f
   return KC_OK;
 }
 
+// defer_combine (one GPU, no shared expert): the combine is left to the
+// caller (the model's next RMSNorm), which reads W.y, W.meta.tok_slot, W.ids
+// and W.w before anything else touches the workspace; out is not written.
 static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const float* h, int n_tok, float* out,
-                        int32_t* ids_out, float* w_out) {
+                        int32_t* ids_out, float* w_out, bool defer_combine = false) {
   if (ctx->ep.world > 1) return ep_pipeline(ctx, L, router, h, n_tok, out, ids_out, w_out);
   const int E = L.n_expert, k = L.k, d = L.d;
   RC(ensure_work(ctx, n_tok, E, k, layer_work_d(L), layer_work_f(L)));
@@ -1013,15 +1036,20 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
     launch_router_logits(router, d, E, d, h, n_tok, W.logits, ctx->status, st);
     CKL();
   }
-  {
+  // Decode batches: route, dispatch and the input records in one launch.
+  const bool front = !ctx->prof.on && is_k(L.t_gate) && route_dispatch_supported(n_tok, E, k, d);
+  if (front) {
+    launch_route_dispatch(W.logits, n_tok, E, k, L.norm_topk, L.weights_scale, W.ids, W.w, W.meta, h, d, W.xrec, st);
+    CKL();
+  } else {
     StageScope ss(ctx, KC_STAGE_ROUTE);
     launch_route(W.logits, n_tok, E, k, L.norm_topk, L.weights_scale, W.ids, W.w, st);
     CKL();
   }
   // 2-6. dispatch, records, gate/up, SwiGLU, down.
-  RC(experts_forward(ctx, W, L, E, L.first_expert, h, n_tok, W.ids, W.w, k));
+  RC(experts_forward(ctx, W, L, E, L.first_expert, h, n_tok, W.ids, W.w, k, front));
   // 7. combine (un-permute, ascending expert id).
-  {
+  if (!defer_combine || L.has_shared) {
     StageScope ss(ctx, KC_STAGE_COMBINE);
     launch_combine(W.y, W.meta.tok_slot, W.ids, W.w, n_tok, k, d, out, st);
     CKL();
@@ -1067,10 +1095,23 @@ struct Model {
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *tmp = nullptr, *ffn = nullptr;
   float *g = nullptr, *u = nullptr, *logits = nullptr;
   uint32_t* tok = nullptr;  // [T]
+  uint8_t* rec = nullptr;   // Q8_K records of the attention norm's output (decode steps)
   uint32_t* next = nullptr; // argmax result
   int* counters = nullptr;  // [0] generated-token index, [1] position (graph-replayed decode steps)
   int64_t bytes = 0;
 };
+
+void free_layer(Layer& L) {
+  cudaFree(L.gate);
+  cudaFree(L.up);
+  cudaFree(L.down);
+  cudaFree(L.router);
+  cudaFree(L.sh_gate.w);
+  cudaFree(L.sh_up.w);
+  cudaFree(L.sh_down.w);
+  cudaFree(L.sh_inp);
+  L = Layer{};
+}
 
 void free_dense(kc_ctx* ctx, Dense& D) {
   if (D.w) cudaFree(D.w);
@@ -1093,7 +1134,7 @@ void model_free(kc_ctx* ctx) {
   cudaFree(m->rope);
   for (void* p : {(void*)m->x, (void*)m->h, (void*)m->qkv, (void*)m->q, (void*)m->att, (void*)m->tmp,
                   (void*)m->ffn, (void*)m->g, (void*)m->u, (void*)m->logits, (void*)m->tok, (void*)m->next,
-                  (void*)m->counters})
+                  (void*)m->counters, (void*)m->rec})
     cudaFree(p);
   delete m;
   ctx->model = nullptr;
@@ -1127,7 +1168,7 @@ int model_buffers(kc_ctx* ctx, Model& m, int T) {
   T = std::max(T, m.T);
   CK(cudaStreamSynchronize(ctx->stream));
   for (void* p : {(void*)m.x, (void*)m.h, (void*)m.qkv, (void*)m.q, (void*)m.att, (void*)m.tmp, (void*)m.ffn,
-                  (void*)m.g, (void*)m.u, (void*)m.tok})
+                  (void*)m.g, (void*)m.u, (void*)m.tok, (void*)m.rec})
     cudaFree(p);
   const int width = (m.nh + 2 * m.nkv) * m.hd;
   CK(cudaMalloc(&m.x, (size_t)T * m.d * 4));
@@ -1140,6 +1181,7 @@ int model_buffers(kc_ctx* ctx, Model& m, int T) {
   CK(cudaMalloc(&m.g, (size_t)T * F * 4));
   CK(cudaMalloc(&m.u, (size_t)T * F * 4));
   CK(cudaMalloc(&m.tok, (size_t)T * 4));
+  CK(cudaMalloc(&m.rec, (size_t)std::min(T, 3) * std::max(1, m.d / 256) * kRecK));
   m.T = T;
   m.F = F;
   return KC_OK;
@@ -1204,12 +1246,54 @@ int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos)
   const float scale = 1.0f / std::sqrt((float)m.hd);  // transformer.rs:598
   launch_embed(m.embd, m.embd_t, m.embd_rb, tok, n, d, m.n_vocab, m.x, ctx->status, st);
   CKL();
-  const float* resid = nullptr;  // the previous FFN output, added before the next norm
+  // The previous FFN's output is added to the residual by the next norm: a
+  // plain buffer, or (routed layers on one GPU without a shared expert) the
+  // MoE combine itself, read from the workspace (moe_pipeline's
+  // defer_combine).
+  const float* resid = nullptr;
+  bool pending_combine = false;
+  int pending_k = 0;
+  auto norm = [&](float* x, const float* w, int rows, int tok0, float* out, uint8_t* rec) {
+    NormArgs na{};
+    na.x = x;
+    na.w = w;
+    na.dim = d;
+    na.eps = m.eps;
+    na.out = out;
+    na.rec = rec;
+    na.rec_slots = rows;
+    na.tok0 = tok0;
+    if (pending_combine) {
+      const Work& W = ctx->ws;
+      na.cy = W.y;
+      na.tok_slot = W.meta.tok_slot;
+      na.ids = W.ids;
+      na.cw = W.w;
+      na.k = pending_k;
+    } else if (resid) {
+      na.y = resid + (int64_t)tok0 * d;
+    }
+    launch_add_rmsnorm(na, rows, st);
+  };
   for (int l = 0; l < m.n_layer; ++l) {
     Model::Lay& y = m.L[l];
-    launch_add_rmsnorm(m.x, resid, y.attn_norm, n, d, m.eps, m.h, st);
+    // Decode rows with a K-quant q/k/v take their Q8_K records from the norm.
+    uint8_t* rec = (n < 4 && is_k(y.qkv.t) && d % 256 == 0) ? m.rec : nullptr;
+    norm(m.x, y.attn_norm, n, 0, m.h, rec);
     CKL();
-    RC(dense_forward(ctx, y.qkv, m.h, n, m.qkv));
+    pending_combine = false;
+    resid = nullptr;
+    if (n >= 4 && ctx->f32_prefill && y.q.t != T_F32) {
+      // The reference multiplies q, k and v separately, each on its own
+      // 48-row tiles (quant.rs:243): in the exact f32 order the fused
+      // matrix would tile rows differently.
+      const int64_t width = (int64_t)(m.nh + 2 * m.nkv) * m.hd;
+      RC(dense_forward(ctx, y.q, m.h, n, m.qkv, nullptr, width));
+      RC(dense_forward(ctx, y.k, m.h, n, m.qkv + y.q.rows, nullptr, width));
+      RC(dense_forward(ctx, y.v, m.h, n, m.qkv + y.q.rows + y.k.rows, nullptr, width));
+    } else {
+      RC(dense_forward(ctx, y.qkv, m.h, n, m.qkv, rec));
+    }
     QkPostArgs qa{};
     qa.qkv = m.qkv;
     qa.n = n;
@@ -1236,11 +1320,18 @@ int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos)
     launch_attention(m.q, qa.kc, qa.vc, n, m.nh, m.nkv, m.hd, pos0, pos_dev, m.n_ctx, scale, m.att, st);
     CKL();
     RC(dense_forward(ctx, y.o, m.att, n, m.tmp));
-    launch_add_rmsnorm(m.x, m.tmp, y.ffn_norm, n, d, m.eps, m.h, st);
+    resid = m.tmp;
+    norm(m.x, y.ffn_norm, n, 0, m.h, nullptr);
     CKL();
+    resid = m.ffn;
     if (!y.gate.w) {  // routed experts (checked in model_finalize)
       const Layer& R = ctx->layers[l];
-      RC(moe_pipeline(ctx, R, R.router, m.h, n, m.ffn, nullptr, nullptr));
+      const bool defer = ctx->ep.world <= 1 && !R.has_shared;
+      RC(moe_pipeline(ctx, R, R.router, m.h, n, m.ffn, nullptr, nullptr, defer));
+      if (defer) {
+        pending_combine = true;
+        pending_k = R.k;
+      }
     } else {
       RC(dense_forward(ctx, y.gate, m.h, n, m.g));
       RC(dense_forward(ctx, y.up, m.h, n, m.u));
@@ -1248,11 +1339,10 @@ int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos)
       CKL();
       RC(dense_forward(ctx, y.down, m.g, n, m.ffn));
     }
-    resid = m.ffn;
   }
   // Final norm of the last row only (transformer.rs:459-466).
   const int64_t last = (int64_t)(n - 1) * d;
-  launch_add_rmsnorm(m.x + last, resid + last, m.out_norm, 1, d, m.eps, m.h, st);
+  norm(m.x + last, m.out_norm, 1, n - 1, m.h, nullptr);
   CKL();
   RC(dense_forward(ctx, m.output, m.h, 1, m.logits));
   launch_argmax(m.logits, m.n_vocab, m.next, st);
@@ -1317,16 +1407,7 @@ void kc_free(kc_ctx* ctx) {
   model_free(ctx);
   ep_free(ctx->ep);
   ep_free_bufs(ctx->epb);
-  for (auto& [id, L] : ctx->layers) {
-    cudaFree(L.gate);
-    cudaFree(L.up);
-    cudaFree(L.down);
-    cudaFree(L.router);
-    cudaFree(L.sh_gate.w);
-    cudaFree(L.sh_up.w);
-    cudaFree(L.sh_down.w);
-    cudaFree(L.sh_inp);
-  }
+  for (auto& [id, L] : ctx->layers) free_layer(L);
   for (auto& [id, D] : ctx->dense) cudaFree(D.w);
   for (auto& r : ctx->prof.recs) {
     cudaEventDestroy(r.a);
@@ -1336,6 +1417,7 @@ void kc_free(kc_ctx* ctx) {
   cudaFree(ctx->ws.arena);
   cudaFree(ctx->ws_ep.arena);
   cudaFree(ctx->status);
+  if (ctx->cap) cudaStreamDestroy(ctx->cap);
   if (ctx->aux) {
     cudaStreamSynchronize(ctx->aux);
     cudaStreamDestroy(ctx->aux);
@@ -1401,6 +1483,7 @@ int kc_upload_experts_range(kc_ctx* ctx, int layer, int n_expert, int first_expe
     return fail(ctx, KC_ERR_SHAPE, "kc_upload_experts: d=%d / ff=%d not a block multiple", d, ff);
   if (d % 256 || ff % 32) return fail(ctx, KC_ERR_SHAPE, "kc_upload_experts: d must be a multiple of 256");
   cudaSetDevice(ctx->device);
+  RC(wait_device_source(ctx, src_on_device != 0));
   Layer& L = ctx->layers[layer];
   cudaFree(L.gate);
   cudaFree(L.up);
@@ -1446,6 +1529,7 @@ int kc_upload_router(kc_ctx* ctx, int layer, const float* router_w, int n_expert
     return fail(ctx, KC_ERR_ARG, "kc_upload_router: bad arguments (E=%d d=%d k=%d; k <= 64, E <= 1024)",
                 n_expert, d, k);
   cudaSetDevice(ctx->device);
+  RC(wait_device_source(ctx, src_on_device != 0));
   Layer& L = ctx->layers[layer];
   if (L.has_experts && (L.n_expert != n_expert || L.d != d))
     return fail(ctx, KC_ERR_SHAPE, "kc_upload_router: shape [%d, %d] does not match the experts [%d, %d]",
@@ -1474,6 +1558,7 @@ int kc_upload_dense(kc_ctx* ctx, int tensor_id, int t, const void* w, int64_t ro
   if (!type_ok(t) && t != T_F32) return fail(ctx, KC_ERR_TYPE, "kc_upload_dense: type %d has no kernel", t);
   if (cols % block_elems(t)) return fail(ctx, KC_ERR_SHAPE, "kc_upload_dense: cols %lld", (long long)cols);
   cudaSetDevice(ctx->device);
+  RC(wait_device_source(ctx, src_on_device != 0));
   Dense& D = ctx->dense[tensor_id];
   cudaFree(D.w);
   D.t = t;
@@ -1502,6 +1587,7 @@ int kc_upload_shared_expert(kc_ctx* ctx, int layer, int ff_shared, int d, int t_
     return fail(ctx, KC_ERR_SHAPE, "kc_upload_shared_expert: d=%d / ff=%d do not fit the block sizes", d,
                 ff_shared);
   cudaSetDevice(ctx->device);
+  RC(wait_device_source(ctx, src_on_device != 0));
   Layer& L = ctx->layers[layer];
   if (L.has_experts && L.d != d) return fail(ctx, KC_ERR_SHAPE, "kc_upload_shared_expert: d differs from the layer's");
   const struct {
@@ -1763,7 +1849,18 @@ int kc_model_init(kc_ctx* ctx, int n_layer, int d, int n_head, int n_head_kv, in
       arch < KC_ARCH_LLAMA || arch > KC_ARCH_QWEN3)
     return fail(ctx, KC_ERR_ARG, "kc_model_init: bad hyper-parameters");
   cudaSetDevice(ctx->device);
+  CK(cudaStreamSynchronize(ctx->stream));
   model_free(ctx);
+  // The new model's routed layers are uploaded after this call under indices
+  // 0 .. n_layer-1: drop what an earlier model left there.
+  for (auto it = ctx->layers.begin(); it != ctx->layers.end();) {
+    if (it->first >= 0 && it->first < n_layer) {
+      free_layer(it->second);
+      it = ctx->layers.erase(it);
+    } else {
+      ++it;
+    }
+  }
   Model* m = new Model();
   ctx->model = m;
   m->n_layer = n_layer; m->d = d; m->nh = n_head; m->nkv = n_head_kv; m->hd = head_dim; m->n_vocab = n_vocab;
@@ -1804,6 +1901,7 @@ int kc_model_tensor(kc_ctx* ctx, int layer, int kind, int t, const void* w, int6
   if (!type_ok(t) && t != T_F32) return fail(ctx, KC_ERR_TYPE, "kc_model_tensor: type %d has no kernel", t);
   if (cols % block_elems(t)) return fail(ctx, KC_ERR_SHAPE, "kc_model_tensor: cols %lld", (long long)cols);
   cudaSetDevice(ctx->device);
+  RC(wait_device_source(ctx, src_on_device != 0));
   const bool on_dev = src_on_device != 0;
   m->ready = false;
   if (layer < 0) {
@@ -1911,12 +2009,20 @@ int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, int n_g
     if (exec) {
       if (cudaGraphLaunch(exec, ctx->stream) != cudaSuccess) rc = fail(ctx, KC_ERR_CUDA, "cudaGraphLaunch failed");
     } else if (i >= 2 && graphs) {
-      if (cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+      // Capture on the context's own capture stream, replay on its stream.
+      if (!ctx->cap && cudaStreamCreateWithFlags(&ctx->cap, cudaStreamNonBlocking) != cudaSuccess) {
+        rc = fail(ctx, KC_ERR_CUDA, "kc_model_generate: capture stream creation failed");
+        break;
+      }
+      cudaStream_t run = ctx->stream;
+      if (cudaStreamBeginCapture(ctx->cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
         rc = fail(ctx, KC_ERR_CUDA, "kc_model_generate: stream capture failed");
         break;
       }
+      ctx->stream = ctx->cap;
       const int src = step();
-      const cudaError_t ec = cudaStreamEndCapture(ctx->stream, &graph);
+      ctx->stream = run;
+      const cudaError_t ec = cudaStreamEndCapture(ctx->cap, &graph);
       if (src != KC_OK) {
         rc = src;
         break;

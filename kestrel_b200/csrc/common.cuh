@@ -219,6 +219,35 @@ __device__ __forceinline__ int q8_round(float v) {
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+// One Q8_K activation record (Q8KRow::quantize, qdot.rs:347-367) of the 256
+// values a warp holds, 8 per lane (lane l: elements 8l .. 8l+7), stored at rb:
+// q[256] int8 | bsums int16[16] at 256 | pair sums int16[8] at 288 | d f32 at
+// 304 (then 12 zero bytes).
+__device__ __forceinline__ void q8k_store_record(const float (&v)[8], uint8_t* rb, int lane) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float scale = __fdiv_rn(amax, 127.0f);
+  const float inv = scale > 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+  int s = 0;
+  uint32_t packed[2] = {0, 0};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int qi = q8_round(__fmul_rn(v[i], inv));
+    s += qi;
+    packed[i / 4] |= (uint32_t)(qi & 0xFF) << (8 * (i % 4));
+  }
+  const int s16 = s + __shfl_xor_sync(0xffffffffu, s, 1);     // bsums[lane / 2]
+  const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);  // bsums pair lane / 4
+  *reinterpret_cast<uint2*>(rb + lane * 8) = make_uint2(packed[0], packed[1]);
+  if ((lane & 1) == 0) reinterpret_cast<int16_t*>(rb + 256)[lane / 2] = (int16_t)s16;
+  if ((lane & 3) == 0) reinterpret_cast<int16_t*>(rb + 288)[lane / 4] = (int16_t)s32;
+  if (lane == 0) reinterpret_cast<float*>(rb + 304)[0] = scale;
+  if (lane >= 1 && lane < 4) reinterpret_cast<uint32_t*>(rb + 304)[lane] = 0u;
+}
+
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
 // ---- programmatic dependent launch -----------------------------------------

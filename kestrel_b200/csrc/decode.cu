@@ -84,29 +84,7 @@ __global__ void q8k_records_kernel(const float* __restrict__ x, const float* __r
     *reinterpret_cast<uint4*>(f16out + slot * cols + b * 256 + lane * 8) = *reinterpret_cast<uint4*>(h);
   }
   if (!rec) return;
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const float scale = __fdiv_rn(amax, 127.0f);
-  const float inv = scale > 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
-  int s = 0;
-  uint32_t packed[2] = {0, 0};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    int qi = q8_round(__fmul_rn(v[i], inv));
-    s += qi;
-    packed[i / 4] |= (uint32_t)(qi & 0xFF) << (8 * (i % 4));
-  }
-  const int s16 = s + __shfl_xor_sync(0xffffffffu, s, 1);     // bsums[lane / 2]
-  const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);  // bsums pair lane / 4
-  uint8_t* rb = rec + (b * rec_slots + slot) * kRecK;
-  *reinterpret_cast<uint2*>(rb + lane * 8) = make_uint2(packed[0], packed[1]);
-  if ((lane & 1) == 0) reinterpret_cast<int16_t*>(rb + 256)[lane / 2] = (int16_t)s16;
-  if ((lane & 3) == 0) reinterpret_cast<int16_t*>(rb + 288)[lane / 4] = (int16_t)s32;
-  if (lane == 0) reinterpret_cast<float*>(rb + 304)[0] = scale;
-  if (lane >= 1 && lane < 4) reinterpret_cast<uint32_t*>(rb + 304)[lane] = 0u;
+  q8k_store_record(v, rec + (b * rec_slots + slot) * kRecK, lane);
 }
 
 // Q8Row::quantize (qdot.rs:29-49); optional SwiGLU first. One warp per

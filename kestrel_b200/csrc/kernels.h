@@ -65,6 +65,11 @@ struct DispatchOut {
   int* large_tt;   // [E+1]: prefix over large_list of ceil(rows / kMmaTileN) token tiles
 };
 int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st);
+// Decode batches (n_tok < 4): route + dispatch + the Q8_K records of each
+// slot's input row (x [n_tok, d], records [d / 256][n_tok * k]) in one launch.
+bool route_dispatch_supported(int n_tok, int E, int k, int d);
+void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
+                           float* w, const DispatchOut& o, const float* x, int d, uint8_t* rec, cudaStream_t st);
 // Metadata of a dense product: one group of n rows, slots = rows 0..n-1.
 void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st);
 void launch_combine(const float* y, const int* tok_slot, const int* ids, const float* w, int n_tok, int k, int d,

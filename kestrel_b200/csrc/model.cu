@@ -12,6 +12,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "decode.h"
 #include "model.h"
 
 namespace kc {
@@ -78,42 +79,122 @@ void launch_embed(const uint8_t* E, int t, int64_t row_bytes, const uint32_t* to
   launch_k(embed_kernel, n, 256, 0, st, E, t, row_bytes, tok, d, n_vocab, x, status);
 }
 
-// One CTA per row. The squares are formed in parallel; thread 0 folds them in
-// order from -0.0 (Rust's f32 Sum), as transformer.rs:333 does.
+// 1 / sqrt(sum / dim + eps) of the squares sq[0..dim) (16-byte aligned) folded
+// in order from -0.0 (Rust's f32 Sum, transformer.rs:333) by one warp: per
+// pass of 1024 squares, lane l holds squares 32 l .. 32 l + 31 in registers,
+// and the running sum visits the lanes in order (shuffled from lane to lane),
+// so the chain of dependent adds never waits on a shared-memory load.
+__device__ float rms_inv_warp(const float* sq, int dim, float eps, int lane) {
+  float ss = -0.0f;
+  for (int base = 0; base < dim; base += 1024) {
+    const int n = min(1024, dim - base);
+    float v[32];
+    const int l0 = lane * 32;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      if (l0 + i + 3 < n) {
+        const float4 q = *reinterpret_cast<const float4*>(sq + base + l0 + i);
+        v[i] = q.x; v[i + 1] = q.y; v[i + 2] = q.z; v[i + 3] = q.w;
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[i + u] = l0 + i + u < n ? sq[base + l0 + i + u] : 0.f;
+      }
+    }
+    const int lanes = (n + 31) / 32;
+    for (int l = 0; l < lanes; ++l) {
+      if (lane == l) {
+        const int cnt = min(32, n - l0);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < cnt) ss = __fadd_rn(ss, v[i]);
+      }
+      ss = __shfl_sync(0xffffffffu, ss, l);
+    }
+  }
+  ss = __fdiv_rn(ss, (float)dim);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, eps)));
+}
+
+// One CTA per row: x += (y or the MoE combine of the row's token), then
+// out = rmsnorm(x, w), and optionally the Q8_K records of out. The squares
+// are formed in parallel; warp 0 folds them (rms_inv_warp). The combine is
+// combine_kernel's arithmetic: the token's k selections ordered by expert id,
+// c = 0; c += w * y in that order (transformer.rs:566-570), then x + c.
 constexpr int NORM_THREADS = 256;
-__global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ y,
-                                                                   const float* __restrict__ w, int dim, float eps,
-                                                                   float* __restrict__ out) {
+__global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(NormArgs a) {
   pdl_enter();
-  extern __shared__ float sq[];
+  extern __shared__ __align__(16) float sq[];
   __shared__ float r_s;
-  float* xr = x + (int64_t)blockIdx.x * dim;
-  float* orow = out + (int64_t)blockIdx.x * dim;
-  for (int j = threadIdx.x; j < dim; j += blockDim.x) {
+  __shared__ int c_slot[64];
+  __shared__ float c_w[64];
+  const int dim = a.dim, tid = threadIdx.x;
+  float* xr = a.x + (int64_t)blockIdx.x * dim;
+  if (a.cy) {
+    const int t = a.tok0 + blockIdx.x;
+    if (tid < a.k) {
+      const int e = a.ids[(int64_t)t * a.k + tid];
+      int rank = 0;
+      for (int i = 0; i < a.k; ++i) {
+        const int ei = a.ids[(int64_t)t * a.k + i];
+        rank += (ei < e || (ei == e && i < tid)) ? 1 : 0;
+      }
+      c_slot[rank] = a.tok_slot[(int64_t)t * a.k + tid];
+      c_w[rank] = a.cw[(int64_t)t * a.k + tid];
+    }
+    __syncthreads();
+  }
+  for (int j = tid; j < dim; j += blockDim.x) {
     float v = xr[j];
-    if (y) {
-      v = __fadd_rn(v, y[(int64_t)blockIdx.x * dim + j]);
+    if (a.y) {
+      v = __fadd_rn(v, a.y[(int64_t)blockIdx.x * dim + j]);
+      xr[j] = v;
+    } else if (a.cy) {
+      float c = 0.f;
+      for (int i = 0; i < a.k; ++i) c = __fadd_rn(c, __fmul_rn(c_w[i], a.cy[(int64_t)c_slot[i] * dim + j]));
+      v = __fadd_rn(v, c);
       xr[j] = v;
     }
     sq[j] = __fmul_rn(v, v);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float ss = -0.0f;
-#pragma unroll 8
-    for (int j = 0; j < dim; ++j) ss = __fadd_rn(ss, sq[j]);
-    ss = __fdiv_rn(ss, (float)dim);
-    r_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, eps)));
+  if (tid < 32) {
+    const float r = rms_inv_warp(sq, dim, a.eps, tid);
+    if (tid == 0) r_s = r;
   }
   __syncthreads();
   const float r = r_s;
-  for (int j = threadIdx.x; j < dim; j += blockDim.x) orow[j] = __fmul_rn(__fmul_rn(xr[j], r), w[j]);
+  for (int j = tid; j < dim; j += blockDim.x) {
+    const float o = __fmul_rn(__fmul_rn(xr[j], r), a.w[j]);
+    if (a.out) a.out[(int64_t)blockIdx.x * dim + j] = o;
+    sq[j] = o;
+  }
+  if (!a.rec) return;
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int b = warp; b < dim / 256; b += NORM_THREADS / 32) {
+    float v[8];
+    const float4 p0 = reinterpret_cast<const float4*>(sq + b * 256 + lane * 8)[0];
+    const float4 p1 = reinterpret_cast<const float4*>(sq + b * 256 + lane * 8)[1];
+    v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w; v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+    q8k_store_record(v, a.rec + ((int64_t)b * a.rec_slots + blockIdx.x) * kRecK, lane);
+  }
+}
+
+void launch_add_rmsnorm(const NormArgs& a, int rows, cudaStream_t st) {
+  if (rows <= 0) return;
+  launch_k(add_rmsnorm_kernel, rows, NORM_THREADS, (size_t)a.dim * 4, st, a);
 }
 
 void launch_add_rmsnorm(float* x, const float* y, const float* w, int rows, int dim, float eps, float* out,
                         cudaStream_t st) {
-  if (rows <= 0) return;
-  launch_k(add_rmsnorm_kernel, rows, NORM_THREADS, (size_t)dim * 4, st, x, y, w, dim, eps, out);
+  NormArgs a{};
+  a.x = x;
+  a.y = y;
+  a.w = w;
+  a.dim = dim;
+  a.eps = eps;
+  a.out = out;
+  launch_add_rmsnorm(a, rows, st);
 }
 
 // One warp per (token, head); the head's hd values live in shared memory.
@@ -121,6 +202,7 @@ constexpr int QK_MAX_HD = 256;
 __global__ void __launch_bounds__(32) qk_post_kernel(QkPostArgs a) {
   pdl_enter();
   __shared__ float v[QK_MAX_HD];
+  __shared__ __align__(16) float sq[QK_MAX_HD];
   __shared__ float r_s;
   const int s = blockIdx.x, head = blockIdx.y, lane = threadIdx.x;
   const int hd = a.hd;
@@ -133,12 +215,10 @@ __global__ void __launch_bounds__(32) qk_post_kernel(QkPostArgs a) {
   __syncwarp();
   const float* nw = kind == 0 ? a.qn : (kind == 1 ? a.kn : nullptr);
   if (nw) {
-    if (lane == 0) {
-      float ss = -0.0f;
-      for (int j = 0; j < hd; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
-      ss = __fdiv_rn(ss, (float)hd);
-      r_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, a.eps)));
-    }
+    for (int j = lane; j < hd; j += 32) sq[j] = __fmul_rn(v[j], v[j]);
+    __syncwarp();
+    const float rr = rms_inv_warp(sq, hd, a.eps, lane);
+    if (lane == 0) r_s = rr;
     __syncwarp();
     const float r = r_s;
     for (int j = lane; j < hd; j += 32) v[j] = __fmul_rn(__fmul_rn(v[j], r), nw[j]);

@@ -19,6 +19,27 @@ void launch_embed(const uint8_t* E, int t, int64_t row_bytes, const uint32_t* to
 // updated in place), then out = rmsnorm(x, w) (transformer.rs:330-340).
 void launch_add_rmsnorm(float* x, const float* y, const float* w, int rows, int dim, float eps, float* out,
                         cudaStream_t st);
+// The general form: the addend is y or the MoE combine of the row's token
+// (cy = the expert products per slot, with the dispatch's tok_slot and the
+// routing ids / weights; row i is token tok0 + i), and the Q8_K records of
+// out can be written for a following int8 product (rec: [dim / 256][rec_slots]
+// records, row i in slot i).
+struct NormArgs {
+  float* x;
+  const float* y;
+  const float* cy;
+  const int* tok_slot;
+  const int* ids;
+  const float* cw;
+  int k, tok0;
+  const float* w;
+  int dim;
+  float eps;
+  float* out;
+  uint8_t* rec;
+  int64_t rec_slots;
+};
+void launch_add_rmsnorm(const NormArgs& a, int rows, cudaStream_t st);
 
 // Per token s and head: the q / k / v rows of qkv [n, (nh + 2 nkv) * hd]
 // get their bias (if any), q / k get rmsnorm over hd with qn / kn (if any)

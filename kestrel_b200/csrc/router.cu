@@ -1,6 +1,9 @@
 // Router logits, softmax/top-k routing, dispatch metadata (the permute) and
 // the weighted combine (the un-permute).
+#include <algorithm>
+
 #include "common.cuh"
+#include "decode.h"
 #include "kernels.h"
 
 namespace kc {
@@ -391,6 +394,58 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
   pdl_enter();
   extern __shared__ uint32_t dsm[];
   dispatch_block(ids, w, n_tok, k, E, o, dsm);
+}
+
+// Decode batches (n_tok < 4): routing (one warp per token), the dispatch
+// metadata and the Q8_K records of every slot's input row in one 1024-thread
+// block, three launches in one. Shared memory: the larger of the routing
+// scratch and dispatch_block's.
+__global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float* __restrict__ logits, int n_tok,
+                                                                     int E, int k, int norm_topk, float weights_scale,
+                                                                     int* __restrict__ ids, float* __restrict__ w,
+                                                                     DispatchOut o, const float* __restrict__ x,
+                                                                     int d, uint8_t* __restrict__ rec) {
+  pdl_enter();
+  extern __shared__ uint32_t dsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    float* p = reinterpret_cast<float*>(dsm) + warp * (E + 2 * RT_MAXK);
+    float* selw = p + E;
+    int* seli = reinterpret_cast<int*>(selw + RT_MAXK);
+    for (int t = warp; t < n_tok; t += DP_THREADS / 32)
+      route_row(logits + (int64_t)t * E, E, k, norm_topk, weights_scale, p, selw, seli, lane, ids + (int64_t)t * k,
+                w + (int64_t)t * k);
+  }
+  __syncthreads();
+  dispatch_block(ids, w, n_tok, k, E, o, dsm);
+  __syncthreads();
+  const int A = n_tok * k, nb = d / 256;
+  for (int task = warp; task < A * nb; task += DP_THREADS / 32) {
+    const int slot = task / nb, b = task - slot * nb;
+    const float* xp = x + (int64_t)o.slot_tok[slot] * d + b * 256 + lane * 8;
+    const float4 a0 = reinterpret_cast<const float4*>(xp)[0], a1 = reinterpret_cast<const float4*>(xp)[1];
+    const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    q8k_store_record(v, rec + ((int64_t)b * A + slot) * kRecK, lane);
+  }
+}
+
+bool route_dispatch_supported(int n_tok, int E, int k, int d) {
+  const size_t route_smem = (size_t)(DP_THREADS / 32) * (E + 2 * RT_MAXK) * 4;
+  const size_t disp_smem = (size_t)(64 * E + 3 * E + 1) * 4;
+  return n_tok >= 1 && n_tok < 4 && E >= 1 && E <= DP_THREADS && k >= 1 && k <= RT_MAXK && k <= E && d % 256 == 0 &&
+         std::max(route_smem, disp_smem) <= 200 * 1024;
+}
+
+void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
+                           float* w, const DispatchOut& o, const float* x, int d, uint8_t* rec, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(route_dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
+  const size_t smem = std::max((size_t)(DP_THREADS / 32) * (E + 2 * RT_MAXK) * 4, (size_t)(64 * E + 3 * E + 1) * 4);
+  launch_k(route_dispatch_kernel, 1, DP_THREADS, smem, st, logits, n_tok, E, k, norm_topk, weights_scale, ids, w, o,
+           x, d, rec);
 }
 
 int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st) {

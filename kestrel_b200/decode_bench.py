@@ -96,6 +96,8 @@ def main():
     import torch
     from .cuda import OPT_F32_PREFILL, Context
     ctx = Context(0)
+    # One stream for torch's weight generation and the library's kernels.
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
     if args.model == "c0":
         cfg = dict(synth.CONFIG0)
         n_prompt, n_gen = args.prompt or 64, args.gen or 64
