@@ -563,6 +563,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     dg.n_list = W.meta.n_lists;
     dg.offsets = W.meta.offsets;
     dg.n_experts = E;
+    dg.early = !front_done;  // the list comes from dispatch_kernel, before the records launch
     dg.rec = W.xrec;
     dg.rec_slots = A;
     dg.out[0] = W.g;
@@ -638,6 +639,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     dd.n_list = W.meta.n_lists;
     dd.offsets = W.meta.offsets;
     dd.n_experts = E;
+    dd.early = true;  // the list was built before the SwiGLU records launch
     dd.rec = W.arec;
     dd.rec_slots = A;
     dd.out[0] = W.y;
@@ -670,7 +672,8 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
   }
   RC(ensure_work(ctx, n, 1, 1, (int)std::min<int64_t>(D.cols, 1 << 30), 256));
   Work& W = ctx->ws;
-  if (W.dmeta_n != n) {
+  const bool meta_ready = W.dmeta_n == n;
+  if (!meta_ready) {
     launch_dense_meta(n, W.dmeta, st);
     CKL();
     W.dmeta_n = n;
@@ -705,6 +708,7 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     dv.n_list = M.n_lists;
     dv.offsets = M.offsets;
     dv.n_experts = 1;
+    dv.early = meta_ready;
     dv.rec = ready ? rec_ready : W.xrec;
     dv.rec_slots = n;
     dv.out[0] = out;
@@ -1843,7 +1847,7 @@ int kc_model_init(kc_ctx* ctx, int n_layer, int d, int n_head, int n_head_kv, in
                   int rope_dim, float rope_base, float rms_eps, int arch) {
   if (!ctx) return KC_ERR_ARG;
   ctx->err.clear();
-  if (n_layer < 1 || d < 1 || n_head < 1 || n_head_kv < 1 || n_head % n_head_kv || head_dim < 1 ||
+  if (n_layer < 1 || d < 1 || d % 4 || n_head < 1 || n_head_kv < 1 || n_head % n_head_kv || head_dim < 1 ||
       head_dim > 256 || head_dim % 8 || n_vocab < 1 || n_ctx < 1 || n_ctx > attention_max_positions(head_dim) ||
       rope_dim < 0 || rope_dim > head_dim || rope_dim % 2 ||
       arch < KC_ARCH_LLAMA || arch > KC_ARCH_QWEN3)

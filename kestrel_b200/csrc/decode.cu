@@ -479,19 +479,25 @@ __device__ __forceinline__ void run_unit_ns(int ns, const DecodeArgs& a, const D
 
 template <int T>
 __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, DecodeGeom g, int n_stages) {
-  pdl_enter();
+  // With a.early the expert list and offsets were written before the
+  // previous kernel ran (only the activation records come from it): the
+  // producer reads them (L2) and starts the first lap's weight copies before
+  // waiting for the previous kernel, whose tail then overlaps the weight
+  // stream's ramp. Otherwise everything waits first.
+  if (a.early) pdl_trigger();
+  else pdl_enter();
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[DMAX_STAGES], empty[DMAX_STAGES];
   __shared__ int list_s[DMAX_E], off_s[DMAX_E + 1];
   constexpr int R = TypeR<T>::R;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_list = min(*a.n_list, DMAX_E);
+  const int n_list = min(__ldcg(a.n_list), DMAX_E);
   const int tiles = (int)(padded_rows(a.rows) / DR);
   const int per_expert = a.n_mat * tiles;
   const int total = n_list * per_expert;
   if (total == 0) return;
-  for (int i = tid; i < n_list; i += blockDim.x) list_s[i] = a.list[i];
-  for (int i = tid; i <= a.n_experts && i <= DMAX_E; i += blockDim.x) off_s[i] = a.offsets[i];
+  for (int i = tid; i < n_list; i += blockDim.x) list_s[i] = __ldcg(a.list + i);
+  for (int i = tid; i <= a.n_experts && i <= DMAX_E; i += blockDim.x) off_s[i] = __ldcg(a.offsets + i);
   if (tid == 0) {
     for (int s = 0; s < n_stages; ++s) {
       mbar_init(&full[s], 1);
@@ -521,20 +527,48 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
     if (lane < DW) {
       const int w = lane;
       bool ok = true;
+      // Unit meta and byte ranges of group gi / segment seg for this lane.
+      auto unit_ptrs = [&](int gi, const uint8_t*& up, const uint8_t*& rp, int& rbytes) {
+        const UnitPos p = unit_at(gi * DW + w);
+        const UnitMeta um = meta_at(list_s, off_s, p.li);
+        up = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(um.e - a.expert_base) * a.expert_stride +
+             (int64_t)p.tile * g.tile_bytes;
+        rp = a.rec + (int64_t)um.slot0 * R;
+        rbytes = um.ns * R;
+      };
+      if (a.early) {
+        // First lap (stages 0 .. n_stages-1, no slot to wait for): weights
+        // now, the records after the wait below. The loop bound depends only
+        // on (gi, seg), so every lane reaches the same __syncwarp calls.
+        for (int gi = 0; gi < n_groups; ++gi) {
+          const int wg = min(DW, n_units - gi * DW);
+          if (gi * g.nseg * DW >= n_stages) break;
+          const bool active = w < wg;
+          const uint8_t *up = nullptr, *rp = nullptr;
+          int rbytes = 0;
+          if (active) unit_ptrs(gi, up, rp, rbytes);
+          int64_t off0 = 0;
+          for (int seg = 0; seg < g.nseg; ++seg) {
+            const int sb0 = seg * g.ks, sb1 = min(g.nsb, sb0 + g.ks);
+            const int64_t off1 = sb1 == g.nsb ? g.tile_bytes : tiled_sb_offset(g.type, a.cols, sb1);
+            const int sid = gi * g.nseg * DW + seg * wg + w;
+            if (active && sid < n_stages) {
+              const uint32_t wbytes = (uint32_t)(off1 - off0);
+              mbar_expect_tx(&full[sid], wbytes + (uint32_t)((sb1 - sb0) * rbytes));
+              bulk_g2s(ring + (int64_t)sid * g.stage_bytes, up + off0, wbytes, &full[sid]);
+            }
+            off0 = off1;
+            __syncwarp((1u << DW) - 1u);
+          }
+        }
+        pdl_wait();
+      }
       for (int gi = 0; gi < n_groups; ++gi) {
         const int wg = min(DW, n_units - gi * DW);
         const bool active = w < wg;
-        const uint8_t* up = nullptr;
-        const uint8_t* rp = nullptr;
+        const uint8_t *up = nullptr, *rp = nullptr;
         int rbytes = 0;
-        if (active) {
-          const UnitPos p = unit_at(gi * DW + w);
-          const UnitMeta um = meta_at(list_s, off_s, p.li);
-          up = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(um.e - a.expert_base) * a.expert_stride +
-               (int64_t)p.tile * g.tile_bytes;
-          rp = a.rec + (int64_t)um.slot0 * R;
-          rbytes = um.ns * R;
-        }
+        if (active) unit_ptrs(gi, up, rp, rbytes);
         int64_t off0 = 0;
         for (int seg = 0; seg < g.nseg; ++seg) {
           const int sb0 = seg * g.ks, sb1 = min(g.nsb, sb0 + g.ks);
@@ -543,13 +577,16 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
             const int sid = gi * g.nseg * DW + seg * wg + w;
             const int st = sid % n_stages;
             const uint32_t ph = (uint32_t)((sid / n_stages) & 1);
+            const bool weights_sent = a.early && sid < n_stages;
             if (sid >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status, W_DEC_EMPTY)) {
               ok = false;
             } else {
               const uint32_t wbytes = (uint32_t)(off1 - off0);
               uint8_t* dst = ring + (int64_t)st * g.stage_bytes;
-              mbar_expect_tx(&full[st], wbytes + (uint32_t)((sb1 - sb0) * rbytes));
-              bulk_g2s(dst, up + off0, wbytes, &full[st]);
+              if (!weights_sent) {
+                mbar_expect_tx(&full[st], wbytes + (uint32_t)((sb1 - sb0) * rbytes));
+                bulk_g2s(dst, up + off0, wbytes, &full[st]);
+              }
               for (int sb = sb0; sb < sb1; ++sb)
                 bulk_g2s(dst + g.rec_off + (sb - sb0) * (DMAXS * R), rp + (int64_t)sb * a.rec_slots * R,
                          (uint32_t)rbytes, &full[st]);
@@ -564,6 +601,8 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
           __syncwarp((1u << DW) - 1u);
         }
       }
+    } else if (a.early) {
+      pdl_wait();
     }
     // Keep the CTA alive until every issued copy has landed (bounded): lane 0
     // waits for the last n_stages stages up to the highest one issued.

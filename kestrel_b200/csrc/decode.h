@@ -38,6 +38,9 @@ struct DecodeArgs {
   float* out[2];           // out[m][slot * out_stride + row]
   int64_t out_stride;
   int* status;
+  // The list, n_list and offsets were written before the previous kernel in
+  // the stream (only rec comes from it): weights stream before the wait.
+  bool early;
 };
 
 // Stage geometry of one weight type / row length (decode.cu).
