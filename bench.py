@@ -470,11 +470,13 @@ def run_ours(args):
             "sweep": sweep,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": B * d * 4,
                     "d2h_bytes_per_step": B * d * 4},
-            # this library's kernels per kc_moe_ffn_dev call: router logits, route, dispatch, 2 record
-            # kernels, int8 and tcgen05 gate/up, int8 and tcgen05 down (the tcgen05 pair only with
-            # B >= 4: an expert holds at most one row per token), combine (+ the expert-parallel
-            # plan, pack, local ids, return plan and return pack with N > 1; NCCL's own not counted)
-            "gpu_launches": args.steps * ((10 if B >= 4 else 8) if world == 1 else 15),
+            # this library's kernels per kc_moe_ffn_dev call on one GPU: router logits; route and
+            # dispatch (one launch for B <= 32, which for B < 4 also makes the input records);
+            # the input records (B >= 4); int8 and tcgen05 gate/up; the SwiGLU records; int8 and
+            # tcgen05 down (the tcgen05 pair only with B >= 4: an expert holds at most one row per
+            # token); combine. N > 1 adds the expert-parallel plan, pack, local ids, return plan
+            # and return pack (NCCL's own kernels not counted).
+            "gpu_launches": args.steps * (((6 if B < 4 else 9) + (1 if B > 32 else 0)) if world == 1 else 15),
             "clocks": clocks,
             "cpu_baseline": cpu,
         }

@@ -316,7 +316,10 @@ KC_API int kc_ep_init(kc_ctx* ctx, int rank, int world, const char uid[128]);
    uploading the layers and routers, on every rank). Calls within that
    capacity then exchange token rows and result rows with this library's own
    kernels through peer memory, with no host synchronisation; larger calls use
-   NCCL. */
+   NCCL. The path is chosen per call from the rank's own token count, so in
+   each call every rank must be on the same side of max_tokens (as when all
+   ranks serve batches of one size); otherwise the ranks on different paths
+   wait for each other until the bounded waits expire (KC_ERR_TIMEOUT). */
 KC_API int kc_ep_reserve(kc_ctx* ctx, int max_tokens);
 
 #ifdef __cplusplus

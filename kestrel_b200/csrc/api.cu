@@ -441,15 +441,16 @@ int num_sms() {
 // gate/up (+SwiGLU), down. Leaves y [slot, d] and the dispatch metadata
 // (slot of every selection in W.meta.tok_slot) in workspace W, which must be
 // sized for (n_rows, E, k, d, ff).
-// front_done: the dispatch metadata and the input rows' records are already
-// in W (route_dispatch_kernel).
+// dispatched / recorded: the dispatch metadata / the input rows' records are
+// already in W (route_dispatch_kernel).
 static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebase, const float* h, int n_rows,
-                           const int* ids, const float* wts, int k, bool front_done = false) {
+                           const int* ids, const float* wts, int k, bool dispatched = false,
+                           bool recorded = false) {
   const int d = L.d, ff = L.ff;
   cudaStream_t st = ctx->stream;
   if (n_rows == 0) return KC_OK;
   // 2. dispatch metadata (permute).
-  if (!front_done) {
+  if (!dispatched) {
     StageScope ss(ctx, KC_STAGE_DISPATCH);
     RC(launch_dispatch(ids, wts, n_rows, k, E, W.meta, st));
     CKL();
@@ -494,7 +495,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   cudaStream_t lst = fork ? ctx->aux : st;  // stream of the n >= 4 launches
   // 3. activation records of every slot's input row (int8 path) and its f16
   //    copy (tensor-core path).
-  if (!front_done) {
+  if (!recorded) {
     StageScope ss(ctx, KC_STAGE_QUANT_X);
     launch_act_records(kq_in, h, nullptr, W.meta.slot_tok, A, d, W.xrec, A, nullptr,
                        mma_gu && any_large ? W.x16 : nullptr, st, W.meta.offsets + E);
@@ -563,7 +564,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     dg.n_list = W.meta.n_lists;
     dg.offsets = W.meta.offsets;
     dg.n_experts = E;
-    dg.early = !front_done;  // the list comes from dispatch_kernel, before the records launch
+    dg.early = !(dispatched && recorded);  // the list is older than the launch just before
     dg.rec = W.xrec;
     dg.rec_slots = A;
     dg.out[0] = W.g;
@@ -1040,10 +1041,13 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
     launch_router_logits(router, d, E, d, h, n_tok, W.logits, ctx->status, st);
     CKL();
   }
-  // Decode batches: route, dispatch and the input records in one launch.
-  const bool front = !ctx->prof.on && is_k(L.t_gate) && route_dispatch_supported(n_tok, E, k, d);
+  // Small batches: route and dispatch in one launch, for decode batches with
+  // the input records too.
+  const bool with_rec = is_k(L.t_gate) && route_dispatch_supported(n_tok, E, k, d, true);
+  const bool front = !ctx->prof.on && (with_rec || route_dispatch_supported(n_tok, E, k, d, false));
   if (front) {
-    launch_route_dispatch(W.logits, n_tok, E, k, L.norm_topk, L.weights_scale, W.ids, W.w, W.meta, h, d, W.xrec, st);
+    launch_route_dispatch(W.logits, n_tok, E, k, L.norm_topk, L.weights_scale, W.ids, W.w, W.meta, h, d,
+                          with_rec ? W.xrec : nullptr, st);
     CKL();
   } else {
     StageScope ss(ctx, KC_STAGE_ROUTE);
@@ -1051,7 +1055,7 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
     CKL();
   }
   // 2-6. dispatch, records, gate/up, SwiGLU, down.
-  RC(experts_forward(ctx, W, L, E, L.first_expert, h, n_tok, W.ids, W.w, k, front));
+  RC(experts_forward(ctx, W, L, E, L.first_expert, h, n_tok, W.ids, W.w, k, front, front && with_rec));
   // 7. combine (un-permute, ascending expert id).
   if (!defer_combine || L.has_shared) {
     StageScope ss(ctx, KC_STAGE_COMBINE);

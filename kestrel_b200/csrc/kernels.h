@@ -65,9 +65,10 @@ struct DispatchOut {
   int* large_tt;   // [E+1]: prefix over large_list of ceil(rows / kMmaTileN) token tiles
 };
 int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st);
-// Decode batches (n_tok < 4): route + dispatch + the Q8_K records of each
-// slot's input row (x [n_tok, d], records [d / 256][n_tok * k]) in one launch.
-bool route_dispatch_supported(int n_tok, int E, int k, int d);
+// Small batches: route + dispatch in one launch (n_tok <= 32), and for decode
+// batches (n_tok < 4, rec non-null) also the Q8_K records of each slot's
+// input row (x [n_tok, d], records [d / 256][n_tok * k]).
+bool route_dispatch_supported(int n_tok, int E, int k, int d, bool with_records);
 void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
                            float* w, const DispatchOut& o, const float* x, int d, uint8_t* rec, cudaStream_t st);
 // Metadata of a dense product: one group of n rows, slots = rows 0..n-1.

@@ -143,18 +143,36 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(NormArgs a) {
     }
     __syncthreads();
   }
-  for (int j = tid; j < dim; j += blockDim.x) {
-    float v = xr[j];
+  // Four consecutive elements per thread and step (dim % 4 == 0): 16-byte
+  // loads, and the k expert rows of the combine loaded before they are added.
+  for (int j = 4 * tid; j < dim; j += 4 * blockDim.x) {
+    float4 v = *reinterpret_cast<const float4*>(xr + j);
     if (a.y) {
-      v = __fadd_rn(v, a.y[(int64_t)blockIdx.x * dim + j]);
-      xr[j] = v;
+      const float4 y = *reinterpret_cast<const float4*>(a.y + (int64_t)blockIdx.x * dim + j);
+      v = make_float4(__fadd_rn(v.x, y.x), __fadd_rn(v.y, y.y), __fadd_rn(v.z, y.z), __fadd_rn(v.w, y.w));
+      *reinterpret_cast<float4*>(xr + j) = v;
     } else if (a.cy) {
-      float c = 0.f;
-      for (int i = 0; i < a.k; ++i) c = __fadd_rn(c, __fmul_rn(c_w[i], a.cy[(int64_t)c_slot[i] * dim + j]));
-      v = __fadd_rn(v, c);
-      xr[j] = v;
+      float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i0 = 0; i0 < a.k; i0 += 8) {
+        float4 yv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (i0 + i < a.k) yv[i] = *reinterpret_cast<const float4*>(a.cy + (int64_t)c_slot[i0 + i] * dim + j);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (i0 + i < a.k) {
+            const float wv = c_w[i0 + i];
+            c.x = __fadd_rn(c.x, __fmul_rn(wv, yv[i].x));
+            c.y = __fadd_rn(c.y, __fmul_rn(wv, yv[i].y));
+            c.z = __fadd_rn(c.z, __fmul_rn(wv, yv[i].z));
+            c.w = __fadd_rn(c.w, __fmul_rn(wv, yv[i].w));
+          }
+      }
+      v = make_float4(__fadd_rn(v.x, c.x), __fadd_rn(v.y, c.y), __fadd_rn(v.z, c.z), __fadd_rn(v.w, c.w));
+      *reinterpret_cast<float4*>(xr + j) = v;
     }
-    sq[j] = __fmul_rn(v, v);
+    *reinterpret_cast<float4*>(sq + j) =
+        make_float4(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y), __fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w));
   }
   __syncthreads();
   if (tid < 32) {
@@ -163,10 +181,13 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(NormArgs a) {
   }
   __syncthreads();
   const float r = r_s;
-  for (int j = tid; j < dim; j += blockDim.x) {
-    const float o = __fmul_rn(__fmul_rn(xr[j], r), a.w[j]);
-    if (a.out) a.out[(int64_t)blockIdx.x * dim + j] = o;
-    sq[j] = o;
+  for (int j = 4 * tid; j < dim; j += 4 * blockDim.x) {
+    const float4 xv = *reinterpret_cast<const float4*>(xr + j);
+    const float4 wv = *reinterpret_cast<const float4*>(a.w + j);
+    const float4 o = make_float4(__fmul_rn(__fmul_rn(xv.x, r), wv.x), __fmul_rn(__fmul_rn(xv.y, r), wv.y),
+                                 __fmul_rn(__fmul_rn(xv.z, r), wv.z), __fmul_rn(__fmul_rn(xv.w, r), wv.w));
+    if (a.out) *reinterpret_cast<float4*>(a.out + (int64_t)blockIdx.x * dim + j) = o;
+    *reinterpret_cast<float4*>(sq + j) = o;
   }
   if (!a.rec) return;
   __syncthreads();

@@ -396,10 +396,10 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
   dispatch_block(ids, w, n_tok, k, E, o, dsm);
 }
 
-// Decode batches (n_tok < 4): routing (one warp per token), the dispatch
-// metadata and the Q8_K records of every slot's input row in one 1024-thread
-// block, three launches in one. Shared memory: the larger of the routing
-// scratch and dispatch_block's.
+// Small batches: routing (one warp per token), the dispatch metadata and,
+// for decode batches (n_tok < 4; rec non-null), the Q8_K records of every
+// slot's input row in one 1024-thread block. Shared memory: the larger of the
+// routing scratch and dispatch_block's.
 __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float* __restrict__ logits, int n_tok,
                                                                      int E, int k, int norm_topk, float weights_scale,
                                                                      int* __restrict__ ids, float* __restrict__ w,
@@ -418,6 +418,7 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
   }
   __syncthreads();
   dispatch_block(ids, w, n_tok, k, E, o, dsm);
+  if (!rec) return;
   __syncthreads();
   const int A = n_tok * k, nb = d / 256;
   for (int task = warp; task < A * nb; task += DP_THREADS / 32) {
@@ -429,10 +430,11 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
   }
 }
 
-bool route_dispatch_supported(int n_tok, int E, int k, int d) {
+bool route_dispatch_supported(int n_tok, int E, int k, int d, bool with_records) {
   const size_t route_smem = (size_t)(DP_THREADS / 32) * (E + 2 * RT_MAXK) * 4;
   const size_t disp_smem = (size_t)(64 * E + 3 * E + 1) * 4;
-  return n_tok >= 1 && n_tok < 4 && E >= 1 && E <= DP_THREADS && k >= 1 && k <= RT_MAXK && k <= E && d % 256 == 0 &&
+  const bool tok_ok = with_records ? (n_tok < 4 && d % 256 == 0) : n_tok <= DP_THREADS / 32;
+  return n_tok >= 1 && tok_ok && E >= 1 && E <= DP_THREADS && k >= 1 && k <= RT_MAXK && k <= E &&
          std::max(route_smem, disp_smem) <= 200 * 1024;
 }
 

@@ -45,29 +45,38 @@ def main():
                        sl(L["t_gate"], L["up"], ff, d), L["t_down"], sl(L["t_down"], L["down"], d, ff),
                        first_expert=blk.first, n_local=blk.count)
     ctx.upload_router(0, L["router"], k)
-    # Calls of up to 32 tokens per rank exchange through peer memory; the
-    # larger case below goes through NCCL.
+    # Calls of up to 32 tokens per rank exchange through peer memory, larger
+    # ones through NCCL. The path is chosen per call from the rank's own token
+    # count, so in every case all ranks are on the same side of 32.
     ctx.ep_reserve(32)
     ref = Context(rank)
     ref.upload_experts(0, E, d, ff, L["t_gate"], L["gate"], L["t_gate"], L["up"], L["t_down"], L["down"])
     ref.upload_router(0, L["router"], k)
 
     results = []
-    cases = [[1] * world, [3] + [0] * (world - 1), [16] * world, [64 - 8 * r for r in range(world)], [1] * world,
-             [32] * world, [4, 28] + [5] * (world - 2)]
+    cases = [[1] * world, [3] + [0] * (world - 1), [16] * world, [40 + 3 * r for r in range(world)], [1] * world,
+             [32] * world, [4, 28] + [5] * (world - 2), [32 - 3 * r for r in range(world)]]
     for ci, ns in enumerate(cases):
         rng = np.random.default_rng(100 + ci)
         h_all = rng.standard_normal((sum(ns), d)).astype(np.float32)
         lo = sum(ns[:rank])
         mine = h_all[lo:lo + ns[rank]]
         out, ids, w = ctx.moe_ffn(0, mine)
-        r_out, all_ids, r_w = ref.moe_ffn(0, h_all)
-        r_out, r_ids, r_w = r_out[lo:lo + ns[rank]], all_ids[lo:lo + ns[rank]], r_w[lo:lo + ns[rank]]
+        # Routing depends on the batch size (quant::matmul's n < 4 dispatch
+        # orders the router's sums differently), so ids / weights are compared
+        # bit for bit with one GPU routing this rank's own tokens...
+        _, own_ids, own_w = ref.moe_ffn(0, mine)
+        # ... and the layer output with one GPU running the union of all
+        # ranks' tokens, which is also bit-exact when the rank's batch and the
+        # union are on the same side of n < 4 and no expert gets 4 rows.
+        u_out, all_ids, u_w = ref.moe_ffn(0, h_all)
+        r_out, r_ids = u_out[lo:lo + ns[rank]], all_ids[lo:lo + ns[rank]]
         max_rows = int(np.bincount(all_ids.reshape(-1), minlength=E).max()) if all_ids.size else 0
-        res = dict(case=ci, ns=ns, rank=rank, ids=bool(np.array_equal(ids, r_ids)),
-                   w=bool(np.array_equal(bits(w), bits(r_w))), max_rows=max_rows)
-        if max_rows <= 3:
-            res["out_bit_exact"] = bool(np.array_equal(bits(out), bits(r_out)))
+        same_side = (ns[rank] < 4) == (sum(ns) < 4)
+        res = dict(case=ci, ns=ns, rank=rank, ids=bool(np.array_equal(ids, own_ids)),
+                   w=bool(np.array_equal(bits(w), bits(own_w))), max_rows=max_rows, same_side=same_side)
+        if same_side and max_rows <= 3:
+            res["out_bit_exact"] = bool(np.array_equal(ids, r_ids) and np.array_equal(bits(out), bits(r_out)))
             res["ok"] = res["ids"] and res["w"] and res["out_bit_exact"]
         else:
             ok, err, scale = tol_ok(out, r_out)
