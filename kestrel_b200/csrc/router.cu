@@ -30,6 +30,8 @@ constexpr int DP_THREADS = 1024; // dispatch: one block
 
 __device__ void dispatch_block(const int* __restrict__ ids, const float* __restrict__ w, int n_tok, int k, int E,
                                const DispatchOut& o, uint32_t* dsm);
+__device__ void dispatch_small(const int* __restrict__ ids, const float* __restrict__ w, int n_tok, int k, int E,
+                               const DispatchOut& o, uint32_t* dsm);
 
 constexpr int RL_E = 8, RL_T = 4, RL_KC = 1024;
 constexpr int RL_ROW = RL_KC + 8;  // padded shared row: the 4 expert rows a warp reads hit distinct banks
@@ -294,12 +296,96 @@ __device__ void dispatch_block(const int* __restrict__ ids, const float* __restr
   }
 }
 
+// dispatch_block's metadata for batches of at most DS_MAXA selections (used
+// for decode batches, where it is the faster of the two). An
+// expert's slot offset is the number of selections with a smaller id, and
+// its place in the int8 (1-3 rows) or tcgen05 (>= 4 rows) list is the number
+// of listed experts below it (bitmasks), so thread e needs no block scan;
+// a selection's slot adds the earlier tokens that chose the same expert.
+constexpr int DS_MAXA = 256;
+__device__ void dispatch_small(const int* __restrict__ ids, const float* __restrict__ w, int n_tok, int k, int E,
+                               const DispatchOut& o, uint32_t* dsm) {
+  int* ids_s = reinterpret_cast<int*>(dsm);        // [A]
+  const int nw = (E + 31) / 32;
+  uint32_t* small_m = dsm + DS_MAXA;               // [nw] experts with 1-3 rows
+  uint32_t* large_m = small_m + 32;                // [nw] experts with >= 4 rows
+  int* cnt_s = reinterpret_cast<int*>(large_m + 32);  // [E]
+  const int tid = threadIdx.x, A = n_tok * k;
+  for (int i = tid; i < nw; i += DP_THREADS) {
+    small_m[i] = 0u;
+    large_m[i] = 0u;
+  }
+  for (int i = tid; i < A; i += DP_THREADS) ids_s[i] = ids[i];
+  __syncthreads();
+  for (int e = tid; e < E; e += DP_THREADS) {
+    int c = 0;
+    for (int i = 0; i < A; ++i) c += ids_s[i] == e ? 1 : 0;
+    cnt_s[e] = c;
+    if (c >= 1 && c <= 3) atomicOr(&small_m[e >> 5], 1u << (e & 31));
+    if (c >= 4) atomicOr(&large_m[e >> 5], 1u << (e & 31));
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += DP_THREADS) {
+    const int c = cnt_s[e];
+    int less = 0;
+    for (int i = 0; i < A; ++i) less += (ids_s[i] >= 0 && ids_s[i] < e) ? 1 : 0;
+    o.counts[e] = c;
+    o.offsets[e] = less;
+    const uint32_t below = (1u << (e & 31)) - 1u;
+    if (c >= 1 && c <= 3) {
+      int pos = __popc(small_m[e >> 5] & below);
+      for (int q = 0; q < (e >> 5); ++q) pos += __popc(small_m[q]);
+      o.small_list[pos] = e;
+    } else if (c >= 4) {
+      int pos = __popc(large_m[e >> 5] & below), tt = 0;
+      for (int q = 0; q < (e >> 5); ++q) pos += __popc(large_m[q]);
+      for (int e2 = 0; e2 < e; ++e2)
+        if (cnt_s[e2] >= 4) tt += (cnt_s[e2] + kMmaTileN - 1) / kMmaTileN;
+      o.large_list[pos] = e;
+      o.large_tt[pos] = tt;
+    }
+  }
+  if (tid == 0) {
+    int n_valid = 0, n_small = 0, n_large = 0, tt = 0;
+    for (int i = 0; i < A; ++i) n_valid += (ids_s[i] >= 0 && ids_s[i] < E) ? 1 : 0;
+    for (int q = 0; q < nw; ++q) {
+      n_small += __popc(small_m[q]);
+      n_large += __popc(large_m[q]);
+    }
+    for (int q = 0; q < nw; ++q)
+      for (uint32_t m = large_m[q]; m; m &= m - 1u) {
+        const int e = 32 * q + __ffs(m) - 1;
+        tt += (cnt_s[e] + kMmaTileN - 1) / kMmaTileN;
+      }
+    o.offsets[E] = n_valid;
+    o.n_lists[0] = n_small;
+    o.n_lists[1] = n_large;
+    o.large_tt[n_large] = tt;
+  }
+  for (int i = tid; i < A; i += DP_THREADS) {
+    const int e = ids_s[i], s = i / k;
+    if (e < 0 || e >= E) {
+      o.tok_slot[i] = 0;
+      continue;
+    }
+    int slot = 0;
+    for (int i2 = 0; i2 < A; ++i2) {
+      const int e2 = ids_s[i2];
+      slot += ((e2 >= 0 && e2 < e) || (e2 == e && i2 / k < s)) ? 1 : 0;
+    }
+    o.slot_tok[slot] = s;
+    o.slot_w[slot] = w[i];
+    o.tok_slot[i] = slot;
+  }
+}
+
 __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restrict__ ids,
                                                                const float* __restrict__ w, int n_tok, int k, int E,
                                                                DispatchOut o) {
   pdl_enter();
   extern __shared__ uint32_t dsm[];
-  dispatch_block(ids, w, n_tok, k, E, o, dsm);
+  if (n_tok < 4 && n_tok * k <= DS_MAXA) dispatch_small(ids, w, n_tok, k, E, o, dsm);
+  else dispatch_block(ids, w, n_tok, k, E, o, dsm);
 }
 
 // Small batches: routing (one warp per token), the dispatch metadata and,
@@ -323,7 +409,10 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
                 w + (int64_t)t * k);
   }
   __syncthreads();
-  dispatch_block(ids, w, n_tok, k, E, o, dsm);
+  // Decode batches: the scan-free dispatch (for larger batches the block scan
+  // of dispatch_block is faster).
+  if (n_tok < 4 && n_tok * k <= DS_MAXA) dispatch_small(ids, w, n_tok, k, E, o, dsm);
+  else dispatch_block(ids, w, n_tok, k, E, o, dsm);
   if (!rec) return;
   __syncthreads();
   const int A = n_tok * k, nb = d / 256;
@@ -357,7 +446,7 @@ void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int nor
 }
 
 int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st) {
-  size_t smem = (size_t)(64 * E + 3 * E + 1) * 4;
+  size_t smem = std::max((size_t)(64 * E + 3 * E + 1), (size_t)(DS_MAXA + 64 + E)) * 4;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
