@@ -157,6 +157,7 @@ struct kc_ctx {
   cudaStream_t stream = nullptr;
   bool own_stream = false;
   int* status = nullptr;  // device word written by kernels on timeout
+  int* status_host = nullptr;  // pinned host copy of it (check_status)
   std::string err;
   std::map<int, Layer> layers;
   std::map<int, Dense> dense;
@@ -331,9 +332,12 @@ int ensure_work(kc_ctx* ctx, Work& w, int T, int E, int K, int D, int F) {
 }
 int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) { return ensure_work(ctx, ctx->ws, T, E, K, D, F); }
 
+// Waits for the context stream and reads the kernels' status word (one
+// stream-ordered copy into pinned memory, then one synchronisation).
 int check_status(kc_ctx* ctx) {
-  int st = 0;
-  CK(cudaMemcpy(&st, ctx->status, sizeof(int), cudaMemcpyDeviceToHost));
+  CK(cudaMemcpyAsync(ctx->status_host, ctx->status, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  const int st = *ctx->status_host;
   if (st != 0) {
     CK(cudaMemset(ctx->status, 0, sizeof(int)));
     static const char* sites[] = {"unknown", "decode producer (empty stage)", "decode consumer (full stage)",
@@ -1453,7 +1457,8 @@ int kc_init(int device, kc_ctx** out) {
   ctx->device = device;
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->status, sizeof(int)) != cudaSuccess ||
-      cudaMemset(ctx->status, 0, sizeof(int)) != cudaSuccess) {
+      cudaMemset(ctx->status, 0, sizeof(int)) != cudaSuccess ||
+      cudaHostAlloc(&ctx->status_host, sizeof(int), cudaHostAllocDefault) != cudaSuccess) {
     delete ctx;
     return fail(nullptr, KC_ERR_CUDA, "kc_init: stream/status allocation failed");
   }
@@ -1479,6 +1484,7 @@ void kc_free(kc_ctx* ctx) {
   cudaFree(ctx->ws.arena);
   cudaFree(ctx->ws_ep.arena);
   cudaFree(ctx->status);
+  if (ctx->status_host) cudaFreeHost(ctx->status_host);
   if (ctx->cap) cudaStreamDestroy(ctx->cap);
   if (ctx->aux) {
     cudaStreamSynchronize(ctx->aux);
@@ -1521,8 +1527,7 @@ int kc_reserve(kc_ctx* ctx, int max_tokens) {
 
 int kc_sync(kc_ctx* ctx) {
   if (!ctx) return KC_ERR_ARG;
-  CK(cudaStreamSynchronize(ctx->stream));
-  return check_status(ctx);
+  return check_status(ctx);  // synchronises the stream
 }
 
 int64_t kc_device_bytes(const kc_ctx* ctx) {
@@ -1741,8 +1746,7 @@ int kc_moe_ffn(kc_ctx* ctx, int layer, const float* h, int n_tok, const float* r
   if (topk_w && n_tok > 0)
     CK(cudaMemcpyAsync(topk_w, ep ? ctx->epb.w_home : W.w, (size_t)n_tok * L.k * 4, cudaMemcpyDeviceToHost,
                        ctx->stream));
-  CK(cudaStreamSynchronize(ctx->stream));
-  return check_status(ctx);
+  return check_status(ctx);  // synchronises the stream
 }
 
 int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out) {
@@ -1771,8 +1775,7 @@ int kc_matmul(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out) {
   CK(cudaMemcpyAsync(W.h_in, x, (size_t)n * D.cols * 4, cudaMemcpyHostToDevice, ctx->stream));
   RC(kc_matmul_dev(ctx, tensor_id, W.h_in, n, W.out));
   CK(cudaMemcpyAsync(out, W.out, (size_t)n * D.rows * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  CK(cudaStreamSynchronize(ctx->stream));
-  return check_status(ctx);
+  return check_status(ctx);  // synchronises the stream
 }
 
 int kc_q8k_quantize_dev(kc_ctx* ctx, const float* x, int64_t n_rows, int64_t cols, int8_t* q, float* d,
@@ -2029,8 +2032,7 @@ int kc_model_forward(kc_ctx* ctx, const uint32_t* tokens, int n, float* logits, 
   RC(model_forward(ctx, tokens, false, n));
   if (logits) CK(cudaMemcpyAsync(logits, m.logits, (size_t)m.n_vocab * 4, cudaMemcpyDeviceToHost, ctx->stream));
   if (next_token) CK(cudaMemcpyAsync(next_token, m.next, 4, cudaMemcpyDeviceToHost, ctx->stream));
-  CK(cudaStreamSynchronize(ctx->stream));
-  return check_status(ctx);
+  return check_status(ctx);  // synchronises the stream
 }
 
 int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, int n_gen, uint32_t* out_tokens) {
@@ -2045,8 +2047,7 @@ int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, int n_g
     return fail(ctx, KC_ERR_ARG, "kc_model_generate: context full (n_ctx = %d)", m.n_ctx);
   RC(model_forward(ctx, prompt, false, n_prompt));
   if (n_gen == 0) {
-    CK(cudaStreamSynchronize(ctx->stream));
-    return check_status(ctx);
+    return check_status(ctx);  // synchronises the stream
   }
   // Decode steps read their token (the previous argmax) and position from
   // device memory and append their argmax to `hist`: no host round trip per
