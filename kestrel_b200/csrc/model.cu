@@ -281,15 +281,43 @@ void launch_qk_post(const QkPostArgs& a, cudaStream_t st) {
 // by one thread in position order from +0.0; each output element then
 // accumulates (score * inv) * v over the positions in order.
 constexpr int ATT_THREADS = 256;
-constexpr int ATT_PC = 64;  // positions per staged chunk
+constexpr int ATT_PC = 128;  // positions per staged chunk (two buffers)
 
-__device__ __forceinline__ void stage_rows(__half* dst, const __half* src, int n_rows, int hd, int64_t row_stride,
-                                           int tid) {
-  // n_rows rows of hd halves (hd % 8 == 0: 16-byte pieces).
+// n_rows rows of hd halves (hd % 8 == 0: 16-byte pieces) into dst with
+// asynchronous copies, committed as one group.
+__device__ __forceinline__ void stage_rows_async(__half* dst, const __half* src, int n_rows, int hd,
+                                                 int64_t row_stride, int tid) {
   const int per_row = hd / 8;
   for (int i = tid; i < n_rows * per_row; i += ATT_THREADS) {
     const int r = i / per_row, c = i - r * per_row;
-    reinterpret_cast<uint4*>(dst + (int64_t)r * hd)[c] = reinterpret_cast<const uint4*>(src + r * row_stride)[c];
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst + (int64_t)r * hd + c * 8)),
+                 "l"(src + r * row_stride + c * 8)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// The chunk loop over positions 0 .. n_pos-1 of one cache (K or V) with two
+// staging buffers of ATT_PC rows: chunk c + 1 is requested before chunk c is
+// used, so the cache reads overlap the work on the previous chunk.
+// body(p0, np, rows) gets the rows [np][hd] of positions p0 ...
+template <class Body>
+__device__ __forceinline__ void for_cache_chunks(__half* buf, const __half* base, int n_pos, int hd, int64_t kvw,
+                                                 int tid, Body body) {
+  const int n_chunks = (n_pos + ATT_PC - 1) / ATT_PC;
+  __syncthreads();
+  stage_rows_async(buf, base, min(ATT_PC, n_pos), hd, kvw, tid);
+  for (int ci = 0; ci < n_chunks; ++ci) {
+    const int p0 = ci * ATT_PC, np = min(ATT_PC, n_pos - p0);
+    if (ci + 1 < n_chunks)
+      stage_rows_async(buf + ((ci + 1) & 1) * ATT_PC * hd, base + (int64_t)(p0 + ATT_PC) * kvw,
+                       min(ATT_PC, n_pos - p0 - ATT_PC), hd, kvw, tid);
+    else
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // chunk c has landed
+    __syncthreads();
+    body(p0, np, buf + (ci & 1) * ATT_PC * hd);
+    __syncthreads();
   }
 }
 
@@ -301,8 +329,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __r
   pdl_enter();
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                                        // [hd]
-  __half* ks = reinterpret_cast<__half*>(sm + hd);      // [ATT_PC][hd] (K, then V)
-  float* sc = sm + hd + ATT_PC * hd / 2;                 // [n_pos]
+  __half* ks = reinterpret_cast<__half*>(sm + hd);      // [2][ATT_PC][hd] (K, then V)
+  float* sc = sm + hd + ATT_PC * hd;                     // [n_pos]
   __shared__ float red[ATT_THREADS / 32];
   __shared__ float inv_s;
   const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
@@ -314,18 +342,14 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __r
   const __half* vbase = vc + (int64_t)kvh * hd;
   const int n8 = hd / 8;
   float mx = -INFINITY;
-  for (int p0 = 0; p0 < n_pos; p0 += ATT_PC) {
-    const int np = min(ATT_PC, n_pos - p0);
-    __syncthreads();
-    stage_rows(ks, kbase + (int64_t)p0 * kvw, np, hd, kvw, tid);
-    __syncthreads();
+  for_cache_chunks(ks, kbase, n_pos, hd, kvw, tid, [&](int p0, int np, const __half* kch) {
     // Whole warps take part in every iteration (the shuffles below): the
     // bound is rounded up to 32 and positions past np compute nothing.
     const int tot = (np * 8 + 31) & ~31;
     for (int t = tid; t < tot; t += ATT_THREADS) {
       const int pp = t >> 3, i = t & 7;
       const bool valid = pp < np;
-      const __half* kr = ks + (valid ? pp : 0) * hd;
+      const __half* kr = kch + (valid ? pp : 0) * hd;
       float acc = 0.f;
       if (valid)
         for (int m = 0; m < n8; ++m) acc = __fadd_rn(acc, __fmul_rn(qs[8 * m + i], __half2float(kr[8 * m + i])));
@@ -341,7 +365,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __r
         mx = fmaxf(mx, v);
       }
     }
-  }
+  });
 #pragma unroll
   for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) red[tid >> 5] = mx;
@@ -358,26 +382,22 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __r
   __syncthreads();
   const float inv = inv_s;
   float o = 0.0f;
-  for (int p0 = 0; p0 < n_pos; p0 += ATT_PC) {
-    const int np = min(ATT_PC, n_pos - p0);
-    __syncthreads();
-    stage_rows(ks, vbase + (int64_t)p0 * kvw, np, hd, kvw, tid);
-    __syncthreads();
+  for_cache_chunks(ks, vbase, n_pos, hd, kvw, tid, [&](int p0, int np, const __half* vch) {
     if (tid < hd)
       for (int pp = 0; pp < np; ++pp)
-        o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[p0 + pp], inv), __half2float(ks[pp * hd + tid])));
-  }
+        o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[p0 + pp], inv), __half2float(vch[pp * hd + tid])));
+  });
   if (tid < hd) out[((int64_t)s * nh + h) * hd + tid] = o;
 }
 
-int attention_max_positions(int hd) { return 200 * 1024 / 4 - hd - ATT_PC * hd / 2; }
+int attention_max_positions(int hd) { return 200 * 1024 / 4 - hd - ATT_PC * hd; }
 
 void launch_attention(const float* q, const __half* kc, const __half* vc, int n, int nh, int nkv, int hd, int pos0,
                       const int* pos_dev, int max_pos, float scale, float* out, cudaStream_t st) {
   if (n <= 0) return;
   // With the position on the device (graph replays), shared memory is sized
   // for max_pos positions.
-  const size_t smem = (size_t)(hd + ATT_PC * hd / 2 + (pos_dev ? max_pos : pos0 + n)) * 4;
+  const size_t smem = (size_t)(hd + ATT_PC * hd + (pos_dev ? max_pos : pos0 + n)) * 4;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);

@@ -102,6 +102,34 @@ def test_decode_steps_bit_exact(ctx, c0):
     assert worst <= 1e-5 * max(float(np.abs(r).max()), 1.0), (n_bad, worst)
 
 
+def test_long_context_steps(ctx, c0):
+    """Attention reads the KV cache in staged chunks of 128 positions through
+    two alternating buffers: a 300-token prompt (exact prefill) and 1-token
+    steps at positions 300-303 cover a full chunk pair, a buffer reused for
+    the third chunk and a ragged last chunk, against the oracle."""
+    from kestrel_b200.cuda import OPT_F32_PREFILL
+    cfg = c0["cfg"]
+    prompt = prompt_of(cfg, 300, seed=5)
+    steps = prompt_of(cfg, 4, seed=6)
+    m = oracle_model(oracle, c0, n_ctx=320)
+    ref = m.forward(prompt)
+    ctx.set_option(OPT_F32_PREFILL, 1)
+    try:
+        synth.load_cuda(ctx, c0, n_ctx=320)
+        logits, _ = ctx.model_forward(prompt)
+    finally:
+        ctx.set_option(OPT_F32_PREFILL, 0)
+    scale = max(float(np.abs(ref).max()), 1.0)
+    assert float(np.abs(logits - ref).max()) <= 1e-5 * scale
+    for t in steps:
+        r = m.forward([t])
+        g, _ = ctx.model_forward([t])
+        # a few ulps at most: exp is a double-precision exp rounded to float
+        # here and the C library's expf in the reference
+        assert float(np.abs(g - r).max()) <= 1e-5 * max(float(np.abs(r).max()), 1.0)
+    assert ctx.model_cached() == 304
+
+
 @pytest.mark.parametrize("variant", ["llama-moe", "qwen2-dense", "qwen3-dense-k6"])
 def test_variants_greedy(ctx, variant):
     cfg = dict(synth.CONFIG0, n_layer=2, d=256, n_head=4, n_kv=2, head_dim=64, rope_dim=64, n_vocab=1024, ff=512)
