@@ -23,7 +23,6 @@
 //    reference, and the row's first thread gathers the eight lanes (warp
 //    shuffles) for the hsum. Integer sums are exact in any order.
 #include <algorithm>
-#include <cstdlib>
 
 #include "common.cuh"
 #include "decode.h"
@@ -129,24 +128,17 @@ void launch_act_records(bool kquant, const float* x, const float* u, const int* 
 // ---------------------------------------------------------------------------
 // Stage geometry: a stage is one 32-row tile x a segment of `ks` consecutive
 // superblocks (Q8_0: chunks of 8 blocks), followed by the unit's activation
-// records for those superblocks. KESTREL_DECODE_KS overrides ks (a tuning
-// knob; the default is two K-quant superblocks or one Q8_0 chunk of 8 blocks
-// per stage, 10.6-15.4 KB with the records).
-static int decode_ks_override() {
-  static const int v = [] {
-    const char* e = std::getenv("KESTREL_DECODE_KS");
-    return e ? std::max(0, std::atoi(e)) : 0;
-  }();
-  return v;
-}
-
+// records for those superblocks: two K-quant superblocks or one Q8_0 chunk of
+// 8 blocks per stage, 10.6-15.4 KB with the records, which gives rings of 14
+// (Q6_K), 19 (Q4_K) or 23 (Q8_0) stages. (Measured on configs[1] at 16
+// tokens: one superblock per stage is 13% slower per layer call; three per
+// stage, a 9-stage Q6_K ring, ran into the bounded empty-stage wait.)
 DecodeGeom decode_geom(int t, int64_t cols) {
   DecodeGeom g{};
   g.type = t;
   g.nb32 = t == T_Q8_0 ? (int)(cols / 32) : 0;
   g.nsb = tiled_nsb(t, cols);
-  const int ov = decode_ks_override();
-  g.ks = std::max(1, std::min(g.nsb, ov > 0 ? ov : (t == T_Q8_0 ? 1 : 2)));
+  g.ks = std::max(1, std::min(g.nsb, t == T_Q8_0 ? 1 : 2));
   g.nseg = (g.nsb + g.ks - 1) / g.ks;
   g.tile_bytes = tiled_tile_bytes(t, cols);
   int mx = 0;
