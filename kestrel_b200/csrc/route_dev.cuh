@@ -28,14 +28,32 @@ __device__ __forceinline__ void rl_step(float wv, float xv, bool odd, bool m1, f
 // optional weights_scale. One warp per token; p lives in shared memory.
 
 // One token's routing by one warp: p [E] and the selection scratch (selw,
-// seli: RT_MAXK each) in shared memory.
-__device__ __forceinline__ void route_row(const float* __restrict__ row, int E, int k, int norm_topk, float weights_scale, float* p,
-                          float* selw, int* seli, int lane, int* __restrict__ ids_out, float* __restrict__ w_out) {
-  float m = -INFINITY;
-  for (int e = lane; e < E; e += 32) m = fmaxf(m, row[e]);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  for (int e = lane; e < E; e += 32) p[e] = exp_rn(__fsub_rn(row[e], m));
+// seli: RT_MAXK each) in shared memory. Lane l owns entries l, l + 32, ...
+// The maximum and each arg-max of the top-k use warp reductions (redux.sync)
+// on integer keys, so a round costs two reductions instead of a shuffle tree.
+
+// Unsigned key with the order of the finite floats.
+__device__ __forceinline__ uint32_t ord_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+__device__ __forceinline__ void route_row(const float* __restrict__ row, int E, int k, int norm_topk,
+                                          float weights_scale, float* p, float* selw, int* seli, int lane,
+                                          int* __restrict__ ids_out, float* __restrict__ w_out) {
+  // Maximum (its sign of zero does not matter: x - (+0) and x - (-0) agree,
+  // and exp(+-0) = 1).
+  uint32_t km = 0u;
+  for (int e = lane; e < E; e += 32) {
+    const float v = row[e];
+    p[e] = v;
+    km = max(km, ord_key(v));
+  }
+  const float m = key_float(__reduce_max_sync(0xffffffffu, km));
+  for (int e = lane; e < E; e += 32) p[e] = exp_rn(__fsub_rn(p[e], m));
   __syncwarp();
   // Sequential sum (transformer.rs:481), loads batched ahead of the adds.
   float sum = -0.0f;
@@ -51,53 +69,62 @@ __device__ __forceinline__ void route_row(const float* __restrict__ row, int E, 
     for (; e < E; ++e) sum = __fadd_rn(sum, p[e]);
   }
   sum = __shfl_sync(0xffffffffu, sum, 0);
-  for (int e = lane; e < E; e += 32) p[e] = __fdiv_rn(p[e], sum);
-  __syncwarp();
-  // Top-k by repeated arg-max (larger p first, ties to the lower index, which
-  // is the first k of the reference's stable sort). Probabilities are >= 0, so
-  // a taken entry is marked with -1 in shared memory.
-  constexpr int NONE = 0x7fffffff;
-  for (int r = 0; r < k; ++r) {
-    float bp = 0.f;
-    int bi = NONE;
-    for (int e = lane; e < E; e += 32) {
-      const float v = p[e];
-      if (v < 0.f) continue;
-      if (bi == NONE || v > bp) {  // e increases within a lane: ties keep the lower index
-        bp = v;
-        bi = e;
-      }
+  // Probabilities (>= 0, so their bits order them; key = bits + 1, 0 = taken)
+  // and each lane's best entry, ties to the lower index.
+  uint32_t lk = 0u;
+  int li = 0;
+  for (int e = lane; e < E; e += 32) {
+    const float v = __fdiv_rn(p[e], sum);
+    p[e] = v;
+    const uint32_t kk = __float_as_uint(v) + 1u;
+    if (kk > lk) {
+      lk = kk;
+      li = e;
     }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const float op = __shfl_xor_sync(0xffffffffu, bp, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (oi != NONE && (bi == NONE || op > bp || (op == bp && oi < bi))) {
-        bp = op;
-        bi = oi;
-      }
-    }
-    if (lane == 0) {
-      seli[r] = bi;
-      selw[r] = bp;
-    }
-    if (bi != NONE && lane == (bi & 31)) p[bi] = -1.f;
-    __syncwarp();
   }
-  if (lane == 0) {
-    if (norm_topk) {
-      float ss = -0.0f;
+  // Top-k by repeated arg-max (larger p first, ties to the lower index: the
+  // first k of the reference's stable sort); k <= E, so a candidate remains.
+  for (int r = 0; r < k; ++r) {
+    const uint32_t mk = __reduce_max_sync(0xffffffffu, lk);
+    const int bi = (int)__reduce_min_sync(0xffffffffu, lk == mk ? (uint32_t)li : 0xffffffffu);
+    if (lane == (r & 31)) {
+      seli[r] = bi;
+      selw[r] = __uint_as_float(mk - 1u);
+    }
+    if (lane == (bi & 31)) {  // the winner's lane takes it and rescans its entries
+      p[bi] = -1.f;
+      lk = 0u;
+      for (int e = lane; e < E; e += 32) {
+        const float v = p[e];
+        const uint32_t kk = v >= 0.f ? __float_as_uint(v) + 1u : 0u;
+        if (kk > lk) {
+          lk = kk;
+          li = e;
+        }
+      }
+    }
+  }
+  __syncwarp();
+  // Renormalisation by the selection's sequential sum clamped at 2^-14, then
+  // weights_scale; each selection's division is independent.
+  float ss = 0.f;
+  if (norm_topk) {
+    if (lane == 0) {
+      ss = -0.0f;
       for (int r = 0; r < k; ++r) ss = __fadd_rn(ss, selw[r]);
       ss = fmaxf(ss, 6.1035156e-5f);
-      for (int r = 0; r < k; ++r) selw[r] = __fdiv_rn(selw[r], ss);
     }
-    if (weights_scale != 0.f && weights_scale != 1.f)
-      for (int r = 0; r < k; ++r) selw[r] = __fmul_rn(selw[r], weights_scale);
+    ss = __shfl_sync(0xffffffffu, ss, 0);
   }
-  __syncwarp();
+  // (the shuffle above follows lane 0's reads, so selw can be overwritten:
+  // it keeps the final weights for the caller)
   for (int r = lane; r < k; r += 32) {
+    float v = selw[r];
+    if (norm_topk) v = __fdiv_rn(v, ss);
+    if (weights_scale != 0.f && weights_scale != 1.f) v = __fmul_rn(v, weights_scale);
+    selw[r] = v;
     ids_out[r] = seli[r];
-    w_out[r] = selw[r];
+    w_out[r] = v;
   }
   __syncwarp();
 }

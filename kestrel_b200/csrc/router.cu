@@ -388,37 +388,108 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
   else dispatch_block(ids, w, n_tok, k, E, o, dsm);
 }
 
-// Small batches: routing (one warp per token), the dispatch metadata and,
-// for decode batches (n_tok < 4; rec non-null), the Q8_K records of every
-// slot's input row in one 1024-thread block. Shared memory: the larger of the
-// routing scratch and dispatch_block's.
+// Route + dispatch for batches of at most 32 tokens (one warp per token), and
+// for decode batches (n_tok < 4; rec non-null) the Q8_K records of every
+// slot's input row, in one 1024-thread block. With at most 32 tokens, each
+// expert's choosers fit one 32-bit token mask (shared atomicOr by the routing
+// warps), so: count = popc(mask); slot offsets, the int8 / tcgen05 lists and
+// the tile prefix come from one warp's scan over the experts; a selection's
+// slot is its expert's offset plus the earlier tokens in the mask. Slots are
+// grouped by ascending expert id and ascending token within an expert, as
+// dispatch_block orders them.
+constexpr int RD_MAXT = DP_THREADS / 32;
+static size_t rd_smem(int E, int k) {
+  return ((size_t)RD_MAXT * (E + 2 * RT_MAXK) + 2 * (size_t)E + 1 + (size_t)RD_MAXT * k) * 4;
+}
+
 __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float* __restrict__ logits, int n_tok,
                                                                      int E, int k, int norm_topk, float weights_scale,
                                                                      int* __restrict__ ids, float* __restrict__ w,
                                                                      DispatchOut o, const float* __restrict__ x,
                                                                      int d, uint8_t* __restrict__ rec) {
-  pdl_enter();
   extern __shared__ uint32_t dsm[];
+  float* scratch = reinterpret_cast<float*>(dsm);                 // [RD_MAXT][E + 2 RT_MAXK]
+  uint32_t* mask_s = dsm + RD_MAXT * (E + 2 * RT_MAXK);            // [E] token mask per expert
+  int* offs_s = reinterpret_cast<int*>(mask_s + E);               // [E + 1]
+  int* slot_tok_s = offs_s + E + 1;                               // [n_tok * k]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  {
-    float* p = reinterpret_cast<float*>(dsm) + warp * (E + 2 * RT_MAXK);
-    float* selw = p + E;
-    int* seli = reinterpret_cast<int*>(selw + RT_MAXK);
-    for (int t = warp; t < n_tok; t += DP_THREADS / 32)
-      route_row(logits + (int64_t)t * E, E, k, norm_topk, weights_scale, p, selw, seli, lane, ids + (int64_t)t * k,
-                w + (int64_t)t * k);
+  for (int e = threadIdx.x; e < E; e += DP_THREADS) mask_s[e] = 0u;
+  pdl_enter();
+  __syncthreads();
+  float* p = scratch + warp * (E + 2 * RT_MAXK);
+  float* selw = p + E;
+  int* seli = reinterpret_cast<int*>(selw + RT_MAXK);
+  if (warp < n_tok) {
+    route_row(logits + (int64_t)warp * E, E, k, norm_topk, weights_scale, p, selw, seli, lane,
+              ids + (int64_t)warp * k, w + (int64_t)warp * k);
+    for (int r = lane; r < k; r += 32) atomicOr(&mask_s[seli[r]], 1u << warp);
   }
   __syncthreads();
-  // Decode batches: the scan-free dispatch (for larger batches the block scan
-  // of dispatch_block is faster).
-  if (n_tok < 4 && n_tok * k <= DS_MAXA) dispatch_small(ids, w, n_tok, k, E, o, dsm);
-  else dispatch_block(ids, w, n_tok, k, E, o, dsm);
+  if (warp == 0) {
+    // Experts [e0, e1) per lane, contiguous, then an exclusive warp scan of
+    // (rows, int8-list entries, tcgen05-list entries, tcgen05 token tiles).
+    const int C = (E + 31) / 32, e0 = min(E, lane * C), e1 = min(E, e0 + C);
+    int sc = 0, ss = 0, sl = 0, st = 0;
+    for (int e = e0; e < e1; ++e) {
+      const int c = __popc(mask_s[e]);
+      sc += c;
+      ss += (c >= 1 && c <= 3) ? 1 : 0;
+      sl += c >= 4 ? 1 : 0;
+      st += c >= 4 ? (c + kMmaTileN - 1) / kMmaTileN : 0;
+    }
+    int ic = sc, is = ss, il = sl, it = st;
+#pragma unroll
+    for (int sh = 1; sh < 32; sh <<= 1) {
+      const int a0 = __shfl_up_sync(0xffffffffu, ic, sh), a1 = __shfl_up_sync(0xffffffffu, is, sh);
+      const int a2 = __shfl_up_sync(0xffffffffu, il, sh), a3 = __shfl_up_sync(0xffffffffu, it, sh);
+      if (lane >= sh) {
+        ic += a0;
+        is += a1;
+        il += a2;
+        it += a3;
+      }
+    }
+    int oc = ic - sc, os = is - ss, ol = il - sl, ot = it - st;
+    for (int e = e0; e < e1; ++e) {
+      const int c = __popc(mask_s[e]);
+      offs_s[e] = oc;
+      o.offsets[e] = oc;
+      o.counts[e] = c;
+      if (c >= 1 && c <= 3) {
+        o.small_list[os++] = e;
+      } else if (c >= 4) {
+        o.large_list[ol] = e;
+        o.large_tt[ol++] = ot;
+        ot += (c + kMmaTileN - 1) / kMmaTileN;
+      }
+      oc += c;
+    }
+    if (lane == 31) {
+      offs_s[E] = oc;
+      o.offsets[E] = oc;
+      o.n_lists[0] = os;
+      o.n_lists[1] = ol;
+      o.large_tt[ol] = ot;
+    }
+  }
+  __syncthreads();
+  const int A = n_tok * k;
+  for (int i = threadIdx.x; i < A; i += DP_THREADS) {
+    const int t = i / k, j = i - t * k;
+    const float* tw = scratch + t * (E + 2 * RT_MAXK) + E;  // token t's final weights (selw)
+    const int e = reinterpret_cast<const int*>(tw + RT_MAXK)[j];
+    const int slot = offs_s[e] + __popc(mask_s[e] & ((1u << t) - 1u));
+    o.slot_tok[slot] = t;
+    o.slot_w[slot] = tw[j];
+    o.tok_slot[i] = slot;
+    slot_tok_s[slot] = t;
+  }
   if (!rec) return;
   __syncthreads();
-  const int A = n_tok * k, nb = d / 256;
+  const int nb = d / 256;
   for (int task = warp; task < A * nb; task += DP_THREADS / 32) {
     const int slot = task / nb, b = task - slot * nb;
-    const float* xp = x + (int64_t)o.slot_tok[slot] * d + b * 256 + lane * 8;
+    const float* xp = x + (int64_t)slot_tok_s[slot] * d + b * 256 + lane * 8;
     const float4 a0 = reinterpret_cast<const float4*>(xp)[0], a1 = reinterpret_cast<const float4*>(xp)[1];
     const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     q8k_store_record(v, rec + ((int64_t)b * A + slot) * kRecK, lane);
@@ -426,11 +497,9 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
 }
 
 bool route_dispatch_supported(int n_tok, int E, int k, int d, bool with_records) {
-  const size_t route_smem = (size_t)(DP_THREADS / 32) * (E + 2 * RT_MAXK) * 4;
-  const size_t disp_smem = (size_t)(64 * E + 3 * E + 1) * 4;
-  const bool tok_ok = with_records ? (n_tok < 4 && d % 256 == 0) : n_tok <= DP_THREADS / 32;
+  const bool tok_ok = with_records ? (n_tok < 4 && d % 256 == 0) : n_tok <= RD_MAXT;
   return n_tok >= 1 && tok_ok && E >= 1 && E <= DP_THREADS && k >= 1 && k <= RT_MAXK && k <= E &&
-         std::max(route_smem, disp_smem) <= 200 * 1024;
+         rd_smem(E, k) <= 200 * 1024;
 }
 
 void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
@@ -440,9 +509,8 @@ void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int nor
     cudaFuncSetAttribute(route_dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr = true;
   }
-  const size_t smem = std::max((size_t)(DP_THREADS / 32) * (E + 2 * RT_MAXK) * 4, (size_t)(64 * E + 3 * E + 1) * 4);
-  launch_k(route_dispatch_kernel, 1, DP_THREADS, smem, st, logits, n_tok, E, k, norm_topk, weights_scale, ids, w, o,
-           x, d, rec);
+  launch_k(route_dispatch_kernel, 1, DP_THREADS, rd_smem(E, k), st, logits, n_tok, E, k, norm_topk, weights_scale,
+           ids, w, o, x, d, rec);
 }
 
 int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st) {

@@ -146,13 +146,15 @@ def test_router_logits_bit_exact(ctx, E, d, n):
     assert np.array_equal(bits(host(logits)), bits(ref))
 
 
-@pytest.mark.parametrize("E,k", [(8, 2), (128, 8), (64, 6)])
+@pytest.mark.parametrize("E,k", [(8, 2), (128, 8), (64, 6), (40, 4), (256, 8)])
 def test_route_topk(ctx, E, k):
     """Top-k ids bit-exact; weights within a few ulps (CUDA expf vs glibc)."""
     rng = np.random.default_rng(E * k)
     n = 37
     logits = rng.standard_normal((n, E)).astype(np.float32)
     logits[0, :4] = 1.5  # exact ties -> lower index first
+    logits[1, :] = -0.25  # every entry tied: ids 0 .. k-1
+    logits[2, ::3] = 3.0  # ties spread over the lanes
     for norm, ws in [(True, 0.0), (False, 0.0), (True, 2.5)]:
         ids = torch.empty((n, k), dtype=torch.int32, device="cuda")
         w = torch.empty((n, k), dtype=torch.float32, device="cuda")
