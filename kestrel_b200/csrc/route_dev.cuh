@@ -41,9 +41,8 @@ __device__ __forceinline__ float key_float(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
-__device__ __forceinline__ void route_row(const float* __restrict__ row, int E, int k, int norm_topk,
-                                          float weights_scale, float* p, float* selw, int* seli, int lane,
-                                          int* __restrict__ ids_out, float* __restrict__ w_out) {
+// Softmax of one token's logits into p (one warp).
+__device__ __forceinline__ void route_probs(const float* __restrict__ row, int E, float* p, int lane) {
   // Maximum (its sign of zero does not matter: x - (+0) and x - (-0) agree,
   // and exp(+-0) = 1).
   uint32_t km = 0u;
@@ -69,21 +68,23 @@ __device__ __forceinline__ void route_row(const float* __restrict__ row, int E, 
     for (; e < E; ++e) sum = __fadd_rn(sum, p[e]);
   }
   sum = __shfl_sync(0xffffffffu, sum, 0);
-  // Probabilities (>= 0, so their bits order them; key = bits + 1, 0 = taken)
-  // and each lane's best entry, ties to the lower index.
+  for (int e = lane; e < E; e += 32) p[e] = __fdiv_rn(p[e], sum);
+  __syncwarp();
+}
+
+// Top-k of p (>= 0, so their bits order them; key = bits + 1, 0 = taken) by
+// repeated arg-max: larger p first, ties to the lower index -- the first k of
+// the reference's stable sort. k <= E, so a candidate always remains.
+__device__ __forceinline__ void route_topk(int E, int k, float* p, float* selw, int* seli, int lane) {
   uint32_t lk = 0u;
   int li = 0;
   for (int e = lane; e < E; e += 32) {
-    const float v = __fdiv_rn(p[e], sum);
-    p[e] = v;
-    const uint32_t kk = __float_as_uint(v) + 1u;
+    const uint32_t kk = __float_as_uint(p[e]) + 1u;
     if (kk > lk) {
       lk = kk;
       li = e;
     }
   }
-  // Top-k by repeated arg-max (larger p first, ties to the lower index: the
-  // first k of the reference's stable sort); k <= E, so a candidate remains.
   for (int r = 0; r < k; ++r) {
     const uint32_t mk = __reduce_max_sync(0xffffffffu, lk);
     const int bi = (int)__reduce_min_sync(0xffffffffu, lk == mk ? (uint32_t)li : 0xffffffffu);
@@ -105,8 +106,14 @@ __device__ __forceinline__ void route_row(const float* __restrict__ row, int E, 
     }
   }
   __syncwarp();
-  // Renormalisation by the selection's sequential sum clamped at 2^-14, then
-  // weights_scale; each selection's division is independent.
+}
+
+// Renormalisation by the selection's sequential sum clamped at 2^-14, then
+// weights_scale; each selection's division is independent. selw keeps the
+// final weights for the caller.
+__device__ __forceinline__ void route_finish(int k, int norm_topk, float weights_scale, float* selw,
+                                             const int* seli, int lane, int* __restrict__ ids_out,
+                                             float* __restrict__ w_out) {
   float ss = 0.f;
   if (norm_topk) {
     if (lane == 0) {
@@ -114,10 +121,8 @@ __device__ __forceinline__ void route_row(const float* __restrict__ row, int E, 
       for (int r = 0; r < k; ++r) ss = __fadd_rn(ss, selw[r]);
       ss = fmaxf(ss, 6.1035156e-5f);
     }
-    ss = __shfl_sync(0xffffffffu, ss, 0);
+    ss = __shfl_sync(0xffffffffu, ss, 0);  // after lane 0's reads: selw may be overwritten
   }
-  // (the shuffle above follows lane 0's reads, so selw can be overwritten:
-  // it keeps the final weights for the caller)
   for (int r = lane; r < k; r += 32) {
     float v = selw[r];
     if (norm_topk) v = __fdiv_rn(v, ss);
@@ -127,6 +132,14 @@ __device__ __forceinline__ void route_row(const float* __restrict__ row, int E, 
     w_out[r] = v;
   }
   __syncwarp();
+}
+
+__device__ __forceinline__ void route_row(const float* __restrict__ row, int E, int k, int norm_topk,
+                                          float weights_scale, float* p, float* selw, int* seli, int lane,
+                                          int* __restrict__ ids_out, float* __restrict__ w_out) {
+  route_probs(row, E, p, lane);
+  route_topk(E, k, p, selw, seli, lane);
+  route_finish(k, norm_topk, weights_scale, selw, seli, lane, ids_out, w_out);
 }
 
 }  // namespace kc

@@ -390,16 +390,19 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
 
 // Route + dispatch for batches of at most 32 tokens (one warp per token), and
 // for decode batches (n_tok < 4; rec non-null) the Q8_K records of every
-// slot's input row, in one 1024-thread block. With at most 32 tokens, each
-// expert's choosers fit one 32-bit token mask (shared atomicOr by the routing
-// warps), so: count = popc(mask); slot offsets, the int8 / tcgen05 lists and
-// the tile prefix come from one warp's scan over the experts; a selection's
-// slot is its expert's offset plus the earlier tokens in the mask. Slots are
-// grouped by ascending expert id and ascending token within an expert, as
-// dispatch_block orders them.
+// slot's input row, in one 1024-thread block. Top-k: with at most one
+// (token, expert) entry per thread, every entry's rank in its token's stable
+// descending order is counted by its own thread (one parallel pass);
+// otherwise each token's warp takes k arg-max rounds. With at most 32 tokens,
+// each expert's choosers fit one 32-bit token mask (shared atomicOr), so:
+// count = popc(mask); slot offsets, list positions and the tile prefix come
+// from one warp's scan over the experts (into shared memory; all threads then
+// store the metadata); a selection's slot is its expert's offset plus the
+// earlier tokens in the mask. Slots are grouped by ascending expert id and
+// ascending token within an expert, as dispatch_block orders them.
 constexpr int RD_MAXT = DP_THREADS / 32;
 static size_t rd_smem(int E, int k) {
-  return ((size_t)RD_MAXT * (E + 2 * RT_MAXK) + 2 * (size_t)E + 1 + (size_t)RD_MAXT * k) * 4;
+  return ((size_t)RD_MAXT * (E + 2 * RT_MAXK) + 5 * (size_t)E + 5 + (size_t)RD_MAXT * k) * 4;
 }
 
 __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float* __restrict__ logits, int n_tok,
@@ -407,22 +410,58 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
                                                                      int* __restrict__ ids, float* __restrict__ w,
                                                                      DispatchOut o, const float* __restrict__ x,
                                                                      int d, uint8_t* __restrict__ rec) {
-  extern __shared__ uint32_t dsm[];
-  float* scratch = reinterpret_cast<float*>(dsm);                 // [RD_MAXT][E + 2 RT_MAXK]
-  uint32_t* mask_s = dsm + RD_MAXT * (E + 2 * RT_MAXK);            // [E] token mask per expert
-  int* offs_s = reinterpret_cast<int*>(mask_s + E);               // [E + 1]
-  int* slot_tok_s = offs_s + E + 1;                               // [n_tok * k]
+  extern __shared__ __align__(16) uint32_t dsm[];
+  const int SW = E + 2 * RT_MAXK;                                 // per-token scratch: p, selw, seli
+  float* scratch = reinterpret_cast<float*>(dsm);                 // [RD_MAXT][SW]
+  uint32_t* mask_s = dsm + RD_MAXT * SW;                          // [E] token mask per expert
+  int* offs_s = reinterpret_cast<int*>(mask_s + E);               // [E + 1] slot offsets
+  int* pos_s = offs_s + E + 1;                                    // [E] place in the int8 / tcgen05 list
+  int* tt_s = pos_s + E;                                          // [E] tcgen05 tile prefix
+  int* tot_s = tt_s + E;                                          // [4] int8 entries, tcgen05 entries, tiles
+  int* slot_tok_s = tot_s + 4;                                    // [n_tok * k]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < E; e += DP_THREADS) mask_s[e] = 0u;
   pdl_enter();
-  __syncthreads();
-  float* p = scratch + warp * (E + 2 * RT_MAXK);
+  float* p = scratch + warp * SW;
   float* selw = p + E;
   int* seli = reinterpret_cast<int*>(selw + RT_MAXK);
-  if (warp < n_tok) {
-    route_row(logits + (int64_t)warp * E, E, k, norm_topk, weights_scale, p, selw, seli, lane,
-              ids + (int64_t)warp * k, w + (int64_t)warp * k);
-    for (int r = lane; r < k; r += 32) atomicOr(&mask_s[seli[r]], 1u << warp);
+  if (n_tok * E <= DP_THREADS) {
+    if (warp < n_tok) route_probs(logits + (int64_t)warp * E, E, p, lane);
+    __syncthreads();
+    const int i = threadIdx.x;
+    if (i < n_tok * E) {
+      const int t = i / E, e = i - t * E;
+      const float* pt = scratch + t * SW;
+      const float v = pt[e];
+      int rank = 0;
+      if ((E & 3) == 0) {
+        for (int e2 = 0; e2 < E; e2 += 4) {
+          const float4 q = *reinterpret_cast<const float4*>(pt + e2);
+          rank += (q.x > v || (q.x == v && e2 < e)) ? 1 : 0;
+          rank += (q.y > v || (q.y == v && e2 + 1 < e)) ? 1 : 0;
+          rank += (q.z > v || (q.z == v && e2 + 2 < e)) ? 1 : 0;
+          rank += (q.w > v || (q.w == v && e2 + 3 < e)) ? 1 : 0;
+        }
+      } else {
+        for (int e2 = 0; e2 < E; ++e2) rank += (pt[e2] > v || (pt[e2] == v && e2 < e)) ? 1 : 0;
+      }
+      if (rank < k) {
+        float* tw = scratch + t * SW + E;
+        tw[rank] = v;
+        reinterpret_cast<int*>(tw + RT_MAXK)[rank] = e;
+        atomicOr(&mask_s[e], 1u << t);
+      }
+    }
+    __syncthreads();
+    if (warp < n_tok)
+      route_finish(k, norm_topk, weights_scale, selw, seli, lane, ids + (int64_t)warp * k, w + (int64_t)warp * k);
+  } else {
+    __syncthreads();  // mask_s zeroed
+    if (warp < n_tok) {
+      route_row(logits + (int64_t)warp * E, E, k, norm_topk, weights_scale, p, selw, seli, lane,
+                ids + (int64_t)warp * k, w + (int64_t)warp * k);
+      for (int r = lane; r < k; r += 32) atomicOr(&mask_s[seli[r]], 1u << warp);
+    }
   }
   __syncthreads();
   if (warp == 0) {
@@ -453,30 +492,44 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
     for (int e = e0; e < e1; ++e) {
       const int c = __popc(mask_s[e]);
       offs_s[e] = oc;
-      o.offsets[e] = oc;
-      o.counts[e] = c;
+      oc += c;
       if (c >= 1 && c <= 3) {
-        o.small_list[os++] = e;
+        pos_s[e] = os++;
       } else if (c >= 4) {
-        o.large_list[ol] = e;
-        o.large_tt[ol++] = ot;
+        pos_s[e] = ol++;
+        tt_s[e] = ot;
         ot += (c + kMmaTileN - 1) / kMmaTileN;
       }
-      oc += c;
     }
     if (lane == 31) {
       offs_s[E] = oc;
-      o.offsets[E] = oc;
-      o.n_lists[0] = os;
-      o.n_lists[1] = ol;
-      o.large_tt[ol] = ot;
+      tot_s[0] = os;
+      tot_s[1] = ol;
+      tot_s[2] = ot;
     }
   }
   __syncthreads();
+  for (int e = threadIdx.x; e < E; e += DP_THREADS) {
+    const int c = __popc(mask_s[e]);
+    o.offsets[e] = offs_s[e];
+    o.counts[e] = c;
+    if (c >= 1 && c <= 3) {
+      o.small_list[pos_s[e]] = e;
+    } else if (c >= 4) {
+      o.large_list[pos_s[e]] = e;
+      o.large_tt[pos_s[e]] = tt_s[e];
+    }
+  }
+  if (threadIdx.x == DP_THREADS - 1) {
+    o.offsets[E] = offs_s[E];
+    o.n_lists[0] = tot_s[0];
+    o.n_lists[1] = tot_s[1];
+    o.large_tt[tot_s[1]] = tot_s[2];
+  }
   const int A = n_tok * k;
   for (int i = threadIdx.x; i < A; i += DP_THREADS) {
     const int t = i / k, j = i - t * k;
-    const float* tw = scratch + t * (E + 2 * RT_MAXK) + E;  // token t's final weights (selw)
+    const float* tw = scratch + t * SW + E;  // token t's final weights (selw), then ids (seli)
     const int e = reinterpret_cast<const int*>(tw + RT_MAXK)[j];
     const int slot = offs_s[e] + __popc(mask_s[e] & ((1u << t) - 1u));
     o.slot_tok[slot] = t;
