@@ -154,8 +154,22 @@ DecodeGeom decode_geom(int t, int64_t cols) {
 }
 
 
+// Producer warps: warp p issues the stages of units p * DUP .. p * DUP + DUP - 1
+// of each group (one lane per unit). Spreading the group's units over several
+// warps lets their copies issue in parallel instead of one lane after another.
+constexpr int DPW = 4;
+constexpr int DUP = DW / DPW;  // units (lanes) per producer warp
+constexpr int DEC_THREADS = 32 * (DC + DPW);
+static_assert(DW % DPW == 0, "producer layout");
+
+// Producer-warp barrier (named barrier 1): the DPW warps move from segment to
+// segment together.
+__device__ __forceinline__ void producer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(DPW * 32) : "memory");
+}
+
 template <int T>
-__global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, DecodeGeom g, int n_stages) {
+__global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, DecodeGeom g, int n_stages) {
   // With a.early the expert list and offsets were written before the
   // previous kernel ran (only the activation records come from it): the
   // producer reads them (L2) and starts the first lap's weight copies before
@@ -193,56 +207,34 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
   uint8_t* ring = smem;
   auto unit_at = [&](int i) { return unit_pos(b + i * G, tiles, a.n_mat); };
 
-  if (warp == 0) {
-    // Producer: group by group, segment-major, one stage per (segment, unit):
+  if (warp < DPW) {
+    // Producers: group by group, segment-major, one stage per (segment, unit):
     // the segment's weight bytes of the unit's 32-row tile (one bulk copy),
     // then the unit's activation records of each superblock of the segment
-    // (one bulk copy per superblock: ns records are contiguous). Lane w
-    // issues unit w's stage of every segment, so the stages of a segment go
-    // out in parallel.
+    // (one bulk copy per superblock: ns records are contiguous). Lane l of
+    // producer warp p issues unit w = p * DUP + l's stage of every segment.
+    // All 32 lanes of the producer warps run the loops (the named barrier
+    // counts whole warps); lanes >= DUP issue nothing.
     int last = -1;  // highest stage number this lane issued
-    if (lane < DW) {
-      const int w = lane;
-      bool ok = true;
-      // Unit meta and byte ranges of group gi / segment seg for this lane.
-      auto unit_ptrs = [&](int gi, const uint8_t*& up, const uint8_t*& rp, int& rbytes) {
-        const UnitPos p = unit_at(gi * DW + w);
-        const UnitMeta um = meta_at(list_s, off_s, p.li);
-        up = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(um.e - a.expert_base) * a.expert_stride +
-             (int64_t)p.tile * g.tile_bytes;
-        rp = a.rec + (int64_t)um.slot0 * R;
-        rbytes = um.ns * R;
-      };
-      if (a.early) {
-        // First lap (stages 0 .. n_stages-1, no slot to wait for): weights
-        // now, the records after the wait below. The loop bound depends only
-        // on (gi, seg), so every lane reaches the same __syncwarp calls.
-        for (int gi = 0; gi < n_groups; ++gi) {
-          const int wg = min(DW, n_units - gi * DW);
-          if (gi * g.nseg * DW >= n_stages) break;
-          const bool active = w < wg;
-          const uint8_t *up = nullptr, *rp = nullptr;
-          int rbytes = 0;
-          if (active) unit_ptrs(gi, up, rp, rbytes);
-          int64_t off0 = 0;
-          for (int seg = 0; seg < g.nseg; ++seg) {
-            const int sb0 = seg * g.ks, sb1 = min(g.nsb, sb0 + g.ks);
-            const int64_t off1 = sb1 == g.nsb ? g.tile_bytes : tiled_sb_offset(g.type, a.cols, sb1);
-            const int sid = gi * g.nseg * DW + seg * wg + w;
-            if (active && sid < n_stages) {
-              const uint32_t wbytes = (uint32_t)(off1 - off0);
-              mbar_expect_tx(&full[sid], wbytes + (uint32_t)((sb1 - sb0) * rbytes));
-              bulk_g2s(ring + (int64_t)sid * g.stage_bytes, up + off0, wbytes, &full[sid]);
-            }
-            off0 = off1;
-            __syncwarp((1u << DW) - 1u);
-          }
-        }
-        pdl_wait();
-      }
+    const int w = warp * DUP + lane;
+    const bool lane_on = lane < DUP;
+    bool ok = true;
+    // Unit meta and byte ranges of group gi for this lane.
+    auto unit_ptrs = [&](int gi, const uint8_t*& up, const uint8_t*& rp, int& rbytes) {
+      const UnitPos p = unit_at(gi * DW + w);
+      const UnitMeta um = meta_at(list_s, off_s, p.li);
+      up = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(um.e - a.expert_base) * a.expert_stride +
+           (int64_t)p.tile * g.tile_bytes;
+      rp = a.rec + (int64_t)um.slot0 * R;
+      rbytes = um.ns * R;
+    };
+    if (a.early) {
+      // First lap (stages 0 .. n_stages-1, no slot to wait for): weights now,
+      // the records after the wait below.
       for (int gi = 0; gi < n_groups; ++gi) {
         const int wg = min(DW, n_units - gi * DW);
-        const bool active = w < wg;
+        if (gi * g.nseg * DW >= n_stages) break;
+        const bool active = lane_on && w < wg;
         const uint8_t *up = nullptr, *rp = nullptr;
         int rbytes = 0;
         if (active) unit_ptrs(gi, up, rp, rbytes);
@@ -250,51 +242,75 @@ __global__ void __launch_bounds__(DTHREADS, 1) decode_kernel(DecodeArgs a, Decod
         for (int seg = 0; seg < g.nseg; ++seg) {
           const int sb0 = seg * g.ks, sb1 = min(g.nsb, sb0 + g.ks);
           const int64_t off1 = sb1 == g.nsb ? g.tile_bytes : tiled_sb_offset(g.type, a.cols, sb1);
-          if (active && ok) {
-            const int sid = gi * g.nseg * DW + seg * wg + w;
-            const int st = sid % n_stages;
-            const uint32_t ph = (uint32_t)((sid / n_stages) & 1);
-            const bool weights_sent = a.early && sid < n_stages;
-            if (sid >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status, W_DEC_EMPTY)) {
-              ok = false;
-            } else {
-              const uint32_t wbytes = (uint32_t)(off1 - off0);
-              uint8_t* dst = ring + (int64_t)st * g.stage_bytes;
-              if (!weights_sent) {
-                mbar_expect_tx(&full[st], wbytes + (uint32_t)((sb1 - sb0) * rbytes));
-                bulk_g2s(dst, up + off0, wbytes, &full[st]);
-              }
-              for (int sb = sb0; sb < sb1; ++sb)
-                bulk_g2s(dst + g.rec_off + (sb - sb0) * (DMAXS * R), rp + (int64_t)sb * a.rec_slots * R,
-                         (uint32_t)rbytes, &full[st]);
-              last = sid;
-            }
+          const int sid = gi * g.nseg * DW + seg * wg + w;
+          if (active && sid < n_stages) {
+            const uint32_t wbytes = (uint32_t)(off1 - off0);
+            mbar_expect_tx(&full[sid], wbytes + (uint32_t)((sb1 - sb0) * rbytes));
+            bulk_g2s(ring + (int64_t)sid * g.stage_bytes, up + off0, wbytes, &full[sid]);
           }
           off0 = off1;
-          // Lanes stay within one segment of each other (independent thread
-          // scheduling could let one run ahead while another waits), so a
-          // slot's previous lap (n_stages > DW stages back) is always issued
-          // before a lane waits for its release.
-          __syncwarp((1u << DW) - 1u);
         }
       }
-    } else if (a.early) {
       pdl_wait();
     }
-    // Keep the CTA alive until every issued copy has landed (bounded): lane 0
-    // waits for the last n_stages stages up to the highest one issued.
-#pragma unroll
-    for (int o = 16; o; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
-    if (lane == 0)
-      for (int k = max(0, last + 1 - n_stages); k <= last; ++k)
-        mbar_wait(&full[k % n_stages], (uint32_t)((k / n_stages) & 1), a.status, W_DEC_DRAIN);
+    for (int gi = 0; gi < n_groups; ++gi) {
+      const int wg = min(DW, n_units - gi * DW);
+      const bool active = lane_on && w < wg;
+      const uint8_t *up = nullptr, *rp = nullptr;
+      int rbytes = 0;
+      if (active) unit_ptrs(gi, up, rp, rbytes);
+      int64_t off0 = 0;
+      for (int seg = 0; seg < g.nseg; ++seg) {
+        const int sb0 = seg * g.ks, sb1 = min(g.nsb, sb0 + g.ks);
+        const int64_t off1 = sb1 == g.nsb ? g.tile_bytes : tiled_sb_offset(g.type, a.cols, sb1);
+        if (active && ok) {
+          const int sid = gi * g.nseg * DW + seg * wg + w;
+          const int st = sid % n_stages;
+          const uint32_t ph = (uint32_t)((sid / n_stages) & 1);
+          const bool weights_sent = a.early && sid < n_stages;
+          if (sid >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status, W_DEC_EMPTY)) {
+            ok = false;
+          } else {
+            const uint32_t wbytes = (uint32_t)(off1 - off0);
+            uint8_t* dst = ring + (int64_t)st * g.stage_bytes;
+            if (!weights_sent) {
+              mbar_expect_tx(&full[st], wbytes + (uint32_t)((sb1 - sb0) * rbytes));
+              bulk_g2s(dst, up + off0, wbytes, &full[st]);
+            }
+            for (int sb = sb0; sb < sb1; ++sb)
+              bulk_g2s(dst + g.rec_off + (sb - sb0) * (DMAXS * R), rp + (int64_t)sb * a.rec_slots * R,
+                       (uint32_t)rbytes, &full[st]);
+            last = sid;
+          }
+        }
+        off0 = off1;
+        // All producer lanes stay within one segment of each other (a lane
+        // waiting for a slot could otherwise be passed by the others), so a
+        // slot's previous lap (n_stages > DW stages back) is always issued
+        // before a lane waits for its release. Every producer thread runs
+        // the same (gi, seg) iterations, so all reach this barrier alike.
+        producer_sync();
+      }
+    }
+    // Keep the CTA alive until every copy has landed (bounded): one thread
+    // waits for the last lap, stages nseg * n_units - n_stages .. the last
+    // (the stage count is fixed, so no later lap of those slots exists).
+    // After a failed wait some stages were never issued; their drain waits
+    // end at the bound.
+    (void)last;
+    if (warp == 0 && lane == 0) {
+      const int total = g.nseg * n_units;
+      bool live = true;
+      for (int k = max(0, total - n_stages); k < total && live; ++k)
+        live = mbar_wait(&full[k % n_stages], (uint32_t)((k / n_stages) & 1), a.status, W_DEC_DRAIN);
+    }
     return;
   }
 
   // Consumers: in group gi (wg units), warp c serves unit c / TPR with
   // TPR = tpr_of(wg) threads per row; the TPR warps of a unit split its 32
   // rows, 32 / TPR each.
-  const int c = warp - 1;
+  const int c = warp - DPW;
   bool ok = true;
   for (int gi = 0; gi < n_groups; ++gi) {
     const int wg = min(DW, n_units - gi * DW);
@@ -326,7 +342,7 @@ static int launch_decode_t(const DecodeArgs& a, const DecodeGeom& g, int max_uni
   }
   const int cap = max_ctas > 0 ? std::min(max_ctas, num_sms()) : num_sms();
   const int grid = std::min(cap, std::max(1, max_units));
-  launch_k(decode_kernel<T>, grid, DTHREADS, smem, st, a, g, n_stages);
+  launch_k(decode_kernel<T>, grid, DEC_THREADS, smem, st, a, g, n_stages);
   return KC_OK;
 }
 
