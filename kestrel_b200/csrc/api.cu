@@ -1246,7 +1246,7 @@ int model_buffers(kc_ctx* ctx, Model& m, int T) {
   CK(cudaMalloc(&m.g, (size_t)T * F * 4));
   CK(cudaMalloc(&m.u, (size_t)T * F * 4));
   CK(cudaMalloc(&m.tok, (size_t)T * 4));
-  CK(cudaMalloc(&m.rec, (size_t)std::min(T, 3) * std::max(1, m.d / 256) * kRecK));
+  CK(cudaMalloc(&m.rec, (size_t)std::min(T, 3) * rec_row_bytes(true, std::max(256, m.d))));
   m.T = T;
   m.F = F;
   return KC_OK;

@@ -74,7 +74,7 @@ __global__ void q8k_records_kernel(const float* __restrict__ x, const float* __r
     *reinterpret_cast<uint4*>(f16out + slot * cols + b * 256 + lane * 8) = *reinterpret_cast<uint4*>(h);
   }
   if (!rec) return;
-  q8k_store_record(v, rec + (b * rec_slots + slot) * kRecK, lane);
+  q8k_store_record(v, rec + rec_index(b, slot, rec_slots) * kRecK, lane);
 }
 
 // Q8Row::quantize (qdot.rs:29-49); optional SwiGLU first. One warp per
@@ -148,8 +148,12 @@ DecodeGeom decode_geom(int t, int64_t cols) {
     mx = std::max(mx, (int)(end - tiled_sb_offset(t, cols, a)));
   }
   g.rec_off = ((mx + 127) / 128) * 128;
+  // Records of a stage: K-quant, the pair block of up to DMAXS slots (two
+  // records each, whether the stage holds one superblock or two); Q8, ks
+  // chunks of DMAXS records.
   const int rb = rec_bytes_of(t != T_Q8_0);
-  g.stage_bytes = ((g.rec_off + g.ks * DMAXS * rb + 127) / 128) * 128;
+  const int rec_region = t != T_Q8_0 ? DMAXS * 2 * rb : g.ks * DMAXS * rb;
+  g.stage_bytes = ((g.rec_off + rec_region + 127) / 128) * 128;
   return g;
 }
 
@@ -220,13 +224,21 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
     const bool lane_on = lane < DUP;
     bool ok = true;
     // Unit meta and byte ranges of group gi for this lane.
+    // K-quant records: one copy per stage, the pair block of the unit's slots
+    // (ns * 2 records; a stage's superblocks are one aligned pair). Q8 records:
+    // one copy per chunk (a stage is one chunk).
+    constexpr bool KQ = T != T_Q8_0;
     auto unit_ptrs = [&](int gi, const uint8_t*& up, const uint8_t*& rp, int& rbytes) {
       const UnitPos p = unit_at(gi * DW + w);
       const UnitMeta um = meta_at(list_s, off_s, p.li);
       up = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(um.e - a.expert_base) * a.expert_stride +
            (int64_t)p.tile * g.tile_bytes;
-      rp = a.rec + (int64_t)um.slot0 * R;
-      rbytes = um.ns * R;
+      rp = a.rec + (int64_t)um.slot0 * (KQ ? 2 * R : R);
+      rbytes = um.ns * (KQ ? 2 * R : R);
+    };
+    // Record bytes of a stage, and the copy of them.
+    auto stage_rec_bytes = [&](int sb0, int sb1, int rbytes) {
+      return KQ ? (uint32_t)rbytes : (uint32_t)((sb1 - sb0) * rbytes);
     };
     if (a.early) {
       // First lap (stages 0 .. n_stages-1, no slot to wait for): weights now,
@@ -245,7 +257,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
           const int sid = gi * g.nseg * DW + seg * wg + w;
           if (active && sid < n_stages) {
             const uint32_t wbytes = (uint32_t)(off1 - off0);
-            mbar_expect_tx(&full[sid], wbytes + (uint32_t)((sb1 - sb0) * rbytes));
+            mbar_expect_tx(&full[sid], wbytes + stage_rec_bytes(sb0, sb1, rbytes));
             bulk_g2s(ring + (int64_t)sid * g.stage_bytes, up + off0, wbytes, &full[sid]);
           }
           off0 = off1;
@@ -274,12 +286,17 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
             const uint32_t wbytes = (uint32_t)(off1 - off0);
             uint8_t* dst = ring + (int64_t)st * g.stage_bytes;
             if (!weights_sent) {
-              mbar_expect_tx(&full[st], wbytes + (uint32_t)((sb1 - sb0) * rbytes));
+              mbar_expect_tx(&full[st], wbytes + stage_rec_bytes(sb0, sb1, rbytes));
               bulk_g2s(dst, up + off0, wbytes, &full[st]);
             }
-            for (int sb = sb0; sb < sb1; ++sb)
-              bulk_g2s(dst + g.rec_off + (sb - sb0) * (DMAXS * R), rp + (int64_t)sb * a.rec_slots * R,
-                       (uint32_t)rbytes, &full[st]);
+            if (KQ) {
+              bulk_g2s(dst + g.rec_off, rp + (int64_t)(sb0 >> 1) * a.rec_slots * (2 * R), (uint32_t)rbytes,
+                       &full[st]);
+            } else {
+              for (int sb = sb0; sb < sb1; ++sb)
+                bulk_g2s(dst + g.rec_off + (sb - sb0) * (DMAXS * R), rp + (int64_t)sb * a.rec_slots * R,
+                         (uint32_t)rbytes, &full[st]);
+            }
             last = sid;
           }
         }
@@ -324,9 +341,14 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
     const int r_out = r < a.rows ? r : -1;  // padding rows are computed, not stored
     float* out = (p.m == 0 ? a.out[0] : a.out[1]) + (int64_t)um.slot0 * a.out_stride;
     const int sid0 = gi * g.nseg * DW + u;
-    if (tpr == 2) run_unit_ns<T, 2>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
-    else if (tpr == 4) run_unit_ns<T, 4>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
-    else run_unit_ns<T, 8>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+    // Stage records: K-quant [slot][superblock of the pair], Q8 [chunk][slot].
+    constexpr int SR = T != T_Q8_0 ? 2 * R : R, SBS = T != T_Q8_0 ? R : DMAXS * R;
+    if (tpr == 2)
+      run_unit_ns<T, 2, SR, SBS>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+    else if (tpr == 4)
+      run_unit_ns<T, 4, SR, SBS>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+    else
+      run_unit_ns<T, 8, SR, SBS>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
   }
 }
 

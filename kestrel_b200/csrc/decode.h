@@ -7,19 +7,25 @@
 
 namespace kc {
 
-// Activation records, one per (superblock, slot), stored superblock-major:
-// record (sb, slot) lives at rec + (sb * rec_slots + slot) * record bytes, so
-// the records of an expert's consecutive slots for one superblock are one
-// contiguous range.
+// Activation records, one per (superblock, slot).
 //   Q8_K record (K-quant weights), 320 B: q[256] int8 | bsums int16[16] at 256
 //     | pair sums int16[8] at 288 (bsums[2i] + bsums[2i+1]) | d f32 at 304
 //   Q8 record (Q8_0 weights), per chunk of 8 blocks, 288 B: q[256] | d[8] f32
+// Q8_K records are stored by superblock pairs: record (sb, slot) is number
+// ((sb / 2) * rec_slots + slot) * 2 + sb % 2 (rec_index), so the records of an
+// expert's consecutive slots for the two superblocks of a decode stage are one
+// contiguous range. Q8 records are stored chunk-major: number
+// chunk * rec_slots + slot.
 constexpr int kRecK = 320;
 constexpr int kRecQ8 = 288;
 inline int rec_bytes_of(bool kquant) { return kquant ? kRecK : kRecQ8; }
-// Records per slot of a row of `cols` values.
+__host__ __device__ __forceinline__ int64_t rec_index(int64_t sb, int64_t slot, int64_t rec_slots) {
+  return ((sb >> 1) * rec_slots + slot) * 2 + (sb & 1);
+}
+// Records per slot of a row of `cols` values (Q8_K: superblocks rounded up to
+// a pair).
 inline int64_t rec_row_bytes(bool kquant, int64_t cols) {
-  return kquant ? cols / 256 * kRecK : (cols / 32 + 7) / 8 * kRecQ8;
+  return kquant ? (cols / 256 + 1) / 2 * 2 * kRecK : (cols / 32 + 7) / 8 * kRecQ8;
 }
 
 struct DecodeArgs {
@@ -33,8 +39,8 @@ struct DecodeArgs {
   const int* n_list;       // device scalar
   const int* offsets;      // [n_experts + 1] slot ranges
   int n_experts;           // entries of offsets minus one (<= 1024)
-  const uint8_t* rec;      // activation records (superblock-major, see above)
-  int64_t rec_slots;       // slots per superblock plane of rec
+  const uint8_t* rec;      // activation records (layout above)
+  int64_t rec_slots;       // slots per superblock (pair) plane of rec
   float* out[2];           // out[m][slot * out_stride + row]
   int64_t out_stride;
   int* status;

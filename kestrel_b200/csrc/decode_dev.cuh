@@ -256,7 +256,9 @@ static_assert(DC == 2 * DW && DW % 4 == 0, "warp layout");
 // `row` (one per lane / TPR) and lanes l0 = (lane % TPR) * LPT .. of each.
 // The unit's stages are sid0, sid0 + wg, sid0 + 2 wg, ... (segment-major
 // order of its group).
-template <int T, int TPR, int NS, class Args>
+// Records of the stage: slot s of superblock j at xr + j * SBS + s * SR
+// (defaults: superblock-major, DMAXS slots per superblock).
+template <int T, int TPR, int NS, class Args, int SR = TypeR<T>::R, int SBS = DMAXS * TypeR<T>::R>
 __device__ __forceinline__ void run_unit(const Args& a, const DecodeGeom& g, const uint8_t* ring,
                                          uint64_t* full, uint64_t* empty, int n_stages, int sid0, int wg, int lane,
                                          int row, float* out, int r_out, bool& ok) {
@@ -287,9 +289,9 @@ __device__ __forceinline__ void run_unit(const Args& a, const DecodeGeom& g, con
       const int sb0 = seg * g.ks;
       const int n = min(g.ks, g.nsb - sb0);
       for (int j = 0; j < n; ++j) {
-        if (T == T_Q4_K) q4k_sb<NS, R, LPT>(sp + 4608 * j, row, l0, xr + j * (DMAXS * R), acc, summs);
-        else if (T == T_Q6_K) q6k_sb<NS, R, LPT>(sp + 6720 * j, row, l0, xr + j * (DMAXS * R), acc);
-        else q8_0_chunk<NS, R, LPT>(sp + 8704 * j, min(8, g.nb32 - 8 * (sb0 + j)), row, l0, xr + j * (DMAXS * R), acc);
+        if (T == T_Q4_K) q4k_sb<NS, SR, LPT>(sp + 4608 * j, row, l0, xr + j * SBS, acc, summs);
+        else if (T == T_Q6_K) q6k_sb<NS, SR, LPT>(sp + 6720 * j, row, l0, xr + j * SBS, acc);
+        else q8_0_chunk<NS, SR, LPT>(sp + 8704 * j, min(8, g.nb32 - 8 * (sb0 + j)), row, l0, xr + j * SBS, acc);
       }
     }
     __syncwarp();
@@ -317,13 +319,13 @@ __device__ __forceinline__ void run_unit(const Args& a, const DecodeGeom& g, con
   }
 }
 
-template <int T, int TPR, class Args>
+template <int T, int TPR, int SR = TypeR<T>::R, int SBS = DMAXS * TypeR<T>::R, class Args>
 __device__ __forceinline__ void run_unit_ns(int ns, const Args& a, const DecodeGeom& g, const uint8_t* ring,
                                             uint64_t* full, uint64_t* empty, int n_stages, int sid0, int wg,
                                             int lane, int row, float* out, int r_out, bool& ok) {
-  if (ns == 1) run_unit<T, TPR, 1>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
-  else if (ns == 2) run_unit<T, TPR, 2>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
-  else run_unit<T, TPR, 3>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+  if (ns == 1) run_unit<T, TPR, 1, Args, SR, SBS>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+  else if (ns == 2) run_unit<T, TPR, 2, Args, SR, SBS>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+  else run_unit<T, TPR, 3, Args, SR, SBS>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
 }
 
 }  // namespace kc

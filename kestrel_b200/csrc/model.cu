@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(NormArgs a) {
     const float4 p0 = reinterpret_cast<const float4*>(sq + b * 256 + lane * 8)[0];
     const float4 p1 = reinterpret_cast<const float4*>(sq + b * 256 + lane * 8)[1];
     v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w; v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
-    q8k_store_record(v, a.rec + ((int64_t)b * a.rec_slots + blockIdx.x) * kRecK, lane);
+    q8k_store_record(v, a.rec + rec_index(b, blockIdx.x, a.rec_slots) * kRecK, lane);
   }
 }
 

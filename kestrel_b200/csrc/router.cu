@@ -545,7 +545,7 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
     const float* xp = x + (int64_t)slot_tok_s[slot] * d + b * 256 + lane * 8;
     const float4 a0 = reinterpret_cast<const float4*>(xp)[0], a1 = reinterpret_cast<const float4*>(xp)[1];
     const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    q8k_store_record(v, rec + ((int64_t)b * A + slot) * kRecK, lane);
+    q8k_store_record(v, rec + rec_index(b, slot, A) * kRecK, lane);
   }
 }
 
