@@ -110,18 +110,53 @@ def algorithmic_bytes(ids: np.ndarray, B: int, block=None) -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """SM clock and clock-event reasons sampled during the timed region: NVML
+    read from a thread about every millisecond (the timed region can be a few
+    ms), else nvidia-smi every 100 ms. Reads only; changes no setting."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvml.h): sw_power_cap 0x4, hw_slowdown 0x8,
+    # sw_thermal_slowdown 0x20, hw_thermal_slowdown 0x40.
+    REASON_BITS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+                   ("hw_thermal_slowdown", 0x40))
 
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
         self.path = None
+        self.thread = None
+        self.samples = []
+        self.max_mhz = None
+        self.stop = False
+
+    def _poll(self, nv, hnd):
+        while not self.stop:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(hnd, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(hnd)
+                self.samples.append((sm, rs))
+            except Exception:
+                break
+            time.sleep(0.001)
 
     def __enter__(self):
+        # A short switch interval lets the polling thread run while the main
+        # thread launches the timed steps (restored on exit).
+        self.switch = sys.getswitchinterval()
+        sys.setswitchinterval(0.0002)
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            hnd = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(hnd, nv.NVML_CLOCK_SM)
+            import threading
+            self.thread = threading.Thread(target=self._poll, args=(nv, hnd), daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
@@ -134,11 +169,23 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        sys.setswitchinterval(self.switch)
+        if self.thread:
+            self.stop = True
+            self.thread.join(timeout=5)
         if self.proc:
             self.proc.terminate()
             self.proc.wait(timeout=5)
 
     def summary(self):
+        if self.thread is not None:
+            if not self.samples:
+                return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0,
+                        "source": "nvml"}
+            reasons = sorted({n for _, rs in self.samples for n, bit in self.REASON_BITS if rs & bit})
+            return {"sm_mhz": statistics.median(float(sm) for sm, _ in self.samples),
+                    "sm_max_mhz": float(self.max_mhz) if self.max_mhz else None, "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml"}
         rows = []
         try:
             for line in open(self.path):
@@ -154,7 +201,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi"}
 
 
 # ----------------------------------------------------------------------------
@@ -489,7 +536,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=48)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c1",
