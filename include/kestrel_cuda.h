@@ -215,7 +215,11 @@ KC_API int kc_profile_read(kc_ctx* ctx, double* stage_ms, int64_t* stage_calls, 
    The first call on each device looks up the array's device address; make
    that first call before capturing a stream. All calls on a device share the
    one array: calls whose kernels may overlap on the GPU (different streams
-   without ordering) race, so serialise them. */
+   without ordering) race, so serialise them.
+   The call returns once its kernels are enqueued. If one of its bounded
+   device-side waits expires (a GPU stalled for seconds), every selection of
+   the call is written as id -1 with weight 0: a caller that cannot rule this
+   out checks the ids for -1 after synchronising the stream. */
 KC_API int kc_route_noalloc(const float* router_w, int n_expert, int d, const float* h, int n_tok, int k,
                             int norm_topk, float weights_scale, int32_t* topk_ids, float* topk_w, void* stream);
 

@@ -433,14 +433,17 @@ bool pdl_enabled() {
 }
 
 int num_sms() {
-  static int dev = -1, sms = 0;
+  // SM count per device, read once per device (several contexts on different
+  // GPUs may share the process and call from different threads).
+  static std::atomic<int> sms_of[PerDeviceOnce::kMaxDev] = {};
   int cur = 0;
-  cudaGetDevice(&cur);
-  if (cur != dev) {
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cur);
-    dev = cur;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur < 0 || cur >= PerDeviceOnce::kMaxDev) return 1;
+  int sms = sms_of[cur].load(std::memory_order_relaxed);
+  if (sms <= 0) {
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cur) != cudaSuccess || sms <= 0) return 1;
+    sms_of[cur].store(sms, std::memory_order_relaxed);
   }
-  return sms > 0 ? sms : 1;
+  return sms;
 }
 }  // namespace kc
 

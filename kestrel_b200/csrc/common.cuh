@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
 #include <utility>
 
 #include "../../include/kestrel_cuda.h"
@@ -265,6 +267,37 @@ __device__ __forceinline__ void pdl_enter() {
 }
 // KESTREL_PDL=0 launches them as ordinary stream-ordered kernels.
 bool pdl_enabled();
+
+// Kernel attributes such as cudaFuncAttributeMaxDynamicSharedMemorySize are
+// per device: a process that drives several GPUs (one context each) must set
+// them on every device it launches on. One PerDeviceOnce per call site runs
+// its setter once per device, the first time a host thread launches there
+// with that device current; concurrent first calls are serialised.
+struct PerDeviceOnce {
+  static constexpr int kMaxDev = 64;
+  std::atomic<uint64_t> done{0};
+  std::mutex mu;
+  template <typename Fn>
+  cudaError_t run(Fn&& setter) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+    const uint64_t bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.load(std::memory_order_relaxed) & bit) return cudaSuccess;
+    e = setter();
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+    return e;
+  }
+};
+// Raises kernel's dynamic shared-memory limit to `bytes` on the current
+// device, once per device (per call site through `once`).
+template <typename... KArgs>
+inline cudaError_t smem_attr_once(PerDeviceOnce& once, void (*kernel)(KArgs...), int bytes) {
+  return once.run([&] { return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); });
+}
 template <typename... KArgs, typename... Args>
 inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                      Args&&... args) {

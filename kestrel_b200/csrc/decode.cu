@@ -357,11 +357,8 @@ static int launch_decode_t(const DecodeArgs& a, const DecodeGeom& g, int max_uni
   const int n_stages = std::min(DMAX_STAGES, DSMEM / g.stage_bytes);
   if (n_stages <= DW) return KC_ERR_SHAPE;
   const size_t smem = (size_t)n_stages * g.stage_bytes;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(decode_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, DSMEM);
-    attr = true;
-  }
+  static PerDeviceOnce attr;
+  if (smem_attr_once(attr, decode_kernel<T>, DSMEM) != cudaSuccess) return KC_ERR_CUDA;
   const int cap = max_ctas > 0 ? std::min(max_ctas, num_sms()) : num_sms();
   const int grid = std::min(cap, std::max(1, max_units));
   launch_k(decode_kernel<T>, grid, DEC_THREADS, smem, st, a, g, n_stages);

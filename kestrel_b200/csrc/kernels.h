@@ -50,8 +50,11 @@ void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int 
 // out[s, :] += g[s] * y[s, :] with g[s] = 1 / (1 + exp(-logit[s])) (logit
 // null: g = 1): the shared expert's contribution (transformer.rs:577-585).
 void launch_shared_add(const float* y, const float* logit, int n_tok, int d, float* out, cudaStream_t st);
+// fail (optional): a status word written by earlier kernels of the call; when
+// it is nonzero at the route kernel, every selection is written as id -1,
+// weight 0.
 void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
-                  float* w, cudaStream_t st);
+                  float* w, cudaStream_t st, const int* fail = nullptr);
 // Dispatch metadata of one routed batch (see router.cu).
 struct DispatchOut {
   int* counts;     // [E]

@@ -524,13 +524,8 @@ bool mma_supported(int t, int64_t cols, int n_mat) {
 template <int T, int NMAT>
 static int launch_t(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st, int max_ctas) {
   const MmaSmem L = mma_smem(T, NMAT);
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(mma_grouped_kernel<T, NMAT>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
-        cudaSuccess)
-      return KC_ERR_CUDA;
-    attr = true;
-  }
+  static PerDeviceOnce attr;
+  if (smem_attr_once(attr, mma_grouped_kernel<T, NMAT>, L.total) != cudaSuccess) return KC_ERR_CUDA;
   // With a split-K workspace every SM gets a CTA (the kernel splits K when the
   // batch has few tiles); otherwise one CTA per tile at most.
   const int cap = max_ctas > 0 ? std::min(max_ctas, num_sms()) : num_sms();

@@ -398,11 +398,8 @@ void launch_attention(const float* q, const __half* kc, const __half* vc, int n,
   // With the position on the device (graph replays), shared memory is sized
   // for max_pos positions.
   const size_t smem = (size_t)(hd + ATT_PC * hd + (pos_dev ? max_pos : pos0 + n)) * 4;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
+  static PerDeviceOnce attr;
+  smem_attr_once(attr, attention_kernel, 200 * 1024);
   launch_k(attention_kernel, dim3(n, nh), ATT_THREADS, smem, st, q, kc, vc, nh, nkv, hd, pos0, pos_dev, scale, out);
 }
 

@@ -128,13 +128,10 @@ __global__ void __launch_bounds__(RL_E * RT * 8) router_logits_kernel(const floa
 void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int d, const float* h, int n_tok,
                           float* logits, int* status, cudaStream_t st, bool force_dot) {
   if (n_tok <= 0) return;
-  static bool attr = false;
+  static PerDeviceOnce attr_gemm, attr_dot;
   const size_t smem = rl_smem(RL_T);
-  if (!attr) {
-    cudaFuncSetAttribute(router_logits_kernel<true, RL_T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(router_logits_kernel<false, RL_T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  smem_attr_once(attr_gemm, router_logits_kernel<true, RL_T>, (int)smem);
+  smem_attr_once(attr_dot, router_logits_kernel<false, RL_T>, (int)smem);
   dim3 grid(ceil_div(E, RL_E), ceil_div(n_tok, RL_T));
   // quant::matmul's dispatch (quant.rs:241): the GEMM path needs >= 4 rows and
   // d % 8 == 0; otherwise quant::dot per output.
@@ -150,12 +147,22 @@ void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int 
 // Transformer::route, one warp per token (route_row, route_dev.cuh).
 __global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __restrict__ logits, int n_tok, int E,
                                                                int k, int norm_topk, float weights_scale,
-                                                               int* __restrict__ ids, float* __restrict__ wout) {
+                                                               int* __restrict__ ids, float* __restrict__ wout,
+                                                               const int* __restrict__ fail) {
   pdl_enter();
   extern __shared__ float sp[];  // [RT_WARPS][E] probabilities, then [RT_WARPS][RT_MAXK] selections
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int s = blockIdx.x * RT_WARPS + warp;
   if (s >= n_tok) return;
+  // An earlier kernel of this call recorded a failure (a bounded wait that
+  // expired): its logits are not trustworthy, so mark the selections invalid.
+  if (fail && *(volatile const int*)fail != 0) {
+    for (int i = lane; i < k; i += 32) {
+      ids[(int64_t)s * k + i] = -1;
+      wout[(int64_t)s * k + i] = 0.0f;
+    }
+    return;
+  }
   float* p = sp + warp * E;
   float* selw = sp + RT_WARPS * E + warp * RT_MAXK;
   int* seli = reinterpret_cast<int*>(sp + RT_WARPS * (E + RT_MAXK)) + warp * RT_MAXK;
@@ -164,11 +171,11 @@ __global__ void __launch_bounds__(RT_WARPS * 32) route_kernel(const float* __res
 }
 
 void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
-                  float* w, cudaStream_t st) {
+                  float* w, cudaStream_t st, const int* fail) {
   if (n_tok <= 0) return;
   size_t smem = (size_t)RT_WARPS * (E + 2 * RT_MAXK) * sizeof(float);
   launch_k(route_kernel, ceil_div(n_tok, RT_WARPS), RT_WARPS * 32, smem, st, logits, n_tok, E, k, norm_topk,
-           weights_scale, ids, w);
+           weights_scale, ids, w, fail);
 }
 
 // ---------------------------------------------------------------------------
@@ -557,22 +564,16 @@ bool route_dispatch_supported(int n_tok, int E, int k, int d, bool with_records)
 
 void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
                            float* w, const DispatchOut& o, const float* x, int d, uint8_t* rec, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(route_dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
+  static PerDeviceOnce attr;
+  smem_attr_once(attr, route_dispatch_kernel, 200 * 1024);
   launch_k(route_dispatch_kernel, 1, DP_THREADS, rd_smem(E, k), st, logits, n_tok, E, k, norm_topk, weights_scale,
            ids, w, o, x, d, rec);
 }
 
 int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st) {
   size_t smem = std::max((size_t)(64 * E + 3 * E + 1), (size_t)(DS_MAXA + 64 + E)) * 4;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set = true;
-  }
+  static PerDeviceOnce attr;
+  smem_attr_once(attr, dispatch_kernel, 200 * 1024);
   if (smem > 200 * 1024 || E > DP_THREADS) return KC_ERR_SHAPE;
   launch_k(dispatch_kernel, 1, DP_THREADS, smem, st, ids, w, n_tok, k, E, o);
   return KC_OK;

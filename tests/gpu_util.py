@@ -16,6 +16,62 @@ def tol_ok(got, ref, tol=1e-3):
     return err <= tol * scale, err, scale
 
 
+def rel_report(got, ref):
+    """Pure elementwise relative error |got - ref| / |ref| over the entries
+    whose |ref| is at least 1% of max|ref| (the reference's criterion above
+    normalises by the output's scale; this shows the per-element view)."""
+    ref = np.asarray(ref, np.float64)
+    got = np.asarray(got, np.float64)
+    scale = max(float(np.abs(ref).max(initial=0.0)), 1e-30)
+    m = np.abs(ref) >= 0.01 * scale
+    if not m.any():
+        return 0.0, 0.0
+    r = np.abs(got[m] - ref[m]) / np.abs(ref[m])
+    return float(np.median(r)), float(r.max())
+
+
+def gpu_layer(ctx, lid, E, k, d, ff, seed, zipf=False):
+    """A seeded full-size MoE layer quantised on the GPU with this library's
+    quantizer (byte-identical to kestrel_b200.ggml's, which numpy would take
+    minutes for at these shapes): Q4_K gate/up + Q6_K down from N(0, 0.02),
+    F32 router N(0, 0.02). Uploaded as layer `lid`; returns the host bytes for
+    the oracle.
+
+    zipf: configs[4]'s skew. The reference's router has no bias term, so the
+    inputs carry it -- feature 0 of every token is 1 (see layer_input) and
+    router column 0 holds beta_e = -1.2 * ln(1 + rank(e)) * sigma_logit
+    (rank: a seeded permutation), which adds beta_e to expert e's logit and
+    makes popularity roughly Zipf s=1.2."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    host = {}
+    for name, t, rows, cols in (("gate", G.Q4_K, E * ff, d), ("up", G.Q4_K, E * ff, d), ("down", G.Q6_K, E * d, ff)):
+        x = torch.empty((rows, cols), dtype=torch.float32, device="cuda").normal_(0.0, 0.02, generator=g)
+        q = torch.empty((rows, G.bytes_for(t, cols)), dtype=torch.uint8, device="cuda")
+        ctx.quantize_dev(t, x, q)
+        torch.cuda.synchronize()
+        host[name] = q.cpu().numpy()
+        del x, q
+    rng = np.random.default_rng(seed)
+    router = (rng.standard_normal((E, d), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    if zipf:
+        sigma = 0.02 * np.sqrt(d)  # std of a router logit for N(0, 1) features
+        rank = rng.permutation(E)
+        router[:, 0] = (-1.2 * np.log1p(rank) * sigma).astype(np.float32)
+    host.update(router=router, E=E, k=k, d=d, ff=ff, zipf=zipf)
+    ctx.upload_experts(lid, E, d, ff, G.Q4_K, host["gate"], G.Q4_K, host["up"], G.Q6_K, host["down"])
+    ctx.upload_router(lid, router, k)
+    torch.cuda.empty_cache()
+    return host
+
+
+def layer_input(host, n, seed):
+    h = np.random.default_rng(seed).standard_normal((n, host["d"])).astype(np.float32)
+    if host["zipf"]:
+        h[:, 0] = 1.0
+    return h
+
+
 def make_layer(E, k, d, ff, t_gate=G.Q4_K, t_down=G.Q6_K, seed=0, router_bias=None):
     """A seeded MoE layer: weights N(0, 0.02) quantised with this project's
     quantizer, F32 router N(0, 0.02)."""
