@@ -148,8 +148,19 @@ class ClockSampler:
         sys.setswitchinterval(0.0002)
         try:
             import pynvml as nv
+            import torch
             nv.nvmlInit()
-            hnd = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            # NVML numbers the machine's GPUs and ignores CUDA_VISIBLE_DEVICES:
+            # open this process's GPU by its PCI bus id.
+            hnd = None
+            try:
+                p = torch.cuda.get_device_properties(self.gpu)
+                bus = "%08x:%02x:%02x.0" % (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+                hnd = nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
+            except Exception:
+                hnd = None
+            if hnd is None:
+                hnd = nv.nvmlDeviceGetHandleByIndex(self.gpu)
             self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(hnd, nv.NVML_CLOCK_SM)
             import threading
             self.thread = threading.Thread(target=self._poll, args=(nv, hnd), daemon=True)
@@ -183,9 +194,12 @@ class ClockSampler:
                 return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0,
                         "source": "nvml"}
             reasons = sorted({n for _, rs in self.samples for n, bit in self.REASON_BITS if rs & bit})
-            return {"sm_mhz": statistics.median(float(sm) for sm, _ in self.samples),
-                    "sm_max_mhz": float(self.max_mhz) if self.max_mhz else None, "reasons": reasons,
-                    "samples": len(self.samples), "source": "nvml"}
+            out = {"sm_mhz": statistics.median(float(sm) for sm, _ in self.samples),
+                   "sm_max_mhz": float(self.max_mhz) if self.max_mhz else None, "reasons": reasons,
+                   "samples": len(self.samples), "source": "nvml"}
+            if len(self.samples) < 10:
+                out["note"] = "fewer than 10 samples: the median is unreliable"
+            return out
         rows = []
         try:
             for line in open(self.path):
@@ -322,15 +336,25 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def timed_steps(torch, ctx, hs, outs, n_layers, B, steps, stream):
+def timed_steps(torch, ctx, hs, outs, n_layers, B, steps, stream, issue=None):
+    """Device time (ms) of `steps` layer calls, CUDA events on the library's
+    stream. issue (optional dict): the host time spent issuing the calls (the
+    loop before the end event's wait) and the kernels they launched."""
+    from kestrel_b200.cuda import kernel_launches
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    n0 = kernel_launches()
     start.record(stream)
+    t0 = time.perf_counter()
     for i in range(steps):
         ctx.moe_ffn_dev(i % n_layers, hs[i % len(hs)], outs[i % len(outs)], n_tok=B)
+    t1 = time.perf_counter()
     end.record(stream)
     end.synchronize()
+    if issue is not None:
+        issue["host_s"] = t1 - t0
+        issue["launches"] = kernel_launches() - n0
     return start.elapsed_time(end)
 
 
@@ -398,8 +422,9 @@ def run_ours(args):
     timed_steps(torch, ctx, pool[B], outs[B], n_layers, B, args.warmup, stream)
     barrier()
     torch.cuda.synchronize()
+    issue = {}
     with ClockSampler(local) as clk:
-        ms_total = timed_steps(torch, ctx, pool[B], outs[B], n_layers, B, args.steps, stream)
+        ms_total = timed_steps(torch, ctx, pool[B], outs[B], n_layers, B, args.steps, stream, issue)
     torch.cuda.synchronize()
     barrier()
     ms_total = max_over_ranks(ms_total)
@@ -517,13 +542,12 @@ def run_ours(args):
             "sweep": sweep,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": B * d * 4,
                     "d2h_bytes_per_step": B * d * 4},
-            # this library's kernels per kc_moe_ffn_dev call on one GPU: router logits; route and
-            # dispatch (one launch for B <= 32, which for B < 4 also makes the input records);
-            # the input records (B >= 4); int8 and tcgen05 gate/up; the SwiGLU records; int8 and
-            # tcgen05 down (the tcgen05 pair only with B >= 4: an expert holds at most one row per
-            # token); combine. N > 1 adds the expert-parallel plan, pack, local ids, return plan
-            # and return pack (NCCL's own kernels not counted).
-            "gpu_launches": args.steps * (((6 if B < 4 else 9) + (1 if B > 32 else 0)) if world == 1 else 15),
+            # this library's kernel launches in the timed region (kc_kernel_launches before and
+            # after; NCCL's own kernels are not counted), and the host time spent issuing the
+            # timed calls (all of them are asynchronous): below the device time per call, the
+            # call is bound by the GPU, not by the host issuing it.
+            "gpu_launches": issue["launches"],
+            "host_issue_us_per_call": issue["host_s"] / args.steps * 1e6,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }

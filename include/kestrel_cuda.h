@@ -196,6 +196,11 @@ enum {
 };
 KC_API int kc_profile_enable(kc_ctx* ctx, int on);
 KC_API int kc_profile_read(kc_ctx* ctx, double* stage_ms, int64_t* stage_calls, int n_stages);
+/* Number of CUDA kernels this library has launched in the process so far
+   (all contexts and threads; graph replays count each captured kernel once,
+   at capture). A caller reads it before and after a run to count the
+   launches the run made. No counterpart in Kestrel (a measurement hook). */
+KC_API int64_t kc_kernel_launches(void);
 
 /* ---- routing without device allocation ----------------------------------
    No counterpart in Kestrel: an addition for hosts that cannot let a library

@@ -19,7 +19,6 @@
 #include "mma.h"
 #include "loader.h"
 #include "model.h"
-#include "moe_decode.h"
 
 using namespace kc;
 
@@ -86,7 +85,6 @@ struct Work {
   float* router_tmp = nullptr;
   float* mma_part = nullptr;  // split-K partial tiles of the tcgen05 kernel
   int* mma_cnt = nullptr;     // its per-tile counters (zeroed at allocation)
-  int* mk_sync = nullptr;     // fused decode kernel's barrier / counters (zeroed at allocation)
   // Metadata of a dense product of dmeta_n rows (one group), kept apart from
   // the MoE dispatch so that repeated products with the same n reuse it.
   DispatchOut dmeta{};
@@ -268,7 +266,6 @@ int ensure_work(kc_ctx* ctx, Work& w, int T, int E, int K, int D, int F) {
       (size_t)T * D * 4, (size_t)T * D * 4,  // h_in, out
       (size_t)E * D * 4,                 // router_tmp
       mma_part_bytes(), mma_cnt_bytes(),  // mma_part, mma_cnt
-      (size_t)moe_decode_sync_words(E, F, D) * 4,  // mk_sync
       64, 64, 64, 64, 64, 64,             // dmeta: counts, offsets, small, large, n_lists, large_tt
   };
   size_t total = 0;
@@ -318,7 +315,6 @@ int ensure_work(kc_ctx* ctx, Work& w, int T, int E, int K, int D, int F) {
   take((void**)&w.router_tmp);
   take((void**)&w.mma_part);
   take((void**)&w.mma_cnt);
-  take((void**)&w.mk_sync);
   take((void**)&w.dmeta.counts);
   take((void**)&w.dmeta.offsets);
   take((void**)&w.dmeta.small_list);
@@ -327,7 +323,6 @@ int ensure_work(kc_ctx* ctx, Work& w, int T, int E, int K, int D, int F) {
   take((void**)&w.dmeta.large_tt);
   w.dmeta_n = -1;
   CK(cudaMemsetAsync(w.mma_cnt, 0, mma_cnt_bytes(), ctx->stream));
-  CK(cudaMemsetAsync(w.mk_sync, 0, (size_t)moe_decode_sync_words(E, F, D) * 4, ctx->stream));
   return KC_OK;
 }
 int ensure_work(kc_ctx* ctx, int T, int E, int K, int D, int F) { return ensure_work(ctx, ctx->ws, T, E, K, D, F); }
@@ -431,6 +426,8 @@ bool pdl_enabled() {
   }();
   return on;
 }
+
+std::atomic<int64_t> g_kernel_launches{0};
 
 int num_sms() {
   // SM count per device, read once per device (several contexts on different
@@ -1041,8 +1038,7 @@ static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const f
 // defer_combine (one GPU, no shared expert): the combine may be left to the
 // caller (the model's next RMSNorm), which then reads W.y, W.meta.tok_slot,
 // W.ids and W.w before anything else touches the workspace, and out is not
-// written; *deferred says whether it was (the fused decode kernel always
-// combines into out).
+// written; *deferred says whether it was.
 static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const float* h, int n_tok, float* out,
                         int32_t* ids_out, float* w_out, bool defer_combine = false, bool* deferred = nullptr) {
   if (deferred) *deferred = false;
@@ -1052,47 +1048,6 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
   Work& W = ctx->ws;
   cudaStream_t st = ctx->stream;
   if (n_tok == 0) return KC_OK;
-  // Decode batches: the whole layer in one persistent launch. Not enabled:
-  // the kernel faulted the GPU at 3 tokens on the configs[2] shape for a
-  // cause not yet found, so it does not run until that is understood.
-  constexpr bool kFusedDecode = false;
-  if (kFusedDecode && !ctx->prof.on && !L.has_shared && L.first_expert == 0 && L.n_local == E &&
-      moe_decode_supported(n_tok, E, k, d, L.ff, L.t_gate, L.t_up, L.t_down) && ((uintptr_t)h & 15) == 0) {
-    MoeDecodeArgs ma{};
-    ma.router = router;
-    ma.E = E;
-    ma.k = k;
-    ma.d = d;
-    ma.ff = L.ff;
-    ma.norm_topk = L.norm_topk;
-    ma.weights_scale = L.weights_scale;
-    ma.gate = L.gate;
-    ma.up = L.up;
-    ma.down = L.down;
-    ma.mb_gate = L.mb_gate;
-    ma.mb_down = L.mb_down;
-    ma.t_gate = L.t_gate;
-    ma.t_down = L.t_down;
-    ma.h = h;
-    ma.n_tok = n_tok;
-    ma.out = out;
-    ma.ids = W.ids;
-    ma.w = W.w;
-    ma.logits = W.logits;
-    ma.xrec = W.xrec;
-    ma.g = W.g;
-    ma.u = W.u;
-    ma.arec = W.arec;
-    ma.y = W.y;
-    ma.sync = W.mk_sync;
-    ma.status = ctx->status;
-    if (launch_moe_decode(ma, st) == KC_OK) {
-      CKL();
-      if (ids_out) CK(cudaMemcpyAsync(ids_out, W.ids, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
-      if (w_out) CK(cudaMemcpyAsync(w_out, W.w, (size_t)n_tok * k * 4, cudaMemcpyDeviceToDevice, st));
-      return KC_OK;
-    }
-  }
   // 1. router logits and top-k (Transformer::route).
   {
     StageScope ss(ctx, KC_STAGE_ROUTER_LOGITS);
@@ -1845,6 +1800,8 @@ int kc_profile_enable(kc_ctx* ctx, int on) {
   ctx->prof.on = on != 0;
   return KC_OK;
 }
+
+int64_t kc_kernel_launches(void) { return kc::g_kernel_launches.load(std::memory_order_relaxed); }
 
 int kc_profile_read(kc_ctx* ctx, double* stage_ms, int64_t* stage_calls, int n_stages) {
   if (!ctx || n_stages < 0) return KC_ERR_ARG;

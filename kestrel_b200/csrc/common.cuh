@@ -267,6 +267,8 @@ __device__ __forceinline__ void pdl_enter() {
 }
 // KESTREL_PDL=0 launches them as ordinary stream-ordered kernels.
 bool pdl_enabled();
+// Every launch_k adds one (kc_kernel_launches reads it).
+extern std::atomic<int64_t> g_kernel_launches;
 
 // Kernel attributes such as cudaFuncAttributeMaxDynamicSharedMemorySize are
 // per device: a process that drives several GPUs (one context each) must set
@@ -312,6 +314,7 @@ inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 }  // namespace kc

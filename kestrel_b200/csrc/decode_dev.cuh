@@ -1,7 +1,7 @@
-// Device building blocks of the decode-sized dequant-dot (decode.cu) and of
-// the fused MoE decode kernel (moe_decode.cu): work-unit geometry constants,
-// shared-memory loads, the per-superblock integer kernels of the reference's
-// Q4_K / Q6_K / Q8_0 x Q8_K / Q8 dot products, and one unit's consumer loop.
+// Device building blocks of the decode-sized dequant-dot (decode.cu):
+// work-unit geometry constants, shared-memory loads, the per-superblock
+// integer kernels of the reference's Q4_K / Q6_K / Q8_0 x Q8_K / Q8 dot
+// products, and one unit's consumer loop.
 #pragma once
 
 #include "common.cuh"

@@ -77,6 +77,7 @@ void launch_q8k_quantize(const float* x, const int* row_map, int64_t n_rows, int
   int64_t warps = n_rows * (cols / 256);
   if (warps <= 0) return;
   q8k_quantize_kernel<<<ceil_div(warps, 8), 256, 0, st>>>(x, row_map, n_rows, cols, q, d, bsums);
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 void launch_q8_quantize(const float* x, const int* row_map, int64_t n_rows, int64_t cols, int8_t* q, float* d,
@@ -84,6 +85,7 @@ void launch_q8_quantize(const float* x, const int* row_map, int64_t n_rows, int6
   int64_t warps = n_rows * (cols / 32);
   if (warps <= 0) return;
   q8_quantize_kernel<<<ceil_div(warps, 8), 256, 0, st>>>(x, row_map, n_rows, cols, q, d, s16);
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 // ---------------------------------------------------------------------------
@@ -211,6 +213,7 @@ int launch_quantize(int t, const float* x, int64_t rows, int64_t cols, void* out
   else if (t == T_Q6_K) quantize_q6_k_kernel<<<grid, 128, 0, st>>>(x, nblocks, o);
   else if (t == T_Q8_0) quantize_q8_0_kernel<<<grid, 128, 0, st>>>(x, nblocks, o);
   else return KC_ERR_TYPE;
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
   return KC_OK;
 }
 
@@ -274,12 +277,14 @@ int launch_repack(int t, const void* src, int64_t n_mats, int64_t rows, int64_t 
   if (t == T_F32) {
     const int64_t rb = cols * 4, ds = round16(rb);
     repack_copy_rows_kernel<<<ceil_div(n_mats * rows * ds, 256), 256, 0, st>>>(s, n_mats * rows, rb, ds, d);
+    g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
     return KC_OK;
   }
   if (t != T_Q4_K && t != T_Q6_K && t != T_Q8_0) return KC_ERR_TYPE;
   if (cudaMemsetAsync(d, 0, n_mats * dev_matrix_bytes(t, rows, cols), st) != cudaSuccess) return KC_ERR_CUDA;
   const int64_t n = n_mats * rows * tiled_nsb(t, cols);
   repack_tiled_kernel<<<ceil_div(n, 128), 128, 0, st>>>(t, s, n_mats, rows, cols, d);
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
   return KC_OK;
 }
 
@@ -349,6 +354,7 @@ void launch_block_sums(int t, const void* w, int64_t rows, int64_t cols, const i
   if (n == 0) return;
   block_sums_kernel<<<ceil_div(n, 128), 128, 0, st>>>(t, static_cast<const uint8_t*>(w), rows, cols, q, bsums,
                                                       n_act, out);
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 }  // namespace kc

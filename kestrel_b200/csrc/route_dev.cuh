@@ -1,6 +1,5 @@
-// Device pieces of the routing front shared by router.cu and the fused MoE
-// decode kernel (moe_decode.cu): one output lane step of the router product
-// and one token's softmax / top-k.
+// Device pieces of the routing front (router.cu): one output lane step of the
+// router product and one token's softmax / top-k.
 #pragma once
 
 #include "common.cuh"

@@ -50,6 +50,7 @@ SIGNATURES = {
     "kc_quantize_dev": (I, [P, I, P, I64, I64, P]),
     "kc_profile_enable": (I, [P, I]),
     "kc_profile_read": (I, [P, P, P, I]),
+    "kc_kernel_launches": (I64, []),
     "kc_route_noalloc": (I, [P, I, I, P, I, I, I, F, P, P, P]),
     "kc_upload_shared_expert": (I, [P, I, I, I, I, P, I, P, I, P, P, I]),
     "kc_ep_unique_id": (I, [ctypes.c_char_p]),
@@ -354,3 +355,9 @@ def ep_unique_id() -> bytes:
     if rc != 0:
         raise KestrelCudaError(rc, "ncclGetUniqueId failed")
     return buf.raw
+
+
+def kernel_launches() -> int:
+    """CUDA kernels this library has launched in the process so far
+    (kc_kernel_launches)."""
+    return int(lib().kc_kernel_launches())

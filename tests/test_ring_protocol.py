@@ -1,16 +1,16 @@
-"""CPU model of the stage ring shared by decode_kernel (decode.cu) and the
-fused decode kernel (moe_decode.cu): one producer issues stage ids in
-(group, segment, unit) order into a ring of n_stages slots; consumer warps
-wait on the slot's `full` mbarrier with the lap's phase parity, after waiting
-on its `empty` mbarrier for the previous lap's release, and release it with
-DARR arrivals in total.
+"""CPU model of decode_kernel's stage ring (decode.cu): one producer issues
+stage ids in (group, segment, unit) order into a ring of n_stages slots;
+consumer warps wait on the slot's `full` mbarrier with the lap's phase
+parity, after waiting on its `empty` mbarrier for the previous lap's
+release, and release it with DARR arrivals in total.
 
 An mbarrier's parity only tells two consecutive phases apart, so a warp may
 never wait on a slot two laps ahead of its last release. The model runs the
-kernels' stage formulas under random interleavings and checks that every
+kernel's stage formulas under random interleavings and checks that every
 wait sees the lap it means and that no phase gets more arrivals than its
-count -- including the fused kernel's case of a partial gate/up group followed
-by down groups, which needs the consumer barrier between the phases.
+count. A multi-phase ring (one unit sequence, then another, in the same
+ring) needs a consumer barrier between the phases when the first one ends in
+a partial group; the model shows it.
 """
 import random
 
@@ -127,10 +127,10 @@ def test_single_phase_ring(units):
         run_ring([(units, 4)], 14, seed, consumer_barrier=False)
 
 
-def test_fused_phases_need_the_consumer_barrier():
-    """7 gate/up units (a partial group) then 11 down units, the unit counts of
-    the fused kernel's CTAs at 3 tokens on configs[1]: without the barrier a
-    warp idle in the partial group reaches a slot two laps ahead."""
+def test_two_phases_need_the_consumer_barrier():
+    """7 units (a partial group) then 11 of another geometry in one ring:
+    without the barrier a warp idle in the partial group reaches a slot two
+    laps ahead."""
     with pytest.raises(AssertionError, match="aliased|more arrivals"):
         for seed in range(200):
             run_ring([(7, 4), (11, 2)], 14, seed, consumer_barrier=False)
@@ -138,9 +138,10 @@ def test_fused_phases_need_the_consumer_barrier():
         run_ring([(7, 4), (11, 2)], 14, seed, consumer_barrier=True)
 
 
-def test_fused_phases_random_shapes():
+def test_two_phases_random_shapes():
     rnd = random.Random(0)
     for trial in range(150):
         n_gu, n_dn = rnd.randint(0, 26), rnd.randint(0, 26)
         nsg, nsd = rnd.choice([(4, 2), (8, 3), (1, 1), (2, 6), (16, 8)])
         run_ring([(n_gu, nsg), (n_dn, nsd)], rnd.choice([9, 14, 19, 27]), trial, consumer_barrier=True)
+
