@@ -252,25 +252,60 @@ def make_layers(ctx, torch, n_layers, seed=0, block=None):
     return host0
 
 
-def cpu_oracle_rate(layer_w, B, budget_s, threads, seed=5):
-    """Tokens/s of the oracle's moe_ffn on one configs[1] layer, B tokens per
-    call, repeated until `budget_s` of CPU time has elapsed."""
+def physical_cores() -> int:
+    """Physical cores of the host (the reference sizes its thread pool by
+    physical cores); logical CPUs if psutil cannot tell."""
+    try:
+        import psutil
+        n = psutil.cpu_count(logical=False)
+        if n:
+            return int(n)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_oracle_rate(layer_w, B, budget_s, threads, seed=5, min_calls=2):
+    """The oracle's moe_ffn (C++ restatement of Kestrel's AVX2 path) on one
+    layer, B tokens per call, `threads` threads, repeated until `budget_s`
+    seconds have elapsed. Returns (tokens/s, calls, seconds, weight GB/s),
+    the GB/s by the GPU arm's algorithmic byte count."""
     import oracle
     from kestrel_b200 import ggml as G
     oracle.set_threads(threads)
     rng = np.random.default_rng(seed)
-    calls, tokens, t0 = 0, 0, time.perf_counter()
+    calls, tokens, nbytes, t0 = 0, 0, 0, time.perf_counter()
     while True:
         h = rng.standard_normal((B, CFG["d"]), dtype=np.float32)
         if CFG["zipf"]:
             h[:, 0] = 1.0
-        oracle.moe_ffn(h, layer_w["router"], CFG["k"], G.Q4_K, layer_w["gate"], G.Q4_K, layer_w["up"], G.Q6_K,
-                       layer_w["down"], CFG["ff"])
+        _, ids, _ = oracle.moe_ffn(h, layer_w["router"], CFG["k"], G.Q4_K, layer_w["gate"], G.Q4_K, layer_w["up"],
+                                   G.Q6_K, layer_w["down"], CFG["ff"])
+        nbytes += algorithmic_bytes(ids, B)["total"]
         calls += 1
         tokens += B
         el = time.perf_counter() - t0
-        if el >= budget_s and calls >= 2:
-            return tokens / el, calls, el
+        if el >= budget_s and calls >= min_calls:
+            return tokens / el, calls, el, nbytes / el / 1e9
+
+
+# The reference's published CPU figure for the same weight format: a Q4_K
+# gemv at 9.19 GB/s on 4 cores (benchmarks/README.md of the reference).
+CPU_ANCHOR = "reference's published Q4_K gemv: 9.19 GB/s on 4 cores"
+
+
+def cpu_baseline_both(layer_w, B, budget_s):
+    """The D4 baseline: all physical cores and one thread, each with its
+    weight GB/s (same byte formula as the GPU arm)."""
+    phys = physical_cores()
+    rate, calls, el, gbs = cpu_oracle_rate(layer_w, B, budget_s, phys)
+    r1, c1, e1, g1 = cpu_oracle_rate(layer_w, B, budget_s / 2, 1, min_calls=1)
+    return {"value": rate, "unit": "tokens/s", "cores": phys, "kind": "port", "gbs": gbs,
+            "one_thread": {"value": r1, "unit": "tokens/s", "gbs": g1, "sample": f"{c1} calls ({e1:.1f} s)"},
+            "logical_cpus": os.cpu_count(), "anchor": CPU_ANCHOR,
+            "sample": f"{calls} calls of layer 0 at B={B} ({el:.1f} s) on {phys} physical cores, oracle "
+                      f"restatement of Kestrel's AVX2 path; weights numpy-quantized from other seeds than the "
+                      f"GPU arm's (same shapes and rules)"}
 
 
 def host_layer_numpy(seed=0):
@@ -309,16 +344,16 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
+    threads = physical_cores()
     w = host_layer_numpy()
     B = args.batch
-    rate, calls, el = None, 0, 0.0
     for _ in range(args.warmup):
         cpu_oracle_rate(w, B, 0.0, threads)
-    times = []
+    times, gbs = [], []
     for i in range(args.steps):
-        r, c, e = cpu_oracle_rate(w, B, 0.0, threads, seed=100 + i)
+        r, c, e, g = cpu_oracle_rate(w, B, 0.0, threads, seed=100 + i)
         times.append(e / c)
+        gbs.append(g)
     ms = 1e3 * sum(times) / len(times)
     value = B / (ms / 1e3)
     line = {
@@ -329,8 +364,10 @@ def run_reference(args):
         "config": {"workload": CFG["name"], "batch_tokens": B, "d_model": CFG["d"], "experts": CFG["E"],
                    "top_k": CFG["k"], "expert_ff": CFG["ff"], "quant": "Q4_K gate/up + Q6_K down"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} calls of one layer at B={B} (oracle restatement of "
-                                   f"Kestrel's AVX2 path; Rust reference not buildable here)"},
+                         "gbs": sum(gbs) / len(gbs), "logical_cpus": os.cpu_count(), "anchor": CPU_ANCHOR,
+                         "sample": f"{args.steps} calls of one layer at B={B} on {threads} physical cores "
+                                   f"(oracle restatement of Kestrel's AVX2 path; Rust reference not buildable "
+                                   f"here)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -515,11 +552,7 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        rate, calls, el = cpu_oracle_rate(host0, B, args.cpu_seconds, threads)
-        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"{calls} calls of layer 0 at B={B} ({el:.1f} s), oracle restatement of Kestrel's "
-                         f"AVX2 path on all host threads"}
+        cpu = cpu_baseline_both(host0, B, args.cpu_seconds)
 
     if rank == 0:
         line = {

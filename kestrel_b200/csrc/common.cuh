@@ -167,6 +167,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
   return true;
 }
+// Release counters of a stage ring (shared memory): each consumer warp adds
+// its share of the DARR releases of a stage; lap L of a slot may be consumed
+// once the slot's counter reaches L * DARR. A monotonic count cannot alias an
+// older lap the way a phase parity can when consumers run at very different
+// speeds (the previous lap of a slot may not even be issued yet when a fast
+// consumer arrives: producer lanes issue a segment's stages independently).
+__device__ __forceinline__ void count_add(int* c, int v) {
+  asm volatile("red.shared.add.s32 [%0], %1;" ::"r"(smem_u32(c)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int count_read(const int* c) {
+  int v;
+  asm volatile("ld.volatile.shared.s32 %0, [%1];" : "=r"(v) : "r"(smem_u32(c)) : "memory");
+  return v;
+}
+// Bounded wait until *c >= target; records KC_ERR_TIMEOUT with the site tag
+// and returns false after kWaitLimitNs.
+__device__ __forceinline__ bool count_wait(const int* c, int target, int* status, int site) {
+  if (count_read(c) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  while (count_read(c) < target) {
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      report(status, KC_ERR_TIMEOUT | (site << 8));
+      return false;
+    }
+  }
+  return true;
+}
+
 // Site tags of the bounded waits.
 enum : int {
   W_DEC_EMPTY = 1, W_DEC_FULL = 2, W_DEC_DRAIN = 3, W_MMA_RAW_EMPTY = 4, W_MMA_OP_EMPTY_P = 5, W_MMA_DRAIN = 6,

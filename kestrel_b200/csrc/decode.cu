@@ -183,6 +183,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
   else pdl_enter();
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[DMAX_STAGES], empty[DMAX_STAGES];
+  __shared__ int rel[DMAX_STAGES];  // release counts per slot (count_wait)
   __shared__ int list_s[DMAX_E], off_s[DMAX_E + 1];
   constexpr int R = TypeR<T>::R;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -197,6 +198,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
     for (int s = 0; s < n_stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], DARR);
+      rel[s] = 0;
     }
     fence_mbar_init();
   }
@@ -344,11 +346,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
     // Stage records: K-quant [slot][superblock of the pair], Q8 [chunk][slot].
     constexpr int SR = T != T_Q8_0 ? 2 * R : R, SBS = T != T_Q8_0 ? R : DMAXS * R;
     if (tpr == 2)
-      run_unit_ns<T, 2, SR, SBS>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+      run_unit_ns<T, 2, SR, SBS>(um.ns, a, g, ring, full, empty, rel, n_stages, sid0, wg, lane, row, out, r_out, ok);
     else if (tpr == 4)
-      run_unit_ns<T, 4, SR, SBS>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+      run_unit_ns<T, 4, SR, SBS>(um.ns, a, g, ring, full, empty, rel, n_stages, sid0, wg, lane, row, out, r_out, ok);
     else
-      run_unit_ns<T, 8, SR, SBS>(um.ns, a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+      run_unit_ns<T, 8, SR, SBS>(um.ns, a, g, ring, full, empty, rel, n_stages, sid0, wg, lane, row, out, r_out, ok);
   }
 }
 

@@ -260,7 +260,8 @@ static_assert(DC == 2 * DW && DW % 4 == 0, "warp layout");
 // (defaults: superblock-major, DMAXS slots per superblock).
 template <int T, int TPR, int NS, class Args, int SR = TypeR<T>::R, int SBS = DMAXS * TypeR<T>::R>
 __device__ __forceinline__ void run_unit(const Args& a, const DecodeGeom& g, const uint8_t* ring,
-                                         uint64_t* full, uint64_t* empty, int n_stages, int sid0, int wg, int lane,
+                                         uint64_t* full, uint64_t* empty, int* rel, int n_stages, int sid0, int wg,
+                                         int lane,
                                          int row, float* out, int r_out, bool& ok) {
   constexpr int R = TypeR<T>::R;
   constexpr int LPT = 8 / TPR;
@@ -280,8 +281,11 @@ __device__ __forceinline__ void run_unit(const Args& a, const DecodeGeom& g, con
     // A slot is used lap after lap by different warps, and bulk copies may land
     // out of order: before waiting on this lap's copy, wait until the slot's
     // previous lap has been released. Only then is the copy barrier known to be
-    // in this lap's phase, so its parity test cannot alias an older phase.
-    if (ok && sid >= n_stages && !mbar_wait(&empty[st], ph ^ 1u, a.status, W_DEC_PREV)) ok = false;
+    // in this lap's phase, so its parity test cannot alias an older phase. The
+    // release is counted (rel), not tested by parity: a fast warp may arrive
+    // here while the previous lap is not yet issued and the lap before it not
+    // yet released, which a parity test would mistake for the release it wants.
+    if (ok && sid >= n_stages && !count_wait(&rel[st], (sid / n_stages) * DARR, a.status, W_DEC_PREV)) ok = false;
     if (ok && !mbar_wait(&full[st], ph, a.status, W_DEC_FULL)) ok = false;
     if (ok) {
       const uint32_t sp = smem_u32(ring) + (uint32_t)(st * g.stage_bytes);
@@ -296,7 +300,10 @@ __device__ __forceinline__ void run_unit(const Args& a, const DecodeGeom& g, con
     }
     __syncwarp();
     // TPR warps hold the unit; each releases DARR / TPR of the slot's DARR arrivals.
-    if (lane == 0) mbar_arrive_cnt(&empty[st], DARR / TPR);
+    if (lane == 0) {
+      mbar_arrive_cnt(&empty[st], DARR / TPR);  // for the producer
+      count_add(&rel[st], DARR / TPR);          // for the next lap's consumers
+    }
     sid += wg;
     st += wg;
     if (st >= n_stages) {
@@ -321,11 +328,11 @@ __device__ __forceinline__ void run_unit(const Args& a, const DecodeGeom& g, con
 
 template <int T, int TPR, int SR = TypeR<T>::R, int SBS = DMAXS * TypeR<T>::R, class Args>
 __device__ __forceinline__ void run_unit_ns(int ns, const Args& a, const DecodeGeom& g, const uint8_t* ring,
-                                            uint64_t* full, uint64_t* empty, int n_stages, int sid0, int wg,
+                                            uint64_t* full, uint64_t* empty, int* rel, int n_stages, int sid0, int wg,
                                             int lane, int row, float* out, int r_out, bool& ok) {
-  if (ns == 1) run_unit<T, TPR, 1, Args, SR, SBS>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
-  else if (ns == 2) run_unit<T, TPR, 2, Args, SR, SBS>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
-  else run_unit<T, TPR, 3, Args, SR, SBS>(a, g, ring, full, empty, n_stages, sid0, wg, lane, row, out, r_out, ok);
+  if (ns == 1) run_unit<T, TPR, 1, Args, SR, SBS>(a, g, ring, full, empty, rel, n_stages, sid0, wg, lane, row, out, r_out, ok);
+  else if (ns == 2) run_unit<T, TPR, 2, Args, SR, SBS>(a, g, ring, full, empty, rel, n_stages, sid0, wg, lane, row, out, r_out, ok);
+  else run_unit<T, TPR, 3, Args, SR, SBS>(a, g, ring, full, empty, rel, n_stages, sid0, wg, lane, row, out, r_out, ok);
 }
 
 }  // namespace kc

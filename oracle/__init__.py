@@ -53,6 +53,7 @@ def lib() -> ctypes.CDLL:
             "ko_moe_ffn": (I, [P, I64, I64, P, I, I, I, F, I, P, I, P, I, P, I64, P, P, P,
                                I, P, I, P, I, P, I64, P]),
             "ko_argmax": (I, [P, I64]),
+            "ko_expert_ffn": (I, [I, P, I, P, I, P, I64, I64, P, I64, P]),
             "ko_model_new": (P, [I, I, I, I, I, I, I, I, F, F, I, I, I, I, F]),
             "ko_model_free": (None, [P]),
             "ko_model_set": (I, [P, I, I, I, P, I64, I64]),
@@ -226,6 +227,19 @@ def moe_ffn(h, router_w, k: int, t_gate: int, gate, t_up: int, up, t_down: int, 
     if rc:
         raise ValueError("oracle moe_ffn rejected its arguments")
     return out, ids, w
+
+
+def expert_ffn(t_gate: int, gate_e, t_up: int, up_e, t_down: int, down_e, d: int, ff: int, xs) -> np.ndarray:
+    """One expert of moe_ffn on its rows xs [n, d] (transformer.rs:551-563):
+    gate/up products, SwiGLU, down product -> [n, d]. gate_e / up_e / down_e
+    are that expert's GGUF bytes ([ff] rows of d, [d] rows of ff)."""
+    xs = _f32(xs).reshape(-1, d)
+    y = np.empty((xs.shape[0], d), np.float32)
+    g, u, dn = _u8(gate_e), _u8(up_e), _u8(down_e)
+    rc = lib().ko_expert_ffn(t_gate, _p(g), t_up, _p(u), t_down, _p(dn), d, ff, _p(xs), xs.shape[0], _p(y))
+    if rc:
+        raise ValueError("oracle expert_ffn rejected the shapes")
+    return y
 
 
 def argmax(logits) -> int:

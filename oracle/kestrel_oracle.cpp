@@ -21,11 +21,13 @@
 
 #include <algorithm>
 #include <atomic>
+#include <condition_variable>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <functional>
 #include <map>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -77,8 +79,71 @@ inline float h2f(const uint8_t* p) {
 // ---------------------------------------------------------------------------
 // Thread pool: tiles of output rows are independent (each output element is
 // written by exactly one tile), so threading never changes results
-// (quant.rs:244-257, 264-278 run the same tiles on rayon).
+// (quant.rs:244-257, 264-278 run the same tiles on rayon). Like rayon's pool
+// the workers persist between parallel regions (a region costs a wake-up,
+// not thread creation), so the timed CPU baseline is not dominated by
+// spawning threads for each of a layer's small products.
 int g_threads = 1;
+
+class Pool {
+ public:
+  ~Pool() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
+  }
+  // Runs fn(0..n-1) on the caller and nt - 1 workers (one region at a time).
+  void run(int nt, int64_t n, const std::function<void(int64_t)>& fn) {
+    std::lock_guard<std::mutex> region(run_mu_);
+    while ((int)workers_.size() < nt - 1) {
+      const int idx = (int)workers_.size();
+      workers_.emplace_back([this, idx] { loop(idx); });
+    }
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      fn_ = &fn;
+      n_ = n;
+      next_.store(0);
+      want_ = nt - 1;
+      pending_ = nt - 1;
+      ++gen_;
+    }
+    cv_.notify_all();
+    for (int64_t i; (i = next_.fetch_add(1)) < n;) fn(i);
+    std::unique_lock<std::mutex> lk(mu_);
+    done_.wait(lk, [&] { return pending_ == 0; });
+  }
+
+ private:
+  void loop(int idx) {
+    uint64_t seen = 0;
+    std::unique_lock<std::mutex> lk(mu_);
+    for (;;) {
+      cv_.wait(lk, [&] { return stop_ || gen_ != seen; });
+      if (stop_) return;
+      seen = gen_;
+      if (idx >= want_) continue;
+      const std::function<void(int64_t)>* fn = fn_;
+      const int64_t n = n_;
+      lk.unlock();
+      for (int64_t i; (i = next_.fetch_add(1)) < n;) (*fn)(i);
+      lk.lock();
+      if (--pending_ == 0) done_.notify_one();
+    }
+  }
+  std::mutex run_mu_, mu_;
+  std::condition_variable cv_, done_;
+  std::vector<std::thread> workers_;
+  const std::function<void(int64_t)>* fn_ = nullptr;
+  int64_t n_ = 0;
+  std::atomic<int64_t> next_{0};
+  int want_ = 0, pending_ = 0;
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+};
 
 void parallel_for(int64_t n, const std::function<void(int64_t)>& fn) {
   int nt = (int)std::min<int64_t>(g_threads, n);
@@ -86,14 +151,8 @@ void parallel_for(int64_t n, const std::function<void(int64_t)>& fn) {
     for (int64_t i = 0; i < n; ++i) fn(i);
     return;
   }
-  std::atomic<int64_t> next{0};
-  std::vector<std::thread> ts;
-  ts.reserve(nt);
-  for (int t = 0; t < nt; ++t)
-    ts.emplace_back([&] {
-      for (int64_t i; (i = next.fetch_add(1)) < n;) fn(i);
-    });
-  for (auto& t : ts) t.join();
+  static Pool pool;
+  pool.run(nt, n, fn);
 }
 
 // scale_min_k4 (quant.rs:54-60, qdot.rs:66-72, avx2.rs:78-84).
@@ -1260,6 +1319,20 @@ int ko_moe_ffn(const float* h, int64_t n_tok, int64_t d, const float* router_w, 
     }
   }
   return 0;
+}
+
+// One expert of Transformer::moe_ffn (transformer.rs:551-563): gate and up
+// products of its n rows xs [n, d], g / (1 + exp(-g)) * u, then the down
+// product -> y [n, d]. Matrices are one expert's rows. Returns 0, or -1 on
+// bad shapes.
+int ko_expert_ffn(int t_gate, const uint8_t* gate, int t_up, const uint8_t* up, int t_down, const uint8_t* down,
+                  int64_t d, int64_t ff, const float* xs, int64_t n, float* y) {
+  if (bytes_for(t_gate, d) < 0 || bytes_for(t_up, d) < 0 || bytes_for(t_down, ff) < 0) return -1;
+  std::vector<float> g(n * ff), u(n * ff);
+  if (int rc = matmul(t_gate, gate, ff, d, xs, n, g.data(), g_exact)) return rc;
+  if (int rc = matmul(t_up, up, ff, d, xs, n, u.data(), g_exact)) return rc;
+  for (int64_t i = 0; i < n * ff; ++i) g[i] = silu_mul(g[i], u[i]);
+  return matmul(t_down, down, d, ff, g.data(), n, y, g_exact);
 }
 
 // ---- model (Transformer) ----------------------------------------------------

@@ -1,16 +1,25 @@
-"""CPU model of decode_kernel's stage ring (decode.cu): one producer issues
-stage ids in (group, segment, unit) order into a ring of n_stages slots;
-consumer warps wait on the slot's `full` mbarrier with the lap's phase
-parity, after waiting on its `empty` mbarrier for the previous lap's
-release, and release it with DARR arrivals in total.
+"""CPU model of decode_kernel's stage ring (csrc/decode.cu, decode_dev.cuh).
 
-An mbarrier's parity only tells two consecutive phases apart, so a warp may
-never wait on a slot two laps ahead of its last release. The model runs the
-kernel's stage formulas under random interleavings and checks that every
-wait sees the lap it means and that no phase gets more arrivals than its
-count. A multi-phase ring (one unit sequence, then another, in the same
-ring) needs a consumer barrier between the phases when the first one ends in
-a partial group; the model shows it.
+The producer side is the kernel's: a CTA's units are taken DW at a time (a
+group); for each segment of the group, producer lane w issues unit w's stage
+(waiting on the slot's `empty` mbarrier for the previous lap's release), the
+lanes independently of one another, and all lanes meet at a named barrier
+before the next segment. Consumer warps (TPR per unit) wait for the slot's
+previous lap to be released, then on the slot's `full` mbarrier with the
+lap's phase parity, and release it with DARR arrivals in total.
+
+An mbarrier's parity only tells two consecutive phases apart. A fast consumer
+can reach lap L of a slot while lap L-1 is not yet issued -- its producer
+lane is still waiting for a slow unit to release lap L-2 -- so a parity test
+of the release barrier would take lap L-2's pending phase for the release it
+wants, read stale data and over-release the slot. The kernel therefore
+counts releases per slot (a monotonic shared-memory counter) for the
+consumers' previous-lap wait; the producer keeps the parity wait, which
+cannot alias (it issues lap L only after lap L-1, and issued lap L-1 only
+after lap L-2 was released). The model runs random interleavings, some with
+a few consumer warps scheduled a hundred times less often, and checks that
+every wait sees the lap it means and that no phase gets more arrivals than
+its count; with a parity previous-lap wait it finds the aliasing.
 """
 import random
 
@@ -51,97 +60,104 @@ class Bar:
         return (self.phase & 1) != parity
 
 
-def run_ring(phases, n_stages, seed, consumer_barrier):
-    """phases: [(units, segments per unit)] processed in order (gate/up, down)."""
+def run_ring(nu, nseg, n_stages, seed, counted=True, slow=()):
+    """One CTA with nu units of nseg segments each in an n_stages ring."""
     rnd = random.Random(seed)
     full = [Bar(1) for _ in range(n_stages)]
     empty = [Bar(DARR) for _ in range(n_stages)]
+    rel = [0] * n_stages  # release counts (count_add / count_wait)
     inflight = []
-    bases, b = [], 0
-    for nu, nseg in phases:
-        bases.append(b)
-        b += nu * nseg
+    n_groups = (nu + DW - 1) // DW
+    met = {}
 
-    def producer():
-        for (nu, nseg), base in zip(phases, bases):
-            for gi in range((nu + DW - 1) // DW):
-                wg = min(DW, nu - gi * DW)
-                for seg in range(nseg):
-                    for w in range(wg):
-                        sid = base + gi * nseg * DW + seg * wg + w
-                        st, ph = sid % n_stages, (sid // n_stages) & 1
-                        if sid >= n_stages:
-                            while not empty[st].try_wait(ph ^ 1):
-                                yield
-                        assert full[st].phase == sid // n_stages, "producer reuses a slot early"
-                        full[st].expect_tx(16)
-                        inflight.append(full[st])
-                    yield
-
-    met = [0]
-
-    def consumer(c):
-        for pi, ((nu, nseg), base) in enumerate(zip(phases, bases)):
-            if pi > 0 and consumer_barrier and phases[pi - 1][0] % DW and nu > 0:
-                met[0] += 1
-                while met[0] < NC * pi:
-                    yield
-            for gi in range((nu + DW - 1) // DW):
-                wg = min(DW, nu - gi * DW)
-                tpr = tpr_of(wg)
-                ul = c // tpr
-                if ul >= wg:
-                    continue
-                sid = base + gi * nseg * DW + ul
-                for _ in range(nseg):
+    def lane(w):
+        for gi in range(n_groups):
+            wg = min(DW, nu - gi * DW)
+            for seg in range(nseg):
+                if w < wg:
+                    sid = gi * nseg * DW + seg * wg + w
                     st, ph = sid % n_stages, (sid // n_stages) & 1
                     if sid >= n_stages:
                         while not empty[st].try_wait(ph ^ 1):
                             yield
-                        assert empty[st].phase == sid // n_stages, "previous-lap wait aliased"
-                    while not full[st].try_wait(ph):
-                        yield
-                    assert full[st].phase == sid // n_stages + 1, "full wait aliased"
+                    assert full[st].phase == sid // n_stages, "producer reuses a slot early"
+                    full[st].expect_tx(16)
+                    inflight.append(full[st])
+                met[(gi, seg)] = met.get((gi, seg), 0) + 1
+                while met[(gi, seg)] < DW:  # producer_sync (named barrier)
                     yield
-                    empty[st].arrive(DARR // tpr)
-                    sid += wg
 
-    alive = [producer()] + [consumer(c) for c in range(NC)]
+    def consumer(c):
+        for gi in range(n_groups):
+            wg = min(DW, nu - gi * DW)
+            tpr = tpr_of(wg)
+            ul = c // tpr
+            if ul >= wg:
+                continue
+            sid = gi * nseg * DW + ul
+            for _ in range(nseg):
+                st, ph = sid % n_stages, (sid // n_stages) & 1
+                if sid >= n_stages:
+                    if counted:
+                        while rel[st] < (sid // n_stages) * DARR:
+                            yield
+                    else:
+                        while not empty[st].try_wait(ph ^ 1):
+                            yield
+                    assert empty[st].phase == sid // n_stages, "previous-lap wait aliased"
+                while not full[st].try_wait(ph):
+                    yield
+                assert full[st].phase == sid // n_stages + 1, "full wait aliased"
+                yield
+                empty[st].arrive(DARR // tpr)
+                rel[st] += DARR // tpr
+                sid += wg
+
+    gens = {("p", w): lane(w) for w in range(DW)}
+    for c in range(NC):
+        gens[c] = consumer(c)
     steps = 0
-    while alive:
+    while gens:
         steps += 1
-        assert steps < 2_000_000, "no progress"
+        assert steps < 5_000_000, "no progress"
         if inflight and rnd.random() < 0.5:
             inflight.pop(rnd.randrange(len(inflight))).complete_tx(16)
-        g = rnd.choice(alive)
+        keys = list(gens)
+        key = rnd.choices(keys, weights=[0.01 if k in slow else 1.0 for k in keys])[0]
         try:
-            next(g)
+            next(gens[key])
         except StopIteration:
-            alive.remove(g)
+            del gens[key]
 
 
-@pytest.mark.parametrize("units", [9, 17, 25, 33, 8, 3])
-def test_single_phase_ring(units):
-    """decode_kernel: groups of one geometry, a partial group only at the end."""
-    for seed in range(40):
-        run_ring([(units, 4)], 14, seed, consumer_barrier=False)
+# Ring geometries of the shipped kernel: Q4_K 19 stages x 4 segments (d=2048),
+# Q6_K 14 x 2 (ff=768), and tighter rings.
+GEOMS = [(4, 19), (2, 14), (4, 14), (2, 9)]
 
 
-def test_two_phases_need_the_consumer_barrier():
-    """7 units (a partial group) then 11 of another geometry in one ring:
-    without the barrier a warp idle in the partial group reaches a slot two
-    laps ahead."""
+@pytest.mark.parametrize("units", [3, 8, 9, 17, 25, 33, 40])
+def test_ring_even_speeds(units):
+    for seed in range(20):
+        nseg, ns = GEOMS[seed % len(GEOMS)]
+        run_ring(units, nseg, ns, seed)
+
+
+def test_ring_with_slow_warps():
+    """A few consumer warps much slower than the rest (an expert with more
+    rows, a warp held up elsewhere): the counted previous-lap wait holds."""
+    for trial in range(200):
+        rnd = random.Random(trial)
+        nseg, ns = rnd.choice(GEOMS)
+        slow = set(rnd.sample(range(NC), rnd.randint(1, 3)))
+        run_ring(rnd.choice([16, 17, 24, 25, 32, 33, 40]), nseg, ns, trial, counted=True, slow=slow)
+
+
+def test_parity_previous_lap_wait_aliases():
+    """The same schedules with a parity test for the previous lap's release
+    (the kernel's earlier form) alias: a fast warp passes two laps early."""
     with pytest.raises(AssertionError, match="aliased|more arrivals"):
-        for seed in range(200):
-            run_ring([(7, 4), (11, 2)], 14, seed, consumer_barrier=False)
-    for seed in range(200):
-        run_ring([(7, 4), (11, 2)], 14, seed, consumer_barrier=True)
-
-
-def test_two_phases_random_shapes():
-    rnd = random.Random(0)
-    for trial in range(150):
-        n_gu, n_dn = rnd.randint(0, 26), rnd.randint(0, 26)
-        nsg, nsd = rnd.choice([(4, 2), (8, 3), (1, 1), (2, 6), (16, 8)])
-        run_ring([(n_gu, nsg), (n_dn, nsd)], rnd.choice([9, 14, 19, 27]), trial, consumer_barrier=True)
-
+        for trial in range(200):
+            rnd = random.Random(trial)
+            nseg, ns = rnd.choice(GEOMS)
+            slow = set(rnd.sample(range(NC), rnd.randint(1, 3)))
+            run_ring(rnd.choice([16, 17, 24, 25, 32, 33, 40]), nseg, ns, trial, counted=False, slow=slow)
