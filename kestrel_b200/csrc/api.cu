@@ -334,7 +334,11 @@ int check_status(kc_ctx* ctx) {
   CK(cudaStreamSynchronize(ctx->stream));
   const int st = *ctx->status_host;
   if (st != 0) {
-    CK(cudaMemset(ctx->status, 0, sizeof(int)));
+    // Cleared on the context's stream (non-blocking: a legacy-stream memset
+    // would not be ordered before the next call's kernels, whose bounded
+    // waits read the word and return early on KC_ERR_STATE).
+    CK(cudaMemsetAsync(ctx->status, 0, sizeof(int), ctx->stream));
+    CK(cudaStreamSynchronize(ctx->stream));
     static const char* sites[] = {"unknown", "decode producer (empty stage)", "decode consumer (full stage)",
                                   "decode drain", "tcgen05 producer (raw stage)", "tcgen05 producer (operand stage)",
                                   "tcgen05 producer drain", "tcgen05 MMA issuer (operand stage)",
@@ -343,8 +347,9 @@ int check_status(kc_ctx* ctx) {
                                   "router logits (bulk copy)", "tcgen05 MMA issuer drain",
                                   "decode consumer (previous lap of a stage)",
                                   "expert-parallel peer exchange (another rank did not publish)",
-                                  "fused MoE decode grid barrier", "fused MoE decode (SwiGLU records of an expert)",
-                                  "fused MoE decode router rows (bulk copy)"};
+                                  "expert-parallel exchange (the ranks chose different paths, peer memory "
+                                  "and NCCL, in one call: every rank must be on the same side of the "
+                                  "kc_ep_reserve capacity)"};
     const int site = st >> 8;
     return fail(ctx, st & 0xFF, "a kernel's bounded wait expired (status %d) at: %s", st & 0xFF,
                 site >= 0 && site < (int)(sizeof(sites) / sizeof(sites[0])) ? sites[site] : "unknown");
@@ -892,6 +897,10 @@ static int ep_pipeline_p2p(kc_ctx* ctx, const Layer& L, const float* router, con
   }
   const int R = G * S.p2p.T;  // owner-side rows: every source's capacity
   RC(ep_grow_owner(ctx, R, 1, k, d));
+  Work& WO = ctx->ws_ep;
+  RC(ensure_work(ctx, WO, R, epr, k, d, ff));
+  // Every host-side step that can fail comes before the sequence number
+  // moves on, so that the ranks' sequence numbers stay equal.
   ++S.p2p.seq;
   const EpP2PArgs pa = ep_p2p_args(S, ctx->status);
   {
@@ -902,8 +911,6 @@ static int ep_pipeline_p2p(kc_ctx* ctx, const Layer& L, const float* router, con
     launch_ep_p2p_local_ids(pa, L.first_expert, epr, B.ids_loc, B.w_loc, st);
     CKL();
   }
-  Work& WO = ctx->ws_ep;
-  RC(ensure_work(ctx, WO, R, epr, k, d, ff));
   Layer LL = L;
   LL.n_expert = epr;
   RC(experts_forward(ctx, WO, LL, epr, 0, reinterpret_cast<const float*>(S.p2p.arena), R, B.ids_loc, B.w_loc, k));
@@ -947,6 +954,22 @@ static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const f
   cudaStream_t st = ctx->stream;
   if (S.p2p.ready && n_tok <= S.p2p.T && d == S.p2p.d && k == S.p2p.k)
     return ep_pipeline_p2p(ctx, L, router, h, n_tok, out, ids_out, w_out);
+  if (S.p2p.ready) {
+    // The peer arenas are mapped, so another rank may have taken the peer
+    // path in this call (its tokens within the reserved capacity while this
+    // rank's are not). An NCCL call would then wait for a rank that never
+    // makes it. So announce this rank's path on every rank's line, wait for
+    // every rank's announcement (bounded) and compare, and make no NCCL call
+    // unless all ranks took NCCL; otherwise the call fails with KC_ERR_STATE
+    // on every rank (the peer-path ranks stop waiting when they see it).
+    ++S.p2p.seq;
+    EpP2PArgs pa = ep_p2p_args(S, ctx->status);
+    pa.path = kEpPathNccl;
+    launch_ep_p2p_announce(pa, st);
+    launch_ep_p2p_wait(pa, 0, st);
+    CKL();
+    RC(check_status(ctx));
+  }
   // 1. route this rank's tokens.
   if (n_tok > 0) {
     {
@@ -1415,7 +1438,7 @@ int kc_init(int device, kc_ctx** out) {
   ctx->device = device;
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->status, sizeof(int)) != cudaSuccess ||
-      cudaMemset(ctx->status, 0, sizeof(int)) != cudaSuccess ||
+      cudaMemsetAsync(ctx->status, 0, sizeof(int), ctx->stream) != cudaSuccess ||
       cudaHostAlloc(&ctx->status_host, sizeof(int), cudaHostAllocDefault) != cudaSuccess) {
     delete ctx;
     return fail(nullptr, KC_ERR_CUDA, "kc_init: stream/status allocation failed");
@@ -1909,7 +1932,9 @@ int kc_model_init(kc_ctx* ctx, int n_layer, int d, int n_head, int n_head_kv, in
       tab[(size_t)p * half + i] = make_float2(std::sin(a), std::cos(a));
     }
   CK(cudaMalloc(&m->rope, tab.size() * sizeof(float2)));
-  CK(cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  // On the context's stream, waited for here: tab is a host temporary.
+  CK(cudaMemcpyAsync(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
   CK(cudaMalloc(&m->logits, (size_t)n_vocab * 4));
   CK(cudaMalloc(&m->next, 4));
   CK(cudaMalloc(&m->counters, 2 * sizeof(int)));
@@ -1938,7 +1963,9 @@ int kc_model_tensor(kc_ctx* ctx, int layer, int kind, int t, const void* w, int6
         m->embd_t = t;
         m->embd_rb = gguf_row_bytes(t, cols);
         CK(cudaMalloc(&m->embd, rows * m->embd_rb));
-        CK(cudaMemcpy(m->embd, w, rows * m->embd_rb, on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(m->embd, w, rows * m->embd_rb, on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                           ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
         return KC_OK;
       case KC_T_OUTPUT_NORM:
         if (t != T_F32 || rows * cols != m->d) return fail(ctx, KC_ERR_SHAPE, "kc_model_tensor: output norm");

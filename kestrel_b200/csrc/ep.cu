@@ -462,6 +462,7 @@ EpP2PArgs ep_p2p_args(const EpState& s, int* status) {
   a.seq = p.seq;
   a.counter = p.counter;
   a.status = status;
+  a.path = kEpPathPeer;
   return a;
 }
 
@@ -485,9 +486,10 @@ __device__ __forceinline__ bool ep_last_cta(int* counter) {
   return last;
 }
 
-__device__ __forceinline__ void ep_publish(uint32_t* line, uint32_t count, uint32_t seq) {
+__device__ __forceinline__ void ep_publish(uint32_t* line, uint32_t count, uint32_t seq, uint32_t path = 0) {
   volatile uint32_t* v = line;
   v[1] = count;
+  v[2] = path;
   __threadfence_system();
   v[0] = seq;
 }
@@ -516,7 +518,7 @@ __global__ void ep_p2p_send_kernel(const EpP2PArgs a, const float* __restrict__ 
   }
   if (ep_last_cta(a.counter)) {
     for (int q = threadIdx.x; q < a.world; q += blockDim.x)
-      ep_publish(ep_line(a.peer[q], a.off_lines, a.me, 0), (uint32_t)xch_out[2 * q], a.seq);
+      ep_publish(ep_line(a.peer[q], a.off_lines, a.me, 0), (uint32_t)xch_out[2 * q], a.seq, (uint32_t)a.path);
   }
 }
 
@@ -528,11 +530,14 @@ void launch_ep_p2p_send(const EpP2PArgs& a, const float* h, const int* ids, cons
 }
 
 // One thread per source: bounded spin until its line carries this call's
-// sequence number.
+// sequence number; on the rows line, then compare the source's path with
+// this rank's.
 __global__ void ep_p2p_wait_kernel(const EpP2PArgs a, int which) {
   pdl_enter();
   const int src = threadIdx.x;
   if (src >= a.world) return;
+  // A call whose ranks already disagree on the path: nothing more will come.
+  if (a.status && (*(volatile int*)a.status & 0xFF) == KC_ERR_STATE) return;
   volatile uint32_t* f = ep_line(a.peer[a.me], a.off_lines, src, which);
   if ((int)(*f - a.seq) < 0) {
     const uint64_t t0 = globaltimer();
@@ -544,6 +549,17 @@ __global__ void ep_p2p_wait_kernel(const EpP2PArgs a, int which) {
     }
   }
   __threadfence_system();
+  if (which == 0 && *f == a.seq && f[2] != (uint32_t)a.path) report(a.status, KC_ERR_STATE | (W_EP_PATH << 8));
+}
+
+__global__ void ep_p2p_announce_kernel(const EpP2PArgs a) {
+  pdl_enter();
+  for (int q = threadIdx.x; q < a.world; q += blockDim.x)
+    ep_publish(ep_line(a.peer[q], a.off_lines, a.me, 0), 0u, a.seq, (uint32_t)a.path);
+}
+
+void launch_ep_p2p_announce(const EpP2PArgs& a, cudaStream_t st) {
+  launch_k(ep_p2p_announce_kernel, 1, 32, 0, st, a);
 }
 
 void launch_ep_p2p_wait(const EpP2PArgs& a, int which, cudaStream_t st) {

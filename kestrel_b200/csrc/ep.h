@@ -21,9 +21,13 @@ constexpr int kEpMaxWorld = 8;
 // arena (CUDA IPC, mapped by every peer) with fixed capacity: T tokens per
 // source rank. Layout (byte offsets, the same on every rank):
 //   rows [src][T][d] f32 | meta [src][T][2k] i32 (ids, weight bits)
-//   | ret [owner][T * k][d] f32 | lines [src][2][32] u32 (flag, count)
+//   | ret [owner][T * k][d] f32 | lines [src][2][32] u32 (flag, count, path)
 // Senders store rows / results straight into the peer's arena, then publish
-// (count, sequence number) on the line [sender][0 rows | 1 results].
+// (count, sequence number) on the line [sender][0 rows | 1 results]. The rows
+// line also carries the exchange path the sender took in this call (peer
+// memory or NCCL): every rank must take the same one, and a rank that sees
+// another path reports KC_ERR_STATE instead of waiting for data that will
+// not come.
 struct EpP2P {
   bool ready = false;
   int T = 0, d = 0, k = 0;
@@ -55,15 +59,24 @@ struct EpP2PArgs {
   uint32_t seq;
   int* counter;
   int* status;
+  int path;  // this rank's exchange path in the call (kEpPathPeer / kEpPathNccl)
 };
+enum : int { kEpPathPeer = 1, kEpPathNccl = 2 };
 EpP2PArgs ep_p2p_args(const EpState& s, int* status);
 // Home: store the rows (and meta) for every owner into its arena at
 // [me][i], then publish (count, seq) on each owner's line [me][0].
 void launch_ep_p2p_send(const EpP2PArgs& a, const float* h, const int* ids, const float* w, const int* send_tok,
                         const int* xch_out, int T_home, cudaStream_t st);
 // Wait (bounded) until every rank has published sequence a.seq on this rank's
-// lines [src][which] (0: rows arrived, 1: results arrived).
+// lines [src][which] (0: rows arrived, 1: results arrived). On the rows line
+// it also checks that the source took this rank's path (a.path) and records
+// KC_ERR_STATE if not; once the status holds KC_ERR_STATE the waits return at
+// once, so a call whose ranks disagree ends quickly on every rank.
 void launch_ep_p2p_wait(const EpP2PArgs& a, int which, cudaStream_t st);
+// A rank that exchanges through NCCL while the peer arenas are mapped
+// publishes (count 0, seq, path NCCL) on every rank's rows line, so that the
+// ranks can compare paths before any NCCL call is made.
+void launch_ep_p2p_announce(const EpP2PArgs& a, cudaStream_t st);
 // Owner: local ids / weights of the arena's rows [src][T] (-1 beyond each
 // source's count and for other owners' experts).
 void launch_ep_p2p_local_ids(const EpP2PArgs& a, int first, int n_local, int* ids_loc, float* w_loc,

@@ -2,6 +2,16 @@
 
   python -m kestrel_b200.decode_bench --model c0 --prompt 64 --gen 64
   python -m kestrel_b200.decode_bench --model c3 --prompt 512 --gen 256
+  python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+      -m kestrel_b200.decode_bench --model c3     # expert parallel over N GPUs
+
+With N ranks (one process per GPU) every MoE layer's experts are sharded in
+contiguous blocks (rank r holds E/N of them, the dense weights are
+replicated), and every rank decodes its own sequence: each step, every rank's
+token goes through its layers, exchanging rows and results with the experts'
+owners over NVLink peer memory inside each layer call. The reported value is
+the tokens all ranks decode per second (weak scaling: one sequence per GPU),
+timed with CUDA events on each rank, max over ranks.
 
 c0 is configs[0] (kestrel_b200.synth.CONFIG0, weights made on the host). c3
 is configs[3]: a random-init Qwen3-30B-A3B-architecture model -- 48 layers,
@@ -11,6 +21,11 @@ embedding, Q6_K output head, RoPE theta 1e6, n_ctx 4096 -- with its ~20 GB of
 weights drawn N(0, 0.02) and quantized on the GPU. Prints one JSON line:
 prefill time of the prompt, decode tokens/s of the greedy steps (batch 1),
 and the weight bytes one decode step streams.
+
+Timing: the prompt is prefilled by kc_model_forward (CUDA events around it);
+the decode steps are then timed alone -- kc_model_generate continues from
+the cached prompt with its first token and runs n_gen one-row forwards,
+bracketed by CUDA events on the library's stream.
 """
 from __future__ import annotations
 
@@ -29,9 +44,11 @@ C3 = dict(name="qwen3-30b-a3b-decode", arch=synth.ARCH_QWEN3, n_layer=48, d=2048
           dense_ff=0)
 
 
-def load_on_gpu(ctx, torch, cfg, n_ctx, seed=0):
+def load_on_gpu(ctx, torch, cfg, n_ctx, seed=0, block=None):
     """Declare cfg and make every weight on the GPU (N(0, 0.02) quantized with
-    kc_quantize_dev; norms 1.0)."""
+    kc_quantize_dev; norms 1.0). With an expert block (expert parallelism)
+    only that block of every layer's experts is uploaded; the weights are
+    drawn identically on every rank."""
     from .cuda import (T_ATTN_K, T_ATTN_K_NORM, T_ATTN_NORM, T_ATTN_OUT, T_ATTN_Q, T_ATTN_Q_NORM, T_ATTN_V,
                        T_FFN_NORM, T_OUTPUT, T_OUTPUT_NORM, T_TOKEN_EMBD)
     gen = torch.Generator(device="cuda").manual_seed(seed)
@@ -67,7 +84,12 @@ def load_on_gpu(ctx, torch, cfg, n_ctx, seed=0):
         gate = quant(cfg["t_gate"], E * ff, d)
         up = quant(cfg["t_gate"], E * ff, d)
         down = quant(cfg["t_down"], E * d, ff)
-        ctx.upload_experts(l, E, d, ff, cfg["t_gate"], gate, cfg["t_gate"], up, cfg["t_down"], down)
+        if block is None:
+            ctx.upload_experts(l, E, d, ff, cfg["t_gate"], gate, cfg["t_gate"], up, cfg["t_down"], down)
+        else:
+            r0, r1 = block.first, block.first + block.count
+            ctx.upload_experts(l, E, d, ff, cfg["t_gate"], gate[r0 * ff:r1 * ff], cfg["t_gate"], up[r0 * ff:r1 * ff],
+                               cfg["t_down"], down[r0 * d:r1 * d], first_expert=block.first, n_local=block.count)
         del gate, up, down
         router = torch.randn((E, d), generator=gen, device="cuda") * 0.02
         ctx.upload_router(l, router, cfg["k"], cfg["norm_topk"], cfg["weights_scale"])
@@ -93,51 +115,97 @@ def main():
     ap.add_argument("--f32-prefill", action="store_true")
     ap.add_argument("--no-warmup", action="store_true", help="skip the warm-up generation (profiling runs)")
     args = ap.parse_args()
+    import os
+
     import torch
     from .cuda import OPT_F32_PREFILL, Context
-    ctx = Context(0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    ctx = Context(local)
     # One stream for torch's weight generation and the library's kernels.
     ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    block = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        from . import ep
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+        ep.join(ctx, rank, world)
     if args.model == "c0":
         cfg = dict(synth.CONFIG0)
         n_prompt, n_gen = args.prompt or 64, args.gen or 64
         n_ctx = args.n_ctx or 256
-        synth.load_cuda(ctx, synth.make_model(cfg, seed=0), n_ctx)
+        if world > 1:
+            from . import ep
+            block = ep.expert_block(cfg["n_expert"], world, rank)
+        synth.load_cuda(ctx, synth.make_model(cfg, seed=0), n_ctx, block=block)
     else:
         cfg = dict(C3)
         n_prompt, n_gen = args.prompt or 512, args.gen or 256
         n_ctx = args.n_ctx or 4096
-        load_on_gpu(ctx, torch, cfg, n_ctx)
+        if world > 1:
+            from . import ep
+            block = ep.expert_block(cfg["n_expert"], world, rank)
+        load_on_gpu(ctx, torch, cfg, n_ctx, block=block)
+    if world > 1:
+        # Every layer call (prompt chunks of up to 256 tokens, decode steps of
+        # one) exchanges through peer memory.
+        ctx.ep_reserve(256)
     ctx.set_option(OPT_F32_PREFILL, 1 if args.f32_prefill else 0)
-    prompt = [int(t) for t in np.random.default_rng(1).integers(0, cfg["n_vocab"], n_prompt)]
+    prompt = [int(t) for t in np.random.default_rng(1 + rank).integers(0, cfg["n_vocab"], n_prompt)]
     # Warm-up (workspace sizing, first launches), then timed runs.
     if not args.no_warmup:
         ctx.model_generate(prompt[:8], 4)
         ctx.model_truncate(0)
-    t0 = time.perf_counter()
-    logits, _ = ctx.model_forward(prompt)
-    t_prefill = time.perf_counter() - t0
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    torch.cuda.synchronize()
+    ev[0].record(stream)
+    logits, first = ctx.model_forward(prompt)
+    ev[1].record(stream)
+    ev[1].synchronize()
+    t_prefill = ev[0].elapsed_time(ev[1]) / 1e3
     finite = bool(np.isfinite(logits).all())
     absmax = float(np.abs(logits[np.isfinite(logits)]).max()) if finite or np.isfinite(logits).any() else None
-    ctx.model_truncate(0)
-    t0 = time.perf_counter()
-    toks = ctx.model_generate(prompt, n_gen)
-    t_all = time.perf_counter() - t0
-    t_decode = max(1e-9, t_all - t_prefill)
-    steps = n_gen - 1  # forwards after the prompt
+    # Decode alone: continue from the cached prompt with its greedy token; every
+    # one of the n_gen forwards is a one-row decode step.
+    torch.cuda.synchronize()
+    ev[2].record(stream)
+    toks = [first] + list(ctx.model_generate([first], n_gen))
+    ev[3].record(stream)
+    ev[3].synchronize()
+    t_decode = max(1e-9, ev[2].elapsed_time(ev[3]) / 1e3)
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([t_decode, t_prefill], dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_decode, t_prefill = float(tt[0]), float(tt[1])
+    steps = n_gen
     k = cfg["k"]
     line = {
-        "metric": "decode_tokens_per_s", "value": steps / t_decode, "unit": "tokens/s", "n_gpus": 1,
-        "batch": 1, "model": cfg["name"], "prompt_tokens": n_prompt, "generated": n_gen,
+        "metric": "decode_tokens_per_s", "value": world * steps / t_decode, "unit": "tokens/s", "n_gpus": world,
+        "batch": 1, "sequences": world, "parallelism": f"ep{world}" if world > 1 else "single",
+        "scaling": "weak (one sequence per GPU)" if world > 1 else None,
+        "model": cfg["name"], "prompt_tokens": n_prompt, "generated": n_gen,
         "ms_per_token": 1e3 * t_decode / steps, "prefill_ms": 1e3 * t_prefill,
         "prefill_tokens_per_s": n_prompt / t_prefill,
         "step_weight_bytes": step_bytes(cfg, k), "step_gbs": step_bytes(cfg, k) / (t_decode / steps) / 1e9,
-        "timing": "wall clock around synchronous kc_model_forward / kc_model_generate calls",
+        "timing": "CUDA events on the library's stream: the prompt's kc_model_forward, then the decode "
+                  "steps alone (kc_model_generate continuing from the cached prompt)",
         "f32_prefill": bool(args.f32_prefill), "tokens_head": toks[:8],
         "prompt_logits_finite": finite, "prompt_logits_absmax": absmax,
     }
-    print(json.dumps(line))
+    if rank == 0:
+        print(json.dumps(line))
     ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -83,8 +83,9 @@ DENSE_KINDS = {"attn_norm": 0, "attn_q": 1, "attn_k": 2, "attn_v": 3, "attn_outp
 MODEL_KINDS = {"token_embd": 0, "output_norm": 1, "output": 2}
 
 
-def load_cuda(ctx, model: dict, n_ctx: int) -> None:
-    """Declare `model` on a cuda.Context and upload its tensors."""
+def load_cuda(ctx, model: dict, n_ctx: int, block=None) -> None:
+    """Declare `model` on a cuda.Context and upload its tensors (with an
+    expert block, only that block of each routed layer's experts)."""
     c = model["cfg"]
     ctx.model_init(c["n_layer"], c["d"], c["n_head"], c["n_kv"], c["head_dim"], c["n_vocab"], n_ctx, c["rope_dim"],
                    c["rope_base"], c["eps"], c["arch"])
@@ -101,5 +102,12 @@ def load_cuda(ctx, model: dict, n_ctx: int) -> None:
         tg, gate, _, _ = by[(l, "ffn_gate_exps")]
         tu, up, _, _ = by[(l, "ffn_up_exps")]
         td, down, _, _ = by[(l, "ffn_down_exps")]
-        ctx.upload_experts(l, c["n_expert"], c["d"], c["ff"], tg, gate, tu, up, td, down)
+        if block is None:
+            ctx.upload_experts(l, c["n_expert"], c["d"], c["ff"], tg, gate, tu, up, td, down)
+        else:
+            from . import ep
+            d, ff = c["d"], c["ff"]
+            ctx.upload_experts(l, c["n_expert"], d, ff, tg, ep.slice_experts(tg, gate, ff, d, block), tu,
+                               ep.slice_experts(tu, up, ff, d, block), td, ep.slice_experts(td, down, d, ff, block),
+                               first_expert=block.first, n_local=block.count)
         ctx.upload_router(l, by[(l, "ffn_gate_inp")][1], c["k"], c["norm_topk"], c["weights_scale"])

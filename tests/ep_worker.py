@@ -26,9 +26,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))
 sys.path.insert(0, HERE)
 
-from gpu_util import bits, make_layer, tol_ok  # noqa: E402
+import oracle  # noqa: E402
+from gpu_util import bits, make_layer, oracle_layer, tol_ok  # noqa: E402
 from kestrel_b200 import ep  # noqa: E402
-from kestrel_b200.cuda import Context  # noqa: E402
+from kestrel_b200.cuda import Context, KestrelCudaError  # noqa: E402
 
 
 def main():
@@ -82,7 +83,36 @@ def main():
             ok, err, scale = tol_ok(out, r_out)
             res.update(out_tol=ok, err=err, scale=scale)
             res["ok"] = res["ids"] and res["w"] and ok
+        # ... and against the CPU oracle on the union (the reference's own
+        # arithmetic): ids where the routing order agrees, the output within
+        # the reference's tolerance.
+        o_out, o_ids, _ = oracle_layer(oracle, L, h_all)
+        ok_o, err_o, scale_o = tol_ok(out, o_out[lo:lo + ns[rank]])
+        res.update(oracle_tol=ok_o, oracle_err=err_o)
+        res["ok"] = res["ok"] and ok_o
         results.append(res)
+    # A call whose ranks take different exchange paths (rank 0 above the
+    # reserved capacity, the others within it) must fail on every rank with
+    # KC_ERR_STATE, quickly, and the next call on one path must work again.
+    rng = np.random.default_rng(99)
+    n_mixed = 40 if rank == 0 else 2
+    try:
+        ctx.moe_ffn(0, rng.standard_normal((n_mixed, d)).astype(np.float32))
+        mixed = "no error"
+    except KestrelCudaError as e:
+        mixed = "state" if e.code == 7 else f"code {e.code}: {e}"
+    # The next call (2 tokens per rank, all on the peer path): ids as one GPU
+    # routes this rank's own tokens, the output within the tolerance of one
+    # GPU running the union (a union of 4 or more tokens routes in gemm order).
+    h_after = np.random.default_rng(100).standard_normal((2 * world, d)).astype(np.float32)
+    out_a, ids_a, _ = ctx.moe_ffn(0, h_after[2 * rank:2 * rank + 2])
+    _, own_ids_a, _ = ref.moe_ffn(0, h_after[2 * rank:2 * rank + 2])
+    u_a, _, _ = ref.moe_ffn(0, h_after)
+    ids_ok = bool(np.array_equal(ids_a, own_ids_a))
+    tol_a, err_a, _ = tol_ok(out_a, u_a[2 * rank:2 * rank + 2])
+    after_ok = ids_ok and tol_a
+    results.append(dict(case="mixed-path", rank=rank, mixed=mixed, after_ok=after_ok, after_ids=ids_ok,
+                        after_err=err_a, ok=mixed == "state" and after_ok))
     gathered = [None] * world
     dist.all_gather_object(gathered, results)
     ctx.close()
