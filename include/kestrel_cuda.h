@@ -32,6 +32,10 @@
  *                            SamplerConfig::greedy (crates/kestrel-engine/src/
  *                            lib.rs:116-145, sampler.rs:25-27, 104-112)
  *   kc_model_truncate        Transformer::truncate (transformer.rs:276-278)
+ *   kc_model_set_sequences / _prefill_seq / _decode_seqs / _generate_batch
+ *                            n independent Engine::generate greedy loops
+ *                            (lib.rs:98-166; the reference serves one sequence
+ *                            per Engine) decoded in lockstep on one context
  *
  * Threading: a context is used by one host thread at a time (the reference's
  * Transformer is `&mut self` per forward, transformer.rs:278). One context per
@@ -285,6 +289,28 @@ KC_API int kc_model_forward(kc_ctx* ctx, const uint32_t* tokens, int n, float* l
    fed to the next step from device memory (no host round trip per token).
    out_tokens [n_gen]. */
 KC_API int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, int n_gen, uint32_t* out_tokens);
+/* Several independent sequences on one context, each with its own KV cache
+   (sequence 0's is the one the calls above use), decoded in lockstep.
+   kc_model_set_sequences: room for n_seq (1..32) sequences; growing it drops
+   every cached position (KC_ERR_OOM if the caches do not fit).
+   kc_model_prefill_seq: evaluate a prompt alone in sequence `seq`'s cache,
+   from position 0; its greedy next token (also returned, may be NULL) becomes
+   the sequence's pending token.
+   kc_model_decode_seqs: n_gen greedy tokens of each of sequences 0..n_seq-1,
+   one row per sequence per step, each row computed as a batch of one would be
+   (router in quant::dot order, int8 products), so sequence s gets exactly the
+   tokens kc_model_generate gives for its prompt alone. out_tokens
+   [n_seq][n_gen]; column 0 is the pending token, and the last token becomes
+   the new pending one (a later call continues). n_seq * top-k <= 1024.
+   kc_model_forward, _generate and _truncate on sequence 0 leave it without a
+   pending token.
+   kc_model_generate_batch: the three in one call (prompts concatenated in
+   `prompts`, prompt_lens[s] tokens each). */
+KC_API int kc_model_set_sequences(kc_ctx* ctx, int n_seq);
+KC_API int kc_model_prefill_seq(kc_ctx* ctx, int seq, const uint32_t* prompt, int n, uint32_t* next_token);
+KC_API int kc_model_decode_seqs(kc_ctx* ctx, int n_seq, int n_gen, uint32_t* out_tokens);
+KC_API int kc_model_generate_batch(kc_ctx* ctx, int n_seq, const uint32_t* prompts, const int* prompt_lens,
+                                   int n_gen, uint32_t* out_tokens);
 /* Forget cached positions from `keep` on; kc_model_cached = positions held. */
 KC_API int kc_model_truncate(kc_ctx* ctx, int keep);
 KC_API int kc_model_cached(const kc_ctx* ctx);

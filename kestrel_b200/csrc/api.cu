@@ -144,6 +144,11 @@ struct kc_ctx {
   // n >= 4 products on CUDA cores in f32 instead of tcgen05 with f16
   // operands (KC_OPT_F32_PREFILL).
   bool f32_prefill = false;
+  // Every row as a batch of one (independent sequences decoded in lockstep):
+  // router sums in quant::dot order, every expert and dense product on the
+  // int8 path in entries of at most three rows. Set only inside
+  // kc_model_decode_seqs's steps.
+  bool rows_mode = false;
   Model* model = nullptr;
   // Auxiliary stream for the n >= 4 products that run beside the int8 ones,
   // and the fork / join events (created on first use).
@@ -255,7 +260,7 @@ int ensure_work(kc_ctx* ctx, Work& w, int T, int E, int K, int D, int F) {
       A * 4, A * 4,                      // ids, w
       (size_t)T * D, (size_t)T * (D / 32 + 1) * 4, (size_t)T * (D / 16 + 1) * 4,  // xq xd xs
       A * rec_bytes(D),                  // xrec
-      (size_t)E * 4, (size_t)(E + 1) * 4, A * 4, A * 4, A * 4, (size_t)E * 4, (size_t)E * 4, 16,  // meta
+      (size_t)E * 4, (size_t)(E + 1) * 4, A * 4, A * 4, A * 4, std::max((size_t)E, A) * 4, (size_t)E * 4, 16,  // meta
       (size_t)(E + 1) * 4,               // large_tt
       A * F * 4, A * F * 4,              // g, u
       A * rec_bytes(F),                  // arec
@@ -468,15 +473,17 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   // 2. dispatch metadata (permute).
   if (!dispatched) {
     StageScope ss(ctx, KC_STAGE_DISPATCH);
-    RC(launch_dispatch(ids, wts, n_rows, k, E, W.meta, st));
+    RC(launch_dispatch(ids, wts, n_rows, k, E, W.meta, st, ctx->rows_mode));
     CKL();
   }
   const bool kq_in = is_k(L.t_gate), kq_dn = is_k(L.t_down);
   const int A = n_rows * k;
-  const int max_small = std::min(E, A);
+  // By rows, the int8 list has up to one entry per selection.
+  const int max_small = ctx->rows_mode ? A : std::min(E, A);
   // An expert holds at most one row per token, so with fewer than 4 rows no
-  // expert reaches the n >= 4 path and its launches are skipped.
-  const bool any_large = n_rows >= 4;
+  // expert reaches the n >= 4 path and its launches are skipped; by rows none
+  // ever does.
+  const bool any_large = n_rows >= 4 && !ctx->rows_mode;
   const bool mma_gu = !ctx->f32_prefill && mma_supported(L.t_gate, d, 2);
   const bool mma_dn = !ctx->f32_prefill && mma_supported(L.t_down, ff, 1) && ff % 256 == 0;
   const int max_tt = ceil_div(A, kMmaTileN) + std::min(E, A / 4);
@@ -683,17 +690,22 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
   cudaStream_t st = ctx->stream;
   if (D.t == T_F32) {
     launch_router_logits(reinterpret_cast<const float*>(D.w), D.rs / 4, (int)D.rows, (int)D.cols, x, n, out, ctx->status,
-                         st);
+                         st, ctx->rows_mode);
     CKL();
     return KC_OK;
   }
-  RC(ensure_work(ctx, n, 1, 1, (int)std::min<int64_t>(D.cols, 1 << 30), 256));
+  // By rows (n >= 4): groups of at most three rows on the int8 path, each
+  // group a list entry over the same matrix.
+  const bool by_rows = ctx->rows_mode && n >= 4;
+  const int groups = by_rows ? (n + 2) / 3 : 1;
+  RC(ensure_work(ctx, n, groups, 1, (int)std::min<int64_t>(D.cols, 1 << 30), 256));
   Work& W = ctx->ws;
-  const bool meta_ready = W.dmeta_n == n;
+  const int meta_key = by_rows ? -n : n;
+  const bool meta_ready = W.dmeta_n == meta_key;
   if (!meta_ready) {
-    launch_dense_meta(n, W.dmeta, st);
+    launch_dense_meta(n, W.dmeta, st, by_rows);
     CKL();
-    W.dmeta_n = n;
+    W.dmeta_n = meta_key;
   }
   const DispatchOut& M = W.dmeta;
   GroupedArgs a = grouped_base(ctx);
@@ -708,7 +720,7 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
   a.af = x;
   a.out = out;
   a.out_stride = out_stride;
-  if (n < 4) {
+  if (n < 4 || by_rows) {
     const bool kq = is_k(D.t);
     const bool ready = rec_ready && kq;
     if (!ready) {
@@ -724,14 +736,15 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     dv.list = M.small_list;
     dv.n_list = M.n_lists;
     dv.offsets = M.offsets;
-    dv.n_experts = 1;
+    dv.n_experts = groups;
+    dv.tile_major = by_rows;
     dv.early = meta_ready;
     dv.rec = ready ? rec_ready : W.xrec;
     dv.rec_slots = n;
     dv.out[0] = out;
     dv.out_stride = out_stride;
     dv.status = ctx->status;
-    RC(launch_decode(dv, ceil_div(D.rows, kTileRows), st));
+    RC(launch_decode(dv, groups * ceil_div(D.rows, kTileRows), st));
   } else if (!ctx->f32_prefill && mma_supported(D.t, D.cols, 1)) {
     launch_act_records(is_k(D.t), x, nullptr, nullptr, n, D.cols, nullptr, n, nullptr, W.x16, st);
     CKL();
@@ -888,7 +901,7 @@ static int ep_pipeline_p2p(kc_ctx* ctx, const Layer& L, const float* router, con
   if (n_tok > 0) {
     {
       StageScope ss(ctx, KC_STAGE_ROUTER_LOGITS);
-      launch_router_logits(router, d, E, d, h, n_tok, ctx->ws.logits, ctx->status, st);
+      launch_router_logits(router, d, E, d, h, n_tok, ctx->ws.logits, ctx->status, st, ctx->rows_mode);
       CKL();
     }
     StageScope ss(ctx, KC_STAGE_ROUTE);
@@ -974,7 +987,7 @@ static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const f
   if (n_tok > 0) {
     {
       StageScope ss(ctx, KC_STAGE_ROUTER_LOGITS);
-      launch_router_logits(router, d, E, d, h, n_tok, ctx->ws.logits, ctx->status, st);
+      launch_router_logits(router, d, E, d, h, n_tok, ctx->ws.logits, ctx->status, st, ctx->rows_mode);
       CKL();
     }
     StageScope ss(ctx, KC_STAGE_ROUTE);
@@ -1074,7 +1087,7 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
   // 1. router logits and top-k (Transformer::route).
   {
     StageScope ss(ctx, KC_STAGE_ROUTER_LOGITS);
-    launch_router_logits(router, d, E, d, h, n_tok, W.logits, ctx->status, st);
+    launch_router_logits(router, d, E, d, h, n_tok, W.logits, ctx->status, st, ctx->rows_mode);
     CKL();
   }
   // Small batches: route and dispatch in one launch, for decode batches with
@@ -1083,7 +1096,7 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
   const bool front = !ctx->prof.on && (with_rec || route_dispatch_supported(n_tok, E, k, d, false));
   if (front) {
     launch_route_dispatch(W.logits, n_tok, E, k, L.norm_topk, L.weights_scale, W.ids, W.w, W.meta, h, d,
-                          with_rec ? W.xrec : nullptr, st);
+                          with_rec ? W.xrec : nullptr, st, ctx->rows_mode);
     CKL();
   } else {
     StageScope ss(ctx, KC_STAGE_ROUTE);
@@ -1116,6 +1129,7 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
 // head and argmax. The matvecs go through dense_forward (quant::matmul's
 // dispatch), so decode steps run the int8 path bit for bit.
 constexpr int kModelBatch = 256;  // Transformer::n_batch (transformer.rs:269)
+constexpr int kMaxSequences = 32;  // rows of a batch step (route_dispatch's one token mask word per expert)
 
 struct Model {
   int n_layer = 0, d = 0, nh = 0, nkv = 0, hd = 0, n_vocab = 0, n_ctx = 0, rd = 0, arch = 0;
@@ -1132,17 +1146,25 @@ struct Model {
   float* out_norm = nullptr;
   Dense output;
   bool ready = false;
-  __half* kc = nullptr;  // [n_layer][n_ctx][nkv * hd]
+  // KV caches of n_seq sequences, [n_seq][n_layer][n_ctx][nkv * hd] each;
+  // the single-sequence calls (kc_model_forward / _generate) use sequence 0.
+  __half* kc = nullptr;
   __half* vc = nullptr;
+  int n_seq = 1;
   float2* rope = nullptr;  // [n_ctx][rd / 2] (sin, cos)
   int cached = 0;
+  int cur = 0;  // sequence whose cache the single-sequence path uses
+  int* row_pos = nullptr;    // [n_seq] positions of the rows of a batch step
+  uint32_t* seq_tok = nullptr;  // [n_seq] each sequence's pending token (kc_model_prefill_seq / _decode_seqs)
+  std::vector<int> seq_pos;     // positions each sequence holds (-1: none yet); [0] mirrors `cached`
+  int64_t seq_elems() const { return (int64_t)n_layer * n_ctx * nkv * hd; }
   // Activations for up to T tokens per forward chunk.
   int T = 0, F = 0;
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *tmp = nullptr, *ffn = nullptr;
   float *g = nullptr, *u = nullptr, *logits = nullptr;
   uint32_t* tok = nullptr;  // [T]
   uint8_t* rec = nullptr;   // Q8_K records of the attention norm's output (decode steps)
-  uint32_t* next = nullptr; // argmax result
+  uint32_t* next = nullptr; // argmax result ([n_seq] in a batch step)
   int* counters = nullptr;  // [0] generated-token index, [1] position (graph-replayed decode steps)
   int64_t bytes = 0;
 };
@@ -1180,7 +1202,7 @@ void model_free(kc_ctx* ctx) {
   cudaFree(m->rope);
   for (void* p : {(void*)m->x, (void*)m->h, (void*)m->qkv, (void*)m->q, (void*)m->att, (void*)m->tmp,
                   (void*)m->ffn, (void*)m->g, (void*)m->u, (void*)m->logits, (void*)m->tok, (void*)m->next,
-                  (void*)m->counters, (void*)m->rec})
+                  (void*)m->counters, (void*)m->rec, (void*)m->row_pos, (void*)m->seq_tok})
     cudaFree(p);
   delete m;
   ctx->model = nullptr;
@@ -1227,7 +1249,7 @@ int model_buffers(kc_ctx* ctx, Model& m, int T) {
   CK(cudaMalloc(&m.g, (size_t)T * F * 4));
   CK(cudaMalloc(&m.u, (size_t)T * F * 4));
   CK(cudaMalloc(&m.tok, (size_t)T * 4));
-  CK(cudaMalloc(&m.rec, (size_t)std::min(T, 3) * rec_row_bytes(true, std::max(256, m.d))));
+  CK(cudaMalloc(&m.rec, (size_t)std::max(std::min(T, 3), m.n_seq) * rec_row_bytes(true, std::max(256, m.d))));
   m.T = T;
   m.F = F;
   return KC_OK;
@@ -1284,11 +1306,15 @@ int model_finalize(kc_ctx* ctx, Model& m) {
 // One forward chunk of n tokens read from `tok` (device); logits of the last
 // token in m.logits and its argmax in m.next. With dev_pos the chunk's
 // position is m.counters[1] on the device (a graph-replayed decode step), and
-// the caller advances m.cached.
-int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos) {
+// the caller advances m.cached. rows (a batch step, ctx->rows_mode): row s is
+// the next token of sequence s, at position m.row_pos[s] of its own cache;
+// every row gets its logits (m.logits [n][n_vocab]) and argmax (m.next[s]).
+int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos, bool rows = false) {
   cudaStream_t st = ctx->stream;
   const int d = m.d, pos0 = m.cached;
   const int* pos_dev = dev_pos ? m.counters + 1 : nullptr;
+  __half* kc0 = m.kc + (rows ? 0 : (int64_t)m.cur * m.seq_elems());
+  __half* vc0 = m.vc + (rows ? 0 : (int64_t)m.cur * m.seq_elems());
   const float scale = 1.0f / std::sqrt((float)m.hd);  // transformer.rs:598
   launch_embed(m.embd, m.embd_t, m.embd_rb, tok, n, d, m.n_vocab, m.x, ctx->status, st);
   CKL();
@@ -1324,7 +1350,7 @@ int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos)
   for (int l = 0; l < m.n_layer; ++l) {
     Model::Lay& y = m.L[l];
     // Decode rows with a K-quant q/k/v take their Q8_K records from the norm.
-    uint8_t* rec = (n < 4 && is_k(y.qkv.t) && d % 256 == 0) ? m.rec : nullptr;
+    uint8_t* rec = ((n < 4 || rows) && is_k(y.qkv.t) && d % 256 == 0) ? m.rec : nullptr;
     norm(m.x, y.attn_norm, n, 0, m.h, rec);
     CKL();
     pending_combine = false;
@@ -1358,12 +1384,15 @@ int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos)
     qa.rope = m.rope;
     qa.q_out = m.q;
     const size_t cache_off = (size_t)l * m.n_ctx * m.nkv * m.hd;
-    qa.kc = m.kc + cache_off;
-    qa.vc = m.vc + cache_off;
+    qa.kc = kc0 + cache_off;
+    qa.vc = vc0 + cache_off;
     qa.pos_dev = pos_dev;
+    qa.row_pos = rows ? m.row_pos : nullptr;
+    qa.seq_stride = m.seq_elems();
     launch_qk_post(qa, st);
     CKL();
-    launch_attention(m.q, qa.kc, qa.vc, n, m.nh, m.nkv, m.hd, pos0, pos_dev, m.n_ctx, scale, m.att, st);
+    launch_attention(m.q, qa.kc, qa.vc, n, m.nh, m.nkv, m.hd, pos0, pos_dev, m.n_ctx, scale, m.att, st, qa.row_pos,
+                     qa.seq_stride);
     CKL();
     RC(dense_forward(ctx, y.o, m.att, n, m.tmp));
     resid = m.tmp;
@@ -1386,6 +1415,15 @@ int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos)
       CKL();
       RC(dense_forward(ctx, y.down, m.g, n, m.ffn));
     }
+  }
+  if (rows) {
+    // Every row is its sequence's last token.
+    norm(m.x, m.out_norm, n, 0, m.h, nullptr);
+    CKL();
+    RC(dense_forward(ctx, m.output, m.h, n, m.logits));
+    launch_argmax(m.logits, m.n_vocab, m.next, st, n);
+    CKL();
+    return KC_OK;
   }
   // Final norm of the last row only (transformer.rs:459-466).
   const int64_t last = (int64_t)(n - 1) * d;
@@ -2016,6 +2054,7 @@ int kc_model_forward(kc_ctx* ctx, const uint32_t* tokens, int n, float* logits, 
   if (!tokens) return fail(ctx, KC_ERR_ARG, "kc_model_forward: tokens is NULL");
   cudaSetDevice(ctx->device);
   Model& m = *ctx->model;
+  if (!m.seq_pos.empty()) m.seq_pos[0] = -1;  // sequence 0 loses its pending token
   RC(model_forward(ctx, tokens, false, n));
   if (logits) CK(cudaMemcpyAsync(logits, m.logits, (size_t)m.n_vocab * 4, cudaMemcpyDeviceToHost, ctx->stream));
   if (next_token) CK(cudaMemcpyAsync(next_token, m.next, 4, cudaMemcpyDeviceToHost, ctx->stream));
@@ -2030,6 +2069,7 @@ int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, int n_g
     return fail(ctx, KC_ERR_ARG, "kc_model_generate: bad arguments");
   cudaSetDevice(ctx->device);
   Model& m = *ctx->model;
+  if (!m.seq_pos.empty()) m.seq_pos[0] = -1;  // sequence 0 loses its pending token
   if (m.cached + n_prompt + std::max(0, n_gen - 1) > m.n_ctx)
     return fail(ctx, KC_ERR_ARG, "kc_model_generate: context full (n_ctx = %d)", m.n_ctx);
   RC(model_forward(ctx, prompt, false, n_prompt));
@@ -2099,10 +2139,222 @@ int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, int n_g
   return check_status(ctx);
 }
 
+// Caches, positions, logits and argmax slots for n_seq sequences (grown, never
+// shrunk). Growing the caches drops every cached position.
+static int model_sequences(kc_ctx* ctx, Model& m, int n_seq) {
+  if (n_seq <= m.n_seq && m.row_pos) return KC_OK;
+  CK(cudaStreamSynchronize(ctx->stream));
+  const int ns = std::max(n_seq, m.n_seq);
+  if (ns > m.n_seq) {
+    const size_t bytes = (size_t)ns * m.seq_elems() * 2;
+    __half *kc = nullptr, *vc = nullptr;
+    if (cudaMalloc(&kc, bytes) != cudaSuccess || cudaMalloc(&vc, bytes) != cudaSuccess) {
+      cudaFree(kc);
+      cudaFree(vc);
+      return fail(ctx, KC_ERR_OOM, "kc_model_set_sequences: KV caches of %d sequences (%.1f GB) do not fit", ns,
+                  2.0 * bytes / 1e9);
+    }
+    CK(cudaMemsetAsync(kc, 0, bytes, ctx->stream));
+    CK(cudaMemsetAsync(vc, 0, bytes, ctx->stream));
+    cudaFree(m.kc);
+    cudaFree(m.vc);
+    m.kc = kc;
+    m.vc = vc;
+    m.cached = 0;
+    m.bytes += (int64_t)(ns - m.n_seq) * m.seq_elems() * 4;
+  }
+  for (void* p : {(void*)m.row_pos, (void*)m.next, (void*)m.logits, (void*)m.rec, (void*)m.seq_tok}) cudaFree(p);
+  m.row_pos = nullptr;
+  m.next = m.seq_tok = nullptr;
+  m.logits = nullptr;
+  m.rec = nullptr;
+  CK(cudaMalloc(&m.row_pos, (size_t)ns * 4));
+  CK(cudaMalloc(&m.next, (size_t)ns * 4));
+  CK(cudaMalloc(&m.seq_tok, (size_t)ns * 4));
+  CK(cudaMalloc(&m.logits, (size_t)ns * m.n_vocab * 4));
+  CK(cudaMalloc(&m.rec, (size_t)std::max(std::min(m.T, 3), ns) * rec_row_bytes(true, std::max(256, m.d))));
+  m.n_seq = ns;
+  m.seq_pos.assign(ns, -1);
+  return KC_OK;
+}
+
+int kc_model_set_sequences(kc_ctx* ctx, int n_seq) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!ctx->model) return fail(ctx, KC_ERR_STATE, "kc_model_set_sequences: call kc_model_init first");
+  if (n_seq < 1 || n_seq > kMaxSequences)
+    return fail(ctx, KC_ERR_ARG, "kc_model_set_sequences: 1 to %d sequences", kMaxSequences);
+  cudaSetDevice(ctx->device);
+  RC(model_sequences(ctx, *ctx->model, n_seq));
+  return KC_OK;
+}
+
+// Transformer::forward of a whole prompt in sequence `seq`'s own cache, from
+// position 0; the greedy token after it becomes the sequence's pending token.
+int kc_model_prefill_seq(kc_ctx* ctx, int seq, const uint32_t* prompt, int n, uint32_t* next_token) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!ctx->model) return fail(ctx, KC_ERR_STATE, "kc_model_prefill_seq: call kc_model_init first");
+  if (!prompt || n < 1) return fail(ctx, KC_ERR_ARG, "kc_model_prefill_seq: empty prompt");
+  cudaSetDevice(ctx->device);
+  Model& m = *ctx->model;
+  if (m.seq_pos.empty()) RC(model_sequences(ctx, m, 1));
+  if (seq < 0 || seq >= m.n_seq)
+    return fail(ctx, KC_ERR_ARG, "kc_model_prefill_seq: sequence %d of %d (kc_model_set_sequences)", seq, m.n_seq);
+  const int keep0 = m.cached;  // sequence 0's position (the single-sequence calls' cache)
+  m.cur = seq;
+  m.cached = 0;
+  int rc = model_forward(ctx, prompt, false, n);
+  m.cur = 0;
+  m.cached = seq == 0 ? (rc == KC_OK ? n : 0) : keep0;
+  RC(rc);
+  CK(cudaMemcpyAsync(m.seq_tok + seq, m.next, 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  if (next_token) CK(cudaMemcpyAsync(next_token, m.next, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  RC(check_status(ctx));  // synchronises the stream
+  m.seq_pos[seq] = n;
+  return KC_OK;
+}
+
+// Greedy decode of sequences 0 .. n_seq-1 in lockstep, each from its pending
+// token and position. Each step runs one row per sequence, each row computed
+// as a batch of one would be (ctx->rows_mode), so each sequence's tokens are
+// kc_model_generate's for its prompt alone.
+int kc_model_decode_seqs(kc_ctx* ctx, int n_seq, int n_gen, uint32_t* out_tokens) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!ctx->model) return fail(ctx, KC_ERR_STATE, "kc_model_decode_seqs: call kc_model_init first");
+  if (n_gen < 0 || (n_gen > 0 && !out_tokens)) return fail(ctx, KC_ERR_ARG, "kc_model_decode_seqs: bad arguments");
+  cudaSetDevice(ctx->device);
+  Model& m = *ctx->model;
+  if (n_seq < 1 || n_seq > m.n_seq || m.seq_pos.empty())
+    return fail(ctx, KC_ERR_ARG, "kc_model_decode_seqs: %d sequences of %d", n_seq, m.n_seq);
+  for (int s = 0; s < n_seq; ++s) {
+    if (m.seq_pos[s] < 1)
+      return fail(ctx, KC_ERR_STATE, "kc_model_decode_seqs: sequence %d has no prompt (kc_model_prefill_seq)", s);
+    if (m.seq_pos[s] + std::max(0, n_gen - 1) > m.n_ctx)
+      return fail(ctx, KC_ERR_ARG, "kc_model_decode_seqs: sequence %d needs more than n_ctx = %d positions", s,
+                  m.n_ctx);
+  }
+  for (auto& kv : ctx->layers)
+    if (kv.second.has_router && (int64_t)n_seq * kv.second.k > 1024)
+      return fail(ctx, KC_ERR_ARG, "kc_model_decode_seqs: n_seq * top-k must be at most 1024");
+  if (n_gen == 0) return KC_OK;
+  uint32_t* hist = nullptr;
+  CK(cudaMalloc(&hist, (size_t)n_seq * n_gen * 4));
+  int rc = KC_OK;
+  // Step state: row s reads its token from next[s] (the pending token, then
+  // the previous step's argmax) and its position from row_pos[s];
+  // advance_rows appends next[s] to sequence s's history (column 0: the
+  // pending token).
+  const int one = 1;
+  if (cudaMemcpy2DAsync(hist, (size_t)n_gen * 4, m.seq_tok, 4, 4, n_seq, cudaMemcpyDeviceToDevice, ctx->stream) !=
+          cudaSuccess ||
+      cudaMemcpyAsync(m.next, m.seq_tok, (size_t)n_seq * 4, cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess ||
+      cudaMemcpyAsync(m.row_pos, m.seq_pos.data(), (size_t)n_seq * 4, cudaMemcpyHostToDevice, ctx->stream) !=
+          cudaSuccess ||
+      cudaMemcpyAsync(m.counters, &one, 4, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess ||
+      cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+    rc = fail(ctx, KC_ERR_CUDA, "kc_model_decode_seqs: copy failed");
+  // The first step runs eagerly (sizing every buffer), the rest replay its
+  // CUDA graph.
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  ctx->rows_mode = true;
+  auto step = [&]() -> int {
+    RC(model_chunk(ctx, m, n_seq, m.next, true, true));
+    launch_advance_rows(m.next, hist, n_gen, n_seq, m.counters, m.row_pos, ctx->stream);
+    CKL();
+    return KC_OK;
+  };
+  const bool graphs = ctx->ep.world <= 1 && !ctx->prof.on && model_graphs_enabled();
+  for (int i = 1; i < n_gen && rc == KC_OK; ++i) {
+    if (exec) {
+      if (cudaGraphLaunch(exec, ctx->stream) != cudaSuccess) rc = fail(ctx, KC_ERR_CUDA, "cudaGraphLaunch failed");
+    } else if (i >= 2 && graphs) {
+      if (!ctx->cap && cudaStreamCreateWithFlags(&ctx->cap, cudaStreamNonBlocking) != cudaSuccess) {
+        rc = fail(ctx, KC_ERR_CUDA, "kc_model_decode_seqs: capture stream creation failed");
+        break;
+      }
+      cudaStream_t run = ctx->stream;
+      if (cudaStreamBeginCapture(ctx->cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        rc = fail(ctx, KC_ERR_CUDA, "kc_model_decode_seqs: stream capture failed");
+        break;
+      }
+      ctx->stream = ctx->cap;
+      const int src = step();
+      ctx->stream = run;
+      const cudaError_t ec = cudaStreamEndCapture(ctx->cap, &graph);
+      if (src != KC_OK) {
+        rc = src;
+        break;
+      }
+      if (ec != cudaSuccess || cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) {
+        rc = fail(ctx, KC_ERR_CUDA, "kc_model_decode_seqs: graph capture of a decode step failed");
+        break;
+      }
+      if (cudaGraphLaunch(exec, ctx->stream) != cudaSuccess) rc = fail(ctx, KC_ERR_CUDA, "cudaGraphLaunch failed");
+    } else {
+      rc = step();
+    }
+  }
+  ctx->rows_mode = false;
+  // The last step's argmax (the last token out) is each sequence's new
+  // pending token.
+  if (rc == KC_OK && n_gen > 1 &&
+      cudaMemcpyAsync(m.seq_tok, m.next, (size_t)n_seq * 4, cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess)
+    rc = fail(ctx, KC_ERR_CUDA, "kc_model_decode_seqs: copy failed");
+  if (rc == KC_OK && cudaMemcpyAsync(out_tokens, hist, (size_t)n_seq * n_gen * 4, cudaMemcpyDeviceToHost,
+                                     ctx->stream) != cudaSuccess)
+    rc = fail(ctx, KC_ERR_CUDA, "kc_model_decode_seqs: copy failed");
+  cudaStreamSynchronize(ctx->stream);
+  if (exec) cudaGraphExecDestroy(exec);
+  if (graph) cudaGraphDestroy(graph);
+  cudaFree(hist);
+  if (rc != KC_OK) {
+    for (int s = 0; s < n_seq; ++s) m.seq_pos[s] = -1;  // partly advanced: needs a new prompt
+    m.cached = 0;
+    return rc;
+  }
+  for (int s = 0; s < n_seq; ++s) m.seq_pos[s] += n_gen - 1;
+  m.cached = m.seq_pos[0];
+  return check_status(ctx);
+}
+
+int kc_model_generate_batch(kc_ctx* ctx, int n_seq, const uint32_t* prompts, const int* prompt_lens, int n_gen,
+                            uint32_t* out_tokens) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!ctx->model) return fail(ctx, KC_ERR_STATE, "kc_model_generate_batch: call kc_model_init first");
+  if (!prompts || !prompt_lens || n_seq < 1 || n_gen < 0 || (n_gen > 0 && !out_tokens))
+    return fail(ctx, KC_ERR_ARG, "kc_model_generate_batch: bad arguments");
+  if (n_seq > kMaxSequences)
+    return fail(ctx, KC_ERR_ARG, "kc_model_generate_batch: at most %d sequences", kMaxSequences);
+  cudaSetDevice(ctx->device);
+  Model& m = *ctx->model;
+  RC(model_finalize(ctx, m));
+  for (int s = 0; s < n_seq; ++s) {
+    if (prompt_lens[s] < 1) return fail(ctx, KC_ERR_ARG, "kc_model_generate_batch: prompt %d is empty", s);
+    if (prompt_lens[s] + std::max(0, n_gen - 1) > m.n_ctx)
+      return fail(ctx, KC_ERR_ARG, "kc_model_generate_batch: sequence %d needs more than n_ctx = %d positions", s,
+                  m.n_ctx);
+  }
+  for (auto& kv : ctx->layers)
+    if (kv.second.has_router && (int64_t)n_seq * kv.second.k > 1024)
+      return fail(ctx, KC_ERR_ARG, "kc_model_generate_batch: n_seq * top-k must be at most 1024");
+  RC(model_sequences(ctx, m, n_seq));
+  int64_t off = 0;
+  for (int s = 0; s < n_seq; ++s) {
+    RC(kc_model_prefill_seq(ctx, s, prompts + off, prompt_lens[s], nullptr));
+    off += prompt_lens[s];
+  }
+  return kc_model_decode_seqs(ctx, n_seq, n_gen, out_tokens);
+}
+
 int kc_model_truncate(kc_ctx* ctx, int keep) {
   if (!ctx) return KC_ERR_ARG;
   if (!ctx->model) return fail(ctx, KC_ERR_STATE, "kc_model_truncate: no model");
   ctx->model->cached = std::min(ctx->model->cached, std::max(0, keep));
+  if (!ctx->model->seq_pos.empty()) ctx->model->seq_pos[0] = -1;
   return KC_OK;
 }
 

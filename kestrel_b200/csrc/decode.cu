@@ -134,11 +134,19 @@ void launch_act_records(bool kquant, const float* x, const float* u, const int* 
 // tokens: one superblock per stage is 13% slower per layer call; three per
 // stage, a 9-stage Q6_K ring, ran into the bounded empty-stage wait.)
 DecodeGeom decode_geom(int t, int64_t cols) {
+  DecodeGeom g = decode_geom_ks(t, cols, t == T_Q8_0 ? 1 : kStageSB);
+  // Stages of more than two superblocks only while the ring keeps more than
+  // DW of them.
+  if (g.ks > 2 && DSMEM / g.stage_bytes <= DW) g = decode_geom_ks(t, cols, 2);
+  return g;
+}
+
+DecodeGeom decode_geom_ks(int t, int64_t cols, int ks) {
   DecodeGeom g{};
   g.type = t;
   g.nb32 = t == T_Q8_0 ? (int)(cols / 32) : 0;
   g.nsb = tiled_nsb(t, cols);
-  g.ks = std::max(1, std::min(g.nsb, t == T_Q8_0 ? 1 : 2));
+  g.ks = std::max(1, std::min(g.nsb, ks));
   g.nseg = (g.nsb + g.ks - 1) / g.ks;
   g.tile_bytes = tiled_tile_bytes(t, cols);
   int mx = 0;
@@ -148,11 +156,11 @@ DecodeGeom decode_geom(int t, int64_t cols) {
     mx = std::max(mx, (int)(end - tiled_sb_offset(t, cols, a)));
   }
   g.rec_off = ((mx + 127) / 128) * 128;
-  // Records of a stage: K-quant, the pair block of up to DMAXS slots (two
-  // records each, whether the stage holds one superblock or two); Q8, ks
-  // chunks of DMAXS records.
+  // Records of a stage: K-quant, per superblock pair of the stage the pair
+  // block of up to DMAXS slots (two records each, whether the pair holds one
+  // superblock or two); Q8, ks chunks of DMAXS records.
   const int rb = rec_bytes_of(t != T_Q8_0);
-  const int rec_region = t != T_Q8_0 ? DMAXS * 2 * rb : g.ks * DMAXS * rb;
+  const int rec_region = t != T_Q8_0 ? ((g.ks + 1) / 2) * DMAXS * 2 * rb : g.ks * DMAXS * rb;
   g.stage_bytes = ((g.rec_off + rec_region + 127) / 128) * 128;
   return g;
 }
@@ -211,7 +219,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
   if (n_units <= 0) return;
   const int n_groups = (n_units + DW - 1) / DW;
   uint8_t* ring = smem;
-  auto unit_at = [&](int i) { return unit_pos(b + i * G, tiles, a.n_mat); };
+  auto unit_at = [&](int i) { return unit_pos(b + i * G, tiles, a.n_mat, a.tile_major, n_list); };
 
   if (warp < DPW) {
     // Producers: group by group, segment-major, one stage per (segment, unit):
@@ -238,9 +246,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
       rp = a.rec + (int64_t)um.slot0 * (KQ ? 2 * R : R);
       rbytes = um.ns * (KQ ? 2 * R : R);
     };
-    // Record bytes of a stage, and the copy of them.
+    // Record bytes of a stage (K-quant: one pair block per superblock pair).
     auto stage_rec_bytes = [&](int sb0, int sb1, int rbytes) {
-      return KQ ? (uint32_t)rbytes : (uint32_t)((sb1 - sb0) * rbytes);
+      return KQ ? (uint32_t)(((sb1 - sb0 + 1) / 2) * rbytes) : (uint32_t)((sb1 - sb0) * rbytes);
     };
     if (a.early) {
       // First lap (stages 0 .. n_stages-1, no slot to wait for): weights now,
@@ -292,8 +300,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
               bulk_g2s(dst, up + off0, wbytes, &full[st]);
             }
             if (KQ) {
-              bulk_g2s(dst + g.rec_off, rp + (int64_t)(sb0 >> 1) * a.rec_slots * (2 * R), (uint32_t)rbytes,
-                       &full[st]);
+              // sb0 is even (a multiple of the even kStageSB, or 0 when one
+              // stage holds the whole row), so the stage's superblocks are
+              // whole pairs (the last one possibly half).
+              for (int pr = 0; pr < (sb1 - sb0 + 1) / 2; ++pr)
+                bulk_g2s(dst + g.rec_off + pr * (DMAXS * 2 * R),
+                         rp + (int64_t)((sb0 >> 1) + pr) * a.rec_slots * (2 * R), (uint32_t)rbytes, &full[st]);
             } else {
               for (int sb = sb0; sb < sb1; ++sb)
                 bulk_g2s(dst + g.rec_off + (sb - sb0) * (DMAXS * R), rp + (int64_t)sb * a.rec_slots * R,

@@ -35,7 +35,7 @@ struct DecodeArgs {
   int expert_base;         // global id of the first expert held
   int rows, cols;          // one expert's matrix
   int type;                // KC_Q4_K / KC_Q6_K / KC_Q8_0
-  const int* list;         // expert ids (1..3 rows each)
+  const int* list;         // expert ids (1..3 rows each; e | part << 16, see meta_at)
   const int* n_list;       // device scalar
   const int* offsets;      // [n_experts + 1] slot ranges
   int n_experts;           // entries of offsets minus one (<= 1024)
@@ -47,6 +47,9 @@ struct DecodeArgs {
   // The list, n_list and offsets were written before the previous kernel in
   // the stream (only rec comes from it): weights stream before the wait.
   bool early;
+  // Units ordered tile by tile over the list entries (n_mat 1, all entries on
+  // one matrix: expert_stride 0) rather than entry by entry.
+  bool tile_major;
 };
 
 // Stage geometry of one weight type / row length (decode.cu).
@@ -62,7 +65,18 @@ struct DecodeGeom {
   int stage_bytes;     // rec_off + ks superblocks x 3 slots of records, rounded to 128
 };
 
+// K-quant superblocks per decode stage (even: a stage's records are whole
+// superblock pairs): the weight bytes of one stage are 32 rows x kStageSB
+// superblocks (fewer when the row has fewer), one bulk copy.
+#ifndef KC_DECODE_STAGE_SB
+#define KC_DECODE_STAGE_SB 4
+#endif
+constexpr int kStageSB = KC_DECODE_STAGE_SB;
+static_assert(kStageSB >= 2 && kStageSB % 2 == 0, "stages hold whole superblock pairs");
 DecodeGeom decode_geom(int t, int64_t cols);
+// The geometry with ks superblocks per stage (1 for Q8_0; even or the whole
+// row for K-quants).
+DecodeGeom decode_geom_ks(int t, int64_t cols, int ks);
 // max_units: an upper bound of the work units (expert x matrix x 32-row tile)
 // used to size the grid; max_ctas (> 0) caps it below the SM count.
 int launch_decode(const DecodeArgs& a, int max_units, cudaStream_t st, int max_ctas = 0);

@@ -218,11 +218,14 @@ struct UnitMeta {
   int e, slot0, ns;
 };
 
-// Meta of list entry li from the shared copies of the list and offsets.
+// Meta of list entry li from the shared copies of the list and offsets. An
+// entry e | part << 16 holds rows DMAXS * part .. of expert e (part 0 unless
+// the list was dispatched by rows).
 __device__ __forceinline__ UnitMeta meta_at(const int* list_s, const int* off_s, int li) {
   UnitMeta m;
-  m.e = list_s[li];
-  m.slot0 = off_s[m.e];
+  const int v = list_s[li];
+  m.e = v & 0xFFFF;
+  m.slot0 = off_s[m.e] + DMAXS * (v >> 16);
   m.ns = max(1, min(DMAXS, off_s[m.e + 1] - m.slot0));
   return m;
 }
@@ -231,8 +234,17 @@ __device__ __forceinline__ UnitMeta meta_at(const int* list_s, const int* off_s,
 struct UnitPos {
   int li, m, tile;
 };
-__device__ __forceinline__ UnitPos unit_pos(int u, int tiles, int n_mat) {
+// tile_major (one matrix): the list entries of a tile are consecutive units,
+// so entries sharing one matrix (a dense product by rows) read each tile
+// close together in time, the later ones from L2.
+__device__ __forceinline__ UnitPos unit_pos(int u, int tiles, int n_mat, bool tile_major = false, int n_list = 1) {
   UnitPos p;
+  if (tile_major) {
+    p.tile = u / n_list;
+    p.li = u - p.tile * n_list;
+    p.m = 0;
+    return p;
+  }
   const int q = u / tiles;
   p.tile = u - q * tiles;
   p.li = n_mat == 2 ? q >> 1 : q;
@@ -256,8 +268,10 @@ static_assert(DC == 2 * DW && DW % 4 == 0, "warp layout");
 // `row` (one per lane / TPR) and lanes l0 = (lane % TPR) * LPT .. of each.
 // The unit's stages are sid0, sid0 + wg, sid0 + 2 wg, ... (segment-major
 // order of its group).
-// Records of the stage: slot s of superblock j at xr + j * SBS + s * SR
-// (defaults: superblock-major, DMAXS slots per superblock).
+// Records of the stage: K-quant, slot s of superblock j at
+// xr + (j / 2) * DMAXS * SR + (j % 2) * SBS + s * SR (pair blocks of DMAXS
+// slots); Q8, chunk j at xr + j * SBS. The defaults (SR = R, SBS = DMAXS * R)
+// make both superblock-major.
 template <int T, int TPR, int NS, class Args, int SR = TypeR<T>::R, int SBS = DMAXS * TypeR<T>::R>
 __device__ __forceinline__ void run_unit(const Args& a, const DecodeGeom& g, const uint8_t* ring,
                                          uint64_t* full, uint64_t* empty, int* rel, int n_stages, int sid0, int wg,
@@ -293,8 +307,10 @@ __device__ __forceinline__ void run_unit(const Args& a, const DecodeGeom& g, con
       const int sb0 = seg * g.ks;
       const int n = min(g.ks, g.nsb - sb0);
       for (int j = 0; j < n; ++j) {
-        if (T == T_Q4_K) q4k_sb<NS, SR, LPT>(sp + 4608 * j, row, l0, xr + j * SBS, acc, summs);
-        else if (T == T_Q6_K) q6k_sb<NS, SR, LPT>(sp + 6720 * j, row, l0, xr + j * SBS, acc);
+        // K-quant records: pair block (j / 2) of the stage, record j % 2 of a slot.
+        const uint32_t xj = xr + (j >> 1) * (DMAXS * SR) + (j & 1) * SBS;
+        if (T == T_Q4_K) q4k_sb<NS, SR, LPT>(sp + 4608 * j, row, l0, xj, acc, summs);
+        else if (T == T_Q6_K) q6k_sb<NS, SR, LPT>(sp + 6720 * j, row, l0, xj, acc);
         else q8_0_chunk<NS, SR, LPT>(sp + 8704 * j, min(8, g.nb32 - 8 * (sb0 + j)), row, l0, xr + j * SBS, acc);
       }
     }

@@ -62,20 +62,27 @@ struct DispatchOut {
   int* slot_tok;   // [n_tok*k] token of each slot
   float* slot_w;   // [n_tok*k] routing weight of each slot
   int* tok_slot;   // [n_tok*k] slot of token s's j-th selection
-  int* small_list; // experts with 1..3 rows (int8 path)
+  int* small_list; // experts with 1..3 rows (int8 path); value e | part << 16
+                   // (rows 3 part .. of expert e; part 0 unless dispatched by rows)
   int* large_list; // experts with >= 4 rows (f32 path)
   int* n_lists;    // [2]: entries in small_list, large_list
   int* large_tt;   // [E+1]: prefix over large_list of ceil(rows / kMmaTileN) token tiles
 };
-int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st);
+// rows: each row computed as a batch of one would be -- every expert in the
+// int8 list, in entries of at most three rows (value e | part << 16), none in
+// the tcgen05 list.
+int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st,
+                    bool rows = false);
 // Small batches: route + dispatch in one launch (n_tok <= 32), and for decode
 // batches (n_tok < 4, rec non-null) also the Q8_K records of each slot's
 // input row (x [n_tok, d], records [d / 256][n_tok * k]).
 bool route_dispatch_supported(int n_tok, int E, int k, int d, bool with_records);
 void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
-                           float* w, const DispatchOut& o, const float* x, int d, uint8_t* rec, cudaStream_t st);
-// Metadata of a dense product: one group of n rows, slots = rows 0..n-1.
-void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st);
+                           float* w, const DispatchOut& o, const float* x, int d, uint8_t* rec, cudaStream_t st,
+                           bool rows = false);
+// Metadata of a dense product: one group of n rows, slots = rows 0..n-1
+// (rows: groups of at most three rows, all on the int8 path).
+void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st, bool rows = false);
 void launch_combine(const float* y, const int* tok_slot, const int* ids, const float* w, int n_tok, int k, int d,
                     float* out, cudaStream_t st);
 

@@ -245,7 +245,8 @@ __global__ void __launch_bounds__(32) qk_post_kernel(QkPostArgs a) {
     for (int j = lane; j < hd; j += 32) v[j] = __fmul_rn(__fmul_rn(v[j], r), nw[j]);
     __syncwarp();
   }
-  const int pos = (a.pos_dev ? *a.pos_dev : a.pos0) + s;
+  const int pos = a.row_pos ? a.row_pos[s] : (a.pos_dev ? *a.pos_dev : a.pos0) + s;
+  const int64_t seq_off = a.row_pos ? (int64_t)s * a.seq_stride : 0;
   if (kind < 2) {
     const int half = a.rd / 2;
     const float2* tab = a.rope + (int64_t)pos * half;
@@ -262,7 +263,7 @@ __global__ void __launch_bounds__(32) qk_post_kernel(QkPostArgs a) {
     float* q = a.q_out + ((int64_t)s * a.nh + hi) * hd;
     for (int j = lane; j < hd; j += 32) q[j] = v[j];
   } else {
-    __half* c = (kind == 1 ? a.kc : a.vc) + (int64_t)pos * a.nkv * hd + (int64_t)hi * hd;
+    __half* c = (kind == 1 ? a.kc : a.vc) + seq_off + (int64_t)pos * a.nkv * hd + (int64_t)hi * hd;
     for (int j = lane; j < hd; j += 32) c[j] = __float2half_rn(v[j]);
   }
 }
@@ -325,7 +326,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __r
                                                                 const __half* __restrict__ kc,
                                                                 const __half* __restrict__ vc, int nh, int nkv,
                                                                 int hd, int pos0, const int* __restrict__ pos_dev,
-                                                                float scale, float* __restrict__ out) {
+                                                                float scale, float* __restrict__ out,
+                                                                const int* __restrict__ row_pos, int64_t seq_stride) {
   pdl_enter();
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                                        // [hd]
@@ -336,10 +338,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __r
   const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
   const int kvh = h / (nh / nkv), kvw = nkv * hd;
   if (pos_dev) pos0 = *pos_dev;
-  const int n_pos = pos0 + s + 1;
+  // Row s is query position pos0 + s of one sequence, or (row_pos) its own
+  // sequence at position row_pos[s].
+  const int n_pos = row_pos ? row_pos[s] + 1 : pos0 + s + 1;
+  const int64_t seq_off = row_pos ? (int64_t)s * seq_stride : 0;
   for (int j = tid; j < hd; j += ATT_THREADS) qs[j] = q[((int64_t)s * nh + h) * hd + j];
-  const __half* kbase = kc + (int64_t)kvh * hd;
-  const __half* vbase = vc + (int64_t)kvh * hd;
+  const __half* kbase = kc + seq_off + (int64_t)kvh * hd;
+  const __half* vbase = vc + seq_off + (int64_t)kvh * hd;
   const int n8 = hd / 8;
   float mx = -INFINITY;
   for_cache_chunks(ks, kbase, n_pos, hd, kvw, tid, [&](int p0, int np, const __half* kch) {
@@ -393,14 +398,16 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float* __r
 int attention_max_positions(int hd) { return 200 * 1024 / 4 - hd - ATT_PC * hd; }
 
 void launch_attention(const float* q, const __half* kc, const __half* vc, int n, int nh, int nkv, int hd, int pos0,
-                      const int* pos_dev, int max_pos, float scale, float* out, cudaStream_t st) {
+                      const int* pos_dev, int max_pos, float scale, float* out, cudaStream_t st, const int* row_pos,
+                      int64_t seq_stride) {
   if (n <= 0) return;
-  // With the position on the device (graph replays), shared memory is sized
-  // for max_pos positions.
-  const size_t smem = (size_t)(hd + ATT_PC * hd + (pos_dev ? max_pos : pos0 + n)) * 4;
+  // With the position on the device (graph replays, rows of sequences),
+  // shared memory is sized for max_pos positions.
+  const size_t smem = (size_t)(hd + ATT_PC * hd + (pos_dev || row_pos ? max_pos : pos0 + n)) * 4;
   static PerDeviceOnce attr;
   smem_attr_once(attr, attention_kernel, 200 * 1024);
-  launch_k(attention_kernel, dim3(n, nh), ATT_THREADS, smem, st, q, kc, vc, nh, nkv, hd, pos0, pos_dev, scale, out);
+  launch_k(attention_kernel, dim3(n, nh), ATT_THREADS, smem, st, q, kc, vc, nh, nkv, hd, pos0, pos_dev, scale, out,
+           row_pos, seq_stride);
 }
 
 // One CTA: strided scans keep the first maximum of each thread, then a
@@ -410,6 +417,8 @@ void launch_attention(const float* q, const __half* kc, const __half* vc, int n,
 constexpr int AM_THREADS = 1024;
 __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restrict__ l, int n, uint32_t* out) {
   pdl_enter();
+  l += (int64_t)blockIdx.x * n;  // row blockIdx.x
+  out += blockIdx.x;
   __shared__ float bv[AM_THREADS / 32];
   __shared__ int bi[AM_THREADS / 32];
   const int tid = threadIdx.x;
@@ -447,8 +456,8 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* __restr
   }
 }
 
-void launch_argmax(const float* l, int n, uint32_t* out, cudaStream_t st) {
-  launch_k(argmax_kernel, 1, AM_THREADS, 0, st, l, n, out);
+void launch_argmax(const float* l, int n, uint32_t* out, cudaStream_t st, int rows) {
+  launch_k(argmax_kernel, std::max(1, rows), AM_THREADS, 0, st, l, n, out);
 }
 
 __global__ void swiglu_kernel(float* __restrict__ g, const float* __restrict__ u, int64_t n) {
@@ -478,5 +487,23 @@ __global__ void advance_kernel(const uint32_t* next, uint32_t* hist, int* step, 
 
 void launch_advance(const uint32_t* next, uint32_t* hist, int* step, int* pos, cudaStream_t st) {
   launch_k(advance_kernel, 1, 1, 0, st, next, hist, step, pos);
+}
+
+__global__ void advance_rows_kernel(const uint32_t* next, uint32_t* hist, int64_t hist_stride, int n, int* step,
+                                    int* pos) {
+  pdl_enter();
+  const int s = threadIdx.x;
+  const int t = *step;
+  __syncthreads();  // every thread has read the step before thread 0 moves it
+  if (s < n) {
+    hist[(int64_t)s * hist_stride + t] = next[s];
+    pos[s] += 1;
+  }
+  if (s == 0) *step = t + 1;
+}
+
+void launch_advance_rows(const uint32_t* next, uint32_t* hist, int64_t hist_stride, int n, int* step, int* pos,
+                         cudaStream_t st) {
+  launch_k(advance_rows_kernel, 1, std::max(32, (n + 31) / 32 * 32), 0, st, next, hist, hist_stride, n, step, pos);
 }
 }  // namespace kc

@@ -56,6 +56,10 @@ struct QkPostArgs {
   float* q_out;
   __half *kc, *vc;
   const int* pos_dev;  // non-null: the position of token 0 is *pos_dev (pos0 ignored)
+  // Non-null: row s is its own sequence, at position row_pos[s], with its
+  // caches at kc / vc + s * seq_stride (pos0 / pos_dev ignored).
+  const int* row_pos;
+  int64_t seq_stride;
 };
 void launch_qk_post(const QkPostArgs& a, cudaStream_t st);
 
@@ -64,14 +68,23 @@ void launch_qk_post(const QkPostArgs& a, cudaStream_t st);
 // attention_max_positions(hd) positions.
 int attention_max_positions(int hd);
 // pos_dev non-null: positions start at *pos_dev (at most max_pos of them).
+// row_pos non-null: row s is its own sequence -- it attends to positions
+// 0 .. row_pos[s] of the caches at kc / vc + s * seq_stride.
 void launch_attention(const float* q, const __half* kc, const __half* vc, int n, int nh, int nkv, int hd, int pos0,
-                      const int* pos_dev, int max_pos, float scale, float* out, cudaStream_t st);
+                      const int* pos_dev, int max_pos, float scale, float* out, cudaStream_t st,
+                      const int* row_pos = nullptr, int64_t seq_stride = 0);
+
+// Rows of independent sequences: hist[s * hist_stride + *step] = next[s] and
+// ++pos[s] for s < n, then ++*step (one block).
+void launch_advance_rows(const uint32_t* next, uint32_t* hist, int64_t hist_stride, int n, int* step, int* pos,
+                         cudaStream_t st);
 
 // hist[*step] = *next; ++*step; ++*pos (one thread).
 void launch_advance(const uint32_t* next, uint32_t* hist, int* step, int* pos, cudaStream_t st);
 
-// sampler::argmax (sampler.rs:104-112) of l [n]: the first maximum.
-void launch_argmax(const float* l, int n, uint32_t* out, cudaStream_t st);
+// sampler::argmax (sampler.rs:104-112) of l [n]: the first maximum; for
+// `rows` rows of l [rows][n], out[r] (one block per row).
+void launch_argmax(const float* l, int n, uint32_t* out, cudaStream_t st, int rows = 1);
 
 // Dense FFN activation in place: g = g / (1 + exp(-g)) * u (transformer.rs:449).
 void launch_swiglu(float* g, const float* u, int64_t n, cudaStream_t st);

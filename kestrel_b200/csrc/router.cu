@@ -29,7 +29,7 @@ constexpr int RT_WARPS = 4;      // route_kernel: tokens (warps) per CTA
 constexpr int DP_THREADS = 1024; // dispatch: one block
 
 __device__ void dispatch_block(const int* __restrict__ ids, const float* __restrict__ w, int n_tok, int k, int E,
-                               const DispatchOut& o, uint32_t* dsm);
+                               const DispatchOut& o, uint32_t* dsm, bool rows);
 __device__ void dispatch_small(const int* __restrict__ ids, const float* __restrict__ w, int n_tok, int k, int E,
                                const DispatchOut& o, uint32_t* dsm);
 
@@ -188,8 +188,11 @@ void launch_route(const float* logits, int n_tok, int E, int k, int norm_topk, f
 
 // The dispatch metadata by one 1024-thread block; dsm: (64 E + 3 E + 1) words
 // of shared memory.
+// rows: every expert's rows go to the int8 list, in entries of at most three
+// (list value e | part << 16: rows 3 part .. 3 part + 2 of expert e), and the
+// tcgen05 list stays empty -- each row computed as a batch of one would be.
 __device__ void dispatch_block(const int* __restrict__ ids, const float* __restrict__ w, int n_tok, int k, int E,
-                               const DispatchOut& o, uint32_t* dsm) {
+                               const DispatchOut& o, uint32_t* dsm, bool rows) {
   uint32_t* mask = dsm;                                // [32][E]
   int* pref = reinterpret_cast<int*>(dsm + 32 * E);    // [32][E]
   int* cnt = pref + 32 * E;                            // [E]
@@ -210,12 +213,19 @@ __device__ void dispatch_block(const int* __restrict__ ids, const float* __restr
   __syncthreads();
   // Block-wide exclusive scan over experts (thread e): slot offsets, positions
   // in the small (1..3 rows) and large (>= 4 rows) lists, and the large
-  // experts' 128-slot tile prefix.
+  // experts' 128-slot tile prefix. The small list holds the 3-row experts,
+  // then the 2-row, then the 1-row ones (ascending id within each): the
+  // decode kernel's units of equal rows then share its groups. Counters
+  // packed in 16-bit fields (E <= 1024): y = 3-row | 2-row << 16,
+  // z = large | 1-row << 16.
   {
     const int e = tid;
     const int c = e < E ? cnt[e] : 0;
-    const int fs = (c >= 1 && c <= 3) ? 1 : 0, fl = c >= 4 ? 1 : 0, ft = fl ? (c + kMmaTileN - 1) / kMmaTileN : 0;
-    int4 v = make_int4(c, fs, fl, ft);
+    // rows: z counts the expert's int8 entries instead (ceil(c / 3)).
+    const int fl = !rows && c >= 4 ? 1 : 0, ft = fl ? (c + kMmaTileN - 1) / kMmaTileN : 0;
+    const int fy = rows ? 0 : (c == 3 ? 1 : (c == 2 ? 1 << 16 : 0));
+    const int fz = rows ? (c + 2) / 3 : fl | (c == 1 ? 1 << 16 : 0);
+    int4 v = make_int4(c, fy, fz, ft);
 #pragma unroll
     for (int sh = 1; sh < 32; sh <<= 1) {
       const int x = __shfl_up_sync(0xffffffffu, v.x, sh), y = __shfl_up_sync(0xffffffffu, v.y, sh);
@@ -246,23 +256,31 @@ __device__ void dispatch_block(const int* __restrict__ ids, const float* __restr
     }
     __syncthreads();
     const int4 wb = warp > 0 ? wsum[warp - 1] : make_int4(0, 0, 0, 0);
-    const int4 ex = make_int4(wb.x + v.x - c, wb.y + v.y - fs, wb.z + v.z - fl, wb.w + v.w - ft);
+    const int4 ex = make_int4(wb.x + v.x - c, wb.y + v.y - fy, wb.z + v.z - fz, wb.w + v.w - ft);
+    const int4 tot = wsum[31];
+    const int n3 = tot.y & 0xFFFF, n2 = tot.y >> 16, n1 = tot.z >> 16, nl = rows ? 0 : tot.z & 0xFFFF;
     if (e < E) {
       offs[e] = ex.x;
       o.offsets[e] = ex.x;
       o.counts[e] = c;
-      if (fs) o.small_list[ex.y] = e;
+      if (rows) {
+        for (int p = 0; p < fz; ++p) o.small_list[ex.z + p] = e | (p << 16);
+      } else {
+        if (c == 3) o.small_list[ex.y & 0xFFFF] = e;
+        if (c == 2) o.small_list[n3 + (ex.y >> 16)] = e;
+        if (c == 1) o.small_list[n3 + n2 + (ex.z >> 16)] = e;
+      }
       if (fl) {
-        o.large_list[ex.z] = e;
-        o.large_tt[ex.z] = ex.w;
+        o.large_list[ex.z & 0xFFFF] = e;
+        o.large_tt[ex.z & 0xFFFF] = ex.w;
       }
     }
     if (e == E - 1) {
       offs[E] = ex.x + c;
       o.offsets[E] = ex.x + c;
-      o.n_lists[0] = ex.y + fs;
-      o.n_lists[1] = ex.z + fl;
-      o.large_tt[ex.z + fl] = ex.w + ft;
+      o.n_lists[0] = rows ? tot.z : n3 + n2 + n1;
+      o.n_lists[1] = nl;
+      o.large_tt[nl] = rows ? 0 : tot.w;
     }
   }
   __syncthreads();
@@ -314,12 +332,12 @@ __device__ void dispatch_small(const int* __restrict__ ids, const float* __restr
                                const DispatchOut& o, uint32_t* dsm) {
   int* ids_s = reinterpret_cast<int*>(dsm);        // [A]
   const int nw = (E + 31) / 32;
-  uint32_t* small_m = dsm + DS_MAXA;               // [nw] experts with 1-3 rows
-  uint32_t* large_m = small_m + 32;                // [nw] experts with >= 4 rows
+  uint32_t* small_m = dsm + DS_MAXA;               // [3][32]: experts with 1, 2, 3 rows
+  uint32_t* large_m = small_m + 3 * 32;            // [nw] experts with >= 4 rows
   int* cnt_s = reinterpret_cast<int*>(large_m + 32);  // [E]
   const int tid = threadIdx.x, A = n_tok * k;
   for (int i = tid; i < nw; i += DP_THREADS) {
-    small_m[i] = 0u;
+    small_m[i] = small_m[32 + i] = small_m[64 + i] = 0u;
     large_m[i] = 0u;
   }
   for (int i = tid; i < A; i += DP_THREADS) ids_s[i] = ids[i];
@@ -328,10 +346,15 @@ __device__ void dispatch_small(const int* __restrict__ ids, const float* __restr
     int c = 0;
     for (int i = 0; i < A; ++i) c += ids_s[i] == e ? 1 : 0;
     cnt_s[e] = c;
-    if (c >= 1 && c <= 3) atomicOr(&small_m[e >> 5], 1u << (e & 31));
+    if (c >= 1 && c <= 3) atomicOr(&small_m[32 * (c - 1) + (e >> 5)], 1u << (e & 31));
     if (c >= 4) atomicOr(&large_m[e >> 5], 1u << (e & 31));
   }
   __syncthreads();
+  // The small list: 3-row experts, then 2-row, then 1-row (ascending id
+  // within each), so that the decode kernel's groups hold units of equal rows.
+  int n_of[3] = {0, 0, 0};
+  for (int q = 0; q < nw; ++q)
+    for (int c = 0; c < 3; ++c) n_of[c] += __popc(small_m[32 * c + q]);
   for (int e = tid; e < E; e += DP_THREADS) {
     const int c = cnt_s[e];
     int less = 0;
@@ -340,8 +363,9 @@ __device__ void dispatch_small(const int* __restrict__ ids, const float* __restr
     o.offsets[e] = less;
     const uint32_t below = (1u << (e & 31)) - 1u;
     if (c >= 1 && c <= 3) {
-      int pos = __popc(small_m[e >> 5] & below);
-      for (int q = 0; q < (e >> 5); ++q) pos += __popc(small_m[q]);
+      const uint32_t* m = small_m + 32 * (c - 1);
+      int pos = __popc(m[e >> 5] & below) + (c < 3 ? n_of[2] : 0) + (c < 2 ? n_of[1] : 0);
+      for (int q = 0; q < (e >> 5); ++q) pos += __popc(m[q]);
       o.small_list[pos] = e;
     } else if (c >= 4) {
       int pos = __popc(large_m[e >> 5] & below), tt = 0;
@@ -355,10 +379,8 @@ __device__ void dispatch_small(const int* __restrict__ ids, const float* __restr
   if (tid == 0) {
     int n_valid = 0, n_small = 0, n_large = 0, tt = 0;
     for (int i = 0; i < A; ++i) n_valid += (ids_s[i] >= 0 && ids_s[i] < E) ? 1 : 0;
-    for (int q = 0; q < nw; ++q) {
-      n_small += __popc(small_m[q]);
-      n_large += __popc(large_m[q]);
-    }
+    n_small = n_of[0] + n_of[1] + n_of[2];
+    for (int q = 0; q < nw; ++q) n_large += __popc(large_m[q]);
     for (int q = 0; q < nw; ++q)
       for (uint32_t m = large_m[q]; m; m &= m - 1u) {
         const int e = 32 * q + __ffs(m) - 1;
@@ -388,11 +410,12 @@ __device__ void dispatch_small(const int* __restrict__ ids, const float* __restr
 
 __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restrict__ ids,
                                                                const float* __restrict__ w, int n_tok, int k, int E,
-                                                               DispatchOut o) {
+                                                               DispatchOut o, bool rows) {
   pdl_enter();
   extern __shared__ uint32_t dsm[];
+  // Fewer than 4 tokens: no expert has more than 3 rows, so `rows` changes nothing.
   if (n_tok < 4 && n_tok * k <= DS_MAXA) dispatch_small(ids, w, n_tok, k, E, o, dsm);
-  else dispatch_block(ids, w, n_tok, k, E, o, dsm);
+  else dispatch_block(ids, w, n_tok, k, E, o, dsm, rows);
 }
 
 // Route + dispatch for batches of at most 32 tokens (one warp per token), and
@@ -416,7 +439,7 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
                                                                      int E, int k, int norm_topk, float weights_scale,
                                                                      int* __restrict__ ids, float* __restrict__ w,
                                                                      DispatchOut o, const float* __restrict__ x,
-                                                                     int d, uint8_t* __restrict__ rec) {
+                                                                     int d, uint8_t* __restrict__ rec, bool rows) {
   extern __shared__ __align__(16) uint32_t dsm[];
   const int SW = E + 2 * RT_MAXK;                                 // per-token scratch: p, selw, seli
   float* scratch = reinterpret_cast<float*>(dsm);                 // [RD_MAXT][SW]
@@ -473,35 +496,58 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
   __syncthreads();
   if (warp == 0) {
     // Experts [e0, e1) per lane, contiguous, then an exclusive warp scan of
-    // (rows, int8-list entries, tcgen05-list entries, tcgen05 token tiles).
+    // (rows, int8-list entries by row count, tcgen05-list entries, tcgen05
+    // token tiles). The int8 list holds the 3-row experts, then the 2-row,
+    // then the 1-row ones (ascending id within each), so that the decode
+    // kernel's groups hold units of equal rows. The 3- and 2-row counts are
+    // packed as 3-row | 2-row << 16 (each at most E <= 1024).
     const int C = (E + 31) / 32, e0 = min(E, lane * C), e1 = min(E, e0 + C);
-    int sc = 0, ss = 0, sl = 0, st = 0;
+    int sc = 0, ss = 0, s1 = 0, sl = 0, st = 0;
+    // rows (dispatch_block's): every expert in the int8 list, in entries of at
+    // most three rows; s1 then counts entries.
     for (int e = e0; e < e1; ++e) {
       const int c = __popc(mask_s[e]);
       sc += c;
-      ss += (c >= 1 && c <= 3) ? 1 : 0;
+      if (rows) {
+        s1 += (c + 2) / 3;
+        continue;
+      }
+      ss += c == 3 ? 1 : (c == 2 ? 1 << 16 : 0);
+      s1 += c == 1 ? 1 : 0;
       sl += c >= 4 ? 1 : 0;
       st += c >= 4 ? (c + kMmaTileN - 1) / kMmaTileN : 0;
     }
-    int ic = sc, is = ss, il = sl, it = st;
+    int ic = sc, is = ss, i1 = s1, il = sl, it = st;
 #pragma unroll
     for (int sh = 1; sh < 32; sh <<= 1) {
       const int a0 = __shfl_up_sync(0xffffffffu, ic, sh), a1 = __shfl_up_sync(0xffffffffu, is, sh);
       const int a2 = __shfl_up_sync(0xffffffffu, il, sh), a3 = __shfl_up_sync(0xffffffffu, it, sh);
+      const int a4 = __shfl_up_sync(0xffffffffu, i1, sh);
       if (lane >= sh) {
         ic += a0;
         is += a1;
         il += a2;
         it += a3;
+        i1 += a4;
       }
     }
+    const int ts = __shfl_sync(0xffffffffu, is, 31), n1 = __shfl_sync(0xffffffffu, i1, 31);
+    const int n3 = ts & 0xFFFF, n2 = ts >> 16;
     int oc = ic - sc, os = is - ss, ol = il - sl, ot = it - st;
+    int o3 = os & 0xFFFF, o2 = n3 + (os >> 16), o1 = n3 + n2 + (i1 - s1);
     for (int e = e0; e < e1; ++e) {
       const int c = __popc(mask_s[e]);
       offs_s[e] = oc;
       oc += c;
-      if (c >= 1 && c <= 3) {
-        pos_s[e] = os++;
+      if (rows) {
+        pos_s[e] = o1;  // first of the expert's (c + 2) / 3 entries
+        o1 += (c + 2) / 3;
+      } else if (c == 3) {
+        pos_s[e] = o3++;
+      } else if (c == 2) {
+        pos_s[e] = o2++;
+      } else if (c == 1) {
+        pos_s[e] = o1++;
       } else if (c >= 4) {
         pos_s[e] = ol++;
         tt_s[e] = ot;
@@ -510,7 +556,7 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
     }
     if (lane == 31) {
       offs_s[E] = oc;
-      tot_s[0] = os;
+      tot_s[0] = rows ? n1 : n3 + n2 + n1;
       tot_s[1] = ol;
       tot_s[2] = ot;
     }
@@ -520,7 +566,9 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
     const int c = __popc(mask_s[e]);
     o.offsets[e] = offs_s[e];
     o.counts[e] = c;
-    if (c >= 1 && c <= 3) {
+    if (rows) {
+      for (int p = 0; p < (c + 2) / 3; ++p) o.small_list[pos_s[e] + p] = e | (p << 16);
+    } else if (c >= 1 && c <= 3) {
       o.small_list[pos_s[e]] = e;
     } else if (c >= 4) {
       o.large_list[pos_s[e]] = e;
@@ -563,25 +611,42 @@ bool route_dispatch_supported(int n_tok, int E, int k, int d, bool with_records)
 }
 
 void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
-                           float* w, const DispatchOut& o, const float* x, int d, uint8_t* rec, cudaStream_t st) {
+                           float* w, const DispatchOut& o, const float* x, int d, uint8_t* rec, cudaStream_t st,
+                           bool rows) {
   static PerDeviceOnce attr;
   smem_attr_once(attr, route_dispatch_kernel, 200 * 1024);
   launch_k(route_dispatch_kernel, 1, DP_THREADS, rd_smem(E, k), st, logits, n_tok, E, k, norm_topk, weights_scale,
-           ids, w, o, x, d, rec);
+           ids, w, o, x, d, rec, rows);
 }
 
-int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st) {
-  size_t smem = std::max((size_t)(64 * E + 3 * E + 1), (size_t)(DS_MAXA + 64 + E)) * 4;
+int launch_dispatch(const int* ids, const float* w, int n_tok, int k, int E, const DispatchOut& o, cudaStream_t st,
+                    bool rows) {
+  size_t smem = std::max((size_t)(64 * E + 3 * E + 1), (size_t)(DS_MAXA + 128 + E)) * 4;
   static PerDeviceOnce attr;
   smem_attr_once(attr, dispatch_kernel, 200 * 1024);
   if (smem > 200 * 1024 || E > DP_THREADS) return KC_ERR_SHAPE;
-  launch_k(dispatch_kernel, 1, DP_THREADS, smem, st, ids, w, n_tok, k, E, o);
+  launch_k(dispatch_kernel, 1, DP_THREADS, smem, st, ids, w, n_tok, k, E, o, rows);
   return KC_OK;
 }
 
 // One group (expert 0) holding rows 0..n-1: the metadata of a dense product.
-__global__ void dense_meta_kernel(int n, DispatchOut o) {
+// rows: groups g of rows 3g .. 3g + 2 instead (all on the int8 path; the
+// product's matrix is shared by every group).
+__global__ void dense_meta_kernel(int n, DispatchOut o, bool rows) {
   pdl_enter();
+  if (rows) {
+    const int ng = (n + 2) / 3;
+    for (int g = 0; g < ng; ++g) {
+      o.counts[g] = min(3, n - 3 * g);
+      o.offsets[g] = 3 * g;
+      o.small_list[g] = g;
+    }
+    o.offsets[ng] = n;
+    o.n_lists[0] = ng;
+    o.n_lists[1] = 0;
+    o.large_tt[0] = 0;
+    return;
+  }
   o.counts[0] = n;
   o.offsets[0] = 0;
   o.offsets[1] = n;
@@ -593,7 +658,9 @@ __global__ void dense_meta_kernel(int n, DispatchOut o) {
   o.large_tt[1] = n >= 4 ? (n + kMmaTileN - 1) / kMmaTileN : 0;
 }
 
-void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st) { launch_k(dense_meta_kernel, 1, 1, 0, st, n, o); }
+void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st, bool rows) {
+  launch_k(dense_meta_kernel, 1, 1, 0, st, n, o, rows);
+}
 
 // ---------------------------------------------------------------------------
 // Combine (transformer.rs:566-570): out[s] = sum over the token's experts in

@@ -61,6 +61,10 @@ SIGNATURES = {
     "kc_model_tensor": (I, [P, I, I, I, P, I64, I64, I]),
     "kc_model_forward": (I, [P, P, I, P, P]),
     "kc_model_generate": (I, [P, P, I, I, P]),
+    "kc_model_generate_batch": (I, [P, I, P, P, I, P]),
+    "kc_model_set_sequences": (I, [P, I]),
+    "kc_model_prefill_seq": (I, [P, I, P, I, P]),
+    "kc_model_decode_seqs": (I, [P, I, I, P]),
     "kc_model_truncate": (I, [P, I]),
     "kc_model_cached": (I, [P]),
     "kc_load_gguf": (I, [P, ctypes.c_char_p, I, ctypes.c_char_p, I64]),
@@ -314,6 +318,31 @@ class Context:
         out = np.zeros(max(1, n_gen), np.uint32)
         self._check(lib().kc_model_generate(self.h, _ptr(tk), tk.size, n_gen, _ptr(out)))
         return [int(t) for t in out[:n_gen]]
+
+    def model_generate_batch(self, prompts, n_gen: int):
+        """kc_model_generate_batch: greedy decode of len(prompts) independent
+        sequences in lockstep; returns one token list per sequence."""
+        lens = np.array([len(p) for p in prompts], dtype=np.int32)
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(p, dtype=np.uint32) for p in prompts]))
+        out = np.zeros((len(prompts), max(1, n_gen)), np.uint32)
+        self._check(lib().kc_model_generate_batch(self.h, len(prompts), _ptr(flat), _ptr(lens), n_gen, _ptr(out)))
+        return [[int(t) for t in row[:n_gen]] for row in out]
+
+    def model_set_sequences(self, n_seq: int):
+        self._check(lib().kc_model_set_sequences(self.h, n_seq))
+
+    def model_prefill_seq(self, seq: int, prompt) -> int:
+        """kc_model_prefill_seq: the prompt alone in sequence `seq`'s cache;
+        returns its greedy next token (the sequence's pending token)."""
+        tk = np.ascontiguousarray(prompt, dtype=np.uint32)
+        nxt = np.zeros(1, np.uint32)
+        self._check(lib().kc_model_prefill_seq(self.h, seq, _ptr(tk), tk.size, _ptr(nxt)))
+        return int(nxt[0])
+
+    def model_decode_seqs(self, n_seq: int, n_gen: int):
+        out = np.zeros((n_seq, max(1, n_gen)), np.uint32)
+        self._check(lib().kc_model_decode_seqs(self.h, n_seq, n_gen, _ptr(out)))
+        return [[int(t) for t in row[:n_gen]] for row in out]
 
     def model_truncate(self, keep: int):
         self._check(lib().kc_model_truncate(self.h, keep))

@@ -2,6 +2,7 @@
 
   python -m kestrel_b200.decode_bench --model c0 --prompt 64 --gen 64
   python -m kestrel_b200.decode_bench --model c3 --prompt 512 --gen 256
+  python -m kestrel_b200.decode_bench --model c3 --batch 8   # 8 sequences in lockstep
   python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
       -m kestrel_b200.decode_bench --model c3     # expert parallel over N GPUs
 
@@ -26,6 +27,12 @@ Timing: the prompt is prefilled by kc_model_forward (CUDA events around it);
 the decode steps are then timed alone -- kc_model_generate continues from
 the cached prompt with its first token and runs n_gen one-row forwards,
 bracketed by CUDA events on the library's stream.
+
+--batch B (B > 1): B independent sequences (prompts of the same length, other
+seeds) in lockstep: each prompt is prefilled alone (kc_model_prefill_seq,
+all B timed together), then kc_model_decode_seqs runs n_gen + 1 tokens per
+sequence -- n_gen steps of B rows, each row computed as a batch of one --
+timed alone. The value counts B * n_gen tokens per decode time.
 """
 from __future__ import annotations
 
@@ -114,6 +121,7 @@ def main():
     ap.add_argument("--n-ctx", type=int, default=None)
     ap.add_argument("--f32-prefill", action="store_true")
     ap.add_argument("--no-warmup", action="store_true", help="skip the warm-up generation (profiling runs)")
+    ap.add_argument("--batch", type=int, default=1, help="independent sequences decoded in lockstep")
     args = ap.parse_args()
     import os
 
@@ -156,29 +164,55 @@ def main():
         # one) exchanges through peer memory.
         ctx.ep_reserve(256)
     ctx.set_option(OPT_F32_PREFILL, 1 if args.f32_prefill else 0)
-    prompt = [int(t) for t in np.random.default_rng(1 + rank).integers(0, cfg["n_vocab"], n_prompt)]
-    # Warm-up (workspace sizing, first launches), then timed runs.
-    if not args.no_warmup:
-        ctx.model_generate(prompt[:8], 4)
-        ctx.model_truncate(0)
+    B = max(1, args.batch)
+    prompts = [[int(t) for t in np.random.default_rng(1 + rank * B + s).integers(0, cfg["n_vocab"], n_prompt)]
+               for s in range(B)]
+    prompt = prompts[0]
     stream = torch.cuda.current_stream()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    torch.cuda.synchronize()
-    ev[0].record(stream)
-    logits, first = ctx.model_forward(prompt)
-    ev[1].record(stream)
-    ev[1].synchronize()
-    t_prefill = ev[0].elapsed_time(ev[1]) / 1e3
-    finite = bool(np.isfinite(logits).all())
-    absmax = float(np.abs(logits[np.isfinite(logits)]).max()) if finite or np.isfinite(logits).any() else None
-    # Decode alone: continue from the cached prompt with its greedy token; every
-    # one of the n_gen forwards is a one-row decode step.
-    torch.cuda.synchronize()
-    ev[2].record(stream)
-    toks = [first] + list(ctx.model_generate([first], n_gen))
-    ev[3].record(stream)
-    ev[3].synchronize()
-    t_decode = max(1e-9, ev[2].elapsed_time(ev[3]) / 1e3)
+    finite, absmax = None, None
+    if B == 1:
+        # Warm-up (workspace sizing, first launches), then timed runs.
+        if not args.no_warmup:
+            ctx.model_generate(prompt[:8], 4)
+            ctx.model_truncate(0)
+        torch.cuda.synchronize()
+        ev[0].record(stream)
+        logits, first = ctx.model_forward(prompt)
+        ev[1].record(stream)
+        ev[1].synchronize()
+        t_prefill = ev[0].elapsed_time(ev[1]) / 1e3
+        finite = bool(np.isfinite(logits).all())
+        absmax = float(np.abs(logits[np.isfinite(logits)]).max()) if finite or np.isfinite(logits).any() else None
+        # Decode alone: continue from the cached prompt with its greedy token;
+        # every one of the n_gen forwards is a one-row decode step.
+        torch.cuda.synchronize()
+        ev[2].record(stream)
+        toks = [first] + list(ctx.model_generate([first], n_gen))
+        ev[3].record(stream)
+        ev[3].synchronize()
+        t_decode = max(1e-9, ev[2].elapsed_time(ev[3]) / 1e3)
+    else:
+        ctx.model_set_sequences(B)
+        if not args.no_warmup:
+            for s in range(B):
+                ctx.model_prefill_seq(s, prompts[s][:8])
+            ctx.model_decode_seqs(B, 4)
+        torch.cuda.synchronize()
+        ev[0].record(stream)
+        firsts = [ctx.model_prefill_seq(s, prompts[s]) for s in range(B)]
+        ev[1].record(stream)
+        ev[1].synchronize()
+        t_prefill = ev[0].elapsed_time(ev[1]) / 1e3
+        # n_gen + 1 tokens per sequence: the pending token, then n_gen steps.
+        torch.cuda.synchronize()
+        ev[2].record(stream)
+        out = ctx.model_decode_seqs(B, n_gen + 1)
+        ev[3].record(stream)
+        ev[3].synchronize()
+        t_decode = max(1e-9, ev[2].elapsed_time(ev[3]) / 1e3)
+        assert [o[0] for o in out] == firsts
+        toks = out[0]
     if world > 1:
         import torch.distributed as dist
         tt = torch.tensor([t_decode, t_prefill], dtype=torch.float64)
@@ -186,16 +220,22 @@ def main():
         t_decode, t_prefill = float(tt[0]), float(tt[1])
     steps = n_gen
     k = cfg["k"]
+    # Weight bytes of a step: with B rows, the experts the step's rows choose
+    # (counted as B * k distinct, an upper bound: the union is smaller when
+    # rows share experts).
+    sb = step_bytes(cfg, min(cfg["n_expert"], k * B))
     line = {
-        "metric": "decode_tokens_per_s", "value": world * steps / t_decode, "unit": "tokens/s", "n_gpus": world,
-        "batch": 1, "sequences": world, "parallelism": f"ep{world}" if world > 1 else "single",
-        "scaling": "weak (one sequence per GPU)" if world > 1 else None,
+        "metric": "decode_tokens_per_s", "value": world * B * steps / t_decode, "unit": "tokens/s", "n_gpus": world,
+        "batch": B, "sequences": world * B, "parallelism": f"ep{world}" if world > 1 else "single",
+        "scaling": f"weak ({B} sequence(s) per GPU)" if world > 1 else None,
         "model": cfg["name"], "prompt_tokens": n_prompt, "generated": n_gen,
-        "ms_per_token": 1e3 * t_decode / steps, "prefill_ms": 1e3 * t_prefill,
-        "prefill_tokens_per_s": n_prompt / t_prefill,
-        "step_weight_bytes": step_bytes(cfg, k), "step_gbs": step_bytes(cfg, k) / (t_decode / steps) / 1e9,
-        "timing": "CUDA events on the library's stream: the prompt's kc_model_forward, then the decode "
-                  "steps alone (kc_model_generate continuing from the cached prompt)",
+        "ms_per_step": 1e3 * t_decode / steps, "ms_per_token": 1e3 * t_decode / steps / B,
+        "prefill_ms": 1e3 * t_prefill, "prefill_tokens_per_s": B * n_prompt / t_prefill,
+        "step_weight_bytes": sb, "step_gbs": sb / (t_decode / steps) / 1e9,
+        "step_bytes_note": "exact" if B == 1 else "upper bound: B * k experts per layer counted distinct",
+        "timing": "CUDA events on the library's stream: the prompts' prefill, then the decode steps alone "
+                  + ("(kc_model_generate continuing from the cached prompt)" if B == 1 else
+                     "(kc_model_decode_seqs after kc_model_prefill_seq of every sequence)"),
         "f32_prefill": bool(args.f32_prefill), "tokens_head": toks[:8],
         "prompt_logits_finite": finite, "prompt_logits_absmax": absmax,
     }

@@ -130,9 +130,10 @@ def run_ring(nu, nseg, n_stages, seed, counted=True, slow=()):
             del gens[key]
 
 
-# Ring geometries of the shipped kernel: Q4_K 19 stages x 4 segments (d=2048),
-# Q6_K 14 x 2 (ff=768), and tighter rings.
-GEOMS = [(4, 19), (2, 14), (4, 14), (2, 9)]
+# Ring geometries of the shipped kernel (segments per unit, stages): Q4_K with
+# four superblocks per stage, 9 stages x 2 segments (d=2048) or x 4 (d=4096);
+# Q6_K with two, 14 x 2 (ff=768) and 7-stage-wide rows; and deeper rings.
+GEOMS = [(2, 9), (4, 9), (2, 14), (4, 14), (4, 19)]
 
 
 @pytest.mark.parametrize("units", [3, 8, 9, 17, 25, 33, 40])
