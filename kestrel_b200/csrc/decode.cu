@@ -128,11 +128,15 @@ void launch_act_records(bool kquant, const float* x, const float* u, const int* 
 // ---------------------------------------------------------------------------
 // Stage geometry: a stage is one 32-row tile x a segment of `ks` consecutive
 // superblocks (Q8_0: chunks of 8 blocks), followed by the unit's activation
-// records for those superblocks: two K-quant superblocks or one Q8_0 chunk of
-// 8 blocks per stage, 10.6-15.4 KB with the records, which gives rings of 14
-// (Q6_K), 19 (Q4_K) or 23 (Q8_0) stages. (Measured on configs[1] at 16
-// tokens: one superblock per stage is 13% slower per layer call; three per
-// stage, a 9-stage Q6_K ring, ran into the bounded empty-stage wait.)
+// records for those superblocks: kStageSB (4) K-quant superblocks -- or the
+// whole row when it has fewer -- or one Q8_0 chunk of 8 blocks per stage. The
+// bulk-copy engine's throughput grows with the size of its copies up to
+// ~18 KB (a B200 streaming probe: ~4 TB/s with 9.2 KB copies, 6.3-7 TB/s from
+// 18 KB), so a Q4_K stage of four superblocks (18.4 KB of weights) gives a
+// 9-stage ring; rows whose 4-superblock stages would leave no more than DW
+// stages (Q6_K at ff = 14336) take two per stage. (Measured on configs[1] at
+// 16 tokens: four superblocks per stage 5% faster per layer call than two;
+// one superblock per stage 13% slower than two.)
 DecodeGeom decode_geom(int t, int64_t cols) {
   DecodeGeom g = decode_geom_ks(t, cols, t == T_Q8_0 ? 1 : kStageSB);
   // Stages of more than two superblocks only while the ring keeps more than
