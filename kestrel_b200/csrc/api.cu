@@ -528,8 +528,8 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   if (fork) RC(fork_aux());
   if (any_large && mma_gu) {
     StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
-    alignas(64) unsigned char tmap[128];
-    if (make_tmap_f16(tmap, W.x16, A, d) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
+    MmaMaps tmap;
+    if (make_tmaps_f16(tmap, W.x16, A, d) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
     MmaArgs ma{};
     ma.part = W.mma_part;
     ma.tile_cnt = W.mma_cnt;
@@ -549,6 +549,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.out[1] = W.u;
     ma.out_stride = ff;
     ma.status = ctx->status;
+    ma.wide = (int64_t)A > 256LL * E;  // more than 256 rows per expert expected
     RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(ff, 128), lst));
     CKL();
   } else if (any_large) {
@@ -609,8 +610,8 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   if (fork) RC(fork_aux());
   if (any_large && mma_dn) {
     StageScope ss(ctx, KC_STAGE_DOWN_F32);
-    alignas(64) unsigned char tmap[128];
-    if (make_tmap_f16(tmap, W.act16, A, ff) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (act16) failed");
+    MmaMaps tmap;
+    if (make_tmaps_f16(tmap, W.act16, A, ff) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (act16) failed");
     MmaArgs ma{};
     ma.part = W.mma_part;
     ma.tile_cnt = W.mma_cnt;
@@ -628,6 +629,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.out[0] = W.y;
     ma.out_stride = d;
     ma.status = ctx->status;
+    ma.wide = (int64_t)A > 256LL * E;
     RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(d, 128), lst));
     CKL();
   } else if (any_large) {
@@ -748,8 +750,8 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
   } else if (!ctx->f32_prefill && mma_supported(D.t, D.cols, 1)) {
     launch_act_records(is_k(D.t), x, nullptr, nullptr, n, D.cols, nullptr, n, nullptr, W.x16, st);
     CKL();
-    alignas(64) unsigned char tmap[128];
-    if (make_tmap_f16(tmap, W.x16, n, D.cols) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
+    MmaMaps tmap;
+    if (make_tmaps_f16(tmap, W.x16, n, D.cols) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
     MmaArgs ma{};
     ma.part = W.mma_part;
     ma.tile_cnt = W.mma_cnt;
@@ -765,6 +767,7 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     ma.out[0] = out;
     ma.out_stride = out_stride;
     ma.status = ctx->status;
+    ma.wide = n > 256;
     RC(launch_mma_grouped(ma, tmap, ceil_div(n, kMmaTileN) * ceil_div(D.rows, 128), st));
   } else {
     a.list = M.large_list;

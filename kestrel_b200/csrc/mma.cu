@@ -42,24 +42,31 @@ constexpr int B_BYTES = MN * MK * 2;  // 32 KB
 __host__ __device__ constexpr int max_sbt_bytes(int t) { return t == T_Q4_K ? 4608 : t == T_Q6_K ? 6720 : 8704; }
 constexpr int M_RT = MM / kTileRows;  // row tiles per M tile
 
-__host__ __device__ constexpr int mma_raw_bytes(int t, int n_mat) {
-  return ((n_mat * M_RT * max_sbt_bytes(t) + 1023) / 1024) * 1024;
+// A work item is 128 weight rows (the MMA's M) of MI matrices x up to NT
+// 256-slot tiles, MI * NT <= 2 accumulators side by side in TMEM:
+//  * MI = 2, NT = 1: gate and up of one slot tile, which share its B tile;
+//  * MI = 1, NT = 2: one matrix for two slot tiles, so that every weight
+//    block is copied and dequantised once for up to 512 slots (prefill).
+__host__ __device__ constexpr int mma_raw_bytes(int t, int mi) {
+  return ((mi * M_RT * max_sbt_bytes(t) + 1023) / 1024) * 1024;
 }
-__host__ __device__ constexpr int mma_op_bytes(int n_mat) { return n_mat * A_BYTES + B_BYTES; }
+__host__ __device__ constexpr int mma_op_bytes(int mi, int nt) { return mi * A_BYTES + nt * B_BYTES; }
+__host__ __device__ constexpr bool mma_fits(int t, int mi, int nt, int ops) {
+  return ops * mma_op_bytes(mi, nt) + M_RAWS * mma_raw_bytes(t, mi) + 1024 <= 227 * 1024;
+}
 // Operand stages: three where they fit in 227 KB of shared memory, else two.
-__host__ __device__ constexpr int mma_ops(int t, int n_mat) {
-  return 3 * mma_op_bytes(n_mat) + M_RAWS * mma_raw_bytes(t, n_mat) + 1024 <= 227 * 1024 ? 3 : 2;
-}
+__host__ __device__ constexpr int mma_ops(int t, int mi, int nt) { return mma_fits(t, mi, nt, 3) ? 3 : 2; }
 struct MmaSmem {
   int op_bytes, raw_bytes, total;
 };
-__host__ __device__ inline MmaSmem mma_smem(int t, int n_mat) {
+__host__ __device__ inline MmaSmem mma_smem(int t, int mi, int nt) {
   MmaSmem s;
-  s.op_bytes = mma_op_bytes(n_mat);
-  s.raw_bytes = mma_raw_bytes(t, n_mat);
-  s.total = mma_ops(t, n_mat) * s.op_bytes + M_RAWS * s.raw_bytes + 1024;  // + alignment slack
+  s.op_bytes = mma_op_bytes(mi, nt);
+  s.raw_bytes = mma_raw_bytes(t, mi);
+  s.total = mma_ops(t, mi, nt) * s.op_bytes + M_RAWS * s.raw_bytes + 1024;  // + alignment slack
   return s;
 }
+constexpr int MMA_MAX_LIST = 1024;  // experts of one launch's tcgen05 list
 
 // ---- tcgen05 / TMA helpers --------------------------------------------------
 // Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row groups 1024 B
@@ -143,7 +150,10 @@ __device__ __forceinline__ float byte_f(uint32_t w, int i, float bias) {
 
 // Half `hf` (32 elements) of the 64-element K chunk kk of a row, per type.
 // Q4_K (quant.rs:138-155): y = (d*sc)*q - dmin*m; half 0 = sub-block 2kk (low
-// nibbles), half 1 = sub-block 2kk+1 (high nibbles).
+// nibbles), half 1 = sub-block 2kk+1 (high nibbles). d*sc has at most 17
+// significant bits (an f16 times a 6-bit scale), so (d*sc)*q (q < 16) is exact
+// in f32 and one fma(d*sc, q, -dmin*m) rounds exactly as the reference's
+// multiply then subtract.
 __device__ __forceinline__ void dq_q4k(const uint8_t* sbt, int rr, int kk, int hf, uint8_t* A, int m) {
   const uint4 hdr = *reinterpret_cast<const uint4*>(sbt + 16 * rr);
   const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
@@ -160,7 +170,7 @@ __device__ __forceinline__ void dq_q4k(const uint8_t* sbt, int rr, int kk, int h
     for (int h2 = 0; h2 < 2; ++h2) {
       const uint32_t nw = (hf ? (qw[2 * c + h2] >> 4) : qw[2 * c + h2]) & 0x0F0F0F0Fu;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[4 * h2 + i] = __fsub_rn(__fmul_rn(d1, byte_f(nw, i, 8388608.0f)), m1);
+      for (int i = 0; i < 4; ++i) v[4 * h2 + i] = __fmaf_rn(d1, byte_f(nw, i, 8388608.0f), -m1);
     }
     put8(A, m, 4 * hf + c, v);
   }
@@ -215,67 +225,107 @@ __device__ __forceinline__ void dq_q8_0(const uint8_t* cb, int nblk, int rr, int
   }
 }
 
-// ---- work tiles ---------------------------------------------------------------
-struct Tile {
-  int e, slot0, t0, nt, rt;
+struct MmaMapsDev {
+  CUtensorMap m[kMmaBoxes];
 };
-__device__ __forceinline__ Tile tile_of(const MmaArgs& a, int w, int row_tiles, int n_large) {
+static_assert(sizeof(MmaMapsDev) == sizeof(MmaMaps), "tensor map block");
+// The box (index, rows) for a tile of nt slots: the smallest of 16 .. 256 rows
+// that holds round16(nt).
+__device__ __forceinline__ int box_index(int nt) {
+  const int n16 = (nt + 15) / 16;  // 1 .. 16
+  return n16 <= 1 ? 0 : (n16 <= 2 ? 1 : (n16 <= 4 ? 2 : (n16 <= 8 ? 3 : 4)));
+}
+
+// ---- work tiles ---------------------------------------------------------------
+// Item w of a launch (before the split): the first of its MI matrices
+// m = (w % (NMAT / MI)) * MI, row tile rt, then the expert's group of up to
+// NT slot tiles. pp_s: prefix over the list of each expert's groups.
+struct Tile {
+  int e, m, rt, slot0, t0, np;
+  int nt[2];  // slots of tile p of the group (nt[1] = 0 when np == 1)
+};
+template <int NMAT, int MI, int NT>
+__device__ __forceinline__ Tile tile_of(const MmaArgs& a, const int* pp_s, int w, int row_tiles, int n_large) {
   Tile t;
-  const int tt = w / row_tiles;
+  constexpr int per = NMAT / MI;
+  t.m = (w % per) * MI;
+  w /= per;
   t.rt = w % row_tiles;
-  int lo = 0, hi = n_large - 1;  // last i with tt_prefix[i] <= tt
+  const int pi = w / row_tiles;
+  int lo = 0, hi = n_large - 1;  // last i with pp_s[i] <= pi
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (a.tt_prefix[mid] <= tt) lo = mid;
+    if (pp_s[mid] <= pi) lo = mid;
     else hi = mid - 1;
   }
   t.e = a.list[lo];
   t.slot0 = a.offsets[t.e];
   const int n = a.offsets[t.e + 1] - t.slot0;
-  t.t0 = (tt - a.tt_prefix[lo]) * MN;
-  t.nt = min(MN, n - t.t0);
+  t.t0 = (pi - pp_s[lo]) * NT * MN;
+  t.nt[0] = min(MN, n - t.t0);
+  t.nt[1] = NT > 1 ? max(0, min(MN, n - t.t0 - MN)) : 0;
+  t.np = t.nt[1] > 0 ? 2 : 1;
   return t;
 }
 
 // Named barrier among the dequantisation/epilogue warps only.
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(32 * M_DQW) : "memory"); }
 
-// Work items: (tile, split). With few tiles (decode-sized batches) the K range
-// of each tile is split over S work items so that more SMs stream weights; each
-// writes an f32 partial tile and the last one to finish (a per-tile counter)
-// adds the S partials in split order and stores the result.
+// Work items: (item, split). With few items (decode-sized batches) the K range
+// of each item is split over S work items so that more SMs stream weights;
+// each writes f32 partial tiles and the last one to finish (a per-item
+// counter) adds the S partials in split order and stores the result.
 __device__ __forceinline__ int split_count(const MmaArgs& a, int total, int nsb) {
   if (!a.part || total <= 0) return 1;
   const int s = min(nsb, (int)gridDim.x / total);
   return s >= 2 ? s : 1;
 }
 
-template <int T, int NMAT>
+template <int T, int NMAT, int MI, int NT>
 __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs a,
-                                                                     const __grid_constant__ CUtensorMap tmap_b) {
+                                                                     const __grid_constant__ MmaMapsDev maps) {
+  static_assert(MI * NT <= 2 && NMAT % MI == 0, "at most two accumulators of 256 columns");
   pdl_enter();
   extern __shared__ uint8_t msm_raw[];
-  constexpr int M_OPS = mma_ops(T, NMAT);
+  constexpr int M_OPS = mma_ops(T, MI, NT);
   __shared__ __align__(8) uint64_t raw_full[M_RAWS], raw_empty[M_RAWS], op_full[M_OPS_MAX], op_empty[M_OPS_MAX];
   __shared__ __align__(8) uint64_t acc_full, acc_empty;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int last_sh;
+  __shared__ int pp_s[MMA_MAX_LIST + 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_large = *a.n_list;
+  const int n_large = min(*a.n_list, MMA_MAX_LIST);
+  // Groups of up to NT slot tiles per expert, prefix over the list.
+  if (warp == 0) {
+    int run = 0;
+    for (int base = 0; base < n_large; base += 32) {
+      const int i = base + lane;
+      int c = i < n_large ? (a.tt_prefix[i + 1] - a.tt_prefix[i] + NT - 1) / NT : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, c, o);
+        if (lane >= o) c += v;
+      }
+      if (i < n_large) pp_s[i + 1] = run + c;
+      run += __shfl_sync(0xffffffffu, c, 31);
+    }
+    if (lane == 0) pp_s[0] = 0;
+  }
+  __syncthreads();
   const int row_tiles = (a.rows + MM - 1) / MM;
-  const int total = n_large > 0 ? a.tt_prefix[n_large] * row_tiles : 0;
+  const int total = n_large > 0 ? pp_s[n_large] * row_tiles * (NMAT / MI) : 0;
   const int nkc = a.cols / MK;
   const int nsb = tiled_nsb(T, a.cols);
   const int S = split_count(a, total, nsb);
   const int items = total * S;
   if ((int)blockIdx.x >= items) return;
-  const MmaSmem L = mma_smem(T, NMAT);
+  const MmaSmem L = mma_smem(T, MI, NT);
   uint8_t* msm = msm_raw + ((1024 - (smem_u32(msm_raw) & 1023)) & 1023);
   uint8_t* ops = msm;
   uint8_t* raws = msm + M_OPS * L.op_bytes;
   const int64_t tile_bytes = tiled_tile_bytes(T, a.cols);
   const int prows = (int)padded_rows(a.rows);
-  const uint32_t tcols = NMAT * MN;  // 256 or 512 TMEM columns
+  const uint32_t tcols = MI * NT * MN;  // 256 or 512 TMEM columns
   // K chunks [kc0, kc1) of split s: whole superblocks (4 chunks of 64).
   auto k_range = [&](int s, int& kc0, int& kc1) {
     kc0 = 4 * (s * nsb / S);
@@ -310,10 +360,13 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
     if (lane == 0) {
       int raw_it = 0, op_it = 0;
       for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
-        const Tile t = tile_of(a, w / S, row_tiles, n_large);
+        const Tile t = tile_of<NMAT, MI, NT>(a, pp_s, w / S, row_tiles, n_large);
         int kc0, kc1;
         k_range(w % S, kc0, kc1);
         const int n_rt = min(M_RT, (prows - MM * t.rt) / kTileRows);
+        // Only the rows each tile uses: boxes of 16 .. 256 rows.
+        int bx[2] = {box_index(t.nt[0]), t.np > 1 ? box_index(t.nt[1]) : 0};
+        const uint32_t b_bytes = (uint32_t)(MK * 2 * ((16 << bx[0]) + (t.np > 1 ? (16 << bx[1]) : 0)));
         for (int kc = kc0; kc < kc1 && ok; ++kc) {
           const int sb = kc >> 2;
           if ((kc & 3) == 0) {
@@ -323,11 +376,11 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
               break;
             }
             const uint32_t sbytes = (uint32_t)tiled_sbt_bytes(T, a.cols, sb);
-            mbar_expect_tx(&raw_full[r], sbytes * n_rt * NMAT);
+            mbar_expect_tx(&raw_full[r], sbytes * n_rt * MI);
             uint8_t* rbase = raws + r * L.raw_bytes;
 #pragma unroll
-            for (int mt = 0; mt < NMAT; ++mt) {
-              const uint8_t* src = a.w[mt] + (int64_t)(t.e - a.expert_base) * a.expert_stride +
+            for (int mt = 0; mt < MI; ++mt) {
+              const uint8_t* src = a.w[t.m + mt] + (int64_t)(t.e - a.expert_base) * a.expert_stride +
                                    (int64_t)(M_RT * t.rt) * tile_bytes + tiled_sb_offset(T, a.cols, sb);
               for (int x = 0; x < n_rt; ++x)
                 bulk_g2s(rbase + (mt * M_RT + x) * max_sbt_bytes(T), src + x * tile_bytes, sbytes, &raw_full[r]);
@@ -339,8 +392,10 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
             ok = false;
             break;
           }
-          mbar_expect_tx(&op_full[o], B_BYTES);
-          tma_load_2d(ops + o * L.op_bytes + NMAT * A_BYTES, &tmap_b, kc * MK, t.slot0 + t.t0, &op_full[o]);
+          mbar_expect_tx(&op_full[o], b_bytes);
+          for (int p = 0; p < t.np; ++p)
+            tma_load_2d(ops + o * L.op_bytes + MI * A_BYTES + p * B_BYTES, &maps.m[bx[p]], kc * MK,
+                        t.slot0 + t.t0 + p * MN, &op_full[o]);
           ++op_it;
         }
       }
@@ -352,11 +407,12 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
     if (lane == 0) {
       int op_it = 0, tile_it = 0;
       for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++tile_it) {
-        const Tile t = tile_of(a, w / S, row_tiles, n_large);
+        const Tile t = tile_of<NMAT, MI, NT>(a, pp_s, w / S, row_tiles, n_large);
         int kc0, kc1;
         k_range(w % S, kc0, kc1);
-        const int n = ((t.nt + 15) / 16) * 16;
-        const uint32_t idesc = f16_idesc(n);
+        uint32_t idesc[2];
+#pragma unroll
+        for (int p = 0; p < 2; ++p) idesc[p] = f16_idesc(((max(t.nt[p], 1) + 15) / 16) * 16);
         if (tile_it > 0 && !mbar_wait(&acc_empty, (tile_it - 1) & 1, a.status, W_MMA_ACC_EMPTY)) {
           ok = false;
           break;
@@ -370,14 +426,18 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
           }
           tc_fence_after();
           const uint32_t sa = smem_u32(ops + o * L.op_bytes);
-          const uint32_t sbb = sa + NMAT * A_BYTES;
+          const uint32_t sbb = sa + MI * A_BYTES;
 #pragma unroll
           for (int k16 = 0; k16 < MK / 16; ++k16) {
-            const uint64_t bd = sw128_desc(sbb + 32 * k16);
             const uint32_t acc = (kc > kc0 || k16 > 0) ? 1u : 0u;
 #pragma unroll
-            for (int mt = 0; mt < NMAT; ++mt)
-              umma_f16(tmem + mt * MN, sw128_desc(sa + mt * A_BYTES + 32 * k16), bd, idesc, acc);
+            for (int mt = 0; mt < MI; ++mt) {
+              const uint64_t ad = sw128_desc(sa + mt * A_BYTES + 32 * k16);
+#pragma unroll
+              for (int p = 0; p < NT; ++p)
+                if (p < t.np)
+                  umma_f16(tmem + (mt * NT + p) * MN, ad, sw128_desc(sbb + p * B_BYTES + 32 * k16), idesc[p], acc);
+            }
           }
           umma_commit(&op_empty[o]);
           ++op_it;
@@ -398,7 +458,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
     // work), so all of them reach the named barriers below equally often.
     for (int w = blockIdx.x; w < items; w += gridDim.x, ++tile_it) {
       const int tile = w / S, split = w % S;
-      const Tile t = tile_of(a, tile, row_tiles, n_large);
+      const Tile t = tile_of<NMAT, MI, NT>(a, pp_s, tile, row_tiles, n_large);
       int kc0, kc1;
       k_range(split, kc0, kc1);
       int r = 0;
@@ -411,14 +471,13 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
         const int o = op_it % M_OPS;
         if (ok && op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status, W_MMA_OP_EMPTY_D)) ok = false;
         if (ok) {
-          uint8_t* A = ops + o * L.op_bytes;
-          const uint8_t* rb = raws + r * L.raw_bytes;
 #pragma unroll
-          for (int mt = 0; mt < NMAT; ++mt) {
-            const uint8_t* sbt = rb + (mt * M_RT + rt_local) * max_sbt_bytes(T);
-            if (T == T_Q4_K) dq_q4k(sbt, rr, kk, hf, A + mt * A_BYTES, m);
-            else if (T == T_Q6_K) dq_q6k(sbt, rr, kk, hf, A + mt * A_BYTES, m);
-            else dq_q8_0(sbt, min(8, a.cols / 32 - 8 * sb), rr, kk, hf, A + mt * A_BYTES, m);
+          for (int mt = 0; mt < MI; ++mt) {
+            uint8_t* A = ops + o * L.op_bytes + mt * A_BYTES;
+            const uint8_t* sbt = raws + r * L.raw_bytes + (mt * M_RT + rt_local) * max_sbt_bytes(T);
+            if (T == T_Q4_K) dq_q4k(sbt, rr, kk, hf, A, m);
+            else if (T == T_Q6_K) dq_q6k(sbt, rr, kk, hf, A, m);
+            else dq_q8_0(sbt, min(8, a.cols / 32 - 8 * sb), rr, kk, hf, A, m);
           }
         }
         fence_async_smem();
@@ -432,39 +491,41 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
         }
       }
       // Epilogue: rows of this warp's TMEM quadrant (warp % 4); the two warps
-      // of a quadrant take alternate 16-column blocks.
+      // of a quadrant take alternate 16-column blocks of each slot tile.
       if (ok && !mbar_wait(&acc_full, tile_it & 1, a.status, W_MMA_ACC_FULL)) ok = false;
       tc_fence_after();
       const int quad = warp & 3, colh = (warp - 2) >> 2;
       const int rl = quad * 32 + lane;
       const int row = MM * t.rt + rl;
-      const int n = ((t.nt + 15) / 16) * 16;
       if (ok) {
-        for (int c0 = 16 * colh; c0 < n; c0 += 32) {
 #pragma unroll
-          for (int mt = 0; mt < NMAT; ++mt) {
-            float v[16];
-            tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + mt * MN + c0, v);
-            if (S == 1) {
-              if (row < a.rows) {
+        for (int mt = 0; mt < MI; ++mt)
+          for (int p = 0; p < t.np; ++p) {
+            const int n = ((t.nt[p] + 15) / 16) * 16;
+            float* outm = a.out[t.m + mt];
+            for (int c0 = 16 * colh; c0 < n; c0 += 32) {
+              float v[16];
+              tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (mt * NT + p) * MN + c0, v);
+              if (S == 1) {
+                if (row < a.rows) {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i)
+                    if (c0 + i < t.nt[p]) outm[(int64_t)(t.slot0 + t.t0 + p * MN + c0 + i) * a.out_stride + row] = v[i];
+                }
+              } else {
+                float* pp = a.part + (((int64_t)w * MI + mt) * NT + p) * (MM * MN);
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
-                  if (c0 + i < t.nt) a.out[mt][(int64_t)(t.slot0 + t.t0 + c0 + i) * a.out_stride + row] = v[i];
+                  if (c0 + i < t.nt[p]) pp[(c0 + i) * MM + rl] = v[i];
               }
-            } else {
-              float* pp = a.part + ((int64_t)w * NMAT + mt) * (MM * MN);
-#pragma unroll
-              for (int i = 0; i < 16; ++i)
-                if (c0 + i < t.nt) pp[(c0 + i) * MM + rl] = v[i];
             }
           }
-        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty);
       if (S > 1) {
-        // Last split of this tile adds the partials in split order.
+        // Last split of this item adds the partials in split order.
         __threadfence();
         epi_sync();
         if (tid == 64) last_sh = atomicAdd(&a.tile_cnt[tile], 1) == S - 1 ? 1 : 0;
@@ -472,15 +533,16 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
         if (last_sh) {
           __threadfence();
           if (ok && row < a.rows) {
-            for (int c = colh; c < t.nt; c += 2) {
 #pragma unroll
-              for (int mt = 0; mt < NMAT; ++mt) {
-                float acc = 0.f;
-                for (int s2 = 0; s2 < S; ++s2)
-                  acc = __fadd_rn(acc, __ldcg(a.part + ((int64_t)(tile * S + s2) * NMAT + mt) * (MM * MN) + c * MM + rl));
-                a.out[mt][(int64_t)(t.slot0 + t.t0 + c) * a.out_stride + row] = acc;
-              }
-            }
+            for (int mt = 0; mt < MI; ++mt)
+              for (int p = 0; p < t.np; ++p)
+                for (int c = colh; c < t.nt[p]; c += 2) {
+                  float acc = 0.f;
+                  for (int s2 = 0; s2 < S; ++s2)
+                    acc = __fadd_rn(acc, __ldcg(a.part + (((int64_t)(tile * S + s2) * MI + mt) * NT + p) * (MM * MN) +
+                                                 c * MM + rl));
+                  a.out[t.m + mt][(int64_t)(t.slot0 + t.t0 + p * MN + c) * a.out_stride + row] = acc;
+                }
           }
           if (tid == 64) a.tile_cnt[tile] = 0;  // ready for the next launch
         }
@@ -495,7 +557,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
 // ---- host side ------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
-int make_tmap_f16(void* map_out, const void* ptr, int64_t rows, int64_t cols) {
+static int make_tmap_f16(void* map_out, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
   if (!g_encode) {
     cudaDriverEntryPointQueryResult q;
     void* fn = nullptr;
@@ -507,7 +569,7 @@ int make_tmap_f16(void* map_out, const void* ptr, int64_t rows, int64_t cols) {
   if (((uintptr_t)ptr & 15) || (cols * 2) % 16) return KC_ERR_SHAPE;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)std::max<int64_t>(rows, 1)};
   cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
-  cuuint32_t box[2] = {MK, MN};
+  cuuint32_t box[2] = {MK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(reinterpret_cast<CUtensorMap*>(map_out), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                         const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -516,39 +578,58 @@ int make_tmap_f16(void* map_out, const void* ptr, int64_t rows, int64_t cols) {
   return r == CUDA_SUCCESS ? KC_OK : KC_ERR_CUDA;
 }
 
-bool mma_supported(int t, int64_t cols, int n_mat) {
-  if (!(t == T_Q4_K || t == T_Q6_K || t == T_Q8_0) || cols % MK != 0) return false;
-  return mma_smem(t, n_mat).total <= 227 * 1024;
+int make_tmaps_f16(MmaMaps& maps, const void* ptr, int64_t rows, int64_t cols) {
+  for (int i = 0; i < kMmaBoxes; ++i) {
+    const int rc = make_tmap_f16(maps.m[i], ptr, rows, cols, 16 << i);
+    if (rc != KC_OK) return rc;
+  }
+  return KC_OK;
 }
 
-template <int T, int NMAT>
-static int launch_t(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st, int max_ctas) {
-  const MmaSmem L = mma_smem(T, NMAT);
+bool mma_supported(int t, int64_t cols, int n_mat) {
+  if (!(t == T_Q4_K || t == T_Q6_K || t == T_Q8_0) || cols % MK != 0) return false;
+  return n_mat == 2 ? mma_fits(t, 2, 1, 2) : mma_fits(t, 1, 1, 2);
+}
+
+template <int T, int NMAT, int MI, int NT>
+static int launch_t(const MmaArgs& a, const MmaMaps& maps, int max_tiles, cudaStream_t st, int max_ctas) {
+  const MmaSmem L = mma_smem(T, MI, NT);
   static PerDeviceOnce attr;
-  if (smem_attr_once(attr, mma_grouped_kernel<T, NMAT>, L.total) != cudaSuccess) return KC_ERR_CUDA;
+  if (smem_attr_once(attr, mma_grouped_kernel<T, NMAT, MI, NT>, L.total) != cudaSuccess) return KC_ERR_CUDA;
   // With a split-K workspace every SM gets a CTA (the kernel splits K when the
   // batch has few tiles); otherwise one CTA per tile at most.
   const int cap = max_ctas > 0 ? std::min(max_ctas, num_sms()) : num_sms();
   const int grid = a.part ? cap : std::max(1, std::min(cap, max_tiles));
-  launch_k(mma_grouped_kernel<T, NMAT>, grid, M_THREADS, (size_t)L.total, st, a,
-           *reinterpret_cast<const CUtensorMap*>(tmap));
+  launch_k(mma_grouped_kernel<T, NMAT, MI, NT>, grid, M_THREADS, (size_t)L.total, st, a,
+           *reinterpret_cast<const MmaMapsDev*>(&maps));
   return KC_OK;
 }
 
-size_t mma_part_bytes() { return (size_t)num_sms() * 2 * MM * MN * sizeof(float); }
+// Item shape per type and launch: gate/up pairs (MI = 2) unless a.wide asks
+// for two slot tiles per weight block; single matrices two tiles wide when
+// a.wide and shared memory allows.
+template <int T>
+static int launch_type(const MmaArgs& a, const MmaMaps& maps, int max_tiles, cudaStream_t st, int max_ctas) {
+  if (a.n_mat == 2) {
+    if constexpr (mma_fits(T, 1, 2, 2))
+      if (a.wide) return launch_t<T, 2, 1, 2>(a, maps, max_tiles, st, max_ctas);
+    if constexpr (mma_fits(T, 2, 1, 2)) return launch_t<T, 2, 2, 1>(a, maps, max_tiles, st, max_ctas);
+    return KC_ERR_SHAPE;
+  }
+  if constexpr (mma_fits(T, 1, 2, 2))
+    if (a.wide) return launch_t<T, 1, 1, 2>(a, maps, max_tiles, st, max_ctas);
+  return launch_t<T, 1, 1, 1>(a, maps, max_tiles, st, max_ctas);
+}
+
+size_t mma_part_bytes() { return (size_t)num_sms() * 2 * MM * MN * sizeof(float); }  // MI * NT <= 2 per item
 size_t mma_cnt_bytes() { return (size_t)num_sms() * sizeof(int); }
 
-int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st, int max_ctas) {
+int launch_mma_grouped(const MmaArgs& a, const MmaMaps& maps, int max_tiles, cudaStream_t st, int max_ctas) {
   if (max_tiles <= 0) return KC_OK;
   if (!mma_supported(a.type, a.cols, a.n_mat)) return KC_ERR_SHAPE;
-  if (a.n_mat == 2) {
-    if (a.type == T_Q4_K) return launch_t<T_Q4_K, 2>(a, tmap, max_tiles, st, max_ctas);
-    if (a.type == T_Q6_K) return launch_t<T_Q6_K, 2>(a, tmap, max_tiles, st, max_ctas);
-    return launch_t<T_Q8_0, 2>(a, tmap, max_tiles, st, max_ctas);
-  }
-  if (a.type == T_Q4_K) return launch_t<T_Q4_K, 1>(a, tmap, max_tiles, st, max_ctas);
-  if (a.type == T_Q6_K) return launch_t<T_Q6_K, 1>(a, tmap, max_tiles, st, max_ctas);
-  return launch_t<T_Q8_0, 1>(a, tmap, max_tiles, st, max_ctas);
+  if (a.type == T_Q4_K) return launch_type<T_Q4_K>(a, maps, max_tiles, st, max_ctas);
+  if (a.type == T_Q6_K) return launch_type<T_Q6_K>(a, maps, max_tiles, st, max_ctas);
+  return launch_type<T_Q8_0>(a, maps, max_tiles, st, max_ctas);
 }
 
 }  // namespace kc

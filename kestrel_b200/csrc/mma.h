@@ -25,17 +25,26 @@ struct MmaArgs {
   // (zero before the first launch; each launch leaves them zero).
   float* part;
   int* tile_cnt;
+  // Prefer items of one matrix x two 256-slot tiles (each weight block
+  // dequantised once for up to 512 slots) over gate+up pairs x one tile: set
+  // when experts are expected to hold more than 256 rows.
+  int wide;
 };
 // Bytes of the split-K workspace a launch may use: partial tiles for one work
 // item per SM, and one counter per SM.
 size_t mma_part_bytes();
 size_t mma_cnt_bytes();
 
-// 128-byte CUtensorMap for an f16 row-major [rows, cols] activation matrix,
-// box 64 x kMmaTileN, 128B swizzle.
-int make_tmap_f16(void* map_out, const void* ptr, int64_t rows, int64_t cols);
+// CUtensorMaps (128 bytes each) of an f16 row-major [rows, cols] activation
+// matrix, 128B swizzle, boxes of 64 columns x 16, 32, 64, 128 and 256 rows: a
+// work tile loads the smallest box that holds its slots.
+constexpr int kMmaBoxes = 5;
+struct MmaMaps {
+  alignas(64) unsigned char m[kMmaBoxes][128];
+};
+int make_tmaps_f16(MmaMaps& maps, const void* ptr, int64_t rows, int64_t cols);
 bool mma_supported(int t, int64_t cols, int n_mat);
 // max_ctas > 0: at most that many CTAs (the kernel splits K over what it gets).
-int launch_mma_grouped(const MmaArgs& a, const void* tmap, int max_tiles, cudaStream_t st, int max_ctas = 0);
+int launch_mma_grouped(const MmaArgs& a, const MmaMaps& maps, int max_tiles, cudaStream_t st, int max_ctas = 0);
 
 }  // namespace kc
