@@ -498,7 +498,7 @@ def run_ours(args):
     # same kernel on the profile_layer B=16 case, as a ratio to that launch's
     # algorithmic bytes (profiles/decode_kernel_c1_b16.md), scaled to this
     # launch's algorithmic bytes. Traffic grows with the experts served.
-    traffic_ratio = {"gate_up_int8": 1.031, "down_int8": 1.037}
+    traffic_ratio = {"gate_up_int8": 1.036, "down_int8": 1.033}
     traffic = (dom_bytes / dom_calls) * traffic_ratio[dom] if dom in traffic_ratio and dom_calls else None
     traffic_src = ("ncu dram read+write / algorithmic bytes of this kernel on the B=16 profile case "
                    "(profiles/decode_kernel_c1_b16.md), times this launch's algorithmic bytes"
