@@ -35,20 +35,21 @@ __device__ void dispatch_small(const int* __restrict__ ids, const float* __restr
 
 constexpr int RL_E = 8, RL_T = 4, RL_KC = 1024;
 constexpr int RL_ROW = RL_KC + 8;  // padded shared row: the 4 expert rows a warp reads hit distinct banks
-constexpr int RL_THREADS = RL_E * RL_T * 8;
-constexpr size_t rl_smem(int rt) { return 2 * (size_t)(RL_E + rt) * RL_ROW * sizeof(float); }
+constexpr size_t rl_smem(int rt, int re) { return 2 * (size_t)(re + rt) * RL_ROW * sizeof(float); }
 
-template <bool GEMM, int RT>
-__global__ void __launch_bounds__(RL_E * RT * 8) router_logits_kernel(const float* __restrict__ w, int64_t ws, int E,
-                                                                      int d, const float* __restrict__ h, int n_tok,
-                                                                      float* __restrict__ logits, int* status) {
+// RE expert rows x RT tokens per block. Decode-sized batches (n < 4) take one
+// expert row per block, so that the router matrix is read by E blocks.
+template <bool GEMM, int RT, int RE = RL_E>
+__global__ void __launch_bounds__(RE * RT * 8) router_logits_kernel(const float* __restrict__ w, int64_t ws, int E,
+                                                                    int d, const float* __restrict__ h, int n_tok,
+                                                                    float* __restrict__ logits, int* status) {
   pdl_enter();
-  extern __shared__ __align__(128) float rsm[];  // [2][RL_E + RT][RL_ROW]
+  extern __shared__ __align__(128) float rsm[];  // [2][RE + RT][RL_ROW]
   __shared__ __align__(8) uint64_t full[2];
   const int tid = threadIdx.x, j = tid & 7, grp = tid >> 3;
-  const int er = grp % RL_E, tr = grp / RL_E;
-  const int e0 = blockIdx.x * RL_E, s0 = blockIdx.y * RT;
-  const int ne = min(RL_E, E - e0), nt = min(RT, n_tok - s0);
+  const int er = grp % RE, tr = grp / RE;
+  const int e0 = blockIdx.x * RE, s0 = blockIdx.y * RT;
+  const int ne = min(RE, E - e0), nt = min(RT, n_tok - s0);
   const int erc = min(er, ne - 1), trc = min(tr, nt - 1);
   const int e = e0 + erc, s = s0 + trc;
   const bool valid = er < ne && tr < nt;
@@ -71,12 +72,12 @@ __global__ void __launch_bounds__(RL_E * RT * 8) router_logits_kernel(const floa
   }
   __syncthreads();
   auto issue = [&](int c) {
-    float* buf = rsm + (c & 1) * (RL_E + RT) * RL_ROW;
+    float* buf = rsm + (c & 1) * (RE + RT) * RL_ROW;
     const int k0 = c * RL_KC, kn = min(RL_KC, d - k0);
     const uint32_t rb = (uint32_t)kn * 4;
     mbar_expect_tx(&full[c & 1], rb * (ne + nt));
     for (int r = 0; r < ne; ++r) bulk_g2s(buf + r * RL_ROW, w + (int64_t)(e0 + r) * ws + k0, rb, &full[c & 1]);
-    for (int r = 0; r < nt; ++r) bulk_g2s(buf + (RL_E + r) * RL_ROW, h + (int64_t)(s0 + r) * d + k0, rb, &full[c & 1]);
+    for (int r = 0; r < nt; ++r) bulk_g2s(buf + (RE + r) * RL_ROW, h + (int64_t)(s0 + r) * d + k0, rb, &full[c & 1]);
   };
   float a0 = 0.f, a1 = 0.f;
   if (bulk_ok) {
@@ -86,9 +87,9 @@ __global__ void __launch_bounds__(RL_E * RT * 8) router_logits_kernel(const floa
     }
     for (int c = 0; c < nchunk; ++c) {
       mbar_wait(&full[c & 1], (c >> 1) & 1, status, W_ROUTER);
-      const float* buf = rsm + (c & 1) * (RL_E + RT) * RL_ROW;
+      const float* buf = rsm + (c & 1) * (RE + RT) * RL_ROW;
       const float* wr = buf + erc * RL_ROW + j;
-      const float* xr = buf + (RL_E + trc) * RL_ROW + j;
+      const float* xr = buf + (RE + trc) * RL_ROW + j;
       const int k0 = c * RL_KC, kn = min(RL_KC, n8 - k0);  // k0 is an even number of 8-chunks
       int cc = 0;
       for (; cc + 64 <= kn; cc += 64) {
@@ -128,19 +129,27 @@ __global__ void __launch_bounds__(RL_E * RT * 8) router_logits_kernel(const floa
 void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int d, const float* h, int n_tok,
                           float* logits, int* status, cudaStream_t st, bool force_dot) {
   if (n_tok <= 0) return;
-  static PerDeviceOnce attr_gemm, attr_dot;
-  const size_t smem = rl_smem(RL_T);
+  static PerDeviceOnce attr_gemm, attr_dot, attr_dot1;
+  const size_t smem = rl_smem(RL_T, RL_E);
   smem_attr_once(attr_gemm, router_logits_kernel<true, RL_T>, (int)smem);
   smem_attr_once(attr_dot, router_logits_kernel<false, RL_T>, (int)smem);
-  dim3 grid(ceil_div(E, RL_E), ceil_div(n_tok, RL_T));
   // quant::matmul's dispatch (quant.rs:241): the GEMM path needs >= 4 rows and
   // d % 8 == 0; otherwise quant::dot per output.
-  if (!force_dot && n_tok >= 4 && d % 8 == 0)
-    launch_k(router_logits_kernel<true, RL_T>, grid, RL_THREADS, smem, st, w, row_stride_floats, E, d, h, n_tok,
+  if (!force_dot && n_tok >= 4 && d % 8 == 0) {
+    dim3 grid(ceil_div(E, RL_E), ceil_div(n_tok, RL_T));
+    launch_k(router_logits_kernel<true, RL_T>, grid, RL_E * RL_T * 8, smem, st, w, row_stride_floats, E, d, h, n_tok,
              logits, status);
-  else
-    launch_k(router_logits_kernel<false, RL_T>, grid, RL_THREADS, smem, st, w, row_stride_floats, E, d, h,
+  } else if (n_tok < 4) {
+    // One expert row and up to 4 tokens per block: E blocks.
+    const size_t smem1 = rl_smem(RL_T, 1);
+    smem_attr_once(attr_dot1, router_logits_kernel<false, RL_T, 1>, (int)smem1);
+    launch_k(router_logits_kernel<false, RL_T, 1>, dim3(E, 1), RL_T * 8, smem1, st, w, row_stride_floats, E, d, h,
              n_tok, logits, status);
+  } else {
+    dim3 grid(ceil_div(E, RL_E), ceil_div(n_tok, RL_T));
+    launch_k(router_logits_kernel<false, RL_T>, grid, RL_E * RL_T * 8, smem, st, w, row_stride_floats, E, d, h,
+             n_tok, logits, status);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -665,7 +674,8 @@ void launch_dense_meta(int n, const DispatchOut& o, cudaStream_t st, bool rows) 
 // ---------------------------------------------------------------------------
 // Combine (transformer.rs:566-570): out[s] = sum over the token's experts in
 // ascending expert id of w * y, each step a separate multiply and add, from
-// +0.0. One block per token.
+// +0.0. Block (token, column slice): CB_THREADS threads x 4 columns; every
+// block orders its token's selections itself (k <= RT_MAXK <= CB_THREADS).
 __global__ void combine_kernel(const float* __restrict__ y, const int* __restrict__ tok_slot,
                                const int* __restrict__ ids, const float* __restrict__ w, int k, int d,
                                float* __restrict__ out) {
@@ -692,7 +702,8 @@ __global__ void combine_kernel(const float* __restrict__ y, const int* __restric
     sw[rank] = wj;
   }
   __syncthreads();
-  for (int c = threadIdx.x * 4; c < d; c += blockDim.x * 4) {
+  const int c_end = min(d, (int)(blockIdx.y + 1) * 4 * (int)blockDim.x);
+  for (int c = (int)blockIdx.y * 4 * blockDim.x + threadIdx.x * 4; c < c_end; c += blockDim.x * 4) {
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < k; ++j) {
       float4 v = *reinterpret_cast<const float4*>(y + (int64_t)ss[j] * d + c);
@@ -706,10 +717,15 @@ __global__ void combine_kernel(const float* __restrict__ y, const int* __restric
   }
 }
 
+constexpr int CB_THREADS = 64;
+static_assert(RT_MAXK <= CB_THREADS, "one thread per selection");
 void launch_combine(const float* y, const int* tok_slot, const int* ids, const float* w, int n_tok, int k, int d,
                     float* out, cudaStream_t st) {
   if (n_tok <= 0) return;
-  launch_k(combine_kernel, n_tok, 256, 0, st, y, tok_slot, ids, w, k, d, out);
+  // Column slices of 256 floats, so that a decode-sized batch spreads over
+  // many SMs (the k rows each slice reads are its whole cost).
+  launch_k(combine_kernel, dim3(n_tok, ceil_div(d, 4 * CB_THREADS)), CB_THREADS, 0, st, y, tok_slot, ids, w, k, d,
+           out);
 }
 
 // ---------------------------------------------------------------------------
