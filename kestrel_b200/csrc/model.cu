@@ -80,12 +80,40 @@ void launch_embed(const uint8_t* E, int t, int64_t row_bytes, const uint32_t* to
 }
 
 // 1 / sqrt(sum / dim + eps) of the squares sq[0..dim) (16-byte aligned) folded
-// in order from -0.0 (Rust's f32 Sum, transformer.rs:333) by one warp: per
-// pass of 1024 squares, lane l holds squares 32 l .. 32 l + 31 in registers,
-// and the running sum visits the lanes in order (shuffled from lane to lane),
-// so the chain of dependent adds never waits on a shared-memory load.
+// in order from -0.0 (Rust's f32 Sum, transformer.rs:333) by one warp. For
+// dim % 32 == 0 lane 0 runs the whole chain, reading the squares 32 at a time
+// with the next 32 requested before the current ones are added, so the chain
+// of dependent adds neither waits on a shared-memory load nor hands the sum
+// from lane to lane. Otherwise, per pass of 1024 squares, lane l holds squares
+// 32 l .. 32 l + 31 in registers and the running sum visits the lanes in order.
 __device__ float rms_inv_warp(const float* sq, int dim, float eps, int lane) {
   float ss = -0.0f;
+  if (dim % 32 == 0) {
+    if (lane == 0) {
+      const float4* q = reinterpret_cast<const float4*>(sq);
+      float4 cur[8], nxt[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) cur[u] = q[u];
+      for (int i = 0; i < dim / 4; i += 8) {
+        if (i + 8 < dim / 4) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) nxt[u] = q[i + 8 + u];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          ss = __fadd_rn(ss, cur[u].x);
+          ss = __fadd_rn(ss, cur[u].y);
+          ss = __fadd_rn(ss, cur[u].z);
+          ss = __fadd_rn(ss, cur[u].w);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+      }
+    }
+    ss = __shfl_sync(0xffffffffu, ss, 0);
+    ss = __fdiv_rn(ss, (float)dim);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, eps)));
+  }
   for (int base = 0; base < dim; base += 1024) {
     const int n = min(1024, dim - base);
     float v[32];
