@@ -12,6 +12,11 @@
  *                            (crates/kestrel-backends/src/lib.rs:125-187)
  *   kc_upload_experts        ExpertStore::preload_all + ExpertBuf::part
  *                            (crates/kestrel-memory/src/expert.rs:620-641, 62-76)
+ *   kc_upload_experts_streamed / kc_expert_cache_reserve / kc_expert_prefetch /
+ *   kc_expert_cache_stats / kc_expert_cache_decay
+ *                            ExpertStore::new / request / get / prefetch /
+ *                            metrics / decay (expert.rs:223-551) with HBM
+ *                            slots as the cache
  *   kc_upload_router         the router tensor ffn_gate_inp.weight read through
  *                            Lease::tensor (crates/kestrel-memory/src/store.rs:233)
  *   kc_upload_dense          WeightStore::lease + Lease::tensor for a dense weight
@@ -134,6 +139,71 @@ KC_API int kc_upload_shared_expert(kc_ctx* ctx, int layer, int ff_shared, int d,
                                    int t_up, const void* up, int t_down, const void* down, const float* gate_inp,
                                    int src_on_device);
 
+/* ---- host-streamed experts (models larger than HBM) ----------------------
+   ExpertStore's expert cache (crates/kestrel-memory/src/expert.rs:305-551)
+   with HBM as the cache and pinned host memory as the backing store, for
+   models whose experts do not all fit on the GPU.
+
+   kc_upload_experts_streamed takes the same arguments as kc_upload_experts
+   (ExpertStore::new's per-layer tensors, expert.rs:223) but keeps the
+   converted experts in pinned host memory. Every kc_moe_ffn* call of such a
+   layer routes on the GPU, reads the routed ids back (one synchronisation),
+   copies the experts it routes to that are not resident into HBM slots
+   (ExpertStore::request + get, expert.rs:358-424, 523-537: hits, misses,
+   evictions by the LFRU or LRU score of expert.rs:305-331) and computes the
+   same results, bit for bit, as the resident layer. A call's experts are
+   resident all at once: capacity + scratch must be at least the number of
+   distinct experts one call routes to. Calls of streamed layers cannot be
+   captured into a CUDA graph (kc_model_generate then runs its steps
+   eagerly). Every streamed layer has the same shape (d, ff, types). Not
+   available with expert parallelism.
+
+   kc_expert_cache_reserve sets `capacity` cache slots and `scratch` slots
+   for experts the cache does not admit (ExpertStore::new's capacity and
+   scratch_slots), and the policy; until it is called a context holds one
+   layer's experts (capacity n_expert, no scratch, LFRU). It forgets what the
+   slots held and resets the counters.
+
+   kc_expert_prefetch is ExpertStore::prefetch (expert.rs:451-521): starts
+   copying experts of `layer` that are not resident, on a copy stream, when
+   the cache admits them; never waits. The whole-model path (kc_model_*)
+   calls it itself, as the router lookahead of transformer.rs:432-436,
+   498-508 does: for steps of at most 4 rows, the next streamed layer's
+   experts are predicted from the current post-attention state
+   (KC_OPT_LOOKAHEAD, on by default).
+
+   kc_expert_cache_stats writes up to n counters (ExpertMetrics,
+   expert.rs:127-153), indexed by KC_XS_*. kc_expert_cache_decay halves the
+   experts' heat (ExpertStore::decay, expert.rs:545-551). */
+enum { KC_EXPERT_POLICY_LFRU = 0, KC_EXPERT_POLICY_LRU = 1 };
+enum {
+  KC_XS_CAPACITY = 0,
+  KC_XS_CACHED = 1,
+  KC_XS_REQUESTS = 2,
+  KC_XS_HITS = 3,
+  KC_XS_LATE = 4,            /* resident but its prefetch copy still landing */
+  KC_XS_MISSES = 5,
+  KC_XS_SCRATCH_LOADS = 6,
+  KC_XS_BYTES_READ = 7,      /* bytes copied host -> HBM                      */
+  KC_XS_PREFETCH_ISSUED = 8,
+  KC_XS_PREFETCH_USED = 9,
+  KC_XS_PREFETCH_WASTED = 10,
+  KC_XS_EVICTIONS = 11,
+  KC_XS_LOOKAHEAD_PREDICTED = 12,
+  KC_XS_LOOKAHEAD_CORRECT = 13,
+  KC_XS_READS = 14,          /* host -> HBM copies issued                     */
+  KC_XS_FORCED = 15,         /* admitted without the policy's consent: scratch slots exhausted */
+  KC_XS_SCRATCH = 16,
+  KC_XS_N = 17
+};
+KC_API int kc_upload_experts_streamed(kc_ctx* ctx, int layer, int n_expert, int d, int ff, int t_gate,
+                                      const void* gate, int t_up, const void* up, int t_down, const void* down,
+                                      int src_on_device);
+KC_API int kc_expert_cache_reserve(kc_ctx* ctx, int capacity, int scratch, int policy);
+KC_API int kc_expert_prefetch(kc_ctx* ctx, int layer, const int32_t* experts, int n);
+KC_API int kc_expert_cache_stats(const kc_ctx* ctx, uint64_t* out, int n);
+KC_API int kc_expert_cache_decay(kc_ctx* ctx);
+
 /* ---- hot path ----------------------------------------------------------- */
 
 /* Transformer::moe_ffn for `layer`: h [n_tok, d] f32 -> out [n_tok, d] f32.
@@ -196,7 +266,8 @@ enum {
   KC_STAGE_DOWN_INT8 = 7,
   KC_STAGE_DOWN_F32 = 8,
   KC_STAGE_COMBINE = 9,
-  KC_N_STAGES = 10
+  KC_STAGE_EXPERT_LOAD = 10, /* host-streamed layers: ids read back, expert copies */
+  KC_N_STAGES = 11
 };
 KC_API int kc_profile_enable(kc_ctx* ctx, int on);
 KC_API int kc_profile_read(kc_ctx* ctx, double* stage_ms, int64_t* stage_calls, int n_stages);
@@ -237,7 +308,10 @@ enum {
   /* value 1: products with n >= 4 rows (prefill) run on CUDA cores in f32 on
      exactly dequantised weights, as quant::matmul's gemm_f32 path does,
      instead of tcgen05 with f16 operands (0, the default). */
-  KC_OPT_F32_PREFILL = 1
+  KC_OPT_F32_PREFILL = 1,
+  /* value 1 (default): the whole-model path predicts the next host-streamed
+     layer's experts and prefetches them (router lookahead); 0: off. */
+  KC_OPT_LOOKAHEAD = 2
 };
 KC_API int kc_set_option(kc_ctx* ctx, int option, int value);
 

@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "decode.h"
+#include "expert_cache.h"
 #include "ep.h"
 #include "kernels.h"
 #include "mma.h"
@@ -28,12 +29,22 @@ struct Layer {
   // Routed experts: expert e (global id) lives at (e - first_expert) in the
   // stacked device buffers.
   bool has_experts = false;
+  int id = -1;  // layer index
   int n_expert = 0, first_expert = 0, n_local = 0, d = 0, ff = 0;
   int t_gate = 0, t_up = 0, t_down = 0;
   int64_t mb_gate = 0, mb_down = 0;  // device bytes of one expert's gate (= up) / down matrix
   uint8_t* gate = nullptr;
   uint8_t* up = nullptr;
   uint8_t* down = nullptr;
+  // Host-streamed experts (kc_upload_experts_streamed): every expert's gate,
+  // up and down in the device layout, one pinned host block of slot_bytes per
+  // expert ([gate | up | down] at 0, up_off, down_off), copied per call into
+  // the context's HBM slots. `slot` is set only on the per-call copy of the
+  // layer that the kernels see (expert e at slot[e]).
+  bool streamed = false;
+  uint8_t* host = nullptr;
+  int64_t slot_bytes = 0, up_off = 0, down_off = 0;
+  const int* slot = nullptr;
   // Router (ffn_gate_inp.weight) and MoeInfo options.
   bool has_router = false;
   float* router = nullptr;
@@ -139,6 +150,32 @@ struct Prof {
 
 struct Model;  // the dense decode path of a whole model (kc_model_*)
 
+// Host-streamed experts (kc_upload_experts_streamed): the HBM slots a call's
+// experts are copied into, their bookkeeping (expert_cache.h), and the
+// buffers of the per-call slot table and the routed ids read back to the host.
+struct ExpertStreams {
+  ExpertCache cache;
+  int capacity = -1, scratch = 0;  // slots; capacity -1: not reserved (default at first use)
+  ExpertPolicy policy = ExpertPolicy::Lfru;
+  int64_t slot_bytes = 0;          // one expert's [gate | up | down]; shared by every streamed layer
+  uint8_t* arena = nullptr;        // [capacity + scratch][slot_bytes]
+  int* slot_dev = nullptr;         // slot table of the current call, [table_e]
+  int* slot_host = nullptr;        // its pinned source
+  int table_e = 0;
+  int32_t* ids_host = nullptr;     // pinned: a call's routed ids, then the lookahead's
+  int ids_cap = 0;
+  cudaStream_t copy = nullptr;     // prefetch copies
+  std::vector<cudaEvent_t> ready;  // per cache slot: its latest prefetch copy
+  int n_layers = 0;                // streamed layers uploaded
+  bool lookahead = true;           // KC_OPT_LOOKAHEAD
+  // Lookahead predictions awaiting their layer's call (recall counters).
+  std::map<int, std::vector<int>> predicted;
+  // A lookahead's ids on the device, read back at the next demand sync.
+  int look_layer = -1;
+  const int32_t* look_ids = nullptr;
+  int look_n = 0;
+};
+
 struct kc_ctx {
   int device = 0;
   // n >= 4 products on CUDA cores in f32 instead of tcgen05 with f16
@@ -167,6 +204,7 @@ struct kc_ctx {
   Work ws;
   Work ws_ep;  // the owner-side expert products of expert parallelism
   int64_t weight_bytes = 0;
+  ExpertStreams xs;
   EpState ep;
   EpBufs epb;
   Prof prof;
@@ -413,6 +451,225 @@ GroupedArgs grouped_base(kc_ctx* ctx) {
   return a;
 }
 
+// ---- host-streamed experts ---------------------------------------------------
+// Experts of a streamed layer live in pinned host memory in the device
+// layout; a call copies the ones it routes to that are not resident into HBM
+// slots (ExpertStore::request / get, crates/kestrel-memory/src/expert.rs:
+// 358-424, 523-537) and the kernels read expert e at slot[e].
+
+void streams_free(kc_ctx* ctx) {
+  ExpertStreams& S = ctx->xs;
+  if (S.copy) cudaStreamSynchronize(S.copy);
+  cudaFree(S.arena);
+  cudaFree(S.slot_dev);
+  if (S.slot_host) cudaFreeHost(S.slot_host);
+  if (S.ids_host) cudaFreeHost(S.ids_host);
+  for (cudaEvent_t e : S.ready) cudaEventDestroy(e);
+  if (S.copy) cudaStreamDestroy(S.copy);
+  S.arena = nullptr;
+  S.slot_dev = S.slot_host = nullptr;
+  S.ids_host = nullptr;
+  S.ids_cap = S.table_e = 0;
+  S.ready.clear();
+  S.copy = nullptr;
+  S.predicted.clear();
+  S.look_layer = -1;
+  S.look_ids = nullptr;
+}
+
+// Forget what the slots hold (a streamed layer was replaced or freed): no
+// copy may still land in them and no kernel may still read them.
+int streams_invalidate(kc_ctx* ctx) {
+  ExpertStreams& S = ctx->xs;
+  if (S.copy) CK(cudaStreamSynchronize(S.copy));
+  CK(cudaStreamSynchronize(ctx->stream));
+  if (S.arena) S.cache.configure(S.capacity, S.scratch, S.policy);
+  S.predicted.clear();
+  S.look_layer = -1;
+  S.look_ids = nullptr;
+  return KC_OK;
+}
+
+// The slot arena for the reserved capacity (default: one layer's experts).
+int streams_alloc(kc_ctx* ctx, int n_expert) {
+  ExpertStreams& S = ctx->xs;
+  if (S.arena) return KC_OK;
+  if (S.capacity < 0) {
+    S.capacity = n_expert;
+    S.scratch = 0;
+  }
+  const int slots = S.capacity + S.scratch;
+  if (slots < 1) return fail(ctx, KC_ERR_STATE, "host-streamed experts: no slots reserved");
+  if (cudaMalloc(&S.arena, (size_t)slots * S.slot_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    S.arena = nullptr;
+    return fail(ctx, KC_ERR_OOM, "host-streamed experts: %d slots of %lld bytes do not fit", slots,
+                (long long)S.slot_bytes);
+  }
+  if (!S.copy) CK(cudaStreamCreateWithFlags(&S.copy, cudaStreamNonBlocking));
+  S.ready.resize(S.capacity, nullptr);
+  for (cudaEvent_t& e : S.ready)
+    if (!e) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  S.cache.configure(S.capacity, S.scratch, S.policy);
+  return KC_OK;
+}
+
+// Prefetch copies that have landed (ExpertBuf's ticket done).
+void streams_refresh(ExpertStreams& S) {
+  for (int s = 0; s < S.capacity; ++s)
+    if (S.cache.pending(s) && cudaEventQuery(S.ready[s]) == cudaSuccess) S.cache.mark_done(s);
+  cudaGetLastError();  // cudaErrorNotReady is not an error of the call
+}
+
+// ExpertStore::prefetch for `experts` (ascending, unique) of streamed layer
+// Lt: copies on the copy stream, each recording its slot's event. The policy
+// picks no slot that work in flight reads (the latest demand call's experts)
+// or that a copy is still filling.
+int streams_prefetch(kc_ctx* ctx, const Layer& Lt, const std::vector<int>& experts) {
+  ExpertStreams& S = ctx->xs;
+  if (experts.empty()) return KC_OK;
+  RC(streams_alloc(ctx, Lt.n_expert));
+  streams_refresh(S);
+  std::vector<ExpertCache::Load> loads;
+  S.cache.prefetch(Lt.id, experts.data(), (int)experts.size(), loads);
+  for (const ExpertCache::Load& ld : loads) {
+    CK(cudaMemcpyAsync(S.arena + (int64_t)ld.slot * S.slot_bytes, Lt.host + (int64_t)ld.expert * S.slot_bytes,
+                       (size_t)S.slot_bytes, cudaMemcpyHostToDevice, S.copy));
+    CK(cudaEventRecord(S.ready[ld.slot], S.copy));
+    S.cache.add_bytes((uint64_t)S.slot_bytes, 1);
+  }
+  return KC_OK;
+}
+
+int grow_pinned(kc_ctx* ctx, void** p, int& cap, int need, size_t elem) {
+  if (need <= cap) return KC_OK;
+  if (*p) cudaFreeHost(*p);
+  *p = nullptr;
+  cap = 0;
+  CK(cudaHostAlloc(p, std::max<size_t>(64, (size_t)need * elem), cudaHostAllocDefault));
+  cap = need;
+  return KC_OK;
+}
+
+// One call of streamed layer L whose routed ids (A of them) are on the
+// device: read them back, make every routed expert resident (demand copies on
+// the context stream, waits on prefetches still landing), upload the slot
+// table, start the lookahead's prefetch if one is pending, and return in Ls
+// the layer as the kernels see it.
+int streams_demand(kc_ctx* ctx, const Layer& L, const int32_t* ids_dev, int A, Layer& Ls) {
+  ExpertStreams& S = ctx->xs;
+  cudaStream_t st = ctx->stream;
+  const int E = L.n_expert;
+  RC(streams_alloc(ctx, E));
+  const int look_n = S.look_ids ? S.look_n : 0;
+  RC(grow_pinned(ctx, (void**)&S.ids_host, S.ids_cap, A + look_n, 4));
+  if (S.table_e < E) {
+    cudaFree(S.slot_dev);
+    if (S.slot_host) cudaFreeHost(S.slot_host);
+    S.slot_dev = S.slot_host = nullptr;
+    S.table_e = 0;
+    CK(cudaMalloc(&S.slot_dev, (size_t)E * 4));
+    CK(cudaHostAlloc(&S.slot_host, (size_t)E * 4, cudaHostAllocDefault));
+    S.table_e = E;
+  }
+  if (A > 0) CK(cudaMemcpyAsync(S.ids_host, ids_dev, (size_t)A * 4, cudaMemcpyDeviceToHost, st));
+  if (look_n) CK(cudaMemcpyAsync(S.ids_host + A, S.look_ids, (size_t)look_n * 4, cudaMemcpyDeviceToHost, st));
+  // Synchronises: every earlier call's kernels are complete after this, so
+  // their slots may be overwritten by this call's copies.
+  RC(check_status(ctx));
+  streams_refresh(S);
+  auto unique_ids = [&](const int32_t* ids, int n, int n_exp) {
+    std::vector<char> seen(n_exp, 0);
+    for (int i = 0; i < n; ++i)
+      if (ids[i] >= 0 && ids[i] < n_exp) seen[ids[i]] = 1;
+    std::vector<int> out;
+    for (int e = 0; e < n_exp; ++e)
+      if (seen[e]) out.push_back(e);
+    return out;
+  };
+  const std::vector<int> need = unique_ids(S.ids_host, A, E);
+  auto pi = S.predicted.find(L.id);
+  if (pi != S.predicted.end()) {  // Transformer::moe_ffn's recall count (transformer.rs:519-524)
+    uint64_t correct = 0;
+    for (int e : pi->second) correct += std::binary_search(need.begin(), need.end(), e) ? 1 : 0;
+    S.cache.record_lookahead(pi->second.size(), correct);
+    S.predicted.erase(pi);
+  }
+  std::vector<int> slot(need.size());
+  std::vector<ExpertCache::Load> loads;
+  std::vector<int> waits;
+  if (!S.cache.demand(L.id, need.data(), (int)need.size(), slot.data(), loads, waits))
+    return fail(ctx, KC_ERR_SHAPE,
+                "host-streamed experts: layer %d routes to %d experts, more than the %d cache + %d scratch slots "
+                "can hold at once (kc_expert_cache_reserve)",
+                L.id, (int)need.size(), S.capacity, S.scratch);
+  for (int s : waits) CK(cudaStreamWaitEvent(st, S.ready[s], 0));
+  for (const ExpertCache::Load& ld : loads) {
+    CK(cudaMemcpyAsync(S.arena + (int64_t)ld.slot * S.slot_bytes, L.host + (int64_t)ld.expert * S.slot_bytes,
+                       (size_t)S.slot_bytes, cudaMemcpyHostToDevice, st));
+    S.cache.add_bytes((uint64_t)S.slot_bytes, 1);
+  }
+  for (size_t i = 0; i < need.size(); ++i) S.slot_host[need[i]] = slot[i];
+  CK(cudaMemcpyAsync(S.slot_dev, S.slot_host, (size_t)E * 4, cudaMemcpyHostToDevice, st));
+  if (look_n) {
+    const int nl = S.look_layer;
+    S.look_ids = nullptr;
+    S.look_layer = -1;
+    auto it = ctx->layers.find(nl);
+    if (it != ctx->layers.end() && it->second.streamed) {
+      std::vector<int> pred = unique_ids(S.ids_host + A, look_n, it->second.n_expert);
+      RC(streams_prefetch(ctx, it->second, pred));
+      S.predicted[nl] = std::move(pred);
+    }
+  }
+  Ls = L;
+  Ls.gate = S.arena;
+  Ls.up = S.arena + L.up_off;
+  Ls.down = S.arena + L.down_off;
+  Ls.mb_gate = Ls.mb_down = S.slot_bytes;
+  Ls.first_expert = 0;
+  Ls.slot = S.slot_dev;
+  return KC_OK;
+}
+
+// Drops a layer's host-streamed experts (its pinned block), if it has them.
+int drop_streamed(kc_ctx* ctx, Layer& L) {
+  if (!L.streamed) return KC_OK;
+  RC(streams_invalidate(ctx));
+  cudaFreeHost(L.host);
+  L.host = nullptr;
+  L.streamed = false;
+  L.has_experts = false;
+  --ctx->xs.n_layers;
+  return KC_OK;
+}
+
+// Reads a pending lookahead's ids back now (its layer's predecessor is not
+// host-streamed, so no demand synchronisation comes first) and prefetches.
+int streams_lookahead_now(kc_ctx* ctx) {
+  ExpertStreams& S = ctx->xs;
+  if (!S.look_ids) return KC_OK;
+  const int nl = S.look_layer, n = S.look_n;
+  const int32_t* ids_dev = S.look_ids;
+  S.look_ids = nullptr;
+  S.look_layer = -1;
+  auto it = ctx->layers.find(nl);
+  if (it == ctx->layers.end() || !it->second.streamed) return KC_OK;
+  RC(grow_pinned(ctx, (void**)&S.ids_host, S.ids_cap, n, 4));
+  CK(cudaMemcpyAsync(S.ids_host, ids_dev, (size_t)n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  RC(check_status(ctx));
+  const int E = it->second.n_expert;
+  std::vector<char> seen(E, 0);
+  for (int i = 0; i < n; ++i)
+    if (S.ids_host[i] >= 0 && S.ids_host[i] < E) seen[S.ids_host[i]] = 1;
+  std::vector<int> pred;
+  for (int e = 0; e < E; ++e)
+    if (seen[e]) pred.push_back(e);
+  RC(streams_prefetch(ctx, it->second, pred));
+  S.predicted[nl] = std::move(pred);
+  return KC_OK;
+}
+
 }  // namespace
 
 namespace kc {
@@ -538,6 +795,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.n_mat = 2;
     ma.expert_stride = L.mb_gate;
     ma.expert_base = ebase;
+    ma.slot = L.slot;
     ma.rows = ff;
     ma.cols = d;
     ma.type = L.t_gate;
@@ -558,6 +816,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     g.w1 = L.up;
     g.expert_stride = L.mb_gate;
     g.expert_base = ebase;
+    g.slot = L.slot;
     g.rows = ff;
     g.cols = d;
     g.type = L.t_gate;
@@ -581,6 +840,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     dg.n_mat = 2;
     dg.expert_stride = L.mb_gate;
     dg.expert_base = ebase;
+    dg.slot = L.slot;
     dg.rows = ff;
     dg.cols = d;
     dg.type = L.t_gate;
@@ -619,6 +879,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.n_mat = 1;
     ma.expert_stride = L.mb_down;
     ma.expert_base = ebase;
+    ma.slot = L.slot;
     ma.rows = d;
     ma.cols = ff;
     ma.type = L.t_down;
@@ -637,6 +898,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     dn.w0 = L.down;
     dn.expert_stride = L.mb_down;
     dn.expert_base = ebase;
+    dn.slot = L.slot;
     dn.rows = d;
     dn.cols = ff;
     dn.type = L.t_down;
@@ -658,6 +920,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     dd.n_mat = 1;
     dd.expert_stride = L.mb_down;
     dd.expert_base = ebase;
+    dd.slot = L.slot;
     dd.rows = d;
     dd.cols = ff;
     dd.type = L.t_down;
@@ -1081,6 +1344,8 @@ static int ep_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const f
 static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const float* h, int n_tok, float* out,
                         int32_t* ids_out, float* w_out, bool defer_combine = false, bool* deferred = nullptr) {
   if (deferred) *deferred = false;
+  if (L.streamed && ctx->ep.world > 1)
+    return fail(ctx, KC_ERR_STATE, "layer %d: host-streamed experts are not served by expert parallelism", L.id);
   if (ctx->ep.world > 1) return ep_pipeline(ctx, L, router, h, n_tok, out, ids_out, w_out);
   const int E = L.n_expert, k = L.k, d = L.d;
   RC(ensure_work(ctx, n_tok, E, k, layer_work_d(L), layer_work_f(L)));
@@ -1106,8 +1371,16 @@ static int moe_pipeline(kc_ctx* ctx, const Layer& L, const float* router, const 
     launch_route(W.logits, n_tok, E, k, L.norm_topk, L.weights_scale, W.ids, W.w, st);
     CKL();
   }
+  // Host-streamed experts: the routed ones copied into HBM slots.
+  Layer Ls;
+  const Layer* LE = &L;
+  if (L.streamed) {
+    StageScope ss(ctx, KC_STAGE_EXPERT_LOAD);
+    RC(streams_demand(ctx, L, W.ids, n_tok * k, Ls));
+    LE = &Ls;
+  }
   // 2-6. dispatch, records, gate/up, SwiGLU, down.
-  RC(experts_forward(ctx, W, L, E, L.first_expert, h, n_tok, W.ids, W.w, k, front, front && with_rec));
+  RC(experts_forward(ctx, W, *LE, E, LE->first_expert, h, n_tok, W.ids, W.w, k, front, front && with_rec));
   // 7. combine (un-permute, ascending expert id).
   if (!defer_combine || L.has_shared) {
     StageScope ss(ctx, KC_STAGE_COMBINE);
@@ -1169,10 +1442,14 @@ struct Model {
   uint8_t* rec = nullptr;   // Q8_K records of the attention norm's output (decode steps)
   uint32_t* next = nullptr; // argmax result ([n_seq] in a batch step)
   int* counters = nullptr;  // [0] generated-token index, [1] position (graph-replayed decode steps)
+  // Router lookahead of host-streamed layers: the next layer's norm of up to
+  // 4 rows, its logits, ids and weights.
+  float* look = nullptr;
   int64_t bytes = 0;
 };
 
 void free_layer(Layer& L) {
+  if (L.host) cudaFreeHost(L.host);
   cudaFree(L.gate);
   cudaFree(L.up);
   cudaFree(L.down);
@@ -1205,7 +1482,7 @@ void model_free(kc_ctx* ctx) {
   cudaFree(m->rope);
   for (void* p : {(void*)m->x, (void*)m->h, (void*)m->qkv, (void*)m->q, (void*)m->att, (void*)m->tmp,
                   (void*)m->ffn, (void*)m->g, (void*)m->u, (void*)m->logits, (void*)m->tok, (void*)m->next,
-                  (void*)m->counters, (void*)m->rec, (void*)m->row_pos, (void*)m->seq_tok})
+                  (void*)m->counters, (void*)m->rec, (void*)m->row_pos, (void*)m->seq_tok, (void*)m->look})
     cudaFree(p);
   delete m;
   ctx->model = nullptr;
@@ -1312,6 +1589,46 @@ int model_finalize(kc_ctx* ctx, Model& m) {
 // the caller advances m.cached. rows (a batch step, ctx->rows_mode): row s is
 // the next token of sequence s, at position m.row_pos[s] of its own cache;
 // every row gets its logits (m.logits [n][n_vocab]) and argmax (m.next[s]).
+// Transformer::lookahead_prefetch (transformer.rs:498-508) for layer l + 1
+// after layer l's attention: RMSNorm of the residual with l + 1's FFN norm,
+// its router and top-k, then ExpertStore::prefetch of the predicted experts.
+// The ids are read back at layer l's own demand synchronisation when l is
+// host-streamed, else here.
+int model_lookahead(kc_ctx* ctx, Model& m, int l, int n) {
+  auto it = ctx->layers.find(l + 1);
+  if (it == ctx->layers.end() || !it->second.streamed || !it->second.has_router || m.L[l + 1].gate.w) return KC_OK;
+  const Layer& R = it->second;
+  if (R.d != m.d) return KC_OK;
+  cudaStream_t st = ctx->stream;
+  const int E = R.n_expert, k = R.k;
+  if (!m.look) CK(cudaMalloc(&m.look, (size_t)4 * (m.d + 1024 + 2 * 64) * 4));
+  float* look_h = m.look;
+  float* logits = look_h + 4 * m.d;
+  int32_t* ids = reinterpret_cast<int32_t*>(logits + 4 * 1024);
+  float* w = logits + 4 * 1024 + 4 * 64;
+  NormArgs na{};
+  na.x = m.x;
+  na.w = m.L[l + 1].ffn_norm;
+  na.dim = m.d;
+  na.eps = m.eps;
+  na.out = look_h;
+  na.rec_slots = n;
+  launch_add_rmsnorm(na, n, st);
+  CKL();
+  launch_router_logits(R.router, R.d, E, R.d, look_h, n, logits, ctx->status, st, ctx->rows_mode);
+  CKL();
+  launch_route(logits, n, E, k, R.norm_topk, R.weights_scale, ids, w, st);
+  CKL();
+  ExpertStreams& S = ctx->xs;
+  S.look_layer = l + 1;
+  S.look_ids = ids;
+  S.look_n = n * k;
+  auto cur = ctx->layers.find(l);
+  const bool cur_streamed = cur != ctx->layers.end() && cur->second.streamed && !m.L[l].gate.w;
+  if (!cur_streamed) RC(streams_lookahead_now(ctx));
+  return KC_OK;
+}
+
 int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos, bool rows = false) {
   cudaStream_t st = ctx->stream;
   const int d = m.d, pos0 = m.cached;
@@ -1401,6 +1718,9 @@ int model_chunk(kc_ctx* ctx, Model& m, int n, const uint32_t* tok, bool dev_pos,
     resid = m.tmp;
     norm(m.x, y.ffn_norm, n, 0, m.h, nullptr);
     CKL();
+    // Router lookahead (transformer.rs:432-436): guess the next streamed
+    // layer's experts from this post-attention state and start loading them.
+    if (ctx->xs.lookahead && ctx->xs.n_layers > 0 && n <= 4 && l + 1 < m.n_layer) RC(model_lookahead(ctx, m, l, n));
     resid = m.ffn;
     if (!y.gate.w) {  // routed experts (checked in model_finalize)
       const Layer& R = ctx->layers[l];
@@ -1496,6 +1816,7 @@ void kc_free(kc_ctx* ctx) {
   model_free(ctx);
   ep_free(ctx->ep);
   ep_free_bufs(ctx->epb);
+  streams_free(ctx);
   for (auto& [id, L] : ctx->layers) free_layer(L);
   for (auto& [id, D] : ctx->dense) cudaFree(D.w);
   for (auto& r : ctx->prof.recs) {
@@ -1553,7 +1874,9 @@ int kc_sync(kc_ctx* ctx) {
 }
 
 int64_t kc_device_bytes(const kc_ctx* ctx) {
-  return ctx ? ctx->weight_bytes + (int64_t)ctx->ws.bytes + (int64_t)ctx->ws_ep.bytes : 0;
+  if (!ctx) return 0;
+  const int64_t slots = ctx->xs.arena ? (int64_t)(ctx->xs.capacity + ctx->xs.scratch) * ctx->xs.slot_bytes : 0;
+  return ctx->weight_bytes + (int64_t)ctx->ws.bytes + (int64_t)ctx->ws_ep.bytes + slots;
 }
 
 int kc_upload_experts_range(kc_ctx* ctx, int layer, int n_expert, int first_expert, int n_local, int d, int ff,
@@ -1574,11 +1897,13 @@ int kc_upload_experts_range(kc_ctx* ctx, int layer, int n_expert, int first_expe
   cudaSetDevice(ctx->device);
   RC(wait_device_source(ctx, src_on_device != 0));
   Layer& L = ctx->layers[layer];
+  RC(drop_streamed(ctx, L));
   cudaFree(L.gate);
   cudaFree(L.up);
   cudaFree(L.down);
   L.gate = L.up = L.down = nullptr;
   L.has_experts = false;
+  L.id = layer;
   if (L.has_router && L.n_expert != n_expert)
     return fail(ctx, KC_ERR_SHAPE, "kc_upload_experts: %d experts but the router has %d", n_expert, L.n_expert);
   L.n_expert = n_expert;
@@ -1608,6 +1933,176 @@ int kc_upload_experts(kc_ctx* ctx, int layer, int n_expert, int d, int ff, int t
                       const void* up, int t_down, const void* down, int src_on_device) {
   return kc_upload_experts_range(ctx, layer, n_expert, 0, n_expert, d, ff, t_gate, gate, t_up, up, t_down, down,
                                  src_on_device);
+}
+
+int kc_upload_experts_streamed(kc_ctx* ctx, int layer, int n_expert, int d, int ff, int t_gate, const void* gate,
+                               int t_up, const void* up, int t_down, const void* down, int src_on_device) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (!gate || !up || !down || n_expert <= 0 || d <= 0 || ff <= 0)
+    return fail(ctx, KC_ERR_ARG, "kc_upload_experts_streamed: bad arguments");
+  if (!type_ok(t_gate) || !type_ok(t_up) || !type_ok(t_down))
+    return fail(ctx, KC_ERR_TYPE, "kc_upload_experts_streamed: types %d/%d/%d (kernels: Q4_K, Q6_K, Q8_0)",
+                t_gate, t_up, t_down);
+  if (t_gate != t_up) return fail(ctx, KC_ERR_TYPE, "kc_upload_experts_streamed: gate and up types differ");
+  if (d % block_elems(t_gate) || ff % block_elems(t_down) || d % 256 || ff % 32)
+    return fail(ctx, KC_ERR_SHAPE, "kc_upload_experts_streamed: d=%d / ff=%d (d %% 256 == 0, ff %% 32 == 0)", d,
+                ff);
+  if (ctx->ep.world > 1)
+    return fail(ctx, KC_ERR_STATE, "kc_upload_experts_streamed: not served by expert parallelism");
+  cudaSetDevice(ctx->device);
+  RC(wait_device_source(ctx, src_on_device != 0));
+  ExpertStreams& S = ctx->xs;
+  Layer& L = ctx->layers[layer];
+  if (L.has_router && L.n_expert != n_expert)
+    return fail(ctx, KC_ERR_SHAPE, "kc_upload_experts_streamed: %d experts but the router has %d", n_expert,
+                L.n_expert);
+  // One expert's gate, up and down side by side, each 256-byte aligned: one
+  // copy per expert, and the kernels' bulk copies stay 16-byte aligned.
+  const int64_t mb_gate = dev_matrix_bytes(t_gate, ff, d), mb_down = dev_matrix_bytes(t_down, d, ff);
+  auto al256 = [](int64_t v) { return (v + 255) / 256 * 256; };
+  const int64_t up_off = al256(mb_gate), down_off = up_off + al256(mb_gate), slot_bytes = down_off + al256(mb_down);
+  const int others = S.n_layers - (L.streamed ? 1 : 0);
+  if (others > 0 && S.slot_bytes != slot_bytes)
+    return fail(ctx, KC_ERR_SHAPE,
+                "kc_upload_experts_streamed: every host-streamed layer shares the slots' shape (%lld bytes per "
+                "expert), layer %d needs %lld",
+                (long long)S.slot_bytes, layer, (long long)slot_bytes);
+  RC(drop_streamed(ctx, L));
+  cudaFree(L.gate);
+  cudaFree(L.up);
+  cudaFree(L.down);
+  L.gate = L.up = L.down = nullptr;
+  L.has_experts = false;
+  if (S.slot_bytes != slot_bytes) {  // new slot shape: the arena is made again at first use
+    RC(streams_invalidate(ctx));
+    cudaFree(S.arena);
+    S.arena = nullptr;
+    S.slot_bytes = slot_bytes;
+  }
+  L.id = layer;
+  L.n_expert = n_expert;
+  L.first_expert = 0;
+  L.n_local = n_expert;
+  L.d = d;
+  L.ff = ff;
+  L.t_gate = t_gate;
+  L.t_up = t_up;
+  L.t_down = t_down;
+  L.mb_gate = mb_gate;
+  L.mb_down = mb_down;
+  L.up_off = up_off;
+  L.down_off = down_off;
+  L.slot_bytes = slot_bytes;
+  if (cudaHostAlloc(&L.host, (size_t)n_expert * slot_bytes, cudaHostAllocDefault) != cudaSuccess) {
+    cudaGetLastError();
+    L.host = nullptr;
+    return fail(ctx, KC_ERR_OOM, "kc_upload_experts_streamed: %lld bytes of pinned host memory",
+                (long long)n_expert * slot_bytes);
+  }
+  // Convert a chunk of experts at a time into the device layout on the GPU,
+  // then read it back beside the other matrices of each expert.
+  const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(n_expert, (256ll << 20) / slot_bytes));
+  uint8_t* tmp = nullptr;
+  CK(cudaMalloc(&tmp, (size_t)chunk * std::max(mb_gate, mb_down)));
+  int rc = KC_OK;
+  struct Part {
+    int t;
+    const void* src;
+    int64_t rows, cols, mb, off;
+  } parts[3] = {{t_gate, gate, ff, d, mb_gate, 0}, {t_up, up, ff, d, mb_gate, up_off},
+                {t_down, down, d, ff, mb_down, down_off}};
+  for (int64_t e0 = 0; e0 < n_expert && rc == KC_OK; e0 += chunk) {
+    const int64_t ne = std::min<int64_t>(chunk, n_expert - e0);
+    for (const Part& p : parts) {
+      const int64_t mat_src = p.rows * gguf_row_bytes(p.t, p.cols);
+      rc = upload_matrix(ctx, p.t, static_cast<const uint8_t*>(p.src) + e0 * mat_src, ne, p.rows, p.cols, tmp,
+                         src_on_device != 0);
+      if (rc != KC_OK) break;
+      cudaError_t e = cudaMemcpy2DAsync(L.host + e0 * slot_bytes + p.off, (size_t)slot_bytes, tmp, (size_t)p.mb,
+                                        (size_t)p.mb, (size_t)ne, cudaMemcpyDeviceToHost, ctx->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+      if (e != cudaSuccess) {
+        rc = fail(ctx, KC_ERR_CUDA, "kc_upload_experts_streamed: %s", cudaGetErrorString(e));
+        break;
+      }
+    }
+  }
+  cudaFree(tmp);
+  if (rc != KC_OK) {
+    cudaFreeHost(L.host);
+    L.host = nullptr;
+    return rc;
+  }
+  L.streamed = true;
+  L.has_experts = true;
+  ++S.n_layers;
+  return KC_OK;
+}
+
+int kc_expert_cache_reserve(kc_ctx* ctx, int capacity, int scratch, int policy) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  if (capacity < 0 || scratch < 0 || capacity + scratch < 1 ||
+      (policy != KC_EXPERT_POLICY_LFRU && policy != KC_EXPERT_POLICY_LRU))
+    return fail(ctx, KC_ERR_ARG, "kc_expert_cache_reserve: capacity %d, scratch %d, policy %d", capacity, scratch,
+                policy);
+  cudaSetDevice(ctx->device);
+  ExpertStreams& S = ctx->xs;
+  RC(streams_invalidate(ctx));
+  cudaFree(S.arena);
+  S.arena = nullptr;
+  while ((int)S.ready.size() > capacity) {
+    cudaEventDestroy(S.ready.back());
+    S.ready.pop_back();
+  }
+  S.capacity = capacity;
+  S.scratch = scratch;
+  S.policy = policy == KC_EXPERT_POLICY_LRU ? ExpertPolicy::Lru : ExpertPolicy::Lfru;
+  S.cache.configure(capacity, scratch, S.policy);
+  // With a streamed layer already uploaded the slots are made now, so that a
+  // reservation HBM cannot hold fails here rather than in a later call.
+  if (S.slot_bytes) RC(streams_alloc(ctx, capacity));
+  return KC_OK;
+}
+
+int kc_expert_prefetch(kc_ctx* ctx, int layer, const int32_t* experts, int n) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->err.clear();
+  auto it = ctx->layers.find(layer);
+  if (it == ctx->layers.end() || !it->second.streamed)
+    return fail(ctx, KC_ERR_STATE, "kc_expert_prefetch: layer %d has no host-streamed experts", layer);
+  const Layer& L = it->second;
+  if (n < 0 || (n > 0 && !experts)) return fail(ctx, KC_ERR_ARG, "kc_expert_prefetch: bad arguments");
+  std::vector<char> seen(L.n_expert, 0);
+  for (int i = 0; i < n; ++i) {
+    if (experts[i] < 0 || experts[i] >= L.n_expert)
+      return fail(ctx, KC_ERR_ARG, "kc_expert_prefetch: expert %d of %d", experts[i], L.n_expert);
+    seen[experts[i]] = 1;
+  }
+  std::vector<int> list;
+  for (int e = 0; e < L.n_expert; ++e)
+    if (seen[e]) list.push_back(e);
+  cudaSetDevice(ctx->device);
+  return streams_prefetch(ctx, L, list);
+}
+
+int kc_expert_cache_stats(const kc_ctx* ctx, uint64_t* out, int n) {
+  if (!ctx || n < 0 || (n > 0 && !out)) return KC_ERR_ARG;
+  const ExpertStreams& S = ctx->xs;
+  const ExpertCacheStats& c = S.cache.stats();
+  const uint64_t v[KC_XS_N] = {(uint64_t)std::max(0, S.capacity), (uint64_t)S.cache.cached(), c.requests, c.hits,
+                               c.late, c.misses, c.scratch_loads, c.bytes_read, c.prefetch_issued, c.prefetch_used,
+                               c.prefetch_wasted, c.evictions, c.lookahead_predicted, c.lookahead_correct, c.reads,
+                               c.forced, (uint64_t)std::max(0, S.scratch)};
+  for (int i = 0; i < n; ++i) out[i] = i < KC_XS_N ? v[i] : 0;
+  return KC_OK;
+}
+
+int kc_expert_cache_decay(kc_ctx* ctx) {
+  if (!ctx) return KC_ERR_ARG;
+  ctx->xs.cache.decay();
+  return KC_OK;
 }
 
 int kc_upload_router(kc_ctx* ctx, int layer, const float* router_w, int n_expert, int d, int k, int norm_topk,
@@ -1925,6 +2420,10 @@ int kc_set_option(kc_ctx* ctx, int option, int value) {
     ctx->f32_prefill = value != 0;
     return KC_OK;
   }
+  if (option == KC_OPT_LOOKAHEAD) {
+    ctx->xs.lookahead = value != 0;
+    return KC_OK;
+  }
 
   return fail(ctx, KC_ERR_ARG, "kc_set_option: unknown option %d", option);
 }
@@ -1945,6 +2444,10 @@ int kc_model_init(kc_ctx* ctx, int n_layer, int d, int n_head, int n_head_kv, in
   // 0 .. n_layer-1: drop what an earlier model left there.
   for (auto it = ctx->layers.begin(); it != ctx->layers.end();) {
     if (it->first >= 0 && it->first < n_layer) {
+      if (it->second.streamed) {
+        streams_invalidate(ctx);
+        --ctx->xs.n_layers;
+      }
       free_layer(it->second);
       it = ctx->layers.erase(it);
     } else {
@@ -2098,7 +2601,7 @@ int kc_model_generate(kc_ctx* ctx, const uint32_t* prompt, int n_prompt, int n_g
   if (cudaMemcpyAsync(hist, m.next, 4, cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess ||
       cudaMemcpyAsync(m.counters, init, sizeof init, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
     rc = fail(ctx, KC_ERR_CUDA, "kc_model_generate: copy failed");
-  const bool graphs = ctx->ep.world <= 1 && !ctx->prof.on && model_graphs_enabled();
+  const bool graphs = ctx->ep.world <= 1 && !ctx->prof.on && ctx->xs.n_layers == 0 && model_graphs_enabled();
   for (int i = 1; i < n_gen && rc == KC_OK; ++i) {
     if (exec) {
       if (cudaGraphLaunch(exec, ctx->stream) != cudaSuccess) rc = fail(ctx, KC_ERR_CUDA, "cudaGraphLaunch failed");
@@ -2269,7 +2772,7 @@ int kc_model_decode_seqs(kc_ctx* ctx, int n_seq, int n_gen, uint32_t* out_tokens
     CKL();
     return KC_OK;
   };
-  const bool graphs = ctx->ep.world <= 1 && !ctx->prof.on && model_graphs_enabled();
+  const bool graphs = ctx->ep.world <= 1 && !ctx->prof.on && ctx->xs.n_layers == 0 && model_graphs_enabled();
   for (int i = 1; i < n_gen && rc == KC_OK; ++i) {
     if (exec) {
       if (cudaGraphLaunch(exec, ctx->stream) != cudaSuccess) rc = fail(ctx, KC_ERR_CUDA, "cudaGraphLaunch failed");

@@ -45,6 +45,10 @@ constexpr int kTileRows = 32;
 constexpr int kPlane = kTileRows * 16;  // one 16-byte chunk of every row of a tile
 
 __host__ __device__ inline int64_t round16(int64_t v) { return (v + 15) & ~int64_t(15); }
+// Position of a local expert's matrices in its stacked buffer: the expert
+// itself (HBM-resident table) or the HBM slot a host-streamed expert was
+// copied into for this call.
+__device__ __forceinline__ int expert_pos(const int* slot, int local) { return slot ? __ldg(slot + local) : local; }
 
 // Superblocks (Q8_0: chunks of 8 blocks) per row.
 __host__ __device__ inline int tiled_nsb(int t, int64_t cols) {

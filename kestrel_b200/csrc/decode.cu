@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
     auto unit_ptrs = [&](int gi, const uint8_t*& up, const uint8_t*& rp, int& rbytes) {
       const UnitPos p = unit_at(gi * DW + w);
       const UnitMeta um = meta_at(list_s, off_s, p.li);
-      up = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)(um.e - a.expert_base) * a.expert_stride +
+      up = (p.m == 0 ? a.w[0] : a.w[1]) + (int64_t)expert_pos(a.slot, um.e - a.expert_base) * a.expert_stride +
            (int64_t)p.tile * g.tile_bytes;
       rp = a.rec + (int64_t)um.slot0 * (KQ ? 2 * R : R);
       rbytes = um.ns * (KQ ? 2 * R : R);

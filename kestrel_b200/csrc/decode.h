@@ -33,6 +33,9 @@ struct DecodeArgs {
   int n_mat;               // 1 or 2
   int64_t expert_stride;   // bytes between experts' matrices
   int expert_base;         // global id of the first expert held
+  // Host-streamed experts: expert e's matrices are at slot[e - expert_base]
+  // * expert_stride (null: at e - expert_base).
+  const int* slot;
   int rows, cols;          // one expert's matrix
   int type;                // KC_Q4_K / KC_Q6_K / KC_Q8_0
   const int* list;         // expert ids (1..3 rows each; e | part << 16, see meta_at)

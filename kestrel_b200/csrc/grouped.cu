@@ -100,8 +100,9 @@ __global__ void __launch_bounds__(F_THREADS) grouped_f32_kernel(GroupedArgs a) {
   // the slots in 4s.
   const int tile = r / 48, trows = min(48, a.rows - tile * 48);
   const bool m1 = !((r - tile * 48) < trows / 3 * 3 && t < n / 4 * 4);
-  const uint8_t* base0 = a.w0 + (int64_t)(e - a.expert_base) * a.expert_stride;
-  const uint8_t* base1 = PAIR ? a.w1 + (int64_t)(e - a.expert_base) * a.expert_stride : nullptr;
+  const int64_t epos = expert_pos(a.slot, e - a.expert_base);
+  const uint8_t* base0 = a.w0 + epos * a.expert_stride;
+  const uint8_t* base1 = PAIR ? a.w1 + epos * a.expert_stride : nullptr;
   float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
   for (int k0 = 0; k0 < a.cols; k0 += F_KC) {
     const int kn = min(F_KC, a.cols - k0);

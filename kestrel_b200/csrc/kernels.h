@@ -16,6 +16,7 @@ struct GroupedArgs {
   const uint8_t* w1;      // second matrix for the gate/up pair (or null)
   int64_t expert_stride;  // bytes between consecutive experts' matrices
   int expert_base;        // global id of the first expert held in w0 / w1
+  const int* slot;        // host-streamed experts: slot of expert e (null: e - expert_base)
   int rows, cols;         // one expert's matrix (tiled device layout)
   int type;               // ggml type of w0 / w1
   const int* list;        // expert ids to process

@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
             uint8_t* rbase = raws + r * L.raw_bytes;
 #pragma unroll
             for (int mt = 0; mt < MI; ++mt) {
-              const uint8_t* src = a.w[t.m + mt] + (int64_t)(t.e - a.expert_base) * a.expert_stride +
+              const uint8_t* src = a.w[t.m + mt] + (int64_t)expert_pos(a.slot, t.e - a.expert_base) * a.expert_stride +
                                    (int64_t)(M_RT * t.rt) * tile_bytes + tiled_sb_offset(T, a.cols, sb);
               for (int x = 0; x < n_rt; ++x)
                 bulk_g2s(rbase + (mt * M_RT + x) * max_sbt_bytes(T), src + x * tile_bytes, sbytes, &raw_full[r]);

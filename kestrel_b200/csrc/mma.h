@@ -12,6 +12,7 @@ struct MmaArgs {
   int n_mat;
   int64_t expert_stride;  // device bytes of one expert's matrix
   int expert_base;
+  const int* slot;        // host-streamed experts: slot of expert e (null: e - expert_base)
   int rows, cols, type;
   const int* list;        // experts to process
   const int* n_list;      // device scalar

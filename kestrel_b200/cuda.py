@@ -69,10 +69,21 @@ SIGNATURES = {
     "kc_model_cached": (I, [P]),
     "kc_load_gguf": (I, [P, ctypes.c_char_p, I, ctypes.c_char_p, I64]),
     "kc_gguf_inspect": (I, [ctypes.c_char_p, ctypes.c_char_p, I64]),
+    "kc_upload_experts_streamed": (I, [P, I, I, I, I, I, P, I, P, I, P, I]),
+    "kc_expert_cache_reserve": (I, [P, I, I, I]),
+    "kc_expert_prefetch": (I, [P, I, P, I]),
+    "kc_expert_cache_stats": (I, [P, P, I]),
+    "kc_expert_cache_decay": (I, [P]),
 }
 
 # Options (kc_set_option) and whole-model tensor kinds (kc_model_tensor).
 OPT_F32_PREFILL = 1
+OPT_LOOKAHEAD = 2
+# Expert-cache policies (kc_expert_cache_reserve) and counters (kc_expert_cache_stats).
+EXPERT_POLICY_LFRU, EXPERT_POLICY_LRU = 0, 1
+XS_COUNTERS = ["capacity", "cached", "requests", "hits", "late", "misses", "scratch_loads", "bytes_read",
+               "prefetch_issued", "prefetch_used", "prefetch_wasted", "evictions", "lookahead_predicted",
+               "lookahead_correct", "reads", "forced", "scratch"]
 ARCH_LLAMA, ARCH_QWEN2, ARCH_QWEN3 = 0, 1, 2
 (T_ATTN_NORM, T_ATTN_Q, T_ATTN_K, T_ATTN_V, T_ATTN_OUT, T_ATTN_Q_BIAS, T_ATTN_K_BIAS, T_ATTN_V_BIAS,
  T_ATTN_Q_NORM, T_ATTN_K_NORM, T_FFN_NORM, T_FFN_GATE, T_FFN_UP, T_FFN_DOWN) = range(14)
@@ -179,6 +190,35 @@ class Context:
         self._check(lib().kc_upload_experts_range(self.h, layer, n_expert, first_expert, n_local, d, ff, t_gate,
                                                   _ptr(gate), t_up, _ptr(up), t_down, _ptr(down), int(dev)))
 
+    def upload_experts_streamed(self, layer: int, n_expert: int, d: int, ff: int, t_gate: int, gate, t_up: int,
+                                up, t_down: int, down):
+        """Like upload_experts, but the experts stay in pinned host memory and
+        each call copies the ones it routes to into HBM slots."""
+        gate, up, down = _host_u8(gate), _host_u8(up), _host_u8(down)
+        dev = _is_dev(gate)
+        for t, a, rows, cols in ((t_gate, gate, ff, d), (t_up, up, ff, d), (t_down, down, d, ff)):
+            want = n_expert * rows * G.bytes_for(t, cols)
+            n = a.size if isinstance(a, np.ndarray) else a.numel() * a.element_size()
+            if n < want:
+                raise ValueError(f"expert tensor holds {n} bytes, {want} needed")
+        self._check(lib().kc_upload_experts_streamed(self.h, layer, n_expert, d, ff, t_gate, _ptr(gate), t_up,
+                                                     _ptr(up), t_down, _ptr(down), int(dev)))
+
+    def expert_cache_reserve(self, capacity: int, scratch: int = 0, policy: int = EXPERT_POLICY_LFRU):
+        self._check(lib().kc_expert_cache_reserve(self.h, capacity, scratch, policy))
+
+    def expert_prefetch(self, layer: int, experts):
+        ids = np.ascontiguousarray(np.asarray(experts, dtype=np.int32))
+        self._check(lib().kc_expert_prefetch(self.h, layer, ids.ctypes.data, ids.size))
+
+    def expert_cache_stats(self) -> dict:
+        out = np.zeros(len(XS_COUNTERS), np.uint64)
+        self._check(lib().kc_expert_cache_stats(self.h, out.ctypes.data, out.size))
+        return {k: int(v) for k, v in zip(XS_COUNTERS, out)}
+
+    def expert_cache_decay(self):
+        self._check(lib().kc_expert_cache_decay(self.h))
+
     def upload_router(self, layer: int, router_w, k: int, norm_topk: bool = True, weights_scale: float = 0.0):
         rw = router_w if _is_dev(router_w) else np.ascontiguousarray(router_w, dtype=np.float32)
         E, d = rw.shape
@@ -270,7 +310,7 @@ class Context:
         self._check(lib().kc_quantize_dev(self.h, t, _ptr(x), rows, cols, _ptr(out)))
 
     STAGES = ["router_logits", "route", "dispatch", "quant_x", "gate_up_int8", "gate_up_f32", "quant_act",
-              "down_int8", "down_f32", "combine"]
+              "down_int8", "down_f32", "combine", "expert_load"]
 
     def profile_enable(self, on: bool = True):
         self._check(lib().kc_profile_enable(self.h, int(on)))

@@ -83,9 +83,10 @@ DENSE_KINDS = {"attn_norm": 0, "attn_q": 1, "attn_k": 2, "attn_v": 3, "attn_outp
 MODEL_KINDS = {"token_embd": 0, "output_norm": 1, "output": 2}
 
 
-def load_cuda(ctx, model: dict, n_ctx: int, block=None) -> None:
+def load_cuda(ctx, model: dict, n_ctx: int, block=None, streamed=False) -> None:
     """Declare `model` on a cuda.Context and upload its tensors (with an
-    expert block, only that block of each routed layer's experts)."""
+    expert block, only that block of each routed layer's experts; streamed:
+    the routed experts stay in host memory, kc_upload_experts_streamed)."""
     c = model["cfg"]
     ctx.model_init(c["n_layer"], c["d"], c["n_head"], c["n_kv"], c["head_dim"], c["n_vocab"], n_ctx, c["rope_dim"],
                    c["rope_base"], c["eps"], c["arch"])
@@ -102,7 +103,9 @@ def load_cuda(ctx, model: dict, n_ctx: int, block=None) -> None:
         tg, gate, _, _ = by[(l, "ffn_gate_exps")]
         tu, up, _, _ = by[(l, "ffn_up_exps")]
         td, down, _, _ = by[(l, "ffn_down_exps")]
-        if block is None:
+        if streamed:
+            ctx.upload_experts_streamed(l, c["n_expert"], c["d"], c["ff"], tg, gate, tu, up, td, down)
+        elif block is None:
             ctx.upload_experts(l, c["n_expert"], c["d"], c["ff"], tg, gate, tu, up, td, down)
         else:
             from . import ep
