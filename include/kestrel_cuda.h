@@ -158,15 +158,18 @@ KC_API int kc_upload_shared_expert(kc_ctx* ctx, int layer, int ff_shared, int d,
    eagerly). Every streamed layer has the same shape (d, ff, types). Not
    available with expert parallelism.
 
-   kc_expert_cache_reserve sets `capacity` cache slots and `scratch` slots
-   for experts the cache does not admit (ExpertStore::new's capacity and
-   scratch_slots), and the policy; until it is called a context holds one
-   layer's experts (capacity n_expert, no scratch, LFRU). It forgets what the
+   kc_expert_cache_reserve sets `capacity` cache slots, `scratch` slots for
+   experts the cache does not admit, `spec` slots for predictions it does
+   not admit (ExpertStore::new's capacity, scratch_slots and spec_slots) and
+   the policy; until it is called a context holds one layer's experts
+   (capacity n_expert, no scratch or spec slots, LFRU). It forgets what the
    slots held and resets the counters.
 
    kc_expert_prefetch is ExpertStore::prefetch (expert.rs:451-521): starts
-   copying experts of `layer` that are not resident, on a copy stream, when
-   the cache admits them; never waits. The whole-model path (kc_model_*)
+   copying experts of `layer` that are not resident, on a copy stream, into
+   cache slots when the cache admits them, else into the speculative slots
+   (replacing the oldest landed guess; paused for 4096 predictions when
+   fewer than half of the last 128 were used); never waits. The whole-model path (kc_model_*)
    calls it itself, as the router lookahead of transformer.rs:432-436,
    498-508 does: for steps of at most 4 rows, the next streamed layer's
    experts are predicted from the current post-attention state
@@ -194,12 +197,14 @@ enum {
   KC_XS_READS = 14,          /* host -> HBM copies issued                     */
   KC_XS_FORCED = 15,         /* admitted without the policy's consent: scratch slots exhausted */
   KC_XS_SCRATCH = 16,
-  KC_XS_N = 17
+  KC_XS_SPEC = 17,
+  KC_XS_SPEC_PAUSES = 18,    /* speculative pool paused for low accuracy     */
+  KC_XS_N = 19
 };
 KC_API int kc_upload_experts_streamed(kc_ctx* ctx, int layer, int n_expert, int d, int ff, int t_gate,
                                       const void* gate, int t_up, const void* up, int t_down, const void* down,
                                       int src_on_device);
-KC_API int kc_expert_cache_reserve(kc_ctx* ctx, int capacity, int scratch, int policy);
+KC_API int kc_expert_cache_reserve(kc_ctx* ctx, int capacity, int scratch, int spec, int policy);
 KC_API int kc_expert_prefetch(kc_ctx* ctx, int layer, const int32_t* experts, int n);
 KC_API int kc_expert_cache_stats(const kc_ctx* ctx, uint64_t* out, int n);
 KC_API int kc_expert_cache_decay(kc_ctx* ctx);

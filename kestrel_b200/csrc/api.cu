@@ -155,22 +155,23 @@ struct Model;  // the dense decode path of a whole model (kc_model_*)
 // buffers of the per-call slot table and the routed ids read back to the host.
 struct ExpertStreams {
   ExpertCache cache;
-  int capacity = -1, scratch = 0;  // slots; capacity -1: not reserved (default at first use)
+  int capacity = -1, scratch = 0, spec = 0;  // slots; capacity -1: not reserved (default at first use)
   ExpertPolicy policy = ExpertPolicy::Lfru;
   int64_t slot_bytes = 0;          // one expert's [gate | up | down]; shared by every streamed layer
-  uint8_t* arena = nullptr;        // [capacity + scratch][slot_bytes]
+  uint8_t* arena = nullptr;        // [capacity + scratch + spec][slot_bytes]
   int* slot_dev = nullptr;         // slot table of the current call, [table_e]
   int* slot_host = nullptr;        // its pinned source
   int table_e = 0;
   int32_t* ids_host = nullptr;     // pinned: a call's routed ids, then the lookahead's
   int ids_cap = 0;
   cudaStream_t copy = nullptr;     // prefetch copies
-  std::vector<cudaEvent_t> ready;  // per cache slot: its latest prefetch copy
+  std::vector<cudaEvent_t> ready;  // per slot: its latest prefetch copy
   int n_layers = 0;                // streamed layers uploaded
   bool lookahead = true;           // KC_OPT_LOOKAHEAD
   // Lookahead predictions awaiting their layer's call (recall counters).
   std::map<int, std::vector<int>> predicted;
-  // A lookahead's ids on the device, read back at the next demand sync.
+  // A lookahead's ids on the device (written on the auxiliary stream), read
+  // back at the next demand synchronisation.
   int look_layer = -1;
   const int32_t* look_ids = nullptr;
   int look_n = 0;
@@ -483,7 +484,7 @@ int streams_invalidate(kc_ctx* ctx) {
   ExpertStreams& S = ctx->xs;
   if (S.copy) CK(cudaStreamSynchronize(S.copy));
   CK(cudaStreamSynchronize(ctx->stream));
-  if (S.arena) S.cache.configure(S.capacity, S.scratch, S.policy);
+  if (S.arena) S.cache.configure(S.capacity, S.scratch, S.spec, S.policy);
   S.predicted.clear();
   S.look_layer = -1;
   S.look_ids = nullptr;
@@ -496,9 +497,9 @@ int streams_alloc(kc_ctx* ctx, int n_expert) {
   if (S.arena) return KC_OK;
   if (S.capacity < 0) {
     S.capacity = n_expert;
-    S.scratch = 0;
+    S.scratch = S.spec = 0;
   }
-  const int slots = S.capacity + S.scratch;
+  const int slots = S.capacity + S.scratch + S.spec;
   if (slots < 1) return fail(ctx, KC_ERR_STATE, "host-streamed experts: no slots reserved");
   if (cudaMalloc(&S.arena, (size_t)slots * S.slot_bytes) != cudaSuccess) {
     cudaGetLastError();
@@ -507,24 +508,24 @@ int streams_alloc(kc_ctx* ctx, int n_expert) {
                 (long long)S.slot_bytes);
   }
   if (!S.copy) CK(cudaStreamCreateWithFlags(&S.copy, cudaStreamNonBlocking));
-  S.ready.resize(S.capacity, nullptr);
+  S.ready.resize(slots, nullptr);
   for (cudaEvent_t& e : S.ready)
     if (!e) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-  S.cache.configure(S.capacity, S.scratch, S.policy);
+  S.cache.configure(S.capacity, S.scratch, S.spec, S.policy);
   return KC_OK;
 }
 
 // Prefetch copies that have landed (ExpertBuf's ticket done).
 void streams_refresh(ExpertStreams& S) {
-  for (int s = 0; s < S.capacity; ++s)
+  for (int s = 0; s < S.cache.slots(); ++s)
     if (S.cache.pending(s) && cudaEventQuery(S.ready[s]) == cudaSuccess) S.cache.mark_done(s);
   cudaGetLastError();  // cudaErrorNotReady is not an error of the call
 }
 
 // ExpertStore::prefetch for `experts` (ascending, unique) of streamed layer
-// Lt: copies on the copy stream, each recording its slot's event. The policy
-// picks no slot that work in flight reads (the latest demand call's experts)
-// or that a copy is still filling.
+// Lt: copies on the copy stream into cache or speculative slots, each
+// recording its slot's event. The policy picks no slot that work in flight
+// reads (the latest demand call's experts) or that a copy is still filling.
 int streams_prefetch(kc_ctx* ctx, const Layer& Lt, const std::vector<int>& experts) {
   ExpertStreams& S = ctx->xs;
   if (experts.empty()) return KC_OK;
@@ -573,10 +574,11 @@ int streams_demand(kc_ctx* ctx, const Layer& L, const int32_t* ids_dev, int A, L
     S.table_e = E;
   }
   if (A > 0) CK(cudaMemcpyAsync(S.ids_host, ids_dev, (size_t)A * 4, cudaMemcpyDeviceToHost, st));
-  if (look_n) CK(cudaMemcpyAsync(S.ids_host + A, S.look_ids, (size_t)look_n * 4, cudaMemcpyDeviceToHost, st));
+  if (look_n) CK(cudaMemcpyAsync(S.ids_host + A, S.look_ids, (size_t)look_n * 4, cudaMemcpyDeviceToHost, ctx->aux));
   // Synchronises: every earlier call's kernels are complete after this, so
   // their slots may be overwritten by this call's copies.
   RC(check_status(ctx));
+  if (look_n) CK(cudaStreamSynchronize(ctx->aux));
   streams_refresh(S);
   auto unique_ids = [&](const int32_t* ids, int n, int n_exp) {
     std::vector<char> seen(n_exp, 0);
@@ -656,8 +658,8 @@ int streams_lookahead_now(kc_ctx* ctx) {
   auto it = ctx->layers.find(nl);
   if (it == ctx->layers.end() || !it->second.streamed) return KC_OK;
   RC(grow_pinned(ctx, (void**)&S.ids_host, S.ids_cap, n, 4));
-  CK(cudaMemcpyAsync(S.ids_host, ids_dev, (size_t)n * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  RC(check_status(ctx));
+  CK(cudaMemcpyAsync(S.ids_host, ids_dev, (size_t)n * 4, cudaMemcpyDeviceToHost, ctx->aux));
+  CK(cudaStreamSynchronize(ctx->aux));
   const int E = it->second.n_expert;
   std::vector<char> seen(E, 0);
   for (int i = 0; i < n; ++i)
@@ -1592,8 +1594,10 @@ int model_finalize(kc_ctx* ctx, Model& m) {
 // Transformer::lookahead_prefetch (transformer.rs:498-508) for layer l + 1
 // after layer l's attention: RMSNorm of the residual with l + 1's FFN norm,
 // its router and top-k, then ExpertStore::prefetch of the predicted experts.
-// The ids are read back at layer l's own demand synchronisation when l is
-// host-streamed, else here.
+// The three kernels run on the auxiliary stream beside layer l's routing.
+// Their ids are read back at layer l's own demand synchronisation when l is
+// host-streamed, else here; either way the auxiliary stream is drained
+// before the residual is next written (the following layer's first norm).
 int model_lookahead(kc_ctx* ctx, Model& m, int l, int n) {
   auto it = ctx->layers.find(l + 1);
   if (it == ctx->layers.end() || !it->second.streamed || !it->second.has_router || m.L[l + 1].gate.w) return KC_OK;
@@ -1602,6 +1606,10 @@ int model_lookahead(kc_ctx* ctx, Model& m, int l, int n) {
   cudaStream_t st = ctx->stream;
   const int E = R.n_expert, k = R.k;
   if (!m.look) CK(cudaMalloc(&m.look, (size_t)4 * (m.d + 1024 + 2 * 64) * 4));
+  RC(ensure_aux(ctx));
+  CK(cudaEventRecord(ctx->ev_fork, st));
+  CK(cudaStreamWaitEvent(ctx->aux, ctx->ev_fork, 0));
+  st = ctx->aux;
   float* look_h = m.look;
   float* logits = look_h + 4 * m.d;
   int32_t* ids = reinterpret_cast<int32_t*>(logits + 4 * 1024);
@@ -1875,7 +1883,7 @@ int kc_sync(kc_ctx* ctx) {
 
 int64_t kc_device_bytes(const kc_ctx* ctx) {
   if (!ctx) return 0;
-  const int64_t slots = ctx->xs.arena ? (int64_t)(ctx->xs.capacity + ctx->xs.scratch) * ctx->xs.slot_bytes : 0;
+  const int64_t slots = ctx->xs.arena ? (int64_t)ctx->xs.cache.slots() * ctx->xs.slot_bytes : 0;
   return ctx->weight_bytes + (int64_t)ctx->ws.bytes + (int64_t)ctx->ws_ep.bytes + slots;
 }
 
@@ -2040,26 +2048,27 @@ int kc_upload_experts_streamed(kc_ctx* ctx, int layer, int n_expert, int d, int 
   return KC_OK;
 }
 
-int kc_expert_cache_reserve(kc_ctx* ctx, int capacity, int scratch, int policy) {
+int kc_expert_cache_reserve(kc_ctx* ctx, int capacity, int scratch, int spec, int policy) {
   if (!ctx) return KC_ERR_ARG;
   ctx->err.clear();
-  if (capacity < 0 || scratch < 0 || capacity + scratch < 1 ||
+  if (capacity < 0 || scratch < 0 || spec < 0 || capacity + scratch < 1 ||
       (policy != KC_EXPERT_POLICY_LFRU && policy != KC_EXPERT_POLICY_LRU))
-    return fail(ctx, KC_ERR_ARG, "kc_expert_cache_reserve: capacity %d, scratch %d, policy %d", capacity, scratch,
-                policy);
+    return fail(ctx, KC_ERR_ARG, "kc_expert_cache_reserve: capacity %d, scratch %d, spec %d, policy %d", capacity,
+                scratch, spec, policy);
   cudaSetDevice(ctx->device);
   ExpertStreams& S = ctx->xs;
   RC(streams_invalidate(ctx));
   cudaFree(S.arena);
   S.arena = nullptr;
-  while ((int)S.ready.size() > capacity) {
+  while ((int)S.ready.size() > capacity + scratch + spec) {
     cudaEventDestroy(S.ready.back());
     S.ready.pop_back();
   }
   S.capacity = capacity;
   S.scratch = scratch;
+  S.spec = spec;
   S.policy = policy == KC_EXPERT_POLICY_LRU ? ExpertPolicy::Lru : ExpertPolicy::Lfru;
-  S.cache.configure(capacity, scratch, S.policy);
+  S.cache.configure(capacity, scratch, spec, S.policy);
   // With a streamed layer already uploaded the slots are made now, so that a
   // reservation HBM cannot hold fails here rather than in a later call.
   if (S.slot_bytes) RC(streams_alloc(ctx, capacity));
@@ -2094,7 +2103,8 @@ int kc_expert_cache_stats(const kc_ctx* ctx, uint64_t* out, int n) {
   const uint64_t v[KC_XS_N] = {(uint64_t)std::max(0, S.capacity), (uint64_t)S.cache.cached(), c.requests, c.hits,
                                c.late, c.misses, c.scratch_loads, c.bytes_read, c.prefetch_issued, c.prefetch_used,
                                c.prefetch_wasted, c.evictions, c.lookahead_predicted, c.lookahead_correct, c.reads,
-                               c.forced, (uint64_t)std::max(0, S.scratch)};
+                               c.forced, (uint64_t)std::max(0, S.scratch), (uint64_t)std::max(0, S.spec),
+                               c.spec_pauses};
   for (int i = 0; i < n; ++i) out[i] = i < KC_XS_N ? v[i] : 0;
   return KC_OK;
 }

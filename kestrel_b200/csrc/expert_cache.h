@@ -4,7 +4,7 @@
 // It restates ExpertStore's cache (crates/kestrel-memory/src/expert.rs):
 //   score / victim / admit / touch   expert.rs:305-356
 //   get                              expert.rs:358-424 (one demand use)
-//   prefetch                         expert.rs:451-521 (the admissible part)
+//   prefetch (+ speculative pool)    expert.rs:451-521
 //   request                          expert.rs:523-537
 //   record_lookahead / decay         expert.rs:539-551
 // and the order Transformer::moe_ffn visits a call's experts (ready ones
@@ -21,8 +21,8 @@
 // * when the call's non-admitted experts outnumber the scratch slots, the
 //   rest are admitted by force (LRU victim) instead of waiting for a scratch
 //   buffer;
-// * predictions the cache does not admit are not loaded (no speculative
-//   pool): a GPU slot taken by a guess is a slot a demand load cannot use.
+// * the speculative pool has its own slots (after the scratch slots), and a
+//   slot a demand call read is not reloaded before that call's kernels end.
 #pragma once
 
 #include <algorithm>
@@ -38,7 +38,7 @@ enum class ExpertPolicy { Lfru = 0, Lru = 1 };  // expert.rs:35-38
 struct ExpertCacheStats {
   uint64_t requests = 0, hits = 0, late = 0, misses = 0, scratch_loads = 0, bytes_read = 0;
   uint64_t prefetch_issued = 0, prefetch_used = 0, prefetch_wasted = 0, evictions = 0;
-  uint64_t lookahead_predicted = 0, lookahead_correct = 0, reads = 0, forced = 0;
+  uint64_t lookahead_predicted = 0, lookahead_correct = 0, reads = 0, forced = 0, spec_pauses = 0;
 };
 
 class ExpertCache {
@@ -48,13 +48,17 @@ class ExpertCache {
     int slot;
   };
 
-  // capacity cache slots [0, capacity) and scratch slots [capacity,
-  // capacity + scratch). Clears all state.
-  void configure(int capacity, int scratch, ExpertPolicy policy) {
+  // Slots: cache [0, capacity), scratch [capacity, capacity + scratch),
+  // speculative pool [capacity + scratch, + spec). Clears all state.
+  void configure(int capacity, int scratch, int spec, ExpertPolicy policy) {
     capacity_ = std::max(0, capacity);
     scratch_ = std::max(0, scratch);
+    spec_n_ = std::max(0, spec);
     policy_ = policy;
     slots_.assign(capacity_, Slot{});
+    spec_.clear();
+    spec_slot_.assign(spec_n_, SpecSlot{});
+    spec_issued_ = spec_used_ = spec_paused_ = 0;
     where_.clear();
     heat_.clear();
     last_.clear();
@@ -65,7 +69,8 @@ class ExpertCache {
   }
   int capacity() const { return capacity_; }
   int scratch() const { return scratch_; }
-  int slots() const { return capacity_ + scratch_; }
+  int spec() const { return spec_n_; }
+  int slots() const { return capacity_ + scratch_ + spec_n_; }
   int cached() const { return n_cached_; }
   const ExpertCacheStats& stats() const { return stats_; }
   void add_bytes(uint64_t bytes, uint64_t reads) {
@@ -78,11 +83,17 @@ class ExpertCache {
     auto it = where_.find(key(layer, e));
     return it == where_.end() ? -1 : it->second;
   }
-  // Whether cache slot s still waits for a prefetch copy.
-  bool pending(int s) const { return s >= 0 && s < capacity_ && slots_[s].pending; }
+  // Whether slot s (cache or speculative) still waits for a prefetch copy.
+  bool pending(int s) const {
+    if (s >= 0 && s < capacity_) return slots_[s].pending;
+    const int i = s - capacity_ - scratch_;
+    return i >= 0 && i < spec_n_ && spec_slot_[i].pending;
+  }
   // The prefetch copy into slot s has landed (ExpertBuf's ticket done).
   void mark_done(int s) {
     if (s >= 0 && s < capacity_) slots_[s].pending = false;
+    const int i = s - capacity_ - scratch_;
+    if (i >= 0 && i < spec_n_) spec_slot_[i].pending = false;
   }
 
   // One MoE call of `layer` over the batch union `experts` (ascending ids,
@@ -146,6 +157,27 @@ class ExpertCache {
         slot_out[i] = it->second;
         continue;
       }
+      // Predicted by lookahead but not cached: served from the speculative
+      // pool (expert.rs:377-388); the slot is free again once this call ends.
+      const int si = spec_find(k);
+      if (si >= 0) {
+        const int s = spec_[si].slot;
+        spec_[si] = spec_.back();  // Vec::swap_remove
+        spec_.pop_back();
+        ++spec_used_;
+        ++stats_.prefetch_used;
+        SpecSlot& ss = spec_slot_[s - capacity_ - scratch_];
+        ss.held = false;
+        ss.call = call_;
+        if (!ss.pending) {
+          ++stats_.hits;
+        } else {
+          ++stats_.late;
+          waits.push_back(s);
+        }
+        slot_out[i] = s;
+        continue;
+      }
       ++stats_.misses;
       int s = admit(k, false, false);
       if (s < 0) {
@@ -194,10 +226,52 @@ class ExpertCache {
       const uint64_t k = key(layer, experts[i]);
       if (where_.count(k)) continue;
       const int s = admit(k, true, false);
-      if (s < 0) continue;
+      if (s >= 0) {
+        ++stats_.prefetch_issued;
+        slots_[s].pending = true;
+        loads.push_back({experts[i], s});
+        continue;
+      }
+      // Not admissible: load into the speculative pool instead, never
+      // displacing a cached expert, while the pool pays off.
+      if (spec_paused_ > 0) {
+        if (--spec_paused_ == 0) spec_issued_ = spec_used_ = 0;  // re-probe
+        continue;
+      }
+      if (spec_n_ == 0 || spec_find(k) >= 0) continue;
+      if (spec_issued_ >= 128) {
+        const double acc = (double)spec_used_ / (double)spec_issued_;
+        spec_issued_ = spec_used_ = 0;
+        if (acc < kSpecMinAccuracy) {
+          ++stats_.spec_pauses;
+          spec_paused_ = 4096;
+          continue;
+        }
+      }
+      int slot = -1;
+      if ((int)spec_.size() < spec_n_) {
+        // A pool slot no prediction holds and no call in flight reads.
+        for (int j = 0; j < spec_n_ && slot < 0; ++j)
+          if (!spec_slot_[j].held && spec_slot_[j].call != call_) slot = capacity_ + scratch_ + j;
+      } else {
+        // Replace the oldest speculative load whose copy has landed (a stale
+        // prediction).
+        for (size_t j = 0; j < spec_.size(); ++j)
+          if (!spec_slot_[spec_[j].slot - capacity_ - scratch_].pending) {
+            ++stats_.prefetch_wasted;
+            slot = spec_[j].slot;
+            spec_.erase(spec_.begin() + j);  // Vec::remove
+            break;
+          }
+      }
+      if (slot < 0) continue;
+      SpecSlot& ss = spec_slot_[slot - capacity_ - scratch_];
+      ss.held = true;
+      ss.pending = true;
+      spec_.push_back({k, slot});
+      ++spec_issued_;
       ++stats_.prefetch_issued;
-      slots_[s].pending = true;
-      loads.push_back({experts[i], s});
+      loads.push_back({experts[i], slot});
     }
   }
 
@@ -236,7 +310,24 @@ class ExpertCache {
     uint64_t call = 0;        // latest demand call that reads it
   };
 
+  struct Spec {
+    uint64_t k;
+    int slot;
+  };
+  struct SpecSlot {
+    bool held = false;     // holds a prediction listed in spec_
+    bool pending = false;  // its copy possibly still in flight
+    uint64_t call = 0;     // latest demand call that read it
+  };
+  static constexpr double kSpecMinAccuracy = 0.5;  // ExpertStore::spec_min_accuracy's default
+
   static uint64_t key(int layer, int e) { return ((uint64_t)(uint32_t)layer << 32) | (uint32_t)e; }
+
+  int spec_find(uint64_t k) const {
+    for (size_t j = 0; j < spec_.size(); ++j)
+      if (spec_[j].k == k) return (int)j;
+    return -1;
+  }
 
   uint64_t score(uint64_t k) const {
     auto li = last_.find(k);
@@ -311,7 +402,10 @@ class ExpertCache {
     return s;
   }
 
-  int capacity_ = 0, scratch_ = 0;
+  int capacity_ = 0, scratch_ = 0, spec_n_ = 0;
+  std::vector<Spec> spec_;           // speculative loads, oldest first
+  std::vector<SpecSlot> spec_slot_;  // [spec_n_]
+  uint64_t spec_issued_ = 0, spec_used_ = 0, spec_paused_ = 0;  // the pool's accuracy window
   ExpertPolicy policy_ = ExpertPolicy::Lfru;
   std::vector<Slot> slots_;
   std::unordered_map<uint64_t, int> where_;

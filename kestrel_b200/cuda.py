@@ -70,7 +70,7 @@ SIGNATURES = {
     "kc_load_gguf": (I, [P, ctypes.c_char_p, I, ctypes.c_char_p, I64]),
     "kc_gguf_inspect": (I, [ctypes.c_char_p, ctypes.c_char_p, I64]),
     "kc_upload_experts_streamed": (I, [P, I, I, I, I, I, P, I, P, I, P, I]),
-    "kc_expert_cache_reserve": (I, [P, I, I, I]),
+    "kc_expert_cache_reserve": (I, [P, I, I, I, I]),
     "kc_expert_prefetch": (I, [P, I, P, I]),
     "kc_expert_cache_stats": (I, [P, P, I]),
     "kc_expert_cache_decay": (I, [P]),
@@ -83,7 +83,7 @@ OPT_LOOKAHEAD = 2
 EXPERT_POLICY_LFRU, EXPERT_POLICY_LRU = 0, 1
 XS_COUNTERS = ["capacity", "cached", "requests", "hits", "late", "misses", "scratch_loads", "bytes_read",
                "prefetch_issued", "prefetch_used", "prefetch_wasted", "evictions", "lookahead_predicted",
-               "lookahead_correct", "reads", "forced", "scratch"]
+               "lookahead_correct", "reads", "forced", "scratch", "spec", "spec_pauses"]
 ARCH_LLAMA, ARCH_QWEN2, ARCH_QWEN3 = 0, 1, 2
 (T_ATTN_NORM, T_ATTN_Q, T_ATTN_K, T_ATTN_V, T_ATTN_OUT, T_ATTN_Q_BIAS, T_ATTN_K_BIAS, T_ATTN_V_BIAS,
  T_ATTN_Q_NORM, T_ATTN_K_NORM, T_FFN_NORM, T_FFN_GATE, T_FFN_UP, T_FFN_DOWN) = range(14)
@@ -204,8 +204,11 @@ class Context:
         self._check(lib().kc_upload_experts_streamed(self.h, layer, n_expert, d, ff, t_gate, _ptr(gate), t_up,
                                                      _ptr(up), t_down, _ptr(down), int(dev)))
 
-    def expert_cache_reserve(self, capacity: int, scratch: int = 0, policy: int = EXPERT_POLICY_LFRU):
-        self._check(lib().kc_expert_cache_reserve(self.h, capacity, scratch, policy))
+    def expert_cache_reserve(self, capacity: int, scratch: int = 0, policy: int = EXPERT_POLICY_LFRU,
+                             spec: int | None = None):
+        """spec: speculative slots (default max(1, scratch), as ExpertStore::new sets)."""
+        spec = max(1, scratch) if spec is None else spec
+        self._check(lib().kc_expert_cache_reserve(self.h, capacity, scratch, spec, policy))
 
     def expert_prefetch(self, layer: int, experts):
         ids = np.ascontiguousarray(np.asarray(experts, dtype=np.int32))

@@ -33,6 +33,18 @@ seeds) in lockstep: each prompt is prefilled alone (kc_model_prefill_seq,
 all B timed together), then kc_model_decode_seqs runs n_gen + 1 tokens per
 sequence -- n_gen steps of B rows, each row computed as a batch of one --
 timed alone. The value counts B * n_gen tokens per decode time.
+
+--forced: the decode steps are fed seeded random tokens (one kc_model_forward
+of one row each) instead of the greedy token: with random weights greedy
+decoding soon repeats one token and routes every step to the same experts,
+while forced tokens route like varied text.
+
+--streamed SLOTS: every layer's experts stay in pinned host memory
+(kc_upload_experts_streamed) and are copied on demand into SLOTS HBM cache
+slots (+ --scratch slots; --policy lfru|lru), with router lookahead unless
+--no-lookahead. The line then carries the cache counters of the decode steps
+(hits, misses, prefetches, bytes copied), their host->HBM GB/s, and a plain
+pinned host->device copy rate measured in the same process for scale.
 """
 from __future__ import annotations
 
@@ -51,7 +63,7 @@ C3 = dict(name="qwen3-30b-a3b-decode", arch=synth.ARCH_QWEN3, n_layer=48, d=2048
           dense_ff=0)
 
 
-def load_on_gpu(ctx, torch, cfg, n_ctx, seed=0, block=None):
+def load_on_gpu(ctx, torch, cfg, n_ctx, seed=0, block=None, streamed=False):
     """Declare cfg and make every weight on the GPU (N(0, 0.02) quantized with
     kc_quantize_dev; norms 1.0). With an expert block (expert parallelism)
     only that block of every layer's experts is uploaded; the weights are
@@ -91,7 +103,9 @@ def load_on_gpu(ctx, torch, cfg, n_ctx, seed=0, block=None):
         gate = quant(cfg["t_gate"], E * ff, d)
         up = quant(cfg["t_gate"], E * ff, d)
         down = quant(cfg["t_down"], E * d, ff)
-        if block is None:
+        if streamed:
+            ctx.upload_experts_streamed(l, E, d, ff, cfg["t_gate"], gate, cfg["t_gate"], up, cfg["t_down"], down)
+        elif block is None:
             ctx.upload_experts(l, E, d, ff, cfg["t_gate"], gate, cfg["t_gate"], up, cfg["t_down"], down)
         else:
             r0, r1 = block.first, block.first + block.count
@@ -113,6 +127,23 @@ def step_bytes(cfg, experts_per_layer) -> int:
     return cfg["n_layer"] * (attn + router + experts_per_layer * expert) + head
 
 
+def pinned_h2d_gbs(torch, nbytes=1 << 30, reps=5) -> float:
+    """A plain host->device copy from pinned memory (the bound on streamed
+    experts), CUDA events, GB/s."""
+    src = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    dst.copy_(src, non_blocking=True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        dst.copy_(src, non_blocking=True)
+    b.record()
+    b.synchronize()
+    gbs = reps * nbytes / (a.elapsed_time(b) / 1e3) / 1e9
+    del src, dst
+    return gbs
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", choices=["c0", "c3"], default="c0")
@@ -122,11 +153,16 @@ def main():
     ap.add_argument("--f32-prefill", action="store_true")
     ap.add_argument("--no-warmup", action="store_true", help="skip the warm-up generation (profiling runs)")
     ap.add_argument("--batch", type=int, default=1, help="independent sequences decoded in lockstep")
+    ap.add_argument("--streamed", type=int, default=0, help="HBM cache slots for host-streamed experts (0: resident)")
+    ap.add_argument("--scratch", type=int, default=128)
+    ap.add_argument("--policy", choices=["lfru", "lru"], default="lfru")
+    ap.add_argument("--no-lookahead", action="store_true")
+    ap.add_argument("--forced", action="store_true", help="decode steps on seeded random tokens (teacher forcing)")
     args = ap.parse_args()
     import os
 
     import torch
-    from .cuda import OPT_F32_PREFILL, Context
+    from .cuda import EXPERT_POLICY_LRU, EXPERT_POLICY_LFRU, OPT_F32_PREFILL, OPT_LOOKAHEAD, Context
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -150,7 +186,7 @@ def main():
         if world > 1:
             from . import ep
             block = ep.expert_block(cfg["n_expert"], world, rank)
-        synth.load_cuda(ctx, synth.make_model(cfg, seed=0), n_ctx, block=block)
+        synth.load_cuda(ctx, synth.make_model(cfg, seed=0), n_ctx, block=block, streamed=args.streamed > 0)
     else:
         cfg = dict(C3)
         n_prompt, n_gen = args.prompt or 512, args.gen or 256
@@ -158,7 +194,11 @@ def main():
         if world > 1:
             from . import ep
             block = ep.expert_block(cfg["n_expert"], world, rank)
-        load_on_gpu(ctx, torch, cfg, n_ctx, block=block)
+        load_on_gpu(ctx, torch, cfg, n_ctx, block=block, streamed=args.streamed > 0)
+    if args.streamed:
+        ctx.expert_cache_reserve(args.streamed, args.scratch,
+                                 EXPERT_POLICY_LRU if args.policy == "lru" else EXPERT_POLICY_LFRU)
+        ctx.set_option(OPT_LOOKAHEAD, 0 if args.no_lookahead else 1)
     if world > 1:
         # Every layer call (prompt chunks of up to 256 tokens, decode steps of
         # one) exchanges through peer memory.
@@ -187,8 +227,15 @@ def main():
         # Decode alone: continue from the cached prompt with its greedy token;
         # every one of the n_gen forwards is a one-row decode step.
         torch.cuda.synchronize()
+        xs0 = ctx.expert_cache_stats()
+        forced = [int(t) for t in np.random.default_rng(97).integers(0, cfg["n_vocab"], n_gen)]
         ev[2].record(stream)
-        toks = [first] + list(ctx.model_generate([first], n_gen))
+        if args.forced:
+            toks = [first]
+            for t in forced:
+                toks.append(ctx.model_forward([t])[1])
+        else:
+            toks = [first] + list(ctx.model_generate([first], n_gen))
         ev[3].record(stream)
         ev[3].synchronize()
         t_decode = max(1e-9, ev[2].elapsed_time(ev[3]) / 1e3)
@@ -206,6 +253,7 @@ def main():
         t_prefill = ev[0].elapsed_time(ev[1]) / 1e3
         # n_gen + 1 tokens per sequence: the pending token, then n_gen steps.
         torch.cuda.synchronize()
+        xs0 = ctx.expert_cache_stats()
         ev[2].record(stream)
         out = ctx.model_decode_seqs(B, n_gen + 1)
         ev[3].record(stream)
@@ -213,6 +261,7 @@ def main():
         t_decode = max(1e-9, ev[2].elapsed_time(ev[3]) / 1e3)
         assert [o[0] for o in out] == firsts
         toks = out[0]
+    xs1 = ctx.expert_cache_stats()
     if world > 1:
         import torch.distributed as dist
         tt = torch.tensor([t_decode, t_prefill], dtype=torch.float64)
@@ -236,9 +285,21 @@ def main():
         "timing": "CUDA events on the library's stream: the prompts' prefill, then the decode steps alone "
                   + ("(kc_model_generate continuing from the cached prompt)" if B == 1 else
                      "(kc_model_decode_seqs after kc_model_prefill_seq of every sequence)"),
-        "f32_prefill": bool(args.f32_prefill), "tokens_head": toks[:8],
+        "f32_prefill": bool(args.f32_prefill), "tokens_head": toks[:8], "forced_tokens": bool(args.forced),
         "prompt_logits_finite": finite, "prompt_logits_absmax": absmax,
     }
+    if args.streamed:
+        dx = {k: xs1[k] - xs0[k] for k in xs1 if k not in ("capacity", "scratch", "spec", "cached")}
+        line["streamed"] = {
+            "slots": args.streamed, "scratch": args.scratch, "policy": args.policy,
+            "lookahead": not args.no_lookahead, "slot_bytes_note": "one expert's gate + up + down",
+            "host_store_bytes": cfg["n_layer"] * cfg["n_expert"] * (
+                2 * cfg["ff"] * G.bytes_for(cfg["t_gate"], cfg["d"]) + cfg["d"] * G.bytes_for(cfg["t_down"], cfg["ff"])),
+            "decode": dx, "hit_rate": dx["hits"] / max(1, dx["requests"]),
+            "lookahead_recall": dx["lookahead_correct"] / max(1, dx["lookahead_predicted"]),
+            "h2d_gbs": dx["bytes_read"] / t_decode / 1e9,
+            "h2d_copy_peak_gbs": pinned_h2d_gbs(torch),
+        }
     if rank == 0:
         print(json.dumps(line))
     ctx.close()

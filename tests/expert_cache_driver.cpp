@@ -1,6 +1,6 @@
 // Drives kestrel_b200/csrc/expert_cache.h from a text script on stdin (used
 // by tests/test_expert_cache.py, on the CPU). One command per line:
-//   config <capacity> <scratch> <policy 0=LFRU 1=LRU>
+//   config <capacity> <scratch> <policy 0=LFRU 1=LRU> [<spec slots>]
 //   demand <layer> <n> <e1> ... <en>   -> "D <slots...> | <expert:slot loads...> | <wait slots...>" or "D fail"
 //   prefetch <layer> <n> <e1> ... <en> -> "P <expert:slot loads...>"
 //   done <slot>                        (a prefetch copy landed)
@@ -8,7 +8,7 @@
 //   slot <layer> <e>                   -> "S <slot or -1>"
 //   heat <layer> <e>                   -> "H <heat> <last>"
 //   stats                              -> "T <requests hits late misses scratch_loads prefetch_issued
-//                                          prefetch_used prefetch_wasted evictions forced cached>"
+//                                          prefetch_used prefetch_wasted evictions forced cached spec_pauses>"
 #include <iostream>
 #include <sstream>
 #include <string>
@@ -26,9 +26,9 @@ int main() {
     std::string cmd;
     if (!(in >> cmd)) continue;
     if (cmd == "config") {
-      int cap, scr, pol;
-      in >> cap >> scr >> pol;
-      c.configure(cap, scr, pol ? kc::ExpertPolicy::Lru : kc::ExpertPolicy::Lfru);
+      int cap, scr, pol, spec = 0;
+      in >> cap >> scr >> pol >> spec;
+      c.configure(cap, scr, spec, pol ? kc::ExpertPolicy::Lru : kc::ExpertPolicy::Lfru);
     } else if (cmd == "demand" || cmd == "prefetch") {
       int layer, n;
       in >> layer >> n;
@@ -70,7 +70,7 @@ int main() {
       const kc::ExpertCacheStats& s = c.stats();
       std::cout << "T " << s.requests << ' ' << s.hits << ' ' << s.late << ' ' << s.misses << ' ' << s.scratch_loads
                 << ' ' << s.prefetch_issued << ' ' << s.prefetch_used << ' ' << s.prefetch_wasted << ' '
-                << s.evictions << ' ' << s.forced << ' ' << c.cached() << '\n';
+                << s.evictions << ' ' << s.forced << ' ' << c.cached() << ' ' << s.spec_pauses << '\n';
     } else {
       std::cerr << "unknown command " << cmd << '\n';
       return 2;

@@ -45,7 +45,7 @@ def prefetch(layer, experts):
 
 
 STATS = ["requests", "hits", "late", "misses", "scratch_loads", "prefetch_issued", "prefetch_used",
-         "prefetch_wasted", "evictions", "forced", "cached"]
+         "prefetch_wasted", "evictions", "forced", "cached", "spec_pauses"]
 
 
 def stats(line):
@@ -138,6 +138,37 @@ def test_prefetch_used_wasted_late(driver):
     assert stats(out[2])["prefetch_wasted"] == 1
 
 
+def test_speculative_pool(driver):
+    """LFRU with a full cache: a cold prediction is not admitted, so it goes
+    to a speculative slot (after the scratch slots); the call that routes to
+    it is served from there (prefetch used); a full pool replaces its oldest
+    landed guess (prefetch wasted)."""
+    hot = ["config 2 1 0 2"] + [demand(0, [1, 2])] * 6
+    out = run(driver, hot + [prefetch(0, [5]), "done 3", demand(0, [1, 2, 5]), "stats"])
+    assert out[6] == "P 5:3"
+    assert out[7] == "D 0 1 3 | |"
+    s = stats(out[8])
+    assert (s["prefetch_issued"], s["prefetch_used"], s["hits"], s["misses"]) == (1, 1, 10 + 3, 2)
+    # two guesses fill the pool; a third replaces the oldest landed one
+    out = run(driver, hot + [prefetch(0, [5, 6]), "done 3", prefetch(0, [7]), "stats"])
+    assert out[6] == "P 5:3 6:4"
+    assert out[7] == "P 7:3"
+    assert stats(out[8])["prefetch_wasted"] == 1
+
+
+def test_speculative_pool_pauses_when_unused(driver):
+    """After 128 speculative loads of which fewer than half were used, the
+    pool pauses for the next 4096 non-admissible predictions
+    (expert.rs:470-487)."""
+    script = ["config 1 0 0 1"] + [demand(0, [0])] * 4
+    for i in range(129):
+        script += [prefetch(0, [1 + i % 50]), "done 1"]
+    script += ["stats"]
+    out = run(driver, script)
+    s = stats(out[-1])
+    assert s["spec_pauses"] == 1 and s["prefetch_issued"] == 128 and s["prefetch_wasted"] == 127
+
+
 def test_decay_halves_heat(driver):
     out = run(driver, ["config 4 0 0"] + [demand(0, [1])] * 5 + [demand(0, [2])] + ["decay", "heat 0 1",
                                                                                    "heat 0 2", "decay", "heat 0 2"])
@@ -150,8 +181,12 @@ class RefCache:
     non-admitted experts take scratch slots, then forced LRU admissions;
     predictions are loaded only when admitted."""
 
-    def __init__(self, capacity, scratch, lru):
-        self.cap, self.scr, self.lru = capacity, scratch, lru
+    def __init__(self, capacity, scratch, lru, spec=0):
+        self.cap, self.scr, self.lru, self.nspec = capacity, scratch, lru, spec
+        self.spec = []                     # [(key, slot)], oldest first
+        self.sslot = [dict(held=False, pending=False, call=0) for _ in range(spec)]
+        self.window = [0, 0]               # speculative loads issued, used
+        self.paused = 0
         self.slots = [None] * capacity   # slot -> dict(key, prefetched, pending, call)
         self.where = {}
         self.heat, self.last = {}, {}
@@ -235,6 +270,23 @@ class RefCache:
                 sl["call"] = self.call
                 slot[e] = self.where[k]
                 continue
+            j = next((j for j, (kk, _) in enumerate(self.spec) if kk == k), None)
+            if j is not None:
+                s = self.spec[j][1]
+                self.spec[j] = self.spec[-1]
+                self.spec.pop()
+                self.window[1] += 1
+                self.st["prefetch_used"] += 1
+                ss = self.sslot[s - self.cap - self.scr]
+                ss["held"] = False
+                ss["call"] = self.call
+                if ss["pending"]:
+                    self.st["late"] += 1
+                    waits.append(s)
+                else:
+                    self.st["hits"] += 1
+                slot[e] = s
+                continue
             self.st["misses"] += 1
             s = self.admit(k, False)
             if s is None:
@@ -271,17 +323,51 @@ class RefCache:
             if k in self.where:
                 continue
             s = self.admit(k, True)
-            if s is None:
+            if s is not None:
+                self.st["prefetch_issued"] += 1
+                self.slots[s]["pending"] = True
+                loads.append((e, s))
                 continue
+            if self.paused:
+                self.paused -= 1
+                if self.paused == 0:
+                    self.window = [0, 0]
+                continue
+            if self.nspec == 0 or any(kk == k for kk, _ in self.spec):
+                continue
+            if self.window[0] >= 128:
+                acc = self.window[1] / self.window[0]
+                self.window = [0, 0]
+                if acc < 0.5:
+                    self.st["spec_pauses"] += 1
+                    self.paused = 4096
+                    continue
+            slot = None
+            if len(self.spec) < self.nspec:
+                slot = next((self.cap + self.scr + j for j, ss in enumerate(self.sslot)
+                             if not ss["held"] and ss["call"] != self.call), None)
+            else:
+                j = next((j for j, (_, s2) in enumerate(self.spec)
+                          if not self.sslot[s2 - self.cap - self.scr]["pending"]), None)
+                if j is not None:
+                    self.st["prefetch_wasted"] += 1
+                    slot = self.spec.pop(j)[1]
+            if slot is None:
+                continue
+            ss = self.sslot[slot - self.cap - self.scr]
+            ss["held"] = ss["pending"] = True
+            self.spec.append((k, slot))
+            self.window[0] += 1
             self.st["prefetch_issued"] += 1
-            self.slots[s]["pending"] = True
-            loads.append((e, s))
+            loads.append((e, slot))
         self.need = None
         return "P" + "".join(f" {e}:{s}" for e, s in loads)
 
     def done(self, s):
         if 0 <= s < self.cap and self.slots[s] is not None:
             self.slots[s]["pending"] = False
+        if 0 <= s - self.cap - self.scr < self.nspec:
+            self.sslot[s - self.cap - self.scr]["pending"] = False
 
     def decay(self):
         self.heat = {k: h >> 1 for k, h in self.heat.items() if h >> 1}
@@ -295,10 +381,10 @@ class RefCache:
 @pytest.mark.parametrize("seed", range(6))
 def test_random_traces_match_restatement(driver, lru, seed):
     rnd = random.Random(seed * 2 + lru)
-    cap, scr = rnd.randint(2, 10), rnd.randint(0, 4)
+    cap, scr, spec = rnd.randint(2, 10), rnd.randint(0, 4), rnd.randint(0, 3)
     n_exp, layers = rnd.choice([6, 12, 24]), rnd.randint(1, 3)
-    ref = RefCache(cap, scr, lru)
-    script, want = [f"config {cap} {scr} {lru}"], []
+    ref = RefCache(cap, scr, lru, spec)
+    script, want = [f"config {cap} {scr} {lru} {spec}"], []
     for _ in range(300):
         r = rnd.random()
         layer = rnd.randrange(layers)
@@ -314,7 +400,7 @@ def test_random_traces_match_restatement(driver, lru, seed):
             script.append(prefetch(layer, experts))
             want.append(ref.prefetch(layer, experts))
         elif r < 0.93:
-            s = rnd.randrange(cap)
+            s = rnd.randrange(cap + scr + spec)
             script.append(f"done {s}")
             ref.done(s)
         else:
