@@ -393,7 +393,8 @@ int check_status(kc_ctx* ctx) {
                                   "expert-parallel peer exchange (another rank did not publish)",
                                   "expert-parallel exchange (the ranks chose different paths, peer memory "
                                   "and NCCL, in one call: every rank must be on the same side of the "
-                                  "kc_ep_reserve capacity)"};
+                                  "kc_ep_reserve capacity)",
+                                  "tcgen05 producer (a slot tile larger than the launch's bound)"};
     const int site = st >> 8;
     return fail(ctx, st & 0xFF, "a kernel's bounded wait expired (status %d) at: %s", st & 0xFF,
                 site >= 0 && site < (int)(sizeof(sites) / sizeof(sites[0])) ? sites[site] : "unknown");
@@ -810,6 +811,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.out_stride = ff;
     ma.status = ctx->status;
     ma.wide = (int64_t)A > 256LL * E;  // more than 256 rows per expert expected
+    ma.bn = std::min(n_rows, kMmaTileN);  // a token adds at most one row to an expert
     RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(ff, 128), lst));
     CKL();
   } else if (any_large) {
@@ -893,6 +895,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.out_stride = d;
     ma.status = ctx->status;
     ma.wide = (int64_t)A > 256LL * E;
+    ma.bn = std::min(n_rows, kMmaTileN);
     RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(d, 128), lst));
     CKL();
   } else if (any_large) {
@@ -1033,6 +1036,7 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     ma.out_stride = out_stride;
     ma.status = ctx->status;
     ma.wide = n > 256;
+    ma.bn = std::min(n, kMmaTileN);
     RC(launch_mma_grouped(ma, tmap, ceil_div(n, kMmaTileN) * ceil_div(D.rows, 128), st));
   } else {
     a.list = M.large_list;

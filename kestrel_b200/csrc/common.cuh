@@ -203,7 +203,7 @@ __device__ __forceinline__ bool count_wait(const int* c, int target, int* status
 enum : int {
   W_DEC_EMPTY = 1, W_DEC_FULL = 2, W_DEC_DRAIN = 3, W_MMA_RAW_EMPTY = 4, W_MMA_OP_EMPTY_P = 5, W_MMA_DRAIN = 6,
   W_MMA_OP_FULL = 7, W_MMA_ACC_EMPTY = 8, W_MMA_RAW_FULL = 9, W_MMA_OP_EMPTY_D = 10, W_MMA_ACC_FULL = 11,
-  W_ROUTER = 12, W_MMA_TC_DRAIN = 13, W_DEC_PREV = 14, W_EP_PEER = 15, W_EP_PATH = 16
+  W_ROUTER = 12, W_MMA_TC_DRAIN = 13, W_DEC_PREV = 14, W_EP_PEER = 15, W_EP_PATH = 16, W_MMA_BOUND = 17
 };
 
 // ---- bulk async copy (TMA, non-tensor): global -> shared ------------------

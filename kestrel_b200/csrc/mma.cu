@@ -34,10 +34,10 @@ constexpr int MK = 64;        // K elements per operand stage (one 128B swizzle 
 constexpr int MN = kMmaTileN; // slots per tile (N of the MMA: up to 256)
 constexpr int M_DQW = 8;      // dequantisation + epilogue warps (two per row: one per 32-element half)
 constexpr int M_THREADS = 64 + 32 * M_DQW;
-constexpr int M_OPS_MAX = 3;  // operand stages (fewer where shared memory is short)
+constexpr int M_OPS_MAX = 6;  // operand stages: as many as shared memory holds, 2 .. 6
 constexpr int M_RAWS = 2;     // raw superblock stages
 constexpr int A_BYTES = MM * MK * 2;  // 16 KB
-constexpr int B_BYTES = MN * MK * 2;  // 32 KB
+constexpr int B_BYTES = MN * MK * 2;  // 32 KB: the activation tile of 256 slots
 
 __host__ __device__ constexpr int max_sbt_bytes(int t) { return t == T_Q4_K ? 4608 : t == T_Q6_K ? 6720 : 8704; }
 constexpr int M_RT = MM / kTileRows;  // row tiles per M tile
@@ -51,19 +51,31 @@ __host__ __device__ constexpr int mma_raw_bytes(int t, int mi) {
   return ((mi * M_RT * max_sbt_bytes(t) + 1023) / 1024) * 1024;
 }
 __host__ __device__ constexpr int mma_op_bytes(int mi, int nt) { return mi * A_BYTES + nt * B_BYTES; }
+// Dynamic shared memory of a launch: 227 KB per block less the kernel's
+// static arrays (~4.2 KB, mostly the list prefix pp_s).
+constexpr int M_SMEM_CAP = 227 * 1024 - 5 * 1024;
 __host__ __device__ constexpr bool mma_fits(int t, int mi, int nt, int ops) {
-  return ops * mma_op_bytes(mi, nt) + M_RAWS * mma_raw_bytes(t, mi) + 1024 <= 227 * 1024;
+  return ops * mma_op_bytes(mi, nt) + M_RAWS * mma_raw_bytes(t, mi) + 1024 <= M_SMEM_CAP;
 }
-// Operand stages: three where they fit in 227 KB of shared memory, else two.
-__host__ __device__ constexpr int mma_ops(int t, int mi, int nt) { return mma_fits(t, mi, nt, 3) ? 3 : 2; }
+// Rows of the TMA box (and of the activation stage) for tiles of up to n
+// slots: 16, 32, 64, 128 or 256.
+__host__ __device__ inline int box_rows(int n) {
+  return n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : 256;
+}
+// Stage geometry of a launch whose tiles hold at most bn slots (0: 256): the
+// activation part of an operand stage holds box_rows(bn) rows, and there are
+// as many operand stages as the shared memory holds (2 .. M_OPS_MAX).
 struct MmaSmem {
-  int op_bytes, raw_bytes, total;
+  int op_bytes, b_bytes, raw_bytes, ops, total;
 };
-__host__ __device__ inline MmaSmem mma_smem(int t, int mi, int nt) {
+__host__ __device__ inline MmaSmem mma_smem(int t, int mi, int nt, int bn) {
   MmaSmem s;
-  s.op_bytes = mma_op_bytes(mi, nt);
+  s.b_bytes = box_rows(bn > 0 ? bn : MN) * MK * 2;
+  s.op_bytes = mi * A_BYTES + nt * s.b_bytes;
   s.raw_bytes = mma_raw_bytes(t, mi);
-  s.total = mma_ops(t, mi, nt) * s.op_bytes + M_RAWS * s.raw_bytes + 1024;  // + alignment slack
+  const int room = M_SMEM_CAP - 1024 - M_RAWS * s.raw_bytes;
+  s.ops = room / s.op_bytes < 2 ? 2 : (room / s.op_bytes > M_OPS_MAX ? M_OPS_MAX : room / s.op_bytes);
+  s.total = s.ops * s.op_bytes + M_RAWS * s.raw_bytes + 1024;  // + alignment slack
   return s;
 }
 constexpr int MMA_MAX_LIST = 1024;  // experts of one launch's tcgen05 list
@@ -119,14 +131,60 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
 }
 
 // ---- dequantisation of one row's 64-element K chunk into the A tile ----------
+// Raw superblocks and the A tile are addressed through the 32-bit shared
+// window (explicit ld/st.shared). Pairs of elements go through the packed
+// f32x2 instructions, which round each lane exactly as the scalar ones do.
+__device__ __forceinline__ uint4 m_lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint16_t m_lds16(uint32_t a) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// f16x2 of the two lanes (lane 0 in the low half), each rounded to nearest.
+__device__ __forceinline__ uint32_t f2_h2(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Exact floats 2^23 + byte i and 2^23 + byte i+1 of w: each byte is placed
+// under the exponent of 2^23 (full-rate byte permutes).
+__device__ __forceinline__ uint64_t bytes_f2(uint32_t w, int i) {
+  return f2_pack(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)i)),
+                 __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)(i + 1))));
+}
+
 // Element k of row m goes to byte (m/8)*1024 + (m%8)*128 + ((k/8 ^ m%8)*16) +
-// (k%8)*2: the canonical K-major SWIZZLE_128B layout.
-__device__ __forceinline__ void put8(uint8_t* A, int m, int c, const float v[8]) {
-  __half2 h[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-  *reinterpret_cast<uint4*>(A + (m >> 3) * 1024 + (m & 7) * 128 + ((c ^ (m & 7)) << 4)) =
-      *reinterpret_cast<uint4*>(h);
+// (k%8)*2: the canonical K-major SWIZZLE_128B layout; h holds 8 elements.
+__device__ __forceinline__ void put8(uint32_t A, int m, int c, const uint32_t h[4]) {
+  const uint32_t a = A + (m >> 3) * 1024 + (m & 7) * 128 + ((c ^ (m & 7)) << 4);
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
+               : "memory");
 }
 
 // Scale and min of Q4_K sub-block jj (scale_min_k4, quant.rs:54-60).
@@ -142,86 +200,86 @@ __device__ __forceinline__ void mma_q4k_sm(int jj, uint32_t w0, uint32_t w1, uin
   }
 }
 
-// Exact float of byte i of w (0..255): the byte is placed under the exponent
-// of 2^23 and 2^23 + `bias` is subtracted, with full-rate instructions.
-__device__ __forceinline__ float byte_f(uint32_t w, int i, float bias) {
-  return __fsub_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)i)), bias);
-}
-
 // Half `hf` (32 elements) of the 64-element K chunk kk of a row, per type.
 // Q4_K (quant.rs:138-155): y = (d*sc)*q - dmin*m; half 0 = sub-block 2kk (low
 // nibbles), half 1 = sub-block 2kk+1 (high nibbles). d*sc has at most 17
 // significant bits (an f16 times a 6-bit scale), so (d*sc)*q (q < 16) is exact
 // in f32 and one fma(d*sc, q, -dmin*m) rounds exactly as the reference's
-// multiply then subtract.
-__device__ __forceinline__ void dq_q4k(const uint8_t* sbt, int rr, int kk, int hf, uint8_t* A, int m) {
-  const uint4 hdr = *reinterpret_cast<const uint4*>(sbt + 16 * rr);
+// multiply then subtract. High nibbles are read in place as 16q with the
+// scale d*sc/16 (a power-of-two step: the same exact product).
+__device__ __forceinline__ void dq_q4k(uint32_t sbt, int rr, int kk, int hf, uint32_t A, int m) {
+  const uint4 hdr = m_lds128(sbt + 16 * rr);
+  const uint4 q0 = m_lds128(sbt + kPlane + kPlane * (2 * kk) + 16 * rr);
+  const uint4 q1 = m_lds128(sbt + kPlane + kPlane * (2 * kk + 1) + 16 * rr);
   const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
   int sc, mn;
   mma_q4k_sm(2 * kk + hf, hdr.y, hdr.z, hdr.w, sc, mn);
-  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
-  const uint4 q0 = *reinterpret_cast<const uint4*>(sbt + kPlane + kPlane * (2 * kk) + 16 * rr);
-  const uint4 q1 = *reinterpret_cast<const uint4*>(sbt + kPlane + kPlane * (2 * kk + 1) + 16 * rr);
+  const float d1 = __fmul_rn(__fmul_rn(d, (float)sc), hf ? 0.0625f : 1.0f), m1 = __fmul_rn(dmin, (float)mn);
+  const uint64_t dd = f2_pack(d1, d1), mm = f2_pack(-m1, -m1), bias = f2_pack(8388608.0f, 8388608.0f);
+  const uint32_t mask = hf ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
   const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    float v[8];
+    uint32_t h[4];
 #pragma unroll
     for (int h2 = 0; h2 < 2; ++h2) {
-      const uint32_t nw = (hf ? (qw[2 * c + h2] >> 4) : qw[2 * c + h2]) & 0x0F0F0F0Fu;
+      const uint32_t nw = qw[2 * c + h2] & mask;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[4 * h2 + i] = __fmaf_rn(d1, byte_f(nw, i, 8388608.0f), -m1);
+      for (int p = 0; p < 2; ++p) h[2 * h2 + p] = f2_h2(f2_fma(dd, f2_sub(bytes_f2(nw, 2 * p), bias), mm));
     }
-    put8(A, m, 4 * hf + c, v);
+    put8(A, m, 4 * hf + c, h);
   }
 }
 
 // Q6_K (quant.rs:180-201): y = (d*sc)*(q-32).
-__device__ __forceinline__ void dq_q6k(const uint8_t* sbt, int rr, int kk, int hf, uint8_t* A, int m) {
+__device__ __forceinline__ void dq_q6k(uint32_t sbt, int rr, int kk, int hf, uint32_t A, int m) {
   const int h = kk >> 1, nib = kk & 1, r2 = 2 * nib + hf;
-  const float d = h2f(*reinterpret_cast<const uint16_t*>(sbt + 13 * kPlane + 2 * rr));
-  const uint4 scw = *reinterpret_cast<const uint4*>(sbt + 12 * kPlane + 16 * rr);
   // ql bytes 64h + 32hf .. +31 = chunks 4h + 2hf (+1); qh bytes 32h .. +31 = chunks 2h (+1).
-  const uint8_t* qlp = sbt + kPlane * (4 * h + 2 * hf) + 16 * rr;
-  const uint8_t* qhp = sbt + 8 * kPlane + kPlane * (2 * h) + 16 * rr;
-  const uint4 l0 = *reinterpret_cast<const uint4*>(qlp), l1 = *reinterpret_cast<const uint4*>(qlp + kPlane);
-  const uint4 h0 = *reinterpret_cast<const uint4*>(qhp), h1 = *reinterpret_cast<const uint4*>(qhp + kPlane);
+  const uint32_t qlp = sbt + kPlane * (4 * h + 2 * hf) + 16 * rr;
+  const uint32_t qhp = sbt + 8 * kPlane + kPlane * (2 * h) + 16 * rr;
+  const uint4 l0 = m_lds128(qlp), l1 = m_lds128(qlp + kPlane);
+  const uint4 h0 = m_lds128(qhp), h1 = m_lds128(qhp + kPlane);
+  const uint4 scw = m_lds128(sbt + 12 * kPlane + 16 * rr);
+  const float d = h2f(m_lds16(sbt + 13 * kPlane + 2 * rr));
   const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
   const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  const uint64_t bias = f2_pack(8388640.0f, 8388640.0f);  // 2^23 + 32: q - 32
 #pragma unroll
   for (int c = 0; c < 4; ++c) {  // 8 elements l = 8c .. 8c+7
     const int si = 8 * h + 2 * r2 + (c >> 1);
     const uint32_t swd = (si >> 3) ? ((si >> 2) & 1 ? scw.w : scw.z) : ((si >> 2) & 1 ? scw.y : scw.x);
     const float dsc = __fmul_rn(d, (float)(int)(int8_t)((swd >> (8 * (si & 3))) & 0xFF));
-    float v[8];
+    const uint64_t dd = f2_pack(dsc, dsc);
+    uint32_t hv[4];
 #pragma unroll
     for (int h2 = 0; h2 < 2; ++h2) {
       const int wi = 2 * c + h2;
       const uint32_t qv = ((lw[wi] >> (4 * nib)) & 0x0F0F0F0Fu) | (((hw[wi] >> (2 * r2)) & 0x03030303u) << 4);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[4 * h2 + i] = __fmul_rn(dsc, byte_f(qv, i, 8388640.0f));  // q - 32
+      for (int p = 0; p < 2; ++p) hv[2 * h2 + p] = f2_h2(f2_mul(dd, f2_sub(bytes_f2(qv, 2 * p), bias)));
     }
-    put8(A, m, 4 * hf + c, v);
+    put8(A, m, 4 * hf + c, hv);
   }
 }
 
 // Q8_0 (quant.rs:82-89): y = q*d; half hf = block 2kk + hf of the chunk.
-__device__ __forceinline__ void dq_q8_0(const uint8_t* cb, int nblk, int rr, int kk, int hf, uint8_t* A, int m) {
+__device__ __forceinline__ void dq_q8_0(uint32_t cb, int nblk, int rr, int kk, int hf, uint32_t A, int m) {
   const int b = 2 * kk + hf;
-  const float d = h2f(*reinterpret_cast<const uint16_t*>(cb + 2 * kPlane * nblk + 16 * rr + 2 * b));
-  const uint4 q0 = *reinterpret_cast<const uint4*>(cb + kPlane * (2 * b) + 16 * rr);
-  const uint4 q1 = *reinterpret_cast<const uint4*>(cb + kPlane * (2 * b + 1) + 16 * rr);
+  const uint4 q0 = m_lds128(cb + kPlane * (2 * b) + 16 * rr);
+  const uint4 q1 = m_lds128(cb + kPlane * (2 * b + 1) + 16 * rr);
+  const float d = h2f(m_lds16(cb + 2 * kPlane * nblk + 16 * rr + 2 * b));
+  const uint64_t dd = f2_pack(d, d), bias = f2_pack(8388736.0f, 8388736.0f);  // 2^23 + 128
   const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    float v[8];
+    uint32_t h[4];
 #pragma unroll
     for (int h2 = 0; h2 < 2; ++h2) {
       const uint32_t uw = qw[2 * c + h2] ^ 0x80808080u;  // q + 128 per byte
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[4 * h2 + i] = __fmul_rn(byte_f(uw, i, 8388736.0f), d);
+      for (int p = 0; p < 2; ++p) h[2 * h2 + p] = f2_h2(f2_mul(f2_sub(bytes_f2(uw, 2 * p), bias), dd));
     }
-    put8(A, m, 4 * hf + c, v);
+    put8(A, m, 4 * hf + c, h);
   }
 }
 
@@ -281,13 +339,28 @@ __device__ __forceinline__ int split_count(const MmaArgs& a, int total, int nsb)
   return s >= 2 ? s : 1;
 }
 
+// Position in the operand-stage ring (its size is a launch value): slot and
+// phase parity advance with each stage instead of dividing every time.
+struct OpRing {
+  int it = 0, slot = 0, n;
+  uint32_t ph = 0;
+  __device__ explicit OpRing(int n_) : n(n_) {}
+  __device__ void next() {
+    ++it;
+    if (++slot == n) {
+      slot = 0;
+      ph ^= 1u;
+    }
+  }
+};
+
 template <int T, int NMAT, int MI, int NT>
 __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs a,
                                                                      const __grid_constant__ MmaMapsDev maps) {
   static_assert(MI * NT <= 2 && NMAT % MI == 0, "at most two accumulators of 256 columns");
+  static_assert(mma_fits(T, MI, NT, 2), "two operand stages of 256-slot tiles fit");
   pdl_enter();
   extern __shared__ uint8_t msm_raw[];
-  constexpr int M_OPS = mma_ops(T, MI, NT);
   __shared__ __align__(8) uint64_t raw_full[M_RAWS], raw_empty[M_RAWS], op_full[M_OPS_MAX], op_empty[M_OPS_MAX];
   __shared__ __align__(8) uint64_t acc_full, acc_empty;
   __shared__ uint32_t tmem_base_sh;
@@ -319,7 +392,8 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
   const int S = split_count(a, total, nsb);
   const int items = total * S;
   if ((int)blockIdx.x >= items) return;
-  const MmaSmem L = mma_smem(T, MI, NT);
+  const MmaSmem L = mma_smem(T, MI, NT, a.bn);
+  const int M_OPS = L.ops;
   uint8_t* msm = msm_raw + ((1024 - (smem_u32(msm_raw) & 1023)) & 1023);
   uint8_t* ops = msm;
   uint8_t* raws = msm + M_OPS * L.op_bytes;
@@ -358,7 +432,8 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
 
   if (warp == 0) {
     if (lane == 0) {
-      int raw_it = 0, op_it = 0;
+      int raw_it = 0;
+      OpRing op(M_OPS);
       for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
         const Tile t = tile_of<NMAT, MI, NT>(a, pp_s, w / S, row_tiles, n_large);
         int kc0, kc1;
@@ -367,6 +442,14 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
         // Only the rows each tile uses: boxes of 16 .. 256 rows.
         int bx[2] = {box_index(t.nt[0]), t.np > 1 ? box_index(t.nt[1]) : 0};
         const uint32_t b_bytes = (uint32_t)(MK * 2 * ((16 << bx[0]) + (t.np > 1 ? (16 << bx[1]) : 0)));
+        // A tile larger than the launch's bound (the host's promise) would
+        // overrun its stage: report it and stop (the other roles' bounded
+        // waits then end).
+        if ((16 << bx[0]) * MK * 2 > L.b_bytes || (t.np > 1 && (16 << bx[1]) * MK * 2 > L.b_bytes)) {
+          report(a.status, KC_ERR_SHAPE | (W_MMA_BOUND << 8));
+          ok = false;
+          break;
+        }
         for (int kc = kc0; kc < kc1 && ok; ++kc) {
           const int sb = kc >> 2;
           if ((kc & 3) == 0) {
@@ -387,25 +470,27 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
             }
             ++raw_it;
           }
-          const int o = op_it % M_OPS;
-          if (op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status, W_MMA_OP_EMPTY_P)) {
+          const int o = op.slot;
+          if (op.it >= M_OPS && !mbar_wait(&op_empty[o], op.ph ^ 1u, a.status, W_MMA_OP_EMPTY_P)) {
             ok = false;
             break;
           }
           mbar_expect_tx(&op_full[o], b_bytes);
           for (int p = 0; p < t.np; ++p)
-            tma_load_2d(ops + o * L.op_bytes + MI * A_BYTES + p * B_BYTES, &maps.m[bx[p]], kc * MK,
+            tma_load_2d(ops + o * L.op_bytes + MI * A_BYTES + p * L.b_bytes, &maps.m[bx[p]], kc * MK,
                         t.slot0 + t.t0 + p * MN, &op_full[o]);
-          ++op_it;
+          op.next();
         }
       }
       // Drain: every issued copy lands before the CTA may exit.
+      const int op_it = op.it;
       for (int i = std::max(0, op_it - M_OPS); i < op_it; ++i)
         mbar_wait(&op_full[i % M_OPS], (i / M_OPS) & 1, a.status, W_MMA_DRAIN);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      int op_it = 0, tile_it = 0;
+      int tile_it = 0;
+      OpRing op(M_OPS);
       for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++tile_it) {
         const Tile t = tile_of<NMAT, MI, NT>(a, pp_s, w / S, row_tiles, n_large);
         int kc0, kc1;
@@ -419,8 +504,8 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
         }
         tc_fence_after();
         for (int kc = kc0; kc < kc1; ++kc) {
-          const int o = op_it % M_OPS;
-          if (!mbar_wait(&op_full[o], (op_it / M_OPS) & 1, a.status, W_MMA_OP_FULL)) {
+          const int o = op.slot;
+          if (!mbar_wait(&op_full[o], op.ph, a.status, W_MMA_OP_FULL)) {
             ok = false;
             break;
           }
@@ -436,16 +521,17 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
 #pragma unroll
               for (int p = 0; p < NT; ++p)
                 if (p < t.np)
-                  umma_f16(tmem + (mt * NT + p) * MN, ad, sw128_desc(sbb + p * B_BYTES + 32 * k16), idesc[p], acc);
+                  umma_f16(tmem + (mt * NT + p) * MN, ad, sw128_desc(sbb + p * L.b_bytes + 32 * k16), idesc[p], acc);
             }
           }
           umma_commit(&op_empty[o]);
-          ++op_it;
+          op.next();
         }
         if (!ok) break;
         umma_commit(&acc_full);
       }
       // Drain: the tensor core has finished with TMEM before it is freed.
+      const int op_it = op.it;
       if (op_it > 0) mbar_wait(&op_empty[(op_it - 1) % M_OPS], ((op_it - 1) / M_OPS) & 1, a.status, W_MMA_TC_DRAIN);
     }
   } else {
@@ -453,7 +539,8 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
     // and half hf = t / 128 of each 64-element K chunk.
     const int t_dq = tid - 64, m = t_dq & (MM - 1), hf = t_dq >> 7;
     const int rt_local = m / kTileRows, rr = m % kTileRows;
-    int raw_it = 0, op_it = 0, tile_it = 0;
+    int raw_it = 0, tile_it = 0;
+    OpRing op(M_OPS);
     // Every dequantisation warp runs every item (failed waits only skip the
     // work), so all of them reach the named barriers below equally often.
     for (int w = blockIdx.x; w < items; w += gridDim.x, ++tile_it) {
@@ -468,13 +555,13 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
           r = raw_it % M_RAWS;
           if (ok && !mbar_wait(&raw_full[r], (raw_it / M_RAWS) & 1, a.status, W_MMA_RAW_FULL)) ok = false;
         }
-        const int o = op_it % M_OPS;
-        if (ok && op_it >= M_OPS && !mbar_wait(&op_empty[o], ((op_it / M_OPS) & 1) ^ 1, a.status, W_MMA_OP_EMPTY_D)) ok = false;
+        const int o = op.slot;
+        if (ok && op.it >= M_OPS && !mbar_wait(&op_empty[o], op.ph ^ 1u, a.status, W_MMA_OP_EMPTY_D)) ok = false;
         if (ok) {
 #pragma unroll
           for (int mt = 0; mt < MI; ++mt) {
-            uint8_t* A = ops + o * L.op_bytes + mt * A_BYTES;
-            const uint8_t* sbt = raws + r * L.raw_bytes + (mt * M_RT + rt_local) * max_sbt_bytes(T);
+            const uint32_t A = smem_u32(ops + o * L.op_bytes + mt * A_BYTES);
+            const uint32_t sbt = smem_u32(raws + r * L.raw_bytes + (mt * M_RT + rt_local) * max_sbt_bytes(T));
             if (T == T_Q4_K) dq_q4k(sbt, rr, kk, hf, A, m);
             else if (T == T_Q6_K) dq_q6k(sbt, rr, kk, hf, A, m);
             else dq_q8_0(sbt, min(8, a.cols / 32 - 8 * sb), rr, kk, hf, A, m);
@@ -483,7 +570,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&op_full[o]);
-        ++op_it;
+        op.next();
         if (kk == 3 || kc == kc1 - 1) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&raw_empty[r]);
@@ -593,9 +680,10 @@ bool mma_supported(int t, int64_t cols, int n_mat) {
 
 template <int T, int NMAT, int MI, int NT>
 static int launch_t(const MmaArgs& a, const MmaMaps& maps, int max_tiles, cudaStream_t st, int max_ctas) {
-  const MmaSmem L = mma_smem(T, MI, NT);
+  const MmaSmem L = mma_smem(T, MI, NT, a.bn);
   static PerDeviceOnce attr;
-  if (smem_attr_once(attr, mma_grouped_kernel<T, NMAT, MI, NT>, L.total) != cudaSuccess) return KC_ERR_CUDA;
+  // Every stage geometry stays within M_SMEM_CAP: the attribute is set once to that.
+  if (smem_attr_once(attr, mma_grouped_kernel<T, NMAT, MI, NT>, M_SMEM_CAP) != cudaSuccess) return KC_ERR_CUDA;
   // With a split-K workspace every SM gets a CTA (the kernel splits K when the
   // batch has few tiles); otherwise one CTA per tile at most.
   const int cap = max_ctas > 0 ? std::min(max_ctas, num_sms()) : num_sms();

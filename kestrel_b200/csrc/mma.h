@@ -30,6 +30,10 @@ struct MmaArgs {
   // dequantised once for up to 512 slots) over gate+up pairs x one tile: set
   // when experts are expected to hold more than 256 rows.
   int wide;
+  // Most slots any tile of the launch holds (0: 256): sizes the activation
+  // part of each operand stage, so that small tiles leave room for more
+  // stages. A tile above it is reported as KC_ERR_SHAPE.
+  int bn;
 };
 // Bytes of the split-K workspace a launch may use: partial tiles for one work
 // item per SM, and one counter per SM.
