@@ -812,6 +812,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.status = ctx->status;
     ma.wide = (int64_t)A > 256LL * E;  // more than 256 rows per expert expected
     ma.bn = std::min(n_rows, kMmaTileN);  // a token adds at most one row to an expert
+    ma.read_once = n_rows <= kMmaTileN;
     RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(ff, 128), lst));
     CKL();
   } else if (any_large) {
@@ -896,6 +897,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.status = ctx->status;
     ma.wide = (int64_t)A > 256LL * E;
     ma.bn = std::min(n_rows, kMmaTileN);
+    ma.read_once = n_rows <= kMmaTileN;
     RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(d, 128), lst));
     CKL();
   } else if (any_large) {
@@ -1037,6 +1039,7 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     ma.status = ctx->status;
     ma.wide = n > 256;
     ma.bn = std::min(n, kMmaTileN);
+    ma.read_once = n <= kMmaTileN;
     RC(launch_mma_grouped(ma, tmap, ceil_div(n, kMmaTileN) * ceil_div(D.rows, 128), st));
   } else {
     a.list = M.large_list;

@@ -216,6 +216,23 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
       : "memory");
 }
 
+// L2 eviction-priority policies (createpolicy) for the cache hints below:
+// weights streamed once are read evict_first.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// bulk_g2s with an L2 cache-policy hint.
+__device__ __forceinline__ void bulk_g2s_hint(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // ---- Kestrel arithmetic helpers -------------------------------------------
 // scale_min_k4 (crates/kestrel-engine/src/quant.rs:54-60) for all eight
 // sub-blocks of a Q4_K superblock, from the 12 packed scale bytes held in

@@ -234,6 +234,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
     // All 32 lanes of the producer warps run the loops (the named barrier
     // counts whole warps); lanes >= DUP issue nothing.
     int last = -1;  // highest stage number this lane issued
+    const uint64_t wpol = l2_evict_first();  // weights are read once
     const int w = warp * DUP + lane;
     const bool lane_on = lane < DUP;
     bool ok = true;
@@ -272,7 +273,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
           if (active && sid < n_stages) {
             const uint32_t wbytes = (uint32_t)(off1 - off0);
             mbar_expect_tx(&full[sid], wbytes + stage_rec_bytes(sb0, sb1, rbytes));
-            bulk_g2s(ring + (int64_t)sid * g.stage_bytes, up + off0, wbytes, &full[sid]);
+            bulk_g2s_hint(ring + (int64_t)sid * g.stage_bytes, up + off0, wbytes, &full[sid], wpol);
           }
           off0 = off1;
         }
@@ -301,7 +302,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(DecodeArgs a, De
             uint8_t* dst = ring + (int64_t)st * g.stage_bytes;
             if (!weights_sent) {
               mbar_expect_tx(&full[st], wbytes + stage_rec_bytes(sb0, sb1, rbytes));
-              bulk_g2s(dst, up + off0, wbytes, &full[st]);
+              bulk_g2s_hint(dst, up + off0, wbytes, &full[st], wpol);
             }
             if (KQ) {
               // sb0 is even (a multiple of the even kStageSB, or 0 when one

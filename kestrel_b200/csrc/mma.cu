@@ -434,6 +434,7 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
     if (lane == 0) {
       int raw_it = 0;
       OpRing op(M_OPS);
+      const uint64_t wpol = l2_evict_first();
       for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
         const Tile t = tile_of<NMAT, MI, NT>(a, pp_s, w / S, row_tiles, n_large);
         int kc0, kc1;
@@ -465,8 +466,13 @@ __global__ void __launch_bounds__(M_THREADS, 1) mma_grouped_kernel(const MmaArgs
             for (int mt = 0; mt < MI; ++mt) {
               const uint8_t* src = a.w[t.m + mt] + (int64_t)expert_pos(a.slot, t.e - a.expert_base) * a.expert_stride +
                                    (int64_t)(M_RT * t.rt) * tile_bytes + tiled_sb_offset(T, a.cols, sb);
-              for (int x = 0; x < n_rt; ++x)
-                bulk_g2s(rbase + (mt * M_RT + x) * max_sbt_bytes(T), src + x * tile_bytes, sbytes, &raw_full[r]);
+              for (int x = 0; x < n_rt; ++x) {
+                if (a.read_once)
+                  bulk_g2s_hint(rbase + (mt * M_RT + x) * max_sbt_bytes(T), src + x * tile_bytes, sbytes,
+                                &raw_full[r], wpol);
+                else
+                  bulk_g2s(rbase + (mt * M_RT + x) * max_sbt_bytes(T), src + x * tile_bytes, sbytes, &raw_full[r]);
+              }
             }
             ++raw_it;
           }

@@ -34,6 +34,9 @@ struct MmaArgs {
   // part of each operand stage, so that small tiles leave room for more
   // stages. A tile above it is reported as KC_ERR_SHAPE.
   int bn;
+  // Every weight block is read by one work item only (no expert holds more
+  // than one slot tile): the raw copies then carry an L2 evict_first hint.
+  int read_once;
 };
 // Bytes of the split-K workspace a launch may use: partial tiles for one work
 // item per SM, and one counter per SM.
