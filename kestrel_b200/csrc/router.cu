@@ -440,8 +440,90 @@ __global__ void __launch_bounds__(DP_THREADS) dispatch_kernel(const int* __restr
 // earlier tokens in the mask. Slots are grouped by ascending expert id and
 // ascending token within an expert, as dispatch_block orders them.
 constexpr int RD_MAXT = DP_THREADS / 32;
-static size_t rd_smem(int E, int k) {
-  return ((size_t)RD_MAXT * (E + 2 * RT_MAXK) + 5 * (size_t)E + 5 + (size_t)RD_MAXT * k) * 4;
+// rec_bytes: the tokens' activation records (n_tok * d/256 * kRecK), held in
+// shared memory between their quantisation and the copies to the slots.
+static size_t rd_smem(int E, int k, size_t rec_bytes) {
+  return ((size_t)RD_MAXT * (E + 2 * RT_MAXK) + 5 * (size_t)E + 5 + (size_t)RD_MAXT * k) * 4 + 16 + rec_bytes;
+}
+
+// Warp 0 of route_dispatch_kernel: from the experts' token masks, the slot
+// offsets, each expert's place in the int8 or tcgen05 list, the tcgen05 tile
+// prefix and the totals. Lane l takes experts [e0, e1) (contiguous) and the
+// lanes' five partial counts (rows, int8-list entries by row count, tcgen05
+// entries, tcgen05 token tiles) are scanned exclusively through shared
+// memory (part_s, 5 x 32 ints) in five steps. The int8 list holds the 3-row
+// experts, then the 2-row, then the 1-row ones (ascending id within each), so
+// that the decode kernel's groups hold units of equal rows; the 3- and 2-row
+// counts are packed as 3-row | 2-row << 16 (each at most E <= 1024). Not
+// inlined: the kernel also runs it once on all-zero masks before it waits
+// for the router, off the critical path. (A register scan with warp shuffles
+// measured ~6,000 cycles here against ~1,000 for this one.)
+__device__ __noinline__ void rd_scan(const uint32_t* mask_s, int E, bool rows, int* offs_s, int* pos_s, int* tt_s,
+                                     int* tot_s, int* part_s, int lane) {
+  const int C = (E + 31) / 32, e0 = min(E, lane * C), e1 = min(E, e0 + C);
+  int v[5] = {0, 0, 0, 0, 0};  // rows, 3|2-row entries, 1-row (or rows-mode) entries, tcgen05 entries, tiles
+  for (int e = e0; e < e1; ++e) {
+    const int c = __popc(mask_s[e]);
+    v[0] += c;
+    if (rows) {
+      v[2] += (c + 2) / 3;
+      continue;
+    }
+    v[1] += c == 3 ? 1 : (c == 2 ? 1 << 16 : 0);
+    v[2] += c == 1 ? 1 : 0;
+    v[3] += c >= 4 ? 1 : 0;
+    v[4] += c >= 4 ? (c + kMmaTileN - 1) / kMmaTileN : 0;
+  }
+  // Inclusive Kogge-Stone scan of the five values over the 32 lanes.
+  int inc[5];
+#pragma unroll
+  for (int j = 0; j < 5; ++j) {
+    inc[j] = v[j];
+    part_s[j * 32 + lane] = v[j];
+  }
+  __syncwarp();
+#pragma unroll
+  for (int sh = 1; sh < 32; sh <<= 1) {
+    int add[5];
+#pragma unroll
+    for (int j = 0; j < 5; ++j) add[j] = lane >= sh ? part_s[j * 32 + lane - sh] : 0;
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 5; ++j) {
+      inc[j] += add[j];
+      part_s[j * 32 + lane] = inc[j];
+    }
+    __syncwarp();
+  }
+  const int ts = part_s[1 * 32 + 31], n1 = part_s[2 * 32 + 31];
+  const int n3 = ts & 0xFFFF, n2 = ts >> 16;
+  int oc = inc[0] - v[0], os = inc[1] - v[1], ol = inc[3] - v[3], ot = inc[4] - v[4];
+  int o3 = os & 0xFFFF, o2 = n3 + (os >> 16), o1 = n3 + n2 + (inc[2] - v[2]);
+  for (int e = e0; e < e1; ++e) {
+    const int c = __popc(mask_s[e]);
+    offs_s[e] = oc;
+    oc += c;
+    if (rows) {
+      pos_s[e] = o1;  // first of the expert's (c + 2) / 3 entries
+      o1 += (c + 2) / 3;
+    } else if (c == 3) {
+      pos_s[e] = o3++;
+    } else if (c == 2) {
+      pos_s[e] = o2++;
+    } else if (c == 1) {
+      pos_s[e] = o1++;
+    } else if (c >= 4) {
+      pos_s[e] = ol++;
+      tt_s[e] = ot;
+      ot += (c + kMmaTileN - 1) / kMmaTileN;
+    }
+  }
+  if (lane == 31) {
+    offs_s[E] = oc;
+    tot_s[0] = rows ? n1 : n3 + n2 + n1;
+    tot_s[1] = ol;
+    tot_s[2] = ot;
+  }
 }
 
 __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float* __restrict__ logits, int n_tok,
@@ -450,6 +532,7 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
                                                                      DispatchOut o, const float* __restrict__ x,
                                                                      int d, uint8_t* __restrict__ rec, bool rows) {
   extern __shared__ __align__(16) uint32_t dsm[];
+  __shared__ int part_s[5 * 32];                                  // rd_scan's partial counts
   const int SW = E + 2 * RT_MAXK;                                 // per-token scratch: p, selw, seli
   float* scratch = reinterpret_cast<float*>(dsm);                 // [RD_MAXT][SW]
   uint32_t* mask_s = dsm + RD_MAXT * SW;                          // [E] token mask per expert
@@ -457,9 +540,29 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
   int* pos_s = offs_s + E + 1;                                    // [E] place in the int8 / tcgen05 list
   int* tt_s = pos_s + E;                                          // [E] tcgen05 tile prefix
   int* tot_s = tt_s + E;                                          // [4] int8 entries, tcgen05 entries, tiles
-  int* slot_tok_s = tot_s + 4;                                    // [n_tok * k]
+  int* slot_tok_s = tot_s + 4;                                    // [RD_MAXT * k]
+  uint8_t* tokrec = reinterpret_cast<uint8_t*>(                   // [n_tok][d / 256] records
+      (reinterpret_cast<uintptr_t>(slot_tok_s + RD_MAXT * k) + 15) & ~uintptr_t(15));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = d / 256;
   for (int e = threadIdx.x; e < E; e += DP_THREADS) mask_s[e] = 0u;
+  __syncthreads();
+  // Before the wait for the router (its logits are the only input written by
+  // the previous kernel; x was complete before it started, and is read
+  // through L2): the tokens' activation records, which do not depend on the
+  // routing, into shared memory; and the dispatch scan once on the zero masks
+  // (instruction-cache warm-up; its shared outputs are rewritten below).
+  if (warp == 0) {
+    rd_scan(mask_s, E, rows, offs_s, pos_s, tt_s, tot_s, part_s, lane);
+  } else if (rec) {
+    for (int task = warp - 1; task < n_tok * nb; task += DP_THREADS / 32 - 1) {
+      const int t = task / nb, b = task - t * nb;
+      const float4* xp = reinterpret_cast<const float4*>(x + (int64_t)t * d + b * 256 + lane * 8);
+      const float4 a0 = __ldcg(xp), a1 = __ldcg(xp + 1);
+      const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      q8k_store_record(v, tokrec + (size_t)task * kRecK, lane);
+    }
+  }
   pdl_enter();
   float* p = scratch + warp * SW;
   float* selw = p + E;
@@ -503,73 +606,7 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
     }
   }
   __syncthreads();
-  if (warp == 0) {
-    // Experts [e0, e1) per lane, contiguous, then an exclusive warp scan of
-    // (rows, int8-list entries by row count, tcgen05-list entries, tcgen05
-    // token tiles). The int8 list holds the 3-row experts, then the 2-row,
-    // then the 1-row ones (ascending id within each), so that the decode
-    // kernel's groups hold units of equal rows. The 3- and 2-row counts are
-    // packed as 3-row | 2-row << 16 (each at most E <= 1024).
-    const int C = (E + 31) / 32, e0 = min(E, lane * C), e1 = min(E, e0 + C);
-    int sc = 0, ss = 0, s1 = 0, sl = 0, st = 0;
-    // rows (dispatch_block's): every expert in the int8 list, in entries of at
-    // most three rows; s1 then counts entries.
-    for (int e = e0; e < e1; ++e) {
-      const int c = __popc(mask_s[e]);
-      sc += c;
-      if (rows) {
-        s1 += (c + 2) / 3;
-        continue;
-      }
-      ss += c == 3 ? 1 : (c == 2 ? 1 << 16 : 0);
-      s1 += c == 1 ? 1 : 0;
-      sl += c >= 4 ? 1 : 0;
-      st += c >= 4 ? (c + kMmaTileN - 1) / kMmaTileN : 0;
-    }
-    int ic = sc, is = ss, i1 = s1, il = sl, it = st;
-#pragma unroll
-    for (int sh = 1; sh < 32; sh <<= 1) {
-      const int a0 = __shfl_up_sync(0xffffffffu, ic, sh), a1 = __shfl_up_sync(0xffffffffu, is, sh);
-      const int a2 = __shfl_up_sync(0xffffffffu, il, sh), a3 = __shfl_up_sync(0xffffffffu, it, sh);
-      const int a4 = __shfl_up_sync(0xffffffffu, i1, sh);
-      if (lane >= sh) {
-        ic += a0;
-        is += a1;
-        il += a2;
-        it += a3;
-        i1 += a4;
-      }
-    }
-    const int ts = __shfl_sync(0xffffffffu, is, 31), n1 = __shfl_sync(0xffffffffu, i1, 31);
-    const int n3 = ts & 0xFFFF, n2 = ts >> 16;
-    int oc = ic - sc, os = is - ss, ol = il - sl, ot = it - st;
-    int o3 = os & 0xFFFF, o2 = n3 + (os >> 16), o1 = n3 + n2 + (i1 - s1);
-    for (int e = e0; e < e1; ++e) {
-      const int c = __popc(mask_s[e]);
-      offs_s[e] = oc;
-      oc += c;
-      if (rows) {
-        pos_s[e] = o1;  // first of the expert's (c + 2) / 3 entries
-        o1 += (c + 2) / 3;
-      } else if (c == 3) {
-        pos_s[e] = o3++;
-      } else if (c == 2) {
-        pos_s[e] = o2++;
-      } else if (c == 1) {
-        pos_s[e] = o1++;
-      } else if (c >= 4) {
-        pos_s[e] = ol++;
-        tt_s[e] = ot;
-        ot += (c + kMmaTileN - 1) / kMmaTileN;
-      }
-    }
-    if (lane == 31) {
-      offs_s[E] = oc;
-      tot_s[0] = rows ? n1 : n3 + n2 + n1;
-      tot_s[1] = ol;
-      tot_s[2] = ot;
-    }
-  }
+  if (warp == 0) rd_scan(mask_s, E, rows, offs_s, pos_s, tt_s, tot_s, part_s, lane);
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += DP_THREADS) {
     const int c = __popc(mask_s[e]);
@@ -603,20 +640,19 @@ __global__ void __launch_bounds__(DP_THREADS) route_dispatch_kernel(const float*
   }
   if (!rec) return;
   __syncthreads();
-  const int nb = d / 256;
-  for (int task = warp; task < A * nb; task += DP_THREADS / 32) {
-    const int slot = task / nb, b = task - slot * nb;
-    const float* xp = x + (int64_t)slot_tok_s[slot] * d + b * 256 + lane * 8;
-    const float4 a0 = reinterpret_cast<const float4*>(xp)[0], a1 = reinterpret_cast<const float4*>(xp)[1];
-    const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    q8k_store_record(v, rec + rec_index(b, slot, A) * kRecK, lane);
+  // Each slot's records are its token's (16-byte copies from shared memory).
+  constexpr int R16 = kRecK / 16;
+  for (int i = threadIdx.x; i < A * nb * R16; i += DP_THREADS) {
+    const int slot = i / (nb * R16), r = i - slot * nb * R16, b = r / R16, j = r - b * R16;
+    const uint4 v = *reinterpret_cast<const uint4*>(tokrec + ((size_t)slot_tok_s[slot] * nb + b) * kRecK + 16 * j);
+    *reinterpret_cast<uint4*>(rec + rec_index(b, slot, A) * kRecK + 16 * j) = v;
   }
 }
 
 bool route_dispatch_supported(int n_tok, int E, int k, int d, bool with_records) {
   const bool tok_ok = with_records ? (n_tok < 4 && d % 256 == 0) : n_tok <= RD_MAXT;
   return n_tok >= 1 && tok_ok && E >= 1 && E <= DP_THREADS && k >= 1 && k <= RT_MAXK && k <= E &&
-         rd_smem(E, k) <= 200 * 1024;
+         rd_smem(E, k, with_records ? (size_t)n_tok * (d / 256) * kRecK : 0) <= 200 * 1024;
 }
 
 void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int norm_topk, float weights_scale, int* ids,
@@ -624,7 +660,8 @@ void launch_route_dispatch(const float* logits, int n_tok, int E, int k, int nor
                            bool rows) {
   static PerDeviceOnce attr;
   smem_attr_once(attr, route_dispatch_kernel, 200 * 1024);
-  launch_k(route_dispatch_kernel, 1, DP_THREADS, rd_smem(E, k), st, logits, n_tok, E, k, norm_topk, weights_scale,
+  launch_k(route_dispatch_kernel, 1, DP_THREADS, rd_smem(E, k, rec ? (size_t)n_tok * (d / 256) * kRecK : 0), st,
+           logits, n_tok, E, k, norm_topk, weights_scale,
            ids, w, o, x, d, rec, rows);
 }
 
