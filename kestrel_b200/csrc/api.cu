@@ -100,6 +100,14 @@ struct Work {
   // the MoE dispatch so that repeated products with the same n reuse it.
   DispatchOut dmeta{};
   int dmeta_n = -1;
+  // Tensor maps of the f16 activation rows (tcgen05 B operand), encoded once
+  // per (buffer, rows, cols): x16 for gate/up and dense products, act16 for
+  // down.
+  struct MapCache {
+    const void* ptr = nullptr;
+    int64_t rows = -1, cols = -1;
+    MmaMaps maps;
+  } map_x16, map_act16;
 };
 
 // Expert-parallel exchange buffers. Home side (this rank's tokens): routing,
@@ -724,6 +732,21 @@ int num_sms() {
 // sized for (n_rows, E, k, d, ff).
 // dispatched / recorded: the dispatch metadata / the input rows' records are
 // already in W (route_dispatch_kernel).
+// The activation tensor maps of a launch, re-encoded only when the buffer or
+// its shape changed since the previous call (a map holds only the address,
+// shape and strides, so equal keys give equal maps).
+static int cached_tmaps(Work::MapCache& c, const void* ptr, int64_t rows, int64_t cols, const MmaMaps*& out) {
+  if (c.ptr != ptr || c.rows != rows || c.cols != cols) {
+    c.ptr = nullptr;
+    if (make_tmaps_f16(c.maps, ptr, rows, cols) != KC_OK) return KC_ERR_CUDA;
+    c.ptr = ptr;
+    c.rows = rows;
+    c.cols = cols;
+  }
+  out = &c.maps;
+  return KC_OK;
+}
+
 static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebase, const float* h, int n_rows,
                            const int* ids, const float* wts, int k, bool dispatched = false,
                            bool recorded = false) {
@@ -788,8 +811,8 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   if (fork) RC(fork_aux());
   if (any_large && mma_gu) {
     StageScope ss(ctx, KC_STAGE_GATE_UP_F32);
-    MmaMaps tmap;
-    if (make_tmaps_f16(tmap, W.x16, A, d) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
+    const MmaMaps* tmap = nullptr;
+    if (cached_tmaps(W.map_x16, W.x16, A, d, tmap) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
     MmaArgs ma{};
     ma.part = W.mma_part;
     ma.tile_cnt = W.mma_cnt;
@@ -813,7 +836,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.wide = (int64_t)A > 256LL * E;  // more than 256 rows per expert expected
     ma.bn = std::min(n_rows, kMmaTileN);  // a token adds at most one row to an expert
     ma.read_once = n_rows <= kMmaTileN;
-    RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(ff, 128), lst));
+    RC(launch_mma_grouped(ma, *tmap, max_tt * ceil_div(ff, 128), lst));
     CKL();
   } else if (any_large) {
     GroupedArgs g = grouped_base(ctx);
@@ -875,8 +898,9 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
   if (fork) RC(fork_aux());
   if (any_large && mma_dn) {
     StageScope ss(ctx, KC_STAGE_DOWN_F32);
-    MmaMaps tmap;
-    if (make_tmaps_f16(tmap, W.act16, A, ff) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (act16) failed");
+    const MmaMaps* tmap = nullptr;
+    if (cached_tmaps(W.map_act16, W.act16, A, ff, tmap) != KC_OK)
+      return fail(ctx, KC_ERR_CUDA, "tensor map (act16) failed");
     MmaArgs ma{};
     ma.part = W.mma_part;
     ma.tile_cnt = W.mma_cnt;
@@ -898,7 +922,7 @@ static int experts_forward(kc_ctx* ctx, Work& W, const Layer& L, int E, int ebas
     ma.wide = (int64_t)A > 256LL * E;
     ma.bn = std::min(n_rows, kMmaTileN);
     ma.read_once = n_rows <= kMmaTileN;
-    RC(launch_mma_grouped(ma, tmap, max_tt * ceil_div(d, 128), lst));
+    RC(launch_mma_grouped(ma, *tmap, max_tt * ceil_div(d, 128), lst));
     CKL();
   } else if (any_large) {
     GroupedArgs dn = grouped_base(ctx);
@@ -1020,8 +1044,9 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
   } else if (!ctx->f32_prefill && mma_supported(D.t, D.cols, 1)) {
     launch_act_records(is_k(D.t), x, nullptr, nullptr, n, D.cols, nullptr, n, nullptr, W.x16, st);
     CKL();
-    MmaMaps tmap;
-    if (make_tmaps_f16(tmap, W.x16, n, D.cols) != KC_OK) return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
+    const MmaMaps* tmap = nullptr;
+    if (cached_tmaps(W.map_x16, W.x16, n, D.cols, tmap) != KC_OK)
+      return fail(ctx, KC_ERR_CUDA, "tensor map (x16) failed");
     MmaArgs ma{};
     ma.part = W.mma_part;
     ma.tile_cnt = W.mma_cnt;
@@ -1040,7 +1065,7 @@ static int dense_forward(kc_ctx* ctx, const Dense& D, const float* x, int n, flo
     ma.wide = n > 256;
     ma.bn = std::min(n, kMmaTileN);
     ma.read_once = n <= kMmaTileN;
-    RC(launch_mma_grouped(ma, tmap, ceil_div(n, kMmaTileN) * ceil_div(D.rows, 128), st));
+    RC(launch_mma_grouped(ma, *tmap, ceil_div(n, kMmaTileN) * ceil_div(D.rows, 128), st));
   } else {
     a.list = M.large_list;
     a.n_list = M.n_lists + 1;

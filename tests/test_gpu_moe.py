@@ -182,3 +182,25 @@ def test_shared_expert_layer(ctx, with_gate):
         assert np.array_equal(ids, r_ids)
         ok, err, scale = tol_ok(out, r_out)
         assert ok, f"n={n}: max err {err} vs scale {scale}"
+
+
+def test_host_and_device_entry_points_agree(ctx):
+    """The host-pointer entry point (kc_moe_ffn: copies in, runs, copies out)
+    and the device-pointer one (kc_moe_ffn_dev) give identical ids and output
+    bits, over a sequence of token counts that repeats shapes (cached tensor
+    maps reused) and regrows the workspace (maps re-encoded)."""
+    L = make_layer(E=16, k=4, d=512, ff=512, seed=21)
+    upload(ctx, 960, L)
+    upload(ctx, 961, make_layer(E=16, k=4, d=512, ff=512, seed=22))
+    rng = np.random.default_rng(40)
+    for n in (1, 2, 3, 1, 4, 9, 1, 1, 33, 2, 2, 64, 3, 1, 16, 16, 16):
+        for lid in (960, 961):
+            h = rng.standard_normal((n, 512)).astype(np.float32)
+            out, ids, _ = ctx.moe_ffn(lid, h)
+            hd = torch.from_numpy(h).cuda()
+            od = torch.empty_like(hd)
+            idd = torch.empty((n, 4), dtype=torch.int32, device="cuda")
+            ctx.moe_ffn_dev(lid, hd, od, idd)
+            torch.cuda.synchronize()
+            assert np.array_equal(ids, idd.cpu().numpy()), (lid, n)
+            assert np.array_equal(bits(out), bits(od.cpu().numpy())), (lid, n)
