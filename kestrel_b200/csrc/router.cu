@@ -129,15 +129,19 @@ __global__ void __launch_bounds__(RE * RT * 8) router_logits_kernel(const float*
 void launch_router_logits(const float* w, int64_t row_stride_floats, int E, int d, const float* h, int n_tok,
                           float* logits, int* status, cudaStream_t st, bool force_dot) {
   if (n_tok <= 0) return;
-  static PerDeviceOnce attr_gemm, attr_dot, attr_dot1;
+  static PerDeviceOnce attr_dot, attr_dot1;
   const size_t smem = rl_smem(RL_T, RL_E);
-  smem_attr_once(attr_gemm, router_logits_kernel<true, RL_T>, (int)smem);
   smem_attr_once(attr_dot, router_logits_kernel<false, RL_T>, (int)smem);
   // quant::matmul's dispatch (quant.rs:241): the GEMM path needs >= 4 rows and
   // d % 8 == 0; otherwise quant::dot per output.
   if (!force_dot && n_tok >= 4 && d % 8 == 0) {
-    dim3 grid(ceil_div(E, RL_E), ceil_div(n_tok, RL_T));
-    launch_k(router_logits_kernel<true, RL_T>, grid, RL_E * RL_T * 8, smem, st, w, row_stride_floats, E, d, h, n_tok,
+    // Two expert rows per block (four times the blocks of RL_E rows: the
+    // router reads 1-4 MB, so more blocks in flight shorten the launch).
+    static PerDeviceOnce attr_gemm2;
+    const size_t smem2 = rl_smem(RL_T, 2);
+    smem_attr_once(attr_gemm2, router_logits_kernel<true, RL_T, 2>, (int)smem2);
+    dim3 grid(ceil_div(E, 2), ceil_div(n_tok, RL_T));
+    launch_k(router_logits_kernel<true, RL_T, 2>, grid, 2 * RL_T * 8, smem2, st, w, row_stride_floats, E, d, h, n_tok,
              logits, status);
   } else if (n_tok < 4) {
     // One expert row and up to 4 tokens per block: E blocks.
