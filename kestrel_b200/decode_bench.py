@@ -153,6 +153,9 @@ def main():
     ap.add_argument("--f32-prefill", action="store_true")
     ap.add_argument("--no-warmup", action="store_true", help="skip the warm-up generation (profiling runs)")
     ap.add_argument("--batch", type=int, default=1, help="independent sequences decoded in lockstep")
+    ap.add_argument("--ep-tokens", type=int, default=0,
+                    help="expert parallelism: tokens per rank and call reserved for the peer-memory exchange "
+                         "(default max(8, batch))")
     ap.add_argument("--streamed", type=int, default=0, help="HBM cache slots for host-streamed experts (0: resident)")
     ap.add_argument("--scratch", type=int, default=128)
     ap.add_argument("--policy", choices=["lfru", "lru"], default="lfru")
@@ -200,9 +203,12 @@ def main():
                                  EXPERT_POLICY_LRU if args.policy == "lru" else EXPERT_POLICY_LFRU)
         ctx.set_option(OPT_LOOKAHEAD, 0 if args.no_lookahead else 1)
     if world > 1:
-        # Every layer call (prompt chunks of up to 256 tokens, decode steps of
-        # one) exchanges through peer memory.
-        ctx.ep_reserve(256)
+        # Layer calls of up to --ep-tokens tokens per rank exchange through
+        # peer memory (decode steps: one token, or --batch rows), larger ones
+        # (prompt chunks of up to 256 tokens) through NCCL. Every owner runs
+        # its expert pipeline over the reserved capacity of all sources, so a
+        # reservation sized for the prompt chunks slows every decode step.
+        ctx.ep_reserve(args.ep_tokens if args.ep_tokens > 0 else max(8, args.batch))
     ctx.set_option(OPT_F32_PREFILL, 1 if args.f32_prefill else 0)
     B = max(1, args.batch)
     prompts = [[int(t) for t in np.random.default_rng(1 + rank * B + s).integers(0, cfg["n_vocab"], n_prompt)]
