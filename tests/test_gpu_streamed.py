@@ -197,3 +197,24 @@ def test_model_with_streamed_layers_decodes_same_tokens(ctx, lookahead):
         assert 0 < st["lookahead_correct"] <= st["lookahead_predicted"]
     else:
         assert st["lookahead_predicted"] == 0 and st["prefetch_issued"] == 0
+
+
+def test_batch_decode_with_streamed_layers(ctx):
+    """Independent sequences decoded in lockstep (kc_model_generate_batch,
+    every row as a batch of one: experts split in entries of at most three
+    rows) over a model whose routed layers are streamed through 8 cache + 8
+    scratch slots, with router lookahead for the 3-row steps: the same tokens
+    as the resident model's batch."""
+    cfg = dict(synth.CONFIG0, n_layer=3)
+    model = synth.make_model(cfg, seed=4)
+    rng = np.random.default_rng(32)
+    prompts = [[int(t) for t in rng.integers(0, cfg["n_vocab"], n)] for n in (5, 9, 2)]
+    synth.load_cuda(ctx, model, n_ctx=48)
+    ref = ctx.model_generate_batch(prompts, 12)
+    synth.load_cuda(ctx, model, n_ctx=48, streamed=True)
+    ctx.expert_cache_reserve(8, 8, 0)
+    got = ctx.model_generate_batch(prompts, 12)
+    assert got == ref
+    st = ctx.expert_cache_stats()
+    check_counters(st)
+    assert st["lookahead_predicted"] > 0
