@@ -119,11 +119,18 @@ def lib() -> ctypes.CDLL:
 
 
 def _ptr(a):
-    """Address of a numpy array or a torch tensor (host or device)."""
+    """Address of a numpy array or a torch tensor (host or device). For a
+    writable numpy array the address comes through the buffer protocol
+    (several times cheaper than ndarray.ctypes, which builds a helper object
+    per call: it matters on the per-call path); read-only, empty or
+    non-contiguous arrays take ndarray.ctypes."""
     if a is None:
         return None
     if isinstance(a, np.ndarray):
-        return a.ctypes.data
+        try:
+            return ctypes.addressof(ctypes.c_char.from_buffer(a))
+        except (TypeError, ValueError, BufferError):
+            return a.ctypes.data
     return a.data_ptr()
 
 
