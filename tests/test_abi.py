@@ -47,3 +47,18 @@ def test_null_context_is_rejected():
     from kestrel_b200 import cuda
     assert cuda.lib().kc_sync(None) == 1
     assert cuda.lib().kc_moe_ffn_dev(None, 0, None, 0, None, None, None) == 1
+
+
+def test_array_addresses_passed_to_the_library():
+    """The binding passes numpy arrays by address through the buffer protocol
+    when it can, else through ndarray.ctypes: both give the array's first
+    element for writable, read-only, offset, strided and empty arrays."""
+    import numpy as np
+    from kestrel_b200.cuda import _ptr
+    a = np.arange(48, dtype=np.float32).reshape(6, 8)
+    ro = np.frombuffer(bytes(range(64)), dtype=np.uint8)
+    cases = [a, a[2:], a[:, 3:], a[:, ::2], ro, ro[5:], np.empty(0, np.float32),
+             np.zeros((3, 4), np.int32, order="F")]
+    for x in cases:
+        assert _ptr(x) == x.__array_interface__["data"][0]
+    assert _ptr(None) is None
