@@ -614,14 +614,23 @@ int streams_demand(kc_ctx* ctx, const Layer& L, const int32_t* ids_dev, int A, L
                 "host-streamed experts: layer %d routes to %d experts, more than the %d cache + %d scratch slots "
                 "can hold at once (kc_expert_cache_reserve)",
                 L.id, (int)need.size(), S.capacity, S.scratch);
-  for (int s : waits) CK(cudaStreamWaitEvent(st, S.ready[s], 0));
+  // The cache now counts this call's experts as resident: if a copy cannot
+  // be enqueued, forget every slot's contents before reporting the error.
+  cudaError_t ce = cudaSuccess;
+  for (int s : waits)
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(st, S.ready[s], 0);
   for (const ExpertCache::Load& ld : loads) {
-    CK(cudaMemcpyAsync(S.arena + (int64_t)ld.slot * S.slot_bytes, L.host + (int64_t)ld.expert * S.slot_bytes,
-                       (size_t)S.slot_bytes, cudaMemcpyHostToDevice, st));
-    S.cache.add_bytes((uint64_t)S.slot_bytes, 1);
+    if (ce != cudaSuccess) break;
+    ce = cudaMemcpyAsync(S.arena + (int64_t)ld.slot * S.slot_bytes, L.host + (int64_t)ld.expert * S.slot_bytes,
+                         (size_t)S.slot_bytes, cudaMemcpyHostToDevice, st);
+    if (ce == cudaSuccess) S.cache.add_bytes((uint64_t)S.slot_bytes, 1);
   }
   for (size_t i = 0; i < need.size(); ++i) S.slot_host[need[i]] = slot[i];
-  CK(cudaMemcpyAsync(S.slot_dev, S.slot_host, (size_t)E * 4, cudaMemcpyHostToDevice, st));
+  if (ce == cudaSuccess) ce = cudaMemcpyAsync(S.slot_dev, S.slot_host, (size_t)E * 4, cudaMemcpyHostToDevice, st);
+  if (ce != cudaSuccess) {
+    S.cache.configure(S.capacity, S.scratch, S.spec, S.policy);
+    return fail(ctx, KC_ERR_CUDA, "host-streamed experts: expert copy failed: %s", cudaGetErrorString(ce));
+  }
   if (look_n) {
     const int nl = S.look_layer;
     S.look_ids = nullptr;
