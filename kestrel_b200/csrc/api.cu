@@ -543,9 +543,18 @@ int streams_prefetch(kc_ctx* ctx, const Layer& Lt, const std::vector<int>& exper
   std::vector<ExpertCache::Load> loads;
   S.cache.prefetch(Lt.id, experts.data(), (int)experts.size(), loads);
   for (const ExpertCache::Load& ld : loads) {
-    CK(cudaMemcpyAsync(S.arena + (int64_t)ld.slot * S.slot_bytes, Lt.host + (int64_t)ld.expert * S.slot_bytes,
-                       (size_t)S.slot_bytes, cudaMemcpyHostToDevice, S.copy));
-    CK(cudaEventRecord(S.ready[ld.slot], S.copy));
+    cudaError_t ce = cudaMemcpyAsync(S.arena + (int64_t)ld.slot * S.slot_bytes,
+                                     Lt.host + (int64_t)ld.expert * S.slot_bytes, (size_t)S.slot_bytes,
+                                     cudaMemcpyHostToDevice, S.copy);
+    if (ce == cudaSuccess) ce = cudaEventRecord(S.ready[ld.slot], S.copy);
+    if (ce != cudaSuccess) {
+      // The slots of this prefetch count as filled by a copy that may never
+      // run (an event that was never recorded reads as complete): forget
+      // every slot's contents once the copies already queued have landed.
+      cudaStreamSynchronize(S.copy);
+      S.cache.configure(S.capacity, S.scratch, S.spec, S.policy);
+      return fail(ctx, KC_ERR_CUDA, "host-streamed experts: prefetch copy failed: %s", cudaGetErrorString(ce));
+    }
     S.cache.add_bytes((uint64_t)S.slot_bytes, 1);
   }
   return KC_OK;
