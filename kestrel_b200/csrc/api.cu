@@ -637,6 +637,9 @@ int streams_demand(kc_ctx* ctx, const Layer& L, const int32_t* ids_dev, int A, L
   for (size_t i = 0; i < need.size(); ++i) S.slot_host[need[i]] = slot[i];
   if (ce == cudaSuccess) ce = cudaMemcpyAsync(S.slot_dev, S.slot_host, (size_t)E * 4, cudaMemcpyHostToDevice, st);
   if (ce != cudaSuccess) {
+    // Prefetch copies still landing would otherwise race with the next
+    // call's copies into the slots the reset frees.
+    cudaStreamSynchronize(S.copy);
     S.cache.configure(S.capacity, S.scratch, S.spec, S.policy);
     return fail(ctx, KC_ERR_CUDA, "host-streamed experts: expert copy failed: %s", cudaGetErrorString(ce));
   }
