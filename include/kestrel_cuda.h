@@ -156,7 +156,10 @@ KC_API int kc_upload_shared_expert(kc_ctx* ctx, int layer, int ff_shared, int d,
    distinct experts one call routes to. Calls of streamed layers cannot be
    captured into a CUDA graph (kc_model_generate then runs its steps
    eagerly). Every streamed layer has the same shape (d, ff, types). Not
-   available with expert parallelism.
+   available with expert parallelism. A call or prefetch whose expert copy
+   CUDA refuses returns KC_ERR_CUDA after emptying the cache (the copies
+   already queued land first), so no slot counts as holding an expert whose
+   copy did not run; the counters are reset with it.
 
    kc_expert_cache_reserve sets `capacity` cache slots, `scratch` slots for
    experts the cache does not admit, `spec` slots for predictions it does
@@ -224,8 +227,12 @@ KC_API int kc_moe_ffn_dev(kc_ctx* ctx, int layer, const float* h, int n_tok, flo
                    float* topk_w);
 
 /* quant::matmul for an uploaded dense tensor: x [n, cols] f32 -> out [n, rows]
-   f32, with the reference's dispatch on n (n < 4: int8 activations for
-   Q4_K/Q6_K/Q8_0; n >= 4: exact f32 arithmetic on dequantised weights). */
+   f32, with the reference's dispatch on n. F32 tensors: the reference's f32
+   summation order, bit-exact, for every n. n < 4: int8 activations for
+   Q4_K/Q6_K/Q8_0, bit-exact. n >= 4: the reference's dequantise-then-f32
+   path, run on tcgen05 tensor cores with f16 operands and f32 accumulation
+   (within 1e-3 of the output's scale), or exactly in f32 on CUDA cores under
+   KC_OPT_F32_PREFILL. */
 KC_API int kc_matmul(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out);
 KC_API int kc_matmul_dev(kc_ctx* ctx, int tensor_id, const float* x, int n, float* out);
 
