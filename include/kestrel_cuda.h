@@ -88,7 +88,8 @@ enum { KC_F32 = 0, KC_Q8_0 = 8, KC_Q4_K = 12, KC_Q6_K = 14 };
 
 /* Create a context on CUDA device `device` with its own stream. */
 KC_API int kc_init(int device, kc_ctx** out);
-/* Free all device memory owned by the context (weights, workspace). */
+/* Free all memory owned by the context: device weights and workspace, and the
+   pinned host memory of host-streamed experts. Waits for its work first. */
 KC_API void kc_free(kc_ctx* ctx);
 /* Message of the last failed call on this context ("" if none). ctx may be
    NULL for errors of kc_init. */
